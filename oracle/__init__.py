@@ -1,0 +1,148 @@
+"""CPU oracle of the GWP-0.5 MoT forward pass — TEST INFRASTRUCTURE ONLY.
+
+Loaded only by tests/, __graft_entry__.smoke() and bench.py's CPU-baseline
+legs, always as the checker (or the timed CPU baseline), never by the product
+path. See oracle.h for what it restates and its parity status.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+from .synth import Geometry, Request, make_weights, statistics  # noqa: F401
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "liboracle.so"
+REF_LIB = HERE / "_ref" / "libwamref.so"
+
+
+class _Geom(C.Structure):
+    _fields_ = [(n, C.c_int) for n in (
+        "hidden", "layers", "heads", "ffn", "action_hidden", "action_ffn", "action_dim",
+        "real_state_dim", "real_action_dim", "num_embodiments", "embodiment_id", "grid_h",
+        "grid_w", "vae_z", "action_chunk", "steps", "prompt_tokens", "text_dim")] + [
+        ("norm_eps", C.c_float), ("flow_shift", C.c_float)]
+
+
+def geom_struct(g: Geometry, cls=_Geom):
+    s = cls()
+    for name, _ in cls._fields_:
+        setattr(s, name, getattr(g, name))
+    return s
+
+
+def build(with_ref: bool = True) -> None:
+    """Builds liboracle.so (and, when the reference tree is present, the
+    reference's own scheduler/semantics into _ref/libwamref.so)."""
+    subprocess.run(["make", "-C", str(HERE), "liboracle.so"], check=True, capture_output=True)
+    if with_ref and Path("/root/reference/src/models/common/scheduler.cpp").exists():
+        subprocess.run(["make", "-C", str(HERE), "ref"], check=True, capture_output=True)
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            build(with_ref=False)
+        l = C.CDLL(str(LIB))
+        f32p = C.POINTER(C.c_float)
+        l.oracle_create.restype = C.c_void_p
+        l.oracle_create.argtypes = [C.POINTER(_Geom), C.c_int, C.POINTER(C.c_char_p),
+                                    C.POINTER(C.c_void_p), C.POINTER(C.c_int64), f32p, f32p,
+                                    f32p, f32p, C.c_char_p, C.c_int]
+        l.oracle_destroy.argtypes = [C.c_void_p]
+        l.oracle_predict.restype = C.c_int
+        l.oracle_predict.argtypes = [C.c_void_p] + [f32p] * 10
+        l.oracle_schedule.argtypes = [C.c_int, C.c_float, f32p, f32p]
+        l.oracle_timestep_embedding.argtypes = [C.c_float, C.c_int, f32p]
+        l.oracle_visual_positions.argtypes = [C.c_int, C.c_int] + [C.POINTER(C.c_int32)] * 3
+        l.oracle_threads.restype = C.c_int
+        _lib = l
+    return _lib
+
+
+def ref_lib():
+    """The reference's own scheduler.cpp/semantics.cpp (None if not built)."""
+    if not REF_LIB.exists():
+        return None
+    l = C.CDLL(str(REF_LIB))
+    f32p = C.POINTER(C.c_float)
+    i32p = C.POINTER(C.c_int32)
+    l.wamref_schedule.argtypes = [C.c_int, C.c_float, f32p, f32p]
+    l.wamref_visual_positions.argtypes = [C.c_int, C.c_int, i32p, i32p, i32p]
+    l.wamref_action_positions.argtypes = [C.c_int, C.c_int, i32p]
+    l.wamref_normalize_state.argtypes = [f32p, C.c_int, C.c_int, f32p, f32p, f32p]
+    l.wamref_postprocess.argtypes = [f32p, C.c_int, C.c_int, C.c_int, f32p, f32p, f32p, C.c_int, f32p]
+    return l
+
+
+def _fp(a):
+    return a.ctypes.data_as(C.POINTER(C.c_float)) if a is not None else None
+
+
+def schedule(steps: int, shift: float):
+    ts = np.zeros(steps, np.float32)
+    sig = np.zeros(steps + 1, np.float32)
+    lib().oracle_schedule(steps, shift, _fp(ts), _fp(sig))
+    return ts, sig
+
+
+def timestep_embedding(t: float, dim: int = 256):
+    out = np.zeros(dim, np.float32)
+    lib().oracle_timestep_embedding(t, dim, _fp(out))
+    return out
+
+
+class OracleModel:
+    """A CPU model over BF16 weights given as {compact name: uint16 array}."""
+
+    def __init__(self, g: Geometry, weights: dict, stats: dict | None = None):
+        self.g = g
+        stats = stats or statistics(g)
+        names = list(weights)
+        arrs = [np.ascontiguousarray(weights[n], dtype=np.uint16) for n in names]
+        cn = (C.c_char_p * len(names))(*[n.encode() for n in names])
+        cd = (C.c_void_p * len(names))(*[a.ctypes.data for a in arrs])
+        ce = (C.c_int64 * len(names))(*[a.size for a in arrs])
+        err = C.create_string_buffer(512)
+        self._stats = {k: np.ascontiguousarray(v, np.float32) for k, v in stats.items()}
+        gs = geom_struct(g)
+        self.h = lib().oracle_create(C.byref(gs), len(names), cn, cd, ce,
+                                     _fp(self._stats["state_q01"]), _fp(self._stats["state_q99"]),
+                                     _fp(self._stats["action_q01"]), _fp(self._stats["action_q99"]),
+                                     err, 512)
+        if not self.h:
+            raise RuntimeError("oracle_create: " + err.value.decode())
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h:
+            lib().oracle_destroy(h)
+            self.h = None
+
+    def predict(self, req: Request, dumps: bool = False) -> dict:
+        g = self.g
+        P, L, Hd, Nt = g.prefix_tokens, g.layers, g.heads, g.prompt_tokens
+        out = np.zeros((g.action_chunk, g.real_action_dim), np.float32)
+        d = {}
+        if dumps:
+            d = {"prefix_k": np.zeros((L, Hd, P, 128), np.float32),
+                 "prefix_v": np.zeros((L, Hd, P, 128), np.float32),
+                 "prompt_k": np.zeros((L, Hd, Nt, 128), np.float32),
+                 "prompt_v": np.zeros((L, Hd, Nt, 128), np.float32),
+                 "velocity": np.zeros((g.steps, g.action_chunk, g.action_dim), np.float32),
+                 "actions": np.zeros((g.steps, g.action_chunk, g.action_dim), np.float32)}
+        args = [np.ascontiguousarray(a, np.float32) for a in (req.state, req.latent, req.prompt, req.noise)]
+        rc = lib().oracle_predict(self.h, *[_fp(a) for a in args], _fp(out),
+                                  *[_fp(d.get(k)) for k in ("prefix_k", "prefix_v", "prompt_k",
+                                                            "prompt_v", "velocity", "actions")])
+        if rc != 0:
+            raise RuntimeError("oracle_predict failed")
+        d["action"] = out
+        return d

@@ -1,0 +1,82 @@
+/*
+ * CPU oracle for the GWP-0.5 MoT forward pass — TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain C++/OpenMP restatement of the reference's BF16 latency path
+ * (GigaAI-research/wam.cpp, src/models/gwp05/engine/{mot,cache,weights,
+ * text_encoder,engine}.cpp, src/models/common/scheduler.cpp,
+ * src/models/gwp05/semantics.cpp). Only tests/, __graft_entry__.smoke() and
+ * bench.py's cpu_baseline / --impl reference legs load it, always as the checker
+ * or the timed CPU baseline, never as part of the product path.
+ *
+ * Parity status: the reference's tensor arithmetic lives in the un-vendored
+ * llama.cpp b9866 ggml, which cannot be built here, so the tensor math is
+ * "parity unpinned" (restated from the reference's call sites and op
+ * definitions). The host-side schedule, positions and state/action
+ * (de)normalisation are pinned against the reference's own scheduler.cpp and
+ * semantics.cpp compiled from source (oracle/Makefile, target ref).
+ */
+#ifndef WAM_ORACLE_H
+#define WAM_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct oracle_geometry {
+  int hidden;          /* H = heads * 128 (visual expert width, attention width) */
+  int layers;          /* L */
+  int heads;           /* H / 128 */
+  int ffn;             /* visual expert FFN width */
+  int action_hidden;   /* E */
+  int action_ffn;      /* action expert FFN width */
+  int action_dim;      /* padded action/state dim A */
+  int real_state_dim;
+  int real_action_dim;
+  int num_embodiments;
+  int embodiment_id;
+  int grid_h, grid_w;  /* visual token grid; latent is [vae_z, 2 grid_h, 2 grid_w] */
+  int vae_z;
+  int action_chunk;    /* T */
+  int steps;           /* S */
+  int prompt_tokens;   /* N_t (cross-attention keys) */
+  int text_dim;        /* D */
+  float norm_eps;
+  float flow_shift;
+} oracle_geometry;
+
+/* Creates a model over BF16 tensors given by compact GGUF name
+ * (gwp.blk.<l>.<a|v>.sa.qkv.weight ...). Data is copied. Returns NULL and
+ * writes err on failure. */
+void* oracle_create(const oracle_geometry* g, int n_tensors, const char** names,
+                    const uint16_t** data, const int64_t* numel, const float* state_q01,
+                    const float* state_q99, const float* action_q01, const float* action_q99,
+                    char* err, int errlen);
+void oracle_destroy(void* model);
+
+/* One request. state: [real_state_dim] raw; latent: [vae_z][2gh][2gw];
+ * prompt: [prompt_tokens][text_dim] (zero-padded by the caller);
+ * noise: [T][A]. action_out: [T][real_action_dim].
+ * Optional dumps (NULL to skip), element (layer, head, row, d):
+ *   prefix_k / prefix_v: [L][heads][1 + V][128] after RoPE, BF16-rounded;
+ *   prompt_k / prompt_v: [L][heads][N_t][128];
+ *   velocity: [S][T][A] decoder outputs; actions: [S][T][A] Euler outputs. */
+int oracle_predict(void* model, const float* state, const float* latent, const float* prompt,
+                   const float* noise, float* action_out, float* prefix_k, float* prefix_v,
+                   float* prompt_k, float* prompt_v, float* velocity, float* actions);
+
+/* Flow-match Euler schedule: timesteps [steps], sigmas [steps + 1]. */
+void oracle_schedule(int steps, float shift, float* timesteps, float* sigmas);
+/* Sinusoidal timestep embedding [dim]: cos block then sin block. */
+void oracle_timestep_embedding(float t, int dim, float* out);
+/* Visual positions for a grid: time/height/width [gh * gw]. */
+void oracle_visual_positions(int gh, int gw, int32_t* t, int32_t* h, int32_t* w);
+/* Threads the oracle's parallel regions use. */
+int oracle_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,126 @@
+"""tcgen05 GEMM parity against a torch F32 reference of the same op.
+
+The GEMM is a floating-point kernel, so its reference is an F32 matmul of the
+same BF16 operands; epilogues are checked against a torch restatement of the
+reference's BF16 rounding points (weights.cpp:819-849, native-bf16.patch:79-91).
+Tolerances: raw F32 accumulators within 1e-5 relative-L2 (summation order only);
+BF16 outputs within 1 BF16 ulp on >99.9% of elements plus 1e-2 relative-L2.
+"""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_l2(a, b):
+    a = a.double()
+    b = b.double()
+    return float((a - b).norm() / (b.norm() + 1e-30))
+
+
+def make(m, n, k, seed=0, dev="cuda"):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    b = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16).to(dev)
+    return x, w, b
+
+
+SHAPES = [
+    (48, 3072, 3072),   # denoise QKV-slice / O projection at batch 1 (split-K)
+    (48, 256, 128),
+    (1, 384, 256),      # single token (state / condition)
+    (10, 1024, 256),    # condition MLP over 10 timesteps
+    (200, 640, 192),    # patch embedding K
+    (768, 3072, 3072),  # prefix visual tokens
+    (384, 1536, 1024),  # batch-8 denoise
+    (1000, 512, 640),   # ragged M
+]
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_gemm_f32_accumulator(cuda_device, m, n, k):
+    from wam_b200 import ops
+
+    x, w, _ = make(m, n, k)
+    y = ops.gemm(x, w, epilogue=ops.EPI_F32_OUT)
+    ref = x.float() @ w.float().T
+    torch.cuda.synchronize()
+    assert rel_l2(y, ref) < 1e-5
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7])
+def test_gemm_forced_splits_deterministic(cuda_device, splits):
+    from wam_b200 import ops
+
+    x, w, _ = make(48, 512, 1024, seed=1)
+    s = ops.Scratch()
+    y1 = ops.gemm(x, w, epilogue=ops.EPI_F32_OUT, scratch=s, force_splits=splits)
+    y2 = ops.gemm(x, w, epilogue=ops.EPI_F32_OUT, scratch=s, force_splits=splits)
+    ref = x.float() @ w.float().T
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    assert rel_l2(y1, ref) < 1e-5
+    assert s.error_code() == 0
+    assert int(s.counters.abs().sum()) == 0
+
+
+def bf(x):
+    return x.to(torch.bfloat16).float()
+
+
+def gelu_tanh(v):
+    return 0.5 * v * (1.0 + torch.tanh(0.7978845608028654 * v * (1.0 + 0.044715 * v * v)))
+
+
+@pytest.mark.parametrize("m,n,k", [(48, 3072, 3072), (768, 1024, 512), (16, 384, 128)])
+@pytest.mark.parametrize("epi", ["bias", "gelu", "silu", "gated", "res", "f32bias"])
+def test_gemm_epilogues(cuda_device, m, n, k, epi):
+    from wam_b200 import ops
+
+    x, w, b = make(m, n, k, seed=2)
+    acc = x.float() @ w.float().T
+    lin = bf(bf(acc) + b.float())
+    gate = torch.randn(n, device="cuda") * 0.5
+    resid = torch.randn(m, n, device="cuda").to(torch.bfloat16)
+    if epi == "bias":
+        y = ops.gemm(x, w, ops.EPI_BIAS, bias=b)
+        ref = lin
+    elif epi == "gelu":
+        y = ops.gemm(x, w, ops.EPI_BIAS_GELU, bias=b)
+        ref = bf(gelu_tanh(bf(acc) + b.float()))
+    elif epi == "silu":
+        y = ops.gemm(x, w, ops.EPI_BIAS_SILU, bias=b)
+        ref = bf(lin * torch.sigmoid(lin))
+    elif epi == "gated":
+        y = ops.gemm(x, w, ops.EPI_GATED_RES, bias=b, gate=gate, residual=resid)
+        ref = bf(resid.float() + lin * gate)
+    elif epi == "res":
+        y = ops.gemm(x, w, ops.EPI_RES, bias=b, residual=resid)
+        ref = bf(resid.float() + lin)
+    else:
+        y = ops.gemm(x, w, ops.EPI_F32_BIAS, bias=b)
+        ref = bf(acc + b.float())
+    torch.cuda.synchronize()
+    y = y.float()
+    assert rel_l2(y, ref) < 1e-2
+    # BF16 rounding of values whose F32 accumulators differ in the last bits can
+    # flip by one ulp; anything beyond that is a real mismatch.
+    ulp = torch.clamp(ref.abs(), min=1e-6) * (2.0 ** -7)
+    bad = ((y - ref).abs() > 1.01 * ulp + 1e-6).float().mean().item()
+    assert bad < 1e-3, f"{bad:.2e} of elements differ by more than one BF16 ulp"
+
+
+def test_gemm_in_place_residual(cuda_device):
+    """The gated-residual epilogue may write over its residual input."""
+    from wam_b200 import ops
+
+    x, w, b = make(48, 768, 512, seed=3)
+    gate = torch.randn(768, device="cuda")
+    h = torch.randn(48, 768, device="cuda").to(torch.bfloat16)
+    expect = bf(h.float() + bf(bf(x.float() @ w.float().T) + b.float()) * gate)
+    ops.gemm(x, w, ops.EPI_GATED_RES, bias=b, gate=gate, residual=h, out=h)
+    torch.cuda.synchronize()
+    assert rel_l2(h.float(), expect) < 1e-2

@@ -1,0 +1,164 @@
+// Host-side interface to the engine's CUDA kernels (sm_100a). Every launcher
+// takes device pointers and a stream; nothing here allocates.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace wamb {
+
+using bf16 = __nv_bfloat16;
+
+// ------------------------------------------------------------------ GEMM
+// y[m, n] = epilogue( sum_k x[m, k] * w[n, k] ), x: [M, K] (row stride ldx),
+// w: [N, K] row-major (GGUF ne = {K, N}). The epilogues restate the rounding
+// points of the reference's BF16 path (src/models/gwp05/engine/weights.cpp:819-849,
+// patches/llama-b9866-native-bf16.patch:79-91,507-514):
+enum GemmEpilogue : int {
+  EPI_BIAS = 0,       // y = bf16(bf16(acc) + b)                    linear_with_activation
+  EPI_BIAS_GELU = 1,  // y = bf16(gelu_tanh(bf16(acc) + b))         linear_gelu_with_activation
+  EPI_BIAS_SILU = 2,  // y = bf16(silu(bf16(bf16(acc) + b)))        linear + ggml_silu
+  EPI_GATED_RES = 3,  // y = bf16(r + bf16(bf16(acc) + b) * gate)   linear + gated_residual
+  EPI_RES = 4,        // y = bf16(r + bf16(bf16(acc) + b))          linear + ggml_add(hidden, .)
+  EPI_F32_BIAS = 5,   // y = bf16(acc + b)                          conv_2d (F32 out) + bias, cast
+  EPI_F32_OUT = 6,    // y_f32 = acc                                 raw accumulator (tests)
+};
+
+struct GemmArgs {
+  int m, n, k;
+  int num_kb;  // k / 64
+  int splits;
+  int tiles_m, tiles_n;
+  int epilogue;
+  const bf16* bias;      // [n] or null
+  const float* gate;     // [n] (EPI_GATED_RES)
+  const bf16* residual;  // [m, ldr] (EPI_GATED_RES / EPI_RES); may alias out
+  int ldr;
+  void* out;  // bf16 [m, ldo] (float for EPI_F32_OUT)
+  int ldo;
+  float* workspace;    // split-K partial tiles
+  unsigned* counters;  // split-K arrival counters, one per output tile, zero at rest
+  unsigned* error;     // device error word
+};
+
+struct GemmScratch {
+  float* workspace = nullptr;
+  size_t workspace_floats = 0;
+  unsigned* counters = nullptr;
+  int counter_slots = 0;
+  unsigned* error = nullptr;
+};
+
+struct GemmOp {
+  CUtensorMap tm_w;
+  CUtensorMap tm_x;
+  GemmArgs args;
+  int bt = 0;
+  int grid = 0;
+  int smem_bytes = 0;
+};
+
+// Plans one GEMM: picks the token tile and split-K factor, encodes the TMA
+// descriptors. Returns nullptr on success or a static error message.
+const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, int n, int k,
+                      int epilogue, const bf16* bias, const float* gate, const bf16* residual,
+                      int ldr, void* out, int ldo, const GemmScratch& scratch, int num_sms,
+                      int force_splits);
+cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream);
+// Split-K scratch a GEMM of this shape would use (floats), and its tile count.
+size_t gemm_scratch_floats(int m, int n, int k, int num_sms, int force_splits, int* tiles_out);
+
+// ------------------------------------------------------------ elementwise
+// LayerNorm (two-pass mean / centred variance, no affine) then AdaLN
+// modulation: y = bf16(n * (1 + scale[c]) + shift[c]); scale/shift F32 [cols]
+// shared by all rows (norm_bf16_fused<affine=false>, native-bf16.patch:368-409).
+void launch_ln_modulate(const bf16* x, int ldx, int rows, int cols, const float* scale,
+                        const float* shift, float eps, bf16* y, int ldy, cudaStream_t s);
+// Affine LayerNorm: y = bf16(n * w[c] + b[c]), w/b BF16 (norm_bf16_fused<affine=true>).
+void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w, const bf16* b,
+                      float eps, bf16* y, int ldy, cudaStream_t s);
+
+// Per-token RMSNorm of q and k over the full attention width, RoPE, BF16 cast
+// and scatter into head-major attention buffers.
+struct QkvScatter {
+  const bf16* qkv;  // source row r at qkv + r * ld_qkv: [q(H) | k(H) | v(H)]
+  int ld_qkv;
+  int rows;          // tokens in this launch
+  int rows_per_seq;  // tokens of one request in this launch
+  int hidden;        // H = heads * 128
+  int heads;
+  const bf16* q_norm;  // [H]
+  const bf16* k_norm;  // [H]
+  float eps;
+  // rope: mode 0 = none, 1 = 1-D over 128 dims with position pos_base + row_in_seq,
+  // 2 = 3-D sections (44/42/42) with per-row positions from pos_thw[row_in_seq][3]
+  int rope_mode;
+  int pos_base;
+  const int* pos_thw;
+  const float* inv_freq;  // 1-D: [64]; 3-D: [22 | 21 | 21]
+  // destinations, element (seq, head, row, d):
+  bf16* q_out;  // may be null
+  long long q_seq_stride, q_head_stride;
+  int q_row_offset;
+  bf16* k_out;
+  bf16* v_out;  // may be null (K-only, e.g. cross K)
+  long long kv_seq_stride, kv_head_stride;
+  int kv_row_offset;
+  int do_v;
+};
+void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s);
+
+// Flash attention over head-major Q/K/V with softmax(scale * QK^T) V,
+// F32 scores, BF16 probabilities, F32 accumulation. Output row r of sequence b
+// goes to out[(b * out_seq_rows + r) * ldo + head * 128 + d]; if split_first,
+// row 0 of each sequence goes to out_first[b * ldo_first + ...] instead and
+// rows 1.. to out[(b * (lq - 1) + r - 1) * ldo ...].
+struct AttnArgs {
+  const bf16* q;
+  long long q_seq_stride, q_head_stride;
+  const bf16* k;
+  const bf16* v;
+  long long kv_seq_stride, kv_head_stride;
+  int lq, lk, heads, batch;
+  float scale;
+  bf16* out;
+  int ldo;
+  bf16* out_first;
+  int ldo_first;
+  int split_first;
+};
+void launch_attention(const AttnArgs& a, cudaStream_t s);
+
+// y[m, n] = act(bf16(bf16(sum_k x[m, k] * w(n, k)) + b[n])) for the small
+// action/state encoder and decoder projections, with w(n, k) =
+// w[n * w_sn + k * w_sk] (handles the transposed embodiment slices).
+enum SmallAct : int { ACT_NONE = 0, ACT_GELU_ERF = 1 };
+void launch_small_linear(const bf16* x, int ldx, int m, int k, const bf16* w, long long w_sn,
+                         long long w_sk, const bf16* b, int n, int act, bf16* y, int ldy,
+                         cudaStream_t s);
+
+// combined[l][j] = f32(mod[j]) + f32(table_l[j]) for all layers (modulation_add,
+// mot.cpp:137-145). tables: L x [width] BF16 pointers packed in a device array.
+void launch_modulation_add(const bf16* mod, const bf16* const* tables, int layers, int width,
+                           float* combined, cudaStream_t s);
+// y = bf16(silu(x)), elementwise.
+void launch_silu(const bf16* x, bf16* y, int n, cudaStream_t s);
+// F32 -> BF16 round to nearest even.
+void launch_f32_to_bf16(const float* x, bf16* y, long long n, cudaStream_t s);
+// im2col of a [C, 2gh, 2gw] F32 latent for the 2x2 stride-2 patch conv:
+// cols[b][y*gw + x][c*4 + dy*2 + dx] = bf16(latent[b][c][2y+dy][2x+dx]).
+void launch_patchify(const float* latent, int batch, int channels, int gh, int gw, bf16* cols,
+                     cudaStream_t s);
+// Euler step a = bf16(f32(a) + f32(v) * dt), with v read from a [rows, ldv] buffer.
+void launch_euler(bf16* action, const bf16* velocity, int n, const float* dt, cudaStream_t s);
+// BF16 -> F32.
+void launch_bf16_to_f32(const bf16* x, float* y, long long n, cudaStream_t s);
+// Deterministic synthetic weights: w[i] = bf16(center + scale * g(seed, i)),
+// g an integer-hash approximation of N(0,1) (sum of four uniform 16-bit draws).
+void launch_synth_bf16(bf16* w, long long n, unsigned long long seed, float scale, float center,
+                       cudaStream_t s);
+
+}  // namespace wamb

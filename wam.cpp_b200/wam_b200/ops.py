@@ -1,0 +1,53 @@
+"""Op-level wrappers over the C ABI, taking torch CUDA tensors.
+
+torch supplies device memory and the current stream only; the arithmetic runs
+in libwam_b200's sm_100a kernels.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from ._lib import check, load
+
+EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_GATED_RES, EPI_RES, EPI_F32_BIAS, EPI_F32_OUT = range(7)
+
+
+def _ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else C.c_void_p(0)
+
+
+def _stream():
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class Scratch:
+    """Split-K workspace + counters + device error word for op-level GEMMs."""
+
+    def __init__(self, floats: int = 1 << 24, slots: int = 1 << 14, device="cuda"):
+        self.ws = torch.zeros(floats, dtype=torch.float32, device=device)
+        self.counters = torch.zeros(slots, dtype=torch.int32, device=device)
+        self.error = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def error_code(self) -> int:
+        return int(self.error.item())
+
+
+def gemm(x, w, epilogue=EPI_BIAS, bias=None, gate=None, residual=None, out=None,
+         scratch: Scratch | None = None, force_splits: int = 0):
+    """out[m, n] = epilogue(x[m, :K] . w[n, :]) via wam_b200_op_gemm."""
+    lib = load()
+    m, k = x.shape[0], w.shape[1]
+    n = w.shape[0]
+    if out is None:
+        dt = torch.float32 if epilogue == EPI_F32_OUT else torch.bfloat16
+        out = torch.empty(m, n, dtype=dt, device=x.device)
+    scratch = scratch or Scratch()
+    rc = lib.wam_b200_op_gemm(
+        _ptr(x), x.stride(0), m, _ptr(w), n, k, epilogue, _ptr(bias), _ptr(gate), _ptr(residual),
+        residual.stride(0) if residual is not None else 0, _ptr(out), out.stride(0),
+        _ptr(scratch.ws), scratch.ws.numel(), _ptr(scratch.counters), scratch.counters.numel(),
+        _ptr(scratch.error), force_splits, _stream())
+    check(rc, "wam_b200_op_gemm")
+    return out
