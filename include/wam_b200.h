@@ -74,6 +74,151 @@ WAM_B200_API int wam_b200_op_gemm(const void* x, int ldx, int m, const void* w, 
 WAM_B200_API size_t wam_b200_gemm_scratch_floats(int m, int n, int k, int force_splits,
                                                  int* tiles_out);
 
+/* Flash attention softmax(scale Q K^T) V over head-major BF16 tensors:
+ * element (seq, head, row, d) of q at q[seq*q_seq_stride + head*q_head_stride +
+ * row*128 + d], k/v likewise with kv strides; out row r of seq b at
+ * out[(b*lq + r)*ldo + head*128 + d]. Replaces the cached joint attention
+ * (src/models/gwp05/engine/mot.cpp:432-446) and cross attention (:299-321). */
+WAM_B200_API int wam_b200_op_attention(const void* q, long long q_seq_stride,
+                                       long long q_head_stride, const void* k, const void* v,
+                                       long long kv_seq_stride, long long kv_head_stride, int lq,
+                                       int lk, int heads, int batch, float scale, void* out,
+                                       int ldo, void* stream);
+
+/* LayerNorm + AdaLN modulation y = bf16(LN(x)(1 + scale) + shift) with F32
+ * scale/shift (modulated_norm, mot.cpp:147-159) when affine == 0; affine
+ * LayerNorm y = bf16(LN(x) w + b) with BF16 w/b (layer_norm, weights.cpp:919-930)
+ * when affine != 0. */
+WAM_B200_API int wam_b200_op_layernorm(const void* x, int rows, int cols, const void* a,
+                                       const void* b, float eps, int affine, void* y,
+                                       void* stream);
+
+/* Deterministic synthetic BF16 tensor (the generator behind synthetic weights):
+ * w[i] = bf16(f32(z_i) * f32(scale / sd) + f32(center)), z_i the Irwin-Hall(4)
+ * sum of the 16-bit lanes of splitmix64(tensor_seed + (i + 1) * golden) minus
+ * its mean. No reference counterpart (the reference loads trained weights). */
+WAM_B200_API int wam_b200_op_synth(void* w, long long n, uint64_t tensor_seed, double scale,
+                                   double center, void* stream);
+/* Seed of a synthetic tensor: splitmix64(seed ^ fnv1a64(name)). */
+WAM_B200_API uint64_t wam_b200_tensor_seed(uint64_t seed, const char* name);
+
+/* ------------------------------------------------- host-side arithmetic */
+
+/* Flow-match Euler schedule: timesteps [steps], sigmas [steps + 1]
+ * (make_flow_match_euler_schedule, src/models/common/scheduler.cpp:26-55). */
+WAM_B200_API int wam_b200_flow_schedule(int steps, float shift, float* timesteps, float* sigmas);
+/* Visual RoPE positions [gh * gw][3] = (t, h, w) (visual_positions,
+ * src/models/gwp05/semantics.cpp:235-257). */
+WAM_B200_API int wam_b200_visual_positions(int gh, int gw, int* thw);
+/* State normalisation to [-1, 1], zero-padded to `padded` (engine.cpp:249-253,
+ * normalize_and_pad_state, semantics.cpp:154-172). */
+WAM_B200_API int wam_b200_normalize_state(const float* state, int n, int padded, const float* q01,
+                                          const float* q99, float* out);
+/* Action de-normalisation plus delta dims 0-5 and 7-12 (engine.cpp:436-445,
+ * postprocess_action, semantics.cpp:178-208): out [steps][real]. */
+WAM_B200_API int wam_b200_postprocess_action(const float* action, int steps, int padded, int real,
+                                             const float* q01, const float* q99,
+                                             const float* raw_state, float* out);
+
+/* --------------------------------------------------------------- engine */
+
+typedef struct wam_b200_engine wam_b200_engine;
+
+/* Error detail of an engine call; message is malloc'd (free with
+ * wam_b200_status_free). Mirrors wam_rpc_result (src/serving/c_api.cpp:18-55). */
+typedef struct wam_b200_status {
+  int code;
+  char* message;
+} wam_b200_status;
+
+/* Model geometry (the gwp05.* GGUF keys, src/models/gwp05/artifact.cpp:20-94),
+ * plus prompt_tokens = cross-attention text length (the reference fixes it at
+ * 64, src/models/gwp05/semantics.h:11) and text_dim = gwp05.t5_hidden. */
+typedef struct wam_b200_geometry {
+  int hidden, layers, heads, ffn, action_hidden, action_ffn, action_dim;
+  int real_state_dim, real_action_dim, num_embodiments, embodiment_id;
+  int grid_h, grid_w, vae_z, action_chunk, steps, prompt_tokens, text_dim;
+  float norm_eps, flow_shift;
+} wam_b200_geometry;
+
+/* Engine options (struct_size-versioned like wam_rpc_model_options_v2,
+ * include/wam/c_api.h). With artifact_path NULL the engine generates
+ * deterministic synthetic weights from (synthetic_geometry, synthetic_seed). */
+typedef struct wam_b200_options {
+  uint32_t struct_size;
+  const char* artifact_path;
+  wam_b200_geometry synthetic_geometry;
+  uint64_t synthetic_seed;
+  float synthetic_bias_scale;
+  int device_index;
+  int max_batch;
+  int use_cuda_graphs;
+  int prompt_cache; /* reuse projected prompt K/V for an identical prompt */
+} wam_b200_options;
+
+/* One request (EngineInputsView, src/models/gwp05/engine/engine.h:91-105, with
+ * the precomputed latent and prompt embedding the external_embedding policy
+ * uses). Host pointers, borrowed for the call. */
+typedef struct wam_b200_request {
+  const float* state;      /* [state_n >= real_state_dim], un-normalised */
+  int state_n;
+  const float* noise;      /* [action_chunk * action_dim] or NULL (engine RNG) */
+  const float* ref_latent; /* [vae_z * 2 grid_h * 2 grid_w] */
+  long long ref_latent_n;
+  const float* prompt_emb; /* [prompt_tokens_in * text_dim], zero-padded to prompt_tokens */
+  int prompt_tokens;
+} wam_b200_request;
+
+typedef struct wam_b200_stats {
+  float ms_total;
+  float ms_device; /* prompt projection + prefix + denoise on the device */
+  int prompt_cache_hit;
+  int kernel_launches;
+  uint64_t resident_device_bytes;
+} wam_b200_stats;
+
+WAM_B200_API void wam_b200_status_free(wam_b200_status* status);
+
+/* engine::create (src/models/gwp05/engine/engine.h:202-203, impl engine.cpp:99-228). */
+WAM_B200_API int wam_b200_create(const wam_b200_options* options, wam_b200_engine** engine,
+                                 wam_b200_status* status);
+WAM_B200_API void wam_b200_destroy(wam_b200_engine* engine);
+/* Engine::reset (engine.h:146): drops the projected-prompt cache. */
+WAM_B200_API int wam_b200_reset(wam_b200_engine* engine);
+WAM_B200_API int wam_b200_geometry_of(const wam_b200_engine* engine, wam_b200_geometry* out);
+
+/* Engine::predict (engine.h:145, impl engine.cpp:230-449): one action chunk.
+ * action_out: [action_chunk * real_action_dim] de-normalised actions. */
+WAM_B200_API int wam_b200_predict(wam_b200_engine* engine, const wam_b200_request* request,
+                                  float* action_out, size_t action_out_n, wam_b200_stats* stats,
+                                  wam_b200_status* status);
+/* Batched predict (no reference counterpart; the reference is batch 1):
+ * action_out: [batch][action_chunk][real_action_dim]. */
+WAM_B200_API int wam_b200_predict_batch(wam_b200_engine* engine, const wam_b200_request* requests,
+                                        int batch, float* action_out, size_t action_out_n,
+                                        wam_b200_stats* stats, wam_b200_status* status);
+
+/* Split form of predict_batch for device-resident timing: stage (host->device
+ * inputs), run (enqueue prompt projection, prefix and denoise on the engine's
+ * stream, no host sync), fetch (sync, device->host, de-normalise). */
+WAM_B200_API int wam_b200_stage(wam_b200_engine* engine, const wam_b200_request* requests,
+                                int batch, wam_b200_status* status);
+WAM_B200_API int wam_b200_run(wam_b200_engine* engine, int batch, wam_b200_status* status);
+WAM_B200_API int wam_b200_fetch(wam_b200_engine* engine, const wam_b200_request* requests,
+                                int batch, float* action_out, size_t action_out_n,
+                                wam_b200_status* status);
+/* The engine's CUDA stream (cudaStream_t) for event timing. */
+WAM_B200_API void* wam_b200_stream(wam_b200_engine* engine);
+/* Kernels one chunk launches at this batch (with / without prompt projection). */
+WAM_B200_API int wam_b200_kernel_launches(wam_b200_engine* engine, int batch, int with_prompt);
+/* Stage dumps as F32 (the reference's WAM_GWP05_CACHE_DUMP_DIR stages,
+ * engine/cache.cpp:441-469): "prefix_k"/"prefix_v" [heads][1+V][128],
+ * "prompt_k"/"prompt_v" [heads][prompt_tokens][128] of one layer,
+ * "velocity" [steps][action_chunk][action_dim] (layer ignored). */
+WAM_B200_API int wam_b200_read_tensor(wam_b200_engine* engine, const char* name, int slot,
+                                      int layer, float* out, size_t out_n,
+                                      wam_b200_status* status);
+
 #ifdef __cplusplus
 }
 #endif

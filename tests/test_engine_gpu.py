@@ -1,0 +1,118 @@
+"""End-to-end parity of the CUDA engine against the CPU oracle (oracle/).
+
+Both sides use the same synthetic BF16 weights (bit-identical generator, see
+test_ops_gpu.py::test_synthetic_weights_bit_exact) and the same seeded inputs.
+Tolerances: per-layer K/V caches within 2e-2
+relative-L2, velocities and final action chunks within 5e-2 relative-L2.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+SEED = 20261201
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / (np.linalg.norm(b) + 1e-30))
+
+
+def _setup(geom, bias_scale=0.02, max_batch=1, graphs=True):
+    import oracle
+    from oracle import synth
+    from wam_b200.engine import Engine
+
+    w = synth.make_weights(geom, SEED, bias_scale=bias_scale)
+    om = oracle.OracleModel(geom, w)
+    eng = Engine(geom, seed=SEED, bias_scale=bias_scale, max_batch=max_batch, graphs=graphs,
+                 prompt_cache=False)
+    return om, eng
+
+
+def _req(geom, seed):
+    from oracle import synth
+    from wam_b200.engine import Req
+
+    r = synth.make_request(geom, seed)
+    return r, Req(r.state, r.latent, r.prompt, r.noise)
+
+
+@pytest.mark.parametrize("geom_name", ["TINY", "SMALL"])
+def test_engine_matches_oracle(cuda_device, geom_name):
+    from oracle import synth
+
+    geom = getattr(synth, geom_name)
+    om, eng = _setup(geom)
+    r, er = _req(geom, 11)
+    ref = om.predict(r, dumps=True)
+    out = eng.predict(er)
+    for layer in range(geom.layers):
+        for name in ("prefix_k", "prefix_v", "prompt_k", "prompt_v"):
+            got = eng.read_tensor(name, 0, layer)
+            err = rel_l2(got, ref[name][layer])
+            assert err < 2e-2, f"{name} layer {layer}: rel-L2 {err:.3e}"
+    vel = eng.read_tensor("velocity")
+    for s in range(geom.steps):
+        err = rel_l2(vel[s], ref["velocity"][s])
+        assert err < 5e-2, f"velocity step {s}: rel-L2 {err:.3e}"
+    assert np.isfinite(out).all()
+    assert rel_l2(out, ref["action"]) < 5e-2
+
+
+def test_graph_and_eager_identical(cuda_device):
+    from oracle import synth
+    from wam_b200.engine import Engine
+
+    geom = synth.TINY
+    r, er = _req(geom, 5)
+    a = Engine(geom, seed=SEED, bias_scale=0.02, graphs=True).predict(er)
+    b = Engine(geom, seed=SEED, bias_scale=0.02, graphs=False).predict(er)
+    assert np.array_equal(a, b)
+
+
+def test_batch_equals_single_requests(cuda_device):
+    from oracle import synth
+    from wam_b200.engine import Engine
+
+    geom = synth.TINY
+    eng = Engine(geom, seed=SEED, bias_scale=0.02, max_batch=3, prompt_cache=False)
+    reqs = [_req(geom, 100 + i)[1] for i in range(3)]
+    batched = eng.predict_batch(reqs)
+    for i, rq in enumerate(reqs):
+        single = eng.predict_batch([rq])[0]
+        assert rel_l2(single, batched[i]) < 1e-2
+
+
+def test_prompt_cache_hit_is_identical(cuda_device):
+    from oracle import synth
+    from wam_b200.engine import Engine
+
+    geom = synth.TINY
+    eng = Engine(geom, seed=SEED, bias_scale=0.02, prompt_cache=True)
+    _, rq = _req(geom, 9)
+    a, sa = eng.predict(rq, stats=True)
+    b, sb = eng.predict(rq, stats=True)
+    assert sa["prompt_cache_hit"] == 0 and sb["prompt_cache_hit"] == 1
+    assert np.array_equal(a, b)
+    eng.reset()
+    c, sc = eng.predict(rq, stats=True)
+    assert sc["prompt_cache_hit"] == 0 and np.array_equal(a, c)
+
+
+def test_invalid_inputs_fail_loudly(cuda_device):
+    from oracle import synth
+    from wam_b200.engine import Engine, EngineError, Req
+
+    geom = synth.TINY
+    eng = Engine(geom, seed=SEED)
+    r, rq = _req(geom, 3)
+    bad = r.state.copy()
+    bad[0] = np.nan
+    with pytest.raises(EngineError, match="NaN"):
+        eng.predict(Req(bad, r.latent, r.prompt, r.noise))
+    with pytest.raises(EngineError, match="latent"):
+        eng.predict(Req(r.state, r.latent[:1], r.prompt, r.noise))
+    # the engine stays usable after rejected requests
+    assert np.isfinite(eng.predict(rq)).all()

@@ -4,6 +4,7 @@
 #include <string>
 
 #include "c_api_util.h"
+#include "engine.h"
 #include "kernels.h"
 #include "wam_b200.h"
 
@@ -68,6 +69,12 @@ WAM_B200_API int wam_b200_op_gemm(const void* x, int ldx, int m, const void* w, 
     set_last_error(why);
     return rc;
   }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (gemm_init(dev) != cudaSuccess) {
+    set_last_error("gemm_init failed");
+    return WAM_B200_CUDA_ERROR;
+  }
   GemmScratch scratch;
   scratch.workspace = workspace;
   scratch.workspace_floats = workspace_floats;
@@ -89,6 +96,99 @@ WAM_B200_API int wam_b200_op_gemm(const void* x, int ldx, int m, const void* w, 
     return WAM_B200_CUDA_ERROR;
   }
   return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_op_attention(const void* q, long long q_seq_stride,
+                                       long long q_head_stride, const void* k, const void* v,
+                                       long long kv_seq_stride, long long kv_head_stride, int lq,
+                                       int lk, int heads, int batch, float scale, void* out,
+                                       int ldo, void* stream) {
+  std::string why;
+  int rc = check_sm100(&why);
+  if (rc != WAM_B200_OK) {
+    set_last_error(why);
+    return rc;
+  }
+  if (lq < 1 || lk < 1 || heads < 1 || batch < 1 || ldo < heads * 128) {
+    set_last_error("attention: bad shape");
+    return WAM_B200_INVALID_ARGUMENT;
+  }
+  if (attention_init() != cudaSuccess) {
+    set_last_error("attention_init failed");
+    return WAM_B200_CUDA_ERROR;
+  }
+  AttnArgs a{};
+  a.q = static_cast<const bf16*>(q);
+  a.q_seq_stride = q_seq_stride;
+  a.q_head_stride = q_head_stride;
+  a.k = static_cast<const bf16*>(k);
+  a.v = static_cast<const bf16*>(v);
+  a.kv_seq_stride = kv_seq_stride;
+  a.kv_head_stride = kv_head_stride;
+  a.lq = lq;
+  a.lk = lk;
+  a.heads = heads;
+  a.batch = batch;
+  a.scale = scale;
+  a.out = static_cast<bf16*>(out);
+  a.ldo = ldo;
+  launch_attention(a, static_cast<cudaStream_t>(stream));
+  cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) {
+    set_last_error(std::string("attention launch: ") + cudaGetErrorString(ce));
+    return WAM_B200_CUDA_ERROR;
+  }
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_op_layernorm(const void* x, int rows, int cols, const void* a,
+                                       const void* b, float eps, int affine, void* y,
+                                       void* stream) {
+  std::string why;
+  int rc = check_sm100(&why);
+  if (rc != WAM_B200_OK) {
+    set_last_error(why);
+    return rc;
+  }
+  if (rows < 1 || cols < 8 || cols % 8) {
+    set_last_error("layernorm: cols must be a positive multiple of 8");
+    return WAM_B200_INVALID_ARGUMENT;
+  }
+  if (affine)
+    launch_ln_affine(static_cast<const bf16*>(x), cols, rows, cols, static_cast<const bf16*>(a),
+                     static_cast<const bf16*>(b), eps, static_cast<bf16*>(y), cols,
+                     static_cast<cudaStream_t>(stream));
+  else
+    launch_ln_modulate(static_cast<const bf16*>(x), cols, rows, cols, static_cast<const float*>(a),
+                       static_cast<const float*>(b), eps, static_cast<bf16*>(y), cols,
+                       static_cast<cudaStream_t>(stream));
+  cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) {
+    set_last_error(std::string("layernorm launch: ") + cudaGetErrorString(ce));
+    return WAM_B200_CUDA_ERROR;
+  }
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_op_synth(void* w, long long n, uint64_t seed, double scale,
+                                   double center, void* stream) {
+  std::string why;
+  int rc = check_sm100(&why);
+  if (rc != WAM_B200_OK) {
+    set_last_error(why);
+    return rc;
+  }
+  launch_synth_bf16(static_cast<bf16*>(w), n, seed, scale, center, static_cast<cudaStream_t>(stream));
+  cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) {
+    set_last_error(std::string("synth launch: ") + cudaGetErrorString(ce));
+    return WAM_B200_CUDA_ERROR;
+  }
+  return WAM_B200_OK;
+}
+
+WAM_B200_API uint64_t wam_b200_tensor_seed(uint64_t seed, const char* name) {
+  return tensor_seed(seed, name ? name : "");
 }
 
 }  // extern "C"

@@ -1,0 +1,360 @@
+// HBM-bound row and elementwise kernels of the MoT forward pass: LayerNorm +
+// AdaLN modulation, affine LayerNorm, q/k RMSNorm + RoPE + scatter, the small
+// encoder/decoder projections, modulation tables, patchify, the Euler update
+// and the deterministic synthetic-weight generator. Rows are processed by one
+// warp each with 16-byte vector loads; reductions use warp shuffles.
+#include <cmath>
+#include <cstdint>
+
+#include "kernels.h"
+#include "mathops.cuh"
+
+namespace wamb {
+
+namespace {
+
+struct alignas(16) Bf16x8 {
+  __nv_bfloat162 v[4];
+};
+
+__device__ __forceinline__ void load8(const bf16* p, float (&f)[8]) {
+  const Bf16x8 x = *reinterpret_cast<const Bf16x8*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(x.v[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ void store8(bf16* p, const float (&f)[8]) {
+  Bf16x8 x;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x.v[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  *reinterpret_cast<Bf16x8*>(p) = x;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+constexpr int kRowsPerBlock = 8;
+
+// mode 0: AdaLN  y = bf16(n * (1 + scale) + shift), scale/shift F32
+// mode 1: affine y = bf16(n * w + b), w/b BF16
+template <int MODE>
+__global__ void __launch_bounds__(kRowsPerBlock * 32)
+    ln_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
+              const void* pb, float eps, bf16* __restrict__ y, int ldy) {
+  const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const bf16* xr = x + static_cast<long long>(row) * ldx;
+  const int chunks = cols >> 3;
+  float s = 0.0f;
+  for (int c = lane; c < chunks; c += 32) {
+    float f[8];
+    load8(xr + c * 8, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += f[i];
+  }
+  const float mean = warp_sum(s) / cols;
+  float v = 0.0f;
+  for (int c = lane; c < chunks; c += 32) {
+    float f[8];
+    load8(xr + c * 8, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float d = f[i] - mean;
+      v += d * d;
+    }
+  }
+  const float inv_std = rsqrtf(warp_sum(v) / cols + eps);
+  bf16* yr = y + static_cast<long long>(row) * ldy;
+  for (int c = lane; c < chunks; c += 32) {
+    float f[8];
+    load8(xr + c * 8, f);
+    if (MODE == 0) {
+      const float4* sc = reinterpret_cast<const float4*>(static_cast<const float*>(pa) + c * 8);
+      const float4* sh = reinterpret_cast<const float4*>(static_cast<const float*>(pb) + c * 8);
+      const float4 s0 = sc[0], s1 = sc[1], h0 = sh[0], h1 = sh[1];
+      const float scl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      const float shf[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = fmaf((f[i] - mean) * inv_std, 1.0f + scl[i], shf[i]);
+    } else {
+      float w[8], b[8];
+      load8(static_cast<const bf16*>(pa) + c * 8, w);
+      load8(static_cast<const bf16*>(pb) + c * 8, b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = fmaf((f[i] - mean) * inv_std, w[i], b[i]);
+    }
+    store8(yr + c * 8, f);
+  }
+}
+
+// One block of 3 warps per token row: warp 0 = q, 1 = k, 2 = v.
+__global__ void __launch_bounds__(96) qkv_scatter_kernel(const QkvScatter a) {
+  const int row = blockIdx.x;
+  const int which = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int col = which == 0 ? a.q_col : (which == 1 ? a.k_col : a.v_col);
+  if (col < 0) return;
+  const bf16* src = a.src + static_cast<long long>(row) * a.ld_src + col;
+  const int seq = row / a.rows_per_seq;
+  const int rin = row - seq * a.rows_per_seq;
+  const int chunks = a.hidden >> 3;
+  bf16* dst_base;
+  long long head_stride;
+  if (which == 0) {
+    dst_base = a.q_out + seq * a.q_seq_stride + static_cast<long long>(a.q_row_offset + rin) * 128;
+    head_stride = a.q_head_stride;
+  } else {
+    dst_base = (which == 1 ? a.k_out : a.v_out) + seq * a.kv_seq_stride +
+               static_cast<long long>(a.kv_row_offset + rin) * 128;
+    head_stride = a.kv_head_stride;
+  }
+  if (which == 2) {
+    for (int c = lane; c < chunks; c += 32) {
+      const int d = c * 8;
+      *reinterpret_cast<Bf16x8*>(dst_base + (d >> 7) * head_stride + (d & 127)) =
+          *reinterpret_cast<const Bf16x8*>(src + d);
+    }
+    return;
+  }
+  const bf16* nw = which == 0 ? a.q_norm : a.k_norm;
+  float inv = 1.0f;
+  if (nw) {
+    float ss = 0.0f;
+    for (int c = lane; c < chunks; c += 32) {
+      float f[8];
+      load8(src + c * 8, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    }
+    inv = rsqrtf(warp_sum(ss) / a.hidden + a.eps);
+  }
+  int pt = 0, ph = 0, pw = 0;
+  if (a.rope_mode == 2) {
+    pt = a.pos_thw[rin * 3 + 0];
+    ph = a.pos_thw[rin * 3 + 1];
+    pw = a.pos_thw[rin * 3 + 2];
+  }
+  const int pos1 = a.pos_base + rin;
+  for (int c = lane; c < chunks; c += 32) {
+    const int d = c * 8;
+    const int hd = d & 127;
+    float f[8];
+    load8(src + d, f);
+    if (nw) {
+      float w[8];
+      load8(nw + d, w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = f[i] * inv * w[i];
+    }
+    if (a.rope_mode != 0) {
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int dim = hd + 2 * p;
+        float theta;
+        if (a.rope_mode == 1) {
+          theta = static_cast<float>(pos1) * a.inv_freq[dim >> 1];
+        } else if (dim < 44) {
+          theta = static_cast<float>(pt) * a.inv_freq[dim >> 1];
+        } else if (dim < 86) {
+          theta = static_cast<float>(ph) * a.inv_freq[22 + ((dim - 44) >> 1)];
+        } else {
+          theta = static_cast<float>(pw) * a.inv_freq[43 + ((dim - 86) >> 1)];
+        }
+        float sn, cs;
+        sincosf(theta, &sn, &cs);
+        const float x0 = f[2 * p], x1 = f[2 * p + 1];
+        f[2 * p] = x0 * cs - x1 * sn;
+        f[2 * p + 1] = x0 * sn + x1 * cs;
+      }
+    }
+    store8(dst_base + (d >> 7) * head_stride + hd, f);
+  }
+}
+
+// One warp per output element.
+__global__ void small_linear_kernel(const bf16* __restrict__ x, int ldx, int m, int k,
+                                    const bf16* __restrict__ w, long long w_sn, long long w_sk,
+                                    const bf16* __restrict__ b, int n, int act,
+                                    bf16* __restrict__ y, int ldy) {
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const int lane = threadIdx.x & 31;
+  for (long long o = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       o < static_cast<long long>(m) * n; o += warps) {
+    const int mi = static_cast<int>(o / n);
+    const int ni = static_cast<int>(o - static_cast<long long>(mi) * n);
+    const bf16* xr = x + static_cast<long long>(mi) * ldx;
+    const bf16* wr = w + ni * w_sn;
+    float acc = 0.0f;
+    for (int kk = lane; kk < k; kk += 32)
+      acc += __bfloat162float(xr[kk]) * __bfloat162float(wr[kk * w_sk]);
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      float v = bf16_round(acc);
+      if (b) v = bf16_round(v + __bfloat162float(b[ni]));
+      if (act == ACT_GELU_ERF) v = gelu_erf(v);
+      y[static_cast<long long>(mi) * ldy + ni] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+__global__ void modulation_add_kernel(const bf16* __restrict__ mod, int ld_mod, int period,
+                                      int steps, const bf16* const* __restrict__ tables,
+                                      int layers, int width, float* __restrict__ out) {
+  const long long total = static_cast<long long>(steps) * layers * width;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int j = static_cast<int>(i % width);
+    const long long sl = i / width;
+    const int l = static_cast<int>(sl % layers);
+    const int s = static_cast<int>(sl / layers);
+    out[i] = __bfloat162float(mod[static_cast<long long>(s) * ld_mod + (j % period)]) +
+             __bfloat162float(tables[l][j]);
+  }
+}
+
+__global__ void silu_kernel(const bf16* __restrict__ x, bf16* __restrict__ y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __float2bfloat16_rn(silu(__bfloat162float(x[i])));
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ x, bf16* __restrict__ y, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    y[i] = __float2bfloat16_rn(x[i]);
+}
+
+__global__ void bf16_to_f32_kernel(const bf16* __restrict__ x, float* __restrict__ y, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    y[i] = __bfloat162float(x[i]);
+}
+
+__global__ void patchify_kernel(const float* __restrict__ lat, int batch, int ch, int gh, int gw,
+                                bf16* __restrict__ cols) {
+  const int kk = ch * 4;
+  const long long total = static_cast<long long>(batch) * gh * gw * kk;
+  const int lh = 2 * gh, lw = 2 * gw;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int q = static_cast<int>(i % kk);
+    const long long bt = i / kk;
+    const int t = static_cast<int>(bt % (gh * gw));
+    const int b = static_cast<int>(bt / (gh * gw));
+    const int c = q >> 2, dy = (q >> 1) & 1, dx = q & 1;
+    const int y = t / gw, x = t - (t / gw) * gw;
+    const float v = lat[((static_cast<long long>(b) * ch + c) * lh + 2 * y + dy) * lw + 2 * x + dx];
+    cols[i] = __float2bfloat16_rn(v);
+  }
+}
+
+// ggml_add(action, ggml_mul(velocity, dt)) in F32, stored BF16 (weights.cpp:897-901).
+__global__ void euler_kernel(bf16* __restrict__ a, const bf16* __restrict__ v, int n,
+                             const float* __restrict__ dt) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float prod = __fmul_rn(__bfloat162float(v[i]), *dt);
+    a[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(a[i]), prod));
+  }
+}
+
+__device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void synth_kernel(bf16* __restrict__ w, long long n, unsigned long long seed, float k,
+                             float center) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const unsigned long long h =
+        mix64(seed + static_cast<unsigned long long>(i + 1) * 0x9E3779B97F4A7C15ull);
+    const int z = static_cast<int>((h & 0xFFFFull) + ((h >> 16) & 0xFFFFull) +
+                                   ((h >> 32) & 0xFFFFull) + (h >> 48)) -
+                  131070;
+    const float v = __fadd_rn(__fmul_rn(static_cast<float>(z), k), center);
+    w[i] = __float2bfloat16_rn(v);
+  }
+}
+
+inline int grid_for(long long n, int threads) {
+  long long g = (n + threads - 1) / threads;
+  if (g > 148 * 32) g = 148 * 32;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+}  // namespace
+
+void launch_ln_modulate(const bf16* x, int ldx, int rows, int cols, const float* scale,
+                        const float* shift, float eps, bf16* y, int ldy, cudaStream_t s) {
+  const int grid = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
+  ln_kernel<0><<<grid, kRowsPerBlock * 32, 0, s>>>(x, ldx, rows, cols, scale, shift, eps, y, ldy);
+}
+
+void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w, const bf16* b,
+                      float eps, bf16* y, int ldy, cudaStream_t s) {
+  const int grid = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
+  ln_kernel<1><<<grid, kRowsPerBlock * 32, 0, s>>>(x, ldx, rows, cols, w, b, eps, y, ldy);
+}
+
+void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s) {
+  qkv_scatter_kernel<<<a.rows, 96, 0, s>>>(a);
+}
+
+void launch_small_linear(const bf16* x, int ldx, int m, int k, const bf16* w, long long w_sn,
+                         long long w_sk, const bf16* b, int n, int act, bf16* y, int ldy,
+                         cudaStream_t s) {
+  const long long outs = static_cast<long long>(m) * n;
+  small_linear_kernel<<<grid_for(outs * 32, 256), 256, 0, s>>>(x, ldx, m, k, w, w_sn, w_sk, b, n,
+                                                               act, y, ldy);
+}
+
+void launch_modulation_add(const bf16* mod, int ld_mod, int period, int steps,
+                           const bf16* const* tables, int layers, int width, float* combined,
+                           cudaStream_t s) {
+  const long long n = static_cast<long long>(steps) * layers * width;
+  modulation_add_kernel<<<grid_for(n, 256), 256, 0, s>>>(mod, ld_mod, period, steps, tables,
+                                                          layers, width, combined);
+}
+
+void launch_silu(const bf16* x, bf16* y, int n, cudaStream_t s) {
+  silu_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, y, n);
+}
+
+void launch_f32_to_bf16(const float* x, bf16* y, long long n, cudaStream_t s) {
+  f32_to_bf16_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n);
+}
+
+void launch_bf16_to_f32(const bf16* x, float* y, long long n, cudaStream_t s) {
+  bf16_to_f32_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n);
+}
+
+void launch_patchify(const float* latent, int batch, int channels, int gh, int gw, bf16* cols,
+                     cudaStream_t s) {
+  const long long n = static_cast<long long>(batch) * gh * gw * channels * 4;
+  patchify_kernel<<<grid_for(n, 256), 256, 0, s>>>(latent, batch, channels, gh, gw, cols);
+}
+
+void launch_euler(bf16* action, const bf16* velocity, int n, const float* dt, cudaStream_t s) {
+  euler_kernel<<<(n + 255) / 256, 256, 0, s>>>(action, velocity, n, dt);
+}
+
+void launch_synth_bf16(bf16* w, long long n, unsigned long long seed, double scale, double center,
+                       cudaStream_t s) {
+  // Unit-variance scaling of the Irwin-Hall(4) sum of 16-bit uniforms, rounded
+  // to F32 once so host (numpy) and device apply the same constant.
+  const double ih4_std = std::sqrt(4.0 * (65536.0 * 65536.0 - 1.0) / 12.0);
+  const float k = static_cast<float>(scale / ih4_std);
+  synth_kernel<<<grid_for(n, 256), 256, 0, s>>>(w, n, seed, k, static_cast<float>(center));
+}
+
+}  // namespace wamb

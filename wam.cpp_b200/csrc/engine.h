@@ -1,0 +1,172 @@
+// B200 MoT engine: the C++ object behind the wam_b200_* C ABI. It plays the
+// role of the reference's Gwp05ModelArch (src/models/gwp05/engine/weights.cpp:339-462,
+// engine.cpp:99-449): owns the device weights, the prefix and prompt K/V caches,
+// and runs prefix + flow-matching denoise for a batch of requests.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <functional>
+#include <map>
+#include <memory>
+#include <random>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "kernels.h"
+
+namespace wamb {
+
+struct Geometry {
+  int hidden = 3072, layers = 30, heads = 24, ffn = 14336;
+  int action_hidden = 3072, action_ffn = 14336, action_dim = 32;
+  int real_state_dim = 14, real_action_dim = 14, num_embodiments = 1, embodiment_id = 0;
+  int grid_h = 32, grid_w = 24, vae_z = 48;
+  int action_chunk = 48, steps = 10, prompt_tokens = 64, text_dim = 4096;
+  float norm_eps = 1e-6f, flow_shift = 5.0f;
+  int visual() const { return grid_h * grid_w; }
+  int prefix() const { return 1 + visual(); }
+};
+
+struct EngineOptions {
+  std::string artifact_path;  // empty: synthetic weights from (geometry, seed)
+  Geometry synthetic;
+  uint64_t seed = 0;
+  double bias_scale = 0.0;
+  int device = 0;
+  int max_batch = 1;
+  bool graphs = true;
+  bool prompt_cache = true;
+};
+
+struct RequestView {
+  const float* state = nullptr;
+  int state_n = 0;
+  const float* noise = nullptr;  // [T * A] or null
+  const float* latent = nullptr;
+  long long latent_n = 0;
+  const float* prompt = nullptr;  // [prompt_tokens_in * text_dim]
+  int prompt_tokens = 0;
+};
+
+struct EngineStats {
+  float ms_total = 0, ms_h2d = 0, ms_prompt = 0, ms_prefix = 0, ms_denoise = 0, ms_d2h = 0;
+  int prompt_cache_hit = 0;
+};
+
+using Launch = std::function<cudaError_t(cudaStream_t)>;
+
+struct Program {
+  std::vector<Launch> ops;
+  int kernels = 0;
+};
+
+// Synthetic tensor distribution rule (scale, center); mirrors init_rule() of
+// the test fixtures' generator.
+void synth_rule(const std::string& name, double bias_scale, double* scale, double* center);
+// (name, element count) of every BF16 tensor the MoT path reads.
+std::vector<std::pair<std::string, int64_t>> tensor_specs(const Geometry& g);
+uint64_t tensor_seed(uint64_t seed, const std::string& name);
+
+class MotEngine {
+ public:
+  static std::unique_ptr<MotEngine> create(const EngineOptions& opt, std::string* err);
+  ~MotEngine();
+
+  const Geometry& geometry() const { return g_; }
+  cudaStream_t stream() const { return stream_; }
+  uint64_t resident_bytes() const { return resident_bytes_; }
+
+  // H2D of a batch's inputs (normalises state on the host, pads the prompt).
+  bool stage(const RequestView* reqs, int batch, std::string* err);
+  // Enqueues prompt projection (unless cached), prefix and denoise.
+  bool run(int batch, std::string* err, EngineStats* stats = nullptr);
+  // Waits, reads the device error word, copies actions back and
+  // de-normalises them: out [batch][T][real_action_dim].
+  bool fetch(const RequestView* reqs, int batch, float* out, std::string* err);
+  bool predict(const RequestView* reqs, int batch, float* out, EngineStats* stats, std::string* err);
+  void reset();
+  int kernels_per_chunk(int batch, bool with_prompt);
+  // Debug view of device state as F32 (names: prefix_k, prefix_v, prompt_k,
+  // prompt_v, velocity, actions).
+  bool read_tensor(const std::string& name, int slot, int layer, float* out, size_t n,
+                   std::string* err);
+
+ private:
+  MotEngine() = default;
+  bool init(const EngineOptions& opt, std::string* err);
+  bool load_weights(std::string* err);
+  bool alloc_buffers(std::string* err);
+  const bf16* W(const std::string& name, int64_t numel);
+  bool build(int batch, std::string* err);
+  bool gemm(Program& p, const bf16* x, int ldx, int m, const std::string& wname, int n, int k,
+            int epi, bool bias, const float* gate, const bf16* resid, int ldr, void* out, int ldo,
+            std::string* err);
+
+  struct Plan {
+    Program prompt, main;
+    cudaGraphExec_t g_prompt = nullptr, g_main = nullptr;
+    int scratch_gen = 0;  // split-K scratch generation the launches point into
+  };
+  void drop_plans();
+  int scratch_gen_ = 0;
+
+  EngineOptions opt_;
+  Geometry g_;
+  int sms_ = 148;
+  cudaStream_t stream_ = nullptr;
+  bool ok_ = false;
+  std::string loader_;
+
+  // weights
+  void* warena_ = nullptr;
+  size_t warena_bytes_ = 0;
+  std::unordered_map<std::string, bf16*> w_;
+  std::unordered_map<std::string, int64_t> wn_;
+  std::vector<float> sq01_, sq99_, aq01_, aq99_;
+  uint64_t resident_bytes_ = 0;
+
+  // device buffers (sized for max_batch)
+  std::vector<void*> allocs_;
+  template <class T>
+  T* dalloc(size_t n, std::string* err);
+
+  float *in_state_ = nullptr, *in_latent_ = nullptr, *in_prompt_ = nullptr, *in_noise_ = nullptr;
+  float *h_state_ = nullptr, *h_latent_ = nullptr, *h_prompt_ = nullptr, *h_noise_ = nullptr;
+  float *h_out_ = nullptr, *d_out_ = nullptr;
+  bf16 *prompt_bf_ = nullptr, *state_bf_ = nullptr, *action_bf_ = nullptr;
+  bf16 *text_tmp_ = nullptr, *text_a_ = nullptr, *text_v_ = nullptr, *ckv_ = nullptr;
+  bf16 *cols_ = nullptr, *hv_ = nullptr, *hs_ = nullptr, *ha_ = nullptr;
+  bf16 *nrm_ = nullptr, *nrm_s_ = nullptr, *qkv_ = nullptr, *qkv_s_ = nullptr;
+  bf16 *qbuf_ = nullptr, *att_ = nullptr, *att_s_ = nullptr, *cq_ = nullptr, *cq_s_ = nullptr;
+  bf16 *qc_ = nullptr, *qc_s_ = nullptr, *catt_ = nullptr, *catt_s_ = nullptr;
+  bf16 *ffn_ = nullptr, *ffn_s_ = nullptr, *s1_ = nullptr, *s2_ = nullptr;
+  bf16 *e1_ = nullptr, *e2_ = nullptr, *d1_ = nullptr, *d2_ = nullptr, *vel_ = nullptr;
+  bf16 *freq_bf_ = nullptr, *ct1_ = nullptr, *temb_a_ = nullptr, *ct2_ = nullptr, *mod_a_ = nullptr;
+  bf16 *cv1_ = nullptr, *temb_v_ = nullptr, *cv2_ = nullptr, *mod_v_ = nullptr;
+  float *comb_a0_ = nullptr, *comb_v_ = nullptr, *comb_steps_ = nullptr, *comb_final_ = nullptr;
+  float *dt_ = nullptr, *inv_freq1_ = nullptr, *inv_freq3_ = nullptr;
+  int* pos_thw_ = nullptr;
+  const bf16** tables_a_ = nullptr;
+  const bf16** tables_v_ = nullptr;
+  const bf16** tables_final_ = nullptr;
+  bf16 *k_self_ = nullptr, *v_self_ = nullptr;      // [B][L][heads][P+T][128]
+  bf16 *k_prompt_ = nullptr, *v_prompt_ = nullptr;  // [B][L][heads][Nt][128] (action expert)
+  bf16 *k_vis_ = nullptr, *v_vis_ = nullptr;        // [B][L][heads][Nt][128] (visual expert)
+  float* ws_ = nullptr;
+  size_t ws_floats_ = 0;
+  unsigned* counters_ = nullptr;
+  int counter_slots_ = 0;
+  unsigned* err_word_ = nullptr;
+
+  std::vector<float> timesteps_, sigmas_;
+  std::map<int, std::unique_ptr<Plan>> plans_;
+  std::vector<std::vector<float>> prompt_sig_;  // per slot, last projected prompt
+  bool prompt_valid_ = false;
+  int staged_batch_ = 0;
+  std::mt19937 rng_{0x5eed};
+};
+
+}  // namespace wamb

@@ -1,0 +1,212 @@
+// Engine-level C ABI (include/wam_b200.h): wraps MotEngine with the reference
+// C ABI's conventions (int return codes, malloc'd status messages,
+// src/serving/c_api.cpp:18-55) and translates its structs.
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "c_api_util.h"
+#include "engine.h"
+#include "wam_b200.h"
+
+struct wam_b200_engine {
+  std::unique_ptr<wamb::MotEngine> impl;
+};
+
+namespace {
+
+int fail(wam_b200_status* st, int code, const std::string& msg) {
+  wamb::set_last_error(msg);
+  if (st) {
+    st->code = code;
+    st->message = static_cast<char*>(std::malloc(msg.size() + 1));
+    if (st->message) std::memcpy(st->message, msg.c_str(), msg.size() + 1);
+  }
+  return code;
+}
+
+int ok(wam_b200_status* st) {
+  if (st) {
+    st->code = WAM_B200_OK;
+    st->message = nullptr;
+  }
+  return WAM_B200_OK;
+}
+
+wamb::Geometry to_geometry(const wam_b200_geometry& g) {
+  wamb::Geometry o;
+  o.hidden = g.hidden;
+  o.layers = g.layers;
+  o.heads = g.heads;
+  o.ffn = g.ffn;
+  o.action_hidden = g.action_hidden;
+  o.action_ffn = g.action_ffn;
+  o.action_dim = g.action_dim;
+  o.real_state_dim = g.real_state_dim;
+  o.real_action_dim = g.real_action_dim;
+  o.num_embodiments = g.num_embodiments;
+  o.embodiment_id = g.embodiment_id;
+  o.grid_h = g.grid_h;
+  o.grid_w = g.grid_w;
+  o.vae_z = g.vae_z;
+  o.action_chunk = g.action_chunk;
+  o.steps = g.steps;
+  o.prompt_tokens = g.prompt_tokens;
+  o.text_dim = g.text_dim;
+  o.norm_eps = g.norm_eps;
+  o.flow_shift = g.flow_shift;
+  return o;
+}
+
+std::vector<wamb::RequestView> views(const wam_b200_request* r, int n) {
+  std::vector<wamb::RequestView> v(n > 0 ? n : 0);
+  for (int i = 0; i < n; ++i) {
+    v[i].state = r[i].state;
+    v[i].state_n = r[i].state_n;
+    v[i].noise = r[i].noise;
+    v[i].latent = r[i].ref_latent;
+    v[i].latent_n = r[i].ref_latent_n;
+    v[i].prompt = r[i].prompt_emb;
+    v[i].prompt_tokens = r[i].prompt_tokens;
+  }
+  return v;
+}
+
+int code_of(const std::string& err) {
+  if (err.find("timed out") != std::string::npos) return WAM_B200_DEVICE_TIMEOUT;
+  if (err.find("cuda") != std::string::npos || err.find("graph") != std::string::npos)
+    return WAM_B200_CUDA_ERROR;
+  return WAM_B200_INFERENCE_FAILED;
+}
+
+}  // namespace
+
+extern "C" {
+
+WAM_B200_API void wam_b200_status_free(wam_b200_status* st) {
+  if (st && st->message) {
+    std::free(st->message);
+    st->message = nullptr;
+  }
+}
+
+WAM_B200_API int wam_b200_create(const wam_b200_options* o, wam_b200_engine** out,
+                                 wam_b200_status* st) {
+  if (!o || !out) return fail(st, WAM_B200_INVALID_ARGUMENT, "options and engine pointer are required");
+  if (o->struct_size < sizeof(wam_b200_options))
+    return fail(st, WAM_B200_INVALID_ARGUMENT, "wam_b200_options.struct_size is too small");
+  *out = nullptr;
+  wamb::EngineOptions eo;
+  if (o->artifact_path) eo.artifact_path = o->artifact_path;
+  eo.synthetic = to_geometry(o->synthetic_geometry);
+  eo.seed = o->synthetic_seed;
+  eo.bias_scale = o->synthetic_bias_scale;
+  eo.device = o->device_index;
+  eo.max_batch = o->max_batch;
+  eo.graphs = o->use_cuda_graphs != 0;
+  eo.prompt_cache = o->prompt_cache != 0;
+  std::string err;
+  auto e = wamb::MotEngine::create(eo, &err);
+  if (!e) {
+    const int code = err.find("artifact") != std::string::npos || err.find("GGUF") != std::string::npos
+                         ? WAM_B200_ARTIFACT_ERROR
+                         : (err.find("sm_100") != std::string::npos ? WAM_B200_UNSUPPORTED
+                                                                    : WAM_B200_INVALID_ARGUMENT);
+    return fail(st, code, err);
+  }
+  *out = new wam_b200_engine{std::move(e)};
+  return ok(st);
+}
+
+WAM_B200_API void wam_b200_destroy(wam_b200_engine* e) { delete e; }
+
+WAM_B200_API int wam_b200_reset(wam_b200_engine* e) {
+  if (!e) return WAM_B200_INVALID_ARGUMENT;
+  e->impl->reset();
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_geometry_of(const wam_b200_engine* e, wam_b200_geometry* out) {
+  if (!e || !out) return WAM_B200_INVALID_ARGUMENT;
+  const wamb::Geometry& g = e->impl->geometry();
+  *out = wam_b200_geometry{g.hidden, g.layers, g.heads, g.ffn, g.action_hidden, g.action_ffn,
+                           g.action_dim, g.real_state_dim, g.real_action_dim, g.num_embodiments,
+                           g.embodiment_id, g.grid_h, g.grid_w, g.vae_z, g.action_chunk, g.steps,
+                           g.prompt_tokens, g.text_dim, g.norm_eps, g.flow_shift};
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_predict_batch(wam_b200_engine* e, const wam_b200_request* r, int batch,
+                                        float* out, size_t n, wam_b200_stats* stats,
+                                        wam_b200_status* st) {
+  if (!e || !r || !out) return fail(st, WAM_B200_INVALID_ARGUMENT, "engine, requests and output are required");
+  const wamb::Geometry& g = e->impl->geometry();
+  if (n < static_cast<size_t>(batch) * g.action_chunk * g.real_action_dim)
+    return fail(st, WAM_B200_INVALID_ARGUMENT, "action output buffer is too small");
+  auto v = views(r, batch);
+  wamb::EngineStats es;
+  std::string err;
+  if (!e->impl->predict(v.data(), batch, out, &es, &err)) return fail(st, code_of(err), err);
+  if (stats) {
+    stats->ms_total = es.ms_total;
+    stats->ms_device = es.ms_denoise;
+    stats->prompt_cache_hit = es.prompt_cache_hit;
+    stats->kernel_launches = e->impl->kernels_per_chunk(batch, !es.prompt_cache_hit);
+    stats->resident_device_bytes = e->impl->resident_bytes();
+  }
+  return ok(st);
+}
+
+WAM_B200_API int wam_b200_predict(wam_b200_engine* e, const wam_b200_request* r, float* out,
+                                  size_t n, wam_b200_stats* stats, wam_b200_status* st) {
+  return wam_b200_predict_batch(e, r, 1, out, n, stats, st);
+}
+
+WAM_B200_API int wam_b200_stage(wam_b200_engine* e, const wam_b200_request* r, int batch,
+                                wam_b200_status* st) {
+  if (!e || !r) return fail(st, WAM_B200_INVALID_ARGUMENT, "engine and requests are required");
+  auto v = views(r, batch);
+  std::string err;
+  if (!e->impl->stage(v.data(), batch, &err)) return fail(st, WAM_B200_INVALID_ARGUMENT, err);
+  return ok(st);
+}
+
+WAM_B200_API int wam_b200_run(wam_b200_engine* e, int batch, wam_b200_status* st) {
+  if (!e) return fail(st, WAM_B200_INVALID_ARGUMENT, "engine is required");
+  std::string err;
+  if (!e->impl->run(batch, &err)) return fail(st, code_of(err), err);
+  return ok(st);
+}
+
+WAM_B200_API int wam_b200_fetch(wam_b200_engine* e, const wam_b200_request* r, int batch,
+                                float* out, size_t n, wam_b200_status* st) {
+  if (!e || !r || !out) return fail(st, WAM_B200_INVALID_ARGUMENT, "engine, requests and output are required");
+  const wamb::Geometry& g = e->impl->geometry();
+  if (n < static_cast<size_t>(batch) * g.action_chunk * g.real_action_dim)
+    return fail(st, WAM_B200_INVALID_ARGUMENT, "action output buffer is too small");
+  auto v = views(r, batch);
+  std::string err;
+  if (!e->impl->fetch(v.data(), batch, out, &err)) return fail(st, code_of(err), err);
+  return ok(st);
+}
+
+WAM_B200_API void* wam_b200_stream(wam_b200_engine* e) {
+  return e ? static_cast<void*>(e->impl->stream()) : nullptr;
+}
+
+WAM_B200_API int wam_b200_kernel_launches(wam_b200_engine* e, int batch, int with_prompt) {
+  return e ? e->impl->kernels_per_chunk(batch, with_prompt != 0) : -1;
+}
+
+WAM_B200_API int wam_b200_read_tensor(wam_b200_engine* e, const char* name, int slot, int layer,
+                                      float* out, size_t n, wam_b200_status* st) {
+  if (!e || !name || !out) return fail(st, WAM_B200_INVALID_ARGUMENT, "engine, name and output are required");
+  std::string err;
+  if (!e->impl->read_tensor(name, slot, layer, out, n, &err))
+    return fail(st, WAM_B200_INVALID_ARGUMENT, err);
+  return ok(st);
+}
+
+}  // extern "C"

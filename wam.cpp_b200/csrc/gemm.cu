@@ -20,6 +20,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "kernels.h"
 #include "mathops.cuh"
@@ -84,6 +85,18 @@ __device__ __forceinline__ void store_out(const GemmArgs& a, int m, int n, float
     }
     case EPI_F32_BIAS: {
       out[o] = __float2bfloat16_rn(acc + b);
+      break;
+    }
+    case EPI_BIAS_GELU_R: {
+      float v = bf16_round(acc);
+      if (a.bias) v = bf16_round(v + b);
+      out[o] = __float2bfloat16_rn(gelu_tanh(v));
+      break;
+    }
+    case EPI_BIAS_GELU_ERF: {
+      float v = bf16_round(acc);
+      if (a.bias) v = bf16_round(v + b);
+      out[o] = __float2bfloat16_rn(gelu_erf(v));
       break;
     }
     default: {
@@ -319,14 +332,13 @@ int pick_splits(int tiles, int nkb, int num_sms) {
 }
 
 template <int BT>
+cudaError_t set_attr_bt() {
+  return cudaFuncSetAttribute(gemm_bf16_tc_kernel<BT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              Cfg<BT>::SMEM);
+}
+
+template <int BT>
 cudaError_t launch_bt(const GemmOp& op, cudaStream_t stream) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BT>::SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
   gemm_bf16_tc_kernel<BT><<<op.grid, kThreads, Cfg<BT>::SMEM, stream>>>(op.tm_w, op.tm_x, op.args);
   return cudaGetLastError();
 }
@@ -367,7 +379,7 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
     return "gemm: operands must be 16-byte aligned";
   if ((epilogue == EPI_GATED_RES && (!gate || !residual)) || (epilogue == EPI_RES && !residual))
     return "gemm: residual epilogue needs its inputs";
-  if (epilogue < 0 || epilogue > EPI_F32_OUT) return "gemm: unknown epilogue";
+  if (epilogue < 0 || epilogue > EPI_BIAS_GELU_ERF) return "gemm: unknown epilogue";
   std::memset(op, 0, sizeof(*op));
   const int bt = pick_bt(m);
   const int tiles_m = (m + bt - 1) / bt;
@@ -405,6 +417,27 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   op->grid = tiles_m * tiles_n * splits;
   op->smem_bytes = smem_for_bt(bt);
   return nullptr;
+}
+
+cudaError_t gemm_init(int device) {
+  // Opt-in shared memory per instantiation, once per device, before any
+  // launch (so that launches can be captured into CUDA graphs).
+  static std::mutex mu;
+  static std::vector<int> done;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int d : done)
+    if (d == device) return cudaSuccess;
+  cudaError_t e;
+  if ((e = set_attr_bt<16>()) != cudaSuccess) return e;
+  if ((e = set_attr_bt<32>()) != cudaSuccess) return e;
+  if ((e = set_attr_bt<48>()) != cudaSuccess) return e;
+  if ((e = set_attr_bt<64>()) != cudaSuccess) return e;
+  if ((e = set_attr_bt<96>()) != cudaSuccess) return e;
+  if ((e = set_attr_bt<128>()) != cudaSuccess) return e;
+  if ((e = set_attr_bt<192>()) != cudaSuccess) return e;
+  if ((e = set_attr_bt<256>()) != cudaSuccess) return e;
+  done.push_back(device);
+  return cudaSuccess;
 }
 
 cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream) {

@@ -1,0 +1,108 @@
+#include "host_math.h"
+
+#include <algorithm>
+#include <cmath>
+
+#include "wam_b200.h"
+
+namespace wamb {
+
+void flow_schedule(int steps, float shift, std::vector<float>* ts, std::vector<float>* sig) {
+  ts->assign(steps, 0.0f);
+  sig->assign(steps + 1, 0.0f);
+  // The endpoint comes from the F32 training schedule; linspace and the shift
+  // transform run in F64, then round to F32.
+  const float training_sigma = 1.0f / 1000.0f;
+  const float smin = shift * training_sigma / (1.0f + (shift - 1.0f) * training_sigma);
+  const double tmin = static_cast<double>(smin) * 1000.0;
+  for (int s = 0; s < steps; ++s) {
+    const double u = steps == 1 ? 1000.0 : 1000.0 + (tmin - 1000.0) * s / (steps - 1);
+    const double sigma = u / 1000.0;
+    const double sh =
+        static_cast<double>(shift) * sigma / (1.0 + (static_cast<double>(shift) - 1.0) * sigma);
+    (*sig)[s] = static_cast<float>(sh);
+    (*ts)[s] = (*sig)[s] * 1000.0f;
+  }
+  (*sig)[steps] = 0.0f;
+}
+
+void timestep_embedding(float t, int dim, float* out) {
+  const int half = dim / 2;
+  for (int i = 0; i < half; ++i) {
+    const float f =
+        std::exp(-std::log(10000.0f) * static_cast<float>(i) / static_cast<float>(half));
+    const float v = t * f;
+    out[i] = std::cos(v);
+    out[i + half] = std::sin(v);
+  }
+}
+
+void visual_positions(int gh, int gw, int* thw) {
+  for (int y = 0; y < gh; ++y)
+    for (int x = 0; x < gw; ++x) {
+      const int t = y * gw + x;
+      thw[t * 3 + 0] = 0;
+      thw[t * 3 + 1] = y;
+      thw[t * 3 + 2] = x;
+    }
+}
+
+void normalize_state(const float* state, int n, int padded, const float* q01, const float* q99,
+                     float* out) {
+  for (int d = 0; d < padded; ++d) out[d] = 0.0f;
+  for (int d = 0; d < n && d < padded; ++d) {
+    const float range = std::max(q99[d] - q01[d], 1e-8f);
+    out[d] = ((state[d] - q01[d]) / range) * 2.0f - 1.0f;
+  }
+}
+
+void postprocess_action(const float* action, int steps, int padded, int real, const float* q01,
+                        const float* q99, const float* raw_state, float* out) {
+  for (int t = 0; t < steps; ++t)
+    for (int d = 0; d < real; ++d) {
+      const float range = std::max(q99[d] - q01[d], 1e-8f);
+      float v = ((action[static_cast<size_t>(t) * padded + d] + 1.0f) * 0.5f) * range + q01[d];
+      if (d < 6 || (d >= 7 && d < 13)) v += raw_state[d];
+      out[static_cast<size_t>(t) * real + d] = v;
+    }
+}
+
+}  // namespace wamb
+
+extern "C" {
+
+WAM_B200_API int wam_b200_flow_schedule(int steps, float shift, float* timesteps, float* sigmas) {
+  if (steps <= 0 || !(shift > 0.0f) || !std::isfinite(shift) || !timesteps || !sigmas)
+    return WAM_B200_INVALID_ARGUMENT;
+  std::vector<float> ts, sg;
+  wamb::flow_schedule(steps, shift, &ts, &sg);
+  std::copy(ts.begin(), ts.end(), timesteps);
+  std::copy(sg.begin(), sg.end(), sigmas);
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_visual_positions(int gh, int gw, int* thw) {
+  if (gh <= 0 || gw <= 0 || !thw) return WAM_B200_INVALID_ARGUMENT;
+  wamb::visual_positions(gh, gw, thw);
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_normalize_state(const float* state, int n, int padded, const float* q01,
+                                          const float* q99, float* out) {
+  if (!state || !q01 || !q99 || !out || n < 1 || n > padded) return WAM_B200_INVALID_ARGUMENT;
+  for (int d = 0; d < n; ++d)
+    if (!std::isfinite(state[d])) return WAM_B200_INVALID_ARGUMENT;
+  wamb::normalize_state(state, n, padded, q01, q99, out);
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_postprocess_action(const float* action, int steps, int padded, int real,
+                                             const float* q01, const float* q99,
+                                             const float* raw_state, float* out) {
+  if (!action || !q01 || !q99 || !raw_state || !out || steps < 1 || real < 1 || real > padded)
+    return WAM_B200_INVALID_ARGUMENT;
+  wamb::postprocess_action(action, steps, padded, real, q01, q99, raw_state, out);
+  return WAM_B200_OK;
+}
+
+}  // extern "C"

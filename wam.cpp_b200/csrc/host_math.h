@@ -1,0 +1,27 @@
+// Host-side arithmetic of the action-chunk path (no device code): flow-match
+// schedule, timestep embedding, visual positions, state normalisation and
+// action post-processing.
+#pragma once
+
+#include <cstdint>
+#include <vector>
+
+namespace wamb {
+
+// make_flow_match_euler_schedule (src/models/common/scheduler.cpp:26-55).
+void flow_schedule(int steps, float shift, std::vector<float>* timesteps,
+                   std::vector<float>* sigmas);
+// timestep_embedding (src/models/gwp05/engine/text_encoder.cpp:1-12).
+void timestep_embedding(float t, int dim, float* out);
+// visual_positions (src/models/gwp05/semantics.cpp:235-257), [gh*gw][3] = (t, h, w).
+void visual_positions(int gh, int gw, int* thw);
+// State normalisation (engine.cpp:249-253, semantics.cpp:154-172): the first
+// n values map to [-1, 1] by the q01/q99 statistics, the rest of the padded
+// vector is zero.
+void normalize_state(const float* state, int n, int padded, const float* q01, const float* q99,
+                     float* out);
+// De-normalisation + delta actions (engine.cpp:436-445, semantics.cpp:178-208).
+void postprocess_action(const float* action, int steps, int padded, int real, const float* q01,
+                        const float* q99, const float* raw_state, float* out);
+
+}  // namespace wamb

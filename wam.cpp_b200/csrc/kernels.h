@@ -25,6 +25,8 @@ enum GemmEpilogue : int {
   EPI_RES = 4,        // y = bf16(r + bf16(bf16(acc) + b))          linear + ggml_add(hidden, .)
   EPI_F32_BIAS = 5,   // y = bf16(acc + b)                          conv_2d (F32 out) + bias, cast
   EPI_F32_OUT = 6,    // y_f32 = acc                                 raw accumulator (tests)
+  EPI_BIAS_GELU_R = 7,  // y = bf16(gelu_tanh(bf16(bf16(acc) + b)))   linear + ggml_gelu (text MLP)
+  EPI_BIAS_GELU_ERF = 8,  // y = bf16(gelu_erf(bf16(bf16(acc) + b)))  linear + ggml_gelu_erf (decoder)
 };
 
 struct GemmArgs {
@@ -68,6 +70,9 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
                       int ldr, void* out, int ldo, const GemmScratch& scratch, int num_sms,
                       int force_splits);
 cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream);
+// Sets per-kernel launch attributes on the current device (call once per
+// device before the first launch or graph capture).
+cudaError_t gemm_init(int device);
 // Split-K scratch a GEMM of this shape would use (floats), and its tile count.
 size_t gemm_scratch_floats(int m, int n, int k, int num_sms, int force_splits, int* tiles_out);
 
@@ -82,32 +87,35 @@ void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w,
                       float eps, bf16* y, int ldy, cudaStream_t s);
 
 // Per-token RMSNorm of q and k over the full attention width, RoPE, BF16 cast
-// and scatter into head-major attention buffers.
+// and scatter into head-major attention buffers (expert_qkv, mot.cpp:210-267;
+// build_cross_kv, mot.cpp:101-128). Source row r holds q / k / v at column
+// offsets q_col / k_col / v_col (-1 = absent). Destination element
+// (seq, head, row, d) of q is q_out[seq * q_seq_stride + head * q_head_stride +
+// (q_row_offset + row) * 128 + d]; k and v likewise with kv_* strides.
 struct QkvScatter {
-  const bf16* qkv;  // source row r at qkv + r * ld_qkv: [q(H) | k(H) | v(H)]
-  int ld_qkv;
+  const bf16* src;
+  int ld_src;
   int rows;          // tokens in this launch
   int rows_per_seq;  // tokens of one request in this launch
   int hidden;        // H = heads * 128
   int heads;
-  const bf16* q_norm;  // [H]
-  const bf16* k_norm;  // [H]
+  int q_col, k_col, v_col;
+  const bf16* q_norm;  // [H] RMSNorm weight, or null for no norm
+  const bf16* k_norm;
   float eps;
-  // rope: mode 0 = none, 1 = 1-D over 128 dims with position pos_base + row_in_seq,
-  // 2 = 3-D sections (44/42/42) with per-row positions from pos_thw[row_in_seq][3]
+  // rope: 0 = none, 1 = 1-D over 128 dims at position pos_base + row_in_seq,
+  // 2 = 3-D sections 44/42/42 at (t, h, w) = pos_thw[row_in_seq * 3 + {0,1,2}]
   int rope_mode;
   int pos_base;
   const int* pos_thw;
   const float* inv_freq;  // 1-D: [64]; 3-D: [22 | 21 | 21]
-  // destinations, element (seq, head, row, d):
-  bf16* q_out;  // may be null
+  bf16* q_out;
   long long q_seq_stride, q_head_stride;
   int q_row_offset;
   bf16* k_out;
-  bf16* v_out;  // may be null (K-only, e.g. cross K)
+  bf16* v_out;
   long long kv_seq_stride, kv_head_stride;
   int kv_row_offset;
-  int do_v;
 };
 void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s);
 
@@ -131,6 +139,7 @@ struct AttnArgs {
   int split_first;
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
+cudaError_t attention_init();
 
 // y[m, n] = act(bf16(bf16(sum_k x[m, k] * w(n, k)) + b[n])) for the small
 // action/state encoder and decoder projections, with w(n, k) =
@@ -140,10 +149,13 @@ void launch_small_linear(const bf16* x, int ldx, int m, int k, const bf16* w, lo
                          long long w_sk, const bf16* b, int n, int act, bf16* y, int ldy,
                          cudaStream_t s);
 
-// combined[l][j] = f32(mod[j]) + f32(table_l[j]) for all layers (modulation_add,
-// mot.cpp:137-145). tables: L x [width] BF16 pointers packed in a device array.
-void launch_modulation_add(const bf16* mod, const bf16* const* tables, int layers, int width,
-                           float* combined, cudaStream_t s);
+// combined[s][l][j] = f32(mod[s * ld_mod + j % period]) + f32(table_l[j]) for
+// steps s, layers l, j < width (modulation_add with f32_accumulation,
+// mot.cpp:137-145; the final head uses period = E to add temb to both halves,
+// mot.cpp:468-486). tables: device array of `layers` BF16 pointers.
+void launch_modulation_add(const bf16* mod, int ld_mod, int period, int steps,
+                           const bf16* const* tables, int layers, int width, float* combined,
+                           cudaStream_t s);
 // y = bf16(silu(x)), elementwise.
 void launch_silu(const bf16* x, bf16* y, int n, cudaStream_t s);
 // F32 -> BF16 round to nearest even.
@@ -158,7 +170,7 @@ void launch_euler(bf16* action, const bf16* velocity, int n, const float* dt, cu
 void launch_bf16_to_f32(const bf16* x, float* y, long long n, cudaStream_t s);
 // Deterministic synthetic weights: w[i] = bf16(center + scale * g(seed, i)),
 // g an integer-hash approximation of N(0,1) (sum of four uniform 16-bit draws).
-void launch_synth_bf16(bf16* w, long long n, unsigned long long seed, float scale, float center,
+void launch_synth_bf16(bf16* w, long long n, unsigned long long seed, double scale, double center,
                        cudaStream_t s);
 
 }  // namespace wamb

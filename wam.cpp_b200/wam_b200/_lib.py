@@ -41,7 +41,18 @@ def load(path: Path | None = None):
     _sig(lib, "wam_b200_gemm_scratch_floats", sz, [i32, i32, i32, i32, C.POINTER(i32)])
     _sig(lib, "wam_b200_op_gemm", i32,
          [vp, i32, i32, vp, i32, i32, i32, vp, vp, vp, i32, vp, i32, vp, sz, vp, i32, vp, i32, vp])
-    from . import _lib_engine  # noqa: F401  (engine prototypes, if present)
+    _sig(lib, "wam_b200_op_attention", i32,
+         [vp, C.c_longlong, C.c_longlong, vp, vp, C.c_longlong, C.c_longlong, i32, i32, i32, i32,
+          C.c_float, vp, i32, vp])
+    _sig(lib, "wam_b200_op_layernorm", i32, [vp, i32, i32, vp, vp, C.c_float, i32, vp, vp])
+    _sig(lib, "wam_b200_op_synth", i32, [vp, C.c_longlong, C.c_uint64, C.c_double, C.c_double, vp])
+    _sig(lib, "wam_b200_tensor_seed", C.c_uint64, [C.c_uint64, C.c_char_p])
+    f32p = C.POINTER(C.c_float)
+    _sig(lib, "wam_b200_flow_schedule", i32, [i32, C.c_float, f32p, f32p])
+    _sig(lib, "wam_b200_visual_positions", i32, [i32, i32, C.POINTER(C.c_int)])
+    _sig(lib, "wam_b200_normalize_state", i32, [f32p, i32, i32, f32p, f32p, f32p])
+    _sig(lib, "wam_b200_postprocess_action", i32, [f32p, i32, i32, i32, f32p, f32p, f32p, f32p])
+    from . import _lib_engine
     _lib_engine.attach(lib, _sig)
     _lib = lib
     return lib

@@ -1,0 +1,172 @@
+"""Host-side mirror of the reference's engine boundary over the wam_b200 C ABI.
+
+Engine mirrors wam::internal::gwp05::engine::Engine
+(src/models/gwp05/engine/engine.h:142-155): predict() returns the de-normalised
+action chunk for one request and raises on failure (the reference returns an
+empty vector that the model layer maps to inference_failed); reset() drops the
+projected-prompt cache. predict_batch() adds the batched entry the reference
+lacks.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._lib import load
+from ._lib_engine import GEOM_FIELDS, Geometry, Options, Request, Stats, Status
+
+
+class EngineError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+
+
+def _raise(lib, rc, st, what):
+    if rc != 0:
+        msg = C.cast(st.message, C.c_char_p).value.decode() if st.message else ""
+        lib.wam_b200_status_free(C.byref(st))
+        raise EngineError(rc, f"{what}: {msg}")
+
+
+def geometry_struct(g) -> Geometry:
+    s = Geometry()
+    for n in GEOM_FIELDS:
+        setattr(s, n, int(getattr(g, n)))
+    s.norm_eps = float(g.norm_eps)
+    s.flow_shift = float(g.flow_shift)
+    return s
+
+
+@dataclass
+class Req:
+    state: np.ndarray
+    latent: np.ndarray
+    prompt: np.ndarray
+    noise: np.ndarray | None = None
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class Engine:
+    def __init__(self, geometry=None, seed: int = 0, artifact: str | None = None,
+                 bias_scale: float = 0.0, device: int = 0, max_batch: int = 1,
+                 graphs: bool = True, prompt_cache: bool = True):
+        self.lib = load()
+        o = Options()
+        o.struct_size = C.sizeof(Options)
+        o.artifact_path = artifact.encode() if artifact else None
+        if geometry is not None:
+            o.synthetic_geometry = geometry_struct(geometry)
+        o.synthetic_seed = seed
+        o.synthetic_bias_scale = bias_scale
+        o.device_index = device
+        o.max_batch = max_batch
+        o.use_cuda_graphs = 1 if graphs else 0
+        o.prompt_cache = 1 if prompt_cache else 0
+        h = C.c_void_p()
+        st = Status()
+        _raise(self.lib, self.lib.wam_b200_create(C.byref(o), C.byref(h), C.byref(st)), st,
+               "wam_b200_create")
+        self.h = h
+        self.max_batch = max_batch
+        g = Geometry()
+        self.lib.wam_b200_geometry_of(self.h, C.byref(g))
+        self.geometry = {n: getattr(g, n) for n in GEOM_FIELDS}
+        self.geometry.update(norm_eps=g.norm_eps, flow_shift=g.flow_shift)
+        self._keep = []
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.wam_b200_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def _requests(self, reqs):
+        arr = (Request * len(reqs))()
+        keep = []
+        for i, r in enumerate(reqs):
+            s, lat, pr = _f32(r.state), _f32(r.latent), _f32(r.prompt)
+            keep += [s, lat, pr]
+            fp = C.POINTER(C.c_float)
+            arr[i].state = s.ctypes.data_as(fp)
+            arr[i].state_n = s.size
+            arr[i].ref_latent = lat.ctypes.data_as(fp)
+            arr[i].ref_latent_n = lat.size
+            arr[i].prompt_emb = pr.ctypes.data_as(fp)
+            arr[i].prompt_tokens = pr.shape[0] if pr.ndim == 2 else pr.size // self.geometry["text_dim"]
+            if r.noise is not None:
+                nz = _f32(r.noise)
+                keep.append(nz)
+                arr[i].noise = nz.ctypes.data_as(fp)
+        return arr, keep
+
+    def _out(self, batch):
+        g = self.geometry
+        return np.zeros((batch, g["action_chunk"], g["real_action_dim"]), np.float32)
+
+    def predict_batch(self, reqs, stats: bool = False):
+        arr, keep = self._requests(reqs)
+        out = self._out(len(reqs))
+        st, s = Status(), Stats()
+        rc = self.lib.wam_b200_predict_batch(self.h, arr, len(reqs),
+                                             out.ctypes.data_as(C.POINTER(C.c_float)), out.size,
+                                             C.byref(s), C.byref(st))
+        _raise(self.lib, rc, st, "wam_b200_predict_batch")
+        if stats:
+            return out, {f: getattr(s, f) for f, _ in Stats._fields_}
+        return out
+
+    def predict(self, req, stats: bool = False):
+        r = self.predict_batch([req], stats)
+        return (r[0][0], r[1]) if stats else r[0]
+
+    def stage(self, reqs):
+        arr, keep = self._requests(reqs)
+        self._keep = keep
+        st = Status()
+        _raise(self.lib, self.lib.wam_b200_stage(self.h, arr, len(reqs), C.byref(st)), st,
+               "wam_b200_stage")
+
+    def run(self, batch: int):
+        st = Status()
+        _raise(self.lib, self.lib.wam_b200_run(self.h, batch, C.byref(st)), st, "wam_b200_run")
+
+    def fetch(self, reqs):
+        arr, keep = self._requests(reqs)
+        out = self._out(len(reqs))
+        st = Status()
+        rc = self.lib.wam_b200_fetch(self.h, arr, len(reqs), out.ctypes.data_as(C.POINTER(C.c_float)),
+                                     out.size, C.byref(st))
+        _raise(self.lib, rc, st, "wam_b200_fetch")
+        return out
+
+    def stream(self) -> int:
+        return self.lib.wam_b200_stream(self.h) or 0
+
+    def kernel_launches(self, batch: int, with_prompt: bool = True) -> int:
+        return self.lib.wam_b200_kernel_launches(self.h, batch, 1 if with_prompt else 0)
+
+    def reset(self):
+        self.lib.wam_b200_reset(self.h)
+
+    def read_tensor(self, name: str, slot: int = 0, layer: int = 0) -> np.ndarray:
+        g = self.geometry
+        P = 1 + g["grid_h"] * g["grid_w"]
+        shapes = {"prefix_k": (g["heads"], P, 128), "prefix_v": (g["heads"], P, 128),
+                  "prompt_k": (g["heads"], g["prompt_tokens"], 128),
+                  "prompt_v": (g["heads"], g["prompt_tokens"], 128),
+                  "velocity": (g["steps"], g["action_chunk"], g["action_dim"])}
+        out = np.zeros(shapes[name], np.float32)
+        st = Status()
+        rc = self.lib.wam_b200_read_tensor(self.h, name.encode(), slot, layer,
+                                           out.ctypes.data_as(C.POINTER(C.c_float)), out.size,
+                                           C.byref(st))
+        _raise(self.lib, rc, st, "wam_b200_read_tensor")
+        return out

@@ -51,3 +51,38 @@ def gemm(x, w, epilogue=EPI_BIAS, bias=None, gate=None, residual=None, out=None,
         _ptr(scratch.error), force_splits, _stream())
     check(rc, "wam_b200_op_gemm")
     return out
+
+
+def attention(q, k, v, scale=None, out=None):
+    """q: [B, heads, lq, 128], k/v: [B, heads, lk, 128] BF16 (contiguous).
+    Returns [B * lq, heads * 128] BF16."""
+    lib = load()
+    B, heads, lq, d = q.shape
+    lk = k.shape[2]
+    assert d == 128 and q.is_contiguous() and k.is_contiguous() and v.is_contiguous()
+    if out is None:
+        out = torch.empty(B * lq, heads * 128, dtype=torch.bfloat16, device=q.device)
+    scale = scale if scale is not None else 1.0 / 128 ** 0.5
+    rc = lib.wam_b200_op_attention(_ptr(q), heads * lq * 128, lq * 128, _ptr(k), _ptr(v),
+                                   heads * lk * 128, lk * 128, lq, lk, heads, B, scale, _ptr(out),
+                                   out.stride(0), _stream())
+    check(rc, "wam_b200_op_attention")
+    return out
+
+
+def layernorm(x, a, b, eps=1e-6, affine=False):
+    lib = load()
+    y = torch.empty_like(x)
+    rc = lib.wam_b200_op_layernorm(_ptr(x), x.shape[0], x.shape[1], _ptr(a), _ptr(b), eps,
+                                   1 if affine else 0, _ptr(y), _stream())
+    check(rc, "wam_b200_op_layernorm")
+    return y
+
+
+def synth(n, seed, name, scale, center, device="cuda"):
+    lib = load()
+    w = torch.empty(n, dtype=torch.bfloat16, device=device)
+    ts = lib.wam_b200_tensor_seed(seed, name.encode())
+    rc = lib.wam_b200_op_synth(_ptr(w), n, ts, scale, center, _stream())
+    check(rc, "wam_b200_op_synth")
+    return w
