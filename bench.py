@@ -1,0 +1,367 @@
+"""Benchmark of the B200 GWP-0.5 MoT engine: action chunks per second.
+
+One "step" = one GWP-0.5 action chunk of BASELINE config 2 (full MoT, batch 1
+per GPU: prompt projection + 30-layer prefix cache + 10 flow-matching Euler
+steps), synthetic random-init BF16 weights and seeded synthetic inputs of the
+config's shapes. With --gpus N the engine runs as N independent data-parallel
+replicas (one process per GPU, no collective); value = all chunks / max-over-
+ranks time.
+
+  python bench.py [--gpus N --steps K --warmup W]        this engine
+  python bench.py --impl reference [...]                 the reference arm: the
+      CPU restatement of the reference's path (oracle/) on the host cores
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import dataclasses
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+sys.path.insert(0, str(REPO / "wam.cpp_b200"))
+
+METRIC = "action chunks/sec/box at batch 1-64 (1/2/4/8 B200); p50 ms per chunk at batch 1"
+UNIT = "action_chunks/s"
+SEED = 20261201
+
+
+def config2(layers: int | None = None):
+    from oracle import synth
+
+    g = dataclasses.replace(synth.CONFIG2, flow_shift=1.0)  # sigmas linear 1 -> 0.001 -> 0
+    if layers is not None:
+        g = dataclasses.replace(g, layers=layers)
+    return g
+
+
+def workload(g, batch: int) -> dict:
+    return {"workload": "config2: GWP-0.5-shaped MoT action chunk (prompt projection + prefix "
+                        "cache + 10 Euler steps)",
+            "layers": g.layers, "hidden": g.hidden, "action_hidden": g.action_hidden,
+            "ffn": g.ffn, "heads": g.heads, "visual_tokens": g.visual_tokens,
+            "prompt_tokens": g.prompt_tokens, "text_dim": g.text_dim,
+            "action_chunk": [g.action_chunk, g.action_dim], "steps": g.steps,
+            "batch_per_gpu": batch, "weights": "synthetic N(0,0.02) BF16, biases 0",
+            "l2": "no flush needed: each chunk streams 19.7 GB of weights (> 126 MB L2)"}
+
+
+def peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        import torch
+
+        try:
+            self.device = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            self.device = str(device)
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(layers: int, timed_runs: int = 1) -> dict:
+    """The oracle (CPU restatement of the reference path) on a bounded sample:
+    one config-2 chunk through `layers` of the 30 layers, extrapolated."""
+    import oracle
+    from oracle import synth
+
+    g = config2(layers)
+    m = oracle.OracleModel(g, None, seed=SEED, bias_scale=0.0)
+    r = synth.make_request(g, SEED)
+    times = []
+    for _ in range(timed_runs):
+        t0 = time.perf_counter()
+        m.predict(r)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    full = t * 30 / layers
+    return {"value": 1.0 / full, "unit": UNIT, "cores": oracle.lib().oracle_threads(),
+            "kind": "port", "sample_seconds": t,
+            "sample": f"one config-2 chunk (prompt projection, prefix, 10 Euler steps) through "
+                      f"{layers} of 30 layers, F32 OpenMP oracle; chunk time extrapolated x{30 / layers:g} "
+                      f"({full:.1f} s/chunk)"}
+
+
+def host_cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # the CPU arm runs once per box, on rank 0
+    import oracle
+    from oracle import synth
+
+    layers = args.cpu_layers
+    g = config2(layers)
+    m = oracle.OracleModel(g, None, seed=SEED, bias_scale=0.0)
+    r = synth.make_request(g, SEED)
+    m.predict(r)  # one untimed warm-up sample (page-in, thread pool start)
+    vals = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        m.predict(r)
+        vals.append((time.perf_counter() - t0) * 30 / layers)
+    per_chunk = statistics.median(vals)
+    value = 1.0 / per_chunk
+    cb = {"value": value, "unit": UNIT, "cores": oracle.lib().oracle_threads(), "kind": "port",
+          "cpu_model": host_cpu_model(),
+          "sample": f"each step: one config-2 chunk (prompt projection, prefix, 10 Euler steps) "
+                    f"through {layers} of 30 layers with the F32 OpenMP oracle, time x{30 / layers:g}"}
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": 1, "ms_per_step": per_chunk * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload(config2(), 1), "cpu_baseline": cb,
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference's ggml CPU path cannot be built here (llama.cpp b9866 is not "
+                    "vendored); this arm times the oracle/ C++ restatement of that path"}
+    print(json.dumps(line), flush=True)
+
+
+def gemm_roofline_probe(batch: int, pk: dict, reps: int = 20) -> tuple[dict, dict]:
+    """Times the engine's GEMM kernel (wam_b200_op_gemm) on one action-expert
+    layer's denoise shapes at this batch (weight streaming, HBM bound) and on
+    the prefix's visual-token shapes (tensor bound), with CUDA events on the
+    launching stream."""
+    import torch
+    from wam_b200 import ops
+
+    dev = torch.device("cuda")
+    E = H = 3072
+    F = 14336
+    shapes = [(3 * H, E), (E, H), (H, E), (E, H), (F, E), (E, F)]  # qkv, o, ca.q, ca.o, ffn in/out
+    ws = [torch.randn(n, k, device=dev).mul_(0.02).to(torch.bfloat16) for n, k in shapes]
+    scratch = ops.Scratch(floats=1 << 25, slots=1 << 14)
+
+    def timed(m: int):
+        xs = [torch.randn(m, k, device=dev).to(torch.bfloat16) for _, k in shapes]
+        ys = [torch.empty(m, n, device=dev, dtype=torch.bfloat16) for n, _ in shapes]
+        for _ in range(3):
+            for w, x, y in zip(ws, xs, ys):
+                ops.gemm(x, w, ops.EPI_BIAS, out=y, scratch=scratch)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            for w, x, y in zip(ws, xs, ys):
+                ops.gemm(x, w, ops.EPI_BIAS, out=y, scratch=scratch)
+        e1.record()
+        torch.cuda.synchronize()
+        launches = reps * len(shapes)
+        sec = e0.elapsed_time(e1) / 1e3 / launches
+        byts = sum((n * k + m * k + m * n) * 2 for n, k in shapes) / len(shapes)
+        flops = sum(2 * m * n * k for n, k in shapes) / len(shapes)
+        return sec, byts, flops
+
+    sec, byts, _ = timed(48 * batch)
+    hbm = {"bound": "hbm", "kernel": "gemm_bf16_tc_kernel (denoise shapes, M=%d)" % (48 * batch),
+           "achieved": byts / sec / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+           "frac": byts / sec / 1e9 / pk["hbm_gbs"], "traffic": None,
+           "algorithmic_bytes_per_launch": byts, "avg_launch_us": sec * 1e6,
+           "peak_source": pk["source"] + " (burst copy, kernel timed alone)"}
+    sec2, _, flops = timed(768 * batch)
+    tc = {"bound": "tensor", "kernel": "gemm_bf16_tc_kernel (prefix shapes, M=%d)" % (768 * batch),
+          "achieved": flops / sec2 / 1e12, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+          "frac": flops / sec2 / 1e12 / pk["bf16_tflops"], "avg_launch_us": sec2 * 1e6,
+          "peak_source": pk["source"] + " (burst cuBLAS, kernel timed alone)"}
+    traffic = REPO / "profiles" / "gemm_traffic.json"
+    if traffic.exists():
+        t = json.loads(traffic.read_text())
+        hbm["traffic"] = t.get("denoise_M48_bytes_per_launch")
+    del ws
+    return hbm, tc
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=1, help="requests per GPU per step")
+    ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    if args.warmup < 3:
+        args.warmup = 3
+
+    import numpy as np
+    import torch
+    from oracle import synth
+    from wam_b200.engine import Engine, Req
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if not dist:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    g = config2()
+    B = args.batch
+    eng = Engine(g, seed=SEED, bias_scale=0.0, device=local, max_batch=B, graphs=True,
+                 prompt_cache=False)
+    reqs = []
+    for i in range(B):
+        r = synth.make_request(g, SEED + 7919 * rank + i)
+        reqs.append(Req(r.state, r.latent, r.prompt, r.noise))
+    stream = torch.cuda.ExternalStream(eng.stream())
+    kernels_per_chunk = eng.kernel_launches(B, with_prompt=True)
+
+    # ---- device-resident throughput: inputs staged in HBM before timing
+    eng.stage(reqs)
+    for _ in range(args.warmup):
+        eng.run(B)
+    torch.cuda.synchronize()
+    barrier()
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            events[0].record()
+            for i in range(args.steps):
+                eng.run(B)
+                events[i + 1].record()
+        torch.cuda.synchronize()
+    barrier()
+    per = [events[i].elapsed_time(events[i + 1]) for i in range(args.steps)]
+    total_s = max_over_ranks(sum(per) / 1e3)
+    value = world * B * args.steps / total_s
+    out = eng.fetch(reqs)
+    assert np.isfinite(out).all(), "non-finite action chunk"
+
+    # ---- end to end through the public C ABI: host inputs -> predict_batch -> host actions
+    for _ in range(2):
+        eng.predict_batch(reqs)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.predict_batch(reqs)
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_value = world * B * args.steps / e2e_s
+    A, T, Nt, D = g.action_dim, g.action_chunk, g.prompt_tokens, g.text_dim
+    h2d = B * 4 * (A + g.vae_z * 4 * g.visual_tokens + Nt * D + T * A)
+    d2h = B * 4 * (T * A + 1)
+
+    pk = peaks()
+    hbm_roof, tc_roof = gemm_roofline_probe(B, pk) if rank == 0 else (None, None)
+    barrier()
+    if dist:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    cb = None
+    if world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(args.cpu_layers)
+        cb["cpu_model"] = host_cpu_model()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_s * 1e3 / args.steps,
+        "p50_ms_per_chunk": statistics.median(per), "p95_ms_per_chunk": float(np.percentile(per, 95)),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": {**workload(g, B), "parallelism": f"dp{world} (replicas, no collective)"},
+        "roofline": hbm_roof, "roofline_tensor": tc_roof, "clocks": clocks.summary(),
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_s * 1e3 / args.steps},
+        "gpu_launches": kernels_per_chunk * args.steps,
+        "kernels_per_chunk": kernels_per_chunk,
+        "cpu_baseline": cb,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

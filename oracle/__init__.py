@@ -57,6 +57,9 @@ def lib():
                                     C.POINTER(C.c_void_p), C.POINTER(C.c_int64), f32p, f32p,
                                     f32p, f32p, C.c_char_p, C.c_int]
         l.oracle_destroy.argtypes = [C.c_void_p]
+        l.oracle_create_synthetic.restype = C.c_void_p
+        l.oracle_create_synthetic.argtypes = [C.POINTER(_Geom), C.c_uint64, C.c_double, C.c_char_p,
+                                              C.c_int]
         l.oracle_predict.restype = C.c_int
         l.oracle_predict.argtypes = [C.c_void_p] + [f32p] * 10
         l.oracle_schedule.argtypes = [C.c_int, C.c_float, f32p, f32p]
@@ -102,8 +105,17 @@ def timestep_embedding(t: float, dim: int = 256):
 class OracleModel:
     """A CPU model over BF16 weights given as {compact name: uint16 array}."""
 
-    def __init__(self, g: Geometry, weights: dict, stats: dict | None = None):
+    def __init__(self, g: Geometry, weights: dict | None, stats: dict | None = None,
+                 seed: int = 0, bias_scale: float = 0.0):
+        """weights None: the synthetic weights of (seed, bias_scale), built in C++."""
         self.g = g
+        if weights is None:
+            err = C.create_string_buffer(512)
+            gs = geom_struct(g)
+            self.h = lib().oracle_create_synthetic(C.byref(gs), seed, bias_scale, err, 512)
+            if not self.h:
+                raise RuntimeError("oracle_create_synthetic: " + err.value.decode())
+            return
         stats = stats or statistics(g)
         names = list(weights)
         arrs = [np.ascontiguousarray(weights[n], dtype=np.uint16) for n in names]

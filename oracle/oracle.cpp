@@ -632,6 +632,114 @@ void* oracle_create(const oracle_geometry* g, int n, const char** names, const u
   return md;
 }
 
+// Builds a model over the deterministic synthetic weights (the generator of
+// oracle/synth.py, restated here so full-width CPU baselines do not have to
+// materialise weights in Python): same names, shapes and bits.
+void* oracle_create_synthetic(const oracle_geometry* g, uint64_t seed, double bias_scale,
+                              char* err, int errlen) {
+  auto fail = [&](const std::string& m) -> void* {
+    if (err && errlen > 0) std::snprintf(err, errlen, "%s", m.c_str());
+    return nullptr;
+  };
+  if (!g || g->heads * 128 != g->hidden) return fail("hidden must equal heads * 128");
+  Model* md = new Model();
+  md->g = *g;
+  const int64_t E = g->action_hidden, H = g->hidden, A = g->action_dim, D = g->text_dim;
+  const int64_t emb = g->num_embodiments;
+  std::vector<std::pair<std::string, int64_t>> s;
+  s.push_back({"gwp.patch.weight", H * g->vae_z * 4});
+  s.push_back({"gwp.patch.bias", H});
+  for (const char* c : {"state", "action"}) {
+    const std::string p = std::string("gwp.") + c;
+    s.push_back({p + ".in.weight", emb * A * 128});
+    s.push_back({p + ".in.bias", emb * 128});
+    s.push_back({p + ".mid.weight", 128 * 128});
+    s.push_back({p + ".mid.bias", 128});
+    s.push_back({p + ".out.weight", E * 128});
+    s.push_back({p + ".out.bias", E});
+  }
+  s.push_back({"gwp.decode.in.weight", 128 * E});
+  s.push_back({"gwp.decode.in.bias", 128});
+  s.push_back({"gwp.decode.mid.weight", 128 * 128});
+  s.push_back({"gwp.decode.mid.bias", 128});
+  s.push_back({"gwp.decode.out.weight", emb * 128 * A});
+  s.push_back({"gwp.decode.out.bias", emb * A});
+  s.push_back({"gwp.action_mod", 2 * E});
+  for (int x = 0; x < 2; ++x) {
+    const std::string p = x == 0 ? "gwp.acond" : "gwp.cond";
+    const int64_t W = x == 0 ? E : H;
+    for (auto& kv : std::vector<std::pair<std::string, int64_t>>{
+             {".time.0.weight", W * 256}, {".time.0.bias", W}, {".time.1.weight", W * W},
+             {".time.1.bias", W}, {".time.out.weight", 6 * W * W}, {".time.out.bias", 6 * W},
+             {".text.0.weight", W * D}, {".text.0.bias", W}, {".text.1.weight", W * W},
+             {".text.1.bias", W}})
+      s.push_back({p + kv.first, kv.second});
+  }
+  for (int l = 0; l < g->layers; ++l)
+    for (int x = 0; x < 2; ++x) {
+      const int64_t W = x == 0 ? E : H, F = x == 0 ? g->action_ffn : g->ffn;
+      const std::string p = "gwp.blk." + std::to_string(l) + (x == 0 ? ".a" : ".v");
+      for (auto& kv : std::vector<std::pair<std::string, int64_t>>{
+               {".sa.qkv.weight", 3 * H * W}, {".sa.qkv.bias", 3 * H}, {".sa.qn.weight", H},
+               {".sa.kn.weight", H}, {".sa.o.weight", W * H}, {".sa.o.bias", W},
+               {".ca.q.weight", H * W}, {".ca.q.bias", H}, {".ca.k.weight", H * W},
+               {".ca.k.bias", H}, {".ca.vproj.weight", H * W}, {".ca.vproj.bias", H},
+               {".ca.o.weight", W * H}, {".ca.o.bias", W}, {".ca.qn.weight", H},
+               {".ca.kn.weight", H}, {".ca_norm.weight", W}, {".ca_norm.bias", W},
+               {".ffn.in.weight", F * W}, {".ffn.in.bias", F}, {".ffn.out.weight", W * F},
+               {".ffn.out.bias", W}, {".mod", 6 * W}})
+        s.push_back({p + kv.first, kv.second});
+    }
+  const double ih4 = std::sqrt(4.0 * (65536.0 * 65536.0 - 1.0) / 12.0);
+  auto ends = [](const std::string& a, const char* b) {
+    const size_t n = std::strlen(b);
+    return a.size() >= n && a.compare(a.size() - n, n, b) == 0;
+  };
+  auto fnv = [](const std::string& x) {
+    uint64_t h = 0xCBF29CE484222325ull;
+    for (unsigned char c : x) {
+      h ^= c;
+      h *= 0x100000001B3ull;
+    }
+    return h;
+  };
+  auto mix = [](uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+  };
+  for (const auto& kv : s) {
+    double scale = 0.02, center = 0.0;
+    if (ends(kv.first, ".bias")) scale = bias_scale;
+    else if (ends(kv.first, ".qn.weight") || ends(kv.first, ".kn.weight") || ends(kv.first, ".ca_norm.weight")) center = 1.0;
+    const uint64_t ts = mix((seed ^ fnv(kv.first)) + 0x9E3779B97F4A7C15ull);
+    const float k = static_cast<float>(scale / ih4), c = static_cast<float>(center);
+    Tensor t;
+    t.numel = kv.second;
+    t.data.resize(kv.second);
+    uint16_t* d = t.data.data();
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < kv.second; ++i) {
+      const uint64_t h = mix(ts + static_cast<uint64_t>(i + 1) * 0x9E3779B97F4A7C15ull);
+      const int z = static_cast<int>((h & 0xFFFFull) + ((h >> 16) & 0xFFFFull) + ((h >> 32) & 0xFFFFull) + (h >> 48)) - 131070;
+      volatile float prod = static_cast<float>(z) * k;  // two separately rounded F32 ops
+      const float v = prod + c;
+      uint32_t u;
+      std::memcpy(&u, &v, 4);
+      u += 0x7fffu + ((u >> 16) & 1u);
+      d[i] = static_cast<uint16_t>(u >> 16);
+    }
+    md->t.emplace(kv.first, std::move(t));
+  }
+  for (int i = 0; i < A; ++i) {
+    md->sq01.push_back(-1.0f - 0.01f * static_cast<float>(i));
+    md->sq99.push_back(1.0f + 0.02f * static_cast<float>(i));
+  }
+  md->aq01 = md->sq01;
+  md->aq99 = md->sq99;
+  return md;
+}
+
 void oracle_destroy(void* m) { delete static_cast<Model*>(m); }
 
 int oracle_predict(void* model, const float* state, const float* latent, const float* prompt,

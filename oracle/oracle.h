@@ -53,6 +53,10 @@ void* oracle_create(const oracle_geometry* g, int n_tensors, const char** names,
                     const uint16_t** data, const int64_t* numel, const float* state_q01,
                     const float* state_q99, const float* action_q01, const float* action_q99,
                     char* err, int errlen);
+/* Model over the deterministic synthetic weights of oracle/synth.py (same bits),
+ * generated in C++ for full-width CPU baselines. */
+void* oracle_create_synthetic(const oracle_geometry* g, uint64_t seed, double bias_scale,
+                              char* err, int errlen);
 void oracle_destroy(void* model);
 
 /* One request. state: [real_state_dim] raw; latent: [vae_z][2gh][2gw];
