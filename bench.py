@@ -191,58 +191,40 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def gemm_roofline_probe(batch: int, pk: dict, reps: int = 20) -> tuple[dict, dict]:
-    """Times the engine's GEMM kernel (wam_b200_op_gemm) on one action-expert
-    layer's denoise shapes at this batch (weight streaming, HBM bound) and on
-    the prefix's visual-token shapes (tensor bound), with CUDA events on the
-    launching stream."""
-    import torch
-    from wam_b200 import ops
+def roofline_from_profile(prof: list[dict], pk: dict) -> tuple[dict, dict, dict]:
+    """Roofline of the dominant kernel from the engine's per-op profile of one
+    chunk (CUDA events around every launch on the engine's stream):
+      * denoise-phase GEMMs (weight streaming, HBM bound): algorithmic bytes
+        (weights + activations in + outputs) / device time;
+      * prefix-phase GEMMs (tensor bound): algorithmic FLOPs / device time."""
+    def agg(phase, kind):
+        ops = [o for o in prof if o["phase"] == phase and o["kind"] == kind]
+        return (sum(o["ms"] for o in ops) / 1e3, sum(o["bytes"] for o in ops),
+                sum(o["flops"] for o in ops), len(ops))
 
-    dev = torch.device("cuda")
-    E = H = 3072
-    F = 14336
-    shapes = [(3 * H, E), (E, H), (H, E), (E, H), (F, E), (E, F)]  # qkv, o, ca.q, ca.o, ffn in/out
-    ws = [torch.randn(n, k, device=dev).mul_(0.02).to(torch.bfloat16) for n, k in shapes]
-    scratch = ops.Scratch(floats=1 << 25, slots=1 << 14)
-
-    def timed(m: int):
-        xs = [torch.randn(m, k, device=dev).to(torch.bfloat16) for _, k in shapes]
-        ys = [torch.empty(m, n, device=dev, dtype=torch.bfloat16) for n, _ in shapes]
-        for _ in range(3):
-            for w, x, y in zip(ws, xs, ys):
-                ops.gemm(x, w, ops.EPI_BIAS, out=y, scratch=scratch)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            for w, x, y in zip(ws, xs, ys):
-                ops.gemm(x, w, ops.EPI_BIAS, out=y, scratch=scratch)
-        e1.record()
-        torch.cuda.synchronize()
-        launches = reps * len(shapes)
-        sec = e0.elapsed_time(e1) / 1e3 / launches
-        byts = sum((n * k + m * k + m * n) * 2 for n, k in shapes) / len(shapes)
-        flops = sum(2 * m * n * k for n, k in shapes) / len(shapes)
-        return sec, byts, flops
-
-    sec, byts, _ = timed(48 * batch)
-    hbm = {"bound": "hbm", "kernel": "gemm_bf16_tc_kernel (denoise shapes, M=%d)" % (48 * batch),
+    sec, byts, _, n = agg("denoise", "gemm")
+    hbm = {"bound": "hbm", "kernel": "gemm_bf16_tc_kernel, denoise phase (M = 48 tokens per request)",
            "achieved": byts / sec / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
            "frac": byts / sec / 1e9 / pk["hbm_gbs"], "traffic": None,
-           "algorithmic_bytes_per_launch": byts, "avg_launch_us": sec * 1e6,
-           "peak_source": pk["source"] + " (burst copy, kernel timed alone)"}
-    sec2, _, flops = timed(768 * batch)
-    tc = {"bound": "tensor", "kernel": "gemm_bf16_tc_kernel (prefix shapes, M=%d)" % (768 * batch),
-          "achieved": flops / sec2 / 1e12, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-          "frac": flops / sec2 / 1e12 / pk["bf16_tflops"], "avg_launch_us": sec2 * 1e6,
-          "peak_source": pk["source"] + " (burst cuBLAS, kernel timed alone)"}
+           "algorithmic_bytes_per_launch": byts / n, "avg_launch_us": sec / n * 1e6, "launches": n,
+           "peak_source": pk["source"] + " HBM copy (burst)"}
     traffic = REPO / "profiles" / "gemm_traffic.json"
     if traffic.exists():
-        t = json.loads(traffic.read_text())
-        hbm["traffic"] = t.get("denoise_M48_bytes_per_launch")
-    del ws
-    return hbm, tc
+        hbm["traffic"] = json.loads(traffic.read_text()).get("denoise_bytes_per_launch")
+    sec2, _, flops, n2 = agg("prefix", "gemm")
+    tc = {"bound": "tensor", "kernel": "gemm_bf16_tc_kernel, prefix phase (768 visual tokens)",
+          "achieved": flops / sec2 / 1e12, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+          "frac": flops / sec2 / 1e12 / pk["bf16_tflops"], "avg_launch_us": sec2 / n2 * 1e6,
+          "launches": n2, "peak_source": pk["source"] + " cuBLAS bf16 (burst)"}
+    total = sum(o["ms"] for o in prof)
+    br = {}
+    for o in prof:
+        k = o["phase"] + "/" + o["kind"]
+        br[k] = br.get(k, 0.0) + o["ms"]
+    breakdown = {k: {"ms": round(v, 3), "share": round(v / total, 4)} for k, v in
+                 sorted(br.items(), key=lambda kv: -kv[1])}
+    breakdown["_total_eager_ms"] = round(total, 3)
+    return hbm, tc, breakdown
 
 
 def main() -> None:
@@ -338,8 +320,12 @@ def main() -> None:
     h2d = B * 4 * (A + g.vae_z * 4 * g.visual_tokens + Nt * D + T * A)
     d2h = B * 4 * (T * A + 1)
 
+    eng.stage(reqs)
+    eng.run(B)
+    phases = eng.phase_ms()
+    prof = eng.profile(B)
     pk = peaks()
-    hbm_roof, tc_roof = gemm_roofline_probe(B, pk) if rank == 0 else (None, None)
+    hbm_roof, tc_roof, breakdown = roofline_from_profile(prof, pk)
     barrier()
     if dist:
         dist.destroy_process_group()
@@ -356,6 +342,7 @@ def main() -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": {**workload(g, B), "parallelism": f"dp{world} (replicas, no collective)"},
         "roofline": hbm_roof, "roofline_tensor": tc_roof, "clocks": clocks.summary(),
+        "phase_ms": phases, "kernel_breakdown": breakdown,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_s * 1e3 / args.steps},
         "gpu_launches": kernels_per_chunk * args.steps,

@@ -211,6 +211,24 @@ WAM_B200_API int wam_b200_fetch(wam_b200_engine* engine, const wam_b200_request*
 WAM_B200_API void* wam_b200_stream(wam_b200_engine* engine);
 /* Kernels one chunk launches at this batch (with / without prompt projection). */
 WAM_B200_API int wam_b200_kernel_launches(wam_b200_engine* engine, int batch, int with_prompt);
+/* Device time (ms) of the phases of the last run/predict: prompt projection
+ * (0 when the projected-prompt cache hit), prefix cache, denoise. */
+WAM_B200_API int wam_b200_phase_ms(wam_b200_engine* engine, float* prompt_ms, float* prefix_ms,
+                                   float* denoise_ms);
+
+/* Per-kernel profile of one chunk on the staged batch: runs every op eagerly
+ * between CUDA events and fills up to max_ops records (phase 0 prompt /
+ * 1 prefix / 2 denoise; kind 0 GEMM, 1 attention, 2 layer norm, 3 q/k/v
+ * norm+RoPE scatter, 4 small linear, 5 elementwise; ms; algorithmic bytes and
+ * FLOPs). Returns the number of ops, or a negative error code. */
+typedef struct wam_b200_op_profile {
+  int phase, kind, launches;
+  float ms;
+  double bytes, flops;
+} wam_b200_op_profile;
+WAM_B200_API int wam_b200_profile(wam_b200_engine* engine, int batch, wam_b200_op_profile* out,
+                                  int max_ops, wam_b200_status* status);
+
 /* Stage dumps as F32 (the reference's WAM_GWP05_CACHE_DUMP_DIR stages,
  * engine/cache.cpp:441-469): "prefix_k"/"prefix_v" [heads][1+V][128],
  * "prompt_k"/"prompt_v" [heads][prompt_tokens][128] of one layer,

@@ -171,6 +171,8 @@ std::unique_ptr<MotEngine> MotEngine::create(const EngineOptions& opt, std::stri
 MotEngine::~MotEngine() {
   if (stream_) cudaStreamSynchronize(stream_);
   drop_plans();
+  for (auto& e : phase_ev_)
+    if (e) cudaEventDestroy(e);
   for (void* p : allocs_) cudaFree(p);
   if (h_state_) cudaFreeHost(h_state_);
   if (h_latent_) cudaFreeHost(h_latent_);
@@ -556,8 +558,11 @@ bool MotEngine::gemm(Program& p, const bf16* x, int ldx, int m, const std::strin
     *err = std::string(e) + " (" + wname + ")";
     return false;
   }
-  p.ops.push_back([op](cudaStream_t s) { return gemm_launch(op, s); });
-  p.kernels += 1;
+  const double extra = (epi == EPI_GATED_RES || epi == EPI_RES) ? 2.0 * m * n : 0.0;
+  p.add([op](cudaStream_t s) { return gemm_launch(op, s); }, OP_GEMM, 1,
+        2.0 * (static_cast<double>(n) * k + static_cast<double>(m) * k + static_cast<double>(m) * n) +
+            2.0 * extra,
+        2.0 * m * n * static_cast<double>(k));
   return true;
 }
 
@@ -581,28 +586,28 @@ bool MotEngine::build(int b, std::string* err) {
                  int ldo) {
       if (ok && !gemm(p, x, ldx, m, wn, n, k, epi, bias, gate, resid, ldr, out, ldo, &e2)) ok = false;
     };
-    auto K = [](Program& p, Launch f) {
-      p.ops.push_back(std::move(f));
-      p.kernels += 1;
-    };
+    auto K = [](Program& p, Launch f) { p.add(std::move(f), OP_ELEMENTWISE); };
     auto scatter = [&](Program& p, const QkvScatter& q) {
-      K(p, [q](cudaStream_t s) {
+      const double parts = (q.q_col >= 0) + (q.k_col >= 0) + (q.v_col >= 0);
+      p.add([q](cudaStream_t s) {
         launch_qkv_scatter(q, s);
         return cudaGetLastError();
-      });
+      }, OP_QKV, 1, 4.0 * parts * q.rows * q.hidden);
     };
     auto attend = [&](Program& p, const AttnArgs& a) {
-      K(p, [a](cudaStream_t s) {
+      const double bq = 2.0 * a.batch * a.heads * a.lq * 128.0;
+      const double bkv = 4.0 * a.batch * a.heads * a.lk * 128.0;
+      p.add([a](cudaStream_t s) {
         launch_attention(a, s);
         return cudaGetLastError();
-      });
+      }, OP_ATTENTION, 1, 2.0 * bq + bkv, 4.0 * a.batch * a.heads * double(a.lq) * a.lk * 128.0);
     };
     auto ln_mod = [&](Program& p, const bf16* x, int rows, int cols, const float* scale,
                       const float* shift, bf16* y) {
-      K(p, [=](cudaStream_t s) {
+      p.add([=](cudaStream_t s) {
         launch_ln_modulate(x, cols, rows, cols, scale, shift, eps, y, cols, s);
         return cudaGetLastError();
-      });
+      }, OP_LAYERNORM, 1, 4.0 * rows * double(cols) + 8.0 * cols);
     };
     auto ln_aff = [&](Program& p, const bf16* x, int rows, int cols, const std::string& wn, bf16* y) {
       const bf16* w = W(wn + ".weight", cols);
@@ -612,10 +617,10 @@ bool MotEngine::build(int b, std::string* err) {
         e2 = "missing " + wn;
         return;
       }
-      K(p, [=](cudaStream_t s) {
+      p.add([=](cudaStream_t s) {
         launch_ln_affine(x, cols, rows, cols, w, bb, eps, y, cols, s);
         return cudaGetLastError();
-      });
+      }, OP_LAYERNORM, 1, 4.0 * rows * double(cols) + 4.0 * cols);
     };
     auto small = [&](Program& p, const bf16* x, int m, int k, const bf16* w, long long sn,
                      long long sk, const bf16* bias, int n, int act, bf16* y) {
@@ -624,10 +629,10 @@ bool MotEngine::build(int b, std::string* err) {
         e2 = "missing encoder/decoder weight";
         return;
       }
-      K(p, [=](cudaStream_t s) {
+      p.add([=](cudaStream_t s) {
         launch_small_linear(x, k, m, k, w, sn, sk, bias, n, act, y, n, s);
         return cudaGetLastError();
-      });
+      }, OP_SMALL, 1, 2.0 * (double(n) * k + double(m) * k + double(m) * n), 2.0 * m * n * double(k));
     };
     auto cross_q = [&](Program& p, const bf16* src, int rows, int rows_per_seq,
                        const std::string& pfx, bf16* qout) {
@@ -680,7 +685,7 @@ bool MotEngine::build(int b, std::string* err) {
     };
 
     // ---------------- prompt projection (cache.cpp:53-137 + build_condition text)
-    Program& pp = plan->prompt;
+    Program& pp = plan->prog[0];
     K(pp, [=](cudaStream_t s) {
       launch_f32_to_bf16(in_prompt_, prompt_bf_, static_cast<long long>(b) * Nt * D, s);
       return cudaGetLastError();
@@ -697,12 +702,13 @@ bool MotEngine::build(int b, std::string* err) {
     }
 
     // ---------------- prefix (cache.cpp:139-485)
-    Program& mp = plan->main;
+    Program& mp = plan->prog[1];
     K(mp, [=](cudaStream_t s) {
       launch_f32_to_bf16(in_state_, state_bf_, static_cast<long long>(b) * A, s);
       launch_f32_to_bf16(in_noise_, action_bf_, static_cast<long long>(b) * T * A, s);
       return cudaGetLastError();
     });
+    mp.ops.back().launches = 2;
     mp.kernels += 1;
     {
       const bf16* w_in = W("gwp.state.in.weight", static_cast<int64_t>(g.num_embodiments) * A * 128);
@@ -740,6 +746,7 @@ bool MotEngine::build(int b, std::string* err) {
       launch_modulation_add(temb_a_ + E, E, E, S, tables_final_, 1, 2 * E, comb_final_, s);
       return cudaGetLastError();
     });
+    mp.ops.back().launches = 4;
     mp.kernels += 3;
     for (int l = 0; l < L && ok; ++l) {
       const std::string ap = "gwp.blk." + std::to_string(l) + ".a";
@@ -851,22 +858,23 @@ bool MotEngine::build(int b, std::string* err) {
     }
 
     // ---------------- denoise (mot.cpp:358-496, unrolled over the schedule)
+    Program& dp = plan->prog[2];
     const bf16* ain_w = W("gwp.action.in.weight", static_cast<int64_t>(g.num_embodiments) * A * 128);
     const bf16* ain_b = W("gwp.action.in.bias", static_cast<int64_t>(g.num_embodiments) * 128);
     const bf16* dout_w = W("gwp.decode.out.weight", static_cast<int64_t>(g.num_embodiments) * 128 * A);
     const bf16* dout_b = W("gwp.decode.out.bias", static_cast<int64_t>(g.num_embodiments) * A);
     for (int s = 0; s < S && ok; ++s) {
       const int M = b * T;
-      small(mp, action_bf_, M, A, ain_w ? ain_w + static_cast<size_t>(emb) * A * 128 : nullptr, 1, 128,
+      small(dp, action_bf_, M, A, ain_w ? ain_w + static_cast<size_t>(emb) * A * 128 : nullptr, 1, 128,
             ain_b ? ain_b + emb * 128 : nullptr, 128, ACT_GELU_ERF, e1_);
-      small(mp, e1_, M, 128, W("gwp.action.mid.weight", 128 * 128), 128, 1,
+      small(dp, e1_, M, 128, W("gwp.action.mid.weight", 128 * 128), 128, 1,
             W("gwp.action.mid.bias", 128), 128, ACT_GELU_ERF, e2_);
-      G(mp, e2_, 128, M, "gwp.action.out", E, 128, EPI_BIAS, true, nullptr, nullptr, 0, ha_, E);
+      G(dp, e2_, 128, M, "gwp.action.out", E, 128, EPI_BIAS, true, nullptr, nullptr, 0, ha_, E);
       for (int l = 0; l < L && ok; ++l) {
         const std::string ap = "gwp.blk." + std::to_string(l) + ".a";
         const float* c = comb_steps_ + (static_cast<size_t>(s) * L + l) * 6 * E;
-        ln_mod(mp, ha_, M, E, c + E, c, nrm_);
-        G(mp, nrm_, E, M, ap + ".sa.qkv", 3 * H, E, EPI_BIAS, true, nullptr, nullptr, 0, qkv_, 3 * H);
+        ln_mod(dp, ha_, M, E, c + E, c, nrm_);
+        G(dp, nrm_, E, M, ap + ".sa.qkv", 3 * H, E, EPI_BIAS, true, nullptr, nullptr, 0, qkv_, 3 * H);
         QkvScatter q{};
         q.src = qkv_;
         q.ld_src = 3 * H;
@@ -891,7 +899,7 @@ bool MotEngine::build(int b, std::string* err) {
         q.kv_seq_stride = selfB;
         q.kv_head_stride = static_cast<long long>(P + T) * 128;
         q.kv_row_offset = P;
-        scatter(mp, q);
+        scatter(dp, q);
         AttnArgs at{};
         at.q = qbuf_;
         at.q_seq_stride = q.q_seq_stride;
@@ -907,11 +915,11 @@ bool MotEngine::build(int b, std::string* err) {
         at.scale = 1.0f / std::sqrt(128.0f);
         at.out = att_;
         at.ldo = H;
-        attend(mp, at);
-        G(mp, att_, H, M, ap + ".sa.o", E, H, EPI_GATED_RES, true, c + 2 * E, ha_, E, ha_, E);
-        ln_aff(mp, ha_, M, E, ap + ".ca_norm", nrm_);
-        G(mp, nrm_, E, M, ap + ".ca.q", H, E, EPI_BIAS, true, nullptr, nullptr, 0, cq_, H);
-        cross_q(mp, cq_, M, T, ap, qc_);
+        attend(dp, at);
+        G(dp, att_, H, M, ap + ".sa.o", E, H, EPI_GATED_RES, true, c + 2 * E, ha_, E, ha_, E);
+        ln_aff(dp, ha_, M, E, ap + ".ca_norm", nrm_);
+        G(dp, nrm_, E, M, ap + ".ca.q", H, E, EPI_BIAS, true, nullptr, nullptr, 0, cq_, H);
+        cross_q(dp, cq_, M, T, ap, qc_);
         AttnArgs cx{};
         cx.q = qc_;
         cx.q_seq_stride = static_cast<long long>(heads) * T * 128;
@@ -927,27 +935,27 @@ bool MotEngine::build(int b, std::string* err) {
         cx.scale = at.scale;
         cx.out = catt_;
         cx.ldo = H;
-        attend(mp, cx);
-        G(mp, catt_, H, M, ap + ".ca.o", E, H, EPI_RES, true, nullptr, ha_, E, ha_, E);
-        ln_mod(mp, ha_, M, E, c + 4 * E, c + 3 * E, nrm_);
-        G(mp, nrm_, E, M, ap + ".ffn.in", Fa, E, EPI_BIAS_GELU, true, nullptr, nullptr, 0, ffn_, Fa);
-        G(mp, ffn_, Fa, M, ap + ".ffn.out", E, Fa, EPI_GATED_RES, true, c + 5 * E, ha_, E, ha_, E);
+        attend(dp, cx);
+        G(dp, catt_, H, M, ap + ".ca.o", E, H, EPI_RES, true, nullptr, ha_, E, ha_, E);
+        ln_mod(dp, ha_, M, E, c + 4 * E, c + 3 * E, nrm_);
+        G(dp, nrm_, E, M, ap + ".ffn.in", Fa, E, EPI_BIAS_GELU, true, nullptr, nullptr, 0, ffn_, Fa);
+        G(dp, ffn_, Fa, M, ap + ".ffn.out", E, Fa, EPI_GATED_RES, true, c + 5 * E, ha_, E, ha_, E);
       }
       const float* cf = comb_final_ + static_cast<size_t>(s) * 2 * E;
-      ln_mod(mp, ha_, M, E, cf + E, cf, nrm_);
-      G(mp, nrm_, E, M, "gwp.decode.in", 128, E, EPI_BIAS_GELU_ERF, true, nullptr, nullptr, 0, d1_, 128);
-      small(mp, d1_, M, 128, W("gwp.decode.mid.weight", 128 * 128), 128, 1,
+      ln_mod(dp, ha_, M, E, cf + E, cf, nrm_);
+      G(dp, nrm_, E, M, "gwp.decode.in", 128, E, EPI_BIAS_GELU_ERF, true, nullptr, nullptr, 0, d1_, 128);
+      small(dp, d1_, M, 128, W("gwp.decode.mid.weight", 128 * 128), 128, 1,
             W("gwp.decode.mid.bias", 128), 128, ACT_GELU_ERF, d2_);
       bf16* vel = vel_ + static_cast<size_t>(s) * opt_.max_batch * T * A;
-      small(mp, d2_, M, 128, dout_w ? dout_w + static_cast<size_t>(emb) * 128 * A : nullptr, 1, A,
+      small(dp, d2_, M, 128, dout_w ? dout_w + static_cast<size_t>(emb) * 128 * A : nullptr, 1, A,
             dout_b ? dout_b + emb * A : nullptr, A, ACT_NONE, vel);
       const float* dts = dt_ + s;
-      K(mp, [=](cudaStream_t st) {
+      K(dp, [=](cudaStream_t st) {
         launch_euler(action_bf_, vel, M * A, dts, st);
         return cudaGetLastError();
       });
     }
-    K(mp, [=](cudaStream_t s) {
+    K(dp, [=](cudaStream_t s) {
       launch_bf16_to_f32(action_bf_, d_out_, static_cast<long long>(b) * T * A, s);
       return cudaGetLastError();
     });
@@ -960,21 +968,21 @@ bool MotEngine::build(int b, std::string* err) {
     // Plans built against an older split-K scratch hold freed pointers.
     for (auto it = plans_.begin(); it != plans_.end();) {
       if (it->second->scratch_gen != scratch_gen_) {
-        if (it->second->g_prompt) cudaGraphExecDestroy(it->second->g_prompt);
-        if (it->second->g_main) cudaGraphExecDestroy(it->second->g_main);
+        for (auto& gx : it->second->graph)
+          if (gx) cudaGraphExecDestroy(gx);
         it = plans_.erase(it);
       } else {
         ++it;
       }
     }
     if (opt_.graphs) {
-      for (int which = 0; which < 2; ++which) {
-        Program& p = which == 0 ? plan->prompt : plan->main;
+      for (int which = 0; which < 3; ++which) {
+        Program& p = plan->prog[which];
         cudaGraph_t graph = nullptr;
         CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
         cudaError_t le = cudaSuccess;
         for (auto& op : p.ops) {
-          le = op(stream_);
+          le = op.fn(stream_);
           if (le != cudaSuccess) break;
         }
         cudaError_t ce = cudaStreamEndCapture(stream_, &graph);
@@ -990,7 +998,7 @@ bool MotEngine::build(int b, std::string* err) {
           *err = std::string("graph instantiate: ") + cudaGetErrorString(ie);
           return false;
         }
-        (which == 0 ? plan->g_prompt : plan->g_main) = exec;
+        plan->graph[which] = exec;
       }
     }
     plans_[b] = std::move(plan);
@@ -1001,10 +1009,9 @@ bool MotEngine::build(int b, std::string* err) {
 }
 
 void MotEngine::drop_plans() {
-  for (auto& kv : plans_) {
-    if (kv.second->g_prompt) cudaGraphExecDestroy(kv.second->g_prompt);
-    if (kv.second->g_main) cudaGraphExecDestroy(kv.second->g_main);
-  }
+  for (auto& kv : plans_)
+    for (auto& gx : kv.second->graph)
+      if (gx) cudaGraphExecDestroy(gx);
   plans_.clear();
 }
 
@@ -1015,7 +1022,8 @@ int MotEngine::kernels_per_chunk(int batch, bool with_prompt) {
     if (!build(batch, &err)) return -1;
     it = plans_.find(batch);
   }
-  return it->second->main.kernels + (with_prompt ? it->second->prompt.kernels : 0);
+  return it->second->prog[1].kernels + it->second->prog[2].kernels +
+         (with_prompt ? it->second->prog[0].kernels : 0);
 }
 
 bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
@@ -1101,16 +1109,20 @@ bool MotEngine::run(int batch, std::string* err, EngineStats* stats) {
     const std::vector<float>& sig = prompt_sig_[i];
     hit = sig.size() == pn && std::memcmp(sig.data(), h_prompt_ + i * pn, pn * 4) == 0;
   }
-  auto exec = [&](Program& p, cudaGraphExec_t gexec) -> bool {
-    if (gexec) {
-      CK(cudaGraphLaunch(gexec, stream_));
+  auto exec = [&](int which) -> bool {
+    if (plan.graph[which]) {
+      CK(cudaGraphLaunch(plan.graph[which], stream_));
       return true;
     }
-    for (auto& op : p.ops) CK(op(stream_));
+    for (auto& op : plan.prog[which].ops) CK(op.fn(stream_));
     return true;
   };
+  if (!phase_ev_[0])
+    for (auto& e : phase_ev_) CK(cudaEventCreate(&e));
+  CK(cudaEventRecord(phase_ev_[0], stream_));
+  phase_prompt_ran_ = !hit;
   if (!hit) {
-    if (!exec(plan.prompt, plan.g_prompt)) return false;
+    if (!exec(0)) return false;
     if (opt_.prompt_cache) {
       for (int i = 0; i < batch; ++i) prompt_sig_[i].assign(h_prompt_ + i * pn, h_prompt_ + (i + 1) * pn);
       for (int i = batch; i < opt_.max_batch; ++i) prompt_sig_[i].clear();
@@ -1118,7 +1130,56 @@ bool MotEngine::run(int batch, std::string* err, EngineStats* stats) {
     }
   }
   if (stats) stats->prompt_cache_hit = hit ? 1 : 0;
-  return exec(plan.main, plan.g_main);
+  CK(cudaEventRecord(phase_ev_[1], stream_));
+  if (!exec(1)) return false;
+  CK(cudaEventRecord(phase_ev_[2], stream_));
+  if (!exec(2)) return false;
+  CK(cudaEventRecord(phase_ev_[3], stream_));
+  return true;
+}
+
+bool MotEngine::last_phase_ms(float* prompt, float* prefix, float* denoise) {
+  if (!phase_ev_[0] || cudaEventSynchronize(phase_ev_[3]) != cudaSuccess) return false;
+  cudaEventElapsedTime(prompt, phase_ev_[0], phase_ev_[1]);
+  cudaEventElapsedTime(prefix, phase_ev_[1], phase_ev_[2]);
+  cudaEventElapsedTime(denoise, phase_ev_[2], phase_ev_[3]);
+  return true;
+}
+
+bool MotEngine::profile(int batch, std::vector<OpProfile>* out, std::string* err) {
+  if (batch != staged_batch_) {
+    *err = "profile() batch differs from the staged batch";
+    return false;
+  }
+  auto it = plans_.find(batch);
+  if (it == plans_.end() || it->second->scratch_gen != scratch_gen_) {
+    if (!build(batch, err)) return false;
+    it = plans_.find(batch);
+  }
+  Plan& plan = *it->second;
+  size_t n = 0;
+  for (auto& p : plan.prog) n += p.ops.size();
+  std::vector<cudaEvent_t> ev(n + 1);
+  for (auto& e : ev) CK(cudaEventCreate(&e));
+  size_t i = 0;
+  CK(cudaEventRecord(ev[0], stream_));
+  for (auto& p : plan.prog)
+    for (auto& op : p.ops) {
+      CK(op.fn(stream_));
+      CK(cudaEventRecord(ev[++i], stream_));
+    }
+  CK(cudaStreamSynchronize(stream_));
+  out->clear();
+  i = 0;
+  for (int ph = 0; ph < 3; ++ph)
+    for (auto& op : plan.prog[ph].ops) {
+      OpProfile r{ph, op.kind, op.launches, 0.0f, op.bytes, op.flops};
+      cudaEventElapsedTime(&r.ms, ev[i], ev[i + 1]);
+      out->push_back(r);
+      ++i;
+    }
+  for (auto& e : ev) cudaEventDestroy(e);
+  return true;
 }
 
 bool MotEngine::fetch(const RequestView* reqs, int batch, float* out, std::string* err) {
@@ -1149,20 +1210,13 @@ bool MotEngine::predict(const RequestView* reqs, int batch, float* out, EngineSt
                         std::string* err) {
   using clk = std::chrono::steady_clock;
   const auto t0 = clk::now();
-  cudaEvent_t ev[3];
-  for (auto& e : ev) CK(cudaEventCreate(&e));
   bool ok = stage(reqs, batch, err);
-  if (ok) cudaEventRecord(ev[0], stream_);
   if (ok) ok = run(batch, err, stats);
-  if (ok) cudaEventRecord(ev[1], stream_);
   if (ok) ok = fetch(reqs, batch, out, err);
   if (ok && stats) {
-    float ms = 0;
-    cudaEventElapsedTime(&ms, ev[0], ev[1]);
-    stats->ms_denoise = ms;
+    last_phase_ms(&stats->ms_prompt, &stats->ms_prefix, &stats->ms_denoise);
     stats->ms_total = std::chrono::duration<float, std::milli>(clk::now() - t0).count();
   }
-  for (auto& e : ev) cudaEventDestroy(e);
   return ok;
 }
 

@@ -52,15 +52,38 @@ struct RequestView {
 };
 
 struct EngineStats {
-  float ms_total = 0, ms_h2d = 0, ms_prompt = 0, ms_prefix = 0, ms_denoise = 0, ms_d2h = 0;
+  float ms_total = 0, ms_prompt = 0, ms_prefix = 0, ms_denoise = 0;
   int prompt_cache_hit = 0;
 };
 
 using Launch = std::function<cudaError_t(cudaStream_t)>;
 
+// Kernel families, for the per-kernel profile (wam_b200_profile).
+enum OpKind : int { OP_GEMM = 0, OP_ATTENTION = 1, OP_LAYERNORM = 2, OP_QKV = 3, OP_SMALL = 4,
+                    OP_ELEMENTWISE = 5 };
+
+struct Op {
+  Launch fn;
+  int kind = OP_ELEMENTWISE;
+  int launches = 1;     // kernels this op launches
+  double bytes = 0.0;   // algorithmic HBM bytes (operands read + results written)
+  double flops = 0.0;   // algorithmic FLOPs
+};
+
 struct Program {
-  std::vector<Launch> ops;
+  std::vector<Op> ops;
   int kernels = 0;
+  void add(Launch f, int kind, int launches = 1, double bytes = 0.0, double flops = 0.0) {
+    ops.push_back(Op{std::move(f), kind, launches, bytes, flops});
+    kernels += launches;
+  }
+};
+
+// One profiled op: phase 0 = prompt projection, 1 = prefix, 2 = denoise.
+struct OpProfile {
+  int phase, kind, launches;
+  float ms;
+  double bytes, flops;
 };
 
 // Synthetic tensor distribution rule (scale, center); mirrors init_rule() of
@@ -89,6 +112,10 @@ class MotEngine {
   bool predict(const RequestView* reqs, int batch, float* out, EngineStats* stats, std::string* err);
   void reset();
   int kernels_per_chunk(int batch, bool with_prompt);
+  // Runs one chunk eagerly with CUDA events around every op (staged inputs).
+  bool profile(int batch, std::vector<OpProfile>* out, std::string* err);
+  // Device times of the phases of the last run() (ms): prompt, prefix, denoise.
+  bool last_phase_ms(float* prompt, float* prefix, float* denoise);
   // Debug view of device state as F32 (names: prefix_k, prefix_v, prompt_k,
   // prompt_v, velocity, actions).
   bool read_tensor(const std::string& name, int slot, int layer, float* out, size_t n,
@@ -106,10 +133,12 @@ class MotEngine {
             std::string* err);
 
   struct Plan {
-    Program prompt, main;
-    cudaGraphExec_t g_prompt = nullptr, g_main = nullptr;
+    Program prog[3];                      // prompt projection, prefix, denoise
+    cudaGraphExec_t graph[3] = {nullptr, nullptr, nullptr};
     int scratch_gen = 0;  // split-K scratch generation the launches point into
   };
+  cudaEvent_t phase_ev_[4] = {nullptr, nullptr, nullptr, nullptr};
+  bool phase_prompt_ran_ = false;
   void drop_plans();
   int scratch_gen_ = 0;
 

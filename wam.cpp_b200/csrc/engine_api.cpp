@@ -151,7 +151,7 @@ WAM_B200_API int wam_b200_predict_batch(wam_b200_engine* e, const wam_b200_reque
   if (!e->impl->predict(v.data(), batch, out, &es, &err)) return fail(st, code_of(err), err);
   if (stats) {
     stats->ms_total = es.ms_total;
-    stats->ms_device = es.ms_denoise;
+    stats->ms_device = es.ms_prompt + es.ms_prefix + es.ms_denoise;
     stats->prompt_cache_hit = es.prompt_cache_hit;
     stats->kernel_launches = e->impl->kernels_per_chunk(batch, !es.prompt_cache_hit);
     stats->resident_device_bytes = e->impl->resident_bytes();
@@ -198,6 +198,26 @@ WAM_B200_API void* wam_b200_stream(wam_b200_engine* e) {
 
 WAM_B200_API int wam_b200_kernel_launches(wam_b200_engine* e, int batch, int with_prompt) {
   return e ? e->impl->kernels_per_chunk(batch, with_prompt != 0) : -1;
+}
+
+WAM_B200_API int wam_b200_phase_ms(wam_b200_engine* e, float* prompt, float* prefix,
+                                   float* denoise) {
+  if (!e || !prompt || !prefix || !denoise) return WAM_B200_INVALID_ARGUMENT;
+  return e->impl->last_phase_ms(prompt, prefix, denoise) ? WAM_B200_OK : WAM_B200_CUDA_ERROR;
+}
+
+WAM_B200_API int wam_b200_profile(wam_b200_engine* e, int batch, wam_b200_op_profile* out,
+                                  int max_ops, wam_b200_status* st) {
+  if (!e || !out) return -fail(st, WAM_B200_INVALID_ARGUMENT, "engine and output are required");
+  std::vector<wamb::OpProfile> prof;
+  std::string err;
+  if (!e->impl->profile(batch, &prof, &err)) return -fail(st, code_of(err), err);
+  const int n = static_cast<int>(prof.size()) < max_ops ? static_cast<int>(prof.size()) : max_ops;
+  for (int i = 0; i < n; ++i)
+    out[i] = wam_b200_op_profile{prof[i].phase, prof[i].kind, prof[i].launches, prof[i].ms,
+                                 prof[i].bytes, prof[i].flops};
+  ok(st);
+  return n;
 }
 
 WAM_B200_API int wam_b200_read_tensor(wam_b200_engine* e, const char* name, int slot, int layer,

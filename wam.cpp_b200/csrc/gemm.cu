@@ -310,25 +310,15 @@ int pick_bt(int m) {
   return 256;
 }
 
-// Split-K factor: minimise (waves x k-blocks per split) plus a fixed cost for
-// the partial-tile round trip, over one resident CTA per SM.
+// Split-K factor. Below ~3/4 of a wave of output tiles the K range is split so
+// that tiles x splits fills at most one wave of SMs, keeping >= 4 k-blocks
+// (256 of K) per split so that the per-CTA set-up and the F32 partial round
+// trip stay small next to the weight stream.
 int pick_splits(int tiles, int nkb, int num_sms) {
-  if (tiles >= num_sms || nkb < 4) return 1;
-  int best = 1;
-  double best_cost = 1e30;
-  const int max_s = nkb < 32 ? nkb : 32;
-  for (int s = 1; s <= max_s; ++s) {
-    if (nkb / s < 2) break;
-    const int ctas = tiles * s;
-    const int waves = (ctas + num_sms - 1) / num_sms;
-    const double per = static_cast<double>((nkb + s - 1) / s);
-    const double cost = waves * per + (s > 1 ? 2.0 : 0.0);
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = s;
-    }
-  }
-  return best;
+  if (tiles * 4 >= num_sms * 3 || nkb < 8) return 1;
+  int s = num_sms / tiles;
+  if (s > nkb / 4) s = nkb / 4;
+  return s < 1 ? 1 : s;
 }
 
 template <int BT>

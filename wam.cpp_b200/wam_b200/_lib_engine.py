@@ -36,6 +36,11 @@ class Stats(C.Structure):
                 ("kernel_launches", C.c_int), ("resident_device_bytes", C.c_uint64)]
 
 
+class OpProfile(C.Structure):
+    _fields_ = [("phase", C.c_int), ("kind", C.c_int), ("launches", C.c_int), ("ms", C.c_float),
+                ("bytes", C.c_double), ("flops", C.c_double)]
+
+
 def attach(lib, sig) -> None:
     vp, i32, sz = C.c_void_p, C.c_int, C.c_size_t
     f32p = C.POINTER(C.c_float)
@@ -54,3 +59,5 @@ def attach(lib, sig) -> None:
     sig(lib, "wam_b200_stream", vp, [vp])
     sig(lib, "wam_b200_kernel_launches", i32, [vp, i32, i32])
     sig(lib, "wam_b200_read_tensor", i32, [vp, C.c_char_p, i32, i32, f32p, sz, st])
+    sig(lib, "wam_b200_phase_ms", i32, [vp, f32p, f32p, f32p])
+    sig(lib, "wam_b200_profile", i32, [vp, i32, C.POINTER(OpProfile), i32, st])

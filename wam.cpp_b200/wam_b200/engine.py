@@ -15,7 +15,10 @@ from dataclasses import dataclass
 import numpy as np
 
 from ._lib import load
-from ._lib_engine import GEOM_FIELDS, Geometry, Options, Request, Stats, Status
+from ._lib_engine import GEOM_FIELDS, Geometry, OpProfile, Options, Request, Stats, Status
+
+KINDS = ("gemm", "attention", "layernorm", "qkv_scatter", "small_linear", "elementwise")
+PHASES = ("prompt", "prefix", "denoise")
 
 
 class EngineError(RuntimeError):
@@ -152,6 +155,25 @@ class Engine:
 
     def kernel_launches(self, batch: int, with_prompt: bool = True) -> int:
         return self.lib.wam_b200_kernel_launches(self.h, batch, 1 if with_prompt else 0)
+
+    def phase_ms(self) -> dict:
+        v = [C.c_float(), C.c_float(), C.c_float()]
+        rc = self.lib.wam_b200_phase_ms(self.h, *[C.byref(x) for x in v])
+        if rc != 0:
+            raise EngineError(rc, "wam_b200_phase_ms")
+        return dict(zip(PHASES, (x.value for x in v)))
+
+    def profile(self, batch: int) -> list[dict]:
+        """Per-op device times of one chunk on the staged batch (eager, events
+        around every op)."""
+        n = 20000
+        arr = (OpProfile * n)()
+        st = Status()
+        rc = self.lib.wam_b200_profile(self.h, batch, arr, n, C.byref(st))
+        if rc < 0:
+            _raise(self.lib, -rc, st, "wam_b200_profile")
+        return [{"phase": PHASES[a.phase], "kind": KINDS[a.kind], "launches": a.launches,
+                 "ms": a.ms, "bytes": a.bytes, "flops": a.flops} for a in arr[:rc]]
 
     def reset(self):
         self.lib.wam_b200_reset(self.h)
