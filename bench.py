@@ -224,6 +224,20 @@ def roofline_from_profile(prof: list[dict], pk: dict) -> tuple[dict, dict, dict]
     breakdown = {k: {"ms": round(v, 3), "share": round(v / total, 4)} for k, v in
                  sorted(br.items(), key=lambda kv: -kv[1])}
     breakdown["_total_eager_ms"] = round(total, 3)
+    shapes = {}
+    for o in prof:
+        if o["kind"] == "gemm" and o["phase"] in ("denoise", "prefix"):
+            m, n, k, sp = o["shape"]
+            key = f'{o["phase"]}:{m}x{n}x{k}/s{sp}'
+            e = shapes.setdefault(key, [0, 0.0, 0.0])
+            e[0] += 1
+            e[1] += o["ms"]
+            e[2] += o["bytes"] if o["phase"] == "denoise" else o["flops"]
+    breakdown["_gemm_shapes"] = {
+        k: {"launches": v[0], "avg_us": round(v[1] / v[0] * 1e3, 2),
+            ("GB/s" if k.startswith("denoise") else "TFLOP/s"):
+                round(v[2] / (v[1] / 1e3) / (1e9 if k.startswith("denoise") else 1e12), 1)}
+        for k, v in sorted(shapes.items(), key=lambda kv: -kv[1][1])}
     return hbm, tc, breakdown
 
 

@@ -56,10 +56,13 @@ WAM_B200_API const char* wam_b200_last_error(void);
  * (GGUF ne = {k, n}), out: [m, ldo] BF16 (F32 for epilogue 6).
  * epilogue: 0 bias, 1 bias+GELU(tanh), 2 bias+SiLU, 3 gated residual
  * (r + linear * gate), 4 residual (r + linear), 5 F32 accumulate + bias,
- * 6 raw F32 accumulator. workspace/counters: split-K scratch (counters zeroed
- * before first use; the kernel leaves them zero). force_splits <= 0 picks
- * automatically. error: device word receiving a non-zero code on a pipeline
- * timeout.
+ * 6 raw F32 accumulator, 7 bias then GELU(tanh) of the rounded linear,
+ * 8 bias then exact-erf GELU. Split-K partial tiles are reduced through
+ * distributed shared memory inside a thread-block cluster when workspace is
+ * NULL (splits 1, 2, 4 or 8), or through the caller's global workspace
+ * (wam_b200_gemm_scratch_floats floats; counters zeroed before first use, the
+ * kernel leaves them zero). force_splits <= 0 picks automatically. error:
+ * device word receiving a non-zero code on a pipeline timeout.
  * Replaces: linear / linear_with_activation / linear_gelu_with_activation
  * (src/models/gwp05/engine/weights.cpp:786-849) and gated_residual
  * (src/models/gwp05/engine/mot.cpp:161-173). */
@@ -225,6 +228,7 @@ typedef struct wam_b200_op_profile {
   int phase, kind, launches;
   float ms;
   double bytes, flops;
+  int shape[4]; /* GEMM: m, n, k, split-K factor */
 } wam_b200_op_profile;
 WAM_B200_API int wam_b200_profile(wam_b200_engine* engine, int batch, wam_b200_op_profile* out,
                                   int max_ops, wam_b200_status* status);

@@ -40,31 +40,44 @@ SHAPES = [
 ]
 
 
+@pytest.mark.parametrize("mode", ["cluster", "workspace"])
 @pytest.mark.parametrize("m,n,k", SHAPES)
-def test_gemm_f32_accumulator(cuda_device, m, n, k):
+def test_gemm_f32_accumulator(cuda_device, m, n, k, mode):
     from wam_b200 import ops
 
     x, w, _ = make(m, n, k)
-    y = ops.gemm(x, w, epilogue=ops.EPI_F32_OUT)
+    scratch = ops.Scratch() if mode == "workspace" else None
+    y = ops.gemm(x, w, epilogue=ops.EPI_F32_OUT, scratch=scratch)
     ref = x.float() @ w.float().T
     torch.cuda.synchronize()
     assert rel_l2(y, ref) < 1e-5
 
 
-@pytest.mark.parametrize("splits", [1, 2, 3, 7])
-def test_gemm_forced_splits_deterministic(cuda_device, splits):
+@pytest.mark.parametrize("splits,mode", [(1, "cluster"), (2, "cluster"), (4, "cluster"),
+                                         (8, "cluster"), (3, "workspace"), (7, "workspace"),
+                                         (4, "workspace")])
+def test_gemm_forced_splits_deterministic(cuda_device, splits, mode):
     from wam_b200 import ops
 
     x, w, _ = make(48, 512, 1024, seed=1)
-    s = ops.Scratch()
+    s = ops.Scratch() if mode == "workspace" else None
     y1 = ops.gemm(x, w, epilogue=ops.EPI_F32_OUT, scratch=s, force_splits=splits)
     y2 = ops.gemm(x, w, epilogue=ops.EPI_F32_OUT, scratch=s, force_splits=splits)
     ref = x.float() @ w.float().T
     torch.cuda.synchronize()
     assert torch.equal(y1, y2)
     assert rel_l2(y1, ref) < 1e-5
-    assert s.error_code() == 0
-    assert int(s.counters.abs().sum()) == 0
+    if s is not None:
+        assert s.error_code() == 0
+        assert int(s.counters.abs().sum()) == 0
+
+
+def test_gemm_cluster_rejects_odd_splits(cuda_device):
+    from wam_b200 import ops
+
+    x, w, _ = make(48, 512, 1024, seed=1)
+    with pytest.raises(RuntimeError, match="cluster split-K"):
+        ops.gemm(x, w, epilogue=ops.EPI_F32_OUT, force_splits=3)
 
 
 def bf(x):
@@ -76,7 +89,8 @@ def gelu_tanh(v):
 
 
 @pytest.mark.parametrize("m,n,k", [(48, 3072, 3072), (768, 1024, 512), (16, 384, 128)])
-@pytest.mark.parametrize("epi", ["bias", "gelu", "silu", "gated", "res", "f32bias"])
+@pytest.mark.parametrize("epi", ["bias", "gelu", "gelu_r", "gelu_erf", "silu", "gated", "res",
+                                 "f32bias"])
 def test_gemm_epilogues(cuda_device, m, n, k, epi):
     from wam_b200 import ops
 
@@ -91,6 +105,12 @@ def test_gemm_epilogues(cuda_device, m, n, k, epi):
     elif epi == "gelu":
         y = ops.gemm(x, w, ops.EPI_BIAS_GELU, bias=b)
         ref = bf(gelu_tanh(bf(acc) + b.float()))
+    elif epi == "gelu_r":
+        y = ops.gemm(x, w, ops.EPI_BIAS_GELU_R, bias=b)
+        ref = bf(gelu_tanh(lin))
+    elif epi == "gelu_erf":
+        y = ops.gemm(x, w, ops.EPI_BIAS_GELU_ERF, bias=b)
+        ref = bf(0.5 * lin * (1.0 + torch.erf(lin / 2 ** 0.5)))
     elif epi == "silu":
         y = ops.gemm(x, w, ops.EPI_BIAS_SILU, bias=b)
         ref = bf(lin * torch.sigmoid(lin))

@@ -12,6 +12,7 @@
 // the prefix attention (engine/cache.cpp:274-287) and the cached cross attention
 // (mot.cpp:299-321).
 #include "kernels.h"
+#include "launch.cuh"
 #include "ptx.cuh"
 
 namespace wamb {
@@ -55,6 +56,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   const int head = blockIdx.y;
   const int seq = blockIdx.z;
 
+  griddep_wait();
+  griddep_launch_dependents();
   const bf16* qg = a.q + seq * a.q_seq_stride + head * a.q_head_stride + static_cast<long long>(q0) * kD;
   const bf16* kg = a.k + seq * a.kv_seq_stride + head * a.kv_head_stride;
   const bf16* vg = a.v + seq * a.kv_seq_stride + head * a.kv_head_stride;
@@ -213,7 +216,7 @@ cudaError_t attention_init() {
 
 void launch_attention(const AttnArgs& a, cudaStream_t s) {
   dim3 grid((a.lq + kBQ - 1) / kBQ, a.heads, a.batch);
-  attention_kernel<<<grid, 128, kSmem, s>>>(a);
+  launch_pdl(attention_kernel, grid, dim3(128), kSmem, s, a);
 }
 
 }  // namespace wamb

@@ -7,7 +7,9 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "launch.cuh"
 #include "mathops.cuh"
+#include "ptx.cuh"
 
 namespace wamb {
 
@@ -48,6 +50,8 @@ template <int MODE>
 __global__ void __launch_bounds__(kRowsPerBlock * 32)
     ln_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
               const void* pb, float eps, bf16* __restrict__ y, int ldy) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -97,6 +101,8 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
 
 // One block of 3 warps per token row: warp 0 = q, 1 = k, 2 = v.
 __global__ void __launch_bounds__(96) qkv_scatter_kernel(const QkvScatter a) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int row = blockIdx.x;
   const int which = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -184,6 +190,8 @@ __global__ void small_linear_kernel(const bf16* __restrict__ x, int ldx, int m, 
                                     const bf16* __restrict__ w, long long w_sn, long long w_sk,
                                     const bf16* __restrict__ b, int n, int act,
                                     bf16* __restrict__ y, int ldy) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   const int lane = threadIdx.x & 31;
   for (long long o = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -208,6 +216,8 @@ __global__ void small_linear_kernel(const bf16* __restrict__ x, int ldx, int m, 
 __global__ void modulation_add_kernel(const bf16* __restrict__ mod, int ld_mod, int period,
                                       int steps, const bf16* const* __restrict__ tables,
                                       int layers, int width, float* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long total = static_cast<long long>(steps) * layers * width;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -221,17 +231,23 @@ __global__ void modulation_add_kernel(const bf16* __restrict__ mod, int ld_mod, 
 }
 
 __global__ void silu_kernel(const bf16* __restrict__ x, bf16* __restrict__ y, int n) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) y[i] = __float2bfloat16_rn(silu(__bfloat162float(x[i])));
 }
 
 __global__ void f32_to_bf16_kernel(const float* __restrict__ x, bf16* __restrict__ y, long long n) {
+  griddep_wait();
+  griddep_launch_dependents();
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x)
     y[i] = __float2bfloat16_rn(x[i]);
 }
 
 __global__ void bf16_to_f32_kernel(const bf16* __restrict__ x, float* __restrict__ y, long long n) {
+  griddep_wait();
+  griddep_launch_dependents();
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x)
     y[i] = __bfloat162float(x[i]);
@@ -239,6 +255,8 @@ __global__ void bf16_to_f32_kernel(const bf16* __restrict__ x, float* __restrict
 
 __global__ void patchify_kernel(const float* __restrict__ lat, int batch, int ch, int gh, int gw,
                                 bf16* __restrict__ cols) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int kk = ch * 4;
   const long long total = static_cast<long long>(batch) * gh * gw * kk;
   const int lh = 2 * gh, lw = 2 * gw;
@@ -258,6 +276,8 @@ __global__ void patchify_kernel(const float* __restrict__ lat, int batch, int ch
 // ggml_add(action, ggml_mul(velocity, dt)) in F32, stored BF16 (weights.cpp:897-901).
 __global__ void euler_kernel(bf16* __restrict__ a, const bf16* __restrict__ v, int n,
                              const float* __restrict__ dt) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) {
     const float prod = __fmul_rn(__bfloat162float(v[i]), *dt);
@@ -273,6 +293,8 @@ __device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
 
 __global__ void synth_kernel(bf16* __restrict__ w, long long n, unsigned long long seed, float k,
                              float center) {
+  griddep_wait();
+  griddep_launch_dependents();
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const unsigned long long h =
@@ -297,55 +319,58 @@ inline int grid_for(long long n, int threads) {
 void launch_ln_modulate(const bf16* x, int ldx, int rows, int cols, const float* scale,
                         const float* shift, float eps, bf16* y, int ldy, cudaStream_t s) {
   const int grid = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
-  ln_kernel<0><<<grid, kRowsPerBlock * 32, 0, s>>>(x, ldx, rows, cols, scale, shift, eps, y, ldy);
+  launch_pdl(ln_kernel<0>, dim3(grid), dim3(kRowsPerBlock * 32), 0, s, x, ldx, rows, cols,
+             static_cast<const void*>(scale), static_cast<const void*>(shift), eps, y, ldy);
 }
 
 void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w, const bf16* b,
                       float eps, bf16* y, int ldy, cudaStream_t s) {
   const int grid = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
-  ln_kernel<1><<<grid, kRowsPerBlock * 32, 0, s>>>(x, ldx, rows, cols, w, b, eps, y, ldy);
+  launch_pdl(ln_kernel<1>, dim3(grid), dim3(kRowsPerBlock * 32), 0, s, x, ldx, rows, cols,
+             static_cast<const void*>(w), static_cast<const void*>(b), eps, y, ldy);
 }
 
 void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s) {
-  qkv_scatter_kernel<<<a.rows, 96, 0, s>>>(a);
+  launch_pdl(qkv_scatter_kernel, dim3(a.rows), dim3(96), 0, s, a);
 }
 
 void launch_small_linear(const bf16* x, int ldx, int m, int k, const bf16* w, long long w_sn,
                          long long w_sk, const bf16* b, int n, int act, bf16* y, int ldy,
                          cudaStream_t s) {
   const long long outs = static_cast<long long>(m) * n;
-  small_linear_kernel<<<grid_for(outs * 32, 256), 256, 0, s>>>(x, ldx, m, k, w, w_sn, w_sk, b, n,
-                                                               act, y, ldy);
+  launch_pdl(small_linear_kernel, dim3(grid_for(outs * 32, 256)), dim3(256), 0, s, x, ldx, m, k, w,
+             w_sn, w_sk, b, n, act, y, ldy);
 }
 
 void launch_modulation_add(const bf16* mod, int ld_mod, int period, int steps,
                            const bf16* const* tables, int layers, int width, float* combined,
                            cudaStream_t s) {
   const long long n = static_cast<long long>(steps) * layers * width;
-  modulation_add_kernel<<<grid_for(n, 256), 256, 0, s>>>(mod, ld_mod, period, steps, tables,
-                                                          layers, width, combined);
+  launch_pdl(modulation_add_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, mod, ld_mod, period,
+             steps, tables, layers, width, combined);
 }
 
 void launch_silu(const bf16* x, bf16* y, int n, cudaStream_t s) {
-  silu_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, y, n);
+  launch_pdl(silu_kernel, dim3((n + 255) / 256), dim3(256), 0, s, x, y, n);
 }
 
 void launch_f32_to_bf16(const float* x, bf16* y, long long n, cudaStream_t s) {
-  f32_to_bf16_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n);
+  launch_pdl(f32_to_bf16_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, x, y, n);
 }
 
 void launch_bf16_to_f32(const bf16* x, float* y, long long n, cudaStream_t s) {
-  bf16_to_f32_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n);
+  launch_pdl(bf16_to_f32_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, x, y, n);
 }
 
 void launch_patchify(const float* latent, int batch, int channels, int gh, int gw, bf16* cols,
                      cudaStream_t s) {
   const long long n = static_cast<long long>(batch) * gh * gw * channels * 4;
-  patchify_kernel<<<grid_for(n, 256), 256, 0, s>>>(latent, batch, channels, gh, gw, cols);
+  launch_pdl(patchify_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, latent, batch, channels, gh,
+             gw, cols);
 }
 
 void launch_euler(bf16* action, const bf16* velocity, int n, const float* dt, cudaStream_t s) {
-  euler_kernel<<<(n + 255) / 256, 256, 0, s>>>(action, velocity, n, dt);
+  launch_pdl(euler_kernel, dim3((n + 255) / 256), dim3(256), 0, s, action, velocity, n, dt);
 }
 
 void launch_synth_bf16(bf16* w, long long n, unsigned long long seed, double scale, double center,
@@ -354,7 +379,8 @@ void launch_synth_bf16(bf16* w, long long n, unsigned long long seed, double sca
   // to F32 once so host (numpy) and device apply the same constant.
   const double ih4_std = std::sqrt(4.0 * (65536.0 * 65536.0 - 1.0) / 12.0);
   const float k = static_cast<float>(scale / ih4_std);
-  synth_kernel<<<grid_for(n, 256), 256, 0, s>>>(w, n, seed, k, static_cast<float>(center));
+  launch_pdl(synth_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, w, n, seed, k,
+             static_cast<float>(center));
 }
 
 }  // namespace wamb

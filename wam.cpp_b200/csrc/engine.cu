@@ -519,38 +519,8 @@ bool MotEngine::gemm(Program& p, const bf16* x, int ldx, int m, const std::strin
     *err = "missing or mis-shaped weight " + wname;
     return false;
   }
-  int tiles = 0;
-  const size_t need = gemm_scratch_floats(m, n, k, sms_, 0, &tiles);
-  if (need > ws_floats_ || tiles > counter_slots_) {
-    // Grow the shared split-K scratch; programs built earlier hold the old
-    // pointers, so they are dropped and rebuilt on next use.
-    if (ws_) {
-      cudaStreamSynchronize(stream_);
-      for (auto it = allocs_.begin(); it != allocs_.end();) {
-        if (*it == ws_ || *it == counters_) {
-          cudaFree(*it);
-          it = allocs_.erase(it);
-        } else {
-          ++it;
-        }
-      }
-      ws_ = nullptr;
-      counters_ = nullptr;
-    }
-    ++scratch_gen_;
-    ws_floats_ = std::max(need, ws_floats_) * 2;
-    counter_slots_ = std::max(tiles, counter_slots_) * 2 + 64;
-    if (!(ws_ = dalloc<float>(ws_floats_, err))) return false;
-    if (!(counters_ = dalloc<unsigned>(counter_slots_, err))) return false;
-    cudaStreamSynchronize(stream_);
-    *err = "__rebuild__";
-    return false;
-  }
+  // Split-K partials are reduced inside thread-block clusters: no scratch.
   GemmScratch sc;
-  sc.workspace = ws_;
-  sc.workspace_floats = ws_floats_;
-  sc.counters = counters_;
-  sc.counter_slots = counter_slots_;
   sc.error = err_word_;
   GemmOp op;
   const char* e = gemm_plan(&op, x, ldx, m, w, n, k, epi, b, gate, resid, ldr, out, ldo, sc, sms_, 0);
@@ -563,6 +533,11 @@ bool MotEngine::gemm(Program& p, const bf16* x, int ldx, int m, const std::strin
         2.0 * (static_cast<double>(n) * k + static_cast<double>(m) * k + static_cast<double>(m) * n) +
             2.0 * extra,
         2.0 * m * n * static_cast<double>(k));
+  Op& rec = p.ops.back();
+  rec.shape[0] = m;
+  rec.shape[1] = n;
+  rec.shape[2] = k;
+  rec.shape[3] = op.args.splits;
   return true;
 }
 
@@ -1173,7 +1148,8 @@ bool MotEngine::profile(int batch, std::vector<OpProfile>* out, std::string* err
   i = 0;
   for (int ph = 0; ph < 3; ++ph)
     for (auto& op : plan.prog[ph].ops) {
-      OpProfile r{ph, op.kind, op.launches, 0.0f, op.bytes, op.flops};
+      OpProfile r{ph, op.kind, op.launches, 0.0f, op.bytes, op.flops,
+                  {op.shape[0], op.shape[1], op.shape[2], op.shape[3]}};
       cudaEventElapsedTime(&r.ms, ev[i], ev[i + 1]);
       out->push_back(r);
       ++i;

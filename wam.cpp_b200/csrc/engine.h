@@ -68,6 +68,7 @@ struct Op {
   int launches = 1;     // kernels this op launches
   double bytes = 0.0;   // algorithmic HBM bytes (operands read + results written)
   double flops = 0.0;   // algorithmic FLOPs
+  int shape[4] = {0, 0, 0, 0};  // GEMM: m, n, k, split-K factor
 };
 
 struct Program {
@@ -84,6 +85,7 @@ struct OpProfile {
   int phase, kind, launches;
   float ms;
   double bytes, flops;
+  int shape[4];
 };
 
 // Synthetic tensor distribution rule (scale, center); mirrors init_rule() of

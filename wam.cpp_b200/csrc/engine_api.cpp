@@ -215,7 +215,9 @@ WAM_B200_API int wam_b200_profile(wam_b200_engine* e, int batch, wam_b200_op_pro
   const int n = static_cast<int>(prof.size()) < max_ops ? static_cast<int>(prof.size()) : max_ops;
   for (int i = 0; i < n; ++i)
     out[i] = wam_b200_op_profile{prof[i].phase, prof[i].kind, prof[i].launches, prof[i].ms,
-                                 prof[i].bytes, prof[i].flops};
+                                 prof[i].bytes, prof[i].flops,
+                                 {prof[i].shape[0], prof[i].shape[1], prof[i].shape[2],
+                                  prof[i].shape[3]}};
   ok(st);
   return n;
 }

@@ -18,6 +18,7 @@
 // path (src/models/gwp05/engine/weights.cpp:786-849; cuBLAS route in
 // patches/llama-b9866-native-bf16.patch:259-313).
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -39,12 +40,18 @@ struct Cfg {
   static constexpr int A_BYTES = kBN * kBK * 2;
   static constexpr int B_BYTES = BT * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  // Small token tiles (the weight-streaming regime) keep ~96 KB of stages so
+  // that two CTAs share an SM; large tiles keep a deep single-CTA pipeline.
+  static constexpr int MIN_BLOCKS = BT <= 64 ? 2 : 1;
+  static constexpr int BUDGET = BT <= 64 ? 96 * 1024 : 200 * 1024;
+  static constexpr int STAGES_RAW = BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int TMEM_COLS = BT <= 32 ? 32 : (BT <= 64 ? 64 : (BT <= 128 ? 128 : 256));
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int PARTIAL_BYTES = BT * kBN * 4;  // F32 split-K partial tile
   static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "UMMA N for M=128");
   static_assert(STAGES >= 2, "pipeline depth");
+  static_assert(PARTIAL_BYTES <= STAGES * STAGE_BYTES, "partial tile reuses the stage buffers");
 };
 
 __device__ __forceinline__ void store_out(const GemmArgs& a, int m, int n, float acc, float b,
@@ -106,8 +113,10 @@ __device__ __forceinline__ void store_out(const GemmArgs& a, int m, int n, float
   }
 }
 
+// CTA x = (tile, split) with the split index fastest, so that in cluster mode
+// one thread-block cluster holds exactly the splits of one output tile.
 template <int BT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, Cfg<BT>::MIN_BLOCKS)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                         const __grid_constant__ CUtensorMap tm_x, const GemmArgs args) {
   using C = Cfg<BT>;
@@ -121,18 +130,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accum = empty + C::STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  float* partial = reinterpret_cast<float*>(smem);  // reuses the stages after the mainloop
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  const int tile_m = blockIdx.x % args.tiles_m;
-  const int rest = blockIdx.x / args.tiles_m;
-  const int tile_n = rest % args.tiles_n;
-  const int split = rest / args.tiles_n;
+  const int split = blockIdx.x % args.splits;
+  const int tile = blockIdx.x / args.splits;
+  const int tile_m = tile % args.tiles_m;
+  const int tile_n = tile / args.tiles_m;
   const int kb0 = static_cast<int>((static_cast<long long>(split) * args.num_kb) / args.splits);
   const int kb1 =
       static_cast<int>((static_cast<long long>(split + 1) * args.num_kb) / args.splits);
   const int nkb = kb1 - kb0;
+  const bool cluster_mode = args.splits > 1 && args.split_mode == SPLIT_CLUSTER;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tm_w);
@@ -154,11 +165,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  bool ok = true;
+  const int q = warp & 3;
+  const int row = q * 32 + lane;
+  const int n = tile_n * kBN + row;
+  const bool n_ok = n < args.n;
+  const int m_base = tile_m * BT;
+  float bias_v = 0.0f, gate_v = 0.0f;
+
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
-      for (int i = 0; i < nkb; ++i) {
+      const int pre = nkb < C::STAGES ? nkb : C::STAGES;
+      // Weights never depend on the preceding kernel: start streaming them
+      // before waiting for it (programmatic dependent launch).
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+        tma_load_2d(smem_a + i * C::A_BYTES, &tm_w, &full[i], (kb0 + i) * kBK, tile_n * kBN, pol_w);
+      }
+      griddep_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(smem_b + i * C::B_BYTES, &tm_x, &full[i], (kb0 + i) * kBK, tile_m * BT, pol_x);
+      for (int i = pre; i < nkb; ++i) {
         const int s = i % C::STAGES;
         const uint32_t ph = (i / C::STAGES) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1)) {
@@ -194,18 +223,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(accum);
     }
   } else {
-    // Epilogue: warps 2..5; TMEM lane quadrant is fixed by warp % 4.
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    const int n = tile_n * kBN + row;
-    const bool n_ok = n < args.n;
-    const float b = (args.bias && n_ok) ? __bfloat162float(args.bias[n]) : 0.0f;
-    const float g = (args.gate && n_ok) ? args.gate[n] : 0.0f;
-    const bool ok = mbar_wait(accum, 0);
+    // Epilogue warps 2..5; the TMEM lane quadrant is fixed by warp % 4.
+    griddep_wait();  // residual / gate / outputs are touched only after the preceding kernel
+    bias_v = (args.bias && n_ok) ? __bfloat162float(args.bias[n]) : 0.0f;
+    gate_v = (args.gate && n_ok) ? args.gate[n] : 0.0f;
+    ok = mbar_wait(accum, 0);
     if (!ok) atomicCAS(args.error, 0u, static_cast<unsigned>(kErrEpilogueTimeout));
     tc_fence_after();
+    griddep_launch_dependents();
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    const int m_base = tile_m * BT;
     if (args.splits == 1) {
 #pragma unroll 1
       for (int c = 0; c < BT; c += 16) {
@@ -216,12 +242,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int m = m_base + c + j;
-            if (m < args.m) store_out(args, m, n, __uint_as_float(r[j]), b, g);
+            if (m < args.m) store_out(args, m, n, __uint_as_float(r[j]), bias_v, gate_v);
           }
         }
       }
+    } else if (cluster_mode) {
+      // Stage this split's F32 partial tile [column][row] in shared memory.
+#pragma unroll 1
+      for (int c = 0; c < BT; c += 16) {
+        uint32_t r[16];
+        tmem_ld_x16(taddr + c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) partial[(c + j) * kBN + row] = __uint_as_float(r[j]);
+      }
     } else {
-      const int tile_id = tile_m * args.tiles_n + tile_n;
+      // Workspace mode: partial tile to global memory; the last CTA of the tile
+      // to arrive reduces all partials in split order and runs the epilogue.
+      const int tile_id = tile;
       float* ws_tile = args.workspace + static_cast<size_t>(tile_id) * args.splits * BT * kBN;
       float* ws = ws_tile + static_cast<size_t>(split) * BT * kBN;
 #pragma unroll 1
@@ -243,19 +281,62 @@ __global__ void __launch_bounds__(kThreads, 1)
         __threadfence();
         if (ok && n_ok) {
 #pragma unroll 1
-          for (int c = 0; c < BT; ++c) {
-            const int m = m_base + c;
-            if (m >= args.m) break;
-            float acc = 0.0f;
+          for (int c0 = 0; c0 < BT; c0 += 8) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-            for (int s = 0; s < args.splits; ++s)
-              acc += __ldcg(ws_tile + (static_cast<size_t>(s) * BT + c) * kBN + row);
-            store_out(args, m, n, acc, b, g);
+            for (int s = 0; s < args.splits; ++s) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                acc[j] += __ldcg(ws_tile + (static_cast<size_t>(s) * BT + c0 + j) * kBN + row);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int m = m_base + c0 + j;
+              if (m < args.m) store_out(args, m, n, acc[j], bias_v, gate_v);
+            }
           }
         }
         if (threadIdx.x == 64) args.counters[tile_id] = 0u;
       }
     }
+  }
+
+  __syncwarp();
+  if (cluster_mode) {
+    // All partial tiles of this output tile are in the cluster's shared memory.
+    cluster_sync_all();
+    if (warp >= 2) {
+      const int S = args.splits;
+      const int cols = (BT + S - 1) / S;
+      const int c0 = split * cols;
+      const int c1 = c0 + cols < BT ? c0 + cols : BT;
+      const uint32_t base = smem_u32(partial) + static_cast<uint32_t>(row) * 4u;
+      uint32_t peer[8];
+#pragma unroll
+      for (int p = 0; p < 8; ++p) peer[p] = mapa_shared(base, p < S ? p : 0);
+#pragma unroll 1
+      for (int c = c0; c < c1; c += 4) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          if (p < S) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if (c + j < c1)
+                acc[j] += ld_shared_cluster_f32(peer[p] + static_cast<uint32_t>((c + j) * kBN) * 4u);
+          }
+        }
+        if (ok && n_ok) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int m = m_base + c + j;
+            if (c + j < c1 && m < args.m) store_out(args, m, n, acc[j], bias_v, gate_v);
+          }
+        }
+      }
+    }
+    // No CTA leaves while a peer may still read its shared memory.
+    cluster_sync_all();
   }
 
   tc_fence_before();
@@ -310,16 +391,23 @@ int pick_bt(int m) {
   return 256;
 }
 
-// Split-K factor. Below ~3/4 of a wave of output tiles the K range is split so
-// that tiles x splits fills at most one wave of SMs, keeping >= 4 k-blocks
-// (256 of K) per split so that the per-CTA set-up and the F32 partial round
-// trip stay small next to the weight stream.
-int pick_splits(int tiles, int nkb, int num_sms) {
-  if (tiles * 4 >= num_sms * 3 || nkb < 8) return 1;
-  int s = num_sms / tiles;
-  if (s > nkb / 4) s = nkb / 4;
-  return s < 1 ? 1 : s;
+// Split-K factor in {1, 2, 4, 8} (cluster sizes). When the output tiles fill
+// less than ~3/4 of the resident CTA slots (two per SM for token tiles <= 64),
+// the K range is split as far as the slots allow, keeping >= 4 k-blocks
+// (256 of K) per split.
+int pick_splits(int tiles, int nkb, int num_sms, int bt) {
+  const int slots = num_sms * (bt <= 64 ? 2 : 1);
+  if (tiles * 4 >= slots * 3) return 1;
+  int best = 1;
+  for (int s = 2; s <= 8; s *= 2)
+    if (tiles * s <= slots && nkb / s >= 4) best = s;
+  return best;
 }
+
+bool g_pdl = [] {
+  const char* v = std::getenv("WAM_B200_DISABLE_PDL");
+  return !(v && *v && *v != '0');
+}();
 
 template <int BT>
 cudaError_t set_attr_bt() {
@@ -329,8 +417,26 @@ cudaError_t set_attr_bt() {
 
 template <int BT>
 cudaError_t launch_bt(const GemmOp& op, cudaStream_t stream) {
-  gemm_bf16_tc_kernel<BT><<<op.grid, kThreads, Cfg<BT>::SMEM, stream>>>(op.tm_w, op.tm_x, op.args);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(op.grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg<BT>::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+  ++na;
+  if (op.args.splits > 1 && op.args.split_mode == SPLIT_CLUSTER) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = op.args.splits;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<BT>, op.tm_w, op.tm_x, op.args);
 }
 
 int smem_for_bt(int bt) {
@@ -352,7 +458,7 @@ size_t gemm_scratch_floats(int m, int n, int k, int num_sms, int force_splits, i
   const int bt = pick_bt(m);
   const int tiles = ((m + bt - 1) / bt) * ((n + kBN - 1) / kBN);
   const int nkb = k / kBK;
-  const int splits = force_splits > 0 ? force_splits : pick_splits(tiles, nkb, num_sms);
+  const int splits = force_splits > 0 ? force_splits : pick_splits(tiles, nkb, num_sms, bt);
   if (tiles_out) *tiles_out = tiles;
   if (splits <= 1) return 0;
   return static_cast<size_t>(tiles) * splits * bt * kBN;
@@ -375,11 +481,16 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   const int tiles_m = (m + bt - 1) / bt;
   const int tiles_n = (n + kBN - 1) / kBN;
   const int nkb = k / kBK;
-  int splits = force_splits > 0 ? force_splits : pick_splits(tiles_m * tiles_n, nkb, num_sms);
+  int splits = force_splits > 0 ? force_splits : pick_splits(tiles_m * tiles_n, nkb, num_sms, bt);
   if (splits > nkb) splits = nkb;
-  if (splits > 1) {
+  // Split-K partials are reduced through distributed shared memory inside a
+  // thread-block cluster unless the caller hands in a global workspace.
+  const int mode = scratch.workspace ? SPLIT_WORKSPACE : SPLIT_CLUSTER;
+  if (splits > 1 && mode == SPLIT_CLUSTER && splits != 2 && splits != 4 && splits != 8)
+    return "gemm: cluster split-K needs 2, 4 or 8 splits (or a workspace)";
+  if (splits > 1 && mode == SPLIT_WORKSPACE) {
     const size_t need = static_cast<size_t>(tiles_m) * tiles_n * splits * bt * kBN;
-    if (!scratch.workspace || need > scratch.workspace_floats || !scratch.counters ||
+    if (need > scratch.workspace_floats || !scratch.counters ||
         tiles_m * tiles_n > scratch.counter_slots)
       return "gemm: split-K scratch too small";
   }
@@ -391,6 +502,7 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   a.k = k;
   a.num_kb = nkb;
   a.splits = splits;
+  a.split_mode = mode;
   a.tiles_m = tiles_m;
   a.tiles_n = tiles_n;
   a.epilogue = epilogue;

@@ -29,10 +29,17 @@ enum GemmEpilogue : int {
   EPI_BIAS_GELU_ERF = 8,  // y = bf16(gelu_erf(bf16(bf16(acc) + b)))  linear + ggml_gelu_erf (decoder)
 };
 
+// Split-K reduction: SPLIT_CLUSTER reduces the F32 partial tiles through
+// distributed shared memory inside one thread-block cluster (splits 2/4/8, no
+// global scratch); SPLIT_WORKSPACE writes them to a caller-provided global
+// workspace and the last CTA of a tile reduces them.
+enum SplitMode : int { SPLIT_CLUSTER = 0, SPLIT_WORKSPACE = 1 };
+
 struct GemmArgs {
   int m, n, k;
   int num_kb;  // k / 64
   int splits;
+  int split_mode;
   int tiles_m, tiles_n;
   int epilogue;
   const bf16* bias;      // [n] or null
@@ -41,8 +48,8 @@ struct GemmArgs {
   int ldr;
   void* out;  // bf16 [m, ldo] (float for EPI_F32_OUT)
   int ldo;
-  float* workspace;    // split-K partial tiles
-  unsigned* counters;  // split-K arrival counters, one per output tile, zero at rest
+  float* workspace;    // SPLIT_WORKSPACE: partial tiles [tile][split][BT][128]
+  unsigned* counters;  // SPLIT_WORKSPACE: arrival counters, one per tile, zero at rest
   unsigned* error;     // device error word
 };
 

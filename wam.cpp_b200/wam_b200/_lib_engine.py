@@ -38,7 +38,7 @@ class Stats(C.Structure):
 
 class OpProfile(C.Structure):
     _fields_ = [("phase", C.c_int), ("kind", C.c_int), ("launches", C.c_int), ("ms", C.c_float),
-                ("bytes", C.c_double), ("flops", C.c_double)]
+                ("bytes", C.c_double), ("flops", C.c_double), ("shape", C.c_int * 4)]
 
 
 def attach(lib, sig) -> None:

@@ -173,7 +173,8 @@ class Engine:
         if rc < 0:
             _raise(self.lib, -rc, st, "wam_b200_profile")
         return [{"phase": PHASES[a.phase], "kind": KINDS[a.kind], "launches": a.launches,
-                 "ms": a.ms, "bytes": a.bytes, "flops": a.flops} for a in arr[:rc]]
+                 "ms": a.ms, "bytes": a.bytes, "flops": a.flops, "shape": list(a.shape)}
+                for a in arr[:rc]]
 
     def reset(self):
         self.lib.wam_b200_reset(self.h)

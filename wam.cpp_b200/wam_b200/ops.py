@@ -11,7 +11,8 @@ import torch
 
 from ._lib import check, load
 
-EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_GATED_RES, EPI_RES, EPI_F32_BIAS, EPI_F32_OUT = range(7)
+(EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_GATED_RES, EPI_RES, EPI_F32_BIAS, EPI_F32_OUT,
+ EPI_BIAS_GELU_R, EPI_BIAS_GELU_ERF) = range(9)
 
 
 def _ptr(t):
@@ -34,21 +35,31 @@ class Scratch:
         return int(self.error.item())
 
 
+_error_words = {}
+
+
 def gemm(x, w, epilogue=EPI_BIAS, bias=None, gate=None, residual=None, out=None,
          scratch: Scratch | None = None, force_splits: int = 0):
-    """out[m, n] = epilogue(x[m, :K] . w[n, :]) via wam_b200_op_gemm."""
+    """out[m, n] = epilogue(x[m, :K] . w[n, :]) via wam_b200_op_gemm.
+
+    Without `scratch`, split-K partials are reduced inside thread-block
+    clusters (splits 1/2/4/8); with it, through its global workspace."""
     lib = load()
     m, k = x.shape[0], w.shape[1]
     n = w.shape[0]
     if out is None:
         dt = torch.float32 if epilogue == EPI_F32_OUT else torch.bfloat16
         out = torch.empty(m, n, dtype=dt, device=x.device)
-    scratch = scratch or Scratch()
+    if scratch is None:
+        err = _error_words.setdefault(x.device, torch.zeros(1, dtype=torch.int32, device=x.device))
+        ws = (C.c_void_p(0), 0, C.c_void_p(0), 0, _ptr(err))
+    else:
+        ws = (_ptr(scratch.ws), scratch.ws.numel(), _ptr(scratch.counters),
+              scratch.counters.numel(), _ptr(scratch.error))
     rc = lib.wam_b200_op_gemm(
         _ptr(x), x.stride(0), m, _ptr(w), n, k, epilogue, _ptr(bias), _ptr(gate), _ptr(residual),
         residual.stride(0) if residual is not None else 0, _ptr(out), out.stride(0),
-        _ptr(scratch.ws), scratch.ws.numel(), _ptr(scratch.counters), scratch.counters.numel(),
-        _ptr(scratch.error), force_splits, _stream())
+        *ws, force_splits, _stream())
     check(rc, "wam_b200_op_gemm")
     return out
 
