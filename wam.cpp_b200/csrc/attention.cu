@@ -43,7 +43,12 @@ __device__ __forceinline__ void load_tile(uint32_t smem, const bf16* g, int rows
   }
 }
 
-__global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
+// SPLIT: the key range is divided among the `splits` CTAs of a cluster (CTA
+// x = q_block * splits + split); each CTA stages its unnormalised output and
+// running max / sum in shared memory and the cluster merges rows through
+// distributed shared memory in fixed peer order.
+template <bool SPLIT>
+__global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a, int splits) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t s_q = smem_u32(smem);
   const uint32_t s_k[2] = {s_q + kTileBytes, s_q + 3 * kTileBytes};
@@ -52,7 +57,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int q0 = blockIdx.x * kBQ;
+  const int split = SPLIT ? static_cast<int>(blockIdx.x) % splits : 0;
+  const int q0 = (SPLIT ? static_cast<int>(blockIdx.x) / splits : static_cast<int>(blockIdx.x)) * kBQ;
   const int head = blockIdx.y;
   const int seq = blockIdx.z;
 
@@ -62,10 +68,15 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   const bf16* kg = a.k + seq * a.kv_seq_stride + head * a.kv_head_stride;
   const bf16* vg = a.v + seq * a.kv_seq_stride + head * a.kv_head_stride;
 
-  const int n_kb = (a.lk + kBKey - 1) / kBKey;
+  const int n_kb_all = (a.lk + kBKey - 1) / kBKey;
+  const int kb_begin = SPLIT ? (split * n_kb_all) / splits : 0;
+  const int kb_end = SPLIT ? ((split + 1) * n_kb_all) / splits : n_kb_all;
+  const int n_kb = kb_end - kb_begin;
   load_tile(s_q, qg, a.lq - q0, tid);
-  load_tile(s_k[0], kg, a.lk, tid);
-  load_tile(s_v[0], vg, a.lk, tid);
+  if (n_kb > 0) {
+    load_tile(s_k[0], kg + static_cast<long long>(kb_begin) * kBKey * kD, a.lk - kb_begin * kBKey, tid);
+    load_tile(s_v[0], vg + static_cast<long long>(kb_begin) * kBKey * kD, a.lk - kb_begin * kBKey, tid);
+  }
   cp_async_commit();
 
   // Q fragments for this warp's 16 rows, 8 k-steps of 16 dims.
@@ -77,9 +88,11 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   float l_run[2] = {0.0f, 0.0f};
   const float sl2 = a.scale * 1.4426950408889634f;
 
-  for (int kb = 0; kb < n_kb; ++kb) {
-    const int buf = kb & 1;
-    if (kb + 1 < n_kb) {
+  if (n_kb == 0) cp_async_wait<0>();
+  for (int it = 0; it < n_kb; ++it) {
+    const int kb = kb_begin + it;
+    const int buf = it & 1;
+    if (it + 1 < n_kb) {
       const int nb = buf ^ 1;
       load_tile(s_k[nb], kg + static_cast<long long>(kb + 1) * kBKey * kD, a.lk - (kb + 1) * kBKey, tid);
       load_tile(s_v[nb], vg + static_cast<long long>(kb + 1) * kBKey * kD, a.lk - (kb + 1) * kBKey, tid);
@@ -89,7 +102,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
       cp_async_wait<0>();
     }
     __syncthreads();
-    if (kb == 0) {
+    if (it == 0) {
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const int row = warp * 16 + (lane & 15);
@@ -186,24 +199,95 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
     __syncthreads();
   }
 
-  // Normalise and store BF16 rows.
-  const float inv[2] = {1.0f / l_run[0], 1.0f / l_run[1]};
+  if constexpr (SPLIT) {
+    // Stage unnormalised O [64][kOld] and (max, sum) per row, merge in the cluster.
+    constexpr int kOld = kD + 4;  // padded row stride (floats)
+    float* o_s = reinterpret_cast<float*>(smem);
+    float* m_s = o_s + kBQ * kOld;
+    float* l_s = m_s + kBQ;
+    __syncthreads();
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int row = q0 + warp * 16 + (lane >> 2) + r * 8;
-    if (row >= a.lq) continue;
-    bf16* dst;
-    if (a.split_first) {
-      dst = row == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
-                     : a.out + (static_cast<long long>(seq) * (a.lq - 1) + row - 1) * a.ldo;
-    } else {
-      dst = a.out + (static_cast<long long>(seq) * a.lq + row) * a.ldo;
+    for (int r = 0; r < 2; ++r) {
+      const int row = warp * 16 + (lane >> 2) + r * 8;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        *reinterpret_cast<float2*>(o_s + row * kOld + i * 8 + (lane & 3) * 2) =
+            make_float2(o[i][2 * r], o[i][2 * r + 1]);
+      if ((lane & 3) == 0) {
+        m_s[row] = m_run[r];
+        l_s[row] = l_run[r];
+      }
     }
-    dst += head * kD + (lane & 3) * 2;
+    cluster_sync_all();
+    const int rows_per = kBQ / splits;
+    const int d = tid;  // one output dim per thread
+    const uint32_t o_base = smem_u32(o_s), m_base = smem_u32(m_s), l_base = smem_u32(l_s);
+#pragma unroll 1
+    for (int rr = 0; rr < rows_per; rr += 4) {
+      float mv[4][8], lv[4][8], ov[4][8];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t v = pack_bf16(o[i][2 * r] * inv[r], o[i][2 * r + 1] * inv[r]);
-      *reinterpret_cast<uint32_t*>(dst + i * 8) = v;
+      for (int j = 0; j < 4; ++j) {
+        const int row = split * rows_per + rr + j;
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          mv[j][p] = -INFINITY;
+          lv[j][p] = 0.0f;
+          ov[j][p] = 0.0f;
+          if (p < splits && rr + j < rows_per) {
+            mv[j][p] = ld_shared_cluster_f32(mapa_shared(m_base + row * 4u, p));
+            lv[j][p] = ld_shared_cluster_f32(mapa_shared(l_base + row * 4u, p));
+            ov[j][p] = ld_shared_cluster_f32(mapa_shared(o_base + (row * kOld + d) * 4u, p));
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int row_l = split * rows_per + rr + j;
+        const int row = q0 + row_l;
+        if (rr + j >= rows_per || row >= a.lq) continue;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int p = 0; p < 8; ++p) mx = fmaxf(mx, mv[j][p]);
+        float num = 0.0f, den = 0.0f;
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          if (p < splits && mv[j][p] != -INFINITY) {
+            const float w = exp2f((mv[j][p] - mx) * sl2);
+            num += w * ov[j][p];
+            den += w * lv[j][p];
+          }
+        }
+        bf16* dst;
+        if (a.split_first) {
+          dst = row == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
+                         : a.out + (static_cast<long long>(seq) * (a.lq - 1) + row - 1) * a.ldo;
+        } else {
+          dst = a.out + (static_cast<long long>(seq) * a.lq + row) * a.ldo;
+        }
+        dst[head * kD + d] = __float2bfloat16_rn(num / den);
+      }
+    }
+    cluster_sync_all();
+  } else {
+    // Normalise and store BF16 rows.
+    const float inv[2] = {1.0f / l_run[0], 1.0f / l_run[1]};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = q0 + warp * 16 + (lane >> 2) + r * 8;
+      if (row >= a.lq) continue;
+      bf16* dst;
+      if (a.split_first) {
+        dst = row == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
+                       : a.out + (static_cast<long long>(seq) * (a.lq - 1) + row - 1) * a.ldo;
+      } else {
+        dst = a.out + (static_cast<long long>(seq) * a.lq + row) * a.ldo;
+      }
+      dst += head * kD + (lane & 3) * 2;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t v = pack_bf16(o[i][2 * r] * inv[r], o[i][2 * r + 1] * inv[r]);
+        *reinterpret_cast<uint32_t*>(dst + i * 8) = v;
+      }
     }
   }
 }
@@ -211,12 +295,53 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
 }  // namespace
 
 cudaError_t attention_init() {
-  return cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  cudaError_t e = cudaFuncSetAttribute(attention_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kSmem);
+}
+
+int attention_splits(const AttnArgs& a, int num_sms) {
+  const int qblocks = (a.lq + kBQ - 1) / kBQ;
+  const int ctas = qblocks * a.heads * a.batch;
+  const int kblocks = (a.lk + kBKey - 1) / kBKey;
+  const int slots = 2 * num_sms;  // 80 KB of shared memory per CTA
+  if (ctas * 2 > slots) return 1;
+  int best = 1;
+  for (int s = 2; s <= 8; s *= 2)
+    if (ctas * s <= slots && kblocks >= s) best = s;
+  return best;
 }
 
 void launch_attention(const AttnArgs& a, cudaStream_t s) {
-  dim3 grid((a.lq + kBQ - 1) / kBQ, a.heads, a.batch);
-  launch_pdl(attention_kernel, grid, dim3(128), kSmem, s, a);
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int splits = attention_splits(a, sms);
+  const int qblocks = (a.lq + kBQ - 1) / kBQ;
+  if (splits == 1) {
+    launch_pdl(attention_kernel<false>, dim3(qblocks, a.heads, a.batch), dim3(128), kSmem, s, a, 1);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(qblocks * splits, a.heads, a.batch);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = splits;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaLaunchKernelEx(&cfg, attention_kernel<true>, a, splits);
 }
 
 }  // namespace wamb

@@ -44,9 +44,11 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 constexpr int kRowsPerBlock = 8;
 
+// Rows of up to 32 * 8 * MAXC columns are held in registers (one pass over
+// memory with every load in flight); MAXC = 0 selects the generic loop.
 // mode 0: AdaLN  y = bf16(n * (1 + scale) + shift), scale/shift F32
 // mode 1: affine y = bf16(n * w + b), w/b BF16
-template <int MODE>
+template <int MODE, int MAXC>
 __global__ void __launch_bounds__(kRowsPerBlock * 32)
     ln_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
               const void* pb, float eps, bf16* __restrict__ y, int ldy) {
@@ -56,30 +58,9 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const bf16* xr = x + static_cast<long long>(row) * ldx;
-  const int chunks = cols >> 3;
-  float s = 0.0f;
-  for (int c = lane; c < chunks; c += 32) {
-    float f[8];
-    load8(xr + c * 8, f);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s += f[i];
-  }
-  const float mean = warp_sum(s) / cols;
-  float v = 0.0f;
-  for (int c = lane; c < chunks; c += 32) {
-    float f[8];
-    load8(xr + c * 8, f);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float d = f[i] - mean;
-      v += d * d;
-    }
-  }
-  const float inv_std = rsqrtf(warp_sum(v) / cols + eps);
   bf16* yr = y + static_cast<long long>(row) * ldy;
-  for (int c = lane; c < chunks; c += 32) {
-    float f[8];
-    load8(xr + c * 8, f);
+  const int chunks = cols >> 3;
+  auto finish = [&](int c, float (&f)[8], float mean, float inv_std) {
     if (MODE == 0) {
       const float4* sc = reinterpret_cast<const float4*>(static_cast<const float*>(pa) + c * 8);
       const float4* sh = reinterpret_cast<const float4*>(static_cast<const float*>(pb) + c * 8);
@@ -96,10 +77,68 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
       for (int i = 0; i < 8; ++i) f[i] = fmaf((f[i] - mean) * inv_std, w[i], b[i]);
     }
     store8(yr + c * 8, f);
+  };
+  if constexpr (MAXC > 0) {
+    float v[MAXC][8];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = lane + i * 32;
+      if (c < chunks) {
+        load8(xr + c * 8, v[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += v[i][j];
+      }
+    }
+    const float mean = warp_sum(s) / cols;
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i)
+      if (lane + i * 32 < chunks) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float d = v[i][j] - mean;
+          q += d * d;
+        }
+      }
+    const float inv_std = rsqrtf(warp_sum(q) / cols + eps);
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = lane + i * 32;
+      if (c < chunks) finish(c, v[i], mean, inv_std);
+    }
+  } else {
+    float s = 0.0f;
+    for (int c = lane; c < chunks; c += 32) {
+      float f[8];
+      load8(xr + c * 8, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += f[i];
+    }
+    const float mean = warp_sum(s) / cols;
+    float q = 0.0f;
+    for (int c = lane; c < chunks; c += 32) {
+      float f[8];
+      load8(xr + c * 8, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = f[i] - mean;
+        q += d * d;
+      }
+    }
+    const float inv_std = rsqrtf(warp_sum(q) / cols + eps);
+    for (int c = lane; c < chunks; c += 32) {
+      float f[8];
+      load8(xr + c * 8, f);
+      finish(c, f, mean, inv_std);
+    }
   }
 }
 
-// One block of 3 warps per token row: warp 0 = q, 1 = k, 2 = v.
+// One block of 3 warps per token row: warp 0 = q, 1 = k, 2 = v. Rows of up to
+// 32 * 8 * MAXC values stay in registers between the RMS reduction and the
+// RoPE/scatter pass (MAXC = 0: generic loop).
+template <int MAXC>
 __global__ void __launch_bounds__(96) qkv_scatter_kernel(const QkvScatter a) {
   griddep_wait();
   griddep_launch_dependents();
@@ -131,17 +170,6 @@ __global__ void __launch_bounds__(96) qkv_scatter_kernel(const QkvScatter a) {
     return;
   }
   const bf16* nw = which == 0 ? a.q_norm : a.k_norm;
-  float inv = 1.0f;
-  if (nw) {
-    float ss = 0.0f;
-    for (int c = lane; c < chunks; c += 32) {
-      float f[8];
-      load8(src + c * 8, f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
-    }
-    inv = rsqrtf(warp_sum(ss) / a.hidden + a.eps);
-  }
   int pt = 0, ph = 0, pw = 0;
   if (a.rope_mode == 2) {
     pt = a.pos_thw[rin * 3 + 0];
@@ -149,11 +177,9 @@ __global__ void __launch_bounds__(96) qkv_scatter_kernel(const QkvScatter a) {
     pw = a.pos_thw[rin * 3 + 2];
   }
   const int pos1 = a.pos_base + rin;
-  for (int c = lane; c < chunks; c += 32) {
+  auto emit = [&](int c, float (&f)[8], float inv) {
     const int d = c * 8;
     const int hd = d & 127;
-    float f[8];
-    load8(src + d, f);
     if (nw) {
       float w[8];
       load8(nw + d, w);
@@ -182,6 +208,42 @@ __global__ void __launch_bounds__(96) qkv_scatter_kernel(const QkvScatter a) {
       }
     }
     store8(dst_base + (d >> 7) * head_stride + hd, f);
+  };
+  if constexpr (MAXC > 0) {
+    float v[MAXC][8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = lane + i * 32;
+      if (c < chunks) {
+        load8(src + c * 8, v[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+      }
+    }
+    const float inv = nw ? rsqrtf(warp_sum(ss) / a.hidden + a.eps) : 1.0f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = lane + i * 32;
+      if (c < chunks) emit(c, v[i], inv);
+    }
+  } else {
+    float inv = 1.0f;
+    if (nw) {
+      float ss = 0.0f;
+      for (int c = lane; c < chunks; c += 32) {
+        float f[8];
+        load8(src + c * 8, f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+      }
+      inv = rsqrtf(warp_sum(ss) / a.hidden + a.eps);
+    }
+    for (int c = lane; c < chunks; c += 32) {
+      float f[8];
+      load8(src + c * 8, f);
+      emit(c, f, inv);
+    }
   }
 }
 
@@ -316,22 +378,45 @@ inline int grid_for(long long n, int threads) {
 
 }  // namespace
 
+template <int MODE>
+void launch_ln(const bf16* x, int ldx, int rows, int cols, const void* pa, const void* pb,
+               float eps, bf16* y, int ldy, cudaStream_t s) {
+  const dim3 grid((rows + kRowsPerBlock - 1) / kRowsPerBlock), block(kRowsPerBlock * 32);
+  const int per_lane = (cols / 8 + 31) / 32;
+  if (per_lane <= 4)
+    launch_pdl(ln_kernel<MODE, 4>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+  else if (per_lane <= 8)
+    launch_pdl(ln_kernel<MODE, 8>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+  else if (per_lane <= 12)
+    launch_pdl(ln_kernel<MODE, 12>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+  else if (per_lane <= 16)
+    launch_pdl(ln_kernel<MODE, 16>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+  else
+    launch_pdl(ln_kernel<MODE, 0>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+}
+
 void launch_ln_modulate(const bf16* x, int ldx, int rows, int cols, const float* scale,
                         const float* shift, float eps, bf16* y, int ldy, cudaStream_t s) {
-  const int grid = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
-  launch_pdl(ln_kernel<0>, dim3(grid), dim3(kRowsPerBlock * 32), 0, s, x, ldx, rows, cols,
-             static_cast<const void*>(scale), static_cast<const void*>(shift), eps, y, ldy);
+  launch_ln<0>(x, ldx, rows, cols, scale, shift, eps, y, ldy, s);
 }
 
 void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w, const bf16* b,
                       float eps, bf16* y, int ldy, cudaStream_t s) {
-  const int grid = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
-  launch_pdl(ln_kernel<1>, dim3(grid), dim3(kRowsPerBlock * 32), 0, s, x, ldx, rows, cols,
-             static_cast<const void*>(w), static_cast<const void*>(b), eps, y, ldy);
+  launch_ln<1>(x, ldx, rows, cols, w, b, eps, y, ldy, s);
 }
 
 void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s) {
-  launch_pdl(qkv_scatter_kernel, dim3(a.rows), dim3(96), 0, s, a);
+  const int per_lane = (a.hidden / 8 + 31) / 32;
+  if (per_lane <= 4)
+    launch_pdl(qkv_scatter_kernel<4>, dim3(a.rows), dim3(96), 0, s, a);
+  else if (per_lane <= 8)
+    launch_pdl(qkv_scatter_kernel<8>, dim3(a.rows), dim3(96), 0, s, a);
+  else if (per_lane <= 12)
+    launch_pdl(qkv_scatter_kernel<12>, dim3(a.rows), dim3(96), 0, s, a);
+  else if (per_lane <= 16)
+    launch_pdl(qkv_scatter_kernel<16>, dim3(a.rows), dim3(96), 0, s, a);
+  else
+    launch_pdl(qkv_scatter_kernel<0>, dim3(a.rows), dim3(96), 0, s, a);
 }
 
 void launch_small_linear(const bf16* x, int ldx, int m, int k, const bf16* w, long long w_sn,
