@@ -73,6 +73,24 @@ WAM_B200_API int wam_b200_op_gemm(const void* x, int ldx, int m, const void* w, 
                                   int counter_slots, unsigned* error, int force_splits,
                                   void* stream);
 
+/* The same GEMM for callers that must not allocate device memory (no
+ * counterpart in the reference). A robot control loop that calls the policy
+ * every cycle cannot afford cudaMalloc/cudaFree (they may synchronize the device
+ * and take unbounded time), and hosting frameworks that own the allocator may
+ * forbid side allocations; wam_b200_op_gemm needs a caller-allocated workspace
+ * for split-K, this entry point uses a fixed library-owned device array instead
+ * (8 MiB of partials + 4096 tile counters, held on every GPU that loads the
+ * library until exit) and calls no allocating routine. Shapes whose split-K
+ * partials exceed it are rejected with WAM_B200_INVALID_ARGUMENT. The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture. All calls share the array: calls
+ * that overlap on the GPU race and must be serialized by the caller. Arguments
+ * as wam_b200_op_gemm, without the workspace. */
+WAM_B200_API int wam_b200_op_gemm_noalloc(const void* x, int ldx, int m, const void* w, int n,
+                                          int k, int epilogue, const void* bias, const float* gate,
+                                          const void* residual, int ldr, void* out, int ldo,
+                                          int force_splits, void* stream);
+
 /* Split-K scratch (floats) and output-tile count wam_b200_op_gemm needs for a shape. */
 WAM_B200_API size_t wam_b200_gemm_scratch_floats(int m, int n, int k, int force_splits,
                                                  int* tiles_out);
