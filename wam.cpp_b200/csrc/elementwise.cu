@@ -42,166 +42,196 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-constexpr int kRowsPerBlock = 8;
 
-// Rows of up to 32 * 8 * MAXC columns are held in registers (one pass over
-// memory with every load in flight); MAXC = 0 selects the generic loop.
+constexpr int kRowThreads = 128;  // threads cooperating on one row
+
+// Sum over the 128 threads of a block (4 warps) via shared memory.
+__device__ __forceinline__ float block128_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  return red[0] + red[1] + red[2] + red[3];
+}
+
+// One 128-thread block per row; each thread holds up to MAXC 8-wide chunks of
+// the row and of its parameters in registers, loaded in one batch so the row
+// costs a single memory round trip.
 // mode 0: AdaLN  y = bf16(n * (1 + scale) + shift), scale/shift F32
 // mode 1: affine y = bf16(n * w + b), w/b BF16
 template <int MODE, int MAXC>
-__global__ void __launch_bounds__(kRowsPerBlock * 32)
+__global__ void __launch_bounds__(kRowThreads)
     ln_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
               const void* pb, float eps, bf16* __restrict__ y, int ldy) {
   griddep_wait();
   griddep_launch_dependents();
-  const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+  __shared__ float red[4];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const bf16* xr = x + static_cast<long long>(row) * ldx;
+  bf16* yr = y + static_cast<long long>(row) * ldy;
+  const int chunks = cols >> 3;
+  float v[MAXC][8], p0[MAXC][8], p1[MAXC][8];
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * kRowThreads;
+    if (c < chunks) {
+      load8(xr + c * 8, v[i]);
+      if (MODE == 0) {
+        const float4* sc = reinterpret_cast<const float4*>(static_cast<const float*>(pa) + c * 8);
+        const float4* sh = reinterpret_cast<const float4*>(static_cast<const float*>(pb) + c * 8);
+        const float4 s0 = sc[0], s1 = sc[1], h0 = sh[0], h1 = sh[1];
+        p0[i][0] = s0.x; p0[i][1] = s0.y; p0[i][2] = s0.z; p0[i][3] = s0.w;
+        p0[i][4] = s1.x; p0[i][5] = s1.y; p0[i][6] = s1.z; p0[i][7] = s1.w;
+        p1[i][0] = h0.x; p1[i][1] = h0.y; p1[i][2] = h0.z; p1[i][3] = h0.w;
+        p1[i][4] = h1.x; p1[i][5] = h1.y; p1[i][6] = h1.z; p1[i][7] = h1.w;
+      } else {
+        load8(static_cast<const bf16*>(pa) + c * 8, p0[i]);
+        load8(static_cast<const bf16*>(pb) + c * 8, p1[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[i][j];
+    }
+  }
+  const float mean = block128_sum(s, red) / cols;
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i)
+    if (tid + i * kRowThreads < chunks) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[i][j] - mean;
+        q += d * d;
+      }
+    }
+  const float inv_std = rsqrtf(block128_sum(q, red) / cols + eps);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * kRowThreads;
+    if (c < chunks) {
+      float f[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        f[j] = MODE == 0 ? fmaf((v[i][j] - mean) * inv_std, 1.0f + p0[i][j], p1[i][j])
+                         : fmaf((v[i][j] - mean) * inv_std, p0[i][j], p1[i][j]);
+      store8(yr + c * 8, f);
+    }
+  }
+}
+
+// Generic fallback for rows wider than 128 * 8 * 4 columns: one warp per row,
+// three passes over the row.
+template <int MODE>
+__global__ void __launch_bounds__(256)
+    ln_wide_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
+                   const void* pb, float eps, bf16* __restrict__ y, int ldy) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const bf16* xr = x + static_cast<long long>(row) * ldx;
   bf16* yr = y + static_cast<long long>(row) * ldy;
   const int chunks = cols >> 3;
-  auto finish = [&](int c, float (&f)[8], float mean, float inv_std) {
+  float s = 0.0f;
+  for (int c = lane; c < chunks; c += 32) {
+    float f[8];
+    load8(xr + c * 8, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += f[i];
+  }
+  const float mean = warp_sum(s) / cols;
+  float q = 0.0f;
+  for (int c = lane; c < chunks; c += 32) {
+    float f[8];
+    load8(xr + c * 8, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float d = f[i] - mean;
+      q += d * d;
+    }
+  }
+  const float inv_std = rsqrtf(warp_sum(q) / cols + eps);
+  for (int c = lane; c < chunks; c += 32) {
+    float f[8], p0[8], p1[8];
+    load8(xr + c * 8, f);
     if (MODE == 0) {
-      const float4* sc = reinterpret_cast<const float4*>(static_cast<const float*>(pa) + c * 8);
-      const float4* sh = reinterpret_cast<const float4*>(static_cast<const float*>(pb) + c * 8);
-      const float4 s0 = sc[0], s1 = sc[1], h0 = sh[0], h1 = sh[1];
-      const float scl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-      const float shf[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) f[i] = fmaf((f[i] - mean) * inv_std, 1.0f + scl[i], shf[i]);
-    } else {
-      float w[8], b[8];
-      load8(static_cast<const bf16*>(pa) + c * 8, w);
-      load8(static_cast<const bf16*>(pb) + c * 8, b);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) f[i] = fmaf((f[i] - mean) * inv_std, w[i], b[i]);
-    }
-    store8(yr + c * 8, f);
-  };
-  if constexpr (MAXC > 0) {
-    float v[MAXC][8];
-    float s = 0.0f;
-#pragma unroll
-    for (int i = 0; i < MAXC; ++i) {
-      const int c = lane + i * 32;
-      if (c < chunks) {
-        load8(xr + c * 8, v[i]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s += v[i][j];
-      }
-    }
-    const float mean = warp_sum(s) / cols;
-    float q = 0.0f;
-#pragma unroll
-    for (int i = 0; i < MAXC; ++i)
-      if (lane + i * 32 < chunks) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float d = v[i][j] - mean;
-          q += d * d;
-        }
-      }
-    const float inv_std = rsqrtf(warp_sum(q) / cols + eps);
-#pragma unroll
-    for (int i = 0; i < MAXC; ++i) {
-      const int c = lane + i * 32;
-      if (c < chunks) finish(c, v[i], mean, inv_std);
-    }
-  } else {
-    float s = 0.0f;
-    for (int c = lane; c < chunks; c += 32) {
-      float f[8];
-      load8(xr + c * 8, f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) s += f[i];
-    }
-    const float mean = warp_sum(s) / cols;
-    float q = 0.0f;
-    for (int c = lane; c < chunks; c += 32) {
-      float f[8];
-      load8(xr + c * 8, f);
-#pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float d = f[i] - mean;
-        q += d * d;
+        p0[i] = static_cast<const float*>(pa)[c * 8 + i];
+        p1[i] = static_cast<const float*>(pb)[c * 8 + i];
       }
+    } else {
+      load8(static_cast<const bf16*>(pa) + c * 8, p0);
+      load8(static_cast<const bf16*>(pb) + c * 8, p1);
     }
-    const float inv_std = rsqrtf(warp_sum(q) / cols + eps);
-    for (int c = lane; c < chunks; c += 32) {
-      float f[8];
-      load8(xr + c * 8, f);
-      finish(c, f, mean, inv_std);
-    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      f[i] = MODE == 0 ? fmaf((f[i] - mean) * inv_std, 1.0f + p0[i], p1[i])
+                       : fmaf((f[i] - mean) * inv_std, p0[i], p1[i]);
+    store8(yr + c * 8, f);
   }
 }
 
-// One block of 3 warps per token row: warp 0 = q, 1 = k, 2 = v. Rows of up to
-// 32 * 8 * MAXC values stay in registers between the RMS reduction and the
-// RoPE/scatter pass (MAXC = 0: generic loop).
+// RoPE inverse frequency and position of the pair starting at head dim `dim`.
+__device__ __forceinline__ float rope_theta(const QkvScatter& a, int dim, int pos1, int pt, int ph,
+                                            int pw) {
+  if (a.rope_mode == 1) return static_cast<float>(pos1) * __ldg(a.inv_freq + (dim >> 1));
+  if (dim < 44) return static_cast<float>(pt) * __ldg(a.inv_freq + (dim >> 1));
+  if (dim < 86) return static_cast<float>(ph) * __ldg(a.inv_freq + 22 + ((dim - 44) >> 1));
+  return static_cast<float>(pw) * __ldg(a.inv_freq + 43 + ((dim - 86) >> 1));
+}
+
+// One block per token row, threadIdx.y = part (0 q, 1 k, 2 v), 128 threads per
+// part; each thread holds up to MAXC 8-wide chunks of its part (and the norm
+// weights) in registers. MAXC = 0: generic loop.
 template <int MAXC>
-__global__ void __launch_bounds__(96) qkv_scatter_kernel(const QkvScatter a) {
+__global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const QkvScatter a) {
   griddep_wait();
   griddep_launch_dependents();
+  __shared__ float red[3][4];
   const int row = blockIdx.x;
-  const int which = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
+  const int which = threadIdx.y;
+  const int tid = threadIdx.x;
   const int col = which == 0 ? a.q_col : (which == 1 ? a.k_col : a.v_col);
-  if (col < 0) return;
-  const bf16* src = a.src + static_cast<long long>(row) * a.ld_src + col;
+  const bf16* src = a.src + static_cast<long long>(row) * a.ld_src + (col < 0 ? 0 : col);
   const int seq = row / a.rows_per_seq;
   const int rin = row - seq * a.rows_per_seq;
   const int chunks = a.hidden >> 3;
-  bf16* dst_base;
-  long long head_stride;
-  if (which == 0) {
-    dst_base = a.q_out + seq * a.q_seq_stride + static_cast<long long>(a.q_row_offset + rin) * 128;
-    head_stride = a.q_head_stride;
-  } else {
-    dst_base = (which == 1 ? a.k_out : a.v_out) + seq * a.kv_seq_stride +
-               static_cast<long long>(a.kv_row_offset + rin) * 128;
-    head_stride = a.kv_head_stride;
-  }
-  if (which == 2) {
-    for (int c = lane; c < chunks; c += 32) {
-      const int d = c * 8;
-      *reinterpret_cast<Bf16x8*>(dst_base + (d >> 7) * head_stride + (d & 127)) =
-          *reinterpret_cast<const Bf16x8*>(src + d);
+  bf16* dst_base = nullptr;
+  long long head_stride = 0;
+  if (col >= 0) {
+    if (which == 0) {
+      dst_base = a.q_out + seq * a.q_seq_stride + static_cast<long long>(a.q_row_offset + rin) * 128;
+      head_stride = a.q_head_stride;
+    } else {
+      dst_base = (which == 1 ? a.k_out : a.v_out) + seq * a.kv_seq_stride +
+                 static_cast<long long>(a.kv_row_offset + rin) * 128;
+      head_stride = a.kv_head_stride;
     }
-    return;
   }
-  const bf16* nw = which == 0 ? a.q_norm : a.k_norm;
+  const bf16* nw = which == 0 ? a.q_norm : (which == 1 ? a.k_norm : nullptr);
   int pt = 0, ph = 0, pw = 0;
-  if (a.rope_mode == 2) {
+  if (a.rope_mode == 2 && which < 2 && col >= 0) {
     pt = a.pos_thw[rin * 3 + 0];
     ph = a.pos_thw[rin * 3 + 1];
     pw = a.pos_thw[rin * 3 + 2];
   }
   const int pos1 = a.pos_base + rin;
-  auto emit = [&](int c, float (&f)[8], float inv) {
+  const bool rope = a.rope_mode != 0 && which < 2;
+  auto emit = [&](int c, float (&f)[8], const float (&w)[8], float inv) {
     const int d = c * 8;
     const int hd = d & 127;
     if (nw) {
-      float w[8];
-      load8(nw + d, w);
 #pragma unroll
       for (int i = 0; i < 8; ++i) f[i] = f[i] * inv * w[i];
     }
-    if (a.rope_mode != 0) {
+    if (rope) {
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
-        const int dim = hd + 2 * p;
-        float theta;
-        if (a.rope_mode == 1) {
-          theta = static_cast<float>(pos1) * a.inv_freq[dim >> 1];
-        } else if (dim < 44) {
-          theta = static_cast<float>(pt) * a.inv_freq[dim >> 1];
-        } else if (dim < 86) {
-          theta = static_cast<float>(ph) * a.inv_freq[22 + ((dim - 44) >> 1)];
-        } else {
-          theta = static_cast<float>(pw) * a.inv_freq[43 + ((dim - 86) >> 1)];
-        }
         float sn, cs;
-        sincosf(theta, &sn, &cs);
+        sincosf(rope_theta(a, hd + 2 * p, pos1, pt, ph, pw), &sn, &cs);
         const float x0 = f[2 * p], x1 = f[2 * p + 1];
         f[2 * p] = x0 * cs - x1 * sn;
         f[2 * p + 1] = x0 * sn + x1 * cs;
@@ -210,39 +240,53 @@ __global__ void __launch_bounds__(96) qkv_scatter_kernel(const QkvScatter a) {
     store8(dst_base + (d >> 7) * head_stride + hd, f);
   };
   if constexpr (MAXC > 0) {
-    float v[MAXC][8];
+    float v[MAXC][8], w[MAXC][8];
     float ss = 0.0f;
+    if (col >= 0) {
 #pragma unroll
-    for (int i = 0; i < MAXC; ++i) {
-      const int c = lane + i * 32;
-      if (c < chunks) {
-        load8(src + c * 8, v[i]);
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kRowThreads;
+        if (c < chunks) {
+          load8(src + c * 8, v[i]);
+          if (nw) load8(nw + c * 8, w[i]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+          for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+        }
       }
     }
-    const float inv = nw ? rsqrtf(warp_sum(ss) / a.hidden + a.eps) : 1.0f;
+    // block-wide sum for this part (all parts take part in the barriers)
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[which][tid >> 5] = ss;
+    __syncthreads();
+    const float tot = red[which][0] + red[which][1] + red[which][2] + red[which][3];
+    if (col < 0) return;
+    const float inv = nw ? rsqrtf(tot / a.hidden + a.eps) : 1.0f;
 #pragma unroll
     for (int i = 0; i < MAXC; ++i) {
-      const int c = lane + i * 32;
-      if (c < chunks) emit(c, v[i], inv);
+      const int c = tid + i * kRowThreads;
+      if (c < chunks) emit(c, v[i], w[i], inv);
     }
   } else {
-    float inv = 1.0f;
-    if (nw) {
-      float ss = 0.0f;
-      for (int c = lane; c < chunks; c += 32) {
+    float ss = 0.0f;
+    if (col >= 0 && nw) {
+      for (int c = tid; c < chunks; c += kRowThreads) {
         float f[8];
         load8(src + c * 8, f);
 #pragma unroll
         for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
       }
-      inv = rsqrtf(warp_sum(ss) / a.hidden + a.eps);
     }
-    for (int c = lane; c < chunks; c += 32) {
-      float f[8];
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[which][tid >> 5] = ss;
+    __syncthreads();
+    const float tot = red[which][0] + red[which][1] + red[which][2] + red[which][3];
+    if (col < 0) return;
+    const float inv = nw ? rsqrtf(tot / a.hidden + a.eps) : 1.0f;
+    for (int c = tid; c < chunks; c += kRowThreads) {
+      float f[8], w[8];
       load8(src + c * 8, f);
-      emit(c, f, inv);
+      if (nw) load8(nw + c * 8, w);
+      emit(c, f, w, inv);
     }
   }
 }
@@ -381,18 +425,19 @@ inline int grid_for(long long n, int threads) {
 template <int MODE>
 void launch_ln(const bf16* x, int ldx, int rows, int cols, const void* pa, const void* pb,
                float eps, bf16* y, int ldy, cudaStream_t s) {
-  const dim3 grid((rows + kRowsPerBlock - 1) / kRowsPerBlock), block(kRowsPerBlock * 32);
-  const int per_lane = (cols / 8 + 31) / 32;
-  if (per_lane <= 4)
+  const int per = (cols / 8 + kRowThreads - 1) / kRowThreads;
+  const dim3 grid(rows), block(kRowThreads);
+  if (per <= 1)
+    launch_pdl(ln_kernel<MODE, 1>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+  else if (per <= 2)
+    launch_pdl(ln_kernel<MODE, 2>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+  else if (per <= 3)
+    launch_pdl(ln_kernel<MODE, 3>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+  else if (per <= 4)
     launch_pdl(ln_kernel<MODE, 4>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
-  else if (per_lane <= 8)
-    launch_pdl(ln_kernel<MODE, 8>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
-  else if (per_lane <= 12)
-    launch_pdl(ln_kernel<MODE, 12>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
-  else if (per_lane <= 16)
-    launch_pdl(ln_kernel<MODE, 16>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
   else
-    launch_pdl(ln_kernel<MODE, 0>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+    launch_pdl(ln_wide_kernel<MODE>, dim3((rows + 7) / 8), dim3(256), 0, s, x, ldx, rows, cols,
+               pa, pb, eps, y, ldy);
 }
 
 void launch_ln_modulate(const bf16* x, int ldx, int rows, int cols, const float* scale,
@@ -406,17 +451,18 @@ void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w,
 }
 
 void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s) {
-  const int per_lane = (a.hidden / 8 + 31) / 32;
-  if (per_lane <= 4)
-    launch_pdl(qkv_scatter_kernel<4>, dim3(a.rows), dim3(96), 0, s, a);
-  else if (per_lane <= 8)
-    launch_pdl(qkv_scatter_kernel<8>, dim3(a.rows), dim3(96), 0, s, a);
-  else if (per_lane <= 12)
-    launch_pdl(qkv_scatter_kernel<12>, dim3(a.rows), dim3(96), 0, s, a);
-  else if (per_lane <= 16)
-    launch_pdl(qkv_scatter_kernel<16>, dim3(a.rows), dim3(96), 0, s, a);
+  const int per = (a.hidden / 8 + kRowThreads - 1) / kRowThreads;
+  const dim3 grid(a.rows), block(kRowThreads, 3);
+  if (per <= 1)
+    launch_pdl(qkv_scatter_kernel<1>, grid, block, 0, s, a);
+  else if (per <= 2)
+    launch_pdl(qkv_scatter_kernel<2>, grid, block, 0, s, a);
+  else if (per <= 3)
+    launch_pdl(qkv_scatter_kernel<3>, grid, block, 0, s, a);
+  else if (per <= 4)
+    launch_pdl(qkv_scatter_kernel<4>, grid, block, 0, s, a);
   else
-    launch_pdl(qkv_scatter_kernel<0>, dim3(a.rows), dim3(96), 0, s, a);
+    launch_pdl(qkv_scatter_kernel<0>, grid, block, 0, s, a);
 }
 
 void launch_small_linear(const bf16* x, int ldx, int m, int k, const bf16* w, long long w_sn,

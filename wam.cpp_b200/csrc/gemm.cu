@@ -164,6 +164,9 @@ __global__ void __launch_bounds__(kThreads, Cfg<BT>::MIN_BLOCKS)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Let the next kernel in the stream start its own set-up now; it waits for
+  // this grid's completion before touching anything this grid writes.
+  griddep_launch_dependents();
 
   bool ok = true;
   const int q = warp & 3;
@@ -230,7 +233,6 @@ __global__ void __launch_bounds__(kThreads, Cfg<BT>::MIN_BLOCKS)
     ok = mbar_wait(accum, 0);
     if (!ok) atomicCAS(args.error, 0u, static_cast<unsigned>(kErrEpilogueTimeout));
     tc_fence_after();
-    griddep_launch_dependents();
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     if (args.splits == 1) {
 #pragma unroll 1
@@ -382,13 +384,29 @@ bool encode_bf16_2d(CUtensorMap* map, const void* base, int cols, int rows, int 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int pick_bt(int m) {
-  static const int opts[] = {16, 32, 48, 64, 96, 128, 192, 256};
-  const int tiles = (m + 255) / 256;
-  const int per = (m + tiles - 1) / tiles;
-  for (int o : opts)
-    if (o >= per) return o;
-  return 256;
+// Token tile: the largest tile for up to 256 tokens; beyond that the tile that
+// minimises (waves x resident CTAs per SM x tile width), i.e. the per-SM
+// tensor work of the slowest SM, preferring larger tiles on ties.
+int pick_bt(int m, int n, int num_sms) {
+  static const int small[] = {16, 32, 48, 64, 96, 128, 192, 256};
+  if (m <= 256) {
+    for (int o : small)
+      if (o >= m) return o;
+  }
+  static const int big[] = {256, 192, 128, 96};
+  const int tiles_n = (n + 127) / 128;
+  int best = 256;
+  long long best_cost = -1;
+  for (int bt : big) {
+    const long long tiles = static_cast<long long>((m + bt - 1) / bt) * tiles_n;
+    const long long waves = (tiles + num_sms - 1) / num_sms;
+    const long long cost = waves * bt;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bt;
+    }
+  }
+  return best;
 }
 
 // Split-K factor in {1, 2, 4, 8} (cluster sizes). When the output tiles fill
@@ -396,7 +414,9 @@ int pick_bt(int m) {
 // the K range is split as far as the slots allow, keeping >= 4 k-blocks
 // (256 of K) per split.
 int pick_splits(int tiles, int nkb, int num_sms, int bt) {
-  const int slots = num_sms * (bt <= 64 ? 2 : 1);
+  // Large token tiles are tensor bound: splitting K only adds partial traffic.
+  if (bt > 64) return 1;
+  const int slots = num_sms * 2;
   if (tiles * 4 >= slots * 3) return 1;
   int best = 1;
   for (int s = 2; s <= 8; s *= 2)
@@ -455,7 +475,7 @@ int smem_for_bt(int bt) {
 }  // namespace
 
 size_t gemm_scratch_floats(int m, int n, int k, int num_sms, int force_splits, int* tiles_out) {
-  const int bt = pick_bt(m);
+  const int bt = pick_bt(m, n, num_sms);
   const int tiles = ((m + bt - 1) / bt) * ((n + kBN - 1) / kBN);
   const int nkb = k / kBK;
   const int splits = force_splits > 0 ? force_splits : pick_splits(tiles, nkb, num_sms, bt);
@@ -477,7 +497,7 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
     return "gemm: residual epilogue needs its inputs";
   if (epilogue < 0 || epilogue > EPI_BIAS_GELU_ERF) return "gemm: unknown epilogue";
   std::memset(op, 0, sizeof(*op));
-  const int bt = pick_bt(m);
+  const int bt = pick_bt(m, n, num_sms);
   const int tiles_m = (m + bt - 1) / bt;
   const int tiles_n = (n + kBN - 1) / kBN;
   const int nkb = k / kBK;
