@@ -13,6 +13,7 @@
 // (mot.cpp:299-321).
 #include "kernels.h"
 #include "launch.cuh"
+#include "prefetch.cuh"
 #include "ptx.cuh"
 
 namespace wamb {
@@ -62,6 +63,9 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a, int sp
   const int head = blockIdx.y;
   const int seq = blockIdx.z;
 
+  if (tid == 0)
+    l2_prefetch_share(a.pf, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z),
+                      gridDim.x * gridDim.y * gridDim.z);
   griddep_wait();
   griddep_launch_dependents();
   const bf16* qg = a.q + seq * a.q_seq_stride + head * a.q_head_stride + static_cast<long long>(q0) * kD;
@@ -219,52 +223,65 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a, int sp
       }
     }
     cluster_sync_all();
+    // Each CTA merges kBQ / splits rows; a row's 128 dims are spread over
+    // 128 / rows_per threads, each owning rows_per consecutive dims.
     const int rows_per = kBQ / splits;
-    const int d = tid;  // one output dim per thread
+    const int tpr = 128 / rows_per;
+    const int row_l = split * rows_per + tid / tpr;
+    const int dseg = (tid % tpr) * rows_per;
+    const int row = q0 + row_l;
     const uint32_t o_base = smem_u32(o_s), m_base = smem_u32(m_s), l_base = smem_u32(l_s);
-#pragma unroll 1
-    for (int rr = 0; rr < rows_per; rr += 4) {
-      float mv[4][8], lv[4][8], ov[4][8];
+    float mv[8], lv[8], wv[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int row = split * rows_per + rr + j;
-#pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          mv[j][p] = -INFINITY;
-          lv[j][p] = 0.0f;
-          ov[j][p] = 0.0f;
-          if (p < splits && rr + j < rows_per) {
-            mv[j][p] = ld_shared_cluster_f32(mapa_shared(m_base + row * 4u, p));
-            lv[j][p] = ld_shared_cluster_f32(mapa_shared(l_base + row * 4u, p));
-            ov[j][p] = ld_shared_cluster_f32(mapa_shared(o_base + (row * kOld + d) * 4u, p));
-          }
-        }
+    for (int p = 0; p < 8; ++p) {
+      mv[p] = -INFINITY;
+      lv[p] = 0.0f;
+      if (p < splits) {
+        mv[p] = ld_shared_cluster_f32(mapa_shared(m_base + row_l * 4u, p));
+        lv[p] = ld_shared_cluster_f32(mapa_shared(l_base + row_l * 4u, p));
       }
+    }
+    float mx = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int row_l = split * rows_per + rr + j;
-        const int row = q0 + row_l;
-        if (rr + j >= rows_per || row >= a.lq) continue;
-        float mx = -INFINITY;
+    for (int p = 0; p < 8; ++p) mx = fmaxf(mx, mv[p]);
+    float den = 0.0f;
 #pragma unroll
-        for (int p = 0; p < 8; ++p) mx = fmaxf(mx, mv[j][p]);
-        float num = 0.0f, den = 0.0f;
+    for (int p = 0; p < 8; ++p) {
+      wv[p] = mv[p] != -INFINITY ? exp2f((mv[p] - mx) * sl2) : 0.0f;
+      den += wv[p] * lv[p];
+    }
+    const float inv_den = 1.0f / den;
+    bf16* dst = nullptr;
+    if (row < a.lq) {
+      if (a.split_first) {
+        dst = row == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
+                       : a.out + (static_cast<long long>(seq) * (a.lq - 1) + row - 1) * a.ldo;
+      } else {
+        dst = a.out + (static_cast<long long>(seq) * a.lq + row) * a.ldo;
+      }
+      dst += head * kD + dseg;
+    }
+#pragma unroll 1
+    for (int c = 0; c < rows_per; c += 4) {
+      float4 v[8];
+      const uint32_t off = (row_l * kOld + dseg + c) * 4u;
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          if (p < splits && mv[j][p] != -INFINITY) {
-            const float w = exp2f((mv[j][p] - mx) * sl2);
-            num += w * ov[j][p];
-            den += w * lv[j][p];
-          }
+      for (int p = 0; p < 8; ++p)
+        if (p < splits) v[p] = ld_shared_cluster_f32x4(mapa_shared(o_base + off, p));
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int p = 0; p < 8; ++p)
+        if (p < splits) {
+          acc.x = fmaf(wv[p], v[p].x, acc.x);
+          acc.y = fmaf(wv[p], v[p].y, acc.y);
+          acc.z = fmaf(wv[p], v[p].z, acc.z);
+          acc.w = fmaf(wv[p], v[p].w, acc.w);
         }
-        bf16* dst;
-        if (a.split_first) {
-          dst = row == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
-                         : a.out + (static_cast<long long>(seq) * (a.lq - 1) + row - 1) * a.ldo;
-        } else {
-          dst = a.out + (static_cast<long long>(seq) * a.lq + row) * a.ldo;
-        }
-        dst[head * kD + d] = __float2bfloat16_rn(num / den);
+      if (dst) {
+        uint2 pk;
+        pk.x = pack_bf16(acc.x * inv_den, acc.y * inv_den);
+        pk.y = pack_bf16(acc.z * inv_den, acc.w * inv_den);
+        *reinterpret_cast<uint2*>(dst + c) = pk;
       }
     }
     cluster_sync_all();

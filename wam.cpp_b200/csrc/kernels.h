@@ -12,6 +12,14 @@ namespace wamb {
 
 using bf16 = __nv_bfloat16;
 
+// Weight ranges the next kernels will stream. A non-GEMM kernel that runs just
+// before them spreads their L2 prefetch over its CTAs, while HBM is otherwise
+// idle; null pointers / zero sizes disable it.
+struct L2Prefetch {
+  const void* ptr[2] = {nullptr, nullptr};
+  long long bytes[2] = {0, 0};
+};
+
 // ------------------------------------------------------------------ GEMM
 // y[m, n] = epilogue( sum_k x[m, k] * w[n, k] ), x: [M, K] (row stride ldx),
 // w: [N, K] row-major (GGUF ne = {K, N}). The epilogues restate the rounding
@@ -88,10 +96,12 @@ size_t gemm_scratch_floats(int m, int n, int k, int num_sms, int force_splits, i
 // modulation: y = bf16(n * (1 + scale[c]) + shift[c]); scale/shift F32 [cols]
 // shared by all rows (norm_bf16_fused<affine=false>, native-bf16.patch:368-409).
 void launch_ln_modulate(const bf16* x, int ldx, int rows, int cols, const float* scale,
-                        const float* shift, float eps, bf16* y, int ldy, cudaStream_t s);
+                        const float* shift, float eps, bf16* y, int ldy, cudaStream_t s,
+                        const L2Prefetch& pf = L2Prefetch());
 // Affine LayerNorm: y = bf16(n * w[c] + b[c]), w/b BF16 (norm_bf16_fused<affine=true>).
 void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w, const bf16* b,
-                      float eps, bf16* y, int ldy, cudaStream_t s);
+                      float eps, bf16* y, int ldy, cudaStream_t s,
+                      const L2Prefetch& pf = L2Prefetch());
 
 // Per-token RMSNorm of q and k over the full attention width, RoPE, BF16 cast
 // and scatter into head-major attention buffers (expert_qkv, mot.cpp:210-267;
@@ -123,6 +133,7 @@ struct QkvScatter {
   bf16* v_out;
   long long kv_seq_stride, kv_head_stride;
   int kv_row_offset;
+  L2Prefetch pf;
 };
 void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s);
 
@@ -144,6 +155,7 @@ struct AttnArgs {
   bf16* out_first;
   int ldo_first;
   int split_first;
+  L2Prefetch pf;
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
 cudaError_t attention_init();

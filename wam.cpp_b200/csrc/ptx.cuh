@@ -191,6 +191,23 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
          (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// Bulk prefetch of a global range into L2 (16-byte aligned address and size).
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)),
+               "r"(bytes)
+               : "memory");
+}
+
+// ld.shared::cluster of four consecutive floats (16-byte aligned address).
+__device__ __forceinline__ float4 ld_shared_cluster_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 // ------------------------------------------------ programmatic dependent launch
 // Wait until the preceding kernel in the stream has completed and its memory
 // is visible (no-op when the kernel was launched without the PDL attribute).
