@@ -871,7 +871,10 @@ bool MotEngine::build(int b, std::string* err) {
       for (int l = 0; l < L && ok; ++l) {
         const std::string ap = "gwp.blk." + std::to_string(l) + ".a";
         const float* c = comb_steps_ + (static_cast<size_t>(s) * L + l) * 6 * E;
-        ln_mod(dp, ha_, M, E, c + E, c, nrm_);
+        // L2 prefetch schedule: each non-GEMM op pulls in the weights of the
+        // next GEMM(s) while it runs (HBM is otherwise idle during it).
+        const long long l2cap = 64ll << 20;
+        ln_mod(dp, ha_, M, E, c + E, c, nrm_, mkpf(wrange(ap + ".sa.qkv", 3LL * H, E, 0, l2cap)));
         G(dp, nrm_, E, M, ap + ".sa.qkv", 3 * H, E, EPI_BIAS, true, nullptr, nullptr, 0, qkv_, 3 * H);
         QkvScatter q{};
         q.src = qkv_;
@@ -913,11 +916,12 @@ bool MotEngine::build(int b, std::string* err) {
         at.scale = 1.0f / std::sqrt(128.0f);
         at.out = att_;
         at.ldo = H;
+        at.pf = mkpf(wrange(ap + ".sa.o", E, H), wrange(ap + ".ca.q", H, E));
         attend(dp, at);
         G(dp, att_, H, M, ap + ".sa.o", E, H, EPI_GATED_RES, true, c + 2 * E, ha_, E, ha_, E);
         ln_aff(dp, ha_, M, E, ap + ".ca_norm", nrm_);
         G(dp, nrm_, E, M, ap + ".ca.q", H, E, EPI_BIAS, true, nullptr, nullptr, 0, cq_, H);
-        cross_q(dp, cq_, M, T, ap, qc_);
+        cross_q(dp, cq_, M, T, ap, qc_, mkpf(wrange(ap + ".ca.o", E, H)));
         AttnArgs cx{};
         cx.q = qc_;
         cx.q_seq_stride = static_cast<long long>(heads) * T * 128;
@@ -933,9 +937,11 @@ bool MotEngine::build(int b, std::string* err) {
         cx.scale = at.scale;
         cx.out = catt_;
         cx.ldo = H;
+        cx.pf = mkpf(wrange(ap + ".ffn.in", Fa, E, 0, l2cap));
         attend(dp, cx);
         G(dp, catt_, H, M, ap + ".ca.o", E, H, EPI_RES, true, nullptr, ha_, E, ha_, E);
-        ln_mod(dp, ha_, M, E, c + 4 * E, c + 3 * E, nrm_);
+        ln_mod(dp, ha_, M, E, c + 4 * E, c + 3 * E, nrm_,
+               mkpf(wrange(ap + ".ffn.in", Fa, E, l2cap)));
         G(dp, nrm_, E, M, ap + ".ffn.in", Fa, E, EPI_BIAS_GELU, true, nullptr, nullptr, 0, ffn_, Fa);
         G(dp, ffn_, Fa, M, ap + ".ffn.out", E, Fa, EPI_GATED_RES, true, c + 5 * E, ha_, E, ha_, E);
       }

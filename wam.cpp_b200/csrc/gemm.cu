@@ -182,10 +182,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BT>::MIN_BLOCKS)
       const uint64_t pol_x = policy_evict_last();
       const int pre = nkb < C::STAGES ? nkb : C::STAGES;
       // Weights never depend on the preceding kernel: start streaming them
-      // before waiting for it (programmatic dependent launch). Tiles beyond the
-      // shared-memory pipeline are requested into L2 right away, so the whole
-      // weight slice of this CTA is in flight from the start.
-      for (int i = pre; i < nkb; ++i) tma_prefetch_2d(&tm_w, (kb0 + i) * kBK, tile_n * kBN);
+      // before waiting for it (programmatic dependent launch).
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
         tma_load_2d(smem_a + i * C::A_BYTES, &tm_w, &full[i], (kb0 + i) * kBK, tile_n * kBN, pol_w);
