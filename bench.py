@@ -241,6 +241,61 @@ def roofline_from_profile(prof: list[dict], pk: dict) -> tuple[dict, dict, dict]
     return hbm, tc, breakdown
 
 
+def run_op_case(args) -> None:
+    """One kernel of the chunk on its own, `--warmup` + `--steps` launches on
+    rotating buffers larger than L2: the case the ncu captures in profiles/ use."""
+    import torch
+    from wam_b200 import ops
+
+    kind, dims = args.op_case.split(":")
+    d = [int(v) for v in dims.split(",")]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device="cpu").manual_seed(SEED)
+    if kind == "gemm":
+        m, n, k = d
+        rot = max(2, (256 << 20) // (n * k * 2) + 1)  # > 2x L2 of weights in rotation
+        ws = [ops.TiledWeight((torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).to(dev))
+              for _ in range(rot)]
+        x = torch.randn(m, k, generator=gen).to(torch.bfloat16).to(dev)
+        b = torch.zeros(n, dtype=torch.bfloat16, device=dev)
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        fn = lambda i: ops.gemm(x, ws[i % rot], ops.EPI_BIAS, bias=b, out=y)
+        algo = n * k * 2 + m * k * 2 + m * n * 2
+    elif kind == "attention":
+        lq, lk, heads = d
+        q = torch.randn(1, heads, lq, 128, generator=gen).to(torch.bfloat16).to(dev)
+        rot = max(2, (256 << 20) // (heads * lk * 128 * 4) + 1)
+        kv = [(torch.randn(1, heads, lk, 128, generator=gen).to(torch.bfloat16).to(dev),
+               torch.randn(1, heads, lk, 128, generator=gen).to(torch.bfloat16).to(dev))
+              for _ in range(rot)]
+        o = torch.empty(lq, heads * 128, dtype=torch.bfloat16, device=dev)
+        fn = lambda i: ops.attention(q, kv[i % rot][0], kv[i % rot][1], out=o)
+        algo = heads * (2 * lq + 2 * lk) * 128 * 2
+    else:
+        raise SystemExit(f"unknown op case {kind}")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            fn(i)
+    torch.cuda.synchronize()
+    # The timed launches replay as one CUDA graph, so host call overhead does
+    # not show up between them.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(args.steps):
+            fn(i)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record()
+        graph.replay()
+        e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    print(json.dumps({"op_case": args.op_case, "launches": args.steps, "avg_us": round(us, 3),
+                      "algorithmic_bytes": algo, "GB/s": round(algo / us / 1e3, 1)}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -250,7 +305,13 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=1, help="requests per GPU per step")
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op-case", default=None,
+                    help="gemm:M,N,K or attention:LQ,LK,HEADS: run one kernel on a small case "
+                         "(for ncu captures) and print its event timing instead of the bench line")
     args = ap.parse_args()
+    if args.op_case:
+        run_op_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

@@ -59,10 +59,13 @@ WAM_B200_API const char* wam_b200_last_error(void);
  * 6 raw F32 accumulator, 7 bias then GELU(tanh) of the rounded linear,
  * 8 bias then exact-erf GELU. Split-K partial tiles are reduced through
  * distributed shared memory inside a thread-block cluster when workspace is
- * NULL (splits 1, 2, 4 or 8), or through the caller's global workspace
+ * NULL (1 to 8 splits), or through the caller's global workspace
  * (wam_b200_gemm_scratch_floats floats; counters zeroed before first use, the
  * kernel leaves them zero). force_splits <= 0 picks automatically. error:
- * device word receiving a non-zero code on a pipeline timeout.
+ * device word receiving a non-zero code on a pipeline timeout. OR-ing
+ * WAM_B200_GEMM_TILED_WEIGHTS into epilogue says w was written by
+ * wam_b200_op_retile_weights (n a multiple of 256): each 256x64 weight tile is
+ * then one contiguous 32 KB block fetched by a single bulk copy.
  * Replaces: linear / linear_with_activation / linear_gelu_with_activation
  * (src/models/gwp05/engine/weights.cpp:786-849) and gated_residual
  * (src/models/gwp05/engine/mot.cpp:161-173). */
@@ -90,6 +93,17 @@ WAM_B200_API int wam_b200_op_gemm_noalloc(const void* x, int ldx, int m, const v
                                           int k, int epilogue, const void* bias, const float* gate,
                                           const void* residual, int ldr, void* out, int ldo,
                                           int force_splits, void* stream);
+
+#define WAM_B200_GEMM_TILED_WEIGHTS 0x100
+
+/* Re-tiles a row-major BF16 weight w[n][k] (n % 256 == 0, k % 64 == 0, the
+ * GGUF ne = {k, n} layout) into dst as contiguous 32 KB tiles
+ * [n/256][k/64][256][64] with the tensor cores' 128-byte shared-memory swizzle
+ * pre-applied (16-byte chunk c of tile row r stored at chunk c ^ (r % 8)). src
+ * and dst must not overlap. No counterpart in the reference, which keeps GGUF's
+ * row-major layout (src/models/gwp05/engine/weights.cpp:702-770 loads tensors
+ * as stored); the engine applies it to every GEMM weight at load time. */
+WAM_B200_API int wam_b200_op_retile_weights(const void* src, void* dst, int n, int k, void* stream);
 
 /* Split-K scratch (floats) and output-tile count wam_b200_op_gemm needs for a shape. */
 WAM_B200_API size_t wam_b200_gemm_scratch_floats(int m, int n, int k, int force_splits,

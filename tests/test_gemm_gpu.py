@@ -53,9 +53,10 @@ def test_gemm_f32_accumulator(cuda_device, m, n, k, mode):
     assert rel_l2(y, ref) < 1e-5
 
 
-@pytest.mark.parametrize("splits,mode", [(1, "cluster"), (2, "cluster"), (4, "cluster"),
-                                         (8, "cluster"), (3, "workspace"), (7, "workspace"),
-                                         (4, "workspace")])
+@pytest.mark.parametrize("splits,mode", [(1, "cluster"), (2, "cluster"), (3, "cluster"),
+                                         (4, "cluster"), (5, "cluster"), (6, "cluster"),
+                                         (7, "cluster"), (8, "cluster"), (3, "workspace"),
+                                         (7, "workspace"), (4, "workspace"), (12, "workspace")])
 def test_gemm_forced_splits_deterministic(cuda_device, splits, mode):
     from wam_b200 import ops
 
@@ -72,12 +73,12 @@ def test_gemm_forced_splits_deterministic(cuda_device, splits, mode):
         assert int(s.counters.abs().sum()) == 0
 
 
-def test_gemm_cluster_rejects_odd_splits(cuda_device):
+def test_gemm_cluster_rejects_more_than_8_splits(cuda_device):
     from wam_b200 import ops
 
     x, w, _ = make(48, 512, 1024, seed=1)
     with pytest.raises(RuntimeError, match="cluster split-K"):
-        ops.gemm(x, w, epilogue=ops.EPI_F32_OUT, force_splits=3)
+        ops.gemm(x, w, epilogue=ops.EPI_F32_OUT, force_splits=9)
 
 
 def bf(x):
@@ -144,3 +145,52 @@ def test_gemm_in_place_residual(cuda_device):
     ops.gemm(x, w, ops.EPI_GATED_RES, bias=b, gate=gate, residual=h, out=h)
     torch.cuda.synchronize()
     assert rel_l2(h.float(), expect) < 1e-2
+
+
+@pytest.mark.parametrize("m,n,k", [(48, 3072, 3072), (768, 1024, 512), (1, 512, 256),
+                                   (384, 1536, 1024), (1000, 512, 640)])
+@pytest.mark.parametrize("mode", ["cluster", "workspace"])
+def test_gemm_tiled_weights_bit_exact(cuda_device, m, n, k, mode):
+    """Re-tiled weights change only where each tile is fetched from, not the
+    accumulation order: the result equals the row-major GEMM bit for bit."""
+    from wam_b200 import ops
+
+    x, w, b = make(m, n, k, seed=4)
+    tw = ops.TiledWeight(w)
+    s = ops.Scratch() if mode == "workspace" else None
+    for epi in (ops.EPI_F32_OUT, ops.EPI_BIAS_GELU):
+        y_row = ops.gemm(x, w, epi, bias=b, scratch=s)
+        y_tiled = ops.gemm(x, tw, epi, bias=b, scratch=s)
+        torch.cuda.synchronize()
+        assert torch.equal(y_row, y_tiled)
+    ref = x.float() @ w.float().T
+    assert rel_l2(ops.gemm(x, tw, ops.EPI_F32_OUT).float(), ref) < 1e-5
+
+
+def test_retile_layout(cuda_device):
+    """Chunk c (8 BF16) of row r of tile (nt, kb) lands at chunk c ^ (r % 8) of
+    that row inside the tile's contiguous 256 x 64 block."""
+    from wam_b200 import ops
+
+    n, k = 512, 192
+    w = torch.arange(n * k, dtype=torch.float32).remainder(251).to(torch.bfloat16).view(n, k)
+    w = w.to("cuda")
+    got = ops.TiledWeight(w).data.view(n // 256, k // 64, 256, 8, 8).cpu()
+    wc = w.cpu().view(n // 256, 256, k // 64, 8, 8).permute(0, 2, 1, 3, 4)  # nt, kb, r, c, e
+    expect = torch.empty_like(got)
+    for r in range(256):
+        for c in range(8):
+            expect[:, :, r, c ^ (r % 8)] = wc[:, :, r, c]
+    assert torch.equal(got, expect)
+
+
+def test_retile_rejects_bad_shapes(cuda_device):
+    from wam_b200 import ops
+
+    with pytest.raises(RuntimeError, match="retile"):
+        ops.TiledWeight(torch.zeros(100, 64, dtype=torch.bfloat16, device="cuda"))
+    x, w, _ = make(16, 256, 64)
+    tw = ops.TiledWeight(w)
+    tw.shape = (128, 64)  # not a whole number of 256-row tiles
+    with pytest.raises(RuntimeError, match="multiple of 256"):
+        ops.gemm(x[:, :64], tw, ops.EPI_F32_OUT)

@@ -49,7 +49,7 @@ __device__ __forceinline__ void load_tile(uint32_t smem, const bf16* g, int rows
 // running max / sum in shared memory and the cluster merges rows through
 // distributed shared memory in fixed peer order.
 template <bool SPLIT>
-__global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a, int splits) {
+__global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ AttnArgs a, int splits) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t s_q = smem_u32(smem);
   const uint32_t s_k[2] = {s_q + kTileBytes, s_q + 3 * kTileBytes};

@@ -81,11 +81,13 @@ WAM_B200_API int wam_b200_op_gemm(const void* x, int ldx, int m, const void* w, 
   scratch.counters = counters;
   scratch.counter_slots = counter_slots;
   scratch.error = error;
+  const bool tiled = (epilogue & WAM_B200_GEMM_TILED_WEIGHTS) != 0;
+  epilogue &= ~WAM_B200_GEMM_TILED_WEIGHTS;
   GemmOp op;
   const char* err = gemm_plan(&op, static_cast<const bf16*>(x), ldx, m, static_cast<const bf16*>(w),
                               n, k, epilogue, static_cast<const bf16*>(bias), gate,
                               static_cast<const bf16*>(residual), ldr, out, ldo, scratch,
-                              num_sms_current(), force_splits);
+                              num_sms_current(), force_splits, tiled);
   if (err) {
     set_last_error(err);
     return WAM_B200_INVALID_ARGUMENT;
@@ -93,6 +95,35 @@ WAM_B200_API int wam_b200_op_gemm(const void* x, int ldx, int m, const void* w, 
   cudaError_t ce = gemm_launch(op, static_cast<cudaStream_t>(stream));
   if (ce != cudaSuccess) {
     set_last_error(std::string("gemm launch: ") + cudaGetErrorString(ce));
+    return WAM_B200_CUDA_ERROR;
+  }
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_op_retile_weights(const void* src, void* dst, int n, int k,
+                                            void* stream) {
+  std::string why;
+  int rc = check_sm100(&why);
+  if (rc != WAM_B200_OK) {
+    set_last_error(why);
+    return rc;
+  }
+  if (!src || !dst || n <= 0 || k <= 0 || n % gemm_weight_tile_rows() || k % 64 ||
+      (reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) % 16) {
+    set_last_error("retile_weights: n % 256, k % 64 and 16-byte aligned pointers required");
+    return WAM_B200_INVALID_ARGUMENT;
+  }
+  const uintptr_t a = reinterpret_cast<uintptr_t>(src), b = reinterpret_cast<uintptr_t>(dst);
+  const uintptr_t bytes = static_cast<uintptr_t>(n) * k * 2;
+  if (a < b + bytes && b < a + bytes) {
+    set_last_error("retile_weights: src and dst overlap");
+    return WAM_B200_INVALID_ARGUMENT;
+  }
+  launch_retile_weights(static_cast<const bf16*>(src), static_cast<bf16*>(dst), n, k,
+                        static_cast<cudaStream_t>(stream));
+  cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) {
+    set_last_error(std::string("retile_weights launch: ") + cudaGetErrorString(ce));
     return WAM_B200_CUDA_ERROR;
   }
   return WAM_B200_OK;

@@ -64,7 +64,7 @@ __device__ __forceinline__ float block128_sum(float v, float* red) {
 template <int MODE, int MAXC>
 __global__ void __launch_bounds__(kRowThreads)
     ln_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
-              const void* pb, float eps, bf16* __restrict__ y, int ldy, const L2Prefetch pf) {
+              const void* pb, float eps, bf16* __restrict__ y, int ldy, const __grid_constant__ L2Prefetch pf) {
   if (threadIdx.x == 0) l2_prefetch_share(pf, blockIdx.x, gridDim.x);
   griddep_wait();
   griddep_launch_dependents();
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(kRowThreads)
 template <int MODE>
 __global__ void __launch_bounds__(256)
     ln_wide_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
-                   const void* pb, float eps, bf16* __restrict__ y, int ldy, const L2Prefetch pf) {
+                   const void* pb, float eps, bf16* __restrict__ y, int ldy, const __grid_constant__ L2Prefetch pf) {
   if (threadIdx.x == 0) l2_prefetch_share(pf, blockIdx.x, gridDim.x);
   griddep_wait();
   griddep_launch_dependents();
@@ -190,7 +190,7 @@ __device__ __forceinline__ float rope_theta(const QkvScatter& a, int dim, int po
 // part; each thread holds up to MAXC 8-wide chunks of its part (and the norm
 // weights) in registers. MAXC = 0: generic loop.
 template <int MAXC>
-__global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const QkvScatter a) {
+__global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const __grid_constant__ QkvScatter a) {
   if (threadIdx.x == 0 && threadIdx.y == 0) l2_prefetch_share(a.pf, blockIdx.x, gridDim.x);
   griddep_wait();
   griddep_launch_dependents();

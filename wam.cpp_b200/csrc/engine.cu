@@ -18,6 +18,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "gguf.h"
@@ -169,6 +170,7 @@ std::unique_ptr<MotEngine> MotEngine::create(const EngineOptions& opt, std::stri
 }
 
 MotEngine::~MotEngine() {
+  if (side_) cudaStreamSynchronize(side_);
   if (stream_) cudaStreamSynchronize(stream_);
   drop_plans();
   for (auto& e : phase_ev_)
@@ -180,6 +182,10 @@ MotEngine::~MotEngine() {
   if (h_noise_) cudaFreeHost(h_noise_);
   if (h_out_) cudaFreeHost(h_out_);
   if (warena_) cudaFree(warena_);
+  if (retile_tmp_) cudaFree(retile_tmp_);
+  if (ev_fork_) cudaEventDestroy(ev_fork_);
+  if (ev_join_) cudaEventDestroy(ev_join_);
+  if (side_) cudaStreamDestroy(side_);
   if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -205,6 +211,12 @@ bool MotEngine::init(const EngineOptions& opt, std::string* err) {
   }
   CK(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, opt.device));
   CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  CK(cudaStreamCreateWithFlags(&side_, cudaStreamNonBlocking));
+  CK(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
+  CK(cudaEventCreateWithFlags(&ev_join_, cudaEventDisableTiming));
+  // Diagnostic switch: keep GEMM weights in GGUF's row-major layout.
+  const char* rm = std::getenv("WAM_B200_ROWMAJOR_WEIGHTS");
+  rowmajor_weights_ = rm && rm[0] && rm[0] != '0';
   CK(gemm_init(opt.device));
   CK(attention_init());
   if (!load_weights(err)) return false;
@@ -465,6 +477,11 @@ bool MotEngine::alloc_buffers(std::string* err) {
   AL(k_vis_, bf16, B * L * heads * Nt * 128);
   AL(v_vis_, bf16, B * L * heads * Nt * 128);
   AL(err_word_, unsigned, 1);
+  // A split GEMM holds at most one wave of CTAs, each with a partial tile of
+  // <= 128 tokens x 256 features: sms x 128 x 256 floats bound every plan.
+  gemm_ws_floats_ = static_cast<size_t>(sms_) * 128 * 256;
+  AL(gemm_ws_[0], float, gemm_ws_floats_);
+  AL(gemm_ws_[1], float, gemm_ws_floats_);
 #undef AL
   // constants: timestep frequencies (row 0: t = 0 for the prefix, rows 1..S the
   // schedule), dt, RoPE inverse frequencies, visual positions, table pointers.
@@ -519,11 +536,39 @@ bool MotEngine::gemm(Program& p, const bf16* x, int ldx, int m, const std::strin
     *err = "missing or mis-shaped weight " + wname;
     return false;
   }
-  // Split-K partials are reduced inside thread-block clusters: no scratch.
+  // Every weight with whole 256-row tiles is re-tiled in place, the first time
+  // a plan uses it, into contiguous 32 KB UMMA tiles (one bulk copy per stage).
+  const bool tiled = !rowmajor_weights_ && n % gemm_weight_tile_rows() == 0 && k % 64 == 0;
+  if (tiled && !tiled_[wname]) {
+    const size_t elems = static_cast<size_t>(n) * k;
+    if (elems > retile_tmp_elems_) {
+      if (retile_tmp_) {
+        CK(cudaStreamSynchronize(stream_));
+        cudaFree(retile_tmp_);
+        retile_tmp_ = nullptr;
+      }
+      cudaError_t ae = cudaMalloc(&retile_tmp_, elems * sizeof(bf16));
+      if (ae != cudaSuccess) {
+        retile_tmp_elems_ = 0;
+        *err = std::string("re-tiling staging buffer: ") + cudaGetErrorString(ae);
+        return false;
+      }
+      retile_tmp_elems_ = elems;
+    }
+    bf16* wm = w_[wname + ".weight"];
+    CK(cudaMemcpyAsync(retile_tmp_, wm, elems * sizeof(bf16), cudaMemcpyDeviceToDevice, stream_));
+    launch_retile_weights(retile_tmp_, wm, n, k, stream_);
+    CK(cudaGetLastError());
+    tiled_[wname] = true;
+  }
+  // Split-K partials go through this lane's workspace inside a cluster.
   GemmScratch sc;
+  sc.workspace = gemm_ws_[p.lane];
+  sc.workspace_floats = gemm_ws_floats_;
   sc.error = err_word_;
   GemmOp op;
-  const char* e = gemm_plan(&op, x, ldx, m, w, n, k, epi, b, gate, resid, ldr, out, ldo, sc, sms_, 0);
+  const char* e =
+      gemm_plan(&op, x, ldx, m, w, n, k, epi, b, gate, resid, ldr, out, ldo, sc, sms_, 0, tiled);
   if (e) {
     *err = std::string(e) + " (" + wname + ")";
     return false;
@@ -562,6 +607,26 @@ bool MotEngine::build(int b, std::string* err) {
       if (ok && !gemm(p, x, ldx, m, wn, n, k, epi, bias, gate, resid, ldr, out, ldo, &e2)) ok = false;
     };
     auto K = [](Program& p, Launch f) { p.add(std::move(f), OP_ELEMENTWISE); };
+    // Lane hand-offs: the side stream waits for everything the main stream has
+    // issued so far (fork), or the main stream for the side stream (join).
+    auto fork_side = [&](Program& p) {
+      const int lane = p.lane;
+      p.lane = 0;
+      p.add([this](cudaStream_t) {
+        cudaError_t e = cudaEventRecord(ev_fork_, stream_);
+        return e == cudaSuccess ? cudaStreamWaitEvent(side_, ev_fork_, 0) : e;
+      }, OP_SYNC, 0);
+      p.lane = lane;
+    };
+    auto join_side = [&](Program& p) {
+      const int lane = p.lane;
+      p.lane = 0;
+      p.add([this](cudaStream_t) {
+        cudaError_t e = cudaEventRecord(ev_join_, side_);
+        return e == cudaSuccess ? cudaStreamWaitEvent(stream_, ev_join_, 0) : e;
+      }, OP_SYNC, 0);
+      p.lane = lane;
+    };
     auto scatter = [&](Program& p, const QkvScatter& q) {
       const double parts = (q.q_col >= 0) + (q.k_col >= 0) + (q.v_col >= 0);
       p.add([q](cudaStream_t s) {
@@ -746,16 +811,17 @@ bool MotEngine::build(int b, std::string* err) {
     });
     mp.ops.back().launches = 4;
     mp.kernels += 3;
+    fork_side(mp);  // the state lane starts from hs_ and the modulation tables
     for (int l = 0; l < L && ok; ++l) {
       const std::string ap = "gwp.blk." + std::to_string(l) + ".a";
       const std::string vp = "gwp.blk." + std::to_string(l) + ".v";
       const float* ca = comb_a0_ + static_cast<size_t>(l) * 6 * E;
       const float* cv = comb_v_ + static_cast<size_t>(l) * 6 * H;
-      ln_mod(mp, hv_, b * V, H, cv + H, cv, nrm_);
-      ln_mod(mp, hs_, b, E, ca + E, ca, nrm_s_);
-      G(mp, nrm_, H, b * V, vp + ".sa.qkv", 3 * H, H, EPI_BIAS, true, nullptr, nullptr, 0, qkv_, 3 * H);
-      G(mp, nrm_s_, E, b, ap + ".sa.qkv", 3 * H, E, EPI_BIAS, true, nullptr, nullptr, 0, qkv_s_, 3 * H);
-      for (int x = 0; x < 2; ++x) {
+      // Two lanes: the visual expert (768 tokens, tensor bound) stays on the main
+      // stream, the state token's action-expert work (one token, weight
+      // streaming) runs beside it on the side stream; they meet at the joint
+      // self-attention, which needs both halves of the layer's K/V.
+      auto scatter_part = [&](int x) {
         QkvScatter q{};
         const bool vis = x == 1;
         const std::string& pf = vis ? vp : ap;
@@ -789,7 +855,16 @@ bool MotEngine::build(int b, std::string* err) {
           e2 = "missing q/k norm of " + pf;
         }
         scatter(mp, q);
-      }
+      };
+      mp.lane = 1;
+      ln_mod(mp, hs_, b, E, ca + E, ca, nrm_s_);
+      G(mp, nrm_s_, E, b, ap + ".sa.qkv", 3 * H, E, EPI_BIAS, true, nullptr, nullptr, 0, qkv_s_, 3 * H);
+      scatter_part(0);
+      mp.lane = 0;
+      ln_mod(mp, hv_, b * V, H, cv + H, cv, nrm_);
+      G(mp, nrm_, H, b * V, vp + ".sa.qkv", 3 * H, H, EPI_BIAS, true, nullptr, nullptr, 0, qkv_, 3 * H);
+      scatter_part(1);
+      join_side(mp);
       if (l + 1 == L) break;  // the last layer's outputs feed no cached K/V
       AttnArgs at{};
       at.q = qbuf_;
@@ -810,8 +885,8 @@ bool MotEngine::build(int b, std::string* err) {
       at.ldo_first = H;
       at.split_first = 1;
       attend(mp, at);
+      fork_side(mp);
       G(mp, att_, H, b * V, vp + ".sa.o", H, H, EPI_GATED_RES, true, cv + 2 * H, hv_, H, hv_, H);
-      G(mp, att_s_, H, b, ap + ".sa.o", E, H, EPI_GATED_RES, true, ca + 2 * E, hs_, E, hs_, E);
       // visual expert: cross attention over its text K/V, FFN
       ln_aff(mp, hv_, b * V, H, vp + ".ca_norm", nrm_);
       G(mp, nrm_, H, b * V, vp + ".ca.q", H, H, EPI_BIAS, true, nullptr, nullptr, 0, cq_, H);
@@ -836,6 +911,8 @@ bool MotEngine::build(int b, std::string* err) {
       ln_mod(mp, hv_, b * V, H, cv + 4 * H, cv + 3 * H, nrm_);
       G(mp, nrm_, H, b * V, vp + ".ffn.in", Fv, H, EPI_BIAS_GELU, true, nullptr, nullptr, 0, ffn_, Fv);
       G(mp, ffn_, Fv, b * V, vp + ".ffn.out", H, Fv, EPI_GATED_RES, true, cv + 5 * H, hv_, H, hv_, H);
+      mp.lane = 1;
+      G(mp, att_s_, H, b, ap + ".sa.o", E, H, EPI_GATED_RES, true, ca + 2 * E, hs_, E, hs_, E);
       // state token (action expert): cross attention over the prompt K/V, FFN
       ln_aff(mp, hs_, b, E, ap + ".ca_norm", nrm_s_);
       G(mp, nrm_s_, E, b, ap + ".ca.q", H, E, EPI_BIAS, true, nullptr, nullptr, 0, cq_s_, H);
@@ -853,8 +930,8 @@ bool MotEngine::build(int b, std::string* err) {
       ln_mod(mp, hs_, b, E, ca + 4 * E, ca + 3 * E, nrm_s_);
       G(mp, nrm_s_, E, b, ap + ".ffn.in", Fa, E, EPI_BIAS_GELU, true, nullptr, nullptr, 0, ffn_s_, Fa);
       G(mp, ffn_s_, Fa, b, ap + ".ffn.out", E, Fa, EPI_GATED_RES, true, ca + 5 * E, hs_, E, hs_, E);
+      mp.lane = 0;
     }
-
     // ---------------- denoise (mot.cpp:358-496, unrolled over the schedule)
     Program& dp = plan->prog[2];
     const bf16* ain_w = W("gwp.action.in.weight", static_cast<int64_t>(g.num_embodiments) * A * 128);
@@ -979,6 +1056,12 @@ bool MotEngine::build(int b, std::string* err) {
         ++it;
       }
     }
+    if (retile_tmp_) {  // weights re-tiled while planning; the staging copy is no longer needed
+      CK(cudaStreamSynchronize(stream_));
+      cudaFree(retile_tmp_);
+      retile_tmp_ = nullptr;
+      retile_tmp_elems_ = 0;
+    }
     if (opt_.graphs) {
       for (int which = 0; which < 3; ++which) {
         Program& p = plan->prog[which];
@@ -986,7 +1069,7 @@ bool MotEngine::build(int b, std::string* err) {
         CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
         cudaError_t le = cudaSuccess;
         for (auto& op : p.ops) {
-          le = op.fn(stream_);
+          le = op.fn(op.lane ? side_ : stream_);
           if (le != cudaSuccess) break;
         }
         cudaError_t ce = cudaStreamEndCapture(stream_, &graph);
@@ -1118,7 +1201,7 @@ bool MotEngine::run(int batch, std::string* err, EngineStats* stats) {
       CK(cudaGraphLaunch(plan.graph[which], stream_));
       return true;
     }
-    for (auto& op : plan.prog[which].ops) CK(op.fn(stream_));
+    for (auto& op : plan.prog[which].ops) CK(op.fn(op.lane ? side_ : stream_));
     return true;
   };
   if (!phase_ev_[0])
@@ -1161,14 +1244,18 @@ bool MotEngine::profile(int batch, std::vector<OpProfile>* out, std::string* err
     it = plans_.find(batch);
   }
   Plan& plan = *it->second;
+  // Every op runs alone on the main stream, timed by a pair of events; the
+  // lane hand-offs are skipped.
   size_t n = 0;
-  for (auto& p : plan.prog) n += p.ops.size();
+  for (auto& p : plan.prog)
+    for (auto& op : p.ops) n += op.kind != OP_SYNC;
   std::vector<cudaEvent_t> ev(n + 1);
   for (auto& e : ev) CK(cudaEventCreate(&e));
   size_t i = 0;
   CK(cudaEventRecord(ev[0], stream_));
   for (auto& p : plan.prog)
     for (auto& op : p.ops) {
+      if (op.kind == OP_SYNC) continue;
       CK(op.fn(stream_));
       CK(cudaEventRecord(ev[++i], stream_));
     }
@@ -1177,6 +1264,7 @@ bool MotEngine::profile(int batch, std::vector<OpProfile>* out, std::string* err
   i = 0;
   for (int ph = 0; ph < 3; ++ph)
     for (auto& op : plan.prog[ph].ops) {
+      if (op.kind == OP_SYNC) continue;
       OpProfile r{ph, op.kind, op.launches, 0.0f, op.bytes, op.flops,
                   {op.shape[0], op.shape[1], op.shape[2], op.shape[3]}};
       cudaEventElapsedTime(&r.ms, ev[i], ev[i + 1]);

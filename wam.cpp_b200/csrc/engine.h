@@ -60,7 +60,7 @@ using Launch = std::function<cudaError_t(cudaStream_t)>;
 
 // Kernel families, for the per-kernel profile (wam_b200_profile).
 enum OpKind : int { OP_GEMM = 0, OP_ATTENTION = 1, OP_LAYERNORM = 2, OP_QKV = 3, OP_SMALL = 4,
-                    OP_ELEMENTWISE = 5 };
+                    OP_ELEMENTWISE = 5, OP_SYNC = 6 /* lane hand-off, no kernel */ };
 
 struct Op {
   Launch fn;
@@ -69,13 +69,18 @@ struct Op {
   double bytes = 0.0;   // algorithmic HBM bytes (operands read + results written)
   double flops = 0.0;   // algorithmic FLOPs
   int shape[4] = {0, 0, 0, 0};  // GEMM: m, n, k, split-K factor
+  int lane = 0;                 // 0: main stream, 1: side stream
 };
 
+// Ops in issue order. Each op runs on the stream of its lane; OP_SYNC ops
+// hand work between the lanes with events (captured as graph edges).
 struct Program {
   std::vector<Op> ops;
   int kernels = 0;
+  int lane = 0;  // lane of the ops added next
   void add(Launch f, int kind, int launches = 1, double bytes = 0.0, double flops = 0.0) {
     ops.push_back(Op{std::move(f), kind, launches, bytes, flops});
+    ops.back().lane = lane;
     kernels += launches;
   }
 };
@@ -148,6 +153,8 @@ class MotEngine {
   Geometry g_;
   int sms_ = 148;
   cudaStream_t stream_ = nullptr;
+  cudaStream_t side_ = nullptr;  // second lane of the prefix program
+  cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
   bool ok_ = false;
   std::string loader_;
 
@@ -156,6 +163,11 @@ class MotEngine {
   size_t warena_bytes_ = 0;
   std::unordered_map<std::string, bf16*> w_;
   std::unordered_map<std::string, int64_t> wn_;
+  // GEMM weights already re-tiled in place into 16 KB UMMA tiles.
+  std::unordered_map<std::string, bool> tiled_;
+  bf16* retile_tmp_ = nullptr;  // staging copy for in-place re-tiling (build only)
+  size_t retile_tmp_elems_ = 0;
+  bool rowmajor_weights_ = false;
   std::vector<float> sq01_, sq99_, aq01_, aq99_;
   uint64_t resident_bytes_ = 0;
 
@@ -186,10 +198,9 @@ class MotEngine {
   bf16 *k_self_ = nullptr, *v_self_ = nullptr;      // [B][L][heads][P+T][128]
   bf16 *k_prompt_ = nullptr, *v_prompt_ = nullptr;  // [B][L][heads][Nt][128] (action expert)
   bf16 *k_vis_ = nullptr, *v_vis_ = nullptr;        // [B][L][heads][Nt][128] (visual expert)
-  float* ws_ = nullptr;
-  size_t ws_floats_ = 0;
-  unsigned* counters_ = nullptr;
-  int counter_slots_ = 0;
+  // Split-K exchange workspace, one per lane (the lanes' GEMMs may overlap).
+  float* gemm_ws_[2] = {nullptr, nullptr};
+  size_t gemm_ws_floats_ = 0;
   unsigned* err_word_ = nullptr;
 
   std::vector<float> timesteps_, sigmas_;

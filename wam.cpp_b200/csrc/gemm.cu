@@ -1,18 +1,22 @@
 // BF16 tcgen05 GEMM for every linear layer of the MoT forward pass.
 //
-// Orientation: the weight tile is the UMMA "A" operand (128 output features =
-// the 128 TMEM lanes) and the token tile is "B" (UMMA N = BT tokens). The
-// accumulator tile D[feature][token] lives in TMEM; each epilogue thread owns
-// one feature (one TMEM lane), so per-feature bias / gate values are register
-// constants and the stores of a warp cover 32 consecutive features.
-// This keeps one kernel efficient for both regimes of the forward pass:
-//   * denoise at batch 1 (48 tokens): weight streaming, HBM bound; split-K over
-//     CTAs fills all 148 SMs and the last CTA to finish a tile reduces the F32
-//     partials (deterministic order) and runs the epilogue;
-//   * prefix / batched denoise (768..49152 tokens): tensor-core bound.
-// Pipeline: warp 0 = TMA producer, warp 1 = TMEM allocator + single-thread
-// UMMA issuer, warps 2-5 = epilogue. Shared-memory stages hold one 128 x 64
-// weight tile and one BT x 64 token tile, both K-major with 128-byte swizzle.
+// Orientation: the token tile is the UMMA "A" operand (M = 128 token rows =
+// the 128 TMEM lanes) and the weight tile is "B" (N = 256 output features =
+// 256 TMEM columns). One tcgen05.mma of M = 128, K = 16 occupies the tensor
+// core for about the same ~130 cycles for every N up to 256 (measured on
+// B200), so 256 weight rows per instruction double the weight bytes an SM can
+// consume per cycle compared with putting the weights on the M side, which is
+// what bounds the batch-1 denoise GEMMs (48 tokens: HBM/weight streaming).
+// Token tiles shorter than 128 rows load only the rows that exist; the
+// accumulator rows of the missing tokens are never read.
+//
+// Pipeline: warp 0 = TMA / bulk-copy producer, warp 1 = TMEM allocator +
+// single-thread UMMA issuer, warps 2-5 = epilogue (warp w reads TMEM lanes
+// 32*(w%4).., i.e. one token per thread, 16 features per tcgen05.ld, and
+// stores them as 16-byte vectors along the feature axis).
+// Split-K: the splits of one output tile form a thread-block cluster and
+// reduce their F32 partial tiles through distributed shared memory, or go
+// through a caller-provided global workspace (the last CTA reduces).
 //
 // Reference: every ggml_mul_mat / ggml_mul_mat_out_type of the BF16 latency
 // path (src/models/gwp05/engine/weights.cpp:786-849; cuBLAS route in
@@ -31,110 +35,300 @@ namespace wamb {
 
 namespace {
 
-constexpr int kBN = 128;  // weight rows per tile (UMMA M, TMEM lanes)
-constexpr int kBK = 64;   // K per stage: one 128-byte swizzle row of BF16
+constexpr int kTM = 128;              // token rows per tile (UMMA M, TMEM lanes)
+constexpr int kWN = 256;              // weight rows per tile (UMMA N, TMEM columns)
+constexpr int kBK = 64;               // K per stage: one 128-byte swizzle row of BF16
+constexpr int kBBytes = kWN * kBK * 2;  // weight tile per stage (32 KB)
 constexpr int kThreads = 192;
+constexpr int kStageBudget = 200 * 1024;
+constexpr int kMaxStages = 8;
+#ifndef WAM_GEMM_WEIGHT_EVICT_FIRST
+#define WAM_GEMM_WEIGHT_EVICT_FIRST 1
+#endif
+constexpr int kPartLd = kWN + 4;      // padded F32 row of a staged partial tile
+constexpr int kSmemTail = 256 + 2 * kWN * 4;  // barriers + staged bias / gate
+constexpr uint32_t kTmemCols = kWN;
 
-template <int BT>
-struct Cfg {
-  static constexpr int A_BYTES = kBN * kBK * 2;
-  static constexpr int B_BYTES = BT * kBK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // Small token tiles (the weight-streaming regime) keep ~96 KB of stages so
-  // that two CTAs share an SM; large tiles keep a deep single-CTA pipeline.
-  static constexpr int MIN_BLOCKS = BT <= 64 ? 2 : 1;
-  static constexpr int BUDGET = BT <= 64 ? 96 * 1024 : 200 * 1024;
-  static constexpr int STAGES_RAW = BUDGET / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-  static constexpr int TMEM_COLS = BT <= 32 ? 32 : (BT <= 64 ? 64 : (BT <= 128 ? 128 : 256));
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
-  static constexpr int PARTIAL_BYTES = BT * kBN * 4;  // F32 split-K partial tile
-  static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "UMMA N for M=128");
-  static_assert(STAGES >= 2, "pipeline depth");
-  static_assert(PARTIAL_BYTES <= STAGES * STAGE_BYTES, "partial tile reuses the stage buffers");
-};
+// Token rows a tile loads: all 128 when the GEMM has that many, else the
+// token count rounded up to 16.
+int a_rows_for(int m) { return m >= kTM ? kTM : ((m + 15) / 16) * 16; }
 
-__device__ __forceinline__ void store_out(const GemmArgs& a, int m, int n, float acc, float b,
-                                          float g) {
-  const long long o = static_cast<long long>(m) * a.ldo + n;
-  bf16* out = static_cast<bf16*>(a.out);
-  switch (a.epilogue) {
-    case EPI_BIAS: {
-      float v = bf16_round(acc);
-      if (a.bias) v = v + b;
-      out[o] = __float2bfloat16_rn(v);
-      break;
+// Pipeline stages: one weight k-block (32 KB) and one token k-block per
+// stage, as many stages as the shared-memory budget holds (the weight stream
+// is latency bound, so the bytes in flight per SM set its rate).
+int stages_for(int a_rows) {
+  const int st = kStageBudget / (a_rows * kBK * 2 + kBBytes);
+  return st > kMaxStages ? kMaxStages : st;
+}
+int smem_for(int a_rows) {
+  return stages_for(a_rows) * (a_rows * kBK * 2 + kBBytes) + 1024 + kSmemTail;
+}
+
+// Epilogue of CNT consecutive features n0.. of token m (CNT = 8 or 16; the
+// epilogue kind is a compile-time constant so each run is straight-line code).
+template <int EPI, int CNT>
+__device__ __forceinline__ void epi_run_t(const GemmArgs& a, int m, int n0, const float* v,
+                                          const float* bias, const float* gate) {
+  float o[CNT];
+  float r[CNT];
+  if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
+    const uint4* rp =
+        reinterpret_cast<const uint4*>(a.residual + static_cast<long long>(m) * a.ldr + n0);
+#pragma unroll
+    for (int q = 0; q < CNT / 8; ++q) {
+      const uint4 u = rp[q];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        r[q * 8 + 2 * j] = __uint_as_float(w[j] << 16);
+        r[q * 8 + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+      }
     }
-    case EPI_BIAS_GELU: {
-      const float v = bf16_round(acc) + b;
-      out[o] = __float2bfloat16_rn(gelu_tanh(v));
-      break;
+  }
+  const bool hb = a.bias != nullptr;
+#pragma unroll
+  for (int j = 0; j < CNT; ++j) {
+    const float acc = v[j];
+    const float b = bias[j];
+    if constexpr (EPI == EPI_BIAS) {
+      float t = bf16_round(acc);
+      if (hb) t = t + b;
+      o[j] = t;
+    } else if constexpr (EPI == EPI_BIAS_GELU) {
+      o[j] = gelu_tanh(bf16_round(acc) + b);
+    } else if constexpr (EPI == EPI_BIAS_SILU) {
+      float t = bf16_round(acc);
+      if (hb) t = bf16_round(t + b);
+      o[j] = silu(t);
+    } else if constexpr (EPI == EPI_GATED_RES) {
+      float t = bf16_round(acc);
+      if (hb) t = bf16_round(t + b);
+      o[j] = fmaf(t, gate[j], r[j]);
+    } else if constexpr (EPI == EPI_RES) {
+      float t = bf16_round(acc);
+      if (hb) t = bf16_round(t + b);
+      o[j] = r[j] + t;
+    } else if constexpr (EPI == EPI_F32_BIAS) {
+      o[j] = acc + b;
+    } else if constexpr (EPI == EPI_BIAS_GELU_R) {
+      float t = bf16_round(acc);
+      if (hb) t = bf16_round(t + b);
+      o[j] = gelu_tanh(t);
+    } else if constexpr (EPI == EPI_BIAS_GELU_ERF) {
+      float t = bf16_round(acc);
+      if (hb) t = bf16_round(t + b);
+      o[j] = gelu_erf(t);
+    } else {
+      o[j] = acc;
     }
-    case EPI_BIAS_SILU: {
-      float v = bf16_round(acc);
-      if (a.bias) v = bf16_round(v + b);
-      out[o] = __float2bfloat16_rn(silu(v));
-      break;
-    }
-    case EPI_GATED_RES: {
-      float v = bf16_round(acc);
-      if (a.bias) v = bf16_round(v + b);
-      const float r = __bfloat162float(a.residual[static_cast<long long>(m) * a.ldr + n]);
-      out[o] = __float2bfloat16_rn(fmaf(v, g, r));
-      break;
-    }
-    case EPI_RES: {
-      float v = bf16_round(acc);
-      if (a.bias) v = bf16_round(v + b);
-      const float r = __bfloat162float(a.residual[static_cast<long long>(m) * a.ldr + n]);
-      out[o] = __float2bfloat16_rn(r + v);
-      break;
-    }
-    case EPI_F32_BIAS: {
-      out[o] = __float2bfloat16_rn(acc + b);
-      break;
-    }
-    case EPI_BIAS_GELU_R: {
-      float v = bf16_round(acc);
-      if (a.bias) v = bf16_round(v + b);
-      out[o] = __float2bfloat16_rn(gelu_tanh(v));
-      break;
-    }
-    case EPI_BIAS_GELU_ERF: {
-      float v = bf16_round(acc);
-      if (a.bias) v = bf16_round(v + b);
-      out[o] = __float2bfloat16_rn(gelu_erf(v));
-      break;
-    }
-    default: {
-      static_cast<float*>(a.out)[o] = acc;
-      break;
+  }
+  if constexpr (EPI == EPI_F32_OUT) {
+    float4* op = reinterpret_cast<float4*>(static_cast<float*>(a.out) +
+                                           static_cast<long long>(m) * a.ldo + n0);
+#pragma unroll
+    for (int q = 0; q < CNT / 4; ++q)
+      op[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+  } else {
+    uint4* op = reinterpret_cast<uint4*>(static_cast<bf16*>(a.out) +
+                                         static_cast<long long>(m) * a.ldo + n0);
+#pragma unroll
+    for (int q = 0; q < CNT / 8; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(o[q * 8 + 2 * j], o[q * 8 + 2 * j + 1]);
+        w[j] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      op[q] = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 }
 
-// CTA x = (tile, split) with the split index fastest, so that in cluster mode
-// one thread-block cluster holds exactly the splits of one output tile.
-template <int BT>
-__global__ void __launch_bounds__(kThreads, Cfg<BT>::MIN_BLOCKS)
-    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
-                        const __grid_constant__ CUtensorMap tm_x, const GemmArgs args) {
-  using C = Cfg<BT>;
+// Dispatches the epilogue once per run (a per-element switch over nine
+// inlined epilogues made every store wait on instruction fetch).
+template <int CNT>
+__device__ __forceinline__ void epi_run(const GemmArgs& a, int m, int n0, const float* v,
+                                        const float* bias, const float* gate) {
+  if (n0 >= a.n) return;
+  switch (a.epilogue) {
+    case EPI_BIAS: epi_run_t<EPI_BIAS, CNT>(a, m, n0, v, bias, gate); break;
+    case EPI_BIAS_GELU: epi_run_t<EPI_BIAS_GELU, CNT>(a, m, n0, v, bias, gate); break;
+    case EPI_BIAS_SILU: epi_run_t<EPI_BIAS_SILU, CNT>(a, m, n0, v, bias, gate); break;
+    case EPI_GATED_RES: epi_run_t<EPI_GATED_RES, CNT>(a, m, n0, v, bias, gate); break;
+    case EPI_RES: epi_run_t<EPI_RES, CNT>(a, m, n0, v, bias, gate); break;
+    case EPI_F32_BIAS: epi_run_t<EPI_F32_BIAS, CNT>(a, m, n0, v, bias, gate); break;
+    case EPI_BIAS_GELU_R: epi_run_t<EPI_BIAS_GELU_R, CNT>(a, m, n0, v, bias, gate); break;
+    case EPI_BIAS_GELU_ERF: epi_run_t<EPI_BIAS_GELU_ERF, CNT>(a, m, n0, v, bias, gate); break;
+    default: epi_run_t<EPI_F32_OUT, CNT>(a, m, n0, v, bias, gate); break;
+  }
+}
+
+// Unsplit tiles leave TMEM in two passes. Pass 1 (one token per thread):
+// bias / activation of 16 features, written to a shared-memory staging tile
+// [token][256] (BF16 rows of 528 bytes, or F32 rows of 1040 bytes for the raw
+// accumulator epilogue; the padding keeps the 16-byte writes of a warp on
+// distinct banks). Pass 2 (8 features per thread, lanes along the feature
+// axis): residual / gate and coalesced 16-byte stores to the output rows.
+constexpr int kStageLdB = kWN + 8;  // BF16 staging row (elements)
+
+template <int EPI>
+__device__ __forceinline__ void stage16_t(const GemmArgs& a, uint8_t* stg, int row, int c,
+                                          const float* v, const float* bias) {
+  const bool hb = a.bias != nullptr;
+  if constexpr (EPI == EPI_F32_OUT) {
+    float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(stg) + row * kPartLd + c);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else {
+    float o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float acc = v[j], b = bias[j];
+      if constexpr (EPI == EPI_BIAS) {
+        float t = bf16_round(acc);
+        if (hb) t = t + b;
+        o[j] = t;
+      } else if constexpr (EPI == EPI_BIAS_GELU) {
+        o[j] = gelu_tanh(bf16_round(acc) + b);
+      } else if constexpr (EPI == EPI_BIAS_SILU) {
+        float t = bf16_round(acc);
+        if (hb) t = bf16_round(t + b);
+        o[j] = silu(t);
+      } else if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
+        // The residual is added in pass 2 to this BF16-exact linear output.
+        float t = bf16_round(acc);
+        if (hb) t = bf16_round(t + b);
+        o[j] = t;
+      } else if constexpr (EPI == EPI_F32_BIAS) {
+        o[j] = acc + b;
+      } else if constexpr (EPI == EPI_BIAS_GELU_R) {
+        float t = bf16_round(acc);
+        if (hb) t = bf16_round(t + b);
+        o[j] = gelu_tanh(t);
+      } else {  // EPI_BIAS_GELU_ERF
+        float t = bf16_round(acc);
+        if (hb) t = bf16_round(t + b);
+        o[j] = gelu_erf(t);
+      }
+    }
+    uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(stg) + row * kStageLdB + c);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(o[q * 8 + 2 * j], o[q * 8 + 2 * j + 1]);
+        w[j] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      d[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+__device__ __forceinline__ void stage16(const GemmArgs& a, uint8_t* stg, int row, int c,
+                                        const float* v, const float* bias) {
+  switch (a.epilogue) {
+    case EPI_BIAS: stage16_t<EPI_BIAS>(a, stg, row, c, v, bias); break;
+    case EPI_BIAS_GELU: stage16_t<EPI_BIAS_GELU>(a, stg, row, c, v, bias); break;
+    case EPI_BIAS_SILU: stage16_t<EPI_BIAS_SILU>(a, stg, row, c, v, bias); break;
+    case EPI_GATED_RES: stage16_t<EPI_GATED_RES>(a, stg, row, c, v, bias); break;
+    case EPI_RES: stage16_t<EPI_RES>(a, stg, row, c, v, bias); break;
+    case EPI_F32_BIAS: stage16_t<EPI_F32_BIAS>(a, stg, row, c, v, bias); break;
+    case EPI_BIAS_GELU_R: stage16_t<EPI_BIAS_GELU_R>(a, stg, row, c, v, bias); break;
+    case EPI_BIAS_GELU_ERF: stage16_t<EPI_BIAS_GELU_ERF>(a, stg, row, c, v, bias); break;
+    default: stage16_t<EPI_F32_OUT>(a, stg, row, c, v, bias); break;
+  }
+}
+
+// Pass 2 over rows x (256 / 8) items, 8 consecutive features each.
+template <int EPI>
+__device__ __forceinline__ void copy_out_t(const GemmArgs& a, const uint8_t* stg, int rows,
+                                           int m_base, int n_base, const float* gate, int t0,
+                                           int nthreads) {
+  const int items = rows * (kWN / 8);
+  for (int it = t0; it < items; it += nthreads) {
+    const int r = it / (kWN / 8), g = it % (kWN / 8);
+    const int n0 = n_base + g * 8;
+    if (n0 >= a.n) continue;
+    const long long m = m_base + r;
+    if constexpr (EPI == EPI_F32_OUT) {
+      const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(stg) +
+                                                          r * kPartLd + g * 8);
+      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + m * a.ldo + n0);
+      dst[0] = src[0];
+      dst[1] = src[1];
+    } else {
+      uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(stg) +
+                                                r * kStageLdB + g * 8);
+      if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
+        const uint4 rv = *reinterpret_cast<const uint4*>(a.residual + m * a.ldr + n0);
+        uint32_t tw[4] = {u.x, u.y, u.z, u.w};
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float t0v = __uint_as_float(tw[j] << 16), t1v = __uint_as_float(tw[j] & 0xFFFF0000u);
+          const float r0v = __uint_as_float(rw[j] << 16), r1v = __uint_as_float(rw[j] & 0xFFFF0000u);
+          float o0, o1;
+          if constexpr (EPI == EPI_GATED_RES) {
+            o0 = fmaf(t0v, gate[g * 8 + 2 * j], r0v);
+            o1 = fmaf(t1v, gate[g * 8 + 2 * j + 1], r1v);
+          } else {
+            o0 = r0v + t0v;
+            o1 = r1v + t1v;
+          }
+          const __nv_bfloat162 h = __floats2bfloat162_rn(o0, o1);
+          tw[j] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        u = make_uint4(tw[0], tw[1], tw[2], tw[3]);
+      }
+      *reinterpret_cast<uint4*>(static_cast<bf16*>(a.out) + m * a.ldo + n0) = u;
+    }
+  }
+}
+
+__device__ __forceinline__ void copy_out(const GemmArgs& a, const uint8_t* stg, int rows,
+                                         int m_base, int n_base, const float* gate, int t0,
+                                         int nthreads) {
+  switch (a.epilogue) {
+    case EPI_GATED_RES:
+      copy_out_t<EPI_GATED_RES>(a, stg, rows, m_base, n_base, gate, t0, nthreads);
+      break;
+    case EPI_RES: copy_out_t<EPI_RES>(a, stg, rows, m_base, n_base, gate, t0, nthreads); break;
+    case EPI_F32_OUT:
+      copy_out_t<EPI_F32_OUT>(a, stg, rows, m_base, n_base, gate, t0, nthreads);
+      break;
+    default: copy_out_t<EPI_BIAS>(a, stg, rows, m_base, n_base, gate, t0, nthreads); break;
+  }
+}
+
+// CTA x = (tile, split) with the split index fastest (one cluster = the splits
+// of one output tile) and the token tile next, so the CTAs that share a weight
+// tile run side by side and the weight tile is read from HBM once.
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
+                   const __grid_constant__ CUtensorMap tm_x,
+                   const __grid_constant__ GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int S = args.stages;
+  const uint32_t a_bytes = static_cast<uint32_t>(args.a_rows) * kBK * 2;
+  // Token stages first: a UMMA reads 128 token rows from every stage, so the
+  // rows past a short tile must land in (unused) shared memory that follows.
   uint8_t* smem_a = smem;
-  uint8_t* smem_b = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_b + C::STAGES * C::B_BYTES);
-  uint64_t* empty = full + C::STAGES;
-  uint64_t* accum = empty + C::STAGES;
+  uint8_t* smem_w = smem + S * a_bytes;
+  uint8_t* tail = smem_w + S * kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* empty = full + S;
+  uint64_t* accum = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  float* bias_s = reinterpret_cast<float*>(tail + 256);
+  float* gate_s = bias_s + kWN;
   float* partial = reinterpret_cast<float*>(smem);  // reuses the stages after the mainloop
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
   const int split = blockIdx.x % args.splits;
   const int tile = blockIdx.x / args.splits;
   const int tile_m = tile % args.tiles_m;
@@ -143,12 +337,16 @@ __global__ void __launch_bounds__(kThreads, Cfg<BT>::MIN_BLOCKS)
   const int kb1 =
       static_cast<int>((static_cast<long long>(split + 1) * args.num_kb) / args.splits);
   const int nkb = kb1 - kb0;
-  const bool cluster_mode = args.splits > 1 && args.split_mode == SPLIT_CLUSTER;
+  const int m_base = tile_m * kTM;
+  const int rows = args.m - m_base < kTM ? args.m - m_base : kTM;  // valid token rows
+  const int n_base = tile_n * kWN;
+  const bool cluster_mode = args.splits > 1 && args.split_mode != SPLIT_WORKSPACE;
+  const bool global_xchg = args.split_mode == SPLIT_CLUSTER_GLOBAL;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tm_w);
     prefetch_tensormap(&tm_x);
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -157,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BT>::MIN_BLOCKS)
     fence_proxy_async_smem();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -169,53 +367,62 @@ __global__ void __launch_bounds__(kThreads, Cfg<BT>::MIN_BLOCKS)
   griddep_launch_dependents();
 
   bool ok = true;
-  const int q = warp & 3;
-  const int row = q * 32 + lane;
-  const int n = tile_n * kBN + row;
-  const bool n_ok = n < args.n;
-  const int m_base = tile_m * BT;
-  float bias_v = 0.0f, gate_v = 0.0f;
-
   if (warp == 0) {
     if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_w = WAM_GEMM_WEIGHT_EVICT_FIRST ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_x = policy_evict_last();
-      const int pre = nkb < C::STAGES ? nkb : C::STAGES;
-      // Weights never depend on the preceding kernel: start streaming them
-      // before waiting for it (programmatic dependent launch).
-      for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-        tma_load_2d(smem_a + i * C::A_BYTES, &tm_w, &full[i], (kb0 + i) * kBK, tile_n * kBN, pol_w);
+      const uint32_t stage_tx = a_bytes + kBBytes;
+      const bf16* w_tiles =
+          args.w_tiled ? args.w_tiled + static_cast<size_t>(tile_n) * args.num_kb * (kWN * kBK)
+                       : nullptr;
+      auto load_w = [&](int stage, int kb) {
+        if (w_tiles)
+          bulk_load(smem_w + stage * kBBytes, w_tiles + static_cast<size_t>(kb) * (kWN * kBK),
+                    kBBytes, &full[stage], pol_w);
+        else
+          tma_load_2d(smem_w + stage * kBBytes, &tm_w, &full[stage], kb * kBK, n_base, pol_w);
+      };
+      const int pre = nkb < S ? nkb : S;
+      // Weights never depend on the preceding kernel: the first two stages'
+      // weight copies start before waiting for it (programmatic dependent
+      // launch). The copies of one SM complete roughly in issue order, so the
+      // remaining first-round copies alternate token / weight by stage.
+      const int pre_w = pre < 2 ? pre : 2;
+      for (int i = 0; i < pre_w; ++i) {
+        mbar_arrive_expect_tx(&full[i], stage_tx);
+        load_w(i, kb0 + i);
       }
       griddep_wait();
-      for (int i = 0; i < pre; ++i)
-        tma_load_2d(smem_b + i * C::B_BYTES, &tm_x, &full[i], (kb0 + i) * kBK, tile_m * BT, pol_x);
+      for (int i = 0; i < pre; ++i) {
+        if (i >= pre_w) mbar_arrive_expect_tx(&full[i], stage_tx);
+        tma_load_2d(smem_a + i * a_bytes, &tm_x, &full[i], (kb0 + i) * kBK, m_base, pol_x);
+        if (i >= pre_w) load_w(i, kb0 + i);
+      }
       for (int i = pre; i < nkb; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1)) {
           atomicCAS(args.error, 0u, static_cast<unsigned>(kErrProducerTimeout));
           break;
         }
-        mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-        const int kc = (kb0 + i) * kBK;
-        tma_load_2d(smem_a + s * C::A_BYTES, &tm_w, &full[s], kc, tile_n * kBN, pol_w);
-        tma_load_2d(smem_b + s * C::B_BYTES, &tm_x, &full[s], kc, tile_m * BT, pol_x);
+        mbar_arrive_expect_tx(&full[s], stage_tx);
+        load_w(s, kb0 + i);
+        tma_load_2d(smem_a + s * a_bytes, &tm_x, &full[s], (kb0 + i) * kBK, m_base, pol_x);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kBN, BT);
+      constexpr uint32_t idesc = umma_idesc_bf16(kTM, kWN);
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
         if (!mbar_wait(&full[s], ph)) {
           atomicCAS(args.error, 0u, static_cast<unsigned>(kErrMmaTimeout));
           break;
         }
         tc_fence_after();
-        const uint64_t da = sw128_kmajor_desc(smem_u32(smem_a + s * C::A_BYTES));
-        const uint64_t db = sw128_kmajor_desc(smem_u32(smem_b + s * C::B_BYTES));
+        const uint64_t da = sw128_kmajor_desc(smem_u32(smem_a + s * a_bytes));
+        const uint64_t db = sw128_kmajor_desc(smem_u32(smem_w + s * kBBytes));
 #pragma unroll
         for (int k = 0; k < kBK / 16; ++k) {
           // +32 bytes along K inside the swizzle row = +2 in the 16-byte address field.
@@ -226,115 +433,217 @@ __global__ void __launch_bounds__(kThreads, Cfg<BT>::MIN_BLOCKS)
       umma_commit(accum);
     }
   } else {
-    // Epilogue warps 2..5; the TMEM lane quadrant is fixed by warp % 4.
+    // Epilogue warps 2..5. Per-feature bias / gate of this tile go to shared
+    // memory while the mainloop runs.
     griddep_wait();  // residual / gate / outputs are touched only after the preceding kernel
-    bias_v = (args.bias && n_ok) ? __bfloat162float(args.bias[n]) : 0.0f;
-    gate_v = (args.gate && n_ok) ? args.gate[n] : 0.0f;
+    const int et = threadIdx.x - 64;
+    for (int j = et; j < kWN; j += 128) {
+      const int n = n_base + j;
+      bias_s[j] = (args.bias && n < args.n) ? __bfloat162float(args.bias[n]) : 0.0f;
+      gate_s[j] = (args.gate && n < args.n) ? args.gate[n] : 0.0f;
+    }
+    named_bar_sync(1, 128);
     ok = mbar_wait(accum, 0);
     if (!ok) atomicCAS(args.error, 0u, static_cast<unsigned>(kErrEpilogueTimeout));
     tc_fence_after();
+    const int q = warp & 3;  // TMEM lane quadrant of this warp
+    const int row = q * 32 + lane;
+    const bool warp_rows = q * 32 < rows;  // warp-uniform: tcgen05.ld is warp-collective
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     if (args.splits == 1) {
-#pragma unroll 1
-      for (int c = 0; c < BT; c += 16) {
-        uint32_t r[16];
-        tmem_ld_x16(taddr + c, r);
+      uint8_t* stg = smem;  // the stages are free once the accumulator is complete
+      if (warp_rows) {
+        // The TMEM load of the next 16 columns is in flight while this chunk
+        // is staged.
+        const bool st = row < rows;
+        uint32_t r0[16], r1[16];
+        tmem_ld_x16(taddr, r0);
         tmem_ld_wait();
-        if (ok && n_ok) {
+#pragma unroll 1
+        for (int c = 0; c < kWN; c += 32) {
+          tmem_ld_x16(taddr + c + 16, r1);
+          if (st) stage16(args, stg, row, c, reinterpret_cast<const float*>(r0), bias_s + c);
+          tmem_ld_wait();
+          if (c + 32 < kWN) tmem_ld_x16(taddr + c + 32, r0);
+          if (st)
+            stage16(args, stg, row, c + 16, reinterpret_cast<const float*>(r1), bias_s + c + 16);
+          tmem_ld_wait();
+        }
+      }
+      named_bar_sync(1, 128);
+      if (ok) copy_out(args, stg, rows, m_base, n_base, gate_s, et, 128);
+    } else if (cluster_mode && global_xchg) {
+      // Partial tile straight from TMEM to the workspace as
+      // [split][16-feature chunk][token][16]: a warp writes 2 KB contiguous.
+      const size_t tile_floats = static_cast<size_t>(args.a_rows) * kWN;
+      float* ws = args.workspace + (static_cast<size_t>(tile) * args.splits + split) * tile_floats;
+      if (warp_rows) {
+        const bool st = row < rows;
+        uint32_t r0[16], r1[16];
+        tmem_ld_x16(taddr, r0);
+        tmem_ld_wait();
+#pragma unroll 1
+        for (int c = 0; c < kWN; c += 32) {
+          tmem_ld_x16(taddr + c + 16, r1);
+          if (st) {
+            float4* d = reinterpret_cast<float4*>(ws + (static_cast<size_t>(c / 16) * args.a_rows + row) * 16);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = m_base + c + j;
-            if (m < args.m) store_out(args, m, n, __uint_as_float(r[j]), bias_v, gate_v);
+            for (int j = 0; j < 4; ++j)
+              d[j] = make_float4(__uint_as_float(r0[4 * j]), __uint_as_float(r0[4 * j + 1]),
+                                 __uint_as_float(r0[4 * j + 2]), __uint_as_float(r0[4 * j + 3]));
           }
+          tmem_ld_wait();
+          if (c + 32 < kWN) tmem_ld_x16(taddr + c + 32, r0);
+          if (st) {
+            float4* d = reinterpret_cast<float4*>(ws + (static_cast<size_t>(c / 16 + 1) * args.a_rows + row) * 16);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              d[j] = make_float4(__uint_as_float(r1[4 * j]), __uint_as_float(r1[4 * j + 1]),
+                                 __uint_as_float(r1[4 * j + 2]), __uint_as_float(r1[4 * j + 3]));
+          }
+          tmem_ld_wait();
         }
       }
     } else if (cluster_mode) {
-      // Stage this split's F32 partial tile [column][row] in shared memory.
+      // Stage this split's F32 partial tile [token][feature] in shared memory.
+      if (warp_rows) {
 #pragma unroll 1
-      for (int c = 0; c < BT; c += 16) {
-        uint32_t r[16];
-        tmem_ld_x16(taddr + c, r);
-        tmem_ld_wait();
+        for (int c = 0; c < kWN; c += 16) {
+          uint32_t r[16];
+          tmem_ld_x16(taddr + c, r);
+          tmem_ld_wait();
+          if (row < rows) {
+            float4* dst = reinterpret_cast<float4*>(partial + row * kPartLd + c);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) partial[(c + j) * kBN + row] = __uint_as_float(r[j]);
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          }
+        }
       }
     } else {
       // Workspace mode: partial tile to global memory; the last CTA of the tile
       // to arrive reduces all partials in split order and runs the epilogue.
-      const int tile_id = tile;
-      float* ws_tile = args.workspace + static_cast<size_t>(tile_id) * args.splits * BT * kBN;
-      float* ws = ws_tile + static_cast<size_t>(split) * BT * kBN;
+      const size_t tile_floats = static_cast<size_t>(args.a_rows) * kWN;
+      float* ws_tile = args.workspace + static_cast<size_t>(tile) * args.splits * tile_floats;
+      float* ws = ws_tile + static_cast<size_t>(split) * tile_floats;
+      if (warp_rows) {
 #pragma unroll 1
-      for (int c = 0; c < BT; c += 16) {
-        uint32_t r[16];
-        tmem_ld_x16(taddr + c, r);
-        tmem_ld_wait();
+        for (int c = 0; c < kWN; c += 16) {
+          uint32_t r[16];
+          tmem_ld_x16(taddr + c, r);
+          tmem_ld_wait();
+          if (row < rows) {
+            float4* dst = reinterpret_cast<float4*>(ws + row * kWN + c);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) ws[(c + j) * kBN + row] = __uint_as_float(r[j]);
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          }
+        }
       }
       __threadfence();
       named_bar_sync(1, 128);
-      if (threadIdx.x == 64) {
-        const unsigned prev = atomicAdd(&args.counters[tile_id], 1u);
+      if (et == 0) {
+        const unsigned prev = atomicAdd(&args.counters[tile], 1u);
         *last_flag = (prev == static_cast<unsigned>(args.splits - 1)) ? 1 : 0;
       }
       named_bar_sync(1, 128);
       if (*last_flag) {
         __threadfence();
-        if (ok && n_ok) {
+        const int items = rows * (kWN / 8);
+        for (int it = et; it < items; it += 128) {
+          const int rr = it / (kWN / 8), g = it % (kWN / 8);
+          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-          for (int c0 = 0; c0 < BT; c0 += 8) {
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-            for (int s = 0; s < args.splits; ++s) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j)
-                acc[j] += __ldcg(ws_tile + (static_cast<size_t>(s) * BT + c0 + j) * kBN + row);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int m = m_base + c0 + j;
-              if (m < args.m) store_out(args, m, n, acc[j], bias_v, gate_v);
-            }
+          for (int sp = 0; sp < args.splits; ++sp) {
+            const float4* src = reinterpret_cast<const float4*>(
+                ws_tile + sp * tile_floats + static_cast<size_t>(rr) * kWN + g * 8);
+            const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
+            acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
+            acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
           }
+          if (ok) epi_run<8>(args, m_base + rr, n_base + g * 8, acc, bias_s + g * 8, gate_s + g * 8);
         }
-        if (threadIdx.x == 64) args.counters[tile_id] = 0u;
+        if (et == 0) args.counters[tile] = 0u;
       }
     }
   }
 
   __syncwarp();
-  if (cluster_mode) {
+  if (cluster_mode && global_xchg) {
+    // Every split's partial tile is in the workspace: each CTA reduces a
+    // slice of (16-feature chunk, token) items over all splits, in split
+    // order; consecutive threads read consecutive 64-byte token rows.
+    cluster_sync_all();
+    if (warp >= 2) {
+      const int et = threadIdx.x - 64;
+      const int sp_n = args.splits;
+      const int items = rows * (kWN / 16);
+      const int i0 = static_cast<int>((static_cast<long long>(split) * items) / sp_n);
+      const int i1 = static_cast<int>((static_cast<long long>(split + 1) * items) / sp_n);
+      const size_t tile_floats = static_cast<size_t>(args.a_rows) * kWN;
+      const float* ws_tile = args.workspace + static_cast<size_t>(tile) * sp_n * tile_floats;
+      for (int it = i0 + et; it < i1; it += 128) {
+        const int c = it / rows, rr = it % rows;
+        const float* src0 = ws_tile + (static_cast<size_t>(c) * args.a_rows + rr) * 16;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float4 x[8][2];
+#pragma unroll
+          for (int p = 0; p < 8; ++p) {
+            if (p < sp_n) {
+              const float4* src = reinterpret_cast<const float4*>(src0 + p * tile_floats + h * 8);
+              x[p][0] = __ldcg(src);
+              x[p][1] = __ldcg(src + 1);
+            }
+          }
+          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int p = 0; p < 8; ++p) {
+            if (p < sp_n) {
+              acc[0] += x[p][0].x; acc[1] += x[p][0].y; acc[2] += x[p][0].z; acc[3] += x[p][0].w;
+              acc[4] += x[p][1].x; acc[5] += x[p][1].y; acc[6] += x[p][1].z; acc[7] += x[p][1].w;
+            }
+          }
+          const int f = c * 16 + h * 8;
+          if (ok) epi_run<8>(args, m_base + rr, n_base + f, acc, bias_s + f, gate_s + f);
+        }
+      }
+    }
+  } else if (cluster_mode) {
     // All partial tiles of this output tile are in the cluster's shared memory.
     cluster_sync_all();
     if (warp >= 2) {
-      const int S = args.splits;
-      const int cols = (BT + S - 1) / S;
-      const int c0 = split * cols;
-      const int c1 = c0 + cols < BT ? c0 + cols : BT;
-      const uint32_t base = smem_u32(partial) + static_cast<uint32_t>(row) * 4u;
-      uint32_t peer[8];
-#pragma unroll
-      for (int p = 0; p < 8; ++p) peer[p] = mapa_shared(base, p < S ? p : 0);
-#pragma unroll 1
-      for (int c = c0; c < c1; c += 4) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int et = threadIdx.x - 64;
+      const int sp_n = args.splits;
+      const int items = rows * (kWN / 8);
+      const int i0 = static_cast<int>((static_cast<long long>(split) * items) / sp_n);
+      const int i1 = static_cast<int>((static_cast<long long>(split + 1) * items) / sp_n);
+      const uint32_t base = smem_u32(partial);
+      for (int it = i0 + et; it < i1; it += 128) {
+        const int rr = it / (kWN / 8), g = it % (kWN / 8);
+        const uint32_t off = static_cast<uint32_t>(rr * kPartLd + g * 8) * 4u;
+        // All peers' loads are issued before any is summed (each DSMEM load
+        // is a round trip); the sum runs in split order.
+        float4 x[8][2];
 #pragma unroll
         for (int p = 0; p < 8; ++p) {
-          if (p < S) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              if (c + j < c1)
-                acc[j] += ld_shared_cluster_f32(peer[p] + static_cast<uint32_t>((c + j) * kBN) * 4u);
+          if (p < sp_n) {
+            const uint32_t pa = mapa_shared(base + off, static_cast<uint32_t>(p));
+            x[p][0] = ld_shared_cluster_f32x4(pa);
+            x[p][1] = ld_shared_cluster_f32x4(pa + 16);
           }
         }
-        if (ok && n_ok) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int m = m_base + c + j;
-            if (c + j < c1 && m < args.m) store_out(args, m, n, acc[j], bias_v, gate_v);
+        for (int p = 0; p < 8; ++p) {
+          if (p < sp_n) {
+            acc[0] += x[p][0].x; acc[1] += x[p][0].y; acc[2] += x[p][0].z; acc[3] += x[p][0].w;
+            acc[4] += x[p][1].x; acc[5] += x[p][1].y; acc[6] += x[p][1].z; acc[7] += x[p][1].w;
           }
         }
+        if (ok) epi_run<8>(args, m_base + rr, n_base + g * 8, acc, bias_s + g * 8, gate_s + g * 8);
       }
     }
     // No CTA leaves while a peer may still read its shared memory.
@@ -345,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BT>::MIN_BLOCKS)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -384,43 +693,24 @@ bool encode_bf16_2d(CUtensorMap* map, const void* base, int cols, int rows, int 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Token tile: the largest tile for up to 256 tokens; beyond that the tile that
-// minimises (waves x resident CTAs per SM x tile width), i.e. the per-SM
-// tensor work of the slowest SM, preferring larger tiles on ties.
-int pick_bt(int m, int n, int num_sms) {
-  static const int small[] = {16, 32, 48, 64, 96, 128, 192, 256};
-  if (m <= 256) {
-    for (int o : small)
-      if (o >= m) return o;
-  }
-  static const int big[] = {256, 192, 128, 96};
-  const int tiles_n = (n + 127) / 128;
-  int best = 256;
-  long long best_cost = -1;
-  for (int bt : big) {
-    const long long tiles = static_cast<long long>((m + bt - 1) / bt) * tiles_n;
-    const long long waves = (tiles + num_sms - 1) / num_sms;
-    const long long cost = waves * bt;
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
-      best = bt;
-    }
-  }
-  return best;
-}
+// Resident CTA slots for a split-K cluster size s (index s = 1..8): clusters
+// are placed inside one GPC, so s-wide clusters of one-CTA-per-SM kernels fit
+// floor(SMs per GPC / s) times per GPC. Filled by gemm_init from
+// cudaOccupancyMaxActiveClusters.
+int g_cluster_slots[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
 
-// Split-K factor in {1, 2, 4, 8} (cluster sizes). When the output tiles fill
-// less than ~3/4 of the resident CTA slots (two per SM for token tiles <= 64),
-// the K range is split as far as the slots allow, keeping >= 4 k-blocks
-// (256 of K) per split.
-int pick_splits(int tiles, int nkb, int num_sms, int bt) {
-  // Large token tiles are tensor bound: splitting K only adds partial traffic.
-  if (bt > 64) return 1;
-  const int slots = num_sms * 2;
-  if (tiles * 4 >= slots * 3) return 1;
+// Split-K factor (1..8 = cluster size). Output tiles that fill less than
+// three quarters of the SMs split K as far as one wave of clusters allows
+// (>= 2 k-blocks per split): the batch-1 denoise GEMMs (48 tokens, 12..56
+// tiles of 256 features) stream their weights from 96..144 SMs instead of
+// 12..56.
+int pick_splits(int tiles, int nkb, int num_sms) {
+  if (tiles * 4 >= num_sms * 3) return 1;
   int best = 1;
-  for (int s = 2; s <= 8; s *= 2)
-    if (tiles * s <= slots && nkb / s >= 4) best = s;
+  for (int s = 2; s <= 8; ++s) {
+    const int slots = g_cluster_slots[s] > 0 ? g_cluster_slots[s] : num_sms;
+    if (tiles * s <= slots && nkb / s >= 2) best = s;
+  }
   return best;
 }
 
@@ -429,93 +719,91 @@ bool g_pdl = [] {
   return !(v && *v && *v != '0');
 }();
 
-template <int BT>
-cudaError_t set_attr_bt() {
-  return cudaFuncSetAttribute(gemm_bf16_tc_kernel<BT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              Cfg<BT>::SMEM);
-}
-
-template <int BT>
-cudaError_t launch_bt(const GemmOp& op, cudaStream_t stream) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(op.grid, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = Cfg<BT>::SMEM;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[na].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
-  ++na;
-  if (op.args.splits > 1 && op.args.split_mode == SPLIT_CLUSTER) {
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = op.args.splits;
-    attr[na].val.clusterDim.y = 1;
-    attr[na].val.clusterDim.z = 1;
-    ++na;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<BT>, op.tm_w, op.tm_x, op.args);
-}
-
-int smem_for_bt(int bt) {
-  switch (bt) {
-    case 16: return Cfg<16>::SMEM;
-    case 32: return Cfg<32>::SMEM;
-    case 48: return Cfg<48>::SMEM;
-    case 64: return Cfg<64>::SMEM;
-    case 96: return Cfg<96>::SMEM;
-    case 128: return Cfg<128>::SMEM;
-    case 192: return Cfg<192>::SMEM;
-    default: return Cfg<256>::SMEM;
+// One thread per 16-byte chunk: chunk c of row r of tile (nt, kb) goes to
+// chunk c ^ (r & 7) of that row in the tile's contiguous 32 KB block.
+__global__ void retile_weights_kernel(const bf16* __restrict__ src, bf16* __restrict__ dst, int n,
+                                      int k) {
+  griddep_wait();
+  const int kbs = k / kBK;
+  const long long total = static_cast<long long>(n) * (k / 8);
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / (k / 8));
+    const int cg = static_cast<int>(i % (k / 8));  // 8-element chunk along k
+    const int kb = cg >> 3, c = cg & 7;
+    const int nt = row / kWN, r = row % kWN;
+    const size_t tile = (static_cast<size_t>(nt) * kbs + kb) * (kWN * kBK);
+    const uint4 v = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(row) * k + cg * 8);
+    *reinterpret_cast<uint4*>(dst + tile + r * kBK + ((c ^ (r & 7)) * 8)) = v;
   }
 }
 
 }  // namespace
 
+int gemm_weight_tile_rows() { return kWN; }
+
+void launch_retile_weights(const bf16* src, bf16* dst, int n, int k, cudaStream_t s) {
+  const long long total = static_cast<long long>(n) * (k / 8);
+  long long grid = (total + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  retile_weights_kernel<<<static_cast<int>(grid), 256, 0, s>>>(src, dst, n, k);
+}
+
 size_t gemm_scratch_floats(int m, int n, int k, int num_sms, int force_splits, int* tiles_out) {
-  const int bt = pick_bt(m, n, num_sms);
-  const int tiles = ((m + bt - 1) / bt) * ((n + kBN - 1) / kBN);
+  const int tiles = ((m + kTM - 1) / kTM) * ((n + kWN - 1) / kWN);
   const int nkb = k / kBK;
-  const int splits = force_splits > 0 ? force_splits : pick_splits(tiles, nkb, num_sms, bt);
+  const int splits = force_splits > 0 ? force_splits : pick_splits(tiles, nkb, num_sms);
   if (tiles_out) *tiles_out = tiles;
   if (splits <= 1) return 0;
-  return static_cast<size_t>(tiles) * splits * bt * kBN;
+  return static_cast<size_t>(tiles) * splits * a_rows_for(m) * kWN;
 }
 
 const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, int n, int k,
                       int epilogue, const bf16* bias, const float* gate, const bf16* residual,
                       int ldr, void* out, int ldo, const GemmScratch& scratch, int num_sms,
-                      int force_splits) {
+                      int force_splits, bool w_tiled) {
   if (m <= 0 || n <= 0 || k <= 0) return "gemm: empty shape";
+  if (w_tiled && (n % kWN != 0 || reinterpret_cast<uintptr_t>(w) % 16 != 0))
+    return "gemm: re-tiled weights need N a multiple of 256 and a 16-byte aligned pointer";
   if (k % kBK != 0) return "gemm: K must be a multiple of 64";
+  if (n % 16 != 0) return "gemm: N must be a multiple of 16";
   if (ldx % 8 != 0 || ldx < k) return "gemm: activation row stride must be >= K and a multiple of 8";
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
     return "gemm: operands must be 16-byte aligned";
   if ((epilogue == EPI_GATED_RES && (!gate || !residual)) || (epilogue == EPI_RES && !residual))
     return "gemm: residual epilogue needs its inputs";
   if (epilogue < 0 || epilogue > EPI_BIAS_GELU_ERF) return "gemm: unknown epilogue";
+  const int out_align = epilogue == EPI_F32_OUT ? 4 : 8;
+  if (ldo < n || ldo % out_align != 0 || (reinterpret_cast<uintptr_t>(out) & 15))
+    return "gemm: output must be 16-byte aligned with a row stride >= N in 16-byte units";
+  if ((epilogue == EPI_GATED_RES || epilogue == EPI_RES) &&
+      (ldr < n || ldr % 8 != 0 || (reinterpret_cast<uintptr_t>(residual) & 15)))
+    return "gemm: residual must be 16-byte aligned with a row stride >= N in 16-byte units";
   std::memset(op, 0, sizeof(*op));
-  const int bt = pick_bt(m, n, num_sms);
-  const int tiles_m = (m + bt - 1) / bt;
-  const int tiles_n = (n + kBN - 1) / kBN;
+  const int a_rows = a_rows_for(m);
+  const int tiles_m = (m + kTM - 1) / kTM;
+  const int tiles_n = (n + kWN - 1) / kWN;
   const int nkb = k / kBK;
-  int splits = force_splits > 0 ? force_splits : pick_splits(tiles_m * tiles_n, nkb, num_sms, bt);
+  int splits = force_splits > 0 ? force_splits : pick_splits(tiles_m * tiles_n, nkb, num_sms);
   if (splits > nkb) splits = nkb;
-  // Split-K partials are reduced through distributed shared memory inside a
-  // thread-block cluster unless the caller hands in a global workspace.
-  const int mode = scratch.workspace ? SPLIT_WORKSPACE : SPLIT_CLUSTER;
-  if (splits > 1 && mode == SPLIT_CLUSTER && splits != 2 && splits != 4 && splits != 8)
-    return "gemm: cluster split-K needs 2, 4 or 8 splits (or a workspace)";
-  if (splits > 1 && mode == SPLIT_WORKSPACE) {
-    const size_t need = static_cast<size_t>(tiles_m) * tiles_n * splits * bt * kBN;
-    if (need > scratch.workspace_floats || !scratch.counters ||
-        tiles_m * tiles_n > scratch.counter_slots)
+  // Split-K partials: with a workspace, the splits of a tile (a cluster of up
+  // to 8 CTAs) exchange them through global memory / L2; without one, through
+  // distributed shared memory; more than 8 splits need a workspace and tile
+  // counters (the last CTA of a tile reduces).
+  int mode = SPLIT_CLUSTER;
+  if (scratch.workspace) mode = splits <= 8 ? SPLIT_CLUSTER_GLOBAL : SPLIT_WORKSPACE;
+  if (splits > 8 && mode == SPLIT_CLUSTER)
+    return "gemm: cluster split-K takes at most 8 splits (or a workspace)";
+  if (splits > 1 && mode != SPLIT_CLUSTER) {
+    const size_t need = static_cast<size_t>(tiles_m) * tiles_n * splits * a_rows * kWN;
+    if (need > scratch.workspace_floats ||
+        (mode == SPLIT_WORKSPACE && (!scratch.counters || tiles_m * tiles_n > scratch.counter_slots)))
       return "gemm: split-K scratch too small";
   }
-  if (!encode_bf16_2d(&op->tm_w, w, k, n, k, kBN)) return "gemm: weight tensor map encode failed";
-  if (!encode_bf16_2d(&op->tm_x, x, k, m, ldx, bt)) return "gemm: activation tensor map encode failed";
+  if (!w_tiled && !encode_bf16_2d(&op->tm_w, w, k, n, k, kWN))
+    return "gemm: weight tensor map encode failed";
+  if (!encode_bf16_2d(&op->tm_x, x, k, m, ldx, a_rows))
+    return "gemm: activation tensor map encode failed";
   GemmArgs& a = op->args;
   a.m = m;
   a.n = n;
@@ -523,6 +811,9 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   a.num_kb = nkb;
   a.splits = splits;
   a.split_mode = mode;
+  a.a_rows = a_rows;
+  a.stages = stages_for(a_rows);
+  a.w_tiled = w_tiled ? w : nullptr;
   a.tiles_m = tiles_m;
   a.tiles_n = tiles_n;
   a.epilogue = epilogue;
@@ -535,45 +826,69 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   a.workspace = scratch.workspace;
   a.counters = scratch.counters;
   a.error = scratch.error;
-  op->bt = bt;
   op->grid = tiles_m * tiles_n * splits;
-  op->smem_bytes = smem_for_bt(bt);
+  op->smem_bytes = smem_for(a_rows);
   return nullptr;
 }
 
 cudaError_t gemm_init(int device) {
-  // Opt-in shared memory per instantiation, once per device, before any
-  // launch (so that launches can be captured into CUDA graphs).
+  // Opt-in shared memory once per device, before any launch (so that launches
+  // can be captured into CUDA graphs), and the cluster occupancy per split.
   static std::mutex mu;
   static std::vector<int> done;
   std::lock_guard<std::mutex> lock(mu);
   for (int d : done)
     if (d == device) return cudaSuccess;
-  cudaError_t e;
-  if ((e = set_attr_bt<16>()) != cudaSuccess) return e;
-  if ((e = set_attr_bt<32>()) != cudaSuccess) return e;
-  if ((e = set_attr_bt<48>()) != cudaSuccess) return e;
-  if ((e = set_attr_bt<64>()) != cudaSuccess) return e;
-  if ((e = set_attr_bt<96>()) != cudaSuccess) return e;
-  if ((e = set_attr_bt<128>()) != cudaSuccess) return e;
-  if ((e = set_attr_bt<192>()) != cudaSuccess) return e;
-  if ((e = set_attr_bt<256>()) != cudaSuccess) return e;
+  const int smem = kStageBudget + 1024 + kSmemTail;  // every stage count stays within the budget
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       smem);
+  if (e != cudaSuccess) return e;
+  int sms = 0;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
+    return e;
+  for (int s = 1; s <= 8; ++s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(s * sms, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = s;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_kernel, &cfg) == cudaSuccess)
+      g_cluster_slots[s] = clusters * s;
+    else
+      cudaGetLastError();
+  }
   done.push_back(device);
   return cudaSuccess;
 }
 
 cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream) {
-  switch (op.bt) {
-    case 16: return launch_bt<16>(op, stream);
-    case 32: return launch_bt<32>(op, stream);
-    case 48: return launch_bt<48>(op, stream);
-    case 64: return launch_bt<64>(op, stream);
-    case 96: return launch_bt<96>(op, stream);
-    case 128: return launch_bt<128>(op, stream);
-    case 192: return launch_bt<192>(op, stream);
-    case 256: return launch_bt<256>(op, stream);
-    default: return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(op.grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = op.smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+  ++na;
+  if (op.args.splits > 1 && op.args.split_mode != SPLIT_WORKSPACE) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = op.args.splits;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, op.tm_w, op.tm_x, op.args);
 }
 
 }  // namespace wamb

@@ -37,17 +37,22 @@ enum GemmEpilogue : int {
   EPI_BIAS_GELU_ERF = 8,  // y = bf16(gelu_erf(bf16(bf16(acc) + b)))  linear + ggml_gelu_erf (decoder)
 };
 
-// Split-K reduction: SPLIT_CLUSTER reduces the F32 partial tiles through
-// distributed shared memory inside one thread-block cluster (splits 2/4/8, no
-// global scratch); SPLIT_WORKSPACE writes them to a caller-provided global
-// workspace and the last CTA of a tile reduces them.
-enum SplitMode : int { SPLIT_CLUSTER = 0, SPLIT_WORKSPACE = 1 };
+// Split-K reduction. SPLIT_CLUSTER: the splits of a tile form a thread-block
+// cluster and reduce their F32 partial tiles through distributed shared memory
+// (no global scratch). SPLIT_CLUSTER_GLOBAL: the same cluster exchanges the
+// partial tiles through a caller-provided global workspace (L2). SPLIT_WORKSPACE
+// (more than 8 splits): partial tiles in the workspace, the last CTA of a tile
+// to arrive (tile counters) reduces them.
+enum SplitMode : int { SPLIT_CLUSTER = 0, SPLIT_WORKSPACE = 1, SPLIT_CLUSTER_GLOBAL = 2 };
 
 struct GemmArgs {
   int m, n, k;
   int num_kb;  // k / 64
   int splits;
   int split_mode;
+  int a_rows;  // token rows loaded per tile (<= 128)
+  int stages;  // pipeline stages (one weight + one token k-block each)
+  const bf16* w_tiled;  // weights re-tiled by launch_retile_weights, or null (tensor map)
   int tiles_m, tiles_n;
   int epilogue;
   const bf16* bias;      // [n] or null
@@ -56,7 +61,7 @@ struct GemmArgs {
   int ldr;
   void* out;  // bf16 [m, ldo] (float for EPI_F32_OUT)
   int ldo;
-  float* workspace;    // SPLIT_WORKSPACE: partial tiles [tile][split][BT][128]
+  float* workspace;    // SPLIT_WORKSPACE: partial tiles [tile][split][a_rows][256]
   unsigned* counters;  // SPLIT_WORKSPACE: arrival counters, one per tile, zero at rest
   unsigned* error;     // device error word
 };
@@ -73,17 +78,23 @@ struct GemmOp {
   CUtensorMap tm_w;
   CUtensorMap tm_x;
   GemmArgs args;
-  int bt = 0;
   int grid = 0;
   int smem_bytes = 0;
 };
 
 // Plans one GEMM: picks the token tile and split-K factor, encodes the TMA
-// descriptors. Returns nullptr on success or a static error message.
+// descriptors. With w_tiled the weights are in the layout written by
+// launch_retile_weights. Returns nullptr on success or a static error message.
 const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, int n, int k,
                       int epilogue, const bf16* bias, const float* gate, const bf16* residual,
                       int ldr, void* out, int ldo, const GemmScratch& scratch, int num_sms,
-                      int force_splits);
+                      int force_splits, bool w_tiled = false);
+// Re-tiles a row-major [n][k] BF16 weight (n % 256 == 0, k % 64 == 0) into
+// contiguous 32 KB tiles [n/256][k/64][256][64] with the 128-byte swizzle of
+// the UMMA operand pre-applied, so one bulk copy fetches a pipeline stage.
+void launch_retile_weights(const bf16* src, bf16* dst, int n, int k, cudaStream_t s);
+// Weight rows per re-tiled tile (256).
+int gemm_weight_tile_rows();
 cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream);
 // Sets per-kernel launch attributes on the current device (call once per
 // device before the first launch or graph capture).

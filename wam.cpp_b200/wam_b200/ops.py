@@ -38,17 +38,38 @@ class Scratch:
 _error_words = {}
 
 
+GEMM_TILED_WEIGHTS = 0x100
+
+
+class TiledWeight:
+    """A [n, k] BF16 weight re-tiled by wam_b200_op_retile_weights into
+    contiguous 16 KB UMMA tiles; `data` is the flat device buffer."""
+
+    def __init__(self, w):
+        n, k = w.shape
+        self.shape = (n, k)
+        self.device = w.device
+        self.data = torch.empty(n * k, dtype=torch.bfloat16, device=w.device)
+        w = w.contiguous()
+        rc = load().wam_b200_op_retile_weights(_ptr(w), _ptr(self.data), n, k, _stream())
+        check(rc, "wam_b200_op_retile_weights")
+
+
 def gemm(x, w, epilogue=EPI_BIAS, bias=None, gate=None, residual=None, out=None,
          scratch: Scratch | None = None, force_splits: int = 0):
     """out[m, n] = epilogue(x[m, :K] . w[n, :]) via wam_b200_op_gemm.
 
     Without `scratch`, split-K partials are reduced inside thread-block
-    clusters (splits 1/2/4/8); with it, through its global workspace."""
+    clusters (splits 1/2/4/8); with it, through its global workspace. `w` is a
+    row-major [n, k] tensor or a TiledWeight."""
     lib = load()
-    m, k = x.shape[0], w.shape[1]
-    n = w.shape[0]
+    m = x.shape[0]
+    n, k = w.shape
+    if isinstance(w, TiledWeight):
+        epilogue |= GEMM_TILED_WEIGHTS
+        w = w.data
     if out is None:
-        dt = torch.float32 if epilogue == EPI_F32_OUT else torch.bfloat16
+        dt = torch.float32 if (epilogue & 0xFF) == EPI_F32_OUT else torch.bfloat16
         out = torch.empty(m, n, dtype=dt, device=x.device)
     if scratch is None:
         err = _error_words.setdefault(x.device, torch.zeros(1, dtype=torch.int32, device=x.device))
