@@ -40,7 +40,10 @@ constexpr int kWN = 256;              // weight rows per tile (UMMA N, TMEM colu
 constexpr int kBK = 64;               // K per stage: one 128-byte swizzle row of BF16
 constexpr int kBBytes = kWN * kBK * 2;  // weight tile per stage (32 KB)
 constexpr int kThreads = 192;
-constexpr int kStageBudget = 200 * 1024;
+#ifndef WAM_GEMM_STAGE_BUDGET_KB
+#define WAM_GEMM_STAGE_BUDGET_KB 200
+#endif
+constexpr int kStageBudget = WAM_GEMM_STAGE_BUDGET_KB * 1024;
 constexpr int kMaxStages = 8;
 #ifndef WAM_GEMM_WEIGHT_EVICT_FIRST
 #define WAM_GEMM_WEIGHT_EVICT_FIRST 1

@@ -1,11 +1,13 @@
 """ctypes loader for libwam_b200.so (the engine's C ABI, include/wam_b200.h).
 
-The library is built in-tree by wam.cpp_b200/build.py. Loading fails loudly if
-it is missing: there is no fallback implementation of any entry point.
+The library is built in-tree by wam.cpp_b200/build.py (WAM_B200_LIB names
+another build of it). Loading fails loudly if it is missing: there is no
+fallback implementation of any entry point.
 """
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
 PKG_ROOT = Path(__file__).resolve().parent.parent
@@ -32,7 +34,7 @@ def load(path: Path | None = None):
     global _lib
     if _lib is not None:
         return _lib
-    p = Path(path) if path else LIB_PATH
+    p = Path(path) if path else Path(os.environ.get("WAM_B200_LIB", LIB_PATH))
     if not p.exists():
         raise RuntimeError(f"libwam_b200.so not built ({p}); run python wam.cpp_b200/build.py")
     lib = C.CDLL(str(p))
