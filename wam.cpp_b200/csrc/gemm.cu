@@ -326,6 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accum = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* ok_flag = last_flag + 1;
   float* bias_s = reinterpret_cast<float*>(tail + 256);
   float* gate_s = bias_s + kWN;
   float* partial = reinterpret_cast<float*>(smem);  // reuses the stages after the mainloop
@@ -482,31 +483,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* ws = args.workspace + (static_cast<size_t>(tile) * args.splits + split) * tile_floats;
       if (warp_rows) {
         const bool st = row < rows;
-        uint32_t r0[16], r1[16];
-        tmem_ld_x16(taddr, r0);
-        tmem_ld_wait();
 #pragma unroll 1
         for (int c = 0; c < kWN; c += 32) {
-          tmem_ld_x16(taddr + c + 16, r1);
-          if (st) {
-            float4* d = reinterpret_cast<float4*>(ws + (static_cast<size_t>(c / 16) * args.a_rows + row) * 16);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              d[j] = make_float4(__uint_as_float(r0[4 * j]), __uint_as_float(r0[4 * j + 1]),
-                                 __uint_as_float(r0[4 * j + 2]), __uint_as_float(r0[4 * j + 3]));
-          }
+          uint32_t r[32];
+          tmem_ld_x32(taddr + c, r);
           tmem_ld_wait();
-          if (c + 32 < kWN) tmem_ld_x16(taddr + c + 32, r0);
           if (st) {
-            float4* d = reinterpret_cast<float4*>(ws + (static_cast<size_t>(c / 16 + 1) * args.a_rows + row) * 16);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              d[j] = make_float4(__uint_as_float(r1[4 * j]), __uint_as_float(r1[4 * j + 1]),
-                                 __uint_as_float(r1[4 * j + 2]), __uint_as_float(r1[4 * j + 3]));
+            for (int h = 0; h < 2; ++h) {
+              float4* d = reinterpret_cast<float4*>(
+                  ws + (static_cast<size_t>(c / 16 + h) * args.a_rows + row) * 16);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                d[j] = make_float4(__uint_as_float(r[16 * h + 4 * j]), __uint_as_float(r[16 * h + 4 * j + 1]),
+                                   __uint_as_float(r[16 * h + 4 * j + 2]), __uint_as_float(r[16 * h + 4 * j + 3]));
+            }
           }
-          tmem_ld_wait();
         }
       }
+      if (threadIdx.x == 64) *ok_flag = ok ? 1 : 0;
     } else if (cluster_mode) {
       // Stage this split's F32 partial tile [token][feature] in shared memory.
       if (warp_rows) {
@@ -579,39 +574,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     // slice of (16-feature chunk, token) items over all splits, in split
     // order; consecutive threads read consecutive 64-byte token rows.
     cluster_sync_all();
-    if (warp >= 2) {
-      const int et = threadIdx.x - 64;
+    {
+      // All 192 threads: one (16-feature chunk, token, half) item each pass.
+      const bool ok_all = *ok_flag != 0;
       const int sp_n = args.splits;
-      const int items = rows * (kWN / 16);
+      const int items = rows * (kWN / 8);
       const int i0 = static_cast<int>((static_cast<long long>(split) * items) / sp_n);
       const int i1 = static_cast<int>((static_cast<long long>(split + 1) * items) / sp_n);
       const size_t tile_floats = static_cast<size_t>(args.a_rows) * kWN;
       const float* ws_tile = args.workspace + static_cast<size_t>(tile) * sp_n * tile_floats;
-      for (int it = i0 + et; it < i1; it += 128) {
-        const int c = it / rows, rr = it % rows;
-        const float* src0 = ws_tile + (static_cast<size_t>(c) * args.a_rows + rr) * 16;
+      for (int it = i0 + static_cast<int>(threadIdx.x); it < i1; it += kThreads) {
+        const int c = it / (2 * rows), rem = it % (2 * rows);
+        const int rr = rem >> 1, h = rem & 1;
+        const float* src0 = ws_tile + (static_cast<size_t>(c) * args.a_rows + rr) * 16 + h * 8;
+        float4 x[8][2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float4 x[8][2];
-#pragma unroll
-          for (int p = 0; p < 8; ++p) {
-            if (p < sp_n) {
-              const float4* src = reinterpret_cast<const float4*>(src0 + p * tile_floats + h * 8);
-              x[p][0] = __ldcg(src);
-              x[p][1] = __ldcg(src + 1);
-            }
+        for (int p = 0; p < 8; ++p) {
+          if (p < sp_n) {
+            const float4* src = reinterpret_cast<const float4*>(src0 + p * tile_floats);
+            x[p][0] = __ldcg(src);
+            x[p][1] = __ldcg(src + 1);
           }
-          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int p = 0; p < 8; ++p) {
-            if (p < sp_n) {
-              acc[0] += x[p][0].x; acc[1] += x[p][0].y; acc[2] += x[p][0].z; acc[3] += x[p][0].w;
-              acc[4] += x[p][1].x; acc[5] += x[p][1].y; acc[6] += x[p][1].z; acc[7] += x[p][1].w;
-            }
-          }
-          const int f = c * 16 + h * 8;
-          if (ok) epi_run<8>(args, m_base + rr, n_base + f, acc, bias_s + f, gate_s + f);
         }
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          if (p < sp_n) {
+            acc[0] += x[p][0].x; acc[1] += x[p][0].y; acc[2] += x[p][0].z; acc[3] += x[p][0].w;
+            acc[4] += x[p][1].x; acc[5] += x[p][1].y; acc[6] += x[p][1].z; acc[7] += x[p][1].w;
+          }
+        }
+        const int f = c * 16 + h * 8;
+        if (ok_all) epi_run<8>(args, m_base + rr, n_base + f, acc, bias_s + f, gate_s + f);
       }
     }
   } else if (cluster_mode) {
@@ -784,6 +778,11 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
     return "gemm: residual must be 16-byte aligned with a row stride >= N in 16-byte units";
   std::memset(op, 0, sizeof(*op));
   const int a_rows = a_rows_for(m);
+  // The epilogue stages a [token][feature] tile (F32 rows of kPartLd floats at
+  // most) in the pipeline stages' shared memory.
+  if (static_cast<long long>(a_rows) * kPartLd * 4 >
+      static_cast<long long>(stages_for(a_rows)) * (a_rows * kBK * 2 + kBBytes))
+    return "gemm: stage budget too small for the epilogue tile";
   const int tiles_m = (m + kTM - 1) / kTM;
   const int tiles_n = (n + kWN - 1) / kWN;
   const int nkb = k / kBK;
