@@ -222,6 +222,27 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
         l_s[row] = l_run[r];
       }
     }
+    // With a workspace, this split's rows go to L2 ([row][kOld] floats with
+    // max / sum in the last two columns) and the merge reads them from there.
+    const bool gx = a.ws != nullptr;
+    const size_t slot_floats = static_cast<size_t>(kBQ) * kOld;
+    float* ws_blk = nullptr;
+    if (gx) {
+      const size_t blk = (static_cast<size_t>(seq) * gridDim.y + head) * (gridDim.x / splits) +
+                         (q0 / kBQ);
+      ws_blk = a.ws + blk * splits * slot_floats;
+      __syncthreads();
+      float* mine = ws_blk + split * slot_floats;
+      for (int i = tid; i < kBQ * (kD / 4); i += 128) {
+        const int r = i / (kD / 4), c4 = i % (kD / 4);
+        reinterpret_cast<float4*>(mine + r * kOld)[c4] =
+            reinterpret_cast<const float4*>(o_s + r * kOld)[c4];
+      }
+      if (tid < kBQ) {
+        mine[tid * kOld + kD] = m_s[tid];
+        mine[tid * kOld + kD + 1] = l_s[tid];
+      }
+    }
     cluster_sync_all();
     // Each CTA merges kBQ / splits rows; a row's 128 dims are spread over
     // 128 / rows_per threads, each owning rows_per consecutive dims.
@@ -237,8 +258,14 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
       mv[p] = -INFINITY;
       lv[p] = 0.0f;
       if (p < splits) {
-        mv[p] = ld_shared_cluster_f32(mapa_shared(m_base + row_l * 4u, p));
-        lv[p] = ld_shared_cluster_f32(mapa_shared(l_base + row_l * 4u, p));
+        if (gx) {
+          const float* st = ws_blk + p * slot_floats + row_l * kOld + kD;
+          mv[p] = __ldcg(st);
+          lv[p] = __ldcg(st + 1);
+        } else {
+          mv[p] = ld_shared_cluster_f32(mapa_shared(m_base + row_l * 4u, p));
+          lv[p] = ld_shared_cluster_f32(mapa_shared(l_base + row_l * 4u, p));
+        }
       }
     }
     float mx = -INFINITY;
@@ -267,7 +294,9 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
       const uint32_t off = (row_l * kOld + dseg + c) * 4u;
 #pragma unroll
       for (int p = 0; p < 8; ++p)
-        if (p < splits) v[p] = ld_shared_cluster_f32x4(mapa_shared(o_base + off, p));
+        if (p < splits)
+          v[p] = gx ? __ldcg(reinterpret_cast<const float4*>(ws_blk + p * slot_floats) + off / 16)
+                    : ld_shared_cluster_f32x4(mapa_shared(o_base + off, p));
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int p = 0; p < 8; ++p)
@@ -284,7 +313,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
         *reinterpret_cast<uint2*>(dst + c) = pk;
       }
     }
-    cluster_sync_all();
+    if (!gx) cluster_sync_all();  // peers may still read this CTA's shared memory
   } else {
     // Normalise and store BF16 rows.
     const float inv[2] = {1.0f / l_run[0], 1.0f / l_run[1]};
@@ -331,7 +360,18 @@ int attention_splits(const AttnArgs& a, int num_sms) {
   return best;
 }
 
-void launch_attention(const AttnArgs& a, cudaStream_t s) {
+size_t attention_ws_floats(const AttnArgs& a) {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int splits = attention_splits(a, sms);
+  if (splits == 1) return 0;
+  const size_t qblocks = (a.lq + kBQ - 1) / kBQ;
+  return qblocks * a.heads * a.batch * splits * kBQ * (kD + 4);
+}
+
+void launch_attention(const AttnArgs& a_in, cudaStream_t s) {
+  AttnArgs a = a_in;
   static int sms = 0;
   if (!sms) {
     int dev = 0;
@@ -340,6 +380,9 @@ void launch_attention(const AttnArgs& a, cudaStream_t s) {
   }
   const int splits = attention_splits(a, sms);
   const int qblocks = (a.lq + kBQ - 1) / kBQ;
+  if (a.ws && static_cast<size_t>(qblocks) * a.heads * a.batch * splits * kBQ * (kD + 4) >
+                  a.ws_floats)
+    a.ws = nullptr;  // too small: merge through distributed shared memory
   if (splits == 1) {
     launch_pdl(attention_kernel<false>, dim3(qblocks, a.heads, a.batch), dim3(128), kSmem, s, a, 1);
     return;

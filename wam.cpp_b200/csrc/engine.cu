@@ -634,7 +634,11 @@ bool MotEngine::build(int b, std::string* err) {
         return cudaGetLastError();
       }, OP_QKV, 1, 4.0 * parts * q.rows * q.hidden);
     };
-    auto attend = [&](Program& p, const AttnArgs& a) {
+    auto attend = [&](Program& p, const AttnArgs& a_in) {
+      // Key splits merge through the lane's workspace (dead between GEMMs).
+      AttnArgs a = a_in;
+      a.ws = gemm_ws_[p.lane];
+      a.ws_floats = gemm_ws_floats_;
       const double bq = 2.0 * a.batch * a.heads * a.lq * 128.0;
       const double bkv = 4.0 * a.batch * a.heads * a.lk * 128.0;
       p.add([a](cudaStream_t s) {

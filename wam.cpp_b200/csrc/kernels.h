@@ -167,8 +167,15 @@ struct AttnArgs {
   int ldo_first;
   int split_first;
   L2Prefetch pf;
+  // Split-KV merge workspace (attention_ws_floats floats) or null: with it the
+  // key splits of a query block exchange their partial rows through L2,
+  // without it through distributed shared memory.
+  float* ws = nullptr;
+  size_t ws_floats = 0;
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
+// Workspace the split-KV merge of `a` needs (0 when it does not split).
+size_t attention_ws_floats(const AttnArgs& a);
 cudaError_t attention_init();
 
 // y[m, n] = act(bf16(bf16(sum_k x[m, k] * w(n, k)) + b[n])) for the small
