@@ -66,8 +66,6 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
   if (tid == 0)
     l2_prefetch_share(a.pf, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z),
                       gridDim.x * gridDim.y * gridDim.z);
-  griddep_wait();
-  griddep_launch_dependents();
   const bf16* qg = a.q + seq * a.q_seq_stride + head * a.q_head_stride + static_cast<long long>(q0) * kD;
   const bf16* kg = a.k + seq * a.kv_seq_stride + head * a.kv_head_stride;
   const bf16* vg = a.v + seq * a.kv_seq_stride + head * a.kv_head_stride;
@@ -76,12 +74,23 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
   const int kb_begin = SPLIT ? (split * n_kb_all) / splits : 0;
   const int kb_end = SPLIT ? ((split + 1) * n_kb_all) / splits : n_kb_all;
   const int n_kb = kb_end - kb_begin;
+  // K/V that the preceding kernel does not write (cached prefix rows, prompt
+  // K/V) start loading before waiting for it; Q always comes from it.
+  const int key_end = kb_end * kBKey < a.lk ? kb_end * kBKey : a.lk;
+  const bool kv_static = key_end <= a.static_keys;
+  auto load_kv0 = [&]() {
+    if (n_kb > 0) {
+      load_tile(s_k[0], kg + static_cast<long long>(kb_begin) * kBKey * kD, a.lk - kb_begin * kBKey, tid);
+      load_tile(s_v[0], vg + static_cast<long long>(kb_begin) * kBKey * kD, a.lk - kb_begin * kBKey, tid);
+    }
+    cp_async_commit();
+  };
+  if (kv_static) load_kv0();
+  griddep_wait();
+  griddep_launch_dependents();
   load_tile(s_q, qg, a.lq - q0, tid);
-  if (n_kb > 0) {
-    load_tile(s_k[0], kg + static_cast<long long>(kb_begin) * kBKey * kD, a.lk - kb_begin * kBKey, tid);
-    load_tile(s_v[0], vg + static_cast<long long>(kb_begin) * kBKey * kD, a.lk - kb_begin * kBKey, tid);
-  }
   cp_async_commit();
+  if (!kv_static) load_kv0();
 
   // Q fragments for this warp's 16 rows, 8 k-steps of 16 dims.
   uint32_t qf[8][4];

@@ -905,6 +905,7 @@ bool MotEngine::build(int b, std::string* err) {
       cx.kv_head_stride = static_cast<long long>(Nt) * 128;
       cx.lq = V;
       cx.lk = Nt;
+      cx.static_keys = Nt;  // prompt K/V, projected before the prefix
       cx.heads = heads;
       cx.batch = b;
       cx.scale = 1.0f / std::sqrt(128.0f);
@@ -992,6 +993,7 @@ bool MotEngine::build(int b, std::string* err) {
         at.kv_head_stride = q.kv_head_stride;
         at.lq = T;
         at.lk = P + T;
+        at.static_keys = P;  // prefix rows; this layer's scatter writes rows P..P+T
         at.heads = heads;
         at.batch = b;
         at.scale = 1.0f / std::sqrt(128.0f);
@@ -1013,6 +1015,7 @@ bool MotEngine::build(int b, std::string* err) {
         cx.kv_head_stride = static_cast<long long>(Nt) * 128;
         cx.lq = T;
         cx.lk = Nt;
+        cx.static_keys = Nt;  // prompt K/V, projected before the prefix
         cx.heads = heads;
         cx.batch = b;
         cx.scale = at.scale;

@@ -167,6 +167,9 @@ struct AttnArgs {
   int ldo_first;
   int split_first;
   L2Prefetch pf;
+  // Keys [0, static_keys) are not written by the preceding kernel: a CTA whose
+  // whole key range lies there loads its K/V before waiting for it.
+  int static_keys = 0;
   // Split-KV merge workspace (attention_ws_floats floats) or null: with it the
   // key splits of a query block exchange their partial rows through L2,
   // without it through distributed shared memory.
