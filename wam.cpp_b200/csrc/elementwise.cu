@@ -455,6 +455,18 @@ void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w,
   launch_ln<1>(x, ldx, rows, cols, w, b, eps, y, ldy, s, pf);
 }
 
+namespace {
+// Every thread of the grid prefetches its share of the ranges into L2.
+__global__ void l2_prefetch_kernel(const __grid_constant__ L2Prefetch pf) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  l2_prefetch_share(pf, t, gridDim.x * blockDim.x);
+}
+}  // namespace
+
+void launch_l2_prefetch(const L2Prefetch& pf, cudaStream_t s) {
+  l2_prefetch_kernel<<<32, 64, 0, s>>>(pf);
+}
+
 void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s) {
   const int per = (a.hidden / 8 + kRowThreads - 1) / kRowThreads;
   const dim3 grid(a.rows), block(kRowThreads, 3);

@@ -217,6 +217,13 @@ bool MotEngine::init(const EngineOptions& opt, std::string* err) {
   // Diagnostic switch: keep GEMM weights in GGUF's row-major layout.
   const char* rm = std::getenv("WAM_B200_ROWMAJOR_WEIGHTS");
   rowmajor_weights_ = rm && rm[0] && rm[0] != '0';
+  // L2 prefetch of the next GEMM's weights while the denoise step's
+  // attention / LayerNorm / scatter kernels run: "kernel" (those kernels issue
+  // it) or "side" (a small prefetch grid on the second stream). Off by
+  // default: on B200 both made the chunk slower (57.7 and 56.7 ms against
+  // 54.9 ms without), the weight stream gains nothing from L2 residency.
+  const char* pm = std::getenv("WAM_B200_L2_PREFETCH");
+  prefetch_mode_ = !pm ? 0 : (std::strcmp(pm, "kernel") == 0 ? 1 : (std::strcmp(pm, "side") == 0 ? 2 : 0));
   CK(gemm_init(opt.device));
   CK(attention_init());
   if (!load_weights(err)) return false;
@@ -618,6 +625,30 @@ bool MotEngine::build(int b, std::string* err) {
       }, OP_SYNC, 0);
       p.lane = lane;
     };
+    // Side-lane L2 prefetch (prefetch_mode_ 2): starts once everything issued
+    // so far on the main stream is done, runs beside the main stream's next
+    // ops; nothing waits for it.
+    auto side_prefetch = [&](Program& p, std::pair<const void*, long long> a,
+                             std::pair<const void*, long long> b = {nullptr, 0}) {
+      if (prefetch_mode_ != 2) return;
+      L2Prefetch pf;
+      pf.ptr[0] = a.first;
+      pf.bytes[0] = a.second;
+      pf.ptr[1] = b.first;
+      pf.bytes[1] = b.second;
+      const int lane = p.lane;
+      p.lane = 0;
+      p.add([this](cudaStream_t) {
+        cudaError_t e = cudaEventRecord(ev_fork_, stream_);
+        return e == cudaSuccess ? cudaStreamWaitEvent(side_, ev_fork_, 0) : e;
+      }, OP_SYNC, 0);
+      p.lane = 1;
+      p.add([pf](cudaStream_t st) {
+        launch_l2_prefetch(pf, st);
+        return cudaGetLastError();
+      }, OP_PREFETCH, 1, 0.0);
+      p.lane = lane;
+    };
     auto join_side = [&](Program& p) {
       const int lane = p.lane;
       p.lane = 0;
@@ -666,9 +697,10 @@ bool MotEngine::build(int b, std::string* err) {
       r.second = bytes;
       return r;
     };
-    auto mkpf = [](std::pair<const void*, long long> a,
-                   std::pair<const void*, long long> b = {nullptr, 0}) {
+    auto mkpf = [&](std::pair<const void*, long long> a,
+                    std::pair<const void*, long long> b = {nullptr, 0}) {
       L2Prefetch pf;
+      if (prefetch_mode_ != 1) return pf;
       pf.ptr[0] = a.first;
       pf.bytes[0] = a.second;
       pf.ptr[1] = b.first;
@@ -950,6 +982,7 @@ bool MotEngine::build(int b, std::string* err) {
       small(dp, e1_, M, 128, W("gwp.action.mid.weight", 128 * 128), 128, 1,
             W("gwp.action.mid.bias", 128), 128, ACT_GELU_ERF, e2_);
       G(dp, e2_, 128, M, "gwp.action.out", E, 128, EPI_BIAS, true, nullptr, nullptr, 0, ha_, E);
+      side_prefetch(dp, wrange("gwp.blk.0.a.sa.qkv", 3LL * H, E));
       for (int l = 0; l < L && ok; ++l) {
         const std::string ap = "gwp.blk." + std::to_string(l) + ".a";
         const float* c = comb_steps_ + (static_cast<size_t>(s) * L + l) * 6 * E;
@@ -958,6 +991,7 @@ bool MotEngine::build(int b, std::string* err) {
         const long long l2cap = 64ll << 20;
         ln_mod(dp, ha_, M, E, c + E, c, nrm_, mkpf(wrange(ap + ".sa.qkv", 3LL * H, E, 0, l2cap)));
         G(dp, nrm_, E, M, ap + ".sa.qkv", 3 * H, E, EPI_BIAS, true, nullptr, nullptr, 0, qkv_, 3 * H);
+        side_prefetch(dp, wrange(ap + ".sa.o", E, H), wrange(ap + ".ca.q", H, E));
         QkvScatter q{};
         q.src = qkv_;
         q.ld_src = 3 * H;
@@ -1004,6 +1038,7 @@ bool MotEngine::build(int b, std::string* err) {
         G(dp, att_, H, M, ap + ".sa.o", E, H, EPI_GATED_RES, true, c + 2 * E, ha_, E, ha_, E);
         ln_aff(dp, ha_, M, E, ap + ".ca_norm", nrm_);
         G(dp, nrm_, E, M, ap + ".ca.q", H, E, EPI_BIAS, true, nullptr, nullptr, 0, cq_, H);
+        side_prefetch(dp, wrange(ap + ".ca.o", E, H));
         cross_q(dp, cq_, M, T, ap, qc_, mkpf(wrange(ap + ".ca.o", E, H)));
         AttnArgs cx{};
         cx.q = qc_;
@@ -1024,10 +1059,13 @@ bool MotEngine::build(int b, std::string* err) {
         cx.pf = mkpf(wrange(ap + ".ffn.in", Fa, E, 0, l2cap));
         attend(dp, cx);
         G(dp, catt_, H, M, ap + ".ca.o", E, H, EPI_RES, true, nullptr, ha_, E, ha_, E);
+        side_prefetch(dp, wrange(ap + ".ffn.in", Fa, E));
         ln_mod(dp, ha_, M, E, c + 4 * E, c + 3 * E, nrm_,
                mkpf(wrange(ap + ".ffn.in", Fa, E, l2cap)));
         G(dp, nrm_, E, M, ap + ".ffn.in", Fa, E, EPI_BIAS_GELU, true, nullptr, nullptr, 0, ffn_, Fa);
         G(dp, ffn_, Fa, M, ap + ".ffn.out", E, Fa, EPI_GATED_RES, true, c + 5 * E, ha_, E, ha_, E);
+        if (l + 1 < L)
+          side_prefetch(dp, wrange("gwp.blk." + std::to_string(l + 1) + ".a.sa.qkv", 3LL * H, E));
       }
       const float* cf = comb_final_ + static_cast<size_t>(s) * 2 * E;
       ln_mod(dp, ha_, M, E, cf + E, cf, nrm_);
@@ -1047,6 +1085,7 @@ bool MotEngine::build(int b, std::string* err) {
       launch_bf16_to_f32(action_bf_, d_out_, static_cast<long long>(b) * T * A, s);
       return cudaGetLastError();
     });
+    if (prefetch_mode_ == 2) join_side(dp);
     if (!ok) {
       if (e2 == "__rebuild__") continue;  // scratch grew: rebuild with the new pointers
       *err = e2;

@@ -60,7 +60,8 @@ using Launch = std::function<cudaError_t(cudaStream_t)>;
 
 // Kernel families, for the per-kernel profile (wam_b200_profile).
 enum OpKind : int { OP_GEMM = 0, OP_ATTENTION = 1, OP_LAYERNORM = 2, OP_QKV = 3, OP_SMALL = 4,
-                    OP_ELEMENTWISE = 5, OP_SYNC = 6 /* lane hand-off, no kernel */ };
+                    OP_ELEMENTWISE = 5, OP_SYNC = 6 /* lane hand-off, no kernel */,
+                    OP_PREFETCH = 7 /* L2 prefetch beside the main stream */ };
 
 struct Op {
   Launch fn;
@@ -168,6 +169,7 @@ class MotEngine {
   bf16* retile_tmp_ = nullptr;  // staging copy for in-place re-tiling (build only)
   size_t retile_tmp_elems_ = 0;
   bool rowmajor_weights_ = false;
+  int prefetch_mode_ = 0;  // 0 off, 1 by the non-GEMM kernels, 2 side-stream grid
   std::vector<float> sq01_, sq99_, aq01_, aq99_;
   uint64_t resident_bytes_ = 0;
 

@@ -177,6 +177,8 @@ struct AttnArgs {
   size_t ws_floats = 0;
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
+// Prefetches the ranges into L2 (a small grid meant to run beside other work).
+void launch_l2_prefetch(const L2Prefetch& pf, cudaStream_t s);
 // Workspace the split-KV merge of `a` needs (0 when it does not split).
 size_t attention_ws_floats(const AttnArgs& a);
 cudaError_t attention_init();

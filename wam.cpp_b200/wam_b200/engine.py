@@ -17,7 +17,8 @@ import numpy as np
 from ._lib import load
 from ._lib_engine import GEOM_FIELDS, Geometry, OpProfile, Options, Request, Stats, Status
 
-KINDS = ("gemm", "attention", "layernorm", "qkv_scatter", "small_linear", "elementwise")
+KINDS = ("gemm", "attention", "layernorm", "qkv_scatter", "small_linear", "elementwise", "sync",
+         "l2_prefetch")
 PHASES = ("prompt", "prefix", "denoise")
 
 
