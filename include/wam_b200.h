@@ -95,6 +95,24 @@ WAM_B200_API int wam_b200_op_gemm_noalloc(const void* x, int ldx, int m, const v
                                           int force_splits, void* stream);
 
 #define WAM_B200_GEMM_TILED_WEIGHTS 0x100
+/* w holds Q8_0 weight tiles written by wam_b200_op_q8_retile (n % 256 == 0):
+ * the GEMM streams 17 KB per 256 x 64 weight tile and converts it to BF16
+ * (q * d rounded to BF16) in shared memory for the tensor cores. */
+#define WAM_B200_GEMM_Q8_WEIGHTS 0x200
+
+/* Quantises n_elems BF16 weights (n_elems % 32 == 0, row-major [n][k]) to GGML
+ * Q8_0 blocks (34 bytes per 32 values: fp16 scale d, 32 int8 q; value q * d)
+ * with the gguf-py quantiser's rules: d = max|x| / 127 in F32, q = x * (1/d)
+ * rounded half away from zero, d rounded to fp16. No counterpart in the
+ * reference, whose artifacts are BF16/F32 only (src/models/gwp05/artifact.cpp:
+ * 129-133); this is the Q8_0 policy of the build's config 5. */
+WAM_B200_API int wam_b200_op_q8_quantize(const void* w, long long n_elems, void* blocks,
+                                         void* stream);
+
+/* Re-tiles row-major Q8_0 blocks of an [n][k] weight (n % 256 == 0, k % 64 ==
+ * 0; the GGUF layout of a Q8_0 tensor with ne = {k, n}) into GEMM tiles
+ * [n/256][k/64] of 17408 bytes: int8 [256][64], then fp16 scales [256][2]. */
+WAM_B200_API int wam_b200_op_q8_retile(const void* blocks, void* tiles, int n, int k, void* stream);
 
 /* Re-tiles a row-major BF16 weight w[n][k] (n % 256 == 0, k % 64 == 0, the
  * GGUF ne = {k, n} layout) into dst as contiguous 32 KB tiles

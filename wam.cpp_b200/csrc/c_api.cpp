@@ -82,12 +82,13 @@ WAM_B200_API int wam_b200_op_gemm(const void* x, int ldx, int m, const void* w, 
   scratch.counter_slots = counter_slots;
   scratch.error = error;
   const bool tiled = (epilogue & WAM_B200_GEMM_TILED_WEIGHTS) != 0;
-  epilogue &= ~WAM_B200_GEMM_TILED_WEIGHTS;
+  const bool q8 = (epilogue & WAM_B200_GEMM_Q8_WEIGHTS) != 0;
+  epilogue &= ~(WAM_B200_GEMM_TILED_WEIGHTS | WAM_B200_GEMM_Q8_WEIGHTS);
   GemmOp op;
   const char* err = gemm_plan(&op, static_cast<const bf16*>(x), ldx, m, static_cast<const bf16*>(w),
                               n, k, epilogue, static_cast<const bf16*>(bias), gate,
                               static_cast<const bf16*>(residual), ldr, out, ldo, scratch,
-                              num_sms_current(), force_splits, tiled);
+                              num_sms_current(), force_splits, tiled, q8);
   if (err) {
     set_last_error(err);
     return WAM_B200_INVALID_ARGUMENT;
@@ -124,6 +125,51 @@ WAM_B200_API int wam_b200_op_retile_weights(const void* src, void* dst, int n, i
   cudaError_t ce = cudaGetLastError();
   if (ce != cudaSuccess) {
     set_last_error(std::string("retile_weights launch: ") + cudaGetErrorString(ce));
+    return WAM_B200_CUDA_ERROR;
+  }
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_op_q8_quantize(const void* w, long long n_elems, void* blocks,
+                                         void* stream) {
+  std::string why;
+  int rc = check_sm100(&why);
+  if (rc != WAM_B200_OK) {
+    set_last_error(why);
+    return rc;
+  }
+  if (!w || !blocks || n_elems <= 0 || n_elems % 32) {
+    set_last_error("q8_quantize: n_elems must be a positive multiple of 32");
+    return WAM_B200_INVALID_ARGUMENT;
+  }
+  launch_q8_quantize(static_cast<const bf16*>(w), n_elems, static_cast<uint8_t*>(blocks),
+                     static_cast<cudaStream_t>(stream));
+  cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) {
+    set_last_error(std::string("q8_quantize launch: ") + cudaGetErrorString(ce));
+    return WAM_B200_CUDA_ERROR;
+  }
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_op_q8_retile(const void* blocks, void* tiles, int n, int k,
+                                       void* stream) {
+  std::string why;
+  int rc = check_sm100(&why);
+  if (rc != WAM_B200_OK) {
+    set_last_error(why);
+    return rc;
+  }
+  if (!blocks || !tiles || n <= 0 || k <= 0 || n % 256 || k % 64 ||
+      reinterpret_cast<uintptr_t>(tiles) % 16) {
+    set_last_error("q8_retile: n % 256, k % 64 and a 16-byte aligned destination required");
+    return WAM_B200_INVALID_ARGUMENT;
+  }
+  launch_q8_retile(static_cast<const uint8_t*>(blocks), static_cast<uint8_t*>(tiles), n, k,
+                   static_cast<cudaStream_t>(stream));
+  cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) {
+    set_last_error(std::string("q8_retile launch: ") + cudaGetErrorString(ce));
     return WAM_B200_CUDA_ERROR;
   }
   return WAM_B200_OK;

@@ -30,6 +30,7 @@
 #include "kernels.h"
 #include "mathops.cuh"
 #include "ptx.cuh"
+#include <cuda_fp16.h>
 
 namespace wamb {
 
@@ -59,12 +60,14 @@ int a_rows_for(int m) { return m >= kTM ? kTM : ((m + 15) / 16) * 16; }
 // Pipeline stages: one weight k-block (32 KB) and one token k-block per
 // stage, as many stages as the shared-memory budget holds (the weight stream
 // is latency bound, so the bytes in flight per SM set its rate).
-int stages_for(int a_rows) {
-  const int st = kStageBudget / (a_rows * kBK * 2 + kBBytes);
+// Q8_0 weights add a raw 17 KB buffer per stage (converted into the BF16 stage).
+int stage_bytes(int a_rows, bool q8) { return a_rows * kBK * 2 + kBBytes + (q8 ? kQ8TileBytes : 0); }
+int stages_for(int a_rows, bool q8 = false) {
+  const int st = kStageBudget / stage_bytes(a_rows, q8);
   return st > kMaxStages ? kMaxStages : st;
 }
-int smem_for(int a_rows) {
-  return stages_for(a_rows) * (a_rows * kBK * 2 + kBBytes) + 1024 + kSmemTail;
+int smem_for(int a_rows, bool q8 = false) {
+  return stages_for(a_rows, q8) * stage_bytes(a_rows, q8) + 1024 + kSmemTail;
 }
 
 // Epilogue of CNT consecutive features n0.. of token m (CNT = 8 or 16; the
@@ -318,12 +321,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t a_bytes = static_cast<uint32_t>(args.a_rows) * kBK * 2;
   // Token stages first: a UMMA reads 128 token rows from every stage, so the
   // rows past a short tile must land in (unused) shared memory that follows.
+  const bool q8 = args.w_q8 != nullptr;
   uint8_t* smem_a = smem;
   uint8_t* smem_w = smem + S * a_bytes;
-  uint8_t* tail = smem_w + S * kBBytes;
+  uint8_t* smem_q8 = smem_w + S * kBBytes;  // Q8_0 stages (q8 only)
+  uint8_t* tail = smem_q8 + (q8 ? S * kQ8TileBytes : 0);
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + S;
-  uint64_t* accum = empty + S;
+  uint64_t* conv = empty + S;  // q8: BF16 weights of the stage are ready
+  uint64_t* accum = conv + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
   int* ok_flag = last_flag + 1;
@@ -353,6 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 1);
     }
     mbar_init(accum, 1);
     fence_barrier_init();
@@ -375,12 +382,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint64_t pol_w = WAM_GEMM_WEIGHT_EVICT_FIRST ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_x = policy_evict_last();
-      const uint32_t stage_tx = a_bytes + kBBytes;
+      const uint32_t stage_tx = a_bytes + (q8 ? kQ8TileBytes : kBBytes);
       const bf16* w_tiles =
           args.w_tiled ? args.w_tiled + static_cast<size_t>(tile_n) * args.num_kb * (kWN * kBK)
                        : nullptr;
       auto load_w = [&](int stage, int kb) {
-        if (w_tiles)
+        if (q8)
+          bulk_load(smem_q8 + stage * kQ8TileBytes,
+                    args.w_q8 + (static_cast<size_t>(tile_n) * args.num_kb + kb) * kQ8TileBytes,
+                    kQ8TileBytes, &full[stage], pol_w);
+        else if (w_tiles)
           bulk_load(smem_w + stage * kBBytes, w_tiles + static_cast<size_t>(kb) * (kWN * kBK),
                     kBBytes, &full[stage], pol_w);
         else
@@ -420,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S;
         const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait(&full[s], ph)) {
+        if (!mbar_wait(q8 ? &conv[s] : &full[s], ph)) {
           atomicCAS(args.error, 0u, static_cast<unsigned>(kErrMmaTimeout));
           break;
         }
@@ -447,6 +458,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       gate_s[j] = (args.gate && n < args.n) ? args.gate[n] : 0.0f;
     }
     named_bar_sync(1, 128);
+    if (q8) {
+      // Q8_0 -> BF16 for every stage of the mainloop: 8 weights (one 16-byte
+      // swizzled chunk of the UMMA operand) per thread and step; value = q * d
+      // (exact in F32) rounded to BF16.
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
+        if (!mbar_wait(&full[s], ph)) {
+          atomicCAS(args.error, 0u, static_cast<unsigned>(kErrMmaTimeout));
+          break;
+        }
+        const uint8_t* raw = smem_q8 + s * kQ8TileBytes;
+        uint8_t* wst = smem_w + s * kBBytes;
+#pragma unroll 4
+        for (int it = et; it < kWN * 8; it += 128) {
+          const int r = it >> 3, c = it & 7;
+          const uint2 qv = *reinterpret_cast<const uint2*>(raw + r * 64 + c * 8);
+          const __half dh = *reinterpret_cast<const __half*>(raw + 16384 + r * 4 + (c >> 2) * 2);
+          const float d = __half2float(dh);
+          const uint32_t qw[2] = {qv.x, qv.y};
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int b0 = static_cast<int8_t>((qw[j >> 1] >> (16 * (j & 1))) & 0xFF);
+            const int b1 = static_cast<int8_t>((qw[j >> 1] >> (16 * (j & 1) + 8)) & 0xFF);
+            const __nv_bfloat162 h = __floats2bfloat162_rn(static_cast<float>(b0) * d,
+                                                           static_cast<float>(b1) * d);
+            o[j] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(wst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        fence_proxy_async_smem();  // generic-proxy writes -> the tensor cores' async proxy
+        named_bar_sync(1, 128);
+        if (et == 0) mbar_arrive(&conv[s]);
+      }
+    }
     ok = mbar_wait(accum, 0);
     if (!ok) atomicCAS(args.error, 0u, static_cast<unsigned>(kErrEpilogueTimeout));
     tc_fence_after();
@@ -758,8 +805,10 @@ size_t gemm_scratch_floats(int m, int n, int k, int num_sms, int force_splits, i
 const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, int n, int k,
                       int epilogue, const bf16* bias, const float* gate, const bf16* residual,
                       int ldr, void* out, int ldo, const GemmScratch& scratch, int num_sms,
-                      int force_splits, bool w_tiled) {
+                      int force_splits, bool w_tiled, bool w_q8) {
   if (m <= 0 || n <= 0 || k <= 0) return "gemm: empty shape";
+  if (w_q8 && (n % kWN != 0 || reinterpret_cast<uintptr_t>(w) % 16 != 0))
+    return "gemm: Q8_0 weight tiles need N a multiple of 256 and a 16-byte aligned pointer";
   if (w_tiled && (n % kWN != 0 || reinterpret_cast<uintptr_t>(w) % 16 != 0))
     return "gemm: re-tiled weights need N a multiple of 256 and a 16-byte aligned pointer";
   if (k % kBK != 0) return "gemm: K must be a multiple of 64";
@@ -781,7 +830,7 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   // The epilogue stages a [token][feature] tile (F32 rows of kPartLd floats at
   // most) in the pipeline stages' shared memory.
   if (static_cast<long long>(a_rows) * kPartLd * 4 >
-      static_cast<long long>(stages_for(a_rows)) * (a_rows * kBK * 2 + kBBytes))
+      static_cast<long long>(stages_for(a_rows, w_q8)) * (a_rows * kBK * 2 + kBBytes))
     return "gemm: stage budget too small for the epilogue tile";
   const int tiles_m = (m + kTM - 1) / kTM;
   const int tiles_n = (n + kWN - 1) / kWN;
@@ -802,7 +851,7 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
         (mode == SPLIT_WORKSPACE && (!scratch.counters || tiles_m * tiles_n > scratch.counter_slots)))
       return "gemm: split-K scratch too small";
   }
-  if (!w_tiled && !encode_bf16_2d(&op->tm_w, w, k, n, k, kWN))
+  if (!w_tiled && !w_q8 && !encode_bf16_2d(&op->tm_w, w, k, n, k, kWN))
     return "gemm: weight tensor map encode failed";
   if (!encode_bf16_2d(&op->tm_x, x, k, m, ldx, a_rows))
     return "gemm: activation tensor map encode failed";
@@ -814,8 +863,9 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   a.splits = splits;
   a.split_mode = mode;
   a.a_rows = a_rows;
-  a.stages = stages_for(a_rows);
-  a.w_tiled = w_tiled ? w : nullptr;
+  a.stages = stages_for(a_rows, w_q8);
+  a.w_tiled = w_tiled && !w_q8 ? w : nullptr;
+  a.w_q8 = w_q8 ? reinterpret_cast<const uint8_t*>(w) : nullptr;
   a.tiles_m = tiles_m;
   a.tiles_n = tiles_n;
   a.epilogue = epilogue;
@@ -829,7 +879,7 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   a.counters = scratch.counters;
   a.error = scratch.error;
   op->grid = tiles_m * tiles_n * splits;
-  op->smem_bytes = smem_for(a_rows);
+  op->smem_bytes = smem_for(a_rows, w_q8);
   return nullptr;
 }
 

@@ -53,6 +53,7 @@ struct GemmArgs {
   int a_rows;  // token rows loaded per tile (<= 128)
   int stages;  // pipeline stages (one weight + one token k-block each)
   const bf16* w_tiled;  // weights re-tiled by launch_retile_weights, or null (tensor map)
+  const uint8_t* w_q8;  // Q8_0 weight tiles (launch_q8_retile), or null
   int tiles_m, tiles_n;
   int epilogue;
   const bf16* bias;      // [n] or null
@@ -88,13 +89,22 @@ struct GemmOp {
 const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, int n, int k,
                       int epilogue, const bf16* bias, const float* gate, const bf16* residual,
                       int ldr, void* out, int ldo, const GemmScratch& scratch, int num_sms,
-                      int force_splits, bool w_tiled = false);
+                      int force_splits, bool w_tiled = false, bool w_q8 = false);
 // Re-tiles a row-major [n][k] BF16 weight (n % 256 == 0, k % 64 == 0) into
 // contiguous 32 KB tiles [n/256][k/64][256][64] with the 128-byte swizzle of
 // the UMMA operand pre-applied, so one bulk copy fetches a pipeline stage.
 void launch_retile_weights(const bf16* src, bf16* dst, int n, int k, cudaStream_t s);
 // Weight rows per re-tiled tile (256).
 int gemm_weight_tile_rows();
+
+// Q8_0 weights (q8.cu). Bytes of one GEMM weight tile (256 rows x 64 of K):
+// int8 [256][64] then fp16 scales [256][2].
+constexpr int kQ8TileBytes = 256 * 64 + 256 * 2 * 2;
+// BF16 weights (n_elems % 32 == 0) -> GGML Q8_0 blocks (34 bytes per 32).
+void launch_q8_quantize(const bf16* w, long long n_elems, uint8_t* out, cudaStream_t s);
+// Row-major Q8_0 blocks of an [n][k] weight (n % 256 == 0, k % 64 == 0) ->
+// GEMM tiles [n/256][k/64][kQ8TileBytes].
+void launch_q8_retile(const uint8_t* src, uint8_t* dst, int n, int k, cudaStream_t s);
 cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream);
 // Sets per-kernel launch attributes on the current device (call once per
 // device before the first launch or graph capture).

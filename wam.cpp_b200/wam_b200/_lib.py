@@ -46,6 +46,8 @@ def load(path: Path | None = None):
     _sig(lib, "wam_b200_op_gemm_noalloc", i32,
          [vp, i32, i32, vp, i32, i32, i32, vp, vp, vp, i32, vp, i32, i32, vp])
     _sig(lib, "wam_b200_op_retile_weights", i32, [vp, vp, i32, i32, vp])
+    _sig(lib, "wam_b200_op_q8_quantize", i32, [vp, C.c_longlong, vp, vp])
+    _sig(lib, "wam_b200_op_q8_retile", i32, [vp, vp, i32, i32, vp])
     _sig(lib, "wam_b200_op_attention", i32,
          [vp, C.c_longlong, C.c_longlong, vp, vp, C.c_longlong, C.c_longlong, i32, i32, i32, i32,
           C.c_float, vp, i32, vp])

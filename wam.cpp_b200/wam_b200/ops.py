@@ -55,6 +55,39 @@ class TiledWeight:
         check(rc, "wam_b200_op_retile_weights")
 
 
+GEMM_Q8_WEIGHTS = 0x200
+Q8_TILE_BYTES = 256 * 64 + 256 * 2 * 2
+
+
+def q8_quantize(w):
+    """BF16 [n, k] -> GGML Q8_0 blocks (uint8 [n * k / 32, 34]) on the device."""
+    w = w.contiguous()
+    out = torch.empty(w.numel() // 32, 34, dtype=torch.uint8, device=w.device)
+    check(load().wam_b200_op_q8_quantize(_ptr(w), w.numel(), _ptr(out), _stream()),
+          "wam_b200_op_q8_quantize")
+    return out
+
+
+class Q8Weight:
+    """A [n, k] weight as Q8_0 GEMM tiles (quantised on the device from BF16,
+    or from given Q8_0 blocks); `data` holds [n/256][k/64] tiles of 17408 bytes."""
+
+    def __init__(self, w=None, blocks=None, shape=None):
+        if blocks is None:
+            n, k = w.shape
+            blocks = q8_quantize(w)
+            device = w.device
+        else:
+            n, k = shape
+            device = blocks.device
+        self.shape = (n, k)
+        self.device = device
+        self.blocks = blocks
+        self.data = torch.empty((n // 256) * (k // 64) * Q8_TILE_BYTES, dtype=torch.uint8, device=device)
+        check(load().wam_b200_op_q8_retile(_ptr(blocks), _ptr(self.data), n, k, _stream()),
+              "wam_b200_op_q8_retile")
+
+
 def gemm(x, w, epilogue=EPI_BIAS, bias=None, gate=None, residual=None, out=None,
          scratch: Scratch | None = None, force_splits: int = 0):
     """out[m, n] = epilogue(x[m, :K] . w[n, :]) via wam_b200_op_gemm.
@@ -67,6 +100,9 @@ def gemm(x, w, epilogue=EPI_BIAS, bias=None, gate=None, residual=None, out=None,
     n, k = w.shape
     if isinstance(w, TiledWeight):
         epilogue |= GEMM_TILED_WEIGHTS
+        w = w.data
+    elif isinstance(w, Q8Weight):
+        epilogue |= GEMM_Q8_WEIGHTS
         w = w.data
     if out is None:
         dt = torch.float32 if (epilogue & 0xFF) == EPI_F32_OUT else torch.bfloat16
