@@ -44,7 +44,14 @@ def config2(layers: int | None = None):
     return g
 
 
-def workload(g, batch: int) -> dict:
+def workload(g, batch: int, weights: str = "bf16") -> dict:
+    if weights == "q8_0":
+        return dict(workload(g, batch),
+                    workload="config5: config 2 with every linear weight Q8_0 (gguf-py rules, "
+                             "quantised on the device; GEMMs convert Q8_0 tiles to BF16 in shared "
+                             "memory)",
+                    weights="synthetic N(0,0.02) BF16 quantised to Q8_0, biases 0",
+                    l2="no flush needed: each chunk streams ~10.5 GB of Q8_0 weights (> 126 MB L2)")
     return {"workload": "config2: GWP-0.5-shaped MoT action chunk (prompt projection + prefix "
                         "cache + 10 Euler steps)",
             "layers": g.layers, "hidden": g.hidden, "action_hidden": g.action_hidden,
@@ -305,6 +312,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=1, help="requests per GPU per step")
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--weights", choices=["bf16", "q8_0"], default="bf16",
+                    help="q8_0: BASELINE config 5 (every linear weight Q8_0) instead of config 2")
     ap.add_argument("--op-case", default=None,
                     help="gemm:M,N,K or attention:LQ,LK,HEADS: run one kernel on a small case "
                          "(for ncu captures) and print its event timing instead of the bench line")
@@ -350,6 +359,7 @@ def main() -> None:
     g = config2()
     B = args.batch
     eng = Engine(g, seed=SEED, bias_scale=0.0, device=local, max_batch=B, graphs=True,
+                 weights=args.weights,
                  prompt_cache=False)
     reqs = []
     for i in range(B):
@@ -415,7 +425,7 @@ def main() -> None:
         "warmup": args.warmup, "ms_per_step": total_s * 1e3 / args.steps,
         "p50_ms_per_chunk": statistics.median(per), "p95_ms_per_chunk": float(np.percentile(per, 95)),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic", "config": {**workload(g, B), "parallelism": f"dp{world} (replicas, no collective)"},
+        "data": "synthetic", "config": {**workload(g, B, args.weights), "parallelism": f"dp{world} (replicas, no collective)"},
         "roofline": hbm_roof, "roofline_tensor": tc_roof, "clocks": clocks.summary(),
         "phase_ms": phases, "kernel_breakdown": breakdown,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -207,6 +207,11 @@ typedef struct wam_b200_options {
   int max_batch;
   int use_cuda_graphs;
   int prompt_cache; /* reuse projected prompt K/V for an identical prompt */
+  /* Added after the first layout (read only when struct_size covers it):
+   * 0 BF16 weights; 1 Q8_0 linear weights (config 5: synthetic weights are
+   * quantised on the device with the gguf-py Q8_0 rules; a GGUF artifact may
+   * hold Q8_0 tensors). Linear layers then compute with q * d rounded to BF16. */
+  int weight_format;
 } wam_b200_options;
 
 /* One request (EngineInputsView, src/models/gwp05/engine/engine.h:91-105, with

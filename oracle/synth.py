@@ -180,6 +180,59 @@ def make_weights(g: Geometry, seed: int, bias_scale: float = 0.02) -> dict[str, 
     return out
 
 
+def linear_inner(name: str, g: Geometry) -> int:
+    """Row length of a linear layer's weight as the engine's Q8_0 policy sees it
+    (0: not a linear weight). Mirrors linear_inner() in wam.cpp_b200/csrc/engine.cu."""
+    if not name.endswith(".weight") or name.endswith((".qn.weight", ".kn.weight",
+                                                        "ca_norm.weight")):
+        return 0
+    E, H = g.action_hidden, g.hidden
+    if name == "gwp.patch.weight":
+        return g.vae_z * 4
+    if name.endswith(".in.weight") and name.startswith(("gwp.state", "gwp.action")):
+        return 128
+    if name.endswith(".mid.weight") or name in ("gwp.state.out.weight", "gwp.action.out.weight"):
+        return 128
+    if name == "gwp.decode.in.weight":
+        return E
+    if name == "gwp.decode.out.weight":
+        return g.action_dim
+    if name.endswith(".time.0.weight"):
+        return 256
+    if name.endswith(".text.0.weight"):
+        return g.text_dim
+    if name.startswith("gwp.acond"):
+        return E
+    if name.startswith("gwp.cond"):
+        return H
+    act = ".a." in name
+    W, F = (E, g.action_ffn) if act else (H, g.ffn)
+    if name.endswith((".sa.o.weight", ".ca.o.weight")):
+        return H
+    if name.endswith(".ffn.out.weight"):
+        return F
+    return W
+
+
+def quantize_q8_linear(g: Geometry, weights: dict[str, np.ndarray]) -> dict[str, np.ndarray]:
+    """Config-5 weights: every linear weight whose rows are whole 32-value
+    blocks goes through the gguf-py Q8_0 codec (quantise, dequantise) and back
+    to BF16, the values the engine's Q8_0 GEMM computes with."""
+    import gguf
+    from gguf import quants
+
+    out = dict(weights)
+    for name, w in weights.items():
+        inner = linear_inner(name, g)
+        if inner <= 0 or inner % 32:
+            continue
+        f = bf16_bits_to_f32(w.reshape(-1)).reshape(-1, 32)
+        q = quants.quantize(f, gguf.GGMLQuantizationType.Q8_0)
+        d = quants.dequantize(q, gguf.GGMLQuantizationType.Q8_0).astype(np.float32)
+        out[name] = f32_to_bf16_bits(d.reshape(-1)).reshape(w.shape)
+    return out
+
+
 def statistics(g: Geometry) -> dict[str, np.ndarray]:
     """state/action q01/q99 statistics (F32 [action_dim]) of the synthetic artifact."""
     i = np.arange(g.action_dim, dtype=np.float32)

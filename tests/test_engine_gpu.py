@@ -61,6 +61,33 @@ def test_engine_matches_oracle(cuda_device, geom_name):
     assert rel_l2(out, ref["action"]) < 5e-2
 
 
+@pytest.mark.parametrize("geom_name", ["TINY", "SMALL"])
+def test_engine_q8_matches_oracle(cuda_device, geom_name):
+    """Config-5 policy: Q8_0 linear weights (quantised on the device, gguf-py
+    rules); the oracle runs on the gguf-py dequantised weights."""
+    pytest.importorskip("gguf")
+    import oracle
+    from oracle import synth
+    from wam_b200.engine import Engine
+
+    geom = getattr(synth, geom_name)
+    w = synth.quantize_q8_linear(geom, synth.make_weights(geom, SEED, bias_scale=0.02))
+    om = oracle.OracleModel(geom, w)
+    eng = Engine(geom, seed=SEED, bias_scale=0.02, prompt_cache=False, weights="q8_0")
+    r, er = _req(geom, 13)
+    ref = om.predict(r, dumps=True)
+    out = eng.predict(er)
+    for layer in range(geom.layers):
+        for name in ("prefix_k", "prefix_v", "prompt_k", "prompt_v"):
+            err = rel_l2(eng.read_tensor(name, 0, layer), ref[name][layer])
+            assert err < 2e-2, f"{name} layer {layer}: rel-L2 {err:.3e}"
+    vel = eng.read_tensor("velocity")
+    for s in range(geom.steps):
+        assert rel_l2(vel[s], ref["velocity"][s]) < 5e-2
+    assert np.isfinite(out).all()
+    assert rel_l2(out, ref["action"]) < 5e-2
+
+
 def test_graph_and_eager_identical(cuda_device):
     from oracle import synth
     from wam_b200.engine import Engine

@@ -79,6 +79,32 @@ void synth_rule(const std::string& name, double bias_scale, double* scale, doubl
 
 // Compact GGUF names (src/models/gwp05/engine/weights.cpp:116-167) and element
 // counts of every tensor the action-chunk path reads.
+int64_t linear_inner(const std::string& name, const Geometry& g) {
+  auto ends = [&](const char* suf) {
+    const size_t n = std::strlen(suf);
+    return name.size() >= n && name.compare(name.size() - n, n, suf) == 0;
+  };
+  if (!ends(".weight") || ends(".qn.weight") || ends(".kn.weight") || ends("ca_norm.weight"))
+    return 0;
+  const int64_t E = g.action_hidden, H = g.hidden;
+  if (name == "gwp.patch.weight") return g.vae_z * 4;
+  if (ends(".in.weight") && (name.rfind("gwp.state", 0) == 0 || name.rfind("gwp.action", 0) == 0))
+    return 128;  // [emb][A][128], torch layout
+  if (ends(".mid.weight") || name == "gwp.state.out.weight" || name == "gwp.action.out.weight")
+    return 128;
+  if (name == "gwp.decode.in.weight") return E;
+  if (name == "gwp.decode.out.weight") return g.action_dim;  // [emb][128][A]
+  if (ends(".time.0.weight")) return 256;
+  if (ends(".text.0.weight")) return g.text_dim;
+  if (name.rfind("gwp.acond", 0) == 0) return E;  // time.1 / time.out / text.1
+  if (name.rfind("gwp.cond", 0) == 0) return H;
+  const bool act = name.find(".a.") != std::string::npos;
+  const int64_t W = act ? E : H, F = act ? g.action_ffn : g.ffn;
+  if (ends(".sa.o.weight") || ends(".ca.o.weight")) return H;
+  if (ends(".ffn.out.weight")) return F;
+  return W;  // sa.qkv, ca.q, ca.k, ca.vproj, ffn.in
+}
+
 std::vector<std::pair<std::string, int64_t>> tensor_specs(const Geometry& g) {
   const int64_t E = g.action_hidden, H = g.hidden, A = g.action_dim, D = g.text_dim;
   const int64_t emb = g.num_embodiments;
@@ -252,6 +278,25 @@ const bf16* MotEngine::W(const std::string& name, int64_t numel) {
   return it->second;
 }
 
+// Q8_0 policy (weight_format 1): every linear weight whose rows are whole
+// 32-value blocks and that the artifact did not already hold as Q8_0 is
+// quantised on the device; its BF16 slot is overwritten with q * d (rounded to
+// BF16), which is what every consumer of the weight then computes with.
+bool MotEngine::quantize_linear_weights(const std::vector<std::pair<std::string, int64_t>>& specs,
+                                        std::string* err) {
+  for (const auto& s : specs) {
+    const int64_t inner = linear_inner(s.first, g_);
+    if (inner <= 0 || inner % 32 != 0 || q8_blocks_.count(s.first)) continue;
+    uint8_t* blocks = dalloc<uint8_t>(static_cast<size_t>(s.second / 32) * 34, err);
+    if (!blocks) return false;
+    launch_q8_quantize(w_[s.first], s.second, blocks, stream_);
+    launch_q8_dequantize(blocks, s.second, w_[s.first], stream_);
+    q8_blocks_[s.first] = blocks;
+  }
+  CK(cudaGetLastError());
+  return true;
+}
+
 bool MotEngine::load_weights(std::string* err) {
   GgufFile file;
   const bool synthetic = opt_.artifact_path.empty();
@@ -336,6 +381,7 @@ bool MotEngine::load_weights(std::string* err) {
       sq99_[i] = aq99_[i] = 1.0f + 0.02f * static_cast<float>(i);
     }
     CK(cudaGetLastError());
+    if (opt_.weight_format == 1 && !quantize_linear_weights(specs, err)) return false;
     CK(cudaStreamSynchronize(stream_));
     return true;
   }
@@ -356,13 +402,28 @@ bool MotEngine::load_weights(std::string* err) {
       ok = false;
       break;
     }
-    if (t->type != GGML_BF16 || static_cast<int64_t>(t->elements()) != s.second) {
-      *err = "artifact tensor " + s.first + " must be BF16 with " + std::to_string(s.second) +
-             " elements";
+    const int64_t inner = linear_inner(s.first, g_);
+    const bool q8 = t->type == GGML_Q8_0 && inner > 0 && inner % 32 == 0;
+    if ((t->type != GGML_BF16 && !q8) || static_cast<int64_t>(t->elements()) != s.second) {
+      *err = "artifact tensor " + s.first + " must be BF16 (or Q8_0 for a linear weight) with " +
+             std::to_string(s.second) + " elements";
       ok = false;
       break;
     }
     uint8_t* dst = reinterpret_cast<uint8_t*>(w_[s.first]);
+    if (q8) {
+      // Q8_0 blocks go to their own buffer; the BF16 slot gets q * d below.
+      if (t->bytes != static_cast<uint64_t>(s.second / 32) * 34) {
+        *err = "artifact tensor " + s.first + ": Q8_0 size mismatch";
+        ok = false;
+        break;
+      }
+      if (!(dst = dalloc<uint8_t>(t->bytes, err))) {
+        ok = false;
+        break;
+      }
+      q8_blocks_[s.first] = dst;
+    }
     for (uint64_t pos = 0; pos < t->bytes; pos += chunk) {
       const uint64_t n = std::min<uint64_t>(chunk, t->bytes - pos);
       cudaEventSynchronize(done[slot]);
@@ -378,6 +439,9 @@ bool MotEngine::load_weights(std::string* err) {
     if (!ok) break;
   }
   cudaStreamSynchronize(stream_);
+  for (const auto& kv : q8_blocks_)
+    launch_q8_dequantize(kv.second, wn_[kv.first], w_[kv.first], stream_);
+  if (ok && opt_.weight_format == 1 && !quantize_linear_weights(specs, err)) ok = false;
   if (ok) {
     const char* names[4] = {"state_q01", "state_q99", "action_q01", "action_q99"};
     std::vector<float>* dsts[4] = {&sq01_, &sq99_, &aq01_, &aq99_};
@@ -543,9 +607,26 @@ bool MotEngine::gemm(Program& p, const bf16* x, int ldx, int m, const std::strin
     *err = "missing or mis-shaped weight " + wname;
     return false;
   }
-  // Every weight with whole 256-row tiles is re-tiled in place, the first time
-  // a plan uses it, into contiguous 32 KB UMMA tiles (one bulk copy per stage).
-  const bool tiled = !rowmajor_weights_ && n % gemm_weight_tile_rows() == 0 && k % 64 == 0;
+  // Q8_0 linear weights with whole 256-row tiles stream as Q8_0 GEMM tiles
+  // (made from the blocks the first time a plan uses them).
+  const auto qb = q8_blocks_.find(wname + ".weight");
+  // Only the weight-streaming GEMMs (few tokens) take the Q8_0 tiles; the
+  // tensor-bound ones (prefix, batched) read the dequantised BF16 copy, which
+  // gives the same results (the Q8_0 GEMM is bit-identical to the BF16 GEMM on
+  // q * d) without converting every tile on the CUDA cores.
+  const bool q8 = qb != q8_blocks_.end() && m <= 64 && n % gemm_weight_tile_rows() == 0 &&
+                  k % 64 == 0;
+  if (q8 && !q8_tiles_.count(wname)) {
+    uint8_t* tiles = dalloc<uint8_t>(static_cast<size_t>(n / 256) * (k / 64) * kQ8TileBytes, err);
+    if (!tiles) return false;
+    launch_q8_retile(qb->second, tiles, n, k, stream_);
+    CK(cudaGetLastError());
+    q8_tiles_[wname] = tiles;
+  }
+  // Every other weight with whole 256-row tiles is re-tiled in place, the
+  // first time a plan uses it, into contiguous 32 KB UMMA tiles (one bulk copy
+  // per stage).
+  const bool tiled = !q8 && !rowmajor_weights_ && n % gemm_weight_tile_rows() == 0 && k % 64 == 0;
   if (tiled && !tiled_[wname]) {
     const size_t elems = static_cast<size_t>(n) * k;
     if (elems > retile_tmp_elems_) {
@@ -574,8 +655,9 @@ bool MotEngine::gemm(Program& p, const bf16* x, int ldx, int m, const std::strin
   sc.workspace_floats = gemm_ws_floats_;
   sc.error = err_word_;
   GemmOp op;
+  const bf16* wsrc = q8 ? reinterpret_cast<const bf16*>(q8_tiles_[wname]) : w;
   const char* e =
-      gemm_plan(&op, x, ldx, m, w, n, k, epi, b, gate, resid, ldr, out, ldo, sc, sms_, 0, tiled);
+      gemm_plan(&op, x, ldx, m, wsrc, n, k, epi, b, gate, resid, ldr, out, ldo, sc, sms_, 0, tiled, q8);
   if (e) {
     *err = std::string(e) + " (" + wname + ")";
     return false;

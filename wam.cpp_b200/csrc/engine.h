@@ -39,6 +39,7 @@ struct EngineOptions {
   int max_batch = 1;
   bool graphs = true;
   bool prompt_cache = true;
+  int weight_format = 0;  // 0 BF16, 1 Q8_0 linear weights
 };
 
 struct RequestView {
@@ -99,6 +100,10 @@ struct OpProfile {
 void synth_rule(const std::string& name, double bias_scale, double* scale, double* center);
 // (name, element count) of every BF16 tensor the MoT path reads.
 std::vector<std::pair<std::string, int64_t>> tensor_specs(const Geometry& g);
+// Innermost (contiguous) length of a linear layer's weight, 0 for tensors that
+// are not linear weights (norm gains, modulation tables, biases). Q8_0 applies
+// to linear weights whose rows are whole 32-value blocks.
+int64_t linear_inner(const std::string& name, const Geometry& g);
 uint64_t tensor_seed(uint64_t seed, const std::string& name);
 
 class MotEngine {
@@ -133,6 +138,8 @@ class MotEngine {
   MotEngine() = default;
   bool init(const EngineOptions& opt, std::string* err);
   bool load_weights(std::string* err);
+  bool quantize_linear_weights(const std::vector<std::pair<std::string, int64_t>>& specs,
+                               std::string* err);
   bool alloc_buffers(std::string* err);
   const bf16* W(const std::string& name, int64_t numel);
   bool build(int batch, std::string* err);
@@ -164,6 +171,10 @@ class MotEngine {
   size_t warena_bytes_ = 0;
   std::unordered_map<std::string, bf16*> w_;
   std::unordered_map<std::string, int64_t> wn_;
+  // Q8_0 mode: GGML blocks of every linear weight (its BF16 slot holds the
+  // dequantised values) and the GEMM tiles made from them.
+  std::unordered_map<std::string, uint8_t*> q8_blocks_;
+  std::unordered_map<std::string, uint8_t*> q8_tiles_;
   // GEMM weights already re-tiled in place into 16 KB UMMA tiles.
   std::unordered_map<std::string, bool> tiled_;
   bf16* retile_tmp_ = nullptr;  // staging copy for in-place re-tiling (build only)

@@ -2,6 +2,7 @@
 // C ABI's conventions (int return codes, malloc'd status messages,
 // src/serving/c_api.cpp:18-55) and translates its structs.
 #include <cstdlib>
+#include <cstddef>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -95,8 +96,10 @@ WAM_B200_API void wam_b200_status_free(wam_b200_status* st) {
 WAM_B200_API int wam_b200_create(const wam_b200_options* o, wam_b200_engine** out,
                                  wam_b200_status* st) {
   if (!o || !out) return fail(st, WAM_B200_INVALID_ARGUMENT, "options and engine pointer are required");
-  if (o->struct_size < sizeof(wam_b200_options))
+  // struct_size versioning: the first layout ends at weight_format.
+  if (o->struct_size < offsetof(wam_b200_options, weight_format))
     return fail(st, WAM_B200_INVALID_ARGUMENT, "wam_b200_options.struct_size is too small");
+  const bool has_format = o->struct_size >= offsetof(wam_b200_options, weight_format) + sizeof(int);
   *out = nullptr;
   wamb::EngineOptions eo;
   if (o->artifact_path) eo.artifact_path = o->artifact_path;
@@ -107,6 +110,9 @@ WAM_B200_API int wam_b200_create(const wam_b200_options* o, wam_b200_engine** ou
   eo.max_batch = o->max_batch;
   eo.graphs = o->use_cuda_graphs != 0;
   eo.prompt_cache = o->prompt_cache != 0;
+  eo.weight_format = has_format ? o->weight_format : 0;
+  if (eo.weight_format != 0 && eo.weight_format != 1)
+    return fail(st, WAM_B200_INVALID_ARGUMENT, "weight_format must be 0 (BF16) or 1 (Q8_0)");
   std::string err;
   auto e = wamb::MotEngine::create(eo, &err);
   if (!e) {

@@ -40,7 +40,7 @@ constexpr int kTM = 128;              // token rows per tile (UMMA M, TMEM lanes
 constexpr int kWN = 256;              // weight rows per tile (UMMA N, TMEM columns)
 constexpr int kBK = 64;               // K per stage: one 128-byte swizzle row of BF16
 constexpr int kBBytes = kWN * kBK * 2;  // weight tile per stage (32 KB)
-constexpr int kThreads = 192;
+constexpr int kThreads = 256;  // warp 0 copies, 1 MMA, 2-5 epilogue, 2-7 Q8_0 conversion
 #ifndef WAM_GEMM_STAGE_BUDGET_KB
 #define WAM_GEMM_STAGE_BUDGET_KB 200
 #endif
@@ -378,6 +378,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   griddep_launch_dependents();
 
   bool ok = true;
+  // Q8_0 -> BF16 of every stage of the mainloop by warps 2-7 (ct = 0..191):
+  // 16 weights (half a Q8_0 block, one scale) per thread and step, two 16-byte
+  // swizzled chunks of the UMMA operand row. value = q * d exactly: the byte
+  // becomes the float 2^23 + (q + 128) through a byte permute; subtracting
+  // 2^23 + 128 leaves q (exact, integers below 2^24), and q * d is exact in F32
+  // (8 + 11 significant bits); then rounded to BF16.
+  auto q8_convert_stages = [&](int ct) {
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % S;
+      const uint32_t ph = (i / S) & 1;
+      if (!mbar_wait(&full[s], ph)) {
+        atomicCAS(args.error, 0u, static_cast<unsigned>(kErrMmaTimeout));
+        break;
+      }
+      const uint8_t* raw = smem_q8 + s * kQ8TileBytes;
+      uint8_t* wst = smem_w + s * kBBytes;
+#pragma unroll 2
+      for (int it = ct; it < kWN * 4; it += 192) {
+        const int r = it >> 2, c2 = it & 3;
+        const uint4 qv = *reinterpret_cast<const uint4*>(raw + r * 64 + c2 * 16);
+        const float d = __half2float(
+            *reinterpret_cast<const __half*>(raw + 16384 + r * 4 + (c2 >> 1) * 2));
+        const uint32_t qw[4] = {qv.x ^ 0x80808080u, qv.y ^ 0x80808080u, qv.z ^ 0x80808080u,
+                                qv.w ^ 0x80808080u};
+        uint32_t o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t word = qw[j >> 1];
+          const uint32_t sel0 = 0x7540u | (2 * (j & 1));
+          const uint32_t sel1 = 0x7540u | (2 * (j & 1) + 1);
+          const float f0 = __uint_as_float(__byte_perm(word, 0x4B000000u, sel0));
+          const float f1 = __uint_as_float(__byte_perm(word, 0x4B000000u, sel1));
+          const __nv_bfloat162 h =
+              __floats2bfloat162_rn((f0 - 8388736.0f) * d, (f1 - 8388736.0f) * d);
+          o[j] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        const int ca = 2 * c2, cb = 2 * c2 + 1;
+        *reinterpret_cast<uint4*>(wst + r * 128 + ((ca ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(wst + r * 128 + ((cb ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+      }
+      fence_proxy_async_smem();  // generic-proxy writes -> the tensor cores' async proxy
+      named_bar_sync(2, 192);
+      if (ct == 0) mbar_arrive(&conv[s]);
+    }
+  };
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol_w = WAM_GEMM_WEIGHT_EVICT_FIRST ? policy_evict_first() : policy_evict_last();
@@ -447,6 +492,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       umma_commit(accum);
     }
+  } else if (warp >= 6) {
+    if (q8) q8_convert_stages(threadIdx.x - 64);
   } else {
     // Epilogue warps 2..5. Per-feature bias / gate of this tile go to shared
     // memory while the mainloop runs.
@@ -458,42 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       gate_s[j] = (args.gate && n < args.n) ? args.gate[n] : 0.0f;
     }
     named_bar_sync(1, 128);
-    if (q8) {
-      // Q8_0 -> BF16 for every stage of the mainloop: 8 weights (one 16-byte
-      // swizzled chunk of the UMMA operand) per thread and step; value = q * d
-      // (exact in F32) rounded to BF16.
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait(&full[s], ph)) {
-          atomicCAS(args.error, 0u, static_cast<unsigned>(kErrMmaTimeout));
-          break;
-        }
-        const uint8_t* raw = smem_q8 + s * kQ8TileBytes;
-        uint8_t* wst = smem_w + s * kBBytes;
-#pragma unroll 4
-        for (int it = et; it < kWN * 8; it += 128) {
-          const int r = it >> 3, c = it & 7;
-          const uint2 qv = *reinterpret_cast<const uint2*>(raw + r * 64 + c * 8);
-          const __half dh = *reinterpret_cast<const __half*>(raw + 16384 + r * 4 + (c >> 2) * 2);
-          const float d = __half2float(dh);
-          const uint32_t qw[2] = {qv.x, qv.y};
-          uint32_t o[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int b0 = static_cast<int8_t>((qw[j >> 1] >> (16 * (j & 1))) & 0xFF);
-            const int b1 = static_cast<int8_t>((qw[j >> 1] >> (16 * (j & 1) + 8)) & 0xFF);
-            const __nv_bfloat162 h = __floats2bfloat162_rn(static_cast<float>(b0) * d,
-                                                           static_cast<float>(b1) * d);
-            o[j] = *reinterpret_cast<const uint32_t*>(&h);
-          }
-          *reinterpret_cast<uint4*>(wst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-        fence_proxy_async_smem();  // generic-proxy writes -> the tensor cores' async proxy
-        named_bar_sync(1, 128);
-        if (et == 0) mbar_arrive(&conv[s]);
-      }
-    }
+    if (q8) q8_convert_stages(threadIdx.x - 64);
     ok = mbar_wait(accum, 0);
     if (!ok) atomicCAS(args.error, 0u, static_cast<unsigned>(kErrEpilogueTimeout));
     tc_fence_after();
@@ -658,7 +670,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (cluster_mode) {
     // All partial tiles of this output tile are in the cluster's shared memory.
     cluster_sync_all();
-    if (warp >= 2) {
+    if (warp >= 2 && warp < 6) {
       const int et = threadIdx.x - 64;
       const int sp_n = args.splits;
       const int items = rows * (kWN / 8);

@@ -102,6 +102,8 @@ int gemm_weight_tile_rows();
 constexpr int kQ8TileBytes = 256 * 64 + 256 * 2 * 2;
 // BF16 weights (n_elems % 32 == 0) -> GGML Q8_0 blocks (34 bytes per 32).
 void launch_q8_quantize(const bf16* w, long long n_elems, uint8_t* out, cudaStream_t s);
+// Q8_0 blocks -> BF16 (q * d rounded to BF16), n_elems values.
+void launch_q8_dequantize(const uint8_t* blocks, long long n_elems, bf16* w, cudaStream_t s);
 // Row-major Q8_0 blocks of an [n][k] weight (n % 256 == 0, k % 64 == 0) ->
 // GEMM tiles [n/256][k/64][kQ8TileBytes].
 void launch_q8_retile(const uint8_t* src, uint8_t* dst, int n, int k, cudaStream_t s);

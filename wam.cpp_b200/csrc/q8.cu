@@ -70,6 +70,19 @@ __global__ void q8_retile_kernel(const uint8_t* __restrict__ src, uint8_t* __res
   }
 }
 
+// One thread per weight: value = q * d (exact in F32), rounded to BF16.
+__global__ void q8_dequantize_kernel(const uint8_t* __restrict__ blocks, long long n,
+                                     bf16* __restrict__ w) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const uint8_t* blk = blocks + (i / kQ8Block) * kQ8Bytes;
+    const unsigned short hb = static_cast<unsigned short>(blk[0] | (blk[1] << 8));
+    const float d = __half2float(__ushort_as_half(hb));
+    const int q = static_cast<int8_t>(blk[2 + (i % kQ8Block)]);
+    w[i] = __float2bfloat16_rn(static_cast<float>(q) * d);
+  }
+}
+
 int grid_for(long long n, int threads) {
   long long g = (n + threads - 1) / threads;
   if (g > 148 * 32) g = 148 * 32;
@@ -82,6 +95,10 @@ int grid_for(long long n, int threads) {
 void launch_q8_quantize(const bf16* w, long long n_elems, uint8_t* out, cudaStream_t s) {
   const long long blocks = n_elems / kQ8Block;
   q8_quantize_kernel<<<grid_for(blocks * 32, 256), 256, 0, s>>>(w, blocks, out);
+}
+
+void launch_q8_dequantize(const uint8_t* blocks, long long n_elems, bf16* w, cudaStream_t s) {
+  q8_dequantize_kernel<<<grid_for(n_elems, 256), 256, 0, s>>>(blocks, n_elems, w);
 }
 
 void launch_q8_retile(const uint8_t* src, uint8_t* dst, int n, int k, cudaStream_t s) {

@@ -21,7 +21,8 @@ class Options(C.Structure):
     _fields_ = [("struct_size", C.c_uint32), ("artifact_path", C.c_char_p),
                 ("synthetic_geometry", Geometry), ("synthetic_seed", C.c_uint64),
                 ("synthetic_bias_scale", C.c_float), ("device_index", C.c_int),
-                ("max_batch", C.c_int), ("use_cuda_graphs", C.c_int), ("prompt_cache", C.c_int)]
+                ("max_batch", C.c_int), ("use_cuda_graphs", C.c_int), ("prompt_cache", C.c_int),
+                ("weight_format", C.c_int)]
 
 
 class Request(C.Structure):

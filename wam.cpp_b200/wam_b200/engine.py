@@ -59,7 +59,7 @@ def _f32(a):
 class Engine:
     def __init__(self, geometry=None, seed: int = 0, artifact: str | None = None,
                  bias_scale: float = 0.0, device: int = 0, max_batch: int = 1,
-                 graphs: bool = True, prompt_cache: bool = True):
+                 graphs: bool = True, prompt_cache: bool = True, weights: str = "bf16"):
         self.lib = load()
         o = Options()
         o.struct_size = C.sizeof(Options)
@@ -72,6 +72,9 @@ class Engine:
         o.max_batch = max_batch
         o.use_cuda_graphs = 1 if graphs else 0
         o.prompt_cache = 1 if prompt_cache else 0
+        if weights not in ("bf16", "q8_0"):
+            raise ValueError("weights must be 'bf16' or 'q8_0'")
+        o.weight_format = 1 if weights == "q8_0" else 0
         h = C.c_void_p()
         st = Status()
         _raise(self.lib, self.lib.wam_b200_create(C.byref(o), C.byref(h), C.byref(st)), st,
