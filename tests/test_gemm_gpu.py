@@ -35,6 +35,8 @@ SHAPES = [
     (10, 1024, 256),    # condition MLP over 10 timesteps
     (200, 640, 192),    # patch embedding K
     (768, 3072, 3072),  # prefix visual tokens
+    (768, 14336, 512),  # more tiles than SMs: persistent kernel
+    (3072, 1024, 256),  # batched denoise shape class: persistent, 24 token tiles
     (384, 1536, 1024),  # batch-8 denoise
     (1000, 512, 640),   # ragged M
 ]

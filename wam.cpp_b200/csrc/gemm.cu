@@ -307,6 +307,171 @@ __device__ __forceinline__ void copy_out(const GemmArgs& a, const uint8_t* stg, 
   }
 }
 
+// Persistent variant for GEMMs with more output tiles than SMs (prefix,
+// batched denoise; no split-K, BF16 weights): CTA c takes tiles c, c + grid,
+// ... The copy ring runs on across tiles, and two TMEM accumulators (2 x 256
+// columns) let the epilogue of one tile overlap the mainloop of the next; the
+// epilogue stores straight from registers (its time is hidden).
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_persistent_kernel(const __grid_constant__ CUtensorMap tm_w,
+                              const __grid_constant__ CUtensorMap tm_x,
+                              const __grid_constant__ GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int S = args.stages;
+  const uint32_t a_bytes = static_cast<uint32_t>(args.a_rows) * kBK * 2;
+  uint8_t* smem_a = smem;
+  uint8_t* smem_w = smem + S * a_bytes;
+  uint8_t* tail = smem_w + S * kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;   // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* bias_s = reinterpret_cast<float*>(tail + 256);
+  float* gate_s = bias_s + kWN;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int nkb = args.num_kb;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tm_w);
+    prefetch_tensormap(&tm_x);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 1);
+    }
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  griddep_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_w = WAM_GEMM_WEIGHT_EVICT_FIRST ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_x = policy_evict_last();
+      const uint32_t stage_tx = a_bytes + kBBytes;
+      int g = 0;  // stages issued so far
+      bool waited = false, good = true;
+      for (int t = blockIdx.x; t < tiles && good; t += gridDim.x) {
+        const int tile_m = t % args.tiles_m, tile_n = t / args.tiles_m;
+        const bf16* w_tiles =
+            args.w_tiled ? args.w_tiled + static_cast<size_t>(tile_n) * nkb * (kWN * kBK) : nullptr;
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % S;
+          if (g >= S && !mbar_wait(&empty[s], ((g / S) & 1) ^ 1)) {
+            atomicCAS(args.error, 0u, static_cast<unsigned>(kErrProducerTimeout));
+            good = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], stage_tx);
+          if (w_tiles)
+            bulk_load(smem_w + s * kBBytes, w_tiles + static_cast<size_t>(kb) * (kWN * kBK),
+                      kBBytes, &full[s], pol_w);
+          else
+            tma_load_2d(smem_w + s * kBBytes, &tm_w, &full[s], kb * kBK, tile_n * kWN, pol_w);
+          if (!waited) {  // weights first; the tokens come from the preceding kernel
+            griddep_wait();
+            waited = true;
+          }
+          tma_load_2d(smem_a + s * a_bytes, &tm_x, &full[s], kb * kBK, tile_m * kTM, pol_x);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kTM, kWN);
+      int g = 0, j = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(&acc_empty[b], ((j >> 1) - 1) & 1)) {
+          atomicCAS(args.error, 0u, static_cast<unsigned>(kErrMmaTimeout));
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem_base + static_cast<uint32_t>(b * kWN);
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % S;
+          if (!mbar_wait(&full[s], (g / S) & 1)) {
+            atomicCAS(args.error, 0u, static_cast<unsigned>(kErrMmaTimeout));
+            kb = nkb;
+            t = tiles;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sw128_kmajor_desc(smem_u32(smem_a + s * a_bytes));
+          const uint64_t db = sw128_kmajor_desc(smem_u32(smem_w + s * kBBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_bf16_ss(acc, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[b]);
+      }
+    }
+  } else if (warp < 6) {
+    griddep_wait();
+    const int et = threadIdx.x - 64;
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    int j = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+      const int b = j & 1;
+      const int tile_m = t % args.tiles_m, tile_n = t / args.tiles_m;
+      const int m_base = tile_m * kTM, n_base = tile_n * kWN;
+      const int rows = args.m - m_base < kTM ? args.m - m_base : kTM;
+      named_bar_sync(1, 128);  // the previous tile's bias / gate are no longer read
+      for (int jj = et; jj < kWN; jj += 128) {
+        const int n = n_base + jj;
+        bias_s[jj] = (args.bias && n < args.n) ? __bfloat162float(args.bias[n]) : 0.0f;
+        gate_s[jj] = (args.gate && n < args.n) ? args.gate[n] : 0.0f;
+      }
+      named_bar_sync(1, 128);
+      const bool ok = mbar_wait(&acc_full[b], (j >> 1) & 1);
+      if (!ok) atomicCAS(args.error, 0u, static_cast<unsigned>(kErrEpilogueTimeout));
+      tc_fence_after();
+      if (q * 32 < rows) {
+        const uint32_t taddr =
+            tmem_base + static_cast<uint32_t>(b * kWN) + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+        for (int c = 0; c < kWN; c += 16) {
+          uint32_t r[16];
+          tmem_ld_x16(taddr + c, r);
+          tmem_ld_wait();
+          if (ok && row < rows)
+            epi_run<16>(args, m_base + row, n_base + c, reinterpret_cast<const float*>(r),
+                        bias_s + c, gate_s + c);
+        }
+      }
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (et == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * kTmemCols);
+  }
+}
+
 // CTA x = (tile, split) with the split index fastest (one cluster = the splits
 // of one output tile) and the token tile next, so the CTAs that share a weight
 // tile run side by side and the weight tile is read from HBM once.
@@ -892,6 +1057,9 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   a.error = scratch.error;
   op->grid = tiles_m * tiles_n * splits;
   op->smem_bytes = smem_for(a_rows, w_q8);
+  // More than a wave of unsplit tiles: persistent CTAs (one per SM).
+  op->persistent = splits == 1 && !w_q8 && tiles_m * tiles_n > num_sms;
+  if (op->persistent) op->grid = num_sms;
   return nullptr;
 }
 
@@ -906,6 +1074,9 @@ cudaError_t gemm_init(int device) {
   const int smem = kStageBudget + 1024 + kSmemTail;  // every stage count stays within the budget
   cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        smem);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(gemm_tc_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           smem);
   if (e != cudaSuccess) return e;
   int sms = 0;
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
@@ -952,6 +1123,7 @@ cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
+  if (op.persistent) return cudaLaunchKernelEx(&cfg, gemm_tc_persistent_kernel, op.tm_w, op.tm_x, op.args);
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, op.tm_w, op.tm_x, op.args);
 }
 

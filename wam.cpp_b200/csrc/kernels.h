@@ -80,6 +80,7 @@ struct GemmOp {
   CUtensorMap tm_x;
   GemmArgs args;
   int grid = 0;
+  bool persistent = false;  // gemm_tc_persistent_kernel (tiles > SMs, no split-K)
   int smem_bytes = 0;
 };
 
