@@ -120,6 +120,14 @@ TINY = Geometry(hidden=256, layers=2, heads=2, ffn=512, action_hidden=256, actio
 SMALL = Geometry(hidden=512, layers=3, heads=4, ffn=1024, action_hidden=384, action_ffn=768,
                  grid_h=6, grid_w=8, vae_z=48, action_chunk=48, steps=4, prompt_tokens=64,
                  text_dim=256)
+# Action-expert widths that are multiples of 256 with the config-2 chunk of 48
+# tokens: the engine runs these denoise steps as its persistent step kernel.
+STEPK = Geometry(hidden=512, layers=3, heads=4, ffn=1024, action_hidden=512, action_ffn=1024,
+                 grid_h=4, grid_w=6, vae_z=16, action_chunk=48, steps=3, prompt_tokens=32,
+                 text_dim=256)
+WIDE = Geometry(hidden=1536, layers=2, heads=12, ffn=3072, action_hidden=1536, action_ffn=3072,
+                grid_h=4, grid_w=4, vae_z=16, action_chunk=48, steps=2, prompt_tokens=32,
+                text_dim=256)
 
 
 def tensor_specs(g: Geometry) -> list[tuple[str, tuple[int, ...]]]:

@@ -20,6 +20,8 @@ enum DeviceError : unsigned {
   kErrProducerTimeout = 1,
   kErrMmaTimeout = 2,
   kErrEpilogueTimeout = 3,
+  kErrStepPhaseTimeout = 4,  // step kernel: a grid phase counter never filled
+  kErrStepRingTimeout = 5,   // step kernel: the copy ring never drained
 };
 
 // Bound on any mbarrier wait, in SM clock cycles (~2 s at the B200's 1.965 GHz

@@ -18,7 +18,7 @@ from ._lib import load
 from ._lib_engine import GEOM_FIELDS, Geometry, OpProfile, Options, Request, Stats, Status
 
 KINDS = ("gemm", "attention", "layernorm", "qkv_scatter", "small_linear", "elementwise", "sync",
-         "l2_prefetch")
+         "l2_prefetch", "denoise_step")
 PHASES = ("prompt", "prefix", "denoise")
 
 
