@@ -367,10 +367,29 @@ bool MotEngine::load_weights(std::string* err) {
   resident_bytes_ += total;
   uint8_t* base = static_cast<uint8_t*>(warena_);
   size_t off = 0;
-  for (const auto& s : specs) {
-    w_[s.first] = reinterpret_cast<bf16*>(base + off);
-    wn_[s.first] = s.second;
-    off += (static_cast<size_t>(s.second) * 2 + 255) / 256 * 256;
+  // Arena order: each expert's prompt projections (ca.k and ca.vproj of every
+  // layer, weights then biases) come first and back to back, so that their
+  // re-tiled weights form one [layers * 2H][K] matrix (256-row tiles are the
+  // outermost dimension of the re-tiled layout) and the prompt projection of
+  // an expert runs as one GEMM; every other tensor follows in spec order.
+  std::unordered_map<std::string, int64_t> numel;
+  for (const auto& s : specs) numel[s.first] = s.second;
+  std::vector<std::string> order;
+  for (const char* x : {".a", ".v"})
+    for (const char* part : {".weight", ".bias"})
+      for (int l = 0; l < g_.layers; ++l)
+        for (const char* proj : {".ca.k", ".ca.vproj"})
+          order.push_back("gwp.blk." + std::to_string(l) + x + proj + part);
+  {
+    std::unordered_map<std::string, bool> first;
+    for (const auto& n : order) first[n] = true;
+    for (const auto& s : specs)
+      if (!first.count(s.first)) order.push_back(s.first);
+  }
+  for (const auto& name : order) {
+    w_[name] = reinterpret_cast<bf16*>(base + off);
+    wn_[name] = numel[name];
+    off += (static_cast<size_t>(numel[name]) * 2 + 255) / 256 * 256;
   }
   const int A = g_.action_dim;
   sq01_.resize(A);
@@ -555,6 +574,12 @@ bool MotEngine::alloc_buffers(std::string* err) {
   AL(v_prompt_, bf16, B * L * heads * Nt * 128);
   AL(k_vis_, bf16, B * L * heads * Nt * 128);
   AL(v_vis_, bf16, B * L * heads * Nt * 128);
+  {
+    // Prompt-projection output of up to 4 GB worth of layers at a time.
+    const size_t per_layer = B * Nt * 2 * H * sizeof(bf16);
+    pkv_layers_ = static_cast<int>(std::min<size_t>(L, std::max<size_t>(1, (4ull << 30) / per_layer)));
+    AL(pkv_, bf16, B * Nt * static_cast<size_t>(pkv_layers_) * 2 * H);
+  }
   AL(err_word_, unsigned, 1);
   // A split GEMM holds at most one wave of CTAs, each with a partial tile of
   // <= 128 tokens x 256 features: sms x 128 x 256 floats bound every plan.
@@ -698,17 +723,24 @@ bool MotEngine::gemm(Program& p, const bf16* x, int ldx, int m, const std::strin
   // per stage).
   const bool tiled = !q8 && !rowmajor_weights_ && n % gemm_weight_tile_rows() == 0 && k % 64 == 0;
   if (tiled && !ensure_tiled(wname, n, k, err)) return false;
+  const bf16* wsrc = q8 ? reinterpret_cast<const bf16*>(q8_tiles_[wname]) : w;
+  return add_gemm(p, x, ldx, m, wsrc, n, k, epi, b, gate, resid, ldr, out, ldo, tiled, q8, wname, err);
+}
+
+bool MotEngine::add_gemm(Program& p, const bf16* x, int ldx, int m, const bf16* wsrc, int n, int k,
+                         int epi, const bf16* b, const float* gate, const bf16* resid, int ldr,
+                         void* out, int ldo, bool tiled, bool q8, const std::string& label,
+                         std::string* err) {
   // Split-K partials go through this lane's workspace inside a cluster.
   GemmScratch sc;
   sc.workspace = gemm_ws_[p.lane];
   sc.workspace_floats = gemm_ws_floats_;
   sc.error = err_word_;
   GemmOp op;
-  const bf16* wsrc = q8 ? reinterpret_cast<const bf16*>(q8_tiles_[wname]) : w;
   const char* e =
       gemm_plan(&op, x, ldx, m, wsrc, n, k, epi, b, gate, resid, ldr, out, ldo, sc, sms_, 0, tiled, q8);
   if (e) {
-    *err = std::string(e) + " (" + wname + ")";
+    *err = std::string(e) + " (" + label + ")";
     return false;
   }
   const double extra = (epi == EPI_GATED_RES || epi == EPI_RES) ? 2.0 * m * n : 0.0;
@@ -924,11 +956,78 @@ bool MotEngine::build(int b, std::string* err) {
     G(pp, text_tmp_, E, b * Nt, "gwp.acond.text.1", E, E, EPI_BIAS, true, nullptr, nullptr, 0, text_a_, E);
     G(pp, prompt_bf_, D, b * Nt, "gwp.cond.text.0", H, D, EPI_BIAS_GELU_R, true, nullptr, nullptr, 0, text_tmp_, H);
     G(pp, text_tmp_, H, b * Nt, "gwp.cond.text.1", H, H, EPI_BIAS, true, nullptr, nullptr, 0, text_v_, H);
-    for (int l = 0; l < L && ok; ++l) {
-      const std::string ap = "gwp.blk." + std::to_string(l) + ".a";
-      const std::string vp = "gwp.blk." + std::to_string(l) + ".v";
-      prompt_kv(pp, text_a_, E, ap, k_prompt_ + l * prL, v_prompt_ + l * prL);
-      prompt_kv(pp, text_v_, H, vp, k_vis_ + l * prL, v_vis_ + l * prL);
+    // An expert's ca.k / ca.vproj weights of all layers are one re-tiled
+    // [L * 2H][tw] matrix (arena order, load_weights): the projection of the
+    // prompt into every layer's K | V runs as one GEMM per chunk of
+    // pkv_layers_ layers, then a norm / scatter per layer.
+    auto pkv_block = [&](const char* xs, int tw, const bf16** wb, const bf16** bb) {
+      const std::string p0 = std::string("gwp.blk.0") + xs;
+      const bf16* w0 = W(p0 + ".ca.k.weight", static_cast<int64_t>(H) * tw);
+      const bf16* b0 = W(p0 + ".ca.k.bias", H);
+      if (!w0 || !b0) return false;
+      for (int l = 0; l < L; ++l)
+        for (int j = 0; j < 2; ++j) {
+          const std::string nm = "gwp.blk." + std::to_string(l) + xs + (j ? ".ca.vproj" : ".ca.k");
+          const size_t idx = static_cast<size_t>(2 * l + j);
+          if (W(nm + ".weight", static_cast<int64_t>(H) * tw) != w0 + idx * H * tw ||
+              W(nm + ".bias", H) != b0 + idx * H)
+            return false;
+        }
+      *wb = w0;
+      *bb = b0;
+      return true;
+    };
+    const bf16 *pw[2] = {nullptr, nullptr}, *pb[2] = {nullptr, nullptr};
+    const bool pkv_ok = pkv_ && !rowmajor_weights_ && H % 256 == 0 && E % 64 == 0 &&
+                        pkv_block(".a", E, &pw[0], &pb[0]) && pkv_block(".v", H, &pw[1], &pb[1]);
+    if (pkv_ok) {
+      for (int x = 0; x < 2 && ok; ++x) {
+        const bf16* text = x ? text_v_ : text_a_;
+        const int tw = x ? H : E;
+        const char* xs = x ? ".v" : ".a";
+        for (int l0 = 0; l0 < L && ok; l0 += pkv_layers_) {
+          const int l1 = std::min(L, l0 + pkv_layers_), nl = l1 - l0;
+          for (int l = l0; l < l1 && ok; ++l)
+            for (const char* proj : {".ca.k", ".ca.vproj"})
+              if (!ensure_tiled("gwp.blk." + std::to_string(l) + xs + proj, H, tw, &e2)) ok = false;
+          if (ok && !add_gemm(pp, text, tw, b * Nt, pw[x] + static_cast<size_t>(l0) * 2 * H * tw,
+                              nl * 2 * H, tw, EPI_BIAS, pb[x] + static_cast<size_t>(l0) * 2 * H,
+                              nullptr, nullptr, 0, pkv_, nl * 2 * H, true, false,
+                              std::string("prompt projection") + xs, &e2))
+            ok = false;
+          for (int l = l0; l < l1 && ok; ++l) {
+            const std::string pfx = "gwp.blk." + std::to_string(l) + xs;
+            QkvScatter q{};
+            q.src = pkv_ + static_cast<size_t>(l - l0) * 2 * H;
+            q.ld_src = nl * 2 * H;
+            q.rows = b * Nt;
+            q.rows_per_seq = Nt;
+            q.hidden = H;
+            q.heads = heads;
+            q.q_col = -1;
+            q.k_col = 0;
+            q.v_col = H;
+            q.k_norm = W(pfx + ".ca.kn.weight", H);
+            q.eps = eps;
+            q.k_out = (x ? k_vis_ : k_prompt_) + l * prL;
+            q.v_out = (x ? v_vis_ : v_prompt_) + l * prL;
+            q.kv_seq_stride = prB;
+            q.kv_head_stride = static_cast<long long>(Nt) * 128;
+            if (!q.k_norm) {
+              ok = false;
+              e2 = "missing " + pfx + ".ca.kn";
+            }
+            scatter(pp, q);
+          }
+        }
+      }
+    } else {
+      for (int l = 0; l < L && ok; ++l) {
+        const std::string ap = "gwp.blk." + std::to_string(l) + ".a";
+        const std::string vp = "gwp.blk." + std::to_string(l) + ".v";
+        prompt_kv(pp, text_a_, E, ap, k_prompt_ + l * prL, v_prompt_ + l * prL);
+        prompt_kv(pp, text_v_, H, vp, k_vis_ + l * prL, v_vis_ + l * prL);
+      }
     }
 
     // ---------------- prefix (cache.cpp:139-485)

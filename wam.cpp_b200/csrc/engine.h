@@ -147,6 +147,10 @@ class MotEngine {
   bool gemm(Program& p, const bf16* x, int ldx, int m, const std::string& wname, int n, int k,
             int epi, bool bias, const float* gate, const bf16* resid, int ldr, void* out, int ldo,
             std::string* err);
+  // Plans one GEMM on prepared weights (re-tiled, Q8_0 tiles or row-major).
+  bool add_gemm(Program& p, const bf16* x, int ldx, int m, const bf16* wsrc, int n, int k, int epi,
+                const bf16* bias, const float* gate, const bf16* resid, int ldr, void* out, int ldo,
+                bool tiled, bool q8, const std::string& label, std::string* err);
   // Re-tiles a GEMM weight in place into 32 KB UMMA tiles (once).
   bool ensure_tiled(const std::string& wname, int n, int k, std::string* err);
   // Whether the denoise step of `batch` requests runs as the persistent step
@@ -219,6 +223,10 @@ class MotEngine {
   bf16 *k_self_ = nullptr, *v_self_ = nullptr;      // [B][L][heads][P+T][128]
   bf16 *k_prompt_ = nullptr, *v_prompt_ = nullptr;  // [B][L][heads][Nt][128] (action expert)
   bf16 *k_vis_ = nullptr, *v_vis_ = nullptr;        // [B][L][heads][Nt][128] (visual expert)
+  // Prompt projection of a chunk of layers, [B * Nt][pkv_layers * 2H] (K | V of
+  // each layer), when an expert's ca.k / ca.vproj weights form one matrix.
+  bf16* pkv_ = nullptr;
+  int pkv_layers_ = 0;
   // Split-K exchange workspace, one per lane (the lanes' GEMMs may overlap).
   float* gemm_ws_[2] = {nullptr, nullptr};
   size_t gemm_ws_floats_ = 0;
