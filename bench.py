@@ -303,6 +303,57 @@ def run_op_case(args) -> None:
                       "algorithmic_bytes": algo, "GB/s": round(algo / us / 1e3, 1)}))
 
 
+def run_attention_bench(args) -> None:
+    """BF16 flash attention of 48 action + 768 video queries
+    over cached K/V of 1280 / 4096 / 16384 keys, 24 heads x 128, batch 1 / 8 /
+    64, Q, K, V ~ N(0, 1) (seeded; RoPE is applied before the kernel, so the
+    kernel's inputs are plain Q / K / V). Each point replays `--steps` launches
+    in a CUDA graph after `--warmup` untimed ones; prints one JSON line."""
+    import torch
+    from wam_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pk = peaks()
+    lq, heads = 48 + 768, 24
+    points = []
+    for lk in (1280, 4096, 16384):
+        for B in (1, 8, 64):
+            gen = torch.Generator(device=dev).manual_seed(SEED + lk + B)
+            q = torch.randn(B, heads, lq, 128, generator=gen, device=dev).to(torch.bfloat16)
+            k = torch.randn(B, heads, lk, 128, generator=gen, device=dev).to(torch.bfloat16)
+            v = torch.randn(B, heads, lk, 128, generator=gen, device=dev).to(torch.bfloat16)
+            o = torch.empty(B * lq, heads * 128, dtype=torch.bfloat16, device=dev)
+            stream = torch.cuda.Stream()
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    ops.attention(q, k, v, out=o)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(args.steps):
+                    ops.attention(q, k, v, out=o)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                e0.record()
+                graph.replay()
+                e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / args.steps
+            flops = 4.0 * B * heads * lq * lk * 128
+            byts = 2.0 * B * heads * (2 * lq + 2 * lk) * 128
+            points.append({"cache": lk, "batch": B, "avg_us": round(us, 2),
+                           "TFLOP/s": round(flops / us / 1e6, 1),
+                           "frac_of_bf16_peak": round(flops / us / 1e6 / pk["bf16_tflops"], 3),
+                           "GB/s": round(byts / us / 1e3, 1)})
+            del q, k, v, o, graph
+            torch.cuda.empty_cache()
+    print(json.dumps({"bench": "config3 attention microbench (attention_kernel, mma.sync BF16)",
+                      "queries": lq, "heads": heads, "steps": args.steps, "warmup": args.warmup,
+                      "peak_tflops": pk["bf16_tflops"], "peak_source": pk["source"],
+                      "points": points}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -317,9 +368,14 @@ def main() -> None:
     ap.add_argument("--op-case", default=None,
                     help="gemm:M,N,K or attention:LQ,LK,HEADS: run one kernel on a small case "
                          "(for ncu captures) and print its event timing instead of the bench line")
+    ap.add_argument("--attention-bench", action="store_true",
+                    help="BASELINE config 3: the attention microbench over cache length and batch")
     args = ap.parse_args()
     if args.op_case:
         run_op_case(args)
+        return
+    if args.attention_bench:
+        run_attention_bench(args)
         return
     if args.impl == "reference":
         run_reference(args)

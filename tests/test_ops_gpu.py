@@ -33,6 +33,8 @@ def torch_attention(q, k, v, scale):
     (2, 3, 1, 64),         # state token cross-attention
     (3, 2, 100, 1280),     # ragged queries, microbench cache length
     (1, 2, 816, 4096),     # microbench: 48 + 768 queries over a 4096 cache
+    (8, 24, 816, 1280),    # config 3: batch 8 over the 1280-key cache, 24 heads
+    (1, 24, 816, 16384),   # config 3: the 16384-key cache, 24 heads
 ])
 def test_attention_vs_torch(cuda_device, B, heads, lq, lk):
     from wam_b200 import ops
