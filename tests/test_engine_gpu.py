@@ -39,7 +39,7 @@ def _req(geom, seed):
     return r, Req(r.state, r.latent, r.prompt, r.noise)
 
 
-@pytest.mark.parametrize("geom_name", ["TINY", "SMALL"])
+@pytest.mark.parametrize("geom_name", ["TINY", "SMALL", "TALL"])
 def test_engine_matches_oracle(cuda_device, geom_name):
     from oracle import synth
 

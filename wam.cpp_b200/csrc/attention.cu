@@ -353,6 +353,7 @@ cudaError_t attention_init() {
   cudaError_t e = cudaFuncSetAttribute(attention_kernel<false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
+  if ((e = attention_tc_init()) != cudaSuccess) return e;
   return cudaFuncSetAttribute(attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               kSmem);
 }
@@ -380,6 +381,7 @@ size_t attention_ws_floats(const AttnArgs& a) {
 }
 
 void launch_attention(const AttnArgs& a_in, cudaStream_t s) {
+  if (attention_tc_eligible(a_in) && launch_attention_tc(a_in, s) == cudaSuccess) return;
   AttnArgs a = a_in;
   static int sms = 0;
   if (!sms) {

@@ -1,0 +1,435 @@
+// tcgen05 flash attention for query blocks of 128 rows: the prefix joint
+// self-attention and visual cross-attention (769 / 768 queries) and the
+// attention microbench (816 queries over 1280-16384 cached keys).
+//
+// One CTA = 128 query rows of one (sequence, head); keys stream in tiles of
+// 128. Both products run on the tensor cores with accumulators in TMEM:
+// S = Q K^T (M = 128 queries, N = 128 keys, K = 128 dims) into one of two S
+// buffers, O += P V^T (M = 128 queries, N = 128 dims, K = 128 keys) into O.
+// Roles (192 threads): warp 0 issues the TMA copies (4-D boxes of 128 rows x
+// 64 dims with the 128-byte swizzle; rows past the end are zero-filled),
+// warp 1 owns TMEM and issues the MMAs (S of tile j + 1 before P V of tile j,
+// so the tensor core runs while the softmax works), warps 2-5 = one thread
+// per query row: softmax from S in TMEM, P as BF16 into a K-major tile, V
+// transposed to K-major in shared memory (ldmatrix.trans / stmatrix), lazy
+// rescaling of O in TMEM (only when the running max grows by more than 2^8),
+// and the final normalised BF16 rows. All operands use the K-major swizzled
+// layout of the GEMM (csrc/gemm.cu).
+//
+// Arithmetic as attention.cu's kernel: F32 scores, softmax(scale * S) with an
+// online max, probabilities rounded to BF16 for P V, F32 accumulation, BF16
+// output. Reference: the prefix attention (src/models/gwp05/engine/cache.cpp:274-287),
+// the cached cross attention (mot.cpp:299-321) and ggml_soft_max_ext with scale
+// 1/sqrt(128) at GGML_PREC_F32 (mot.cpp:432-446).
+#include <cmath>
+#include <cstdlib>
+#include <mutex>
+
+#include "kernels.h"
+#include "launch.cuh"
+#include "ptx.cuh"
+
+namespace wamb {
+
+namespace {
+
+constexpr int kThreads = 192;             // warp 0 copies, 1 MMA, 2-5 softmax
+constexpr int kRows = 128;                // queries per CTA (UMMA M, TMEM lanes)
+constexpr int kKeys = 128;                // keys per tile
+constexpr int kHalf = 128 * 64 * 2;       // 128 rows x 64 dims (or keys), swizzled: 16 KB
+constexpr int kTile = 2 * kHalf;          // 32 KB
+constexpr int kOffQ = 0;                  // Q [2 halves of dims]
+constexpr int kOffK = kTile;              // K ring [2][2 halves]
+constexpr int kOffV = 3 * kTile;          // V staging [2 halves of dims], rows = keys
+constexpr int kOffVt = 4 * kTile;         // V^T [2 halves of keys], rows = dims
+constexpr int kOffP = 5 * kTile;          // P [2 halves of keys], rows = queries
+constexpr int kOffBar = 6 * kTile;
+constexpr int kSmem = 6 * kTile + 256 + 1024;
+constexpr uint32_t kTmemCols = 512;       // S[0], S[1], O (128 columns each)
+
+__device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+
+__device__ __forceinline__ void fail(const AttnArgs& a, unsigned code) {
+  if (a.error) atomicCAS(a.error, 0u, code);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sq = smem + kOffQ;
+  uint8_t* sk = smem + kOffK;
+  uint8_t* sv = smem + kOffV;
+  uint8_t* svt = smem + kOffVt;
+  uint8_t* sp = smem + kOffP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 6;
+  uint64_t* s_full = bars + 7;   // [2]
+  uint64_t* s_free = bars + 9;   // [2]
+  uint64_t* p_full = bars + 11;
+  uint64_t* pv_done = bars + 12;
+  uint64_t* o_full = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * kRows, head = blockIdx.y, seq = blockIdx.z;
+  const int nk = (a.lk + kKeys - 1) / kKeys;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tm_q);
+    prefetch_tensormap(&tm_k);
+    prefetch_tensormap(&tm_v);
+    for (int i = 0; i < 14; ++i) mbar_init(&bars[i], 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s[2] = {tmem, tmem + 128};
+  const uint32_t t_o = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------- copy producer
+      const uint64_t pol_kv = policy_evict_last();  // K / V are read by every query tile of the head
+      const uint64_t pol_q = policy_evict_first();
+      auto load_k = [&](int j) {
+        const int b = j & 1;
+        mbar_arrive_expect_tx(&k_full[b], kTile);
+        tma_load_4d(sk + b * kTile, &tm_k, &k_full[b], 0, j * kKeys, head, seq, pol_kv);
+        tma_load_4d(sk + b * kTile + kHalf, &tm_k, &k_full[b], 64, j * kKeys, head, seq, pol_kv);
+      };
+      auto load_v = [&](int j) {
+        mbar_arrive_expect_tx(v_full, kTile);
+        tma_load_4d(sv, &tm_v, v_full, 0, j * kKeys, head, seq, pol_kv);
+        tma_load_4d(sv + kHalf, &tm_v, v_full, 64, j * kKeys, head, seq, pol_kv);
+      };
+      int nk_issued = 0, nv_issued = 0;
+      // K / V the preceding kernel does not write start before waiting for it.
+      if (nk > 0 && (a.lk < kKeys ? a.lk : kKeys) <= a.static_keys) {
+        load_k(0);
+        load_v(0);
+        nk_issued = nv_issued = 1;
+      }
+      griddep_wait();
+      griddep_launch_dependents();
+      mbar_arrive_expect_tx(q_full, kTile);
+      tma_load_4d(sq, &tm_q, q_full, 0, q0, head, seq, pol_q);
+      tma_load_4d(sq + kHalf, &tm_q, q_full, 64, q0, head, seq, pol_q);
+      bool ok = true;
+      for (int j = 0; j < nk && ok; ++j) {
+        if (j >= nk_issued) {
+          if (j >= 2 && !mbar_wait(&k_empty[j & 1], ((j >> 1) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          load_k(j);
+          nk_issued = j + 1;
+        }
+        if (j >= nv_issued) {
+          if (j >= 1 && !mbar_wait(v_empty, (j - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          load_v(j);
+          nv_issued = j + 1;
+        }
+      }
+      if (!ok) fail(a, kErrProducerTimeout);
+      // Every issued copy lands before the CTA leaves.
+      mbar_wait(q_full, 0);
+      for (int j = nk_issued - 2 > 0 ? nk_issued - 2 : 0; j < nk_issued; ++j)
+        mbar_wait(&k_full[j & 1], (j >> 1) & 1);
+      if (nv_issued > 0) mbar_wait(v_full, (nv_issued - 1) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc = umma_idesc_bf16(kRows, kKeys);
+      bool ok = mbar_wait(q_full, 0);
+      for (int j = 0; j <= nk && ok; ++j) {
+        if (j < nk) {
+          const int b = j & 1;
+          if (!mbar_wait(&k_full[b], (j >> 1) & 1) ||
+              (j >= 2 && !mbar_wait(&s_free[b], ((j >> 1) - 1) & 1))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint64_t da = sw128_kmajor_desc(smem_u32(sq + c * kHalf));
+            const uint64_t db = sw128_kmajor_desc(smem_u32(sk + b * kTile + c * kHalf));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16_ss(t_s[b], da + 2 * kk, db + 2 * kk, idesc, (c | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[b]);
+          umma_commit(&k_empty[b]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1;
+          if (!mbar_wait(p_full, jj & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint64_t da = sw128_kmajor_desc(smem_u32(sp + c * kHalf));
+            const uint64_t db = sw128_kmajor_desc(smem_u32(svt + c * kHalf));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16_ss(t_o, da + 2 * kk, db + 2 * kk, idesc, (jj > 0 || c != 0 || kk != 0) ? 1u : 0u);
+          }
+          umma_commit(pv_done);
+        }
+      }
+      if (!ok) fail(a, kErrMmaTimeout);
+      umma_commit(o_full);  // arrives once every MMA issued above has completed
+      mbar_wait(o_full, 0);
+    }
+  } else {
+    // ----------------------------------------- softmax / P / V^T / output
+    const int wt = threadIdx.x - 64;
+    const int qd = warp & 3;  // TMEM lane quadrant
+    const int row = qd * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
+    const float sl2 = a.scale * 1.4426950408889634f;
+    float m_used = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nk; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int valid = a.lk - j * kKeys < kKeys ? a.lk - j * kKeys : kKeys;
+      // pass 1: the tile's row max over valid keys
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kKeys; c += 32) {
+        uint32_t r[32];
+        tmem_ld_x32(t_s[b] + lane_off + c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c + i < valid) mt = fmaxf(mt, u2f(r[i]));
+      }
+      const float m_new = fmaxf(m_used, mt);
+      const bool rescale = j == 0 || (m_new - m_used) * sl2 > 8.0f;
+      const float mb = (rescale ? m_new : m_used) * sl2;
+      // pass 2: probabilities relative to the max in use, BF16-packed
+      uint32_t pk[kKeys / 2];
+      float ls = 0.0f;
+#pragma unroll
+      for (int c = 0; c < kKeys; c += 32) {
+        uint32_t r[32];
+        tmem_ld_x32(t_s[b] + lane_off + c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = c + i < valid ? exp2f(u2f(r[i]) * sl2 - mb) : 0.0f;
+          const float p1 = c + i + 1 < valid ? exp2f(u2f(r[i + 1]) * sl2 - mb) : 0.0f;
+          ls += p0 + p1;
+          pk[(c + i) >> 1] = pack_bf16(p0, p1);
+        }
+      }
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (wt == 0) mbar_arrive(&s_free[b]);
+      // P, V^T and O are free once the previous tile's P V has completed.
+      if (j >= 1 && !mbar_wait(pv_done, (j - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (rescale && j > 0) {
+        const float corr = exp2f((m_used - m_new) * sl2);
+#pragma unroll 1
+        for (int c = 0; c < kRows; c += 32) {
+          uint32_t r[32];
+          tmem_ld_x32(t_o + lane_off + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(u2f(r[i]) * corr);
+          tmem_st_x32(t_o + lane_off + c, r);
+        }
+        tmem_st_wait();
+        l *= corr;
+      }
+      if (rescale) m_used = m_new;
+      l += ls;
+      // V tile j -> V^T (K-major over keys): each warp transposes 4 key groups
+      // x 16 dim groups of 8 x 8 blocks.
+      if (!mbar_wait(v_full, j & 1)) {
+        ok = false;
+        break;
+      }
+      {
+        const int m = lane >> 3, i8 = lane & 7;
+#pragma unroll
+        for (int kgi = 0; kgi < 4; ++kgi) {
+          const int kg = (wt >> 5) * 4 + kgi;
+          const int key = 8 * kg + i8;
+#pragma unroll
+          for (int dq = 0; dq < 16; dq += 4) {
+            const int dg = dq + m;
+            const uint32_t src = smem_u32(sv) + (dg >> 3) * kHalf + key * 128 +
+                                 ((((dg & 7) ^ (key & 7))) << 4);
+            uint32_t r0, r1, r2, r3;
+            ldmatrix_x4_trans(src, r0, r1, r2, r3);
+            const int dr = 8 * dg + i8;  // row i8 of destination matrix m
+            const uint32_t dst = smem_u32(svt) + (kg >> 3) * kHalf + dr * 128 +
+                                 ((((kg & 7) ^ (dr & 7))) << 4);
+            stmatrix_x4(dst, r0, r1, r2, r3);
+          }
+        }
+      }
+      // P row -> K-major tile over keys
+#pragma unroll
+      for (int kc = 0; kc < kKeys / 8; ++kc) {
+        const uint32_t off = (kc >> 3) * kHalf + row * 128 + (((kc & 7) ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(sp + off) =
+            make_uint4(pk[kc * 4], pk[kc * 4 + 1], pk[kc * 4 + 2], pk[kc * 4 + 3]);
+      }
+      fence_proxy_async_smem();  // P and V^T (generic stores) are read by the tensor core
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (wt == 0) {
+        mbar_arrive(v_empty);
+        mbar_arrive(p_full);
+      }
+    }
+    if (!ok) fail(a, kErrEpilogueTimeout);
+    if (ok && mbar_wait(o_full, 0)) {
+      tc_fence_after();
+      const int qr = q0 + row;
+      bf16* dst = nullptr;
+      if (qr < a.lq) {
+        if (a.split_first) {
+          dst = qr == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
+                        : a.out + (static_cast<long long>(seq) * (a.lq - 1) + qr - 1) * a.ldo;
+        } else {
+          dst = a.out + (static_cast<long long>(seq) * a.lq + qr) * a.ldo;
+        }
+        dst += head * 128;
+      }
+      const float inv = 1.0f / l;
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t r[32];
+        tmem_ld_x32(t_o + lane_off + c, r);
+        tmem_ld_wait();
+        if (dst) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(dst + c + q * 8) =
+                make_uint4(pack_bf16(u2f(r[8 * q]) * inv, u2f(r[8 * q + 1]) * inv),
+                           pack_bf16(u2f(r[8 * q + 2]) * inv, u2f(r[8 * q + 3]) * inv),
+                           pack_bf16(u2f(r[8 * q + 4]) * inv, u2f(r[8 * q + 5]) * inv),
+                           pack_bf16(u2f(r[8 * q + 6]) * inv, u2f(r[8 * q + 7]) * inv));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// [batch][heads][rows][128] BF16 with the given strides (elements), boxes of
+// 128 rows x 64 dims with the 128-byte swizzle; rows past `rows` read as zero.
+bool encode_rows(CUtensorMap* m, const void* base, int rows, int heads, int batch,
+                 long long head_stride, long long seq_stride) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  if (batch == 1) seq_stride = head_stride * heads;
+  const cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(heads),
+                              static_cast<cuuint64_t>(batch)};
+  const cuuint64_t strides[3] = {256, static_cast<cuuint64_t>(head_stride) * 2,
+                                 static_cast<cuuint64_t>(seq_stride) * 2};
+  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool tc_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("WAM_B200_ATTN_TC");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+}  // namespace
+
+cudaError_t attention_tc_init() {
+  return cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+}
+
+bool attention_tc_eligible(const AttnArgs& a) {
+  return tc_enabled() && a.lq >= kRows && a.lk >= 1 &&
+         (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.k) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(a.v) & 15) == 0 && a.q_head_stride % 8 == 0 &&
+         a.q_seq_stride % 8 == 0 && a.kv_head_stride % 8 == 0 && a.kv_seq_stride % 8 == 0 &&
+         a.ldo % 8 == 0 && (!a.split_first || a.ldo_first % 8 == 0);
+}
+
+cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s) {
+  CUtensorMap mq, mk, mv;
+  if (!encode_rows(&mq, a.q, a.lq, a.heads, a.batch, a.q_head_stride, a.q_seq_stride) ||
+      !encode_rows(&mk, a.k, a.lk, a.heads, a.batch, a.kv_head_stride, a.kv_seq_stride) ||
+      !encode_rows(&mv, a.v, a.lk, a.heads, a.batch, a.kv_head_stride, a.kv_seq_stride))
+    return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.lq + kRows - 1) / kRows, a.heads, a.batch);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_tc_kernel, mq, mk, mv, a);
+}
+
+}  // namespace wamb

@@ -833,6 +833,7 @@ bool MotEngine::build(int b, std::string* err) {
       AttnArgs a = a_in;
       a.ws = gemm_ws_[p.lane];
       a.ws_floats = gemm_ws_floats_;
+      a.error = err_word_;
       const double bq = 2.0 * a.batch * a.heads * a.lq * 128.0;
       const double bkv = 4.0 * a.batch * a.heads * a.lk * 128.0;
       p.add([a](cudaStream_t s) {

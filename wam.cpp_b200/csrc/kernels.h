@@ -188,8 +188,14 @@ struct AttnArgs {
   // without it through distributed shared memory.
   float* ws = nullptr;
   size_t ws_floats = 0;
+  unsigned* error = nullptr;  // device error word for a wait that gave up (tcgen05 kernel)
 };
+// Picks the kernel: 128-query tcgen05 tiles (attention_tc.cu) for >= 128
+// queries, the mma.sync kernel below otherwise.
 void launch_attention(const AttnArgs& a, cudaStream_t s);
+cudaError_t attention_tc_init();
+bool attention_tc_eligible(const AttnArgs& a);
+cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s);
 // ------------------------------------------------ persistent denoise step
 // One grid runs every action-expert layer of one flow-matching step for up to
 // 128 tokens (step.cu). The step is a list of ops; each op waits for the one
