@@ -348,7 +348,7 @@ def run_attention_bench(args) -> None:
                            "GB/s": round(byts / us / 1e3, 1)})
             del q, k, v, o, graph
             torch.cuda.empty_cache()
-    print(json.dumps({"bench": "config3 attention microbench (attention_kernel, mma.sync BF16)",
+    print(json.dumps({"bench": "config3 attention microbench (launch_attention: tcgen05 kernel for >= 128 queries)",
                       "queries": lq, "heads": heads, "steps": args.steps, "warmup": args.warmup,
                       "peak_tflops": pk["bf16_tflops"], "peak_source": pk["source"],
                       "points": points}), flush=True)

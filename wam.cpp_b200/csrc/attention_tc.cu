@@ -6,11 +6,12 @@
 // 128. Both products run on the tensor cores with accumulators in TMEM:
 // S = Q K^T (M = 128 queries, N = 128 keys, K = 128 dims) into one of two S
 // buffers, O += P V^T (M = 128 queries, N = 128 dims, K = 128 keys) into O.
-// Roles (192 threads): warp 0 issues the TMA copies (4-D boxes of 128 rows x
+// Roles (320 threads): warp 0 issues the TMA copies (4-D boxes of 128 rows x
 // 64 dims with the 128-byte swizzle; rows past the end are zero-filled),
 // warp 1 owns TMEM and issues the MMAs (S of tile j + 1 before P V of tile j,
-// so the tensor core runs while the softmax works), warps 2-5 = one thread
-// per query row: softmax from S in TMEM, P as BF16 into a K-major tile, V
+// so the tensor core runs while the softmax works), warps 2-9 = two threads
+// per query row, each over half the keys / dims (the row max is exchanged
+// through shared memory): softmax from S in TMEM, P as BF16 into a K-major tile, V
 // transposed to K-major in shared memory (ldmatrix.trans / stmatrix), lazy
 // rescaling of O in TMEM (only when the running max grows by more than 2^8),
 // and the final normalised BF16 rows. All operands use the K-major swizzled
@@ -33,7 +34,7 @@ namespace wamb {
 
 namespace {
 
-constexpr int kThreads = 192;             // warp 0 copies, 1 MMA, 2-5 softmax
+constexpr int kThreads = 320;             // warp 0 copies, 1 MMA, 2-9 softmax (2 per row)
 constexpr int kRows = 128;                // queries per CTA (UMMA M, TMEM lanes)
 constexpr int kKeys = 128;                // keys per tile
 constexpr int kHalf = 128 * 64 * 2;       // 128 rows x 64 dims (or keys), swizzled: 16 KB
@@ -44,7 +45,8 @@ constexpr int kOffV = 3 * kTile;          // V staging [2 halves of dims], rows 
 constexpr int kOffVt = 4 * kTile;         // V^T [2 halves of keys], rows = dims
 constexpr int kOffP = 5 * kTile;          // P [2 halves of keys], rows = queries
 constexpr int kOffBar = 6 * kTile;
-constexpr int kSmem = 6 * kTile + 256 + 1024;
+constexpr int kOffXch = kOffBar + 256;    // row max / sum exchange between a row's two threads
+constexpr int kSmem = 6 * kTile + 256 + 1024 + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;       // S[0], S[1], O (128 columns each)
 
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
@@ -203,56 +205,70 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ----------------------------------------- softmax / P / V^T / output
+    // Two threads per query row (warps w and w + 4 share a TMEM lane
+    // quadrant); thread half h owns key columns and output dims 64h..64h+63.
     const int wt = threadIdx.x - 64;
     const int qd = warp & 3;  // TMEM lane quadrant
+    const int half = (warp - 2) >> 2;
     const int row = qd * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
+    const int c0 = half * 64;
+    float* xch = reinterpret_cast<float*>(smem + kOffXch);  // [2][128]
     const float sl2 = a.scale * 1.4426950408889634f;
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
       const int b = j & 1;
-      if (!mbar_wait(&s_full[b], (j >> 1) & 1)) {
-        ok = false;
-        break;
-      }
+      // Each wait's outcome is AND-ed over the 256 threads at the next named
+      // barrier, so they all leave the loop together (a thread giving up
+      // alone would strand the others at the barrier).
+      ok = mbar_wait(&s_full[b], (j >> 1) & 1);
       tc_fence_after();
       const int valid = a.lk - j * kKeys < kKeys ? a.lk - j * kKeys : kKeys;
-      // pass 1: the tile's row max over valid keys
+      // pass 1: row max over this thread's valid keys, combined with its partner
       float mt = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kKeys; c += 32) {
+      for (int c = 0; c < 64; c += 32) {
         uint32_t r[32];
-        tmem_ld_x32(t_s[b] + lane_off + c, r);
+        tmem_ld_x32(t_s[b] + lane_off + c0 + c, r);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          if (c + i < valid) mt = fmaxf(mt, u2f(r[i]));
+          if (c0 + c + i < valid) mt = fmaxf(mt, u2f(r[i]));
       }
+      xch[half * 128 + row] = mt;
+      if (!named_bar_and(1, 256, ok)) {
+        ok = false;
+        break;
+      }
+      mt = fmaxf(xch[row], xch[128 + row]);
       const float m_new = fmaxf(m_used, mt);
       const bool rescale = j == 0 || (m_new - m_used) * sl2 > 8.0f;
       const float mb = (rescale ? m_new : m_used) * sl2;
       // pass 2: probabilities relative to the max in use, BF16-packed
-      uint32_t pk[kKeys / 2];
+      uint32_t pk[32];
       float ls = 0.0f;
 #pragma unroll
-      for (int c = 0; c < kKeys; c += 32) {
+      for (int c = 0; c < 64; c += 32) {
         uint32_t r[32];
-        tmem_ld_x32(t_s[b] + lane_off + c, r);
+        tmem_ld_x32(t_s[b] + lane_off + c0 + c, r);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float p0 = c + i < valid ? exp2f(u2f(r[i]) * sl2 - mb) : 0.0f;
-          const float p1 = c + i + 1 < valid ? exp2f(u2f(r[i + 1]) * sl2 - mb) : 0.0f;
+          const int k = c0 + c + i;
+          const float p0 = k < valid ? exp2f(u2f(r[i]) * sl2 - mb) : 0.0f;
+          const float p1 = k + 1 < valid ? exp2f(u2f(r[i + 1]) * sl2 - mb) : 0.0f;
           ls += p0 + p1;
           pk[(c + i) >> 1] = pack_bf16(p0, p1);
         }
       }
       tc_fence_before();
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 256);
       if (wt == 0) mbar_arrive(&s_free[b]);
       // P, V^T and O are free once the previous tile's P V has completed.
-      if (j >= 1 && !mbar_wait(pv_done, (j - 1) & 1)) {
+      if (j >= 1) ok = mbar_wait(pv_done, (j - 1) & 1);
+      if (ok) ok = mbar_wait(v_full, j & 1);
+      if (!named_bar_and(1, 256, ok)) {
         ok = false;
         break;
       }
@@ -260,30 +276,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (rescale && j > 0) {
         const float corr = exp2f((m_used - m_new) * sl2);
 #pragma unroll 1
-        for (int c = 0; c < kRows; c += 32) {
+        for (int c = 0; c < 64; c += 32) {
           uint32_t r[32];
-          tmem_ld_x32(t_o + lane_off + c, r);
+          tmem_ld_x32(t_o + lane_off + c0 + c, r);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(u2f(r[i]) * corr);
-          tmem_st_x32(t_o + lane_off + c, r);
+          tmem_st_x32(t_o + lane_off + c0 + c, r);
         }
         tmem_st_wait();
         l *= corr;
       }
       if (rescale) m_used = m_new;
       l += ls;
-      // V tile j -> V^T (K-major over keys): each warp transposes 4 key groups
+      // V tile j -> V^T (K-major over keys): each warp transposes 2 key groups
       // x 16 dim groups of 8 x 8 blocks.
-      if (!mbar_wait(v_full, j & 1)) {
-        ok = false;
-        break;
-      }
       {
         const int m = lane >> 3, i8 = lane & 7;
 #pragma unroll
-        for (int kgi = 0; kgi < 4; ++kgi) {
-          const int kg = (wt >> 5) * 4 + kgi;
+        for (int kgi = 0; kgi < 2; ++kgi) {
+          const int kg = (wt >> 5) * 2 + kgi;
           const int key = 8 * kg + i8;
 #pragma unroll
           for (int dq = 0; dq < 16; dq += 4) {
@@ -299,23 +311,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // P row -> K-major tile over keys
+      // this thread's 64 keys of the P row -> K-major tile over keys
 #pragma unroll
-      for (int kc = 0; kc < kKeys / 8; ++kc) {
-        const uint32_t off = (kc >> 3) * kHalf + row * 128 + (((kc & 7) ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(sp + off) =
-            make_uint4(pk[kc * 4], pk[kc * 4 + 1], pk[kc * 4 + 2], pk[kc * 4 + 3]);
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t off = half * kHalf + row * 128 + ((i ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(sp + off) = make_uint4(pk[i * 4], pk[i * 4 + 1], pk[i * 4 + 2], pk[i * 4 + 3]);
       }
       fence_proxy_async_smem();  // P and V^T (generic stores) are read by the tensor core
       tc_fence_before();
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 256);
       if (wt == 0) {
         mbar_arrive(v_empty);
         mbar_arrive(p_full);
       }
     }
     if (!ok) fail(a, kErrEpilogueTimeout);
-    if (ok && mbar_wait(o_full, 0)) {
+    // row sum = both halves' sums
+    xch[half * 128 + row] = l;
+    named_bar_sync(1, 256);
+    l = xch[row] + xch[128 + row];
+    if (ok) ok = mbar_wait(o_full, 0);
+    if (named_bar_and(1, 256, ok)) {
       tc_fence_after();
       const int qr = q0 + row;
       bf16* dst = nullptr;
@@ -326,13 +342,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           dst = a.out + (static_cast<long long>(seq) * a.lq + qr) * a.ldo;
         }
-        dst += head * 128;
+        dst += head * 128 + c0;
       }
       const float inv = 1.0f / l;
 #pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
+      for (int c = 0; c < 64; c += 32) {
         uint32_t r[32];
-        tmem_ld_x32(t_o + lane_off + c, r);
+        tmem_ld_x32(t_o + lane_off + c0 + c, r);
         tmem_ld_wait();
         if (dst) {
 #pragma unroll
