@@ -235,7 +235,8 @@ def roofline_from_profile(prof: list[dict], pk: dict) -> tuple[dict, dict, dict]
     for o in prof:
         if o["kind"] == "gemm" and o["phase"] in ("denoise", "prefix"):
             m, n, k, sp = o["shape"]
-            key = f'{o["phase"]}:{m}x{n}x{k}/s{sp}'
+            # sp < 0: the CTA-pair kernel with -sp splits
+            key = f'{o["phase"]}:{m}x{n}x{k}/' + (f"p{-sp}" if sp < 0 else f"s{sp}")
             e = shapes.setdefault(key, [0, 0.0, 0.0])
             e[0] += 1
             e[1] += o["ms"]
@@ -279,6 +280,25 @@ def run_op_case(args) -> None:
         o = torch.empty(lq, heads * 128, dtype=torch.bfloat16, device=dev)
         fn = lambda i: ops.attention(q, kv[i % rot][0], kv[i % rot][1], out=o)
         algo = heads * (2 * lq + 2 * lk) * 128 * 2
+    elif kind == "layernorm":
+        # LayerNorm + AdaLN modulation (F32 scale / shift) of a token-major
+        # BF16 activation, e.g. 49152 x 3072 = the batch-64 prefix rows.
+        rows, cols = d
+        rot = max(2, (256 << 20) // (rows * cols * 2) + 1)
+        xs = [torch.randn(rows, cols, generator=gen).to(torch.bfloat16).to(dev) for _ in range(rot)]
+        ys = [torch.empty_like(xs[0]) for _ in range(rot)]
+        sc = (torch.randn(cols, generator=gen) * 0.02).to(dev)
+        sh = (torch.randn(cols, generator=gen) * 0.02).to(dev)
+        fn = lambda i: ops.layernorm(xs[i % rot], sc, sh, out=ys[i % rot])
+        algo = rows * cols * 2 * 2 + cols * 4 * 2
+    elif kind == "q8quant":
+        # BF16 [n, k] weight -> GGML Q8_0 blocks (the config-5 load-time quantiser).
+        n, k = d
+        rot = max(2, (256 << 20) // (n * k * 2) + 1)
+        ws = [(torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).to(dev) for _ in range(rot)]
+        bs = [torch.empty(n * k // 32, 34, dtype=torch.uint8, device=dev) for _ in range(rot)]
+        fn = lambda i: ops.q8_quantize(ws[i % rot], out=bs[i % rot])
+        algo = n * k * 2 + n * k // 32 * 34
     else:
         raise SystemExit(f"unknown op case {kind}")
     stream = torch.cuda.Stream()

@@ -99,6 +99,14 @@ WAM_B200_API int wam_b200_op_gemm_noalloc(const void* x, int ldx, int m, const v
  * the GEMM streams 17 KB per 256 x 64 weight tile and converts it to BF16
  * (q * d rounded to BF16) in shared memory for the tensor cores. */
 #define WAM_B200_GEMM_Q8_WEIGHTS 0x200
+/* Run a GEMM of >= 256 token rows on CTA pairs (tcgen05.mma.cta_group::2: one
+ * UMMA of 256 tokens x 256 features over two SMs, each holding 128 token rows
+ * and 128 weight rows per k-block), split over 2 or 4 pairs of one cluster when
+ * the output tiles are few and a workspace is given. BF16 weights only (row-major
+ * or WAM_B200_GEMM_TILED_WEIGHTS); ignored with force_splits > 0 or Q8_0
+ * weights. The engine uses it for every such GEMM when the environment variable
+ * WAM_B200_GEMM_PAIR=1 is set at load. */
+#define WAM_B200_GEMM_PAIR 0x400
 
 /* Quantises n_elems BF16 weights (n_elems % 32 == 0, row-major [n][k]) to GGML
  * Q8_0 blocks (34 bytes per 32 values: fp16 scale d, 32 int8 q; value q * d)
@@ -283,7 +291,7 @@ typedef struct wam_b200_op_profile {
   int phase, kind, launches;
   float ms;
   double bytes, flops;
-  int shape[4]; /* GEMM: m, n, k, split-K factor */
+  int shape[4]; /* GEMM: m, n, k, split-K factor (negative: CTA-pair kernel, -splits) */
 } wam_b200_op_profile;
 WAM_B200_API int wam_b200_profile(wam_b200_engine* engine, int batch, wam_b200_op_profile* out,
                                   int max_ops, wam_b200_status* status);

@@ -130,6 +130,11 @@ STEPK = Geometry(hidden=512, layers=3, heads=4, ffn=1024, action_hidden=512, act
 TALL = Geometry(hidden=256, layers=2, heads=2, ffn=512, action_hidden=256, action_ffn=384,
                 grid_h=12, grid_w=12, vae_z=16, action_chunk=16, steps=2, prompt_tokens=16,
                 text_dim=128)
+# 320 visual and 272 prompt tokens: the prefix and prompt GEMMs (>= 256 token
+# rows) run on CTA pairs, split over 2 or 4 pairs where their tiles are few.
+PAIR = Geometry(hidden=512, layers=2, heads=4, ffn=1024, action_hidden=512, action_ffn=1024,
+                grid_h=16, grid_w=20, vae_z=16, action_chunk=16, steps=2, prompt_tokens=272,
+                text_dim=256)
 WIDE = Geometry(hidden=1536, layers=2, heads=12, ffn=3072, action_hidden=1536, action_ffn=3072,
                 grid_h=4, grid_w=4, vae_z=16, action_chunk=48, steps=2, prompt_tokens=32,
                 text_dim=256)

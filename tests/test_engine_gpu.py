@@ -39,7 +39,7 @@ def _req(geom, seed):
     return r, Req(r.state, r.latent, r.prompt, r.noise)
 
 
-@pytest.mark.parametrize("geom_name", ["TINY", "SMALL", "TALL"])
+@pytest.mark.parametrize("geom_name", ["TINY", "SMALL", "TALL", "PAIR"])
 def test_engine_matches_oracle(cuda_device, geom_name):
     from oracle import synth
 
@@ -143,3 +143,38 @@ def test_invalid_inputs_fail_loudly(cuda_device):
         eng.predict(Req(r.state, r.latent[:1], r.prompt, r.noise))
     # the engine stays usable after rejected requests
     assert np.isfinite(eng.predict(rq)).all()
+
+
+def test_engine_pair_gemm_matches_oracle(cuda_device):
+    """The engine with WAM_B200_GEMM_PAIR=1 (every GEMM of >= 256 token rows on
+    CTA pairs: the PAIR geometry's prefix and prompt GEMMs, split over pairs
+    through the engine's workspace) against the oracle. The switch is read when
+    the library loads, so this runs in a child process."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parents[1]
+    code = (
+        "import sys; sys.path[:0] = [%r, %r]\n"
+        "import numpy as np\n"
+        "from tests.test_engine_gpu import _setup, _req, rel_l2\n"
+        "from oracle import synth\n"
+        "geom = synth.PAIR\n"
+        "om, eng = _setup(geom)\n"
+        "r, er = _req(geom, 13)\n"
+        "ref = om.predict(r, dumps=True)\n"
+        "out = eng.predict(er)\n"
+        "errs = [rel_l2(eng.read_tensor(n, 0, l), ref[n][l]) for l in range(geom.layers)\n"
+        "        for n in ('prefix_k', 'prefix_v', 'prompt_k', 'prompt_v')]\n"
+        "vel = eng.read_tensor('velocity')\n"
+        "verr = [rel_l2(vel[s], ref['velocity'][s]) for s in range(geom.steps)]\n"
+        "aerr = rel_l2(out, ref['action'])\n"
+        "print('kv', max(errs), 'vel', max(verr), 'action', aerr)\n"
+        "assert max(errs) < 2e-2 and max(verr) < 5e-2 and aerr < 5e-2 and np.isfinite(out).all()\n"
+    ) % (str(repo), str(repo / "wam.cpp_b200"))
+    env = dict(os.environ, WAM_B200_GEMM_PAIR="1")
+    res = subprocess.run([sys.executable, "-c", code], env=env, cwd=str(repo),
+                         capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]

@@ -196,3 +196,59 @@ def test_retile_rejects_bad_shapes(cuda_device):
     tw.shape = (128, 64)  # not a whole number of 256-row tiles
     with pytest.raises(RuntimeError, match="multiple of 256"):
         ops.gemm(x[:, :64], tw, ops.EPI_F32_OUT)
+
+
+PAIR_SHAPES = [
+    (256, 512, 512),     # one pair tile
+    (300, 768, 512),     # ragged: the second pair's odd CTA has no token rows
+    (768, 3072, 3072),   # prefix O / cross projections (split over pairs with a workspace)
+    (768, 3072, 14336),  # prefix FFN down (long K)
+    (512, 9216, 1024),   # more pair tiles than resident pairs: persistent loop
+    (1000, 512, 640),    # ragged M, 10 k-blocks
+]
+
+
+@pytest.mark.parametrize("layout", ["rowmajor", "tiled"])
+@pytest.mark.parametrize("mode", ["cluster", "workspace"])
+@pytest.mark.parametrize("m,n,k", PAIR_SHAPES)
+def test_gemm_pair_matches_single_cta(cuda_device, m, n, k, mode, layout):
+    """The CTA-pair (cta_group::2) kernel (pair=True, >= 256 token rows) and the
+    default one-CTA plan: both against the F32 product, and the BF16
+    gated-residual epilogue of both within one BF16 ulp of each other."""
+    from wam_b200 import ops
+
+    x, w, b = make(m, n, k, seed=5)
+    wt = ops.TiledWeight(w) if layout == "tiled" else w
+    scratch = ops.Scratch() if mode == "workspace" else None
+    ref = x.float() @ w.float().T
+    y_pair = ops.gemm(x, wt, epilogue=ops.EPI_F32_OUT, scratch=scratch, pair=True)
+    y_one = ops.gemm(x, wt, epilogue=ops.EPI_F32_OUT, scratch=scratch)
+    gate = torch.randn(n, device="cuda") * 0.5
+    resid = torch.randn(m, n, device="cuda").to(torch.bfloat16)
+    g_pair = ops.gemm(x, wt, ops.EPI_GATED_RES, bias=b, gate=gate, residual=resid, scratch=scratch,
+                      pair=True)
+    g_one = ops.gemm(x, wt, ops.EPI_GATED_RES, bias=b, gate=gate, residual=resid, scratch=scratch)
+    torch.cuda.synchronize()
+    # F32 accumulation error grows with the reduction length (~sqrt(K)).
+    tol = 1e-5 * max(1.0, math.sqrt(k / 4096))
+    assert rel_l2(y_pair, ref) < tol
+    assert rel_l2(y_one, ref) < tol
+    g_pair, g_one = g_pair.float(), g_one.float()
+    ulp = torch.clamp(g_one.abs(), min=1e-6) * (2.0 ** -7)
+    bad = ((g_pair - g_one).abs() > 1.01 * ulp + 1e-6).float().mean().item()
+    assert bad < 1e-3, f"{bad:.2e} of gated-residual outputs differ by more than one BF16 ulp"
+    if scratch is not None:
+        assert scratch.error_code() == 0
+
+
+def test_gemm_pair_repeat_deterministic(cuda_device):
+    """Split-over-pairs reduction runs in split order: repeated launches agree bit for bit."""
+    from wam_b200 import ops
+
+    x, w, _ = make(768, 3072, 3072, seed=6)
+    s = ops.Scratch()
+    y1 = ops.gemm(x, w, epilogue=ops.EPI_F32_OUT, scratch=s, pair=True)
+    y2 = ops.gemm(x, w, epilogue=ops.EPI_F32_OUT, scratch=s, pair=True)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    assert s.error_code() == 0

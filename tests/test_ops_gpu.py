@@ -50,7 +50,8 @@ def test_attention_vs_torch(cuda_device, B, heads, lq, lk):
     assert rel_l2(y.float(), ref) < 1e-2
 
 
-@pytest.mark.parametrize("rows,cols", [(48, 3072), (769, 3072), (5, 256), (3, 4096)])
+@pytest.mark.parametrize("rows,cols", [(48, 3072), (769, 3072), (5, 256), (3, 4096), (3072, 3072),
+                                       (1500, 4096)])
 @pytest.mark.parametrize("affine", [False, True])
 def test_layernorm_vs_torch(cuda_device, rows, cols, affine):
     from wam_b200 import ops
@@ -75,6 +76,28 @@ def test_layernorm_vs_torch(cuda_device, rows, cols, affine):
     ulp = torch.clamp(ref.abs(), min=1e-3) * 2.0 ** -7
     assert ((yf - ref).abs() > 1.01 * ulp).float().mean().item() < 1e-3
     assert rel_l2(yf, ref) < 5e-3
+
+
+@pytest.mark.parametrize("affine", [False, True])
+def test_layernorm_many_rows_bit_identical(cuda_device, affine):
+    """>= 1024 rows take the streaming LayerNorm kernel; the same rows in
+    launches of 512 take the latency kernel. Same arithmetic: same bits."""
+    from wam_b200 import ops
+
+    rows, cols = 2048, 3072
+    g = torch.Generator(device="cpu").manual_seed(77)
+    x = (torch.randn(rows, cols, generator=g) * 2 - 0.3).to(torch.bfloat16).cuda()
+    if affine:
+        a = (1 + 0.1 * torch.randn(cols, generator=g)).to(torch.bfloat16).cuda()
+        b = (0.1 * torch.randn(cols, generator=g)).to(torch.bfloat16).cuda()
+    else:
+        a = (0.1 * torch.randn(cols, generator=g)).float().cuda()
+        b = (0.1 * torch.randn(cols, generator=g)).float().cuda()
+    y = ops.layernorm(x, a, b, eps=1e-6, affine=affine)
+    parts = [ops.layernorm(x[i:i + 512].contiguous(), a, b, eps=1e-6, affine=affine)
+             for i in range(0, rows, 512)]
+    torch.cuda.synchronize()
+    assert torch.equal(y, torch.cat(parts))
 
 
 @pytest.mark.parametrize("name,n,scale,center", [

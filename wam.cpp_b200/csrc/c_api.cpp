@@ -83,12 +83,13 @@ WAM_B200_API int wam_b200_op_gemm(const void* x, int ldx, int m, const void* w, 
   scratch.error = error;
   const bool tiled = (epilogue & WAM_B200_GEMM_TILED_WEIGHTS) != 0;
   const bool q8 = (epilogue & WAM_B200_GEMM_Q8_WEIGHTS) != 0;
-  epilogue &= ~(WAM_B200_GEMM_TILED_WEIGHTS | WAM_B200_GEMM_Q8_WEIGHTS);
+  const bool pair = (epilogue & WAM_B200_GEMM_PAIR) != 0;
+  epilogue &= ~(WAM_B200_GEMM_TILED_WEIGHTS | WAM_B200_GEMM_Q8_WEIGHTS | WAM_B200_GEMM_PAIR);
   GemmOp op;
   const char* err = gemm_plan(&op, static_cast<const bf16*>(x), ldx, m, static_cast<const bf16*>(w),
                               n, k, epilogue, static_cast<const bf16*>(bias), gate,
                               static_cast<const bf16*>(residual), ldr, out, ldo, scratch,
-                              num_sms_current(), force_splits, tiled, q8);
+                              num_sms_current(), force_splits, tiled, q8, pair);
   if (err) {
     set_last_error(err);
     return WAM_B200_INVALID_ARGUMENT;

@@ -123,6 +123,80 @@ __global__ void __launch_bounds__(kRowThreads)
   }
 }
 
+// The same LayerNorm for many rows (batched prefix / prompt, >= 1024 rows):
+// the row stays packed as BF16 in registers and the parameters are read in
+// the output pass (they stay in L1 / L2 across rows), so twelve blocks fit per
+// SM instead of five and three times the row bytes are in flight. Same
+// arithmetic and summation order as ln_kernel: bit-identical outputs.
+template <int MODE, int MAXC>
+__global__ void __launch_bounds__(kRowThreads, 12)
+    ln_stream_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
+                     const void* pb, float eps, bf16* __restrict__ y, int ldy) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ float red[4];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const bf16* xr = x + static_cast<long long>(row) * ldx;
+  bf16* yr = y + static_cast<long long>(row) * ldy;
+  const int chunks = cols >> 3;
+  uint4 raw[MAXC];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * kRowThreads;
+    if (c < chunks) raw[i] = *reinterpret_cast<const uint4*>(xr + c * 8);
+  }
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i)
+    if (tid + i * kRowThreads < chunks) {
+      float v[8];
+      load8(reinterpret_cast<const bf16*>(&raw[i]), v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[j];
+    }
+  const float mean = block128_sum(s, red) / cols;
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i)
+    if (tid + i * kRowThreads < chunks) {
+      float v[8];
+      load8(reinterpret_cast<const bf16*>(&raw[i]), v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[j] - mean;
+        q += d * d;
+      }
+    }
+  const float inv_std = rsqrtf(block128_sum(q, red) / cols + eps);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * kRowThreads;
+    if (c < chunks) {
+      float v[8], p0[8], p1[8];
+      load8(reinterpret_cast<const bf16*>(&raw[i]), v);
+      if (MODE == 0) {
+        const float4* sc = reinterpret_cast<const float4*>(static_cast<const float*>(pa) + c * 8);
+        const float4* sh = reinterpret_cast<const float4*>(static_cast<const float*>(pb) + c * 8);
+        const float4 s0 = __ldg(sc), s1 = __ldg(sc + 1), h0 = __ldg(sh), h1 = __ldg(sh + 1);
+        p0[0] = s0.x; p0[1] = s0.y; p0[2] = s0.z; p0[3] = s0.w;
+        p0[4] = s1.x; p0[5] = s1.y; p0[6] = s1.z; p0[7] = s1.w;
+        p1[0] = h0.x; p1[1] = h0.y; p1[2] = h0.z; p1[3] = h0.w;
+        p1[4] = h1.x; p1[5] = h1.y; p1[6] = h1.z; p1[7] = h1.w;
+      } else {
+        load8(static_cast<const bf16*>(pa) + c * 8, p0);
+        load8(static_cast<const bf16*>(pb) + c * 8, p1);
+      }
+      float f[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        f[j] = MODE == 0 ? fmaf((v[j] - mean) * inv_std, 1.0f + p0[j], p1[j])
+                         : fmaf((v[j] - mean) * inv_std, p0[j], p1[j]);
+      store8(yr + c * 8, f);
+    }
+  }
+}
+
 // Generic fallback for rows wider than 128 * 8 * 4 columns: one warp per row,
 // three passes over the row.
 template <int MODE>
@@ -431,6 +505,17 @@ void launch_ln(const bf16* x, int ldx, int rows, int cols, const void* pa, const
                float eps, bf16* y, int ldy, cudaStream_t s, const L2Prefetch& pf) {
   const int per = (cols / 8 + kRowThreads - 1) / kRowThreads;
   const dim3 grid(rows), block(kRowThreads);
+  if (rows >= 1024 && per <= 4 && !pf.ptr[0] && !pf.ptr[1]) {  // many rows: bandwidth shape
+    if (per <= 1)
+      launch_pdl(ln_stream_kernel<MODE, 1>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+    else if (per <= 2)
+      launch_pdl(ln_stream_kernel<MODE, 2>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+    else if (per <= 3)
+      launch_pdl(ln_stream_kernel<MODE, 3>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+    else
+      launch_pdl(ln_stream_kernel<MODE, 4>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
+    return;
+  }
   if (per <= 1)
     launch_pdl(ln_kernel<MODE, 1>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy, pf);
   else if (per <= 2)

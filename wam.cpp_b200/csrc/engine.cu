@@ -752,7 +752,7 @@ bool MotEngine::add_gemm(Program& p, const bf16* x, int ldx, int m, const bf16* 
   rec.shape[0] = m;
   rec.shape[1] = n;
   rec.shape[2] = k;
-  rec.shape[3] = op.args.splits;
+  rec.shape[3] = op.pair ? -op.args.splits : op.args.splits;  // negative: CTA-pair kernel
   return true;
 }
 

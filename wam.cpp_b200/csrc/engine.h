@@ -71,7 +71,7 @@ struct Op {
   int launches = 1;     // kernels this op launches
   double bytes = 0.0;   // algorithmic HBM bytes (operands read + results written)
   double flops = 0.0;   // algorithmic FLOPs
-  int shape[4] = {0, 0, 0, 0};  // GEMM: m, n, k, split-K factor
+  int shape[4] = {0, 0, 0, 0};  // GEMM: m, n, k, split-K factor (negative: CTA-pair kernel)
   int lane = 0;                 // 0: main stream, 1: side stream
 };
 

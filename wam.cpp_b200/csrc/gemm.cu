@@ -879,6 +879,282 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------ CTA-pair GEMM
+// Tensor-bound GEMMs (>= 256 token rows: the prefix, prompt and batched
+// GEMMs) run on CTA pairs with tcgen05.mma.cta_group::2: one UMMA covers 256
+// tokens x 256 features, each CTA holding 128 token rows and 128 of the 256
+// weight rows of every k-block (16 + 16 KB per stage instead of 16 + 32 KB).
+// At the same shared memory that is six stages instead of four and a third
+// less data per SM per UMMA. The one-CTA kernel measured at 45% tensor-pipe
+// activity with the L2 -> SM crossbar at a third of its peak: its copies are
+// latency bound (bytes in flight per SM), which this layout relieves.
+//
+// Roles as in gemm_tc_persistent_kernel; in addition the leader (even CTA)
+// issues every UMMA of the pair, both CTAs' copies complete on the leader's
+// stage barriers (cta_group::2 TMA), and the leader's commits arrive on the
+// stage / accumulator barriers of both CTAs (multicast commit). The leader's
+// accumulator-empty barriers count both CTAs' epilogues.
+// Clusters of 2 * splits CTAs: rank = split * 2 + half. splits == 1: the
+// cluster (one pair) loops over pair tiles (persistent). splits > 1: one pair
+// tile per cluster; each pair sums a K range and the partial tiles meet in
+// the caller's workspace, as in the SPLIT_CLUSTER_GLOBAL mode of gemm_tc_kernel.
+constexpr int kPairRows = 128;                              // token rows per CTA
+constexpr uint32_t kPairA = kPairRows * kBK * 2;            // 16 KB
+constexpr uint32_t kPairB = (kWN / 2) * kBK * 2;            // 16 KB
+constexpr uint32_t kPairStage = kPairA + kPairB;
+constexpr uint32_t kPairTmemCols = 2 * kWN;                 // two accumulators
+
+int pair_stages() {
+  const int st = kStageBudget / static_cast<int>(kPairStage);
+  return st > kMaxStages ? kMaxStages : st;
+}
+int pair_smem() { return pair_stages() * static_cast<int>(kPairStage) + 1024 + kSmemTail; }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_w,
+                        const __grid_constant__ CUtensorMap tm_x,
+                        const __grid_constant__ GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int S = args.stages;
+  uint8_t* smem_a = smem;
+  uint8_t* smem_w = smem + S * kPairA;
+  uint8_t* tail = smem_w + S * kPairB;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);  // leader's count both CTAs' copies
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;      // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2], leader's: both CTAs' epilogues
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int* ok_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  float* bias_s = reinterpret_cast<float*>(tail + 256);
+  float* gate_s = bias_s + kWN;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const int half = static_cast<int>(crank & 1u);
+  const int split = static_cast<int>(crank >> 1);
+  const bool leader = half == 0;
+  const uint32_t lead_rank = crank & ~1u;
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << lead_rank);
+  const int csize = 2 * args.splits;
+  const int cl = blockIdx.x / csize, ncl = gridDim.x / csize;
+  const int tiles = args.tiles_m * args.tiles_n;  // pair tiles (256 tokens x 256 features)
+  const int kb0 = static_cast<int>((static_cast<long long>(split) * args.num_kb) / args.splits);
+  const int kb1 = static_cast<int>((static_cast<long long>(split + 1) * args.num_kb) / args.splits);
+  const int nkb = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tm_w);
+    prefetch_tensormap(&tm_x);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2);
+    }
+    *ok_flag = 1;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kPairTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // the peer's barriers exist before any copy or commit reaches them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  griddep_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_w = WAM_GEMM_WEIGHT_EVICT_FIRST ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_x = policy_evict_last();
+      const uint32_t full_lead = mapa_shared(smem_u32(full), lead_rank);
+      int g = 0;
+      bool waited = false, good = true;
+      for (int t = cl; t < tiles && good; t += ncl) {
+        const int tile_m = t % args.tiles_m, tile_n = t / args.tiles_m;
+        const int m_row = tile_m * (2 * kPairRows) + half * kPairRows;
+        for (int i = 0; i < nkb; ++i, ++g) {
+          const int s = g % S;
+          if (g >= S && !mbar_wait(&empty[s], ((g / S) & 1) ^ 1)) {
+            atomicCAS(args.error, 0u, static_cast<unsigned>(kErrProducerTimeout));
+            good = false;
+            break;
+          }
+          const uint32_t fb = full_lead + static_cast<uint32_t>(s) * 8u;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * kPairStage);
+          const int kb = kb0 + i;
+          // Re-tiled weights: row ((tile_n * K/64 + kb) * 256 + half * 128) of the
+          // [N * K / 64][64] view, 128 pre-swizzled rows copied verbatim.
+          if (args.w_tiled)
+            tma_load_2d_pair(smem_w + s * kPairB, &tm_w, fb, 0,
+                             (tile_n * args.num_kb + kb) * kWN + half * (kWN / 2), pol_w);
+          else
+            tma_load_2d_pair(smem_w + s * kPairB, &tm_w, fb, kb * kBK,
+                             tile_n * kWN + half * (kWN / 2), pol_w);
+          if (!waited) {  // weights first; the tokens come from the preceding kernel
+            griddep_wait();
+            waited = true;
+          }
+          tma_load_2d_pair(smem_a + s * kPairA, &tm_x, fb, kb * kBK, m_row, pol_x);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(2 * kPairRows, kWN);
+      int g = 0, j = 0;
+      bool good = true;
+      for (int t = cl; t < tiles && good; t += ncl, ++j) {
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait_cluster(&acc_empty[b], ((j >> 1) - 1) & 1)) {
+          atomicCAS(args.error, 0u, static_cast<unsigned>(kErrMmaTimeout));
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem_base + static_cast<uint32_t>(b * kWN);
+        for (int i = 0; i < nkb; ++i, ++g) {
+          const int s = g % S;
+          if (!mbar_wait(&full[s], (g / S) & 1)) {
+            atomicCAS(args.error, 0u, static_cast<unsigned>(kErrMmaTimeout));
+            good = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sw128_kmajor_desc(smem_u32(smem_a + s * kPairA));
+          const uint64_t db = sw128_kmajor_desc(smem_u32(smem_w + s * kPairB));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_bf16_ss_pair(acc, da + 2 * k, db + 2 * k, idesc, (i | k) != 0 ? 1u : 0u);
+          umma_commit_pair_mc(&empty[s], pair_mask);
+        }
+        if (good) umma_commit_pair_mc(&acc_full[b], pair_mask);
+      }
+    }
+  } else if (warp < 6) {
+    griddep_wait();  // residual / gate / outputs are touched only after the preceding kernel
+    const int et = threadIdx.x - 64;
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t acc_empty_lead = mapa_shared(smem_u32(acc_empty), lead_rank);
+    int j = 0;
+    for (int t = cl; t < tiles; t += ncl, ++j) {
+      const int b = j & 1;
+      const int tile_m = t % args.tiles_m, tile_n = t / args.tiles_m;
+      const int m_base = tile_m * (2 * kPairRows) + half * kPairRows, n_base = tile_n * kWN;
+      int rows = args.m - m_base;
+      rows = rows < 0 ? 0 : (rows > kPairRows ? kPairRows : rows);
+      named_bar_sync(1, 128);  // the previous tile's bias / gate are no longer read
+      for (int jj = et; jj < kWN; jj += 128) {
+        const int n = n_base + jj;
+        bias_s[jj] = (args.bias && n < args.n) ? __bfloat162float(args.bias[n]) : 0.0f;
+        gate_s[jj] = (args.gate && n < args.n) ? args.gate[n] : 0.0f;
+      }
+      named_bar_sync(1, 128);
+      const bool ok = mbar_wait(&acc_full[b], (j >> 1) & 1);
+      if (!ok) atomicCAS(args.error, 0u, static_cast<unsigned>(kErrEpilogueTimeout));
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + static_cast<uint32_t>(b * kWN) + (static_cast<uint32_t>(q * 32) << 16);
+      if (args.splits == 1) {
+        if (q * 32 < rows) {
+#pragma unroll 1
+          for (int c = 0; c < kWN; c += 16) {
+            uint32_t r[16];
+            tmem_ld_x16(taddr + c, r);
+            tmem_ld_wait();
+            if (ok && row < rows)
+              epi_run<16>(args, m_base + row, n_base + c, reinterpret_cast<const float*>(r),
+                          bias_s + c, gate_s + c);
+          }
+        }
+      } else {
+        // Partial tile [16-feature chunk][token][16] of (pair tile, half, split).
+        const size_t tile_floats = static_cast<size_t>(kPairRows) * kWN;
+        float* ws = args.workspace +
+                    ((static_cast<size_t>(t) * 2 + half) * args.splits + split) * tile_floats;
+        if (q * 32 < rows) {
+#pragma unroll 1
+          for (int c = 0; c < kWN; c += 32) {
+            uint32_t r[32];
+            tmem_ld_x32(taddr + c, r);
+            tmem_ld_wait();
+            if (row < rows) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                float4* d = reinterpret_cast<float4*>(
+                    ws + (static_cast<size_t>(c / 16 + h) * kPairRows + row) * 16);
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj)
+                  d[jj] = make_float4(__uint_as_float(r[16 * h + 4 * jj]),
+                                      __uint_as_float(r[16 * h + 4 * jj + 1]),
+                                      __uint_as_float(r[16 * h + 4 * jj + 2]),
+                                      __uint_as_float(r[16 * h + 4 * jj + 3]));
+              }
+            }
+          }
+        }
+        if (!ok && et == 0) *ok_flag = 0;
+      }
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (et == 0) mbar_arrive_cluster(acc_empty_lead + static_cast<uint32_t>(b) * 8u);
+      if (!ok) break;
+    }
+  }
+
+  __syncwarp();
+  if (args.splits > 1) {
+    // Every split's partial tile is in the workspace (cluster barrier =
+    // release / acquire): each CTA reduces its slice of its half's items over
+    // the splits, in split order, and runs the epilogue.
+    cluster_sync_all();
+    const int t = cl;
+    if (t < tiles) {
+      const int tile_m = t % args.tiles_m, tile_n = t / args.tiles_m;
+      const int m_base = tile_m * (2 * kPairRows) + half * kPairRows, n_base = tile_n * kWN;
+      int rows = args.m - m_base;
+      rows = rows < 0 ? 0 : (rows > kPairRows ? kPairRows : rows);
+      const bool ok_all = *ok_flag != 0;
+      const int sp_n = args.splits;
+      const int items = rows * (kWN / 8);
+      const int i0 = static_cast<int>((static_cast<long long>(split) * items) / sp_n);
+      const int i1 = static_cast<int>((static_cast<long long>(split + 1) * items) / sp_n);
+      const size_t tile_floats = static_cast<size_t>(kPairRows) * kWN;
+      const float* ws_tile =
+          args.workspace + (static_cast<size_t>(t) * 2 + half) * sp_n * tile_floats;
+      for (int it = i0 + static_cast<int>(threadIdx.x); it < i1; it += kThreads) {
+        const int c = it / (2 * rows), rem = it % (2 * rows);
+        const int rr = rem >> 1, h = rem & 1;
+        const float* src0 = ws_tile + (static_cast<size_t>(c) * kPairRows + rr) * 16 + h * 8;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+        for (int p = 0; p < sp_n; ++p) {
+          const float4* src = reinterpret_cast<const float4*>(src0 + p * tile_floats);
+          const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
+          acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
+          acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
+        }
+        const int f = c * 16 + h * 8;
+        if (ok_all) epi_run<8>(args, m_base + rr, n_base + f, acc, bias_s + f, gate_s + f);
+      }
+    }
+  }
+
+  // No CTA frees its TMEM while its peer's UMMAs or epilogue may still use it.
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kPairTmemCols);
+  }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -940,6 +1216,48 @@ bool g_pdl = [] {
   return !(v && *v && *v != '0');
 }();
 
+// CTA-pair kernel for every GEMM of >= 256 token rows when
+// WAM_B200_GEMM_PAIR=1 (off by default: measured no faster than the one-CTA
+// kernels on the config-2 prefix shapes); a caller can also ask for it per
+// GEMM (gemm_plan's pair argument).
+bool g_pair = [] {
+  const char* v = std::getenv("WAM_B200_GEMM_PAIR");
+  return v && *v == '1';
+}();
+
+// Kernel and split-K choice of one GEMM shape. Pair tiles (256 tokens x 256
+// features) that leave more than a quarter of the resident pairs idle split K
+// over 2 or 4 pairs of one cluster (one wave of clusters, >= 4 k-blocks each)
+// when the caller gives a workspace.
+struct ShapeChoice {
+  bool pair = false;
+  int splits = 1;
+  int tiles = 0;  // output tiles of the chosen kernel (pair tiles for the pair kernel)
+};
+
+ShapeChoice choose_shape(int m, int n, int k, int num_sms, int force_splits, bool w_q8,
+                         bool workspace, bool want_pair) {
+  ShapeChoice c;
+  const int nkb = k / kBK;
+  if ((g_pair || want_pair) && !w_q8 && force_splits <= 0 && m >= 2 * kTM) {
+    c.pair = true;
+    c.tiles = ((m + 2 * kTM - 1) / (2 * kTM)) * ((n + kWN - 1) / kWN);
+    const int pairs = g_cluster_slots[2] > 0 ? g_cluster_slots[2] / 2 : num_sms / 2;
+    if (workspace && c.tiles * 4 < pairs * 3) {
+      for (int s = 2; s <= 4; s *= 2) {
+        const int clusters = g_cluster_slots[2 * s] > 0 ? g_cluster_slots[2 * s] / (2 * s)
+                                                        : num_sms / (2 * s);
+        if (c.tiles <= clusters && nkb / s >= 4) c.splits = s;
+      }
+    }
+    return c;
+  }
+  c.tiles = ((m + kTM - 1) / kTM) * ((n + kWN - 1) / kWN);
+  c.splits = force_splits > 0 ? force_splits : pick_splits(c.tiles, nkb, num_sms);
+  if (c.splits > nkb) c.splits = nkb;
+  return c;
+}
+
 // One thread per 16-byte chunk: chunk c of row r of tile (nt, kb) goes to
 // chunk c ^ (r & 7) of that row in the tile's contiguous 32 KB block.
 __global__ void retile_weights_kernel(const bf16* __restrict__ src, bf16* __restrict__ dst, int n,
@@ -971,18 +1289,84 @@ void launch_retile_weights(const bf16* src, bf16* dst, int n, int k, cudaStream_
 }
 
 size_t gemm_scratch_floats(int m, int n, int k, int num_sms, int force_splits, int* tiles_out) {
-  const int tiles = ((m + kTM - 1) / kTM) * ((n + kWN - 1) / kWN);
-  const int nkb = k / kBK;
-  const int splits = force_splits > 0 ? force_splits : pick_splits(tiles, nkb, num_sms);
-  if (tiles_out) *tiles_out = tiles;
-  if (splits <= 1) return 0;
-  return static_cast<size_t>(tiles) * splits * a_rows_for(m) * kWN;
+  const ShapeChoice c = choose_shape(m, n, k, num_sms, force_splits, false, true, false);
+  if (tiles_out) *tiles_out = c.tiles;
+  if (c.splits <= 1) return 0;
+  if (c.pair) return static_cast<size_t>(c.tiles) * 2 * c.splits * kPairRows * kWN;
+  return static_cast<size_t>(c.tiles) * c.splits * a_rows_for(m) * kWN;
 }
+
+namespace {
+
+// Tensor map over re-tiled weights viewed as [N * K / 64][64] BF16 rows (the
+// 128-byte swizzle is already in the data): box = 128 rows copied verbatim,
+// half of one 256 x 64 tile.
+bool encode_tiled_rows(CUtensorMap* map, const void* base, long long rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kBK), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(kBK) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(kWN / 2)};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+const char* plan_pair(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, int n, int k,
+                      int epilogue, const bf16* bias, const float* gate, const bf16* residual,
+                      int ldr, void* out, int ldo, const GemmScratch& scratch, int num_sms,
+                      const ShapeChoice& c, bool w_tiled) {
+  const int nkb = k / kBK;
+  if (w_tiled) {
+    if (!encode_tiled_rows(&op->tm_w, w, static_cast<long long>(n) * nkb))
+      return "gemm: weight tensor map encode failed";
+  } else if (!encode_bf16_2d(&op->tm_w, w, k, n, k, kWN / 2)) {
+    return "gemm: weight tensor map encode failed";
+  }
+  if (!encode_bf16_2d(&op->tm_x, x, k, m, ldx, kPairRows))
+    return "gemm: activation tensor map encode failed";
+  GemmArgs& a = op->args;
+  a.m = m;
+  a.n = n;
+  a.k = k;
+  a.num_kb = nkb;
+  a.splits = c.splits;
+  a.split_mode = SPLIT_CLUSTER_GLOBAL;
+  a.a_rows = kPairRows;
+  a.stages = pair_stages();
+  a.w_tiled = w_tiled ? w : nullptr;
+  a.w_q8 = nullptr;
+  a.tiles_m = (m + 2 * kTM - 1) / (2 * kTM);
+  a.tiles_n = (n + kWN - 1) / kWN;
+  a.epilogue = epilogue;
+  a.bias = bias;
+  a.gate = gate;
+  a.residual = residual;
+  a.ldr = ldr;
+  a.out = out;
+  a.ldo = ldo;
+  a.workspace = scratch.workspace;
+  a.counters = scratch.counters;
+  a.error = scratch.error;
+  op->pair = true;
+  op->cluster = 2 * c.splits;
+  int clusters = c.tiles;
+  if (c.splits == 1) {  // persistent: at most one wave of pairs
+    const int pairs = g_cluster_slots[2] > 0 ? g_cluster_slots[2] / 2 : num_sms / 2;
+    if (clusters > pairs) clusters = pairs;
+  }
+  op->grid = clusters * op->cluster;
+  op->smem_bytes = pair_smem();
+  return nullptr;
+}
+
+}  // namespace
 
 const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, int n, int k,
                       int epilogue, const bf16* bias, const float* gate, const bf16* residual,
                       int ldr, void* out, int ldo, const GemmScratch& scratch, int num_sms,
-                      int force_splits, bool w_tiled, bool w_q8) {
+                      int force_splits, bool w_tiled, bool w_q8, bool pair) {
   if (m <= 0 || n <= 0 || k <= 0) return "gemm: empty shape";
   if (w_q8 && (n % kWN != 0 || reinterpret_cast<uintptr_t>(w) % 16 != 0))
     return "gemm: Q8_0 weight tiles need N a multiple of 256 and a 16-byte aligned pointer";
@@ -1003,6 +1387,17 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
       (ldr < n || ldr % 8 != 0 || (reinterpret_cast<uintptr_t>(residual) & 15)))
     return "gemm: residual must be 16-byte aligned with a row stride >= N in 16-byte units";
   std::memset(op, 0, sizeof(*op));
+  {
+    ShapeChoice c =
+        choose_shape(m, n, k, num_sms, force_splits, w_q8, scratch.workspace != nullptr, pair);
+    if (c.pair) {
+      if (c.splits > 1 &&
+          static_cast<size_t>(c.tiles) * 2 * c.splits * kPairRows * kWN > scratch.workspace_floats)
+        c.splits = 1;
+      return plan_pair(op, x, ldx, m, w, n, k, epilogue, bias, gate, residual, ldr, out, ldo,
+                       scratch, num_sms, c, w_tiled);
+    }
+  }
   const int a_rows = a_rows_for(m);
   // The epilogue stages a [token][feature] tile (F32 rows of kPartLd floats at
   // most) in the pipeline stages' shared memory.
@@ -1078,6 +1473,9 @@ cudaError_t gemm_init(int device) {
   e = cudaFuncSetAttribute(gemm_tc_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            smem);
   if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(gemm_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           pair_smem());
+  if (e != cudaSuccess) return e;
   int sms = 0;
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
     return e;
@@ -1121,8 +1519,17 @@ cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream) {
     attr[na].val.clusterDim.z = 1;
     ++na;
   }
+  if (op.pair) {
+    na = 1;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = op.cluster;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = na;
+  if (op.pair) return cudaLaunchKernelEx(&cfg, gemm_tc_pair_kernel, op.tm_w, op.tm_x, op.args);
   if (op.persistent) return cudaLaunchKernelEx(&cfg, gemm_tc_persistent_kernel, op.tm_w, op.tm_x, op.args);
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, op.tm_w, op.tm_x, op.args);
 }

@@ -81,16 +81,21 @@ struct GemmOp {
   GemmArgs args;
   int grid = 0;
   bool persistent = false;  // gemm_tc_persistent_kernel (tiles > SMs, no split-K)
+  bool pair = false;        // gemm_tc_pair_kernel (>= 256 tokens, CTA pairs, cta_group::2)
+  int cluster = 1;          // pair kernel: cluster size (2 x splits)
   int smem_bytes = 0;
 };
 
 // Plans one GEMM: picks the token tile and split-K factor, encodes the TMA
 // descriptors. With w_tiled the weights are in the layout written by
-// launch_retile_weights. Returns nullptr on success or a static error message.
+// launch_retile_weights. pair asks for the CTA-pair (cta_group::2) kernel when
+// m >= 256 (BF16 weights, automatic split count; WAM_B200_GEMM_PAIR=1 asks for
+// it everywhere). Returns nullptr on success or a static error message.
 const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, int n, int k,
                       int epilogue, const bf16* bias, const float* gate, const bf16* residual,
                       int ldr, void* out, int ldo, const GemmScratch& scratch, int num_sms,
-                      int force_splits, bool w_tiled = false, bool w_q8 = false);
+                      int force_splits, bool w_tiled = false, bool w_q8 = false,
+                      bool pair = false);
 // Re-tiles a row-major [n][k] BF16 weight (n % 256 == 0, k % 64 == 0) into
 // contiguous 32 KB tiles [n/256][k/64][256][64] with the 128-byte swizzle of
 // the UMMA operand pre-applied, so one bulk copy fetches a pipeline stage.

@@ -56,13 +56,15 @@ class TiledWeight:
 
 
 GEMM_Q8_WEIGHTS = 0x200
+GEMM_PAIR = 0x400  # CTA-pair (cta_group::2) kernel for >= 256 token rows
 Q8_TILE_BYTES = 256 * 64 + 256 * 2 * 2
 
 
-def q8_quantize(w):
+def q8_quantize(w, out=None):
     """BF16 [n, k] -> GGML Q8_0 blocks (uint8 [n * k / 32, 34]) on the device."""
     w = w.contiguous()
-    out = torch.empty(w.numel() // 32, 34, dtype=torch.uint8, device=w.device)
+    if out is None:
+        out = torch.empty(w.numel() // 32, 34, dtype=torch.uint8, device=w.device)
     check(load().wam_b200_op_q8_quantize(_ptr(w), w.numel(), _ptr(out), _stream()),
           "wam_b200_op_q8_quantize")
     return out
@@ -89,7 +91,7 @@ class Q8Weight:
 
 
 def gemm(x, w, epilogue=EPI_BIAS, bias=None, gate=None, residual=None, out=None,
-         scratch: Scratch | None = None, force_splits: int = 0):
+         scratch: Scratch | None = None, force_splits: int = 0, pair: bool = False):
     """out[m, n] = epilogue(x[m, :K] . w[n, :]) via wam_b200_op_gemm.
 
     Without `scratch`, split-K partials are reduced inside thread-block
@@ -98,6 +100,8 @@ def gemm(x, w, epilogue=EPI_BIAS, bias=None, gate=None, residual=None, out=None,
     lib = load()
     m = x.shape[0]
     n, k = w.shape
+    if pair:
+        epilogue |= GEMM_PAIR
     if isinstance(w, TiledWeight):
         epilogue |= GEMM_TILED_WEIGHTS
         w = w.data
@@ -138,9 +142,9 @@ def attention(q, k, v, scale=None, out=None):
     return out
 
 
-def layernorm(x, a, b, eps=1e-6, affine=False):
+def layernorm(x, a, b, eps=1e-6, affine=False, out=None):
     lib = load()
-    y = torch.empty_like(x)
+    y = torch.empty_like(x) if out is None else out
     rc = lib.wam_b200_op_layernorm(_ptr(x), x.shape[0], x.shape[1], _ptr(a), _ptr(b), eps,
                                    1 if affine else 0, _ptr(y), _stream())
     check(rc, "wam_b200_op_layernorm")
