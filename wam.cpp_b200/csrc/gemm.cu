@@ -514,6 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nkb = kb1 - kb0;
   const int m_base = tile_m * kTM;
   const int rows = args.m - m_base < kTM ? args.m - m_base : kTM;  // valid token rows
+  const bool m64 = args.a_rows <= 64;  // token tile of <= 64 rows: M = 64 UMMAs
   const int n_base = tile_n * kWN;
   const bool cluster_mode = args.splits > 1 && args.split_mode != SPLIT_WORKSPACE;
   const bool global_xchg = args.split_mode == SPLIT_CLUSTER_GLOBAL;
@@ -637,7 +638,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kTM, kWN);
+      // Token tiles of <= 64 rows run M = 64 UMMAs: half the tensor-core work
+      // per weight k-block of an M = 128 instruction on the same 256 features.
+      const uint32_t idesc = umma_idesc_bf16(m64 ? 64 : kTM, kWN);
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S;
         const uint32_t ph = (i / S) & 1;
@@ -675,15 +678,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok) atomicCAS(args.error, 0u, static_cast<unsigned>(kErrEpilogueTimeout));
     tc_fence_after();
     const int q = warp & 3;  // TMEM lane quadrant of this warp
-    const int row = q * 32 + lane;
-    const bool warp_rows = q * 32 < rows;  // warp-uniform: tcgen05.ld is warp-collective
+    // M = 128: token q*32 + lane in lane q*32 + lane. M = 64: tokens 16q..16q+15
+    // in lanes 32q..32q+15 of the quadrant (lanes 16-31 hold nothing).
+    const int row = m64 ? q * 16 + (lane & 15) : q * 32 + lane;
+    const bool lane_ok = !m64 || lane < 16;
+    const bool warp_rows = (m64 ? q * 16 : q * 32) < rows;  // warp-uniform: tcgen05.ld is warp-collective
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     if (args.splits == 1) {
       uint8_t* stg = smem;  // the stages are free once the accumulator is complete
       if (warp_rows) {
         // The TMEM load of the next 16 columns is in flight while this chunk
         // is staged.
-        const bool st = row < rows;
+        const bool st = lane_ok && row < rows;
         uint32_t r0[16], r1[16];
         tmem_ld_x16(taddr, r0);
         tmem_ld_wait();
@@ -706,7 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const size_t tile_floats = static_cast<size_t>(args.a_rows) * kWN;
       float* ws = args.workspace + (static_cast<size_t>(tile) * args.splits + split) * tile_floats;
       if (warp_rows) {
-        const bool st = row < rows;
+        const bool st = lane_ok && row < rows;
 #pragma unroll 1
         for (int c = 0; c < kWN; c += 32) {
           uint32_t r[32];
@@ -734,7 +740,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t r[16];
           tmem_ld_x16(taddr + c, r);
           tmem_ld_wait();
-          if (row < rows) {
+          if (lane_ok && row < rows) {
             float4* dst = reinterpret_cast<float4*>(partial + row * kPartLd + c);
 #pragma unroll
             for (int j = 0; j < 4; ++j)
@@ -755,7 +761,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t r[16];
           tmem_ld_x16(taddr + c, r);
           tmem_ld_wait();
-          if (row < rows) {
+          if (lane_ok && row < rows) {
             float4* dst = reinterpret_cast<float4*>(ws + row * kWN + c);
 #pragma unroll
             for (int j = 0; j < 4; ++j)
