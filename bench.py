@@ -268,7 +268,9 @@ def run_op_case(args) -> None:
         x = torch.randn(m, k, generator=gen).to(torch.bfloat16).to(dev)
         b = torch.zeros(n, dtype=torch.bfloat16, device=dev)
         y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-        fn = lambda i: ops.gemm(x, ws[i % rot], ops.EPI_BIAS, bias=b, out=y)
+        sc = ops.Scratch() if args.scratch else None
+        fn = lambda i: ops.gemm(x, ws[i % rot], ops.EPI_BIAS, bias=b, out=y, scratch=sc,
+                                force_splits=args.force_splits)
         algo = n * k * 2 + m * k * 2 + m * n * 2
     elif kind == "attention":
         lq, lk, heads = d
@@ -319,7 +321,8 @@ def run_op_case(args) -> None:
         e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / args.steps
-    print(json.dumps({"op_case": args.op_case, "launches": args.steps, "avg_us": round(us, 3),
+    print(json.dumps({"op_case": args.op_case, "force_splits": args.force_splits,
+                      "scratch": bool(args.scratch), "launches": args.steps, "avg_us": round(us, 3),
                       "algorithmic_bytes": algo, "GB/s": round(algo / us / 1e3, 1)}))
 
 
@@ -388,6 +391,10 @@ def main() -> None:
     ap.add_argument("--op-case", default=None,
                     help="gemm:M,N,K or attention:LQ,LK,HEADS: run one kernel on a small case "
                          "(for ncu captures) and print its event timing instead of the bench line")
+    ap.add_argument("--force-splits", type=int, default=0,
+                    help="op case gemm: split-K factor (0 = the planner's choice)")
+    ap.add_argument("--scratch", action="store_true",
+                    help="op case gemm: split-K partials through a global workspace (as the engine)")
     ap.add_argument("--attention-bench", action="store_true",
                     help="BASELINE config 3: the attention microbench over cache length and batch")
     args = ap.parse_args()
