@@ -35,6 +35,8 @@ def torch_attention(q, k, v, scale):
     (1, 2, 816, 4096),     # microbench: 48 + 768 queries over a 4096 cache
     (8, 24, 816, 1280),    # config 3: batch 8 over the 1280-key cache, 24 heads
     (1, 24, 816, 16384),   # config 3: the 16384-key cache, 24 heads
+    (1, 24, 816, 1280),    # config 3 batch 1: 168 CTAs (1.14 waves)
+    (1, 24, 769, 769),     # prefix joint attention at config-2 widths, ragged last key tile
 ])
 def test_attention_vs_torch(cuda_device, B, heads, lq, lk):
     from wam_b200 import ops
