@@ -969,6 +969,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc_pair(tmem_slot, kPairTmemCols);
     tmem_relinquish_pair();
   }
+  __syncwarp();  // warp 0 reconverges after thread 0's set-up: the cluster barrier is .aligned
   tc_fence_before();
   cluster_sync_all();  // the peer's barriers exist before any copy or commit reaches them
   tc_fence_after();
