@@ -413,6 +413,7 @@ def main() -> None:
     import numpy as np
     import torch
     from oracle import synth
+    from wam_b200 import dp as dp_host
     from wam_b200.engine import Engine, Req
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -433,11 +434,7 @@ def main() -> None:
             dist.barrier()
 
     def max_over_ranks(x: float) -> float:
-        if not dist:
-            return x
-        t = torch.tensor([x], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return dp_host.max_over_ranks(x, dist, device=torch.device("cuda", local))
 
     g = config2()
     B = args.batch
@@ -446,7 +443,7 @@ def main() -> None:
                  prompt_cache=False)
     reqs = []
     for i in range(B):
-        r = synth.make_request(g, SEED + 7919 * rank + i)
+        r = synth.make_request(g, dp_host.request_seed(SEED, rank, i))
         reqs.append(Req(r.state, r.latent, r.prompt, r.noise))
     stream = torch.cuda.ExternalStream(eng.stream())
     kernels_per_chunk = eng.kernel_launches(B, with_prompt=True)
@@ -471,7 +468,7 @@ def main() -> None:
     barrier()
     per = [events[i].elapsed_time(events[i + 1]) for i in range(args.steps)]
     total_s = max_over_ranks(sum(per) / 1e3)
-    value = world * B * args.steps / total_s
+    value = dp_host.job_throughput([B * args.steps] * world, total_s)
     out = eng.fetch(reqs)
     assert np.isfinite(out).all(), "non-finite action chunk"
 
@@ -483,7 +480,7 @@ def main() -> None:
     for _ in range(args.steps):
         eng.predict_batch(reqs)
     e2e_s = max_over_ranks(time.perf_counter() - t0)
-    e2e_value = world * B * args.steps / e2e_s
+    e2e_value = dp_host.job_throughput([B * args.steps] * world, e2e_s)
     A, T, Nt, D = g.action_dim, g.action_chunk, g.prompt_tokens, g.text_dim
     h2d = B * 4 * (A + g.vae_z * 4 * g.visual_tokens + Nt * D + T * A)
     d2h = B * 4 * (T * A + 1)
