@@ -380,7 +380,8 @@ def run_attention_bench(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=15,
+                    help="timed chunks (15 = the reference wam-bench repetitions, p50 / p95 over them)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=1, help="requests per GPU per step")
