@@ -390,7 +390,8 @@ def main() -> None:
     ap.add_argument("--weights", choices=["bf16", "q8_0"], default="bf16",
                     help="q8_0: BASELINE config 5 (every linear weight Q8_0) instead of config 2")
     ap.add_argument("--op-case", default=None,
-                    help="gemm:M,N,K or attention:LQ,LK,HEADS: run one kernel on a small case "
+                    help="gemm:M,N,K, attention:LQ,LK,HEADS, layernorm:ROWS,COLS or "
+                         "q8quant:N,K: run one kernel on a small case "
                          "(for ncu captures) and print its event timing instead of the bench line")
     ap.add_argument("--force-splits", type=int, default=0,
                     help="op case gemm: split-K factor (0 = the planner's choice)")
