@@ -36,9 +36,9 @@ SEED = 20261201
 
 
 def config2(layers: int | None = None):
-    from oracle import synth
+    from wam_b200 import workload
 
-    g = dataclasses.replace(synth.CONFIG2, flow_shift=1.0)  # sigmas linear 1 -> 0.001 -> 0
+    g = dataclasses.replace(workload.CONFIG2, flow_shift=1.0)  # sigmas linear 1 -> 0.001 -> 0
     if layers is not None:
         g = dataclasses.replace(g, layers=layers)
     return g
@@ -414,8 +414,8 @@ def main() -> None:
 
     import numpy as np
     import torch
-    from oracle import synth
     from wam_b200 import dp as dp_host
+    from wam_b200 import workload
     from wam_b200.engine import Engine, Req
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -445,7 +445,7 @@ def main() -> None:
                  prompt_cache=False)
     reqs = []
     for i in range(B):
-        r = synth.make_request(g, dp_host.request_seed(SEED, rank, i))
+        r = workload.make_request(g, dp_host.request_seed(SEED, rank, i))
         reqs.append(Req(r.state, r.latent, r.prompt, r.noise))
     stream = torch.cuda.ExternalStream(eng.stream())
     kernels_per_chunk = eng.kernel_launches(B, with_prompt=True)

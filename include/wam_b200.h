@@ -84,15 +84,22 @@ WAM_B200_API int wam_b200_op_gemm(const void* x, int ldx, int m, const void* w, 
  * for split-K, this entry point uses a fixed library-owned device array instead
  * (8 MiB of partials + 4096 tile counters, held on every GPU that loads the
  * library until exit) and calls no allocating routine. Shapes whose split-K
- * partials exceed it are rejected with WAM_B200_INVALID_ARGUMENT. The first call
- * on a device looks up the array's device address (cudaGetSymbolAddress); make
- * that first call before any stream capture. All calls share the array: calls
- * that overlap on the GPU race and must be serialized by the caller. Arguments
- * as wam_b200_op_gemm, without the workspace. */
+ * partials exceed it are rejected with WAM_B200_INVALID_ARGUMENT; unsplit and
+ * persistent shapes need none of it, whatever their size. The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress); make that
+ * first call before any stream capture. All calls share the array: calls that
+ * overlap on the GPU race and must be serialized by the caller. Arguments as
+ * wam_b200_op_gemm, without the workspace and the error word (flags
+ * WAM_B200_GEMM_TILED_WEIGHTS / _Q8_WEIGHTS / _PAIR accepted). */
 WAM_B200_API int wam_b200_op_gemm_noalloc(const void* x, int ldx, int m, const void* w, int n,
                                           int k, int epilogue, const void* bias, const float* gate,
                                           const void* residual, int ldr, void* out, int ldo,
                                           int force_splits, void* stream);
+/* Device error word of the last wam_b200_op_gemm_noalloc call on the current
+ * device (0: no pipeline wait timed out; otherwise the code the kernel set).
+ * Blocking: synchronises with that call through a device-to-host copy of one
+ * word into *code. Allocates nothing. */
+WAM_B200_API int wam_b200_op_gemm_noalloc_error(unsigned* code);
 
 #define WAM_B200_GEMM_TILED_WEIGHTS 0x100
 /* w holds Q8_0 weight tiles written by wam_b200_op_q8_retile (n % 256 == 0):
@@ -153,6 +160,46 @@ WAM_B200_API int wam_b200_op_attention(const void* q, long long q_seq_stride,
 WAM_B200_API int wam_b200_op_layernorm(const void* x, int rows, int cols, const void* a,
                                        const void* b, float eps, int affine, void* y,
                                        void* stream);
+
+/* Q/K/V post-processing of a packed QKV projection and its scatter into the
+ * head-major K/V cache (expert_qkv's RMSNorm + RoPE + cast, src/models/gwp05/
+ * engine/mot.cpp:210-267, and the prefix cache write of engine/cache.cpp:
+ * 441-469, in this engine's layout). For token row r (sequence b = r /
+ * rows_per_seq, row i = r % rows_per_seq in it) and part x in {q, k, v} with a
+ * source column >= 0: optional RMSNorm over the whole hidden width (F32,
+ * x * rsqrt(mean(x^2) + eps) * norm; v is never normalised), optional RoPE
+ * NORMAL on pairs (2j, 2j+1) at 1-D position pos_base + i (rope_mode 1) or at the
+ * 3-D position pos_thw[i] = (t, h, w) over sections 44/42/42 (rope_mode 2;
+ * v never roped), cast to BF16, and element (head, d) stored at
+ *   q: q_out[b*q_seq_stride + head*q_head_stride + (q_row_offset + i)*128 + d]
+ *   k/v: k_out/v_out[b*kv_seq_stride + head*kv_head_stride + (kv_row_offset + i)*128 + d].
+ * The engine's cache is [heads][prefix rows + action rows][128] per request and
+ * layer: row 0 the state token, rows 1..V the visual tokens, rows P..P+T-1 the
+ * action tokens. inv_freq: a device copy of wam_b200_rope_inv_freq(rope_mode).
+ * All pointers are device pointers; pos_thw is int32 [rows_per_seq][3]. */
+typedef struct wam_b200_qkv_scatter_args {
+  const void* src; /* BF16 [rows][ld_src] */
+  int ld_src, rows, rows_per_seq, heads;
+  int q_col, k_col, v_col; /* first source column of each part, -1 to skip it */
+  const void* q_norm;      /* BF16 [heads*128] or NULL (no RMSNorm) */
+  const void* k_norm;
+  float eps;
+  int rope_mode, pos_base;
+  const int* pos_thw;
+  const float* inv_freq;
+  void* q_out;
+  long long q_seq_stride, q_head_stride;
+  int q_row_offset;
+  void* k_out;
+  void* v_out;
+  long long kv_seq_stride, kv_head_stride;
+  int kv_row_offset;
+} wam_b200_qkv_scatter_args;
+WAM_B200_API int wam_b200_op_qkv_scatter(const wam_b200_qkv_scatter_args* args, void* stream);
+/* RoPE inverse frequencies [64] (mode 1: 1-D over 128 dims; mode 2: visual
+ * sections 44/42/42 at [0..21], [22..42], [43..63]), as the engine uploads them
+ * (ggml_rope_ext NORMAL, theta_scale = 10000^(-2/n_dims); mot.cpp:175-202). */
+WAM_B200_API int wam_b200_rope_inv_freq(int mode, float* out64);
 
 /* Deterministic synthetic BF16 tensor (the generator behind synthetic weights):
  * w[i] = bf16(f32(z_i) * f32(scale / sd) + f32(center)), z_i the Irwin-Hall(4)

@@ -7,6 +7,7 @@ path. See oracle.h for what it restates and its parity status.
 from __future__ import annotations
 
 import ctypes as C
+import os
 import subprocess
 from pathlib import Path
 
@@ -34,12 +35,23 @@ def geom_struct(g: Geometry, cls=_Geom):
     return s
 
 
+def reference_root() -> Path | None:
+    """The reference source tree named by WAM_REFERENCE_ROOT, if it holds the
+    host sources the _ref build compiles (None otherwise)."""
+    root = os.environ.get("WAM_REFERENCE_ROOT")
+    if root and (Path(root) / "src" / "models" / "common" / "scheduler.cpp").exists():
+        return Path(root)
+    return None
+
+
 def build(with_ref: bool = True) -> None:
-    """Builds liboracle.so (and, when the reference tree is present, the
-    reference's own scheduler/semantics into _ref/libwamref.so)."""
+    """Builds liboracle.so (and, when WAM_REFERENCE_ROOT names the reference
+    tree, the reference's own scheduler/semantics into _ref/libwamref.so)."""
     subprocess.run(["make", "-C", str(HERE), "liboracle.so"], check=True, capture_output=True)
-    if with_ref and Path("/root/reference/src/models/common/scheduler.cpp").exists():
-        subprocess.run(["make", "-C", str(HERE), "ref"], check=True, capture_output=True)
+    ref = reference_root()
+    if with_ref and ref is not None:
+        subprocess.run(["make", "-C", str(HERE), "ref", f"REF={ref}"], check=True,
+                       capture_output=True)
 
 
 _lib = None
@@ -66,6 +78,9 @@ def lib():
         l.oracle_timestep_embedding.argtypes = [C.c_float, C.c_int, f32p]
         l.oracle_visual_positions.argtypes = [C.c_int, C.c_int] + [C.POINTER(C.c_int32)] * 3
         l.oracle_threads.restype = C.c_int
+        l.oracle_quantize_q8.argtypes = [C.c_void_p]
+        l.oracle_q8_roundtrip.argtypes = [C.c_void_p, C.c_int64, f32p]
+        l.oracle_set_uncached.argtypes = [C.c_void_p, C.c_int]
         _lib = l
     return _lib
 
@@ -94,6 +109,14 @@ def schedule(steps: int, shift: float):
     sig = np.zeros(steps + 1, np.float32)
     lib().oracle_schedule(steps, shift, _fp(ts), _fp(sig))
     return ts, sig
+
+
+def q8_roundtrip(bf16_bits: np.ndarray) -> np.ndarray:
+    """GGML Q8_0 quantise + dequantise (F32 q * d) of BF16 bit patterns."""
+    b = np.ascontiguousarray(bf16_bits, dtype=np.uint16).reshape(-1)
+    out = np.zeros(b.size, np.float32)
+    lib().oracle_q8_roundtrip(b.ctypes.data, b.size, _fp(out))
+    return out
 
 
 def timestep_embedding(t: float, dim: int = 256):
@@ -131,6 +154,16 @@ class OracleModel:
                                      err, 512)
         if not self.h:
             raise RuntimeError("oracle_create: " + err.value.decode())
+
+    def quantize_q8(self) -> "OracleModel":
+        """Config 5: linear weights become their exact F32 Q8_0 dequantisation."""
+        lib().oracle_quantize_q8(self.h)
+        return self
+
+    def set_uncached(self, uncached: bool = True) -> "OracleModel":
+        """Recompute the prefix every step (the reference's CPU mode)."""
+        lib().oracle_set_uncached(self.h, 1 if uncached else 0)
+        return self
 
     def __del__(self):
         h = getattr(self, "h", None)

@@ -57,8 +57,49 @@ inline float gelu_tanh(float x) {
 inline float gelu_erf(float x) { return 0.5f * x * (1.0f + std::erf(x * 0.70710678118654752440f)); }
 inline float silu(float x) { return x / (1.0f + std::exp(-x)); }
 
+// F32 -> IEEE fp16 (round to nearest even, subnormals kept) -> F32.
+inline float f16_round(float x) {
+  if (x == 0.0f || !std::isfinite(x)) return x;
+  int e;
+  std::frexp(x, &e);  // |x| = m * 2^e, m in [0.5, 1)
+  // fp16 keeps 11 significant bits for normals (e >= -13), fewer below.
+  const int bits = e >= -13 ? 11 : 11 - (-13 - e);
+  if (bits <= 0) return std::copysign(0.0f, x);
+  const float q = std::ldexp(1.0f, e - bits);  // spacing of representable values
+  const float r = std::nearbyint(x / q) * q;   // current rounding mode: to nearest even
+  return std::fabs(r) > 65504.0f ? std::copysign(INFINITY, x) : r;
+}
+
+// Row length of a linear layer's weight as the Q8_0 policy sees it (0: not a
+// linear weight); the same rule as the engine's linear_inner().
+int64_t linear_inner(const std::string& n, const oracle_geometry& g) {
+  auto ends = [&](const char* suf) {
+    const size_t k = std::strlen(suf);
+    return n.size() >= k && n.compare(n.size() - k, k, suf) == 0;
+  };
+  auto starts = [&](const char* pre) { return n.rfind(pre, 0) == 0; };
+  if (!ends(".weight") || ends(".qn.weight") || ends(".kn.weight") || ends("ca_norm.weight"))
+    return 0;
+  const int64_t E = g.action_hidden, H = g.hidden;
+  if (n == "gwp.patch.weight") return static_cast<int64_t>(g.vae_z) * 4;
+  if (ends(".in.weight") && (starts("gwp.state") || starts("gwp.action"))) return 128;
+  if (ends(".mid.weight") || n == "gwp.state.out.weight" || n == "gwp.action.out.weight") return 128;
+  if (n == "gwp.decode.in.weight") return E;
+  if (n == "gwp.decode.out.weight") return g.action_dim;
+  if (ends(".time.0.weight")) return 256;
+  if (ends(".text.0.weight")) return g.text_dim;
+  if (starts("gwp.acond")) return E;
+  if (starts("gwp.cond")) return H;
+  const bool act = n.find(".a.") != std::string::npos;
+  const int64_t W = act ? E : H, F = act ? g.action_ffn : g.ffn;
+  if (ends(".sa.o.weight") || ends(".ca.o.weight")) return H;
+  if (ends(".ffn.out.weight")) return F;
+  return W;
+}
+
 struct Tensor {
   std::vector<uint16_t> data;
+  std::vector<float> f32;  // Q8_0 mode: exact F32 dequantised values q * d (data unused)
   int64_t numel = 0;
 };
 
@@ -66,6 +107,13 @@ struct Model {
   oracle_geometry g{};
   std::unordered_map<std::string, Tensor> t;
   Vec sq01, sq99, aq01, aq99;
+  bool uncached = false;  // recompute the prefix every step (the reference's CPU mode)
+
+  // F32 weights of a tensor the Q8_0 policy quantised (nullptr otherwise).
+  const float* wf(const std::string& name) const {
+    auto it = t.find(name);
+    return it == t.end() || it->second.f32.empty() ? nullptr : it->second.f32.data();
+  }
 
   const uint16_t* w(const std::string& name, int64_t expect) const {
     auto it = t.find(name);
@@ -85,7 +133,9 @@ struct Model {
 // ---------------------------------------------------------------- GEMM
 // acc[m][n] = sum_k x[m][k] * W[n][k], F32. W is BF16 [N][K] row-major (GGUF
 // ne = {K, N}); ggml_mul_mat(W, x) (weights.cpp:788, 826).
-void gemm_acc(const float* x, int M, int K, const uint16_t* W, int N, float* acc) {
+// Wf (when given) holds F32 weights of the same layout, used instead of W.
+void gemm_acc(const float* x, int M, int K, const uint16_t* W, int N, float* acc,
+              const float* Wf = nullptr) {
 #pragma omp parallel
   {
     std::vector<float> wb(static_cast<size_t>(4) * K);
@@ -95,7 +145,9 @@ void gemm_acc(const float* x, int M, int K, const uint16_t* W, int N, float* acc
       const int nn = std::min(4, N - n0);
       for (int j = 0; j < 4; ++j) {
         float* dst = wb.data() + static_cast<size_t>(j) * K;
-        if (j < nn) {
+        if (j < nn && Wf) {
+          std::memcpy(dst, Wf + static_cast<size_t>(n0 + j) * K, sizeof(float) * K);
+        } else if (j < nn) {
           const uint16_t* src = W + static_cast<size_t>(n0 + j) * K;
           for (int k = 0; k < K; ++k) dst[k] = bf2f(src[k]);
         } else {
@@ -159,7 +211,7 @@ Vec linear(const Model& md, const Vec& x, int M, int K, const std::string& name,
   const uint16_t* b = md.w(name + ".bias", N);
   Vec y(static_cast<size_t>(M) * N);
   if (!W || !b) return Vec();
-  gemm_acc(xb.data(), M, K, W, N, y.data());
+  gemm_acc(xb.data(), M, K, W, N, y.data(), md.wf(name + ".weight"));
   for (int m = 0; m < M; ++m)
     for (int n = 0; n < N; ++n) {
       float& v = y[static_cast<size_t>(m) * N + n];
@@ -176,11 +228,16 @@ Vec embodiment_linear(const Model& md, const Vec& x, int M, int in, int out,
   const uint16_t* W = md.w(name + ".weight", static_cast<int64_t>(md.g.num_embodiments) * in * out);
   const uint16_t* b = md.w(name + ".bias", static_cast<int64_t>(md.g.num_embodiments) * out);
   const uint16_t* We = W + static_cast<size_t>(emb) * in * out;
+  const float* Wf = md.wf(name + ".weight");
+  const float* Wfe = Wf ? Wf + static_cast<size_t>(emb) * in * out : nullptr;
   Vec y(static_cast<size_t>(M) * out);
   for (int m = 0; m < M; ++m)
     for (int o = 0; o < out; ++o) {
       float s = 0.0f;
-      for (int i = 0; i < in; ++i) s += bfr(x[static_cast<size_t>(m) * in + i]) * bf2f(We[static_cast<size_t>(i) * out + o]);
+      for (int i = 0; i < in; ++i) {
+        const size_t wi = static_cast<size_t>(i) * out + o;
+        s += bfr(x[static_cast<size_t>(m) * in + i]) * (Wfe ? Wfe[wi] : bf2f(We[wi]));
+      }
       y[static_cast<size_t>(m) * out + o] = bfr(bfr(s) + bf2f(b[static_cast<size_t>(emb) * out + o]));
     }
   return y;
@@ -505,7 +562,8 @@ PrefixOut prefix(const Model& md, const Vec& state_norm, const float* latent, co
             cols[(static_cast<size_t>(y) * gw + x) * C * 4 + c * 4 + dy * 2 + dx] =
                 bfr(latent[(static_cast<size_t>(c) * lh + 2 * y + dy) * lw + 2 * x + dx]);
   Vec hv(static_cast<size_t>(V) * H);
-  gemm_acc(cols.data(), V, C * 4, md.w("gwp.patch.weight", static_cast<int64_t>(H) * C * 4), H, hv.data());
+  gemm_acc(cols.data(), V, C * 4, md.w("gwp.patch.weight", static_cast<int64_t>(H) * C * 4), H,
+           hv.data(), md.wf("gwp.patch.weight"));
   const uint16_t* pb = md.w("gwp.patch.bias", H);
   for (int t = 0; t < V; ++t)
     for (int n = 0; n < H; ++n) hv[static_cast<size_t>(t) * H + n] = bfr(hv[static_cast<size_t>(t) * H + n] + bf2f(pb[n]));
@@ -740,6 +798,49 @@ void* oracle_create_synthetic(const oracle_geometry* g, uint64_t seed, double bi
   return md;
 }
 
+// GGML Q8_0 round trip of 32-value blocks, restating the gguf-py codec
+// (gguf.quants Q8_0, gguf 0.19.0; the wam.cpp reference has no Q8_0): d =
+// max|x| / 127 in F32, q = x * (1/d) rounded half away from zero, d stored as
+// fp16; dequantised value = fp16(d) * q in F32 (dequantize_row_q8_0).
+void oracle_q8_roundtrip(const uint16_t* bf16, int64_t n, float* out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < n / 32; ++b) {
+    float x[32], amax = 0.0f;
+    for (int j = 0; j < 32; ++j) {
+      x[j] = bf2f(bf16[b * 32 + j]);
+      amax = std::max(amax, std::fabs(x[j]));
+    }
+    const float d = amax / 127.0f;
+    const float id = d == 0.0f ? 0.0f : 1.0f / d;
+    const float d16 = f16_round(d);
+    for (int j = 0; j < 32; ++j) {
+      const float v = x[j] * id;
+      const float a = std::fabs(v);
+      const float fl = std::floor(a);
+      // stored as int8, so a negative value that rounds to 0 is +0
+      const int q = static_cast<int>(std::copysign(fl + std::floor(2.0f * (a - fl)), v));
+      out[b * 32 + j] = d16 * static_cast<float>(q);
+    }
+  }
+}
+
+// Config-5 policy: every linear weight whose rows are whole 32-value blocks
+// (linear_inner) is replaced by its exact F32 Q8_0 dequantisation.
+int oracle_quantize_q8(void* model) {
+  Model& md = *static_cast<Model*>(model);
+  for (auto& kv : md.t) {
+    const int64_t inner = linear_inner(kv.first, md.g);
+    if (inner <= 0 || inner % 32 != 0 || kv.second.numel % 32 != 0) continue;
+    kv.second.f32.resize(kv.second.numel);
+    oracle_q8_roundtrip(kv.second.data.data(), kv.second.numel, kv.second.f32.data());
+  }
+  return 0;
+}
+
+void oracle_set_uncached(void* model, int uncached) {
+  static_cast<Model*>(model)->uncached = uncached != 0;
+}
+
 void oracle_destroy(void* m) { delete static_cast<Model*>(m); }
 
 int oracle_predict(void* model, const float* state, const float* latent, const float* prompt,
@@ -777,6 +878,9 @@ int oracle_predict(void* model, const float* state, const float* latent, const f
   Vec a(noise, noise + static_cast<size_t>(T) * A);
   bfr_inplace(a);
   for (int s = 0; s < g.steps; ++s) {
+    // The reference's CPU mode runs the whole MoT every step (engine.cpp:334-337,
+    // run_mot_step): the prefix half is recomputed from the same inputs.
+    if (md.uncached && s > 0) pre = prefix(md, sn, latent, pr);
     Vec vel = action_step(md, pre, a, ts[s]);
     const float dt = sig[s + 1] - sig[s];
     for (size_t i = 0; i < a.size(); ++i) {

@@ -58,6 +58,14 @@ void* oracle_create(const oracle_geometry* g, int n_tensors, const char** names,
 void* oracle_create_synthetic(const oracle_geometry* g, uint64_t seed, double bias_scale,
                               char* err, int errlen);
 void oracle_destroy(void* model);
+/* Config-5 policy: replaces every linear weight whose rows are whole 32-value
+ * blocks by its exact F32 Q8_0 dequantisation (no BF16 rounding of q * d). */
+int oracle_quantize_q8(void* model);
+/* GGML Q8_0 quantise + dequantise of n BF16 values (n % 32 == 0) into F32. */
+void oracle_q8_roundtrip(const uint16_t* bf16, int64_t n, float* out);
+/* uncached != 0: recompute the prefix at every step, as the reference's CPU
+ * backend does (engine.cpp:334-337). Results are identical; only time differs. */
+void oracle_set_uncached(void* model, int uncached);
 
 /* One request. state: [real_state_dim] raw; latent: [vae_z][2gh][2gw];
  * prompt: [prompt_tokens][text_dim] (zero-padded by the caller);

@@ -1,4 +1,7 @@
-"""Deterministic synthetic GWP-0.5 weights and inputs — TEST INFRASTRUCTURE.
+"""Deterministic synthetic GWP-0.5 weights — TEST INFRASTRUCTURE.
+
+(The geometries and seeded request inputs live in the product package,
+wam_b200.workload, and are re-exported here for the tests.)
 
 The same integer-hash generator runs on the device inside the engine
 (launch_synth_bf16 in wam.cpp_b200/csrc/elementwise.cu): every BF16 value is a
@@ -16,9 +19,17 @@ Tensor names and shapes follow the reference's compact GGUF naming
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+import sys
+from pathlib import Path
 
 import numpy as np
+
+_PKG = Path(__file__).resolve().parent.parent / "wam.cpp_b200"
+if str(_PKG) not in sys.path:
+    sys.path.insert(0, str(_PKG))
+
+from wam_b200.workload import (CONFIG2, CONFIG2_L1, CONFIG2_L2, PAIR, SMALL, STEPK,  # noqa: E402,F401
+                               TALL, TINY, WIDE, Geometry, Request, make_request, statistics)
 
 GOLDEN = np.uint64(0x9E3779B97F4A7C15)
 M1 = np.uint64(0xBF58476D1CE4E5B9)
@@ -78,66 +89,6 @@ def synth_bits(seed: int, name: str, n: int, scale: float, center: float) -> np.
         v = z.astype(np.float32) * k + c
         out[s:s + len(idx)] = f32_to_bf16_bits(v)
     return out
-
-
-@dataclass
-class Geometry:
-    hidden: int = 3072
-    layers: int = 30
-    heads: int = 24
-    ffn: int = 14336
-    action_hidden: int = 3072
-    action_ffn: int = 14336
-    action_dim: int = 32
-    real_state_dim: int = 14
-    real_action_dim: int = 14
-    num_embodiments: int = 1
-    embodiment_id: int = 0
-    grid_h: int = 32
-    grid_w: int = 24
-    vae_z: int = 48
-    action_chunk: int = 48
-    steps: int = 10
-    prompt_tokens: int = 512
-    text_dim: int = 4096
-    norm_eps: float = 1e-6
-    flow_shift: float = 1.0
-
-    @property
-    def visual_tokens(self) -> int:
-        return self.grid_h * self.grid_w
-
-    @property
-    def prefix_tokens(self) -> int:
-        return 1 + self.visual_tokens
-
-
-# BASELINE config 2 (full GWP-0.5-shaped MoT) and small parity configs.
-CONFIG2 = Geometry()
-TINY = Geometry(hidden=256, layers=2, heads=2, ffn=512, action_hidden=256, action_ffn=384,
-                grid_h=4, grid_w=4, vae_z=16, action_chunk=16, steps=3, prompt_tokens=16,
-                text_dim=128)
-SMALL = Geometry(hidden=512, layers=3, heads=4, ffn=1024, action_hidden=384, action_ffn=768,
-                 grid_h=6, grid_w=8, vae_z=48, action_chunk=48, steps=4, prompt_tokens=64,
-                 text_dim=256)
-# Action-expert widths that are multiples of 256 with the config-2 chunk of 48
-# tokens: the engine runs these denoise steps as its persistent step kernel.
-STEPK = Geometry(hidden=512, layers=3, heads=4, ffn=1024, action_hidden=512, action_ffn=1024,
-                 grid_h=4, grid_w=6, vae_z=16, action_chunk=48, steps=3, prompt_tokens=32,
-                 text_dim=256)
-# 144 visual tokens: the prefix attention (145 / 144 queries) runs as 128-query
-# tensor-core tiles.
-TALL = Geometry(hidden=256, layers=2, heads=2, ffn=512, action_hidden=256, action_ffn=384,
-                grid_h=12, grid_w=12, vae_z=16, action_chunk=16, steps=2, prompt_tokens=16,
-                text_dim=128)
-# 320 visual and 272 prompt tokens: the prefix and prompt GEMMs (>= 256 token
-# rows) run on CTA pairs, split over 2 or 4 pairs where their tiles are few.
-PAIR = Geometry(hidden=512, layers=2, heads=4, ffn=1024, action_hidden=512, action_ffn=1024,
-                grid_h=16, grid_w=20, vae_z=16, action_chunk=16, steps=2, prompt_tokens=272,
-                text_dim=256)
-WIDE = Geometry(hidden=1536, layers=2, heads=12, ffn=3072, action_hidden=1536, action_ffn=3072,
-                grid_h=4, grid_w=4, vae_z=16, action_chunk=48, steps=2, prompt_tokens=32,
-                text_dim=256)
 
 
 def tensor_specs(g: Geometry) -> list[tuple[str, tuple[int, ...]]]:
@@ -249,30 +200,3 @@ def quantize_q8_linear(g: Geometry, weights: dict[str, np.ndarray]) -> dict[str,
         d = quants.dequantize(q, gguf.GGMLQuantizationType.Q8_0).astype(np.float32)
         out[name] = f32_to_bf16_bits(d.reshape(-1)).reshape(w.shape)
     return out
-
-
-def statistics(g: Geometry) -> dict[str, np.ndarray]:
-    """state/action q01/q99 statistics (F32 [action_dim]) of the synthetic artifact."""
-    i = np.arange(g.action_dim, dtype=np.float32)
-    lo = (-1.0 - 0.01 * i).astype(np.float32)
-    hi = (1.0 + 0.02 * i).astype(np.float32)
-    return {"state_q01": lo, "state_q99": hi, "action_q01": lo.copy(), "action_q99": hi.copy()}
-
-
-@dataclass
-class Request:
-    state: np.ndarray   # [real_state_dim]
-    latent: np.ndarray  # [vae_z, 2 gh, 2 gw]
-    prompt: np.ndarray  # [prompt_tokens, text_dim]
-    noise: np.ndarray   # [T, A]
-    extra: dict = field(default_factory=dict)
-
-
-def make_request(g: Geometry, seed: int) -> Request:
-    r = np.random.Generator(np.random.PCG64(seed))
-    return Request(
-        state=r.standard_normal(g.real_state_dim, dtype=np.float32),
-        latent=r.standard_normal((g.vae_z, 2 * g.grid_h, 2 * g.grid_w), dtype=np.float32),
-        prompt=r.standard_normal((g.prompt_tokens, g.text_dim), dtype=np.float32),
-        noise=r.standard_normal((g.action_chunk, g.action_dim), dtype=np.float32),
-    )

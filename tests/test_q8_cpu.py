@@ -36,3 +36,28 @@ def test_q8_restatement_matches_gguf(seed):
     d = ref[:, :2].copy().view(np.float16).astype(np.float32)
     q = ref[:, 2:].view(np.int8).astype(np.float32)
     assert np.array_equal((q * d).reshape(x.shape), deq)
+
+
+@pytest.mark.parametrize("seed", [0, 3])
+def test_oracle_q8_f32_dequant_matches_gguf(seed):
+    """The oracle's config-5 weights are dequantize_row_q8_0's F32 values
+    (gguf.quants.dequantize), bit for bit: no BF16 rounding of q * d."""
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(repo)]
+    import oracle
+    from oracle import synth
+
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal(64 * 512) * 0.02).astype(np.float32)
+    x[:32] = 0.0                                   # zero block: d = 0, q = 0
+    x[32:64] = np.float32(1e-6) * np.arange(32)    # tiny block (fp16 d near subnormal)
+    x[64:96] = np.linspace(-1, 1, 32, dtype=np.float32) * np.float32(127 / 64)  # ties
+    bits = synth.f32_to_bf16_bits(x)
+    xf = synth.bf16_bits_to_f32(bits).reshape(-1, 32)
+    want = quants.dequantize(quants.quantize(xf, gguf.GGMLQuantizationType.Q8_0),
+                             gguf.GGMLQuantizationType.Q8_0).astype(np.float32).reshape(-1)
+    got = oracle.q8_roundtrip(bits)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))

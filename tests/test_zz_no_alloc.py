@@ -6,12 +6,18 @@ and unbounded latency an allocation may cause, and a host framework that owns
 the device allocator may forbid side allocations. This entry point runs the
 same GEMM with its split-K scratch in a fixed, library-owned device array.
 
-Checked here through the C ABI: its output matches the existing entry point
-(wam_b200_op_gemm) within the GEMM tests' tolerance (raw F32 accumulators
-within 1e-5 relative-L2, BF16 epilogue outputs within 1e-2) on two calls in a
-row (the second call reuses the array's leftover contents), and shapes beyond
-the array's size are rejected. This file is collected last so that a run that
-stops at the first failure has already run every other test.
+Checked here through the C ABI, on two calls in a row (the second call reuses
+the array's leftover contents: its tile counters and error word):
+  * the output matches the existing entry point (wam_b200_op_gemm with a
+    caller workspace) within the GEMM tests' tolerance (raw F32 accumulators
+    within 1e-5 relative-L2, BF16 epilogue outputs within 1e-2) and an
+    independent F32 matmul of the same BF16 operands within 1e-2;
+  * the error word reads 0 after every call;
+  * a split count above 8 (tile counters, the last CTA of a tile reduces),
+    and an unsplit shape with more output tiles than the array has counters,
+    both run; a split-K shape whose partials exceed the array is rejected.
+This file is collected last so that a run that stops at the first failure has
+already run every other test.
 """
 import ctypes as C
 
@@ -37,9 +43,24 @@ def _noalloc(lib, x, w, epi, bias, out, splits):
                                         out.stride(0), splits, s)
 
 
+def _error_word(lib):
+    code = C.c_uint(0xFFFFFFFF)
+    assert lib.wam_b200_op_gemm_noalloc_error(C.byref(code)) == 0
+    return code.value
+
+
+def _f32_reference(x, w, b, epi):
+    acc = x.float() @ w.float().T
+    if epi == 6:
+        return acc
+    # EPI_BIAS: bf16(bf16(acc) + b)
+    return (acc.to(torch.bfloat16).float() + b.float()).to(torch.bfloat16)
+
+
 @pytest.mark.parametrize("m,n,k,splits,epi", [
     (48, 3072, 3072, 0, 6),     # batch-1 denoise projection, automatic split-K, F32 out
     (48, 3072, 3072, 3, 6),     # a split count clusters cannot take
+    (48, 3072, 3072, 12, 6),    # > 8 splits: tile counters, the last CTA reduces
     (48, 768, 1024, 7, 0),      # BF16 output with bias
 ])
 def test_noalloc_matches_workspace_gemm_twice(cuda_device, m, n, k, splits, epi):
@@ -47,20 +68,45 @@ def test_noalloc_matches_workspace_gemm_twice(cuda_device, m, n, k, splits, epi)
     from wam_b200 import ops
 
     lib = wam_b200.load()
-    g = torch.Generator(device="cpu").manual_seed(m + n + k)
+    g = torch.Generator(device="cpu").manual_seed(m + n + k + splits)
     x = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
     w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).cuda()
     b = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16).cuda()
     dt = torch.float32 if epi == 6 else torch.bfloat16
     ref = ops.gemm(x, w, epi, bias=b, scratch=ops.Scratch(), force_splits=splits)
+    f32 = _f32_reference(x, w, b, epi)
     tol = 1e-5 if epi == 6 else 1e-2
     for _ in range(2):
         out = torch.full((m, n), float("nan"), dtype=dt, device="cuda")
         rc = _noalloc(lib, x, w, epi, b, out, splits)
         assert rc == 0, wam_b200.last_error()
         torch.cuda.synchronize()
+        assert _error_word(lib) == 0
         assert torch.isfinite(out.float()).all()
         assert rel_l2(out.float(), ref.float()) < tol
+        assert rel_l2(out.float(), f32.float()) < 1e-2
+
+
+def test_noalloc_large_unsplit_shape(cuda_device):
+    """Batch-64 prefix shape: 384 x 12 = 4608 output tiles (more than the
+    array's 4096 tile counters) but unsplit and persistent, so it needs none
+    of the array's partials or counters."""
+    import wam_b200
+
+    lib = wam_b200.load()
+    g = torch.Generator(device="cpu").manual_seed(5)
+    m, n, k = 49152, 3072, 3072
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    b = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16).cuda()
+    ref = _f32_reference(x, w, b, 0)
+    for _ in range(2):
+        out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        rc = _noalloc(lib, x, w, 0, b, out, 0)
+        assert rc == 0, wam_b200.last_error()
+        torch.cuda.synchronize()
+        assert _error_word(lib) == 0
+        assert rel_l2(out.float(), ref.float()) < 1e-2
 
 
 def test_noalloc_rejects_oversized_split(cuda_device):

@@ -248,6 +248,61 @@ WAM_B200_API int wam_b200_op_layernorm(const void* x, int rows, int cols, const 
   return WAM_B200_OK;
 }
 
+WAM_B200_API int wam_b200_op_qkv_scatter(const wam_b200_qkv_scatter_args* p, void* stream) {
+  std::string why;
+  int rc = check_sm100(&why);
+  if (rc != WAM_B200_OK) {
+    set_last_error(why);
+    return rc;
+  }
+  if (!p || !p->src || p->rows < 1 || p->rows_per_seq < 1 || p->rows % p->rows_per_seq ||
+      p->heads < 1 || p->ld_src % 8 || p->rope_mode < 0 || p->rope_mode > 2 ||
+      (p->rope_mode && !p->inv_freq) || (p->rope_mode == 2 && !p->pos_thw) ||
+      (p->q_col >= 0 && !p->q_out) || (p->k_col >= 0 && !p->k_out) || (p->v_col >= 0 && !p->v_out)) {
+    set_last_error("qkv_scatter: invalid arguments");
+    return WAM_B200_INVALID_ARGUMENT;
+  }
+  const int H = p->heads * 128;
+  for (int c : {p->q_col, p->k_col, p->v_col})
+    if (c >= 0 && (c % 8 || c + H > p->ld_src)) {
+      set_last_error("qkv_scatter: source columns must be multiples of 8 inside the row");
+      return WAM_B200_INVALID_ARGUMENT;
+    }
+  QkvScatter q{};
+  q.src = static_cast<const bf16*>(p->src);
+  q.ld_src = p->ld_src;
+  q.rows = p->rows;
+  q.rows_per_seq = p->rows_per_seq;
+  q.hidden = H;
+  q.heads = p->heads;
+  q.q_col = p->q_col;
+  q.k_col = p->k_col;
+  q.v_col = p->v_col;
+  q.q_norm = static_cast<const bf16*>(p->q_norm);
+  q.k_norm = static_cast<const bf16*>(p->k_norm);
+  q.eps = p->eps;
+  q.rope_mode = p->rope_mode;
+  q.pos_base = p->pos_base;
+  q.pos_thw = p->pos_thw;
+  q.inv_freq = p->inv_freq;
+  q.q_out = static_cast<bf16*>(p->q_out);
+  q.q_seq_stride = p->q_seq_stride;
+  q.q_head_stride = p->q_head_stride;
+  q.q_row_offset = p->q_row_offset;
+  q.k_out = static_cast<bf16*>(p->k_out);
+  q.v_out = static_cast<bf16*>(p->v_out);
+  q.kv_seq_stride = p->kv_seq_stride;
+  q.kv_head_stride = p->kv_head_stride;
+  q.kv_row_offset = p->kv_row_offset;
+  launch_qkv_scatter(q, static_cast<cudaStream_t>(stream));
+  cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) {
+    set_last_error(std::string("qkv_scatter launch: ") + cudaGetErrorString(ce));
+    return WAM_B200_CUDA_ERROR;
+  }
+  return WAM_B200_OK;
+}
+
 WAM_B200_API int wam_b200_op_synth(void* w, long long n, uint64_t seed, double scale,
                                    double center, void* stream) {
   std::string why;

@@ -618,19 +618,11 @@ bool MotEngine::alloc_buffers(std::string* err) {
   std::vector<float> dt(S);
   for (size_t s = 0; s < S; ++s) dt[s] = sigmas_[s + 1] - sigmas_[s];
   CK(cudaMemcpyAsync(dt_, dt.data(), S * 4, cudaMemcpyHostToDevice, stream_));
-  // RoPE NORMAL inverse frequencies theta_scale^i, theta_scale = base^(-2/n_dims)
-  // (ggml_rope_ext, mot.cpp:175-202), one table for the 1-D action rope and one
-  // for the three visual sections.
-  std::vector<float> f1(64), f3(64, 0.0f);
-  {
-    const float ts = std::pow(10000.0f, -2.0f / 128.0f);
-    for (int i = 0; i < 64; ++i) f1[i] = std::pow(ts, static_cast<float>(i));
-    const int sec[3] = {44, 42, 42}, base[3] = {0, 22, 43};
-    for (int k = 0; k < 3; ++k) {
-      const float t3 = std::pow(10000.0f, -2.0f / static_cast<float>(sec[k]));
-      for (int i = 0; i < sec[k] / 2; ++i) f3[base[k] + i] = std::pow(t3, static_cast<float>(i));
-    }
-  }
+  // RoPE inverse frequencies: one table for the 1-D action rope and one for
+  // the three visual sections.
+  std::vector<float> f1(64), f3(64);
+  rope_inv_freq(1, f1.data());
+  rope_inv_freq(2, f3.data());
   CK(cudaMemcpyAsync(inv_freq1_, f1.data(), 256, cudaMemcpyHostToDevice, stream_));
   CK(cudaMemcpyAsync(inv_freq3_, f3.data(), 256, cudaMemcpyHostToDevice, stream_));
   // visual_positions (semantics.cpp:235-257): t = 0, h = y, w = x.

@@ -14,8 +14,10 @@
 // kScratchFloats floats plus kScratchCounters counters until the process exits.
 // All calls share it and it keeps the last call's contents, so the counters and
 // the error word are cleared (cudaMemsetAsync, no allocation) before every
-// launch. Calls that overlap on the GPU (two streams, or two host threads on
-// the same device) race on the array and must be serialized by the caller.
+// launch; wam_b200_op_gemm_noalloc_error reads the error word back (the status
+// of the last call on the current device). Calls that overlap on the GPU (two
+// streams, or two host threads on the same device) race on the array and must
+// be serialized by the caller.
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -86,15 +88,6 @@ WAM_B200_API int wam_b200_op_gemm_noalloc(const void* x, int ldx, int m, const v
     set_last_error(std::string("gemm_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(ce));
     return WAM_B200_CUDA_ERROR;
   }
-  int tiles = 0;
-  const size_t need = gemm_scratch_floats(m, n, k, num_sms_current(), force_splits, &tiles);
-  if (need > kScratchFloats || tiles > kScratchCounters) {
-    set_last_error("gemm_noalloc: shape needs " + std::to_string(need) +
-                   " split-K floats and " + std::to_string(tiles) + " tile counters; the built-in "
-                   "scratch holds " + std::to_string(kScratchFloats) + " and " +
-                   std::to_string(kScratchCounters) + " (use wam_b200_op_gemm with a workspace)");
-    return WAM_B200_INVALID_ARGUMENT;
-  }
   GemmScratch scratch;
   scratch.workspace = static_cast<float*>(base);
   scratch.workspace_floats = kScratchFloats;
@@ -103,14 +96,27 @@ WAM_B200_API int wam_b200_op_gemm_noalloc(const void* x, int ldx, int m, const v
   scratch.error = scratch.counters + kScratchCounters;
   const bool tiled = (epilogue & WAM_B200_GEMM_TILED_WEIGHTS) != 0;
   const bool q8 = (epilogue & WAM_B200_GEMM_Q8_WEIGHTS) != 0;
-  epilogue &= ~(WAM_B200_GEMM_TILED_WEIGHTS | WAM_B200_GEMM_Q8_WEIGHTS);
+  const bool pair = (epilogue & WAM_B200_GEMM_PAIR) != 0;
+  epilogue &= ~(WAM_B200_GEMM_TILED_WEIGHTS | WAM_B200_GEMM_Q8_WEIGHTS | WAM_B200_GEMM_PAIR);
   GemmOp op;
+  // gemm_plan checks the exact scratch need of the mode it picks: unsplit,
+  // persistent and cluster-split shapes need no counters whatever their tile
+  // count; only split-K partials must fit the array.
   const char* err = gemm_plan(&op, static_cast<const bf16*>(x), ldx, m, static_cast<const bf16*>(w),
                               n, k, epilogue, static_cast<const bf16*>(bias), gate,
                               static_cast<const bf16*>(residual), ldr, out, ldo, scratch,
-                              num_sms_current(), force_splits, tiled, q8);
+                              num_sms_current(), force_splits, tiled, q8, pair);
   if (err) {
-    set_last_error(err);
+    std::string msg(err);
+    if (msg.find("scratch too small") != std::string::npos) {
+      int tiles = 0;
+      const size_t need = gemm_scratch_floats(m, n, k, num_sms_current(), force_splits, &tiles);
+      msg = "gemm_noalloc: shape needs " + std::to_string(need) + " split-K floats and " +
+            std::to_string(tiles) + " output tiles; the built-in scratch holds " +
+            std::to_string(kScratchFloats) + " floats and " + std::to_string(kScratchCounters) +
+            " tile counters (use wam_b200_op_gemm with a workspace)";
+    }
+    set_last_error(msg);
     return WAM_B200_INVALID_ARGUMENT;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -120,6 +126,29 @@ WAM_B200_API int wam_b200_op_gemm_noalloc(const void* x, int ldx, int m, const v
   if (ce == cudaSuccess) ce = gemm_launch(op, s);
   if (ce != cudaSuccess) {
     set_last_error(std::string("gemm_noalloc launch: ") + cudaGetErrorString(ce));
+    return WAM_B200_CUDA_ERROR;
+  }
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_op_gemm_noalloc_error(unsigned* code) {
+  if (!code) {
+    set_last_error("gemm_noalloc_error: null output");
+    return WAM_B200_INVALID_ARGUMENT;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_last_error("gemm_noalloc_error: no usable current device");
+    return WAM_B200_CUDA_ERROR;
+  }
+  void* base = nullptr;
+  cudaError_t ce = scratch_address(dev, &base);
+  if (ce == cudaSuccess)
+    ce = cudaMemcpy(code, reinterpret_cast<unsigned*>(static_cast<float*>(base) + kScratchFloats) +
+                              kScratchCounters,
+                    sizeof(unsigned), cudaMemcpyDeviceToHost);
+  if (ce != cudaSuccess) {
+    set_last_error(std::string("gemm_noalloc_error: ") + cudaGetErrorString(ce));
     return WAM_B200_CUDA_ERROR;
   }
   return WAM_B200_OK;

@@ -37,6 +37,20 @@ void timestep_embedding(float t, int dim, float* out) {
   }
 }
 
+void rope_inv_freq(int mode, float* out) {
+  for (int i = 0; i < 64; ++i) out[i] = 0.0f;
+  if (mode == 1) {
+    const float ts = std::pow(10000.0f, -2.0f / 128.0f);
+    for (int i = 0; i < 64; ++i) out[i] = std::pow(ts, static_cast<float>(i));
+    return;
+  }
+  const int sec[3] = {44, 42, 42}, base[3] = {0, 22, 43};
+  for (int k = 0; k < 3; ++k) {
+    const float t3 = std::pow(10000.0f, -2.0f / static_cast<float>(sec[k]));
+    for (int i = 0; i < sec[k] / 2; ++i) out[base[k] + i] = std::pow(t3, static_cast<float>(i));
+  }
+}
+
 void visual_positions(int gh, int gw, int* thw) {
   for (int y = 0; y < gh; ++y)
     for (int x = 0; x < gw; ++x) {
@@ -78,6 +92,12 @@ WAM_B200_API int wam_b200_flow_schedule(int steps, float shift, float* timesteps
   wamb::flow_schedule(steps, shift, &ts, &sg);
   std::copy(ts.begin(), ts.end(), timesteps);
   std::copy(sg.begin(), sg.end(), sigmas);
+  return WAM_B200_OK;
+}
+
+WAM_B200_API int wam_b200_rope_inv_freq(int mode, float* out64) {
+  if ((mode != 1 && mode != 2) || !out64) return WAM_B200_INVALID_ARGUMENT;
+  wamb::rope_inv_freq(mode, out64);
   return WAM_B200_OK;
 }
 

@@ -13,6 +13,12 @@ void flow_schedule(int steps, float shift, std::vector<float>* timesteps,
                    std::vector<float>* sigmas);
 // timestep_embedding (src/models/gwp05/engine/text_encoder.cpp:1-12).
 void timestep_embedding(float t, int dim, float* out);
+// RoPE NORMAL inverse frequencies theta_scale^i, theta_scale = base^(-2/n_dims)
+// (ggml_rope_ext as called by apply_rope_1d / apply_visual_rope,
+// src/models/gwp05/engine/mot.cpp:175-202). mode 1: the 1-D action rope over
+// 128 dims, out[0..63]; mode 2: the three visual sections 44/42/42 at
+// out[0..21], out[22..42], out[43..63].
+void rope_inv_freq(int mode, float* out64);
 // visual_positions (src/models/gwp05/semantics.cpp:235-257), [gh*gw][3] = (t, h, w).
 void visual_positions(int gh, int gw, int* thw);
 // State normalisation (engine.cpp:249-253, semantics.cpp:154-172): the first

@@ -45,6 +45,7 @@ def load(path: Path | None = None):
          [vp, i32, i32, vp, i32, i32, i32, vp, vp, vp, i32, vp, i32, vp, sz, vp, i32, vp, i32, vp])
     _sig(lib, "wam_b200_op_gemm_noalloc", i32,
          [vp, i32, i32, vp, i32, i32, i32, vp, vp, vp, i32, vp, i32, i32, vp])
+    _sig(lib, "wam_b200_op_gemm_noalloc_error", i32, [u32p])
     _sig(lib, "wam_b200_op_retile_weights", i32, [vp, vp, i32, i32, vp])
     _sig(lib, "wam_b200_op_q8_quantize", i32, [vp, C.c_longlong, vp, vp])
     _sig(lib, "wam_b200_op_q8_retile", i32, [vp, vp, i32, i32, vp])
@@ -52,6 +53,8 @@ def load(path: Path | None = None):
          [vp, C.c_longlong, C.c_longlong, vp, vp, C.c_longlong, C.c_longlong, i32, i32, i32, i32,
           C.c_float, vp, i32, vp])
     _sig(lib, "wam_b200_op_layernorm", i32, [vp, i32, i32, vp, vp, C.c_float, i32, vp, vp])
+    _sig(lib, "wam_b200_op_qkv_scatter", i32, [vp, vp])
+    _sig(lib, "wam_b200_rope_inv_freq", i32, [i32, C.POINTER(C.c_float)])
     _sig(lib, "wam_b200_op_synth", i32, [vp, C.c_longlong, C.c_uint64, C.c_double, C.c_double, vp])
     _sig(lib, "wam_b200_tensor_seed", C.c_uint64, [C.c_uint64, C.c_char_p])
     f32p = C.POINTER(C.c_float)

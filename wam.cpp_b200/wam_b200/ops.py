@@ -158,3 +158,73 @@ def synth(n, seed, name, scale, center, device="cuda"):
     rc = lib.wam_b200_op_synth(_ptr(w), n, ts, scale, center, _stream())
     check(rc, "wam_b200_op_synth")
     return w
+
+
+class QkvScatterArgs(C.Structure):
+    """wam_b200_qkv_scatter_args (include/wam_b200.h)."""
+
+    _fields_ = [("src", C.c_void_p), ("ld_src", C.c_int), ("rows", C.c_int),
+                ("rows_per_seq", C.c_int), ("heads", C.c_int), ("q_col", C.c_int),
+                ("k_col", C.c_int), ("v_col", C.c_int), ("q_norm", C.c_void_p),
+                ("k_norm", C.c_void_p), ("eps", C.c_float), ("rope_mode", C.c_int),
+                ("pos_base", C.c_int), ("pos_thw", C.c_void_p), ("inv_freq", C.c_void_p),
+                ("q_out", C.c_void_p), ("q_seq_stride", C.c_longlong),
+                ("q_head_stride", C.c_longlong), ("q_row_offset", C.c_int),
+                ("k_out", C.c_void_p), ("v_out", C.c_void_p), ("kv_seq_stride", C.c_longlong),
+                ("kv_head_stride", C.c_longlong), ("kv_row_offset", C.c_int)]
+
+
+def rope_inv_freq(mode: int, device="cuda"):
+    """RoPE inverse frequencies [64] of wam_b200_rope_inv_freq, on the device."""
+    buf = (C.c_float * 64)()
+    check(load().wam_b200_rope_inv_freq(mode, buf), "wam_b200_rope_inv_freq")
+    return torch.tensor(list(buf), dtype=torch.float32, device=device)
+
+
+def qkv_scatter(src, heads, rows_per_seq, q_out=None, k_out=None, v_out=None, q_norm=None,
+                k_norm=None, eps=1e-6, rope_mode=0, pos_base=0, pos_thw=None, q_row_offset=0,
+                kv_row_offset=0, cols=(0, None, None)):
+    """src: [rows, ld] BF16 packed projection; q_out: [B, heads, Rq, 128],
+    k_out / v_out: [B, heads, Rkv, 128] BF16 caches (written at the row offsets).
+    cols: first source column of (q, k, v); None skips a part."""
+    H = heads * 128
+    a = QkvScatterArgs()
+    a.src = src.data_ptr()
+    a.ld_src = src.stride(0)
+    a.rows = src.shape[0]
+    a.rows_per_seq = rows_per_seq
+    a.heads = heads
+    qc, kc, vc = cols
+    a.q_col = -1 if qc is None else qc
+    a.k_col = -1 if kc is None else kc
+    a.v_col = -1 if vc is None else vc
+    a.q_norm = q_norm.data_ptr() if q_norm is not None else None
+    a.k_norm = k_norm.data_ptr() if k_norm is not None else None
+    a.eps = eps
+    a.rope_mode = rope_mode
+    a.pos_base = pos_base
+    keep = []
+    if rope_mode:
+        inv = rope_inv_freq(rope_mode, src.device)
+        keep.append(inv)
+        a.inv_freq = inv.data_ptr()
+    if pos_thw is not None:
+        a.pos_thw = pos_thw.data_ptr()
+    if q_out is not None:
+        a.q_out = q_out.data_ptr()
+        a.q_seq_stride = q_out.stride(0)
+        a.q_head_stride = q_out.stride(1)
+    a.q_row_offset = q_row_offset
+    kv = k_out if k_out is not None else v_out
+    if k_out is not None:
+        a.k_out = k_out.data_ptr()
+    if v_out is not None:
+        a.v_out = v_out.data_ptr()
+    if kv is not None:
+        a.kv_seq_stride = kv.stride(0)
+        a.kv_head_stride = kv.stride(1)
+    a.kv_row_offset = kv_row_offset
+    assert H <= src.shape[1]
+    rc = load().wam_b200_op_qkv_scatter(C.byref(a), _stream())
+    check(rc, "wam_b200_op_qkv_scatter")
+    torch.cuda.current_stream().synchronize() if keep else None
