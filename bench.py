@@ -5,7 +5,8 @@ per GPU: prompt projection + 30-layer prefix cache + 10 flow-matching Euler
 steps), synthetic random-init BF16 weights and seeded synthetic inputs of the
 config's shapes. With --gpus N the engine runs as N independent data-parallel
 replicas (one process per GPU, no collective); value = all chunks / max-over-
-ranks time.
+ranks time. The same line carries "config4": BASELINE config 4, 64 requests
+per box split 64/N per GPU (strong scaling), timed after the main measurement.
 
   python bench.py [--gpus N --steps K --warmup W]        this engine
   python bench.py --impl reference [...]                 the reference arm: the
@@ -132,27 +133,48 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(layers: int, timed_runs: int = 1) -> dict:
-    """The oracle (CPU restatement of the reference path) on a bounded sample:
-    one config-2 chunk through `layers` of the 30 layers, extrapolated."""
+def cpu_sample(layers: int, uncached: bool = False, runs: int = 1, warmup: int = 0) -> dict:
+    """Times the oracle (the CPU restatement of the reference path) on a bounded
+    sample: one config-2 chunk through `layers` of the 30 layers. Cached mode =
+    prefix once + 10 action-expert steps (this engine's schedule); un-cached =
+    the whole MoT every step, the reference's own CPU behaviour
+    (engine.cpp:334-337)."""
     import oracle
-    from oracle import synth
+    from wam_b200 import workload as wl
 
     g = config2(layers)
     m = oracle.OracleModel(g, None, seed=SEED, bias_scale=0.0)
-    r = synth.make_request(g, SEED)
+    if uncached:
+        m.set_uncached(True)
+    r = wl.make_request(g, SEED)
+    for _ in range(warmup):
+        m.predict(r)
     times = []
-    for _ in range(timed_runs):
+    for _ in range(runs):
         t0 = time.perf_counter()
         m.predict(r)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
-    full = t * 30 / layers
-    return {"value": 1.0 / full, "unit": UNIT, "cores": oracle.lib().oracle_threads(),
-            "kind": "port", "sample_seconds": t,
-            "sample": f"one config-2 chunk (prompt projection, prefix, 10 Euler steps) through "
-                      f"{layers} of 30 layers, F32 OpenMP oracle; chunk time extrapolated x{30 / layers:g} "
-                      f"({full:.1f} s/chunk)"}
+    return {"sample_seconds": t, "runs": runs, "layers": layers, "factor": 30 / layers,
+            "chunk_seconds_extrapolated": t * 30 / layers, "mode": "uncached" if uncached else "cached",
+            "cores": oracle.lib().oracle_threads()}
+
+
+def cpu_baseline(layers: int) -> dict:
+    """The cpu_baseline object of the bench line: cached (value) and the
+    labelled un-cached mode, each one bounded sample extrapolated to 30 layers."""
+    c = cpu_sample(layers)
+    u = cpu_sample(layers, uncached=True)
+    return {"value": 1.0 / c["chunk_seconds_extrapolated"], "unit": UNIT, "cores": c["cores"],
+            "kind": "port", "sample_seconds": c["sample_seconds"],
+            "sample": f"one config-2 chunk (prompt projection, prefix once, 10 Euler steps) through "
+                      f"{layers} of 30 layers, F32 OpenMP oracle, {c['sample_seconds']:.2f} s; chunk "
+                      f"time extrapolated x{30 / layers:g} ({c['chunk_seconds_extrapolated']:.1f} s/chunk)",
+            "uncached": {"value": 1.0 / u["chunk_seconds_extrapolated"], "unit": UNIT,
+                         "sample_seconds": u["sample_seconds"],
+                         "sample": f"the reference's CPU mode (whole MoT every step): {layers} of 30 "
+                                   f"layers, {u['sample_seconds']:.2f} s, extrapolated x{30 / layers:g} "
+                                   f"({u['chunk_seconds_extrapolated']:.1f} s/chunk)"}}
 
 
 def host_cpu_model() -> str:
@@ -166,87 +188,38 @@ def host_cpu_model() -> str:
 
 
 def run_reference(args) -> None:
+    """The reference arm: the CPU restatement of the reference's path on the
+    host cores (the reference's own ggml CPU path cannot be built here). Each
+    step is one bounded sample (one config-2 chunk through --cpu-layers of the
+    30 layers, cached mode); ms_per_step is that sample's measured time, and
+    value is the chunk rate extrapolated to 30 layers (field "extrapolation")."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # the CPU arm runs once per box, on rank 0
-    import oracle
-    from oracle import synth
-
     layers = args.cpu_layers
-    g = config2(layers)
-    m = oracle.OracleModel(g, None, seed=SEED, bias_scale=0.0)
-    r = synth.make_request(g, SEED)
-    m.predict(r)  # one untimed warm-up sample (page-in, thread pool start)
-    vals = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        m.predict(r)
-        vals.append((time.perf_counter() - t0) * 30 / layers)
-    per_chunk = statistics.median(vals)
+    smp = cpu_sample(layers, runs=args.steps, warmup=args.warmup)
+    per_chunk = smp["chunk_seconds_extrapolated"]
     value = 1.0 / per_chunk
-    cb = {"value": value, "unit": UNIT, "cores": oracle.lib().oracle_threads(), "kind": "port",
+    unc = cpu_sample(layers, uncached=True)
+    cb = {"value": value, "unit": UNIT, "cores": smp["cores"], "kind": "port",
           "cpu_model": host_cpu_model(),
-          "sample": f"each step: one config-2 chunk (prompt projection, prefix, 10 Euler steps) "
-                    f"through {layers} of 30 layers with the F32 OpenMP oracle, time x{30 / layers:g}"}
+          "sample": f"each step: one config-2 chunk (prompt projection, prefix once, 10 Euler "
+                    f"steps) through {layers} of 30 layers with the F32 OpenMP oracle "
+                    f"({smp['sample_seconds']:.2f} s median), rate extrapolated x{30 / layers:g}",
+          "uncached": {"value": 1.0 / unc["chunk_seconds_extrapolated"], "unit": UNIT,
+                       "sample_seconds": unc["sample_seconds"],
+                       "sample": "the reference's own CPU mode (whole MoT every step, "
+                                 "engine.cpp:334-337), one run of the same sample"}}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": 1, "ms_per_step": per_chunk * 1e3,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": smp["sample_seconds"] * 1e3,
+            "extrapolation": {"measured": f"{layers} of 30 layers per step",
+                              "factor": 30 / layers, "ms_per_chunk": per_chunk * 1e3},
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": workload(config2(), 1), "cpu_baseline": cb,
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference's ggml CPU path cannot be built here (llama.cpp b9866 is not "
                     "vendored); this arm times the oracle/ C++ restatement of that path"}
     print(json.dumps(line), flush=True)
-
-
-def roofline_from_profile(prof: list[dict], pk: dict) -> tuple[dict, dict, dict]:
-    """Roofline of the dominant kernel from the engine's per-op profile of one
-    chunk (CUDA events around every launch on the engine's stream):
-      * denoise-phase GEMMs (weight streaming, HBM bound): algorithmic bytes
-        (weights + activations in + outputs) / device time;
-      * prefix-phase GEMMs (tensor bound): algorithmic FLOPs / device time."""
-    def agg(phase, kind):
-        ops = [o for o in prof if o["phase"] == phase and o["kind"] == kind]
-        return (sum(o["ms"] for o in ops) / 1e3, sum(o["bytes"] for o in ops),
-                sum(o["flops"] for o in ops), len(ops))
-
-    sec, byts, _, n = agg("denoise", "gemm")
-    hbm = {"bound": "hbm", "kernel": "gemm_bf16_tc_kernel, denoise phase (M = 48 tokens per request)",
-           "achieved": byts / sec / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
-           "frac": byts / sec / 1e9 / pk["hbm_gbs"], "traffic": None,
-           "algorithmic_bytes_per_launch": byts / n, "avg_launch_us": sec / n * 1e6, "launches": n,
-           "peak_source": pk["source"] + " HBM copy (burst)"}
-    traffic = REPO / "profiles" / "gemm_traffic.json"
-    if traffic.exists():
-        hbm["traffic"] = json.loads(traffic.read_text()).get("denoise_bytes_per_launch")
-    sec2, _, flops, n2 = agg("prefix", "gemm")
-    tc = {"bound": "tensor", "kernel": "gemm_bf16_tc_kernel, prefix phase (768 visual tokens)",
-          "achieved": flops / sec2 / 1e12, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-          "frac": flops / sec2 / 1e12 / pk["bf16_tflops"], "avg_launch_us": sec2 / n2 * 1e6,
-          "launches": n2, "peak_source": pk["source"] + " cuBLAS bf16 (burst)"}
-    total = sum(o["ms"] for o in prof)
-    br = {}
-    for o in prof:
-        k = o["phase"] + "/" + o["kind"]
-        br[k] = br.get(k, 0.0) + o["ms"]
-    breakdown = {k: {"ms": round(v, 3), "share": round(v / total, 4)} for k, v in
-                 sorted(br.items(), key=lambda kv: -kv[1])}
-    breakdown["_total_eager_ms"] = round(total, 3)
-    shapes = {}
-    for o in prof:
-        if o["kind"] == "gemm" and o["phase"] in ("denoise", "prefix"):
-            m, n, k, sp = o["shape"]
-            # sp < 0: the CTA-pair kernel with -sp splits
-            key = f'{o["phase"]}:{m}x{n}x{k}/' + (f"p{-sp}" if sp < 0 else f"s{sp}")
-            e = shapes.setdefault(key, [0, 0.0, 0.0])
-            e[0] += 1
-            e[1] += o["ms"]
-            e[2] += o["bytes"] if o["phase"] == "denoise" else o["flops"]
-    breakdown["_gemm_shapes"] = {
-        k: {"launches": v[0], "avg_us": round(v[1] / v[0] * 1e3, 2),
-            ("GB/s" if k.startswith("denoise") else "TFLOP/s"):
-                round(v[2] / (v[1] / 1e3) / (1e9 if k.startswith("denoise") else 1e12), 1)}
-        for k, v in sorted(shapes.items(), key=lambda kv: -kv[1][1])}
-    return hbm, tc, breakdown
 
 
 def run_op_case(args) -> None:
@@ -397,6 +370,10 @@ def main() -> None:
                     help="op case gemm: split-K factor (0 = the planner's choice)")
     ap.add_argument("--scratch", action="store_true",
                     help="op case gemm: split-K partials through a global workspace (as the engine)")
+    ap.add_argument("--config4-requests", type=int, default=64,
+                    help="BASELINE config 4: requests per box, split over the GPUs (0 = skip)")
+    ap.add_argument("--config4-steps", type=int, default=3,
+                    help="timed chunks of the config-4 block per GPU")
     ap.add_argument("--attention-bench", action="store_true",
                     help="BASELINE config 3: the attention microbench over cache length and batch")
     args = ap.parse_args()
@@ -415,7 +392,7 @@ def main() -> None:
     import numpy as np
     import torch
     from wam_b200 import dp as dp_host
-    from wam_b200 import workload
+    from wam_b200 import workload as wl
     from wam_b200.engine import Engine, Req
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -445,7 +422,7 @@ def main() -> None:
                  prompt_cache=False)
     reqs = []
     for i in range(B):
-        r = workload.make_request(g, dp_host.request_seed(SEED, rank, i))
+        r = wl.make_request(g, dp_host.request_seed(SEED, rank, i))
         reqs.append(Req(r.state, r.latent, r.prompt, r.noise))
     stream = torch.cuda.ExternalStream(eng.stream())
     kernels_per_chunk = eng.kernel_launches(B, with_prompt=True)
@@ -490,9 +467,24 @@ def main() -> None:
     eng.stage(reqs)
     eng.run(B)
     phases = eng.phase_ms()
-    prof = eng.profile(B)
     pk = peaks()
-    hbm_roof, tc_roof, breakdown = roofline_from_profile(prof, pk)
+    # Roofline of the dominant kernels: their launches replayed alone inside a
+    # CUDA graph (same plans and buffers as the timed chunk); the eager per-op
+    # profile after it only gives the breakdown by kind.
+    hbm_roof = graph_roofline(eng, B, "denoise", pk, "hbm")
+    tc_roof = graph_roofline(eng, B, "prefix", pk, "tensor")
+    eng.stage(reqs)
+    prof = eng.profile(B)
+    breakdown = breakdown_from_profile(prof)
+    del eng
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    barrier()
+
+    # ---- 64 requests per box, 64 / N per GPU (strong scaling)
+    c4 = None
+    if args.config4_requests > 0:
+        c4 = run_config4(args, g, world, rank, local, barrier, max_over_ranks)
     barrier()
     if dist:
         dist.destroy_process_group()
@@ -509,14 +501,118 @@ def main() -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": {**workload(g, B, args.weights), "parallelism": f"dp{world} (replicas, no collective)"},
         "roofline": hbm_roof, "roofline_tensor": tc_roof, "clocks": clocks.summary(),
-        "phase_ms": phases, "kernel_breakdown": breakdown,
+        "phase_ms": phases, "kernel_breakdown_eager": breakdown,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_s * 1e3 / args.steps},
         "gpu_launches": kernels_per_chunk * args.steps,
         "kernels_per_chunk": kernels_per_chunk,
+        "config4": c4,
         "cpu_baseline": cb,
     }
     print(json.dumps(line), flush=True)
+
+
+def run_config4(args, g, world, rank, local, barrier, max_over_ranks) -> dict:
+    """R independent requests per box (default 64), sharded
+    in contiguous blocks of R / N per GPU (wam_b200.dp.shard), one engine per
+    GPU running its block as one batch; no collective on the data path. Times
+    `--config4-steps` chunks of the whole block after 3 warm-up ones."""
+    import torch
+    from wam_b200 import dp as dp_host
+    from wam_b200 import workload as wl
+    from wam_b200.engine import Engine, Req
+
+    R = args.config4_requests
+    start, stop = dp_host.shard(R, world, rank)
+    b = stop - start
+    eng = Engine(g, seed=SEED, bias_scale=0.0, device=local, max_batch=b, graphs=True,
+                 weights=args.weights, prompt_cache=False)
+    reqs = []
+    for i in range(start, stop):
+        r = wl.make_request(g, dp_host.request_seed(SEED, 0, i))
+        reqs.append(Req(r.state, r.latent, r.prompt, r.noise))
+    eng.stage(reqs)
+    for _ in range(3):
+        eng.run(b)
+    stream = torch.cuda.ExternalStream(eng.stream())
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record()
+        for _ in range(args.config4_steps):
+            eng.run(b)
+        e1.record()
+    torch.cuda.synchronize()
+    t = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    phases = eng.phase_ms()
+    del eng
+    torch.cuda.empty_cache()
+    return {"workload": f"config4: {R} independent config-2 requests per box in contiguous blocks "
+                        f"of {R}/{world} per GPU (data parallel, no collective)",
+            "requests_per_box": R, "requests_per_gpu": b, "steps": args.config4_steps, "warmup": 3,
+            "value": R * args.config4_steps / t, "unit": UNIT, "scaling": "strong",
+            "ms_per_step": t * 1e3 / args.config4_steps, "phase_ms_rank0": phases}
+
+
+def graph_roofline(eng, B, phase, pk, bound) -> dict:
+    """Achieved HBM bandwidth (denoise GEMMs, weight streaming) or tensor
+    throughput (prefix GEMMs) of one phase's GEMM launches, replayed alone in a
+    CUDA graph (wam_b200_profile_graph) and timed with CUDA events on the
+    engine's stream."""
+    r = eng.profile_graph(B, phase, "gemm", reps=5)
+    sec = r["ms"] / 1e3
+    n = max(r["launches"], 1)
+    if bound == "hbm":
+        ach = r["bytes"] / sec / 1e9
+        out = {"bound": "hbm", "kernel": "gemm_tc_kernel, denoise phase (M = 48 tokens per request)",
+               "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
+               "algorithmic_bytes_per_launch": r["bytes"] / n,
+               "peak_source": pk["source"] + " HBM copy (burst)"}
+        traffic = REPO / "profiles" / "gemm_traffic.json"
+        out["traffic"] = (json.loads(traffic.read_text()).get("denoise_bytes_per_launch")
+                          if traffic.exists() else None)
+        out["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the same GEMM "
+                                 "shapes, launch-weighted (profiles/gemm_traffic.json); not measured "
+                                 "in this run")
+    else:
+        ach = r["flops"] / sec / 1e12
+        out = {"bound": "tensor", "kernel": "gemm_tc_kernel / persistent, prefix phase (768 visual tokens)",
+               "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+               "frac": ach / pk["bf16_tflops"], "peak_source": pk["source"] + " cuBLAS bf16 (burst)"}
+    out.update({"avg_launch_us": sec / n * 1e6, "launches": r["launches"],
+                "timing": f"the chunk's {r['launches']} {phase}-phase GEMM launches captured alone in "
+                          f"a CUDA graph (same plans, buffers and PDL), CUDA events around 5 replays"})
+    return out
+
+
+def breakdown_from_profile(prof: list[dict]) -> dict:
+    """Device time by (phase, kind) and by GEMM shape from the engine's eager
+    per-op profile (CUDA events around every op, no graph, no PDL overlap)."""
+    total = sum(o["ms"] for o in prof)
+    br = {}
+    for o in prof:
+        k = o["phase"] + "/" + o["kind"]
+        br[k] = br.get(k, 0.0) + o["ms"]
+    breakdown = {k: {"ms": round(v, 3), "share": round(v / total, 4)} for k, v in
+                 sorted(br.items(), key=lambda kv: -kv[1])}
+    breakdown["_total_eager_ms"] = round(total, 3)
+    shapes = {}
+    for o in prof:
+        if o["kind"] == "gemm" and o["phase"] in ("denoise", "prefix"):
+            m, n, k, sp = o["shape"]
+            # sp < 0: the CTA-pair kernel with -sp splits
+            key = f'{o["phase"]}:{m}x{n}x{k}/' + (f"p{-sp}" if sp < 0 else f"s{sp}")
+            e = shapes.setdefault(key, [0, 0.0, 0.0])
+            e[0] += 1
+            e[1] += o["ms"]
+            e[2] += o["bytes"] if o["phase"] == "denoise" else o["flops"]
+    breakdown["_gemm_shapes"] = {
+        k: {"launches": v[0], "avg_us": round(v[1] / v[0] * 1e3, 2),
+            ("GB/s" if k.startswith("denoise") else "TFLOP/s"):
+                round(v[2] / (v[1] / 1e3) / (1e9 if k.startswith("denoise") else 1e12), 1)}
+        for k, v in sorted(shapes.items(), key=lambda kv: -kv[1][1])}
+    return breakdown
 
 
 if __name__ == "__main__":

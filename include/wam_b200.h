@@ -343,6 +343,22 @@ typedef struct wam_b200_op_profile {
 WAM_B200_API int wam_b200_profile(wam_b200_engine* engine, int batch, wam_b200_op_profile* out,
                                   int max_ops, wam_b200_status* status);
 
+/* Device time of one (phase, kind) of the staged batch's chunk inside a CUDA
+ * graph: the ops of that phase and kind (e.g. phase 2, kind 0 = every denoise
+ * GEMM) captured alone, in issue order, with the same launches and buffers as
+ * the chunk's graphs, replayed `reps` times between CUDA events after one
+ * warm-up replay. ms = device time per replay; bytes / flops = the ops'
+ * algorithmic HBM bytes / FLOPs per replay; launches = kernels per replay.
+ * Leaves the engine's activations overwritten (the next run recomputes them). */
+typedef struct wam_b200_graph_profile {
+  float ms;
+  double bytes, flops;
+  int launches;
+} wam_b200_graph_profile;
+WAM_B200_API int wam_b200_profile_graph(wam_b200_engine* engine, int batch, int phase, int kind,
+                                        int reps, wam_b200_graph_profile* out,
+                                        wam_b200_status* status);
+
 /* Stage dumps as F32 (the reference's WAM_GWP05_CACHE_DUMP_DIR stages,
  * engine/cache.cpp:441-469): "prefix_k"/"prefix_v" [heads][1+V][128],
  * "prompt_k"/"prompt_v" [heads][prompt_tokens][128] of one layer,

@@ -195,3 +195,20 @@ def test_oracle_prefix_state_row_uses_action_rope_position_zero(tiny_oracle):
     r = synth.make_request(g, 3)
     d = om.predict(r, dumps=True)
     assert d["prefix_k"].shape[2] == 1 + g.grid_h * g.grid_w
+
+
+def test_engine_adapter_library_exports():
+    """lib/libwam_b200_adapter.so (B200Engine compiled against the reference's
+    engine.h) loads next to libwam_b200.so and exports its harness; no GPU call."""
+    import ctypes as C
+
+    adapter = REPO / "wam.cpp_b200" / "lib" / "libwam_b200_adapter.so"
+    if not adapter.exists():
+        pytest.skip("adapter not built here (needs WAM_REFERENCE_ROOT at build time)")
+    import wam_b200
+
+    wam_b200.load()
+    lib = C.CDLL(str(adapter))
+    for sym in ("wam_b200_adapter_create", "wam_b200_adapter_destroy", "wam_b200_adapter_predict",
+                "wam_b200_adapter_reset", "wam_b200_adapter_cfg", "wam_b200_adapter_stats"):
+        assert hasattr(lib, sym), sym

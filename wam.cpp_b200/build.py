@@ -21,6 +21,8 @@ CSRC = HERE / "csrc"
 BUILD = HERE / "_build"
 LIB_DIR = HERE / "lib"
 LIB = LIB_DIR / "libwam_b200.so"
+ADAPTER_SRC = HERE / "adapter" / "b200_engine.cpp"
+ADAPTER_LIB = LIB_DIR / "libwam_b200_adapter.so"
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -70,9 +72,36 @@ def build(force: bool = False, jobs: int | None = None) -> Path:
     return LIB
 
 
+def build_adapter(reference_root: str | os.PathLike, force: bool = False) -> Path:
+    """Compiles the B200Engine adapter (adapter/b200_engine.cpp) against the
+    reference's own engine.h (reference_root/src, reference_root/include: the
+    headers only, no reference source is compiled) into lib/libwam_b200_adapter.so,
+    linked to libwam_b200.so."""
+    ref = Path(reference_root)
+    if not (ref / "src" / "models" / "gwp05" / "engine" / "engine.h").exists():
+        raise SystemExit(f"{ref} does not hold the reference's engine.h")
+    deps = [ADAPTER_SRC, HERE / "adapter" / "b200_engine.h", REPO / "include" / "wam_b200.h", LIB]
+    if (not force and ADAPTER_LIB.exists()
+            and ADAPTER_LIB.stat().st_mtime >= max(d.stat().st_mtime for d in deps)):
+        return ADAPTER_LIB
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-fvisibility=hidden",
+           "-I", str(ref / "src"), "-I", str(ref / "include"), "-I", str(REPO / "include"),
+           "-I", str(HERE / "adapter"), str(ADAPTER_SRC), "-L", str(LIB_DIR), "-lwam_b200",
+           "-Wl,-rpath,$ORIGIN", "-o", str(ADAPTER_LIB)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise SystemExit("adapter build failed")
+    return ADAPTER_LIB
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--jobs", type=int, default=None)
+    ap.add_argument("--reference", default=os.environ.get("WAM_REFERENCE_ROOT"),
+                    help="reference source tree: also build the B200Engine adapter against it")
     a = ap.parse_args()
     print(build(a.force, a.jobs))
+    if a.reference:
+        print(build_adapter(a.reference, a.force))

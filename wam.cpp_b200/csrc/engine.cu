@@ -1902,6 +1902,70 @@ bool MotEngine::profile(int batch, std::vector<OpProfile>* out, std::string* err
   return true;
 }
 
+bool MotEngine::profile_graph(int batch, int phase, int kind, int reps, float* ms, double* bytes,
+                              double* flops, int* launches, std::string* err) {
+  if (batch != staged_batch_) {
+    *err = "profile_graph() batch differs from the staged batch";
+    return false;
+  }
+  if (phase < 0 || phase > 2 || reps < 1) {
+    *err = "profile_graph(): phase 0..2 and reps >= 1";
+    return false;
+  }
+  auto it = plans_.find(batch);
+  if (it == plans_.end() || it->second->scratch_gen != scratch_gen_) {
+    if (!build(batch, err)) return false;
+    it = plans_.find(batch);
+  }
+  Program& p = it->second->prog[phase];
+  *bytes = 0.0;
+  *flops = 0.0;
+  *launches = 0;
+  cudaGraph_t graph = nullptr;
+  CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+  cudaError_t le = cudaSuccess;
+  for (auto& op : p.ops) {
+    if (op.kind != kind) continue;
+    le = op.fn(stream_);  // every lane on the main stream: one chain of launches
+    if (le != cudaSuccess) break;
+    *bytes += op.bytes;
+    *flops += op.flops;
+    *launches += op.launches;
+  }
+  cudaError_t ce = cudaStreamEndCapture(stream_, &graph);
+  if (le != cudaSuccess || ce != cudaSuccess || !graph) {
+    if (graph) cudaGraphDestroy(graph);
+    *err = std::string("profile_graph capture: ") + cudaGetErrorString(le != cudaSuccess ? le : ce);
+    return false;
+  }
+  cudaGraphExec_t exec = nullptr;
+  ce = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ce != cudaSuccess) {
+    *err = std::string("profile_graph instantiate: ") + cudaGetErrorString(ce);
+    return false;
+  }
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  ce = cudaEventCreate(&e0);
+  if (ce == cudaSuccess) ce = cudaEventCreate(&e1);
+  if (ce == cudaSuccess) ce = cudaGraphLaunch(exec, stream_);  // warm-up replay
+  if (ce == cudaSuccess) ce = cudaEventRecord(e0, stream_);
+  for (int r = 0; r < reps && ce == cudaSuccess; ++r) ce = cudaGraphLaunch(exec, stream_);
+  if (ce == cudaSuccess) ce = cudaEventRecord(e1, stream_);
+  if (ce == cudaSuccess) ce = cudaEventSynchronize(e1);
+  float total = 0.0f;
+  if (ce == cudaSuccess) ce = cudaEventElapsedTime(&total, e0, e1);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  cudaGraphExecDestroy(exec);
+  if (ce != cudaSuccess) {
+    *err = std::string("profile_graph replay: ") + cudaGetErrorString(ce);
+    return false;
+  }
+  *ms = total / reps;
+  return true;
+}
+
 bool MotEngine::fetch(const RequestView* reqs, int batch, float* out, std::string* err) {
   const Geometry& g = g_;
   const int A = g.action_dim, T = g.action_chunk, R = g.real_action_dim;

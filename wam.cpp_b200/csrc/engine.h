@@ -128,6 +128,12 @@ class MotEngine {
   int kernels_per_chunk(int batch, bool with_prompt);
   // Runs one chunk eagerly with CUDA events around every op (staged inputs).
   bool profile(int batch, std::vector<OpProfile>* out, std::string* err);
+  // Device time of the ops of one (phase, kind) of the staged batch's plan,
+  // captured alone into a CUDA graph (same launches, same buffers, PDL between
+  // them) and replayed `reps` times between events: ms per replay, plus their
+  // algorithmic bytes / FLOPs and kernel launches per replay.
+  bool profile_graph(int batch, int phase, int kind, int reps, float* ms, double* bytes,
+                     double* flops, int* launches, std::string* err);
   // Device times of the phases of the last run() (ms): prompt, prefix, denoise.
   bool last_phase_ms(float* prompt, float* prefix, float* denoise);
   // Debug view of device state as F32 (names: prefix_k, prefix_v, prompt_k,

@@ -228,6 +228,23 @@ WAM_B200_API int wam_b200_profile(wam_b200_engine* e, int batch, wam_b200_op_pro
   return n;
 }
 
+WAM_B200_API int wam_b200_profile_graph(wam_b200_engine* e, int batch, int phase, int kind,
+                                        int reps, wam_b200_graph_profile* out,
+                                        wam_b200_status* st) {
+  if (!e || !out) return fail(st, WAM_B200_INVALID_ARGUMENT, "engine and output are required");
+  std::string err;
+  float ms = 0.0f;
+  double bytes = 0.0, flops = 0.0;
+  int launches = 0;
+  if (!e->impl->profile_graph(batch, phase, kind, reps, &ms, &bytes, &flops, &launches, &err))
+    return fail(st, code_of(err), err);
+  out->ms = ms;
+  out->bytes = bytes;
+  out->flops = flops;
+  out->launches = launches;
+  return ok(st);
+}
+
 WAM_B200_API int wam_b200_read_tensor(wam_b200_engine* e, const char* name, int slot, int layer,
                                       float* out, size_t n, wam_b200_status* st) {
   if (!e || !name || !out) return fail(st, WAM_B200_INVALID_ARGUMENT, "engine, name and output are required");

@@ -42,6 +42,11 @@ class OpProfile(C.Structure):
                 ("bytes", C.c_double), ("flops", C.c_double), ("shape", C.c_int * 4)]
 
 
+class GraphProfile(C.Structure):
+    _fields_ = [("ms", C.c_float), ("bytes", C.c_double), ("flops", C.c_double),
+                ("launches", C.c_int)]
+
+
 def attach(lib, sig) -> None:
     vp, i32, sz = C.c_void_p, C.c_int, C.c_size_t
     f32p = C.POINTER(C.c_float)
@@ -62,3 +67,4 @@ def attach(lib, sig) -> None:
     sig(lib, "wam_b200_read_tensor", i32, [vp, C.c_char_p, i32, i32, f32p, sz, st])
     sig(lib, "wam_b200_phase_ms", i32, [vp, f32p, f32p, f32p])
     sig(lib, "wam_b200_profile", i32, [vp, i32, C.POINTER(OpProfile), i32, st])
+    sig(lib, "wam_b200_profile_graph", i32, [vp, i32, i32, i32, i32, C.POINTER(GraphProfile), st])

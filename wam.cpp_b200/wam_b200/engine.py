@@ -15,7 +15,8 @@ from dataclasses import dataclass
 import numpy as np
 
 from ._lib import load
-from ._lib_engine import GEOM_FIELDS, Geometry, OpProfile, Options, Request, Stats, Status
+from ._lib_engine import (GEOM_FIELDS, Geometry, GraphProfile, OpProfile, Options, Request, Stats,
+                          Status)
 
 KINDS = ("gemm", "attention", "layernorm", "qkv_scatter", "small_linear", "elementwise", "sync",
          "l2_prefetch", "denoise_step")
@@ -179,6 +180,15 @@ class Engine:
         return [{"phase": PHASES[a.phase], "kind": KINDS[a.kind], "launches": a.launches,
                  "ms": a.ms, "bytes": a.bytes, "flops": a.flops, "shape": list(a.shape)}
                 for a in arr[:rc]]
+
+    def profile_graph(self, batch: int, phase: str, kind: str, reps: int = 5) -> dict:
+        """Device time of the (phase, kind) ops of the staged batch replayed
+        alone in a CUDA graph (wam_b200_profile_graph)."""
+        out, st = GraphProfile(), Status()
+        rc = self.lib.wam_b200_profile_graph(self.h, batch, PHASES.index(phase), KINDS.index(kind),
+                                             reps, C.byref(out), C.byref(st))
+        _raise(self.lib, rc, st, "wam_b200_profile_graph")
+        return {"ms": out.ms, "bytes": out.bytes, "flops": out.flops, "launches": out.launches}
 
     def reset(self):
         self.lib.wam_b200_reset(self.h)
