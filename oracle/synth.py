@@ -28,7 +28,7 @@ _PKG = Path(__file__).resolve().parent.parent / "wam.cpp_b200"
 if str(_PKG) not in sys.path:
     sys.path.insert(0, str(_PKG))
 
-from wam_b200.workload import (CONFIG2, CONFIG2_L1, CONFIG2_L2, PAIR, SMALL, STEPK,  # noqa: E402,F401
+from wam_b200.workload import (CONFIG2, CONFIG2_L1, CONFIG2_L2, PAIR, SMALL,  # noqa: E402,F401
                                TALL, TINY, WIDE, Geometry, Request, make_request, statistics)
 
 GOLDEN = np.uint64(0x9E3779B97F4A7C15)

@@ -13,7 +13,6 @@
 // (mot.cpp:299-321).
 #include "kernels.h"
 #include "launch.cuh"
-#include "prefetch.cuh"
 #include "ptx.cuh"
 
 namespace wamb {
@@ -63,9 +62,6 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
   const int head = blockIdx.y;
   const int seq = blockIdx.z;
 
-  if (tid == 0)
-    l2_prefetch_share(a.pf, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z),
-                      gridDim.x * gridDim.y * gridDim.z);
   const bf16* qg = a.q + seq * a.q_seq_stride + head * a.q_head_stride + static_cast<long long>(q0) * kD;
   const bf16* kg = a.k + seq * a.kv_seq_stride + head * a.kv_head_stride;
   const bf16* vg = a.v + seq * a.kv_seq_stride + head * a.kv_head_stride;

@@ -9,7 +9,6 @@
 #include "kernels.h"
 #include "launch.cuh"
 #include "mathops.cuh"
-#include "prefetch.cuh"
 #include "ptx.cuh"
 
 namespace wamb {
@@ -64,8 +63,7 @@ __device__ __forceinline__ float block128_sum(float v, float* red) {
 template <int MODE, int MAXC>
 __global__ void __launch_bounds__(kRowThreads)
     ln_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
-              const void* pb, float eps, bf16* __restrict__ y, int ldy, const __grid_constant__ L2Prefetch pf) {
-  if (threadIdx.x == 0) l2_prefetch_share(pf, blockIdx.x, gridDim.x);
+              const void* pb, float eps, bf16* __restrict__ y, int ldy) {
   griddep_wait();
   griddep_launch_dependents();
   __shared__ float red[4];
@@ -202,8 +200,7 @@ __global__ void __launch_bounds__(kRowThreads, 12)
 template <int MODE>
 __global__ void __launch_bounds__(256)
     ln_wide_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
-                   const void* pb, float eps, bf16* __restrict__ y, int ldy, const __grid_constant__ L2Prefetch pf) {
-  if (threadIdx.x == 0) l2_prefetch_share(pf, blockIdx.x, gridDim.x);
+                   const void* pb, float eps, bf16* __restrict__ y, int ldy) {
   griddep_wait();
   griddep_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -265,7 +262,6 @@ __device__ __forceinline__ float rope_theta(const QkvScatter& a, int dim, int po
 // weights) in registers. MAXC = 0: generic loop.
 template <int MAXC>
 __global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const __grid_constant__ QkvScatter a) {
-  if (threadIdx.x == 0 && threadIdx.y == 0) l2_prefetch_share(a.pf, blockIdx.x, gridDim.x);
   griddep_wait();
   griddep_launch_dependents();
   __shared__ float red[3][4];
@@ -502,10 +498,10 @@ inline int grid_for(long long n, int threads) {
 
 template <int MODE>
 void launch_ln(const bf16* x, int ldx, int rows, int cols, const void* pa, const void* pb,
-               float eps, bf16* y, int ldy, cudaStream_t s, const L2Prefetch& pf) {
+               float eps, bf16* y, int ldy, cudaStream_t s) {
   const int per = (cols / 8 + kRowThreads - 1) / kRowThreads;
   const dim3 grid(rows), block(kRowThreads);
-  if (rows >= 1024 && per <= 4 && !pf.ptr[0] && !pf.ptr[1]) {  // many rows: bandwidth shape
+  if (rows >= 1024 && per <= 4) {  // many rows: bandwidth shape
     if (per <= 1)
       launch_pdl(ln_stream_kernel<MODE, 1>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
     else if (per <= 2)
@@ -517,39 +513,26 @@ void launch_ln(const bf16* x, int ldx, int rows, int cols, const void* pa, const
     return;
   }
   if (per <= 1)
-    launch_pdl(ln_kernel<MODE, 1>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy, pf);
+    launch_pdl(ln_kernel<MODE, 1>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
   else if (per <= 2)
-    launch_pdl(ln_kernel<MODE, 2>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy, pf);
+    launch_pdl(ln_kernel<MODE, 2>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
   else if (per <= 3)
-    launch_pdl(ln_kernel<MODE, 3>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy, pf);
+    launch_pdl(ln_kernel<MODE, 3>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
   else if (per <= 4)
-    launch_pdl(ln_kernel<MODE, 4>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy, pf);
+    launch_pdl(ln_kernel<MODE, 4>, grid, block, 0, s, x, ldx, rows, cols, pa, pb, eps, y, ldy);
   else
     launch_pdl(ln_wide_kernel<MODE>, dim3((rows + 7) / 8), dim3(256), 0, s, x, ldx, rows, cols,
-               pa, pb, eps, y, ldy, pf);
+               pa, pb, eps, y, ldy);
 }
 
 void launch_ln_modulate(const bf16* x, int ldx, int rows, int cols, const float* scale,
-                        const float* shift, float eps, bf16* y, int ldy, cudaStream_t s,
-                        const L2Prefetch& pf) {
-  launch_ln<0>(x, ldx, rows, cols, scale, shift, eps, y, ldy, s, pf);
+                        const float* shift, float eps, bf16* y, int ldy, cudaStream_t s) {
+  launch_ln<0>(x, ldx, rows, cols, scale, shift, eps, y, ldy, s);
 }
 
 void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w, const bf16* b,
-                      float eps, bf16* y, int ldy, cudaStream_t s, const L2Prefetch& pf) {
-  launch_ln<1>(x, ldx, rows, cols, w, b, eps, y, ldy, s, pf);
-}
-
-namespace {
-// Every thread of the grid prefetches its share of the ranges into L2.
-__global__ void l2_prefetch_kernel(const __grid_constant__ L2Prefetch pf) {
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  l2_prefetch_share(pf, t, gridDim.x * blockDim.x);
-}
-}  // namespace
-
-void launch_l2_prefetch(const L2Prefetch& pf, cudaStream_t s) {
-  l2_prefetch_kernel<<<32, 64, 0, s>>>(pf);
+                      float eps, bf16* y, int ldy, cudaStream_t s) {
+  launch_ln<1>(x, ldx, rows, cols, w, b, eps, y, ldy, s);
 }
 
 void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s) {

@@ -243,23 +243,8 @@ bool MotEngine::init(const EngineOptions& opt, std::string* err) {
   // Diagnostic switch: keep GEMM weights in GGUF's row-major layout.
   const char* rm = std::getenv("WAM_B200_ROWMAJOR_WEIGHTS");
   rowmajor_weights_ = rm && rm[0] && rm[0] != '0';
-  // L2 prefetch of the next GEMM's weights while the denoise step's
-  // attention / LayerNorm / scatter kernels run: "kernel" (those kernels issue
-  // it) or "side" (a small prefetch grid on the second stream). Off by
-  // default: on B200 both made the chunk slower (57.7 and 56.7 ms against
-  // 54.9 ms without), the weight stream gains nothing from L2 residency.
-  const char* pm = std::getenv("WAM_B200_L2_PREFETCH");
-  prefetch_mode_ = !pm ? 0 : (std::strcmp(pm, "kernel") == 0 ? 1 : (std::strcmp(pm, "side") == 0 ? 2 : 0));
-  // WAM_B200_STEP_KERNEL=1: run each denoise step of <= 128 tokens as the
-  // persistent step kernel (step.cu) instead of separate kernels (GEMM,
-  // LayerNorm, scatter, attention). Off by default: on B200 at batch 1 it
-  // measured 53.2 ms for the 10 steps against 36.5 ms for the separate
-  // kernels (its phases are latency bound; see the step kernel's notes).
-  const char* sk = std::getenv("WAM_B200_STEP_KERNEL");
-  step_kernel_ = sk && sk[0] == '1';
   CK(gemm_init(opt.device));
   CK(attention_init());
-  CK(step_init());
   if (!load_weights(err)) return false;
   const Geometry& g = g_;
   if (g.heads * 128 != g.hidden || g.hidden % 128 || g.action_hidden % 128 || g.ffn % 128 ||
@@ -587,24 +572,6 @@ bool MotEngine::alloc_buffers(std::string* err) {
   AL(gemm_ws_[0], float, gemm_ws_floats_);
   AL(gemm_ws_[1], float, gemm_ws_floats_);
   // Persistent denoise step (batches of up to 128 tokens).
-  step_batch_ = 0;
-  for (int b = static_cast<int>(B); b >= 1; --b)
-    if (step_usable(b)) {
-      step_batch_ = b;
-      break;
-    }
-  if (step_batch_ > 0) {
-    const size_t Fa = g.action_ffn;
-    AL(xa_t_, bf16, E * 128);
-    AL(at_t_, bf16, H * 128);
-    AL(ff_t_, bf16, Fa * 128);
-    AL(step_ws_, float, step_ws_floats(sms_, 128));
-    // attention split rows [batch][heads][8 splits][64][132], then the row-join
-    // statistics [128][8][2]
-    AL(step_attn_ws_, float, static_cast<size_t>(step_batch_) * heads * 8 * 64 * 132 + 128 * 8 * 2);
-    step_ctr_n_ = static_cast<size_t>(16 * L + 8) + static_cast<size_t>(step_batch_) * heads + 128 + 2;
-    AL(step_ctr_, unsigned, step_ctr_n_);
-  }
 #undef AL
   // constants: timestep frequencies (row 0: t = 0 for the prefix, rows 1..S the
   // schedule), dt, RoPE inverse frequencies, visual positions, table pointers.
@@ -669,20 +636,6 @@ bool MotEngine::ensure_tiled(const std::string& wname, int n, int k, std::string
   CK(cudaGetLastError());
   tiled_[wname] = true;
   return true;
-}
-
-bool MotEngine::step_usable(int batch) const {
-  if (!step_kernel_ || rowmajor_weights_ || opt_.weight_format != 0) return false;
-  const Geometry& g = g_;
-  const int T = g.action_chunk, M = batch * T;
-  const int E = g.action_hidden, H = g.hidden, Fa = g.action_ffn;
-  if (M > 128 || T > 64 || E % 256 || H % 256 || Fa % 256 || E > 4096 || H > 4096 ||
-      g.heads * 128 != H)
-    return false;
-  // Stream-K: a CTA's k-block range spans at most 2 tiles when there are no
-  // more weight tiles than CTAs.
-  auto fits = [&](long long n, long long k) { return n / step_tile_rows() <= sms_ && k >= 64; };
-  return fits(3LL * H, E) && fits(E, H) && fits(H, E) && fits(Fa, E) && fits(E, Fa);
 }
 
 bool MotEngine::gemm(Program& p, const bf16* x, int ldx, int m, const std::string& wname, int n,
@@ -780,30 +733,6 @@ bool MotEngine::build(int b, std::string* err) {
       }, OP_SYNC, 0);
       p.lane = lane;
     };
-    // Side-lane L2 prefetch (prefetch_mode_ 2): starts once everything issued
-    // so far on the main stream is done, runs beside the main stream's next
-    // ops; nothing waits for it.
-    auto side_prefetch = [&](Program& p, std::pair<const void*, long long> a,
-                             std::pair<const void*, long long> b = {nullptr, 0}) {
-      if (prefetch_mode_ != 2) return;
-      L2Prefetch pf;
-      pf.ptr[0] = a.first;
-      pf.bytes[0] = a.second;
-      pf.ptr[1] = b.first;
-      pf.bytes[1] = b.second;
-      const int lane = p.lane;
-      p.lane = 0;
-      p.add([this](cudaStream_t) {
-        cudaError_t e = cudaEventRecord(ev_fork_, stream_);
-        return e == cudaSuccess ? cudaStreamWaitEvent(side_, ev_fork_, 0) : e;
-      }, OP_SYNC, 0);
-      p.lane = 1;
-      p.add([pf](cudaStream_t st) {
-        launch_l2_prefetch(pf, st);
-        return cudaGetLastError();
-      }, OP_PREFETCH, 1, 0.0);
-      p.lane = lane;
-    };
     auto join_side = [&](Program& p) {
       const int lane = p.lane;
       p.lane = 0;
@@ -834,34 +763,11 @@ bool MotEngine::build(int b, std::string* err) {
       }, OP_ATTENTION, 1, 2.0 * bq + bkv, 4.0 * a.batch * a.heads * double(a.lq) * a.lk * 128.0);
     };
     auto ln_mod = [&](Program& p, const bf16* x, int rows, int cols, const float* scale,
-                      const float* shift, bf16* y, L2Prefetch pf = L2Prefetch()) {
+                      const float* shift, bf16* y) {
       p.add([=](cudaStream_t s) {
-        launch_ln_modulate(x, cols, rows, cols, scale, shift, eps, y, cols, s, pf);
+        launch_ln_modulate(x, cols, rows, cols, scale, shift, eps, y, cols, s);
         return cudaGetLastError();
       }, OP_LAYERNORM, 1, 4.0 * rows * double(cols) + 8.0 * cols);
-    };
-    // Weight bytes of a GEMM, for L2 prefetch by the op that precedes it.
-    auto wrange = [&](const std::string& wn, long long n, long long k, long long skip = 0,
-                      long long cap = -1) {
-      std::pair<const void*, long long> r{nullptr, 0};
-      const bf16* w = W(wn + ".weight", n * k);
-      if (!w) return r;
-      long long bytes = n * k * 2 - skip;
-      if (cap >= 0 && bytes > cap) bytes = cap;
-      if (bytes <= 0) return r;
-      r.first = reinterpret_cast<const char*>(w) + skip;
-      r.second = bytes;
-      return r;
-    };
-    auto mkpf = [&](std::pair<const void*, long long> a,
-                    std::pair<const void*, long long> b = {nullptr, 0}) {
-      L2Prefetch pf;
-      if (prefetch_mode_ != 1) return pf;
-      pf.ptr[0] = a.first;
-      pf.bytes[0] = a.second;
-      pf.ptr[1] = b.first;
-      pf.bytes[1] = b.second;
-      return pf;
     };
     auto ln_aff = [&](Program& p, const bf16* x, int rows, int cols, const std::string& wn, bf16* y) {
       const bf16* w = W(wn + ".weight", cols);
@@ -889,9 +795,8 @@ bool MotEngine::build(int b, std::string* err) {
       }, OP_SMALL, 1, 2.0 * (double(n) * k + double(m) * k + double(m) * n), 2.0 * m * n * double(k));
     };
     auto cross_q = [&](Program& p, const bf16* src, int rows, int rows_per_seq,
-                       const std::string& pfx, bf16* qout, L2Prefetch pf = L2Prefetch()) {
+                       const std::string& pfx, bf16* qout) {
       QkvScatter q{};
-      q.pf = pf;
       q.src = src;
       q.ld_src = H;
       q.rows = rows;
@@ -1198,349 +1103,6 @@ bool MotEngine::build(int b, std::string* err) {
     const bf16* ain_b = W("gwp.action.in.bias", static_cast<int64_t>(g.num_embodiments) * 128);
     const bf16* dout_w = W("gwp.decode.out.weight", static_cast<int64_t>(g.num_embodiments) * 128 * A);
     const bf16* dout_b = W("gwp.decode.out.bias", static_cast<int64_t>(g.num_embodiments) * A);
-    // Persistent step kernel (step.cu): one launch per step runs every layer.
-    const bool use_step = step_usable(b) && b <= step_batch_;
-    const int step_nops = 14 * L + 1, step_ngemm = 6 * L;
-    std::vector<StepOp> hops;
-    std::vector<StepGemm> hgemms;
-    StepOp* d_ops = nullptr;
-    StepGemm* d_gemms = nullptr;
-    if (use_step) {
-      if (static_cast<size_t>(step_nops) + static_cast<size_t>(b) * heads + 128 + 2 > step_ctr_n_) {
-        *err = "step kernel: counter buffer too small";
-        return false;
-      }
-      d_ops = dalloc<StepOp>(static_cast<size_t>(S) * step_nops, err);
-      if (!d_ops) return false;
-      d_gemms = dalloc<StepGemm>(static_cast<size_t>(S) * step_ngemm, err);
-      if (!d_gemms) return false;
-    }
-    const int step_mr = ((b * T + 15) / 16) * 16;
-    auto attn_splits = [&](int lk) {
-      const int nk = (lk + 63) / 64;
-      int best = 1;
-      for (int c = 2; c <= 8; ++c)
-        if (b * heads * c <= sms_ && nk / c >= 2) best = c;
-      return best;
-    };
-    // Ops of one step in the step kernel's order (mot.cpp:358-496), with the
-    // same operands and rounding points as the multi-kernel loop below.
-    // Stream-K partial-slot tables, one per GEMM shape: tile t of an n x k GEMM
-    // split over `ctas` CTAs is held by the CTAs whose k-block ranges meet it
-    // (at most 8 when ctas <= 7 tiles); entry = cta * 2 + slot, -1 = none.
-    std::vector<int> seg_host;
-    std::map<std::pair<int, int>, std::pair<size_t, int>> seg_of;  // (n, k) -> (offset, max slots)
-    std::vector<size_t> seg_fix;  // per hops entry: table offset + 1 (0 = none)
-    auto seg_table = [&](int n, int k, int ctas) -> std::pair<size_t, int> {
-      auto f = seg_of.find({n, k});
-      if (f != seg_of.end()) return f->second;
-      const long long tiles = n / step_tile_rows(), nkb = k / 64, total = tiles * nkb;
-      auto start = [&](long long c) { return c * total / ctas; };
-      const size_t off = seg_host.size();
-      int mx = 0;
-      for (long long tt = 0; tt < tiles; ++tt) {
-        int cnt = 0;
-        for (long long c = 0; c < ctas; ++c) {
-          const long long s0 = start(c), s1 = start(c + 1);
-          if (s0 >= s1 || s1 <= tt * nkb || s0 >= (tt + 1) * nkb) continue;
-          if (cnt < 8) seg_host.push_back(static_cast<int>(c * 2 + (tt - s0 / nkb)));
-          ++cnt;
-        }
-        if (cnt > 8) {
-          ok = false;
-          e2 = "step kernel: more than 8 partial slots per tile";
-        }
-        for (int r = cnt; r < 8; ++r) seg_host.push_back(-1);
-        mx = std::max(mx, cnt);
-      }
-      seg_of[{n, k}] = {off, mx};
-      return {off, mx};
-    };
-    int row_target = 0, head_target = 0;  // cumulative join targets within one launch
-    auto step_ops = [&](int s) {
-      const size_t base = hops.size();
-      double bytes = 0.0, flops = 0.0;
-      const int M = b * T;
-      row_target = 0;
-      head_target = 0;
-      int last_nseg = 4;  // partial slots per tile of the last GEMM added
-      size_t last_seg = 0;  // its slot table (offset + 1), given to the next row op
-      // Row ops read the partial-slot table of the GEMM just before them.
-      auto take_seg = [&]() {
-        seg_fix.resize(hops.size() + 1, 0);
-        seg_fix.back() = last_seg;
-        last_seg = 0;
-      };
-      // consumer_ch: 8-wide chunks per thread of the row op reading this GEMM's
-      // partials; its staging holds ch * slots <= 20 records, so the GEMM's CTA
-      // count is capped to keep the slots per tile <= 8 (ch <= 2) or <= 4.
-      auto gop = [&](const std::string& wn, const bf16* a, int n, int k, int consumer_ch) {
-        if (!ok) return;
-        if (!ensure_tiled(wn, n, k, &e2)) {
-          ok = false;
-          return;
-        }
-        StepOp o{};
-        o.kind = STEP_GEMM;
-        o.w = W(wn + ".weight", static_cast<int64_t>(n) * k);
-        o.a = a;
-        o.n = n;
-        o.k = k;
-        o.ctas = std::min(sms_, (consumer_ch <= 2 ? 7 : 3) * (n / step_tile_rows()));
-        const auto tb = seg_table(n, k, o.ctas);
-        last_nseg = tb.second <= 4 ? 4 : 8;
-        last_seg = tb.first + 1;
-        StepGemm sg{};
-        sg.w = o.w;
-        sg.a = a;
-        sg.nk = n | (k << 16);
-        sg.cop = o.ctas | (static_cast<int>(hops.size() - base) << 16);
-        hgemms.push_back(sg);
-        hops.push_back(o);
-        bytes += 2.0 * (double(n) * k + double(M) * k + double(M) * n);
-        flops += 2.0 * M * double(n) * k;
-      };
-      // Row-op split: LN / CQ rows in `nblk` column blocks that join per row
-      // (all units resident: M * nblk <= SMs), one 8-wide chunk per thread
-      // where possible.
-      auto ln_blocks = [&](int width) {
-        for (int c = 8; c >= 2; --c)
-          if (M * c <= sms_ && (width / 8) % c == 0 && width / 8 / c <= 128) return c;
-        return 1;
-      };
-      auto ln_ch = [&](int width) { return (width / 8 / ln_blocks(width) + 127) / 128; };
-      auto plan_join = [&](StepOp& o, int width) {
-        const int nb = ln_blocks(width);
-        o.nblk = nb;
-        o.nseg = last_nseg;
-        o.ch = ln_ch(width);
-        if (nb > 1) {
-          o.sync_base = row_target;
-          row_target += nb;
-        }
-      };
-      // GELU / RES: blocks of ch * 1024 features, the fewest chunks per thread
-      // (compiled variants 1, 3, 5) that keep the units within one wave.
-      auto block_ch = [&](int width) {
-        for (int c : {1, 3, 5})
-          if (M * ((width + c * 1024 - 1) / (c * 1024)) <= sms_) return c;
-        return 1;
-      };
-      auto plan_block = [&](StepOp& o, int width) {
-        int ch = block_ch(width);
-        if (ch > 1 && last_nseg != 4) ch = 1;  // compiled: (1, 4), (1, 8), (3, 4), (5, 4)
-        o.ch = ch;
-        o.nseg = last_nseg;
-        o.nblk = (width + ch * 1024 - 1) / (ch * 1024);
-      };
-      auto need = [&](const void* q, const std::string& what) {
-        if (!q && ok) {
-          ok = false;
-          e2 = "step kernel: missing " + what;
-        }
-      };
-      const float* cprev = nullptr;
-      std::string prev;
-      for (int l = 0; l < L && ok; ++l) {
-        const std::string ap = "gwp.blk." + std::to_string(l) + ".a";
-        const float* c = comb_steps_ + (static_cast<size_t>(s) * L + l) * 6 * E;
-        StepOp ln{};
-        ln.kind = STEP_LN;
-        ln.width = E;
-        ln.resid = ha_;
-        ln.ldr = E;
-        ln.ln = 0;
-        ln.p0 = c + E;
-        ln.p1 = c;
-        ln.eps = eps;
-        ln.out_a = xa_t_;
-        if (l > 0) {
-          ln.epi = EPI_GATED_RES;
-          ln.bias = W(prev + ".ffn.out.bias", E);
-          ln.gate = cprev + 5 * E;
-          need(ln.bias, prev + ".ffn.out.bias");
-        }
-        plan_join(ln, E);
-        take_seg();
-        hops.push_back(ln);
-        gop(ap + ".sa.qkv", xa_t_, 3 * H, E, (H / 8 + 127) / 128);
-        StepOp q{};
-        q.kind = STEP_QKV;
-        q.width = H;
-        q.epi = EPI_BIAS;
-        q.bias = W(ap + ".sa.qkv.bias", 3LL * H);
-        q.eps = eps;
-        q.q_norm = W(ap + ".sa.qn.weight", H);
-        q.k_norm = W(ap + ".sa.kn.weight", H);
-        need(q.bias, ap + ".sa.qkv.bias");
-        need(q.q_norm, ap + ".sa.qn");
-        need(q.k_norm, ap + ".sa.kn");
-        q.q_out = qbuf_;
-        q.q_seq_stride = static_cast<long long>(heads) * T * 128;
-        q.q_head_stride = static_cast<long long>(T) * 128;
-        q.k_out = k_self_ + l * selfL;
-        q.v_out = v_self_ + l * selfL;
-        q.kv_seq_stride = selfB;
-        q.kv_head_stride = static_cast<long long>(P + T) * 128;
-        q.kv_row_offset = P;
-        q.rope = 1;
-        q.pos_base = 1;  // action_positions(tokens, false) = 1..T (semantics.cpp:210-222)
-        q.nblk = 1;  // (row, part) units, no join
-        q.ch = (H / 8 + 127) / 128;
-        q.nseg = last_nseg;
-        take_seg();
-        hops.push_back(q);
-        StepOp at{};
-        at.kind = STEP_ATTN;
-        at.att_q = qbuf_;
-        at.q_seq_stride = q.q_seq_stride;
-        at.q_head_stride = q.q_head_stride;
-        at.att_k = k_self_ + l * selfL;
-        at.att_v = v_self_ + l * selfL;
-        at.kv_seq_stride = selfB;
-        at.kv_head_stride = q.kv_head_stride;
-        at.lq = T;
-        at.lk = P + T;
-        at.heads = heads;
-        at.batch = b;
-        at.splits = attn_splits(P + T);
-        at.static_keys = P;
-        at.scale = 1.0f / std::sqrt(128.0f);
-        at.out_a = at_t_;
-        at.sync_base = head_target;
-        if (at.splits > 1) head_target += at.splits;
-        hops.push_back(at);
-        bytes += 4.0 * b * heads * double(P + T) * 128;
-        flops += 4.0 * b * heads * double(T) * (P + T) * 128;
-        gop(ap + ".sa.o", at_t_, E, H, ln_ch(E));
-        StepOp l2{};
-        l2.kind = STEP_LN;
-        l2.width = E;
-        l2.epi = EPI_GATED_RES;
-        l2.bias = W(ap + ".sa.o.bias", E);
-        l2.gate = c + 2 * E;
-        l2.resid = ha_;
-        l2.ldr = E;
-        l2.ln = 1;
-        l2.p0 = W(ap + ".ca_norm.weight", E);
-        l2.p1 = W(ap + ".ca_norm.bias", E);
-        l2.eps = eps;
-        l2.out_a = xa_t_;
-        need(l2.bias, ap + ".sa.o.bias");
-        need(l2.p0, ap + ".ca_norm.weight");
-        need(l2.p1, ap + ".ca_norm.bias");
-        plan_join(l2, E);
-        take_seg();
-        hops.push_back(l2);
-        gop(ap + ".ca.q", xa_t_, H, E, ln_ch(H));
-        StepOp cq{};
-        cq.kind = STEP_CQ;
-        cq.width = H;
-        cq.epi = EPI_BIAS;
-        cq.bias = W(ap + ".ca.q.bias", H);
-        cq.eps = eps;
-        cq.q_norm = W(ap + ".ca.qn.weight", H);
-        need(cq.bias, ap + ".ca.q.bias");
-        need(cq.q_norm, ap + ".ca.qn");
-        cq.q_out = qc_;
-        cq.q_seq_stride = static_cast<long long>(heads) * T * 128;
-        cq.q_head_stride = static_cast<long long>(T) * 128;
-        plan_join(cq, H);
-        take_seg();
-        hops.push_back(cq);
-        StepOp cx{};
-        cx.kind = STEP_ATTN;
-        cx.att_q = qc_;
-        cx.q_seq_stride = cq.q_seq_stride;
-        cx.q_head_stride = cq.q_head_stride;
-        cx.att_k = k_prompt_ + l * prL;
-        cx.att_v = v_prompt_ + l * prL;
-        cx.kv_seq_stride = prB;
-        cx.kv_head_stride = static_cast<long long>(Nt) * 128;
-        cx.lq = T;
-        cx.lk = Nt;
-        cx.heads = heads;
-        cx.batch = b;
-        cx.splits = attn_splits(Nt);
-        cx.static_keys = Nt;
-        cx.scale = at.scale;
-        cx.out_a = at_t_;
-        cx.sync_base = head_target;
-        if (cx.splits > 1) head_target += cx.splits;
-        hops.push_back(cx);
-        bytes += 4.0 * b * heads * double(Nt) * 128;
-        flops += 4.0 * b * heads * double(T) * Nt * 128;
-        gop(ap + ".ca.o", at_t_, E, H, ln_ch(E));
-        StepOp l3{};
-        l3.kind = STEP_LN;
-        l3.width = E;
-        l3.epi = EPI_RES;
-        l3.bias = W(ap + ".ca.o.bias", E);
-        l3.resid = ha_;
-        l3.ldr = E;
-        l3.ln = 0;
-        l3.p0 = c + 4 * E;
-        l3.p1 = c + 3 * E;
-        l3.eps = eps;
-        l3.out_a = xa_t_;
-        need(l3.bias, ap + ".ca.o.bias");
-        plan_join(l3, E);
-        take_seg();
-        hops.push_back(l3);
-        gop(ap + ".ffn.in", xa_t_, Fa, E, block_ch(Fa));
-        StepOp gl{};
-        gl.kind = STEP_GELU;
-        gl.width = Fa;
-        gl.epi = EPI_BIAS_GELU;
-        gl.bias = W(ap + ".ffn.in.bias", Fa);
-        gl.out_a = ff_t_;
-        need(gl.bias, ap + ".ffn.in.bias");
-        plan_block(gl, Fa);
-        take_seg();
-        hops.push_back(gl);
-        gop(ap + ".ffn.out", ff_t_, E, Fa, l + 1 < L ? ln_ch(E) : block_ch(E));
-        prev = ap;
-        cprev = c;
-      }
-      StepOp rs{};
-      rs.kind = STEP_RES;
-      rs.width = E;
-      rs.epi = EPI_GATED_RES;
-      rs.bias = W(prev + ".ffn.out.bias", E);
-      rs.gate = cprev + 5 * E;
-      rs.resid = ha_;
-      rs.ldr = E;
-      need(rs.bias, prev + ".ffn.out.bias");
-      plan_block(rs, E);
-      take_seg();
-      hops.push_back(rs);
-      if (!ok) return;
-      if (hops.size() - base != static_cast<size_t>(step_nops) ||
-          hgemms.size() != static_cast<size_t>(s + 1) * step_ngemm) {
-        ok = false;
-        e2 = "step kernel: op count mismatch";
-        return;
-      }
-      StepArgs sa{};
-      sa.ops = d_ops + static_cast<size_t>(s) * step_nops;
-      sa.num_ops = step_nops;
-      sa.gemms = d_gemms + static_cast<size_t>(s) * step_ngemm;
-      sa.num_gemms = step_ngemm;
-      sa.attn_counters = b * heads;
-      sa.m = M;
-      sa.mr = step_mr;
-      sa.rows_per_seq = T;
-      sa.stages = step_stages(step_mr, step_ngemm);
-      sa.inv_freq = inv_freq1_;
-      sa.ws = step_ws_;
-      sa.attn_ws = step_attn_ws_;
-      sa.stats = step_attn_ws_ + static_cast<size_t>(step_batch_) * heads * 8 * 64 * 132;
-      sa.counters = step_ctr_;
-      sa.error = err_word_;
-      const int grid = sms_;
-      dp.add([sa, grid](cudaStream_t st) { return step_launch(sa, grid, st); }, OP_STEP, 1, bytes,
-             flops);
-    };
     for (int s = 0; s < S && ok; ++s) {
       const int M = b * T;
       small(dp, action_bf_, M, A, ain_w ? ain_w + static_cast<size_t>(emb) * A * 128 : nullptr, 1, 128,
@@ -1548,17 +1110,11 @@ bool MotEngine::build(int b, std::string* err) {
       small(dp, e1_, M, 128, W("gwp.action.mid.weight", 128 * 128), 128, 1,
             W("gwp.action.mid.bias", 128), 128, ACT_GELU_ERF, e2_);
       G(dp, e2_, 128, M, "gwp.action.out", E, 128, EPI_BIAS, true, nullptr, nullptr, 0, ha_, E);
-      if (use_step) step_ops(s);
-      if (!use_step) side_prefetch(dp, wrange("gwp.blk.0.a.sa.qkv", 3LL * H, E));
-      for (int l = 0; l < L && ok && !use_step; ++l) {
+      for (int l = 0; l < L && ok; ++l) {
         const std::string ap = "gwp.blk." + std::to_string(l) + ".a";
         const float* c = comb_steps_ + (static_cast<size_t>(s) * L + l) * 6 * E;
-        // L2 prefetch schedule: each non-GEMM op pulls in the weights of the
-        // next GEMM(s) while it runs (HBM is otherwise idle during it).
-        const long long l2cap = 64ll << 20;
-        ln_mod(dp, ha_, M, E, c + E, c, nrm_, mkpf(wrange(ap + ".sa.qkv", 3LL * H, E, 0, l2cap)));
+        ln_mod(dp, ha_, M, E, c + E, c, nrm_);
         G(dp, nrm_, E, M, ap + ".sa.qkv", 3 * H, E, EPI_BIAS, true, nullptr, nullptr, 0, qkv_, 3 * H);
-        side_prefetch(dp, wrange(ap + ".sa.o", E, H), wrange(ap + ".ca.q", H, E));
         QkvScatter q{};
         q.src = qkv_;
         q.ld_src = 3 * H;
@@ -1600,13 +1156,11 @@ bool MotEngine::build(int b, std::string* err) {
         at.scale = 1.0f / std::sqrt(128.0f);
         at.out = att_;
         at.ldo = H;
-        at.pf = mkpf(wrange(ap + ".sa.o", E, H), wrange(ap + ".ca.q", H, E));
         attend(dp, at);
         G(dp, att_, H, M, ap + ".sa.o", E, H, EPI_GATED_RES, true, c + 2 * E, ha_, E, ha_, E);
         ln_aff(dp, ha_, M, E, ap + ".ca_norm", nrm_);
         G(dp, nrm_, E, M, ap + ".ca.q", H, E, EPI_BIAS, true, nullptr, nullptr, 0, cq_, H);
-        side_prefetch(dp, wrange(ap + ".ca.o", E, H));
-        cross_q(dp, cq_, M, T, ap, qc_, mkpf(wrange(ap + ".ca.o", E, H)));
+        cross_q(dp, cq_, M, T, ap, qc_);
         AttnArgs cx{};
         cx.q = qc_;
         cx.q_seq_stride = static_cast<long long>(heads) * T * 128;
@@ -1623,16 +1177,11 @@ bool MotEngine::build(int b, std::string* err) {
         cx.scale = at.scale;
         cx.out = catt_;
         cx.ldo = H;
-        cx.pf = mkpf(wrange(ap + ".ffn.in", Fa, E, 0, l2cap));
         attend(dp, cx);
         G(dp, catt_, H, M, ap + ".ca.o", E, H, EPI_RES, true, nullptr, ha_, E, ha_, E);
-        side_prefetch(dp, wrange(ap + ".ffn.in", Fa, E));
-        ln_mod(dp, ha_, M, E, c + 4 * E, c + 3 * E, nrm_,
-               mkpf(wrange(ap + ".ffn.in", Fa, E, l2cap)));
+        ln_mod(dp, ha_, M, E, c + 4 * E, c + 3 * E, nrm_);
         G(dp, nrm_, E, M, ap + ".ffn.in", Fa, E, EPI_BIAS_GELU, true, nullptr, nullptr, 0, ffn_, Fa);
         G(dp, ffn_, Fa, M, ap + ".ffn.out", E, Fa, EPI_GATED_RES, true, c + 5 * E, ha_, E, ha_, E);
-        if (l + 1 < L)
-          side_prefetch(dp, wrange("gwp.blk." + std::to_string(l + 1) + ".a.sa.qkv", 3LL * H, E));
       }
       const float* cf = comb_final_ + static_cast<size_t>(s) * 2 * E;
       ln_mod(dp, ha_, M, E, cf + E, cf, nrm_);
@@ -1652,21 +1201,6 @@ bool MotEngine::build(int b, std::string* err) {
       launch_bf16_to_f32(action_bf_, d_out_, static_cast<long long>(b) * T * A, s);
       return cudaGetLastError();
     });
-    if (use_step && ok) {
-      int* d_segs = dalloc<int>(seg_host.size(), err);
-      if (!d_segs) return false;
-      seg_fix.resize(hops.size(), 0);
-      for (size_t i = 0; i < hops.size(); ++i)
-        if (seg_fix[i]) hops[i].segs = d_segs + (seg_fix[i] - 1);
-      CK(cudaMemcpyAsync(d_segs, seg_host.data(), seg_host.size() * sizeof(int), cudaMemcpyHostToDevice,
-                         stream_));
-      CK(cudaMemcpyAsync(d_ops, hops.data(), hops.size() * sizeof(StepOp), cudaMemcpyHostToDevice,
-                         stream_));
-      CK(cudaMemcpyAsync(d_gemms, hgemms.data(), hgemms.size() * sizeof(StepGemm),
-                         cudaMemcpyHostToDevice, stream_));
-      CK(cudaStreamSynchronize(stream_));
-    }
-    if (prefetch_mode_ == 2) join_side(dp);
     if (!ok) {
       if (e2 == "__rebuild__") continue;  // scratch grew: rebuild with the new pointers
       *err = e2;
@@ -1975,7 +1509,6 @@ bool MotEngine::fetch(const RequestView* reqs, int batch, float* out, std::strin
   CK(cudaStreamSynchronize(stream_));
   if (code != 0) {
     cudaMemsetAsync(err_word_, 0, 4, stream_);
-    if (step_ctr_) cudaMemsetAsync(step_ctr_, 0, step_ctr_n_ * sizeof(unsigned), stream_);
     cudaStreamSynchronize(stream_);
     *err = "device pipeline wait timed out (code " + std::to_string(code) + ")";
     return false;

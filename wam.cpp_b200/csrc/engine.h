@@ -61,9 +61,7 @@ using Launch = std::function<cudaError_t(cudaStream_t)>;
 
 // Kernel families, for the per-kernel profile (wam_b200_profile).
 enum OpKind : int { OP_GEMM = 0, OP_ATTENTION = 1, OP_LAYERNORM = 2, OP_QKV = 3, OP_SMALL = 4,
-                    OP_ELEMENTWISE = 5, OP_SYNC = 6 /* lane hand-off, no kernel */,
-                    OP_PREFETCH = 7 /* L2 prefetch beside the main stream */,
-                    OP_STEP = 8 /* persistent denoise-step kernel (all layers of a step) */ };
+                    OP_ELEMENTWISE = 5, OP_SYNC = 6 /* lane hand-off, no kernel */ };
 
 struct Op {
   Launch fn;
@@ -162,7 +160,6 @@ class MotEngine {
   // Whether the denoise step of `batch` requests runs as the persistent step
   // kernel (step.cu): <= 128 tokens, BF16 re-tiled weights, widths that are
   // multiples of 256 (<= 4096) and no GEMM with more 128-row tiles than SMs.
-  bool step_usable(int batch) const;
 
   struct Plan {
     Program prog[3];                      // prompt projection, prefix, denoise
@@ -197,8 +194,6 @@ class MotEngine {
   bf16* retile_tmp_ = nullptr;  // staging copy for in-place re-tiling (build only)
   size_t retile_tmp_elems_ = 0;
   bool rowmajor_weights_ = false;
-  int prefetch_mode_ = 0;  // 0 off, 1 by the non-GEMM kernels, 2 side-stream grid
-  bool step_kernel_ = false;  // WAM_B200_STEP_KERNEL=1 selects the persistent step kernel
   std::vector<float> sq01_, sq99_, aq01_, aq99_;
   uint64_t resident_bytes_ = 0;
 
@@ -237,14 +232,6 @@ class MotEngine {
   float* gemm_ws_[2] = {nullptr, nullptr};
   size_t gemm_ws_floats_ = 0;
   unsigned* err_word_ = nullptr;
-  // Persistent denoise step: token-tile activations ([K/64][mr][64], swizzled)
-  // of the self/cross/FFN GEMM inputs, stream-K partials, attention split rows,
-  // phase counters (zero at rest), and the op lists of the plans.
-  bf16 *xa_t_ = nullptr, *at_t_ = nullptr, *ff_t_ = nullptr;
-  float *step_ws_ = nullptr, *step_attn_ws_ = nullptr;
-  unsigned* step_ctr_ = nullptr;
-  size_t step_ctr_n_ = 0;
-  int step_batch_ = 0;  // largest batch the step buffers hold
 
   std::vector<float> timesteps_, sigmas_;
   std::map<int, std::unique_ptr<Plan>> plans_;

@@ -12,14 +12,6 @@ namespace wamb {
 
 using bf16 = __nv_bfloat16;
 
-// Weight ranges the next kernels will stream. A non-GEMM kernel that runs just
-// before them spreads their L2 prefetch over its CTAs, while HBM is otherwise
-// idle; null pointers / zero sizes disable it.
-struct L2Prefetch {
-  const void* ptr[2] = {nullptr, nullptr};
-  long long bytes[2] = {0, 0};
-};
-
 // ------------------------------------------------------------------ GEMM
 // y[m, n] = epilogue( sum_k x[m, k] * w[n, k] ), x: [M, K] (row stride ldx),
 // w: [N, K] row-major (GGUF ne = {K, N}). The epilogues restate the rounding
@@ -125,12 +117,10 @@ size_t gemm_scratch_floats(int m, int n, int k, int num_sms, int force_splits, i
 // modulation: y = bf16(n * (1 + scale[c]) + shift[c]); scale/shift F32 [cols]
 // shared by all rows (norm_bf16_fused<affine=false>, native-bf16.patch:368-409).
 void launch_ln_modulate(const bf16* x, int ldx, int rows, int cols, const float* scale,
-                        const float* shift, float eps, bf16* y, int ldy, cudaStream_t s,
-                        const L2Prefetch& pf = L2Prefetch());
+                        const float* shift, float eps, bf16* y, int ldy, cudaStream_t s);
 // Affine LayerNorm: y = bf16(n * w[c] + b[c]), w/b BF16 (norm_bf16_fused<affine=true>).
 void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w, const bf16* b,
-                      float eps, bf16* y, int ldy, cudaStream_t s,
-                      const L2Prefetch& pf = L2Prefetch());
+                      float eps, bf16* y, int ldy, cudaStream_t s);
 
 // Per-token RMSNorm of q and k over the full attention width, RoPE, BF16 cast
 // and scatter into head-major attention buffers (expert_qkv, mot.cpp:210-267;
@@ -162,7 +152,6 @@ struct QkvScatter {
   bf16* v_out;
   long long kv_seq_stride, kv_head_stride;
   int kv_row_offset;
-  L2Prefetch pf;
 };
 void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s);
 
@@ -184,7 +173,6 @@ struct AttnArgs {
   bf16* out_first;
   int ldo_first;
   int split_first;
-  L2Prefetch pf;
   // Keys [0, static_keys) are not written by the preceding kernel: a CTA whose
   // whole key range lies there loads its K/V before waiting for it.
   int static_keys = 0;
@@ -201,101 +189,7 @@ void launch_attention(const AttnArgs& a, cudaStream_t s);
 cudaError_t attention_tc_init();
 bool attention_tc_eligible(const AttnArgs& a);
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s);
-// ------------------------------------------------ persistent denoise step
-// One grid runs every action-expert layer of one flow-matching step for up to
-// 128 tokens (step.cu). The step is a list of ops; each op waits for the one
-// before it on all CTAs (grid phase counters), except GEMM ops, whose weight
-// copies run ahead and whose token copies wait for the op that wrote them.
-enum StepOpKind : int {
-  STEP_GEMM = 0,  // stream-K partials of a[m, k] * w[n, k]^T (w re-tiled, n % 256 == 0)
-  STEP_LN = 1,    // epilogue of the GEMM before (if any) into resid, LayerNorm -> out_a
-  STEP_QKV = 2,   // q/k/v: epilogue, q/k RMSNorm, RoPE, head-major scatter
-  STEP_CQ = 3,    // cross-attention q: epilogue, RMSNorm, head-major scatter
-  STEP_GELU = 4,  // FFN up: bias + GELU(tanh) -> out_a
-  STEP_RES = 5,   // last gated residual of the step -> resid
-  STEP_ATTN = 6,  // softmax(scale QK^T)V, key splits merged by the last split -> out_a
-};
 
-struct alignas(16) StepOp {
-  int kind;
-  // GEMM: w re-tiled ([n/256][k/64][256][64], swizzled); a in the token-tile
-  // layout [k/64][mr][64] (128-byte swizzle) written by the op before.
-  const bf16* w;
-  const bf16* a;
-  int n, k;
-  int ctas;         // CTAs 0..ctas-1 split the GEMM's tiles x k-blocks stream-K
-  // Row ops: the partial-slot table of the GEMM before them, [n/128][8]
-  // entries cta * 2 + slot holding each tile in CTA order, -1 = none.
-  const int* segs;
-  // Row ops: width of the row part they produce, the epilogue of the GEMM
-  // before them (EPI_BIAS, EPI_BIAS_GELU, EPI_GATED_RES, EPI_RES) and its
-  // operands; resid [m][ldr] is read and (LN / RES) rewritten in place.
-  int width;
-  int epi;
-  const bf16* bias;
-  const float* gate;
-  bf16* resid;
-  int ldr;
-  int nblk;       // column blocks of a row op (> 1: the blocks of a row join per row)
-  int ch, nseg;   // row-op variant: 8-wide chunks per thread, partial slots per tile (4 / 8)
-  int sync_base;  // row ops with nblk > 1 and ATTN: join-counter target before this op
-  int ln;  // -1 none, 0 AdaLN (p0 = scale, p1 = shift, F32), 1 affine (p0 = w, p1 = b, BF16)
-  const void* p0;
-  const void* p1;
-  float eps;
-  bf16* out_a;  // token-tile layout destination (LN, GELU, ATTN)
-  // QKV / CQ destinations (as QkvScatter) and attention sources.
-  const bf16* q_norm;
-  const bf16* k_norm;
-  bf16* q_out;
-  long long q_seq_stride, q_head_stride;
-  bf16* k_out;
-  bf16* v_out;
-  long long kv_seq_stride, kv_head_stride;
-  int kv_row_offset;
-  int rope, pos_base;  // rope 1: 1-D at pos_base + row_in_seq
-  const bf16* att_q;  // ATTN: head-major Q / K / V ([seq][head][row][128] with the strides above)
-  const bf16* att_k;
-  const bf16* att_v;
-  int lq, lk, heads, batch, splits, static_keys;
-  float scale;
-};
-
-// A GEMM op as the copy, MMA and poller roles need it (kept in shared memory).
-struct StepGemm {
-  const bf16* w;
-  const bf16* a;
-  int nk;   // n | k << 16
-  int cop;  // ctas | op index << 16
-};
-
-struct StepArgs {
-  const StepOp* ops;  // device array (16-byte aligned)
-  int num_ops;
-  const StepGemm* gemms;  // the GEMM ops of `ops`, in order
-  int num_gemms;
-  int attn_counters;  // batch * heads merge counters after the phase counters
-  int m;              // token rows (batch * rows_per_seq), <= 128
-  int mr;             // rows of the token-tile layout (m rounded up to 16)
-  int rows_per_seq;
-  int stages;         // step_stages(mr)
-  const float* inv_freq;  // 1-D RoPE inverse frequencies [64]
-  float* ws;          // stream-K partials, step_ws_floats(grid, mr)
-  float* attn_ws;     // attention key-split rows, batch * heads * splits * 64 * 132
-  float* stats;       // row-join statistics [128 rows][8 blocks][2]
-  unsigned* counters; // num_ops + attn_counters + 128 (rows) + 2 (exit, abort), zero at rest
-  unsigned* error;    // device error word
-};
-int step_stages(int mr, int num_gemms);
-size_t step_smem_bytes(int mr, int num_gemms);
-size_t step_ws_floats(int grid, int mr);
-int step_tile_rows();  // weight rows per stream-K tile
-cudaError_t step_init();
-// grid = the SM count (one CTA per SM; every CTA must be resident at once).
-cudaError_t step_launch(const StepArgs& a, int grid, cudaStream_t s);
-
-// Prefetches the ranges into L2 (a small grid meant to run beside other work).
-void launch_l2_prefetch(const L2Prefetch& pf, cudaStream_t s);
 // Workspace the split-KV merge of `a` needs (0 when it does not split).
 size_t attention_ws_floats(const AttnArgs& a);
 cudaError_t attention_init();

@@ -18,8 +18,7 @@ from ._lib import load
 from ._lib_engine import (GEOM_FIELDS, Geometry, GraphProfile, OpProfile, Options, Request, Stats,
                           Status)
 
-KINDS = ("gemm", "attention", "layernorm", "qkv_scatter", "small_linear", "elementwise", "sync",
-         "l2_prefetch", "denoise_step")
+KINDS = ("gemm", "attention", "layernorm", "qkv_scatter", "small_linear", "elementwise", "sync")
 PHASES = ("prompt", "prefix", "denoise")
 
 

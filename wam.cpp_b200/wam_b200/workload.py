@@ -62,11 +62,6 @@ SMALL = Geometry(hidden=512, layers=3, heads=4, ffn=1024, action_hidden=384, act
 # plans, persistent GEMMs and attention splits as the full model).
 CONFIG2_L2 = Geometry(layers=2, steps=2)
 CONFIG2_L1 = Geometry(layers=1, steps=2)
-# Action-expert widths that are multiples of 256 with the config-2 chunk of 48
-# tokens: the engine runs these denoise steps as its persistent step kernel.
-STEPK = Geometry(hidden=512, layers=3, heads=4, ffn=1024, action_hidden=512, action_ffn=1024,
-                 grid_h=4, grid_w=6, vae_z=16, action_chunk=48, steps=3, prompt_tokens=32,
-                 text_dim=256)
 # 144 visual tokens: the prefix attention (145 / 144 queries) runs as 128-query
 # tensor-core tiles.
 TALL = Geometry(hidden=256, layers=2, heads=2, ffn=512, action_hidden=256, action_ffn=384,
