@@ -81,6 +81,11 @@ def lib():
         l.oracle_quantize_q8.argtypes = [C.c_void_p]
         l.oracle_q8_roundtrip.argtypes = [C.c_void_p, C.c_int64, f32p]
         l.oracle_set_uncached.argtypes = [C.c_void_p, C.c_int]
+        l.oracle_create_synthetic_ex.restype = C.c_void_p
+        l.oracle_create_synthetic_ex.argtypes = [C.POINTER(_Geom), C.c_uint64, C.c_double, C.c_int,
+                                                 C.c_char_p, C.c_int]
+        l.oracle_block.restype = C.c_int
+        l.oracle_block.argtypes = [C.c_void_p, C.c_int, C.c_float] + [f32p] * 6
         _lib = l
     return _lib
 
@@ -129,13 +134,15 @@ class OracleModel:
     """A CPU model over BF16 weights given as {compact name: uint16 array}."""
 
     def __init__(self, g: Geometry, weights: dict | None, stats: dict | None = None,
-                 seed: int = 0, bias_scale: float = 0.0):
-        """weights None: the synthetic weights of (seed, bias_scale), built in C++."""
+                 seed: int = 0, bias_scale: float = 0.0, ffn_kind: int = 0):
+        """weights None: the synthetic weights of (seed, bias_scale), built in C++
+        (ffn_kind 1: SiLU-gated FFN weights, the config-1 variant)."""
         self.g = g
         if weights is None:
             err = C.create_string_buffer(512)
             gs = geom_struct(g)
-            self.h = lib().oracle_create_synthetic(C.byref(gs), seed, bias_scale, err, 512)
+            self.h = lib().oracle_create_synthetic_ex(C.byref(gs), seed, bias_scale, ffn_kind, err,
+                                                      512)
             if not self.h:
                 raise RuntimeError("oracle_create_synthetic: " + err.value.decode())
             return
@@ -164,6 +171,19 @@ class OracleModel:
         """Recompute the prefix every step (the reference's CPU mode)."""
         lib().oracle_set_uncached(self.h, 1 if uncached else 0)
         return self
+
+    def block(self, t: float, xv, xa, tv, ta, norm_kind: int = 0):
+        """Config 1: one MoT layer over given hidden states (oracle_block).
+        xv [V, H], xa [1 + T, E] (state row first), tv [Nt, H], ta [Nt, E].
+        Returns (visual out [V, H], action stream out [1 + T, E])."""
+        g = self.g
+        args = [np.ascontiguousarray(a, np.float32) for a in (xv, xa, tv, ta)]
+        ov = np.zeros((g.visual_tokens, g.hidden), np.float32)
+        oa = np.zeros((1 + g.action_chunk, g.action_hidden), np.float32)
+        rc = lib().oracle_block(self.h, norm_kind, t, *[_fp(a) for a in args], _fp(ov), _fp(oa))
+        if rc != 0:
+            raise RuntimeError("oracle_block failed")
+        return ov, oa
 
     def __del__(self):
         h = getattr(self, "h", None)

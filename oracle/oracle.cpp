@@ -108,6 +108,10 @@ struct Model {
   std::unordered_map<std::string, Tensor> t;
   Vec sq01, sq99, aq01, aq99;
   bool uncached = false;  // recompute the prefix every step (the reference's CPU mode)
+  // Block variants (config 1 as BASELINE states it): ffn_kind 0 = GELU(tanh)
+  // FFN (the reference), 1 = SiLU-gated FFN with ffn.in = [gate rows | up rows];
+  // norm_kind 0 = LayerNorm inside AdaLN (the reference), 1 = RMSNorm.
+  int ffn_kind = 0, norm_kind = 0;
 
   // F32 weights of a tensor the Q8_0 policy quantised (nullptr otherwise).
   const float* wf(const std::string& name) const {
@@ -203,21 +207,33 @@ void gemm_acc(const float* x, int M, int K, const uint16_t* W, int N, float* acc
 // y = bf16(bf16(x·W) + b); the input is cast to BF16 first. With gelu set, the
 // linear_gelu_with_activation form (weights.cpp:833-849, bias_gelu_bf16_kernel):
 // y = bf16(gelu_tanh(bf16(x·W) + b)).
-Vec linear(const Model& md, const Vec& x, int M, int K, const std::string& name, int N,
-           bool gelu = false) {
+// Rows [row0, row0 + N) of a weight with `total` rows (total = N: the whole
+// weight). act 1: GELU(tanh) as above; act 2: SiLU of the BF16 linear output
+// (ggml_silu on a BF16 tensor): y = bf16(silu(bf16(bf16(x·W) + b))).
+Vec linear_rows(const Model& md, const Vec& x, int M, int K, const std::string& name, int row0,
+                int N, int total, int act) {
   Vec xb(x);
   bfr_inplace(xb);
-  const uint16_t* W = md.w(name + ".weight", static_cast<int64_t>(N) * K);
-  const uint16_t* b = md.w(name + ".bias", N);
+  const uint16_t* W = md.w(name + ".weight", static_cast<int64_t>(total) * K);
+  const uint16_t* b = md.w(name + ".bias", total);
   Vec y(static_cast<size_t>(M) * N);
   if (!W || !b) return Vec();
-  gemm_acc(xb.data(), M, K, W, N, y.data(), md.wf(name + ".weight"));
+  const float* Wf = md.wf(name + ".weight");
+  gemm_acc(xb.data(), M, K, W + static_cast<size_t>(row0) * K, N, y.data(),
+           Wf ? Wf + static_cast<size_t>(row0) * K : nullptr);
   for (int m = 0; m < M; ++m)
     for (int n = 0; n < N; ++n) {
       float& v = y[static_cast<size_t>(m) * N + n];
-      v = gelu ? bfr(gelu_tanh(bfr(v) + bf2f(b[n]))) : bfr(bfr(v) + bf2f(b[n]));
+      const float bb = bf2f(b[row0 + n]);
+      v = act == 1 ? bfr(gelu_tanh(bfr(v) + bb)) : act == 2 ? bfr(silu(bfr(bfr(v) + bb)))
+                                                            : bfr(bfr(v) + bb);
     }
   return y;
+}
+
+Vec linear(const Model& md, const Vec& x, int M, int K, const std::string& name, int N,
+           bool gelu = false) {
+  return linear_rows(md, x, M, K, name, 0, N, N, gelu ? 1 : 0);
 }
 
 // Embodiment-sliced projection (mot.cpp:1-14): torch weight [emb][in][out],
@@ -278,12 +294,22 @@ void ln_stats(const float* x, int n, float eps, float* mean, float* inv_std) {
 }
 
 // modulated_norm (mot.cpp:147-159): bf16(LN(x) * (1 + scale) + shift).
-Vec modulated_norm(const Vec& x, int M, int n, const float* scale, const float* shift, float eps) {
+// rms: the config-1 RMSNorm variant, n = x * rsqrt(mean(x^2) + eps) (no mean
+// subtraction), then the same AdaLN modulation.
+Vec modulated_norm(const Vec& x, int M, int n, const float* scale, const float* shift, float eps,
+                   bool rms = false) {
   Vec y(x.size());
   for (int m = 0; m < M; ++m) {
     const float* r = x.data() + static_cast<size_t>(m) * n;
     float mu, is;
-    ln_stats(r, n, eps, &mu, &is);
+    if (rms) {
+      float ss = 0.0f;
+      for (int i = 0; i < n; ++i) ss += r[i] * r[i];
+      mu = 0.0f;
+      is = 1.0f / std::sqrt(ss / n + eps);
+    } else {
+      ln_stats(r, n, eps, &mu, &is);
+    }
     for (int i = 0; i < n; ++i)
       y[static_cast<size_t>(m) * n + i] = bfr(std::fma((r[i] - mu) * is, 1.0f + scale[i], shift[i]));
   }
@@ -439,7 +465,7 @@ ExpertQkv expert_qkv(const Model& md, const std::string& pfx, const Vec& hidden,
                      const int32_t* pt, const int32_t* ph, const int32_t* pw) {
   const oracle_geometry& g = md.g;
   const int H = g.hidden;
-  Vec n = modulated_norm(hidden, rows, W, scale, shift, g.norm_eps);
+  Vec n = modulated_norm(hidden, rows, W, scale, shift, g.norm_eps, md.norm_kind == 1);
   Vec qkv = linear(md, n, rows, W, pfx + ".sa.qkv", 3 * H);
   rms_norm_rows(qkv, rows, 3 * H, 0, H, md.w(pfx + ".sa.qn.weight", H), g.norm_eps);
   rms_norm_rows(qkv, rows, 3 * H, H, H, md.w(pfx + ".sa.kn.weight", H), g.norm_eps);
@@ -497,8 +523,16 @@ Vec cross_ffn(const Model& md, const std::string& pfx, const Vec& hidden, int ro
   Vec o = linear(md, att, rows, H, pfx + ".ca.o", W);
   Vec h(hidden.size());
   for (size_t i = 0; i < h.size(); ++i) h[i] = bfr(hidden[i] + o[i]);  // ggml_add, :338
-  Vec m = modulated_norm(h, rows, W, cscale, cshift, g.norm_eps);
-  Vec f = linear(md, m, rows, W, pfx + ".ffn.in", F, true);
+  Vec m = modulated_norm(h, rows, W, cscale, cshift, g.norm_eps, md.norm_kind == 1);
+  Vec f;
+  if (md.ffn_kind == 1) {
+    // SiLU-gated FFN: silu(gate) * up, each a BF16 linear output, product in BF16
+    f = linear_rows(md, m, rows, W, pfx + ".ffn.in", 0, F, 2 * F, 2);
+    Vec u = linear_rows(md, m, rows, W, pfx + ".ffn.in", F, F, 2 * F, 0);
+    for (size_t i = 0; i < f.size(); ++i) f[i] = bfr(f[i] * u[i]);
+  } else {
+    f = linear(md, m, rows, W, pfx + ".ffn.in", F, true);
+  }
   Vec d = linear(md, f, rows, F, pfx + ".ffn.out", W);
   for (size_t i = 0; i < h.size(); ++i)  // gated_residual (mot.cpp:161-173)
     h[i] = bfr(std::fma(d[i], cgate[i % W], h[i]));
@@ -642,6 +676,63 @@ Vec action_step(const Model& md, const PrefixOut& pre, const Vec& action, float 
   return action_decoder(md, n, T);
 }
 
+// One MoT layer (layer 0) of the reference's un-cached forward (run_mot_step,
+// src/models/gwp05/engine/mot.cpp:870-1100, layer body :1008-1067): the action
+// stream [state; actions] through the action expert with the state row at
+// timestep 0 and the action rows at t (action_timesteps with the clean state,
+// semantics.cpp:224-233), the visual tokens through the visual expert at
+// t = 0, one joint self-attention in which state and visual queries see only
+// state and visual keys and action queries see every key (the mask built at
+// mot.cpp:1147-1158), then each expert's cross attention over its text hidden
+// states (projected by the layer: build_attention, text_encoder.cpp:26-73, F32
+// q/k) and its FFN. xv [V][H], xa [1 + T][E], tv [Nt][H], ta [Nt][E] (F32,
+// rounded to BF16 as the hidden stream is); outputs likewise.
+void block_forward(const Model& md, float t, const float* xv, const float* xa, const float* tv,
+                   const float* ta, float* ov, float* oa) {
+  const oracle_geometry& g = md.g;
+  const int H = g.hidden, E = g.action_hidden, T = g.action_chunk, V = g.grid_h * g.grid_w;
+  const int P = 1 + V, J = P + T, Nt = g.prompt_tokens;
+  const std::string ap = "gwp.blk.0.a", vp = "gwp.blk.0.v";
+  Vec hv(xv, xv + static_cast<size_t>(V) * H), hs(xa, xa + E);
+  Vec ha(xa + E, xa + static_cast<size_t>(1 + T) * E);
+  Vec text_v(tv, tv + static_cast<size_t>(Nt) * H), text_a(ta, ta + static_cast<size_t>(Nt) * E);
+  for (Vec* v : {&hv, &hs, &ha, &text_v, &text_a}) bfr_inplace(*v);
+  Condition c0a = condition(md, "acond", 0.0f, E);
+  Condition cta = condition(md, "acond", t, E);
+  Condition c0v = condition(md, "cond", 0.0f, H);
+  Vec am0 = combined_mod(md, c0a.mod, ap + ".mod", E);
+  Vec amt = combined_mod(md, cta.mod, ap + ".mod", E);
+  Vec vm = combined_mod(md, c0v.mod, vp + ".mod", H);
+  std::vector<int32_t> pt(V), ph(V), pw(V);
+  oracle_visual_positions(g.grid_h, g.grid_w, pt.data(), ph.data(), pw.data());
+  ExpertQkv s = expert_qkv(md, ap, hs, 1, E, &am0[0], &am0[E], false, 0, nullptr, nullptr, nullptr);
+  ExpertQkv a = expert_qkv(md, ap, ha, T, E, &amt[0], &amt[E], false, 1, nullptr, nullptr, nullptr);
+  ExpertQkv v = expert_qkv(md, vp, hv, V, H, &vm[0], &vm[H], true, 0, pt.data(), ph.data(), pw.data());
+  auto cat = [&](std::initializer_list<const Vec*> parts, size_t rows) {
+    Vec out;
+    out.reserve(rows * H);
+    for (const Vec* p : parts) out.insert(out.end(), p->begin(), p->end());
+    return out;
+  };
+  Vec qp = cat({&s.q, &v.q}, P), kp = cat({&s.k, &v.k}, P), vv = cat({&s.v, &v.v}, P);
+  Vec kj = cat({&s.k, &a.k, &v.k}, J), vj = cat({&s.v, &a.v, &v.v}, J);
+  Vec att_p = attention(qp, P, kp, vv, P, g.heads);
+  Vec att_a = attention(a.q, T, kj, vj, J, g.heads);
+  Vec att_s(att_p.begin(), att_p.begin() + H), att_v(att_p.begin() + H, att_p.end());
+  gated_add(hs, linear(md, att_s, 1, H, ap + ".sa.o", E), &am0[2 * E], E);
+  gated_add(ha, linear(md, att_a, T, H, ap + ".sa.o", E), &amt[2 * E], E);
+  gated_add(hv, linear(md, att_v, V, H, vp + ".sa.o", H), &vm[2 * H], H);
+  hs = cross_ffn(md, ap, hs, 1, E, g.action_ffn, nullptr, nullptr, &text_a, E, &am0[3 * E],
+                 &am0[4 * E], &am0[5 * E]);
+  ha = cross_ffn(md, ap, ha, T, E, g.action_ffn, nullptr, nullptr, &text_a, E, &amt[3 * E],
+                 &amt[4 * E], &amt[5 * E]);
+  hv = cross_ffn(md, vp, hv, V, H, g.ffn, nullptr, nullptr, &text_v, H, &vm[3 * H], &vm[4 * H],
+                 &vm[5 * H]);
+  std::memcpy(ov, hv.data(), sizeof(float) * hv.size());
+  std::memcpy(oa, hs.data(), sizeof(float) * E);
+  std::memcpy(oa + E, ha.data(), sizeof(float) * ha.size());
+}
+
 }  // namespace
 
 extern "C" {
@@ -695,6 +786,11 @@ void* oracle_create(const oracle_geometry* g, int n, const char** names, const u
 // materialise weights in Python): same names, shapes and bits.
 void* oracle_create_synthetic(const oracle_geometry* g, uint64_t seed, double bias_scale,
                               char* err, int errlen) {
+  return oracle_create_synthetic_ex(g, seed, bias_scale, 0, err, errlen);
+}
+
+void* oracle_create_synthetic_ex(const oracle_geometry* g, uint64_t seed, double bias_scale,
+                                 int ffn_kind, char* err, int errlen) {
   auto fail = [&](const std::string& m) -> void* {
     if (err && errlen > 0) std::snprintf(err, errlen, "%s", m.c_str());
     return nullptr;
@@ -702,6 +798,8 @@ void* oracle_create_synthetic(const oracle_geometry* g, uint64_t seed, double bi
   if (!g || g->heads * 128 != g->hidden) return fail("hidden must equal heads * 128");
   Model* md = new Model();
   md->g = *g;
+  md->ffn_kind = ffn_kind;
+  const int64_t fin = ffn_kind == 1 ? 2 : 1;  // SiLU-gated: ffn.in holds gate and up rows
   const int64_t E = g->action_hidden, H = g->hidden, A = g->action_dim, D = g->text_dim;
   const int64_t emb = g->num_embodiments;
   std::vector<std::pair<std::string, int64_t>> s;
@@ -744,7 +842,7 @@ void* oracle_create_synthetic(const oracle_geometry* g, uint64_t seed, double bi
                {".ca.k.bias", H}, {".ca.vproj.weight", H * W}, {".ca.vproj.bias", H},
                {".ca.o.weight", W * H}, {".ca.o.bias", W}, {".ca.qn.weight", H},
                {".ca.kn.weight", H}, {".ca_norm.weight", W}, {".ca_norm.bias", W},
-               {".ffn.in.weight", F * W}, {".ffn.in.bias", F}, {".ffn.out.weight", W * F},
+               {".ffn.in.weight", fin * F * W}, {".ffn.in.bias", fin * F}, {".ffn.out.weight", W * F},
                {".ffn.out.bias", W}, {".mod", 6 * W}})
         s.push_back({p + kv.first, kv.second});
     }
@@ -834,6 +932,15 @@ int oracle_quantize_q8(void* model) {
     kv.second.f32.resize(kv.second.numel);
     oracle_q8_roundtrip(kv.second.data.data(), kv.second.numel, kv.second.f32.data());
   }
+  return 0;
+}
+
+int oracle_block(void* model, int norm_kind, float t, const float* xv, const float* xa,
+                 const float* tv, const float* ta, float* ov, float* oa) {
+  Model& md = *static_cast<Model*>(model);
+  md.norm_kind = norm_kind;
+  block_forward(md, t, xv, xa, tv, ta, ov, oa);
+  md.norm_kind = 0;
   return 0;
 }
 

@@ -57,7 +57,19 @@ void* oracle_create(const oracle_geometry* g, int n_tensors, const char** names,
  * generated in C++ for full-width CPU baselines. */
 void* oracle_create_synthetic(const oracle_geometry* g, uint64_t seed, double bias_scale,
                               char* err, int errlen);
+/* The same with a config-1 FFN variant: ffn_kind 0 GELU(tanh) (the
+ * reference), 1 SiLU-gated (ffn.in weights hold [gate rows; up rows], 2F x W). */
+void* oracle_create_synthetic_ex(const oracle_geometry* g, uint64_t seed, double bias_scale,
+                                 int ffn_kind, char* err, int errlen);
 void oracle_destroy(void* model);
+/* Config 1: one MoT layer (layer 0) of the un-cached forward over given hidden
+ * states. xv [V][H] visual tokens, xa [1 + T][E] state token then action
+ * tokens, tv [Nt][H] / ta [Nt][E] text hidden states of the visual / action
+ * experts, t the action tokens' timestep (the state token and the visual
+ * tokens run at 0). norm_kind 0 LayerNorm inside AdaLN (the reference),
+ * 1 RMSNorm. Outputs ov [V][H], oa [1 + T][E]. */
+int oracle_block(void* model, int norm_kind, float t, const float* xv, const float* xa,
+                 const float* tv, const float* ta, float* ov, float* oa);
 /* Config-5 policy: replaces every linear weight whose rows are whole 32-value
  * blocks by its exact F32 Q8_0 dequantisation (no BF16 rounding of q * d). */
 int oracle_quantize_q8(void* model);

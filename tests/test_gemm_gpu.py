@@ -252,3 +252,4 @@ def test_gemm_pair_repeat_deterministic(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(y1, y2)
     assert s.error_code() == 0
+

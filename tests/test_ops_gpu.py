@@ -39,10 +39,27 @@ def torch_attention(q, k, v, scale):
     (1, 24, 769, 769),     # prefix joint attention at config-2 widths, ragged last key tile
 ])
 def test_attention_vs_torch(cuda_device, B, heads, lq, lk):
+    _attention_case(B, heads, lq, lk, 1.0)
+
+
+@pytest.mark.parametrize("B,heads,lq,lk,qs", [
+    (2, 24, 48, 817, 1.0),    # batch 2: 4 key splits of 2 tiles (online softmax across tiles)
+    (8, 24, 48, 817, 1.0),    # batch 8: one CTA per (sequence, head), 7 key tiles
+    (1, 24, 1, 512, 1.0),     # prefix state token over the prompt keys
+    (1, 2, 64, 3000, 4.0),    # 64 query rows, 24 tiles per CTA, wide scores (O rescaled)
+    (3, 5, 33, 250, 8.0),     # ragged rows / keys, very wide scores
+])
+def test_decode_attention_vs_torch(cuda_device, B, heads, lq, lk, qs):
+    """The tcgen05 decode attention (<= 64 queries per head, key splits merged
+    in a cluster) against torch F32, including multi-tile online softmax."""
+    _attention_case(B, heads, lq, lk, qs)
+
+
+def _attention_case(B, heads, lq, lk, qs):
     from wam_b200 import ops
 
     g = torch.Generator(device="cpu").manual_seed(lq * 31 + lk)
-    q = torch.randn(B, heads, lq, 128, generator=g).to(torch.bfloat16).cuda()
+    q = (torch.randn(B, heads, lq, 128, generator=g) * qs).to(torch.bfloat16).cuda()
     k = torch.randn(B, heads, lk, 128, generator=g).to(torch.bfloat16).cuda()
     v = torch.randn(B, heads, lk, 128, generator=g).to(torch.bfloat16).cuda()
     y = ops.attention(q, k, v)

@@ -125,8 +125,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         load_v(0);
         nk_issued = nv_issued = 1;
       }
+      griddep_launch_dependents();  // the next kernel may start its own pre-wait work
       griddep_wait();
-      griddep_launch_dependents();
       mbar_arrive_expect_tx(q_full, kTile);
       tma_load_4d(sq, &tm_q, q_full, 0, q0, head, seq, pol_q);
       tma_load_4d(sq + kHalf, &tm_q, q_full, 64, q0, head, seq, pol_q);
@@ -273,19 +273,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      if (rescale && j > 0) {
+      // The TMEM loads / stores are warp-collective: the warp runs them when
+      // any of its rows rescales, and the other rows scale by 1.
+      if (__any_sync(0xffffffffu, rescale) && j > 0) {
         const float corr = exp2f((m_used - m_new) * sl2);
+        const float f = rescale ? corr : 1.0f;
 #pragma unroll 1
         for (int c = 0; c < 64; c += 32) {
           uint32_t r[32];
           tmem_ld_x32(t_o + lane_off + c0 + c, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(u2f(r[i]) * corr);
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(u2f(r[i]) * f);
           tmem_st_x32(t_o + lane_off + c0 + c, r);
         }
         tmem_st_wait();
-        l *= corr;
+        if (rescale) l *= corr;
       }
       if (rescale) m_used = m_new;
       l += ls;

@@ -60,12 +60,14 @@ __device__ __forceinline__ float block128_sum(float v, float* red) {
 // costs a single memory round trip.
 // mode 0: AdaLN  y = bf16(n * (1 + scale) + shift), scale/shift F32
 // mode 1: affine y = bf16(n * w + b), w/b BF16
+// mode 2: AdaLN over RMSNorm (n = x * rsqrt(mean(x^2) + eps), no mean
+//         subtraction; the config-1 variant), scale/shift F32
 template <int MODE, int MAXC>
 __global__ void __launch_bounds__(kRowThreads)
     ln_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
               const void* pb, float eps, bf16* __restrict__ y, int ldy) {
+  griddep_launch_dependents();  // the next kernel may start its own pre-wait work
   griddep_wait();
-  griddep_launch_dependents();
   __shared__ float red[4];
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
@@ -79,7 +81,7 @@ __global__ void __launch_bounds__(kRowThreads)
     const int c = tid + i * kRowThreads;
     if (c < chunks) {
       load8(xr + c * 8, v[i]);
-      if (MODE == 0) {
+      if (MODE != 1) {
         const float4* sc = reinterpret_cast<const float4*>(static_cast<const float*>(pa) + c * 8);
         const float4* sh = reinterpret_cast<const float4*>(static_cast<const float*>(pb) + c * 8);
         const float4 s0 = sc[0], s1 = sc[1], h0 = sh[0], h1 = sh[1];
@@ -95,7 +97,7 @@ __global__ void __launch_bounds__(kRowThreads)
       for (int j = 0; j < 8; ++j) s += v[i][j];
     }
   }
-  const float mean = block128_sum(s, red) / cols;
+  const float mean = MODE == 2 ? 0.0f : block128_sum(s, red) / cols;
   float q = 0.0f;
 #pragma unroll
   for (int i = 0; i < MAXC; ++i)
@@ -114,7 +116,7 @@ __global__ void __launch_bounds__(kRowThreads)
       float f[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        f[j] = MODE == 0 ? fmaf((v[i][j] - mean) * inv_std, 1.0f + p0[i][j], p1[i][j])
+        f[j] = MODE != 1 ? fmaf((v[i][j] - mean) * inv_std, 1.0f + p0[i][j], p1[i][j])
                          : fmaf((v[i][j] - mean) * inv_std, p0[i][j], p1[i][j]);
       store8(yr + c * 8, f);
     }
@@ -130,8 +132,8 @@ template <int MODE, int MAXC>
 __global__ void __launch_bounds__(kRowThreads, 12)
     ln_stream_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
                      const void* pb, float eps, bf16* __restrict__ y, int ldy) {
+  griddep_launch_dependents();  // the next kernel may start its own pre-wait work
   griddep_wait();
-  griddep_launch_dependents();
   __shared__ float red[4];
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
@@ -153,7 +155,7 @@ __global__ void __launch_bounds__(kRowThreads, 12)
 #pragma unroll
       for (int j = 0; j < 8; ++j) s += v[j];
     }
-  const float mean = block128_sum(s, red) / cols;
+  const float mean = MODE == 2 ? 0.0f : block128_sum(s, red) / cols;
   float q = 0.0f;
 #pragma unroll
   for (int i = 0; i < MAXC; ++i)
@@ -173,7 +175,7 @@ __global__ void __launch_bounds__(kRowThreads, 12)
     if (c < chunks) {
       float v[8], p0[8], p1[8];
       load8(reinterpret_cast<const bf16*>(&raw[i]), v);
-      if (MODE == 0) {
+      if (MODE != 1) {
         const float4* sc = reinterpret_cast<const float4*>(static_cast<const float*>(pa) + c * 8);
         const float4* sh = reinterpret_cast<const float4*>(static_cast<const float*>(pb) + c * 8);
         const float4 s0 = __ldg(sc), s1 = __ldg(sc + 1), h0 = __ldg(sh), h1 = __ldg(sh + 1);
@@ -188,7 +190,7 @@ __global__ void __launch_bounds__(kRowThreads, 12)
       float f[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        f[j] = MODE == 0 ? fmaf((v[j] - mean) * inv_std, 1.0f + p0[j], p1[j])
+        f[j] = MODE != 1 ? fmaf((v[j] - mean) * inv_std, 1.0f + p0[j], p1[j])
                          : fmaf((v[j] - mean) * inv_std, p0[j], p1[j]);
       store8(yr + c * 8, f);
     }
@@ -201,8 +203,8 @@ template <int MODE>
 __global__ void __launch_bounds__(256)
     ln_wide_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
                    const void* pb, float eps, bf16* __restrict__ y, int ldy) {
+  griddep_launch_dependents();  // the next kernel may start its own pre-wait work
   griddep_wait();
-  griddep_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -216,7 +218,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int i = 0; i < 8; ++i) s += f[i];
   }
-  const float mean = warp_sum(s) / cols;
+  const float mean = MODE == 2 ? 0.0f : warp_sum(s) / cols;
   float q = 0.0f;
   for (int c = lane; c < chunks; c += 32) {
     float f[8];
@@ -231,7 +233,7 @@ __global__ void __launch_bounds__(256)
   for (int c = lane; c < chunks; c += 32) {
     float f[8], p0[8], p1[8];
     load8(xr + c * 8, f);
-    if (MODE == 0) {
+    if (MODE != 1) {
       for (int i = 0; i < 8; ++i) {
         p0[i] = static_cast<const float*>(pa)[c * 8 + i];
         p1[i] = static_cast<const float*>(pb)[c * 8 + i];
@@ -242,7 +244,7 @@ __global__ void __launch_bounds__(256)
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      f[i] = MODE == 0 ? fmaf((f[i] - mean) * inv_std, 1.0f + p0[i], p1[i])
+      f[i] = MODE != 1 ? fmaf((f[i] - mean) * inv_std, 1.0f + p0[i], p1[i])
                        : fmaf((f[i] - mean) * inv_std, p0[i], p1[i]);
     store8(yr + c * 8, f);
   }
@@ -262,8 +264,8 @@ __device__ __forceinline__ float rope_theta(const QkvScatter& a, int dim, int po
 // weights) in registers. MAXC = 0: generic loop.
 template <int MAXC>
 __global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const __grid_constant__ QkvScatter a) {
+  griddep_launch_dependents();  // the next kernel may start its own pre-wait work
   griddep_wait();
-  griddep_launch_dependents();
   __shared__ float red[3][4];
   const int row = blockIdx.x;
   const int which = threadIdx.y;
@@ -533,6 +535,11 @@ void launch_ln_modulate(const bf16* x, int ldx, int rows, int cols, const float*
 void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w, const bf16* b,
                       float eps, bf16* y, int ldy, cudaStream_t s) {
   launch_ln<1>(x, ldx, rows, cols, w, b, eps, y, ldy, s);
+}
+
+void launch_rms_modulate(const bf16* x, int ldx, int rows, int cols, const float* scale,
+                         const float* shift, float eps, bf16* y, int ldy, cudaStream_t s) {
+  launch_ln<2>(x, ldx, rows, cols, scale, shift, eps, y, ldy, s);
 }
 
 void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s) {

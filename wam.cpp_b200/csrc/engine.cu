@@ -640,13 +640,24 @@ bool MotEngine::ensure_tiled(const std::string& wname, int n, int k, std::string
 
 bool MotEngine::gemm(Program& p, const bf16* x, int ldx, int m, const std::string& wname, int n,
                      int k, int epi, bool bias, const float* gate, const bf16* resid, int ldr,
-                     void* out, int ldo, std::string* err) {
-  const bf16* w = W(wname + ".weight", static_cast<int64_t>(n) * k);
-  const bf16* b = bias ? W(wname + ".bias", n) : nullptr;
-  if (!w || (bias && !b)) {
+                     void* out, int ldo, std::string* err, int total_n, int row0) {
+  // Rows [row0, row0 + n) of a weight with total_n rows (default: all n rows).
+  if (total_n < 0) total_n = n;
+  if (row0 < 0 || row0 + n > total_n ||
+      (row0 % gemm_weight_tile_rows() != 0 && total_n % gemm_weight_tile_rows() == 0)) {
+    *err = "bad weight row range of " + wname;
+    return false;
+  }
+  const bf16* w_all = W(wname + ".weight", static_cast<int64_t>(total_n) * k);
+  const bf16* b_all = bias ? W(wname + ".bias", total_n) : nullptr;
+  if (!w_all || (bias && !b_all)) {
     *err = "missing or mis-shaped weight " + wname;
     return false;
   }
+  // Row-major and re-tiled layouts both keep rows in order (whole 256-row
+  // tiles outermost), so a row range starting on a tile starts at row0 * k.
+  const bf16* w = w_all + static_cast<size_t>(row0) * k;
+  const bf16* b = b_all ? b_all + row0 : nullptr;
   // Q8_0 linear weights with whole 256-row tiles stream as Q8_0 GEMM tiles
   // (made from the blocks the first time a plan uses them).
   const auto qb = q8_blocks_.find(wname + ".weight");
@@ -654,21 +665,26 @@ bool MotEngine::gemm(Program& p, const bf16* x, int ldx, int m, const std::strin
   // tensor-bound ones (prefix, batched) read the dequantised BF16 copy, which
   // gives the same results (the Q8_0 GEMM is bit-identical to the BF16 GEMM on
   // q * d) without converting every tile on the CUDA cores.
-  const bool q8 = qb != q8_blocks_.end() && m <= 64 && n % gemm_weight_tile_rows() == 0 &&
-                  k % 64 == 0;
+  const bool q8 = qb != q8_blocks_.end() && m <= 64 && total_n % gemm_weight_tile_rows() == 0 &&
+                  n % gemm_weight_tile_rows() == 0 && k % 64 == 0;
   if (q8 && !q8_tiles_.count(wname)) {
-    uint8_t* tiles = dalloc<uint8_t>(static_cast<size_t>(n / 256) * (k / 64) * kQ8TileBytes, err);
+    uint8_t* tiles =
+        dalloc<uint8_t>(static_cast<size_t>(total_n / 256) * (k / 64) * kQ8TileBytes, err);
     if (!tiles) return false;
-    launch_q8_retile(qb->second, tiles, n, k, stream_);
+    launch_q8_retile(qb->second, tiles, total_n, k, stream_);
     CK(cudaGetLastError());
     q8_tiles_[wname] = tiles;
   }
   // Every other weight with whole 256-row tiles is re-tiled in place, the
   // first time a plan uses it, into contiguous 32 KB UMMA tiles (one bulk copy
   // per stage).
-  const bool tiled = !q8 && !rowmajor_weights_ && n % gemm_weight_tile_rows() == 0 && k % 64 == 0;
-  if (tiled && !ensure_tiled(wname, n, k, err)) return false;
-  const bf16* wsrc = q8 ? reinterpret_cast<const bf16*>(q8_tiles_[wname]) : w;
+  const bool tiled = !q8 && !rowmajor_weights_ && total_n % gemm_weight_tile_rows() == 0 &&
+                     n % gemm_weight_tile_rows() == 0 && k % 64 == 0;
+  if (tiled && !ensure_tiled(wname, total_n, k, err)) return false;
+  const bf16* wsrc =
+      q8 ? reinterpret_cast<const bf16*>(q8_tiles_[wname] +
+                                         static_cast<size_t>(row0 / 256) * (k / 64) * kQ8TileBytes)
+         : w;
   return add_gemm(p, x, ldx, m, wsrc, n, k, epi, b, gate, resid, ldr, out, ldo, tiled, q8, wname, err);
 }
 

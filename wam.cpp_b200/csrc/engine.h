@@ -150,7 +150,7 @@ class MotEngine {
   bool build(int batch, std::string* err);
   bool gemm(Program& p, const bf16* x, int ldx, int m, const std::string& wname, int n, int k,
             int epi, bool bias, const float* gate, const bf16* resid, int ldr, void* out, int ldo,
-            std::string* err);
+            std::string* err, int total_n = -1, int row0 = 0);
   // Plans one GEMM on prepared weights (re-tiled, Q8_0 tiles or row-major).
   bool add_gemm(Program& p, const bf16* x, int ldx, int m, const bf16* wsrc, int n, int k, int epi,
                 const bf16* bias, const float* gate, const bf16* resid, int ldr, void* out, int ldo,

@@ -77,7 +77,7 @@ __device__ __forceinline__ void epi_run_t(const GemmArgs& a, int m, int n0, cons
                                           const float* bias, const float* gate) {
   float o[CNT];
   float r[CNT];
-  if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
+  if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES || EPI == EPI_MUL) {
     const uint4* rp =
         reinterpret_cast<const uint4*>(a.residual + static_cast<long long>(m) * a.ldr + n0);
 #pragma unroll
@@ -114,6 +114,10 @@ __device__ __forceinline__ void epi_run_t(const GemmArgs& a, int m, int n0, cons
       float t = bf16_round(acc);
       if (hb) t = bf16_round(t + b);
       o[j] = r[j] + t;
+    } else if constexpr (EPI == EPI_MUL) {
+      float t = bf16_round(acc);
+      if (hb) t = bf16_round(t + b);
+      o[j] = r[j] * t;
     } else if constexpr (EPI == EPI_F32_BIAS) {
       o[j] = acc + b;
     } else if constexpr (EPI == EPI_BIAS_GELU_R) {
@@ -162,6 +166,7 @@ __device__ __forceinline__ void epi_run(const GemmArgs& a, int m, int n0, const 
     case EPI_BIAS_SILU: epi_run_t<EPI_BIAS_SILU, CNT>(a, m, n0, v, bias, gate); break;
     case EPI_GATED_RES: epi_run_t<EPI_GATED_RES, CNT>(a, m, n0, v, bias, gate); break;
     case EPI_RES: epi_run_t<EPI_RES, CNT>(a, m, n0, v, bias, gate); break;
+    case EPI_MUL: epi_run_t<EPI_MUL, CNT>(a, m, n0, v, bias, gate); break;
     case EPI_F32_BIAS: epi_run_t<EPI_F32_BIAS, CNT>(a, m, n0, v, bias, gate); break;
     case EPI_BIAS_GELU_R: epi_run_t<EPI_BIAS_GELU_R, CNT>(a, m, n0, v, bias, gate); break;
     case EPI_BIAS_GELU_ERF: epi_run_t<EPI_BIAS_GELU_ERF, CNT>(a, m, n0, v, bias, gate); break;
@@ -200,8 +205,8 @@ __device__ __forceinline__ void stage16_t(const GemmArgs& a, uint8_t* stg, int r
         float t = bf16_round(acc);
         if (hb) t = bf16_round(t + b);
         o[j] = silu(t);
-      } else if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
-        // The residual is added in pass 2 to this BF16-exact linear output.
+      } else if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES || EPI == EPI_MUL) {
+        // The residual is added (multiplied) in pass 2 to this BF16-exact linear output.
         float t = bf16_round(acc);
         if (hb) t = bf16_round(t + b);
         o[j] = t;
@@ -239,6 +244,7 @@ __device__ __forceinline__ void stage16(const GemmArgs& a, uint8_t* stg, int row
     case EPI_BIAS_SILU: stage16_t<EPI_BIAS_SILU>(a, stg, row, c, v, bias); break;
     case EPI_GATED_RES: stage16_t<EPI_GATED_RES>(a, stg, row, c, v, bias); break;
     case EPI_RES: stage16_t<EPI_RES>(a, stg, row, c, v, bias); break;
+    case EPI_MUL: stage16_t<EPI_MUL>(a, stg, row, c, v, bias); break;
     case EPI_F32_BIAS: stage16_t<EPI_F32_BIAS>(a, stg, row, c, v, bias); break;
     case EPI_BIAS_GELU_R: stage16_t<EPI_BIAS_GELU_R>(a, stg, row, c, v, bias); break;
     case EPI_BIAS_GELU_ERF: stage16_t<EPI_BIAS_GELU_ERF>(a, stg, row, c, v, bias); break;
@@ -266,7 +272,7 @@ __device__ __forceinline__ void copy_out_t(const GemmArgs& a, const uint8_t* stg
     } else {
       uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(stg) +
                                                 r * kStageLdB + g * 8);
-      if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES) {
+      if constexpr (EPI == EPI_GATED_RES || EPI == EPI_RES || EPI == EPI_MUL) {
         const uint4 rv = *reinterpret_cast<const uint4*>(a.residual + m * a.ldr + n0);
         uint32_t tw[4] = {u.x, u.y, u.z, u.w};
         const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
@@ -278,6 +284,9 @@ __device__ __forceinline__ void copy_out_t(const GemmArgs& a, const uint8_t* stg
           if constexpr (EPI == EPI_GATED_RES) {
             o0 = fmaf(t0v, gate[g * 8 + 2 * j], r0v);
             o1 = fmaf(t1v, gate[g * 8 + 2 * j + 1], r1v);
+          } else if constexpr (EPI == EPI_MUL) {
+            o0 = r0v * t0v;
+            o1 = r1v * t1v;
           } else {
             o0 = r0v + t0v;
             o1 = r1v + t1v;
@@ -300,6 +309,7 @@ __device__ __forceinline__ void copy_out(const GemmArgs& a, const uint8_t* stg, 
       copy_out_t<EPI_GATED_RES>(a, stg, rows, m_base, n_base, gate, t0, nthreads);
       break;
     case EPI_RES: copy_out_t<EPI_RES>(a, stg, rows, m_base, n_base, gate, t0, nthreads); break;
+    case EPI_MUL: copy_out_t<EPI_MUL>(a, stg, rows, m_base, n_base, gate, t0, nthreads); break;
     case EPI_F32_OUT:
       copy_out_t<EPI_F32_OUT>(a, stg, rows, m_base, n_base, gate, t0, nthreads);
       break;
@@ -609,11 +619,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(smem_w + stage * kBBytes, &tm_w, &full[stage], kb * kBK, n_base, pol_w);
       };
       const int pre = nkb < S ? nkb : S;
-      // Weights never depend on the preceding kernel: the first two stages'
+      // Weights never depend on the preceding kernel: the first pre_w stages'
       // weight copies start before waiting for it (programmatic dependent
       // launch). The copies of one SM complete roughly in issue order, so the
       // remaining first-round copies alternate token / weight by stage.
-      const int pre_w = pre < 2 ? pre : 2;
+      const int pre_w = pre < args.pre_w ? pre : args.pre_w;
       for (int i = 0; i < pre_w; ++i) {
         mbar_arrive_expect_tx(&full[i], stage_tx);
         load_w(i, kb0 + i);
@@ -1231,6 +1241,13 @@ bool g_pair = [] {
   const char* v = std::getenv("WAM_B200_GEMM_PAIR");
   return v && *v == '1';
 }();
+// Stages whose weight copies a GEMM CTA issues before waiting for the
+// preceding kernel (WAM_B200_GEMM_PREW, default 2).
+int g_pre_w = [] {
+  const char* v = std::getenv("WAM_B200_GEMM_PREW");
+  const int n = v ? std::atoi(v) : 2;
+  return n < 0 ? 0 : (n > kMaxStages ? kMaxStages : n);
+}();
 
 // Kernel and split-K choice of one GEMM shape. Pair tiles (256 tokens x 256
 // features) that leave more than a quarter of the resident pairs idle split K
@@ -1384,13 +1401,14 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   if (ldx % 8 != 0 || ldx < k) return "gemm: activation row stride must be >= K and a multiple of 8";
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
     return "gemm: operands must be 16-byte aligned";
-  if ((epilogue == EPI_GATED_RES && (!gate || !residual)) || (epilogue == EPI_RES && !residual))
+  if ((epilogue == EPI_GATED_RES && (!gate || !residual)) ||
+      ((epilogue == EPI_RES || epilogue == EPI_MUL) && !residual))
     return "gemm: residual epilogue needs its inputs";
-  if (epilogue < 0 || epilogue > EPI_BIAS_GELU_ERF) return "gemm: unknown epilogue";
+  if (epilogue < 0 || epilogue > EPI_MUL) return "gemm: unknown epilogue";
   const int out_align = epilogue == EPI_F32_OUT ? 4 : 8;
   if (ldo < n || ldo % out_align != 0 || (reinterpret_cast<uintptr_t>(out) & 15))
     return "gemm: output must be 16-byte aligned with a row stride >= N in 16-byte units";
-  if ((epilogue == EPI_GATED_RES || epilogue == EPI_RES) &&
+  if ((epilogue == EPI_GATED_RES || epilogue == EPI_RES || epilogue == EPI_MUL) &&
       (ldr < n || ldr % 8 != 0 || (reinterpret_cast<uintptr_t>(residual) & 15)))
     return "gemm: residual must be 16-byte aligned with a row stride >= N in 16-byte units";
   std::memset(op, 0, sizeof(*op));
@@ -1443,6 +1461,7 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   a.split_mode = mode;
   a.a_rows = a_rows;
   a.stages = stages_for(a_rows, w_q8);
+  a.pre_w = g_pre_w;
   a.w_tiled = w_tiled && !w_q8 ? w : nullptr;
   a.w_q8 = w_q8 ? reinterpret_cast<const uint8_t*>(w) : nullptr;
   a.tiles_m = tiles_m;

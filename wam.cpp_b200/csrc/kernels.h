@@ -27,6 +27,7 @@ enum GemmEpilogue : int {
   EPI_F32_OUT = 6,    // y_f32 = acc                                 raw accumulator (tests)
   EPI_BIAS_GELU_R = 7,  // y = bf16(gelu_tanh(bf16(bf16(acc) + b)))   linear + ggml_gelu (text MLP)
   EPI_BIAS_GELU_ERF = 8,  // y = bf16(gelu_erf(bf16(bf16(acc) + b)))  linear + ggml_gelu_erf (decoder)
+  EPI_MUL = 9,        // y = bf16(r * bf16(bf16(acc) + b))          linear + ggml_mul (SiLU-gated FFN up)
 };
 
 // Split-K reduction. SPLIT_CLUSTER: the splits of a tile form a thread-block
@@ -44,6 +45,7 @@ struct GemmArgs {
   int split_mode;
   int a_rows;  // token rows loaded per tile (<= 128)
   int stages;  // pipeline stages (one weight + one token k-block each)
+  int pre_w;   // stages whose weight copies start before the grid-dependency wait
   const bf16* w_tiled;  // weights re-tiled by launch_retile_weights, or null (tensor map)
   const uint8_t* w_q8;  // Q8_0 weight tiles (launch_q8_retile), or null
   int tiles_m, tiles_n;
@@ -118,6 +120,10 @@ size_t gemm_scratch_floats(int m, int n, int k, int num_sms, int force_splits, i
 // shared by all rows (norm_bf16_fused<affine=false>, native-bf16.patch:368-409).
 void launch_ln_modulate(const bf16* x, int ldx, int rows, int cols, const float* scale,
                         const float* shift, float eps, bf16* y, int ldy, cudaStream_t s);
+// RMSNorm (n = x * rsqrt(mean(x^2) + eps)) then the same AdaLN modulation: the
+// config-1 "RMSNorm + AdaLN" block variant (no reference counterpart).
+void launch_rms_modulate(const bf16* x, int ldx, int rows, int cols, const float* scale,
+                         const float* shift, float eps, bf16* y, int ldy, cudaStream_t s);
 // Affine LayerNorm: y = bf16(n * w[c] + b[c]), w/b BF16 (norm_bf16_fused<affine=true>).
 void launch_ln_affine(const bf16* x, int ldx, int rows, int cols, const bf16* w, const bf16* b,
                       float eps, bf16* y, int ldy, cudaStream_t s);
@@ -189,6 +195,12 @@ void launch_attention(const AttnArgs& a, cudaStream_t s);
 cudaError_t attention_tc_init();
 bool attention_tc_eligible(const AttnArgs& a);
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s);
+// tcgen05 attention for <= 64 query rows per (sequence, head) with key splits
+// merged inside a thread-block cluster (attention_dec.cu).
+cudaError_t attention_dec_init();
+bool attention_dec_eligible(const AttnArgs& a);
+int attention_dec_splits(const AttnArgs& a, int num_sms);
+cudaError_t launch_attention_dec(const AttnArgs& a, int num_sms, cudaStream_t s);
 
 // Workspace the split-KV merge of `a` needs (0 when it does not split).
 size_t attention_ws_floats(const AttnArgs& a);

@@ -20,8 +20,6 @@ enum DeviceError : unsigned {
   kErrProducerTimeout = 1,
   kErrMmaTimeout = 2,
   kErrEpilogueTimeout = 3,
-  kErrStepPhaseTimeout = 4,  // step kernel: a grid phase counter never filled
-  kErrStepRingTimeout = 5,   // step kernel: the copy ring never drained
 };
 
 // Bound on any mbarrier wait, in SM clock cycles (~2 s at the B200's 1.965 GHz
@@ -367,6 +365,29 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
+}
+
+// Split cluster barrier: every thread arrives (release) early and waits
+// (acquire) only where it needs the peers' earlier writes. Warps must be
+// converged (.aligned).
+__device__ __forceinline__ void cluster_arrive_aligned() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_aligned() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, 16-byte aligned) from this CTA's
+// shared memory into another CTA's (shared::cluster addresses of the
+// destination and of its mbarrier), completion counted in bytes on that
+// mbarrier. No multicast.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes,
+                                                  uint32_t remote_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "r"(src), "r"(bytes), "r"(remote_bar)
+      : "memory");
 }
 
 __device__ __forceinline__ void cluster_sync_all() {
