@@ -6,7 +6,9 @@ steps), synthetic random-init BF16 weights and seeded synthetic inputs of the
 config's shapes. With --gpus N the engine runs as N independent data-parallel
 replicas (one process per GPU, no collective); value = all chunks / max-over-
 ranks time. The same line carries "config4": BASELINE config 4, 64 requests
-per box split 64/N per GPU (strong scaling), timed after the main measurement.
+per box split 64/N per GPU (strong scaling), timed after the main measurement,
+and (one GPU) "config1": one MoT block through wam_b200_block_forward in the
+reference's form and BASELINE's literal form, beside the CPU oracle's block.
 
   python bench.py [--gpus N --steps K --warmup W]        this engine
   python bench.py --impl reference [...]                 the reference arm: the
@@ -370,6 +372,8 @@ def main() -> None:
                     help="op case gemm: split-K factor (0 = the planner's choice)")
     ap.add_argument("--scratch", action="store_true",
                     help="op case gemm: split-K partials through a global workspace (as the engine)")
+    ap.add_argument("--no-config1", action="store_true",
+                    help="skip the config-1 single-block point (GPU and CPU) of the bench line")
     ap.add_argument("--config4-requests", type=int, default=64,
                     help="BASELINE config 4: requests per box, split over the GPUs (0 = skip)")
     ap.add_argument("--config4-steps", type=int, default=3,
@@ -491,9 +495,12 @@ def main() -> None:
     if rank != 0:
         return
     cb = None
+    c1 = None
     if world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(args.cpu_layers)
         cb["cpu_model"] = host_cpu_model()
+    if world == 1 and not args.no_config1:
+        c1 = run_config1(local, cpu=not args.no_cpu_baseline)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_s * 1e3 / args.steps,
@@ -507,9 +514,75 @@ def main() -> None:
         "gpu_launches": kernels_per_chunk * args.steps,
         "kernels_per_chunk": kernels_per_chunk,
         "config4": c4,
+        "config1": c1,
         "cpu_baseline": cb,
     }
     print(json.dumps(line), flush=True)
+
+
+def block_flops(g, ffn: str) -> float:
+    """Algorithmic FLOPs of one config-1 block (2 per MAC): both experts'
+    projections (QKV, O, cross Q / K / V / O, FFN up and down; the SiLU-gated
+    FFN has twice the up rows) and the joint / cross attention products."""
+    H, E, V, T, Nt = g.hidden, g.action_hidden, g.visual_tokens, g.action_chunk, g.prompt_tokens
+    fin = 2 if ffn == "swiglu" else 1
+    rows = {"v": (V, H, g.ffn), "a": (1 + T, E, g.action_ffn)}
+    f = 0.0
+    for m, w, ff in rows.values():
+        f += 2.0 * m * (3 * H * w + H * w + H * w + H * w + fin * ff * w + w * ff)
+        f += 2.0 * Nt * 2 * H * w  # text K / V projection of this expert
+    P = 1 + V
+    f += 4.0 * P * P * H + 4.0 * T * (P + T) * H  # joint attention (prefix rows, action rows)
+    f += 4.0 * (V + 1 + T) * Nt * H  # cross attention of both experts
+    return f
+
+
+def run_config1(dev_index: int = 0, reps: int = 10, cpu: bool = True) -> dict:
+    """one MoT block at config-2 widths (768 visual + 1 state
+    + 48 action tokens, 512 text tokens as cross-attention keys) through
+    wam_b200_block_forward, for the reference's form (LayerNorm AdaLN, GELU
+    FFN) and BASELINE's literal form (RMSNorm AdaLN, SiLU-gated FFN). GPU: device
+    ms per block (CUDA events around the block's three graphs) and end-to-end ms
+    (host inputs and outputs); CPU: the oracle's block_forward on the host cores."""
+    import torch
+    from wam_b200 import workload as wl
+    from wam_b200.engine import Engine
+
+    g = wl.CONFIG1
+    x = wl.make_block_inputs(g, SEED)
+    out = {"workload": "config1: one MoT block over given hidden states (768 visual, 1 state, "
+                       "48 action tokens; 512 text tokens as cross-attention keys)", "variants": {}}
+    pk = peaks()
+    for ffn, norm in (("gelu", "layernorm"), ("swiglu", "rmsnorm")):
+        eng = Engine(g, seed=SEED, bias_scale=0.0, device=dev_index, prompt_cache=False, ffn=ffn,
+                     norm=norm, block=True)
+        for _ in range(3):
+            eng.block_forward(x["t"], x["xv"], x["xa"], x["tv"], x["ta"])
+        dev_ms, wall = [], []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            _, _, ms = eng.block_forward(x["t"], x["xv"], x["xa"], x["tv"], x["ta"], with_time=True)
+            wall.append((time.perf_counter() - t0) * 1e3)
+            dev_ms.append(ms)
+        del eng
+        torch.cuda.empty_cache()
+        fl = block_flops(g, ffn)
+        d = statistics.median(dev_ms)
+        rec = {"device_ms_p50": d, "e2e_ms_p50": statistics.median(wall), "gflop": fl / 1e9,
+               "tflops": fl / d / 1e9, "frac_of_bf16_peak": fl / d / 1e9 / pk["bf16_tflops"]}
+        if cpu:
+            import oracle
+
+            om = oracle.OracleModel(g, None, seed=SEED, bias_scale=0.0,
+                                    ffn_kind=1 if ffn == "swiglu" else 0)
+            om.block(x["t"], x["xv"], x["xa"], x["tv"], x["ta"], norm_kind=1 if norm == "rmsnorm" else 0)
+            t0 = time.perf_counter()
+            om.block(x["t"], x["xv"], x["xa"], x["tv"], x["ta"], norm_kind=1 if norm == "rmsnorm" else 0)
+            rec["cpu_ms"] = (time.perf_counter() - t0) * 1e3
+            rec["cpu_cores"] = oracle.lib().oracle_threads()
+            rec["cpu_kind"] = "port (F32 OpenMP oracle)"
+        out["variants"][f"{ffn}+{norm}"] = rec
+    return out
 
 
 def run_config4(args, g, world, rank, local, barrier, max_over_ranks) -> dict:

@@ -267,6 +267,17 @@ typedef struct wam_b200_options {
    * quantised on the device with the gguf-py Q8_0 rules; a GGUF artifact may
    * hold Q8_0 tensors). Linear layers then compute with q * d rounded to BF16. */
   int weight_format;
+  /* Added with the single-block entry (read only when struct_size covers them).
+   * ffn_kind: 0 GELU(tanh) FFN (the reference, mot.cpp:341-346), 1 SiLU-gated
+   * FFN silu(x Wg + bg) * (x Wu + bu) with ffn.in holding [gate rows; up rows]
+   * (2F x W); norm_kind: 0 LayerNorm inside the AdaLN modulated norms (the
+   * reference, mot.cpp:147-159), 1 RMSNorm; block_mode != 0 creates an engine
+   * for wam_b200_block_forward (synthetic weights, layers == 1, steps == 1,
+   * max_batch == 1, prompt_cache == 0). The variants are BASELINE config 1's
+   * literal block ("RMSNorm + AdaLN, SiLU-gated MLP"); synthetic weights only. */
+  int ffn_kind;
+  int norm_kind;
+  int block_mode;
 } wam_b200_options;
 
 /* One request (EngineInputsView, src/models/gwp05/engine/engine.h:91-105, with
@@ -310,6 +321,30 @@ WAM_B200_API int wam_b200_predict(wam_b200_engine* engine, const wam_b200_reques
 WAM_B200_API int wam_b200_predict_batch(wam_b200_engine* engine, const wam_b200_request* requests,
                                         int batch, float* action_out, size_t action_out_n,
                                         wam_b200_stats* stats, wam_b200_status* status);
+
+/* One MoT layer over given hidden states: the layer body
+ * of the reference's un-cached forward, run_mot_step (src/models/gwp05/engine/
+ * mot.cpp:1008-1067), for layer 0 of a block-mode engine. The action stream
+ * [state token; action tokens] runs through the action expert (state token at
+ * timestep 0, action tokens at `timestep`; action_timesteps with the clean
+ * state, semantics.cpp:224-233), the visual tokens through the visual expert
+ * at 0; one joint self-attention where state and visual queries see the state
+ * and visual keys and action queries see every key (the mask built at
+ * mot.cpp:1147-1158); then each expert's cross attention over its text hidden
+ * states (projected and normalised by the layer) and its FFN. Host pointers:
+ * visual [V][H], action [1 + T][E], text_visual [N_t][H], text_action
+ * [N_t][E] (F32, used as BF16 hidden states); outputs likewise. */
+typedef struct wam_b200_block_inputs {
+  const float* visual;
+  const float* action;
+  const float* text_visual;
+  const float* text_action;
+  float timestep;
+} wam_b200_block_inputs;
+WAM_B200_API int wam_b200_block_forward(wam_b200_engine* engine, const wam_b200_block_inputs* in,
+                                        float* visual_out, size_t visual_out_n, float* action_out,
+                                        size_t action_out_n, float* device_ms,
+                                        wam_b200_status* status);
 
 /* Split form of predict_batch for device-resident timing: stage (host->device
  * inputs), run (enqueue prompt projection, prefix and denoise on the engine's

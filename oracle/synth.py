@@ -28,8 +28,9 @@ _PKG = Path(__file__).resolve().parent.parent / "wam.cpp_b200"
 if str(_PKG) not in sys.path:
     sys.path.insert(0, str(_PKG))
 
-from wam_b200.workload import (CONFIG2, CONFIG2_L1, CONFIG2_L2, PAIR, SMALL,  # noqa: E402,F401
-                               TALL, TINY, WIDE, Geometry, Request, make_request, statistics)
+from wam_b200.workload import (CONFIG1, CONFIG2, CONFIG2_L1, CONFIG2_L2, PAIR,  # noqa: E402,F401
+                               SMALL, TALL, TINY, WIDE, Geometry, Request, make_block_inputs,
+                               make_request, statistics)
 
 GOLDEN = np.uint64(0x9E3779B97F4A7C15)
 M1 = np.uint64(0xBF58476D1CE4E5B9)

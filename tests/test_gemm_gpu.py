@@ -93,7 +93,7 @@ def gelu_tanh(v):
 
 @pytest.mark.parametrize("m,n,k", [(48, 3072, 3072), (768, 1024, 512), (16, 384, 128)])
 @pytest.mark.parametrize("epi", ["bias", "gelu", "gelu_r", "gelu_erf", "silu", "gated", "res",
-                                 "f32bias"])
+                                 "f32bias", "mul"])
 def test_gemm_epilogues(cuda_device, m, n, k, epi):
     from wam_b200 import ops
 
@@ -123,6 +123,9 @@ def test_gemm_epilogues(cuda_device, m, n, k, epi):
     elif epi == "res":
         y = ops.gemm(x, w, ops.EPI_RES, bias=b, residual=resid)
         ref = bf(resid.float() + lin)
+    elif epi == "mul":
+        y = ops.gemm(x, w, ops.EPI_MUL, bias=b, residual=resid)
+        ref = bf(resid.float() * lin)
     else:
         y = ops.gemm(x, w, ops.EPI_F32_BIAS, bias=b)
         ref = bf(acc + b.float())
@@ -253,3 +256,35 @@ def test_gemm_pair_repeat_deterministic(cuda_device):
     assert torch.equal(y1, y2)
     assert s.error_code() == 0
 
+
+
+STREAM_SHAPES = [(48, 3072, 3072), (48, 9216, 3072), (48, 14336, 3072), (48, 3072, 14336),
+                 (1, 3072, 3072), (11, 18432, 3072), (64, 2048, 1024), (33, 1536, 640),
+                 (16, 4096, 256)]
+
+
+@pytest.mark.parametrize("m,n,k", STREAM_SHAPES)
+def test_gemm_stream_shapes(cuda_device, m, n, k):
+    """Token tiles of <= 64 rows: the streaming kernel (full K per CTA, 128
+    features each, multi-k-block TMA boxes) where it is planned (N / 128 >= 96,
+    K <= 4096: 48 x 14336 x 3072, 11 x 18432 x 3072) and split-K elsewhere:
+    raw accumulators against F32, re-tiled weights equal to row-major bit for
+    bit, a gated residual written in place over its input."""
+    from wam_b200 import ops
+
+    x, w, b = make(m, n, k, seed=m + n + k)
+    tw = ops.TiledWeight(w)
+    ref = x.float() @ w.float().T
+    y_row = ops.gemm(x, w, ops.EPI_F32_OUT)
+    y_tiled = ops.gemm(x, tw, ops.EPI_F32_OUT)
+    torch.cuda.synchronize()
+    # one F32 accumulator per output over the whole K (no split partials): the
+    # rounding error grows like sqrt(K)
+    assert rel_l2(y_tiled, ref) < 1e-5 * max(1.0, (k / 3072) ** 0.5)
+    assert torch.equal(y_row, y_tiled)
+    gate = torch.randn(n, device="cuda")
+    h = torch.randn(m, n, device="cuda").to(torch.bfloat16)
+    expect = bf(h.float() + bf(bf(ref) + b.float()) * gate)
+    ops.gemm(x, tw, ops.EPI_GATED_RES, bias=b, gate=gate, residual=h, out=h)
+    torch.cuda.synchronize()
+    assert rel_l2(h.float(), expect) < 1e-2

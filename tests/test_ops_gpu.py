@@ -50,8 +50,9 @@ def test_attention_vs_torch(cuda_device, B, heads, lq, lk):
     (3, 5, 33, 250, 8.0),     # ragged rows / keys, very wide scores
 ])
 def test_decode_attention_vs_torch(cuda_device, B, heads, lq, lk, qs):
-    """The tcgen05 decode attention (<= 64 queries per head, key splits merged
-    in a cluster) against torch F32, including multi-tile online softmax."""
+    """The decode attention (<= 64 queries per head, key splits merged in a
+    cluster) against torch F32, including multi-tile online softmax and wide
+    score ranges."""
     _attention_case(B, heads, lq, lk, qs)
 
 

@@ -82,8 +82,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
     cp_async_commit();
   };
   if (kv_static) load_kv0();
-  griddep_launch_dependents();  // the next kernel may start its own pre-wait work
   griddep_wait();
+  griddep_launch_dependents();
   load_tile(s_q, qg, a.lq - q0, tid);
   cp_async_commit();
   if (!kv_static) load_kv0();
@@ -350,7 +350,6 @@ cudaError_t attention_init() {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
   if ((e = attention_tc_init()) != cudaSuccess) return e;
-  if ((e = attention_dec_init()) != cudaSuccess) return e;
   return cudaFuncSetAttribute(attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               kSmem);
 }
@@ -385,7 +384,6 @@ void launch_attention(const AttnArgs& a_in, cudaStream_t s) {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
-  if (attention_dec_eligible(a_in) && launch_attention_dec(a_in, sms, s) == cudaSuccess) return;
   AttnArgs a = a_in;
   const int splits = attention_splits(a, sms);
   const int qblocks = (a.lq + kBQ - 1) / kBQ;

@@ -125,8 +125,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         load_v(0);
         nk_issued = nv_issued = 1;
       }
-      griddep_launch_dependents();  // the next kernel may start its own pre-wait work
       griddep_wait();
+      griddep_launch_dependents();
       mbar_arrive_expect_tx(q_full, kTile);
       tma_load_4d(sq, &tm_q, q_full, 0, q0, head, seq, pol_q);
       tma_load_4d(sq + kHalf, &tm_q, q_full, 64, q0, head, seq, pol_q);

@@ -66,8 +66,8 @@ template <int MODE, int MAXC>
 __global__ void __launch_bounds__(kRowThreads)
     ln_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
               const void* pb, float eps, bf16* __restrict__ y, int ldy) {
-  griddep_launch_dependents();  // the next kernel may start its own pre-wait work
   griddep_wait();
+  griddep_launch_dependents();
   __shared__ float red[4];
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
@@ -132,8 +132,8 @@ template <int MODE, int MAXC>
 __global__ void __launch_bounds__(kRowThreads, 12)
     ln_stream_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
                      const void* pb, float eps, bf16* __restrict__ y, int ldy) {
-  griddep_launch_dependents();  // the next kernel may start its own pre-wait work
   griddep_wait();
+  griddep_launch_dependents();
   __shared__ float red[4];
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
@@ -203,8 +203,8 @@ template <int MODE>
 __global__ void __launch_bounds__(256)
     ln_wide_kernel(const bf16* __restrict__ x, int ldx, int rows, int cols, const void* pa,
                    const void* pb, float eps, bf16* __restrict__ y, int ldy) {
-  griddep_launch_dependents();  // the next kernel may start its own pre-wait work
   griddep_wait();
+  griddep_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -264,8 +264,8 @@ __device__ __forceinline__ float rope_theta(const QkvScatter& a, int dim, int po
 // weights) in registers. MAXC = 0: generic loop.
 template <int MAXC>
 __global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const __grid_constant__ QkvScatter a) {
-  griddep_launch_dependents();  // the next kernel may start its own pre-wait work
   griddep_wait();
+  griddep_launch_dependents();
   __shared__ float red[3][4];
   const int row = blockIdx.x;
   const int which = threadIdx.y;

@@ -164,8 +164,9 @@ std::vector<std::pair<std::string, int64_t>> tensor_specs(const Geometry& g) {
       s.push_back({p + ".ca.kn.weight", H});
       s.push_back({p + ".ca_norm.weight", W});
       s.push_back({p + ".ca_norm.bias", W});
-      s.push_back({p + ".ffn.in.weight", F * W});
-      s.push_back({p + ".ffn.in.bias", F});
+      const int64_t fin = g.ffn_kind == 1 ? 2 : 1;  // SiLU-gated: [gate; up] rows
+      s.push_back({p + ".ffn.in.weight", fin * F * W});
+      s.push_back({p + ".ffn.in.bias", fin * F});
       s.push_back({p + ".ffn.out.weight", W * F});
       s.push_back({p + ".ffn.out.bias", W});
       s.push_back({p + ".mod", 6 * W});
@@ -254,6 +255,14 @@ bool MotEngine::init(const EngineOptions& opt, std::string* err) {
       g.real_state_dim > g.action_dim || g.embodiment_id >= g.num_embodiments) {
     *err = "unsupported geometry: widths must be multiples of 128 (text_dim, 4*vae_z of 64), "
            "head_dim 128, action_dim a multiple of 8 <= 128";
+    return false;
+  }
+  if (opt.block && (g.layers != 1 || g.steps != 1 || opt.max_batch != 1 || opt.prompt_cache)) {
+    *err = "block engines need layers == 1, steps == 1, max_batch == 1 and no prompt cache";
+    return false;
+  }
+  if ((g.ffn_kind != 0 && g.ffn_kind != 1) || (g.norm_kind != 0 && g.norm_kind != 1)) {
+    *err = "ffn_kind and norm_kind must be 0 or 1";
     return false;
   }
   flow_schedule(g.steps, g.flow_shift, &timesteps_, &sigmas_);
@@ -571,17 +580,19 @@ bool MotEngine::alloc_buffers(std::string* err) {
   gemm_ws_floats_ = static_cast<size_t>(sms_) * 128 * 256;
   AL(gemm_ws_[0], float, gemm_ws_floats_);
   AL(gemm_ws_[1], float, gemm_ws_floats_);
-  // Persistent denoise step (batches of up to 128 tokens).
+  if (opt_.block) {
+    AL(blk_in_, float, V * H + (1 + T) * E + Nt * H + Nt * E);
+    AL(blk_out_, float, V * H + (1 + T) * E);
+  }
 #undef AL
   // constants: timestep frequencies (row 0: t = 0 for the prefix, rows 1..S the
   // schedule), dt, RoPE inverse frequencies, visual positions, table pointers.
   std::vector<float> freq((1 + S) * 256);
   timestep_embedding(0.0f, 256, freq.data());
   for (size_t s = 0; s < S; ++s) timestep_embedding(timesteps_[s], 256, freq.data() + (1 + s) * 256);
-  float* freq_f32 = nullptr;
-  if (!(freq_f32 = dalloc<float>(freq.size(), err))) return false;
-  CK(cudaMemcpyAsync(freq_f32, freq.data(), freq.size() * 4, cudaMemcpyHostToDevice, stream_));
-  launch_f32_to_bf16(freq_f32, freq_bf_, static_cast<long long>(freq.size()), stream_);
+  if (!(freq_f32_ = dalloc<float>(freq.size(), err))) return false;
+  CK(cudaMemcpyAsync(freq_f32_, freq.data(), freq.size() * 4, cudaMemcpyHostToDevice, stream_));
+  launch_f32_to_bf16(freq_f32_, freq_bf_, static_cast<long long>(freq.size()), stream_);
   std::vector<float> dt(S);
   for (size_t s = 0; s < S; ++s) dt[s] = sigmas_[s + 1] - sigmas_[s];
   CK(cudaMemcpyAsync(dt_, dt.data(), S * 4, cudaMemcpyHostToDevice, stream_));
@@ -730,6 +741,8 @@ bool MotEngine::build(int b, std::string* err) {
     const long long prL = static_cast<long long>(heads) * Nt * 128;
     const long long prB = prL * L;
     const float eps = g.norm_eps;
+    const bool rms = g.norm_kind == 1;   // config-1 variant: RMSNorm inside AdaLN
+    const bool block = opt_.block;       // config 1: one layer over given hidden states
     bool ok = true;
     std::string e2;
     auto G = [&](Program& p, const bf16* x, int ldx, int m, const std::string& wn, int n, int k,
@@ -738,6 +751,21 @@ bool MotEngine::build(int b, std::string* err) {
       if (ok && !gemm(p, x, ldx, m, wn, n, k, epi, bias, gate, resid, ldr, out, ldo, &e2)) ok = false;
     };
     auto K = [](Program& p, Launch f) { p.add(std::move(f), OP_ELEMENTWISE); };
+    // FFN up projection: GELU(tanh) (the reference), or the config-1 SiLU-gated
+    // form silu(x Wg + bg) * (x Wu + bu) over ffn.in's [gate; up] rows.
+    auto ffn_in = [&](Program& p, const bf16* x, int ldx, int m, const std::string& pfx, int F,
+                      int W, bf16* out) {
+      if (g.ffn_kind == 0) {
+        G(p, x, ldx, m, pfx + ".ffn.in", F, W, EPI_BIAS_GELU, true, nullptr, nullptr, 0, out, F);
+        return;
+      }
+      if (ok && !gemm(p, x, ldx, m, pfx + ".ffn.in", F, W, EPI_BIAS_SILU, true, nullptr, nullptr,
+                      0, out, F, &e2, 2 * F, 0))
+        ok = false;
+      if (ok && !gemm(p, x, ldx, m, pfx + ".ffn.in", F, W, EPI_MUL, true, nullptr, out, F, out, F,
+                      &e2, 2 * F, F))
+        ok = false;
+    };
     // Lane hand-offs: the side stream waits for everything the main stream has
     // issued so far (fork), or the main stream for the side stream (join).
     auto fork_side = [&](Program& p) {
@@ -780,6 +808,16 @@ bool MotEngine::build(int b, std::string* err) {
     };
     auto ln_mod = [&](Program& p, const bf16* x, int rows, int cols, const float* scale,
                       const float* shift, bf16* y) {
+      p.add([=](cudaStream_t s) {
+        if (rms)
+          launch_rms_modulate(x, cols, rows, cols, scale, shift, eps, y, cols, s);
+        else
+          launch_ln_modulate(x, cols, rows, cols, scale, shift, eps, y, cols, s);
+        return cudaGetLastError();
+      }, OP_LAYERNORM, 1, 4.0 * rows * double(cols) + 8.0 * cols);
+    };
+    auto p_ln_final = [&](Program& p, const bf16* x, int rows, int cols, const float* scale,
+                          const float* shift, bf16* y) {
       p.add([=](cudaStream_t s) {
         launch_ln_modulate(x, cols, rows, cols, scale, shift, eps, y, cols, s);
         return cudaGetLastError();
@@ -862,14 +900,30 @@ bool MotEngine::build(int b, std::string* err) {
 
     // ---------------- prompt projection (cache.cpp:53-137 + build_condition text)
     Program& pp = plan->prog[0];
-    K(pp, [=](cudaStream_t s) {
-      launch_f32_to_bf16(in_prompt_, prompt_bf_, static_cast<long long>(b) * Nt * D, s);
-      return cudaGetLastError();
-    });
-    G(pp, prompt_bf_, D, b * Nt, "gwp.acond.text.0", E, D, EPI_BIAS_GELU_R, true, nullptr, nullptr, 0, text_tmp_, E);
-    G(pp, text_tmp_, E, b * Nt, "gwp.acond.text.1", E, E, EPI_BIAS, true, nullptr, nullptr, 0, text_a_, E);
-    G(pp, prompt_bf_, D, b * Nt, "gwp.cond.text.0", H, D, EPI_BIAS_GELU_R, true, nullptr, nullptr, 0, text_tmp_, H);
-    G(pp, text_tmp_, H, b * Nt, "gwp.cond.text.1", H, H, EPI_BIAS, true, nullptr, nullptr, 0, text_v_, H);
+    // Block engines: [xv | xa | tv | ta] F32 in blk_in_.
+    const float* blk_xv = blk_in_;
+    const float* blk_xa = blk_in_ ? blk_in_ + static_cast<size_t>(V) * H : nullptr;
+    const float* blk_tv = blk_xa ? blk_xa + static_cast<size_t>(1 + T) * E : nullptr;
+    const float* blk_ta = blk_tv ? blk_tv + static_cast<size_t>(Nt) * H : nullptr;
+    if (block) {
+      // the experts' text hidden states are the inputs (no text embedders)
+      K(pp, [=](cudaStream_t s) {
+        launch_f32_to_bf16(blk_tv, text_v_, static_cast<long long>(Nt) * H, s);
+        launch_f32_to_bf16(blk_ta, text_a_, static_cast<long long>(Nt) * E, s);
+        return cudaGetLastError();
+      });
+      pp.ops.back().launches = 2;
+      pp.kernels += 1;
+    } else {
+      K(pp, [=](cudaStream_t s) {
+        launch_f32_to_bf16(in_prompt_, prompt_bf_, static_cast<long long>(b) * Nt * D, s);
+        return cudaGetLastError();
+      });
+      G(pp, prompt_bf_, D, b * Nt, "gwp.acond.text.0", E, D, EPI_BIAS_GELU_R, true, nullptr, nullptr, 0, text_tmp_, E);
+      G(pp, text_tmp_, E, b * Nt, "gwp.acond.text.1", E, E, EPI_BIAS, true, nullptr, nullptr, 0, text_a_, E);
+      G(pp, prompt_bf_, D, b * Nt, "gwp.cond.text.0", H, D, EPI_BIAS_GELU_R, true, nullptr, nullptr, 0, text_tmp_, H);
+      G(pp, text_tmp_, H, b * Nt, "gwp.cond.text.1", H, H, EPI_BIAS, true, nullptr, nullptr, 0, text_v_, H);
+    }
     // An expert's ca.k / ca.vproj weights of all layers are one re-tiled
     // [L * 2H][tw] matrix (arena order, load_weights): the projection of the
     // prompt into every layer's K | V runs as one GEMM per chunk of
@@ -946,6 +1000,17 @@ bool MotEngine::build(int b, std::string* err) {
 
     // ---------------- prefix (cache.cpp:139-485)
     Program& mp = plan->prog[1];
+    if (block) {
+      // state token (row 0 of xa), action tokens (rows 1..T) and visual tokens
+      K(mp, [=](cudaStream_t s) {
+        launch_f32_to_bf16(blk_xa, hs_, static_cast<long long>(E), s);
+        launch_f32_to_bf16(blk_xa + E, ha_, static_cast<long long>(T) * E, s);
+        launch_f32_to_bf16(blk_xv, hv_, static_cast<long long>(V) * H, s);
+        return cudaGetLastError();
+      });
+      mp.ops.back().launches = 3;
+      mp.kernels += 2;
+    } else {
     K(mp, [=](cudaStream_t s) {
       launch_f32_to_bf16(in_state_, state_bf_, static_cast<long long>(b) * A, s);
       launch_f32_to_bf16(in_noise_, action_bf_, static_cast<long long>(b) * T * A, s);
@@ -967,6 +1032,7 @@ bool MotEngine::build(int b, std::string* err) {
       return cudaGetLastError();
     });
     G(mp, cols_, 4 * C, b * V, "gwp.patch", H, 4 * C, EPI_F32_BIAS, true, nullptr, nullptr, 0, hv_, H);
+    }  // not block
     // conditioning MLPs: acond at t = 0 and every schedule timestep, cond at t = 0.
     G(mp, freq_bf_, 256, 1 + S, "gwp.acond.time.0", E, 256, EPI_BIAS_SILU, true, nullptr, nullptr, 0, ct1_, E);
     G(mp, ct1_, E, 1 + S, "gwp.acond.time.1", E, E, EPI_BIAS, true, nullptr, nullptr, 0, temb_a_, E);
@@ -1045,7 +1111,7 @@ bool MotEngine::build(int b, std::string* err) {
       G(mp, nrm_, H, b * V, vp + ".sa.qkv", 3 * H, H, EPI_BIAS, true, nullptr, nullptr, 0, qkv_, 3 * H);
       scatter_part(1);
       join_side(mp);
-      if (l + 1 == L) break;  // the last layer's outputs feed no cached K/V
+      if (l + 1 == L && !block) break;  // the last layer's outputs feed no cached K/V
       AttnArgs at{};
       at.q = qbuf_;
       at.q_seq_stride = static_cast<long long>(heads) * P * 128;
@@ -1090,7 +1156,7 @@ bool MotEngine::build(int b, std::string* err) {
       attend(mp, cx);
       G(mp, catt_, H, b * V, vp + ".ca.o", H, H, EPI_RES, true, nullptr, hv_, H, hv_, H);
       ln_mod(mp, hv_, b * V, H, cv + 4 * H, cv + 3 * H, nrm_);
-      G(mp, nrm_, H, b * V, vp + ".ffn.in", Fv, H, EPI_BIAS_GELU, true, nullptr, nullptr, 0, ffn_, Fv);
+      ffn_in(mp, nrm_, H, b * V, vp, Fv, H, ffn_);
       G(mp, ffn_, Fv, b * V, vp + ".ffn.out", H, Fv, EPI_GATED_RES, true, cv + 5 * H, hv_, H, hv_, H);
       mp.lane = 1;
       G(mp, att_s_, H, b, ap + ".sa.o", E, H, EPI_GATED_RES, true, ca + 2 * E, hs_, E, hs_, E);
@@ -1109,10 +1175,11 @@ bool MotEngine::build(int b, std::string* err) {
       attend(mp, cs);
       G(mp, catt_s_, H, b, ap + ".ca.o", E, H, EPI_RES, true, nullptr, hs_, E, hs_, E);
       ln_mod(mp, hs_, b, E, ca + 4 * E, ca + 3 * E, nrm_s_);
-      G(mp, nrm_s_, E, b, ap + ".ffn.in", Fa, E, EPI_BIAS_GELU, true, nullptr, nullptr, 0, ffn_s_, Fa);
+      ffn_in(mp, nrm_s_, E, b, ap, Fa, E, ffn_s_);
       G(mp, ffn_s_, Fa, b, ap + ".ffn.out", E, Fa, EPI_GATED_RES, true, ca + 5 * E, hs_, E, hs_, E);
       mp.lane = 0;
     }
+    if (block) join_side(mp);  // the state token's last layer ran on the side lane
     // ---------------- denoise (mot.cpp:358-496, unrolled over the schedule)
     Program& dp = plan->prog[2];
     const bf16* ain_w = W("gwp.action.in.weight", static_cast<int64_t>(g.num_embodiments) * A * 128);
@@ -1121,11 +1188,13 @@ bool MotEngine::build(int b, std::string* err) {
     const bf16* dout_b = W("gwp.decode.out.bias", static_cast<int64_t>(g.num_embodiments) * A);
     for (int s = 0; s < S && ok; ++s) {
       const int M = b * T;
-      small(dp, action_bf_, M, A, ain_w ? ain_w + static_cast<size_t>(emb) * A * 128 : nullptr, 1, 128,
-            ain_b ? ain_b + emb * 128 : nullptr, 128, ACT_GELU_ERF, e1_);
-      small(dp, e1_, M, 128, W("gwp.action.mid.weight", 128 * 128), 128, 1,
-            W("gwp.action.mid.bias", 128), 128, ACT_GELU_ERF, e2_);
-      G(dp, e2_, 128, M, "gwp.action.out", E, 128, EPI_BIAS, true, nullptr, nullptr, 0, ha_, E);
+      if (!block) {  // block engines take the action tokens' hidden states as input
+        small(dp, action_bf_, M, A, ain_w ? ain_w + static_cast<size_t>(emb) * A * 128 : nullptr, 1,
+              128, ain_b ? ain_b + emb * 128 : nullptr, 128, ACT_GELU_ERF, e1_);
+        small(dp, e1_, M, 128, W("gwp.action.mid.weight", 128 * 128), 128, 1,
+              W("gwp.action.mid.bias", 128), 128, ACT_GELU_ERF, e2_);
+        G(dp, e2_, 128, M, "gwp.action.out", E, 128, EPI_BIAS, true, nullptr, nullptr, 0, ha_, E);
+      }
       for (int l = 0; l < L && ok; ++l) {
         const std::string ap = "gwp.blk." + std::to_string(l) + ".a";
         const float* c = comb_steps_ + (static_cast<size_t>(s) * L + l) * 6 * E;
@@ -1196,11 +1265,13 @@ bool MotEngine::build(int b, std::string* err) {
         attend(dp, cx);
         G(dp, catt_, H, M, ap + ".ca.o", E, H, EPI_RES, true, nullptr, ha_, E, ha_, E);
         ln_mod(dp, ha_, M, E, c + 4 * E, c + 3 * E, nrm_);
-        G(dp, nrm_, E, M, ap + ".ffn.in", Fa, E, EPI_BIAS_GELU, true, nullptr, nullptr, 0, ffn_, Fa);
+        ffn_in(dp, nrm_, E, M, ap, Fa, E, ffn_);
         G(dp, ffn_, Fa, M, ap + ".ffn.out", E, Fa, EPI_GATED_RES, true, c + 5 * E, ha_, E, ha_, E);
       }
+      if (block) break;  // one layer, no decoder / Euler step
       const float* cf = comb_final_ + static_cast<size_t>(s) * 2 * E;
-      ln_mod(dp, ha_, M, E, cf + E, cf, nrm_);
+      // the final head's modulated norm is the reference's LayerNorm in every variant
+      p_ln_final(dp, ha_, M, E, cf + E, cf, nrm_);
       G(dp, nrm_, E, M, "gwp.decode.in", 128, E, EPI_BIAS_GELU_ERF, true, nullptr, nullptr, 0, d1_, 128);
       small(dp, d1_, M, 128, W("gwp.decode.mid.weight", 128 * 128), 128, 1,
             W("gwp.decode.mid.bias", 128), 128, ACT_GELU_ERF, d2_);
@@ -1213,10 +1284,23 @@ bool MotEngine::build(int b, std::string* err) {
         return cudaGetLastError();
       });
     }
-    K(dp, [=](cudaStream_t s) {
-      launch_bf16_to_f32(action_bf_, d_out_, static_cast<long long>(b) * T * A, s);
-      return cudaGetLastError();
-    });
+    if (block) {
+      float* ov = blk_out_;
+      float* oa = blk_out_ ? blk_out_ + static_cast<size_t>(V) * H : nullptr;
+      K(dp, [=](cudaStream_t s) {
+        launch_bf16_to_f32(hv_, ov, static_cast<long long>(V) * H, s);
+        launch_bf16_to_f32(hs_, oa, static_cast<long long>(E), s);
+        launch_bf16_to_f32(ha_, oa + E, static_cast<long long>(T) * E, s);
+        return cudaGetLastError();
+      });
+      dp.ops.back().launches = 3;
+      dp.kernels += 2;
+    } else {
+      K(dp, [=](cudaStream_t s) {
+        launch_bf16_to_f32(action_bf_, d_out_, static_cast<long long>(b) * T * A, s);
+        return cudaGetLastError();
+      });
+    }
     if (!ok) {
       if (e2 == "__rebuild__") continue;  // scratch grew: rebuild with the new pointers
       *err = e2;
@@ -1291,6 +1375,10 @@ int MotEngine::kernels_per_chunk(int batch, bool with_prompt) {
 }
 
 bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
+  if (opt_.block) {
+    *err = "a block engine runs wam_b200_block_forward only (no action-chunk requests)";
+    return false;
+  }
   const Geometry& g = g_;
   if (!ok_) {
     *err = "engine is not initialised";
@@ -1537,6 +1625,52 @@ bool MotEngine::fetch(const RequestView* reqs, int batch, float* out, std::strin
   for (int i = 0; i < batch; ++i)
     postprocess_action(h_out_ + static_cast<size_t>(i) * T * A, T, A, R, aq01_.data(), aq99_.data(),
                        reqs[i].state, out + static_cast<size_t>(i) * T * R);
+  return true;
+}
+
+bool MotEngine::block_forward(const float* xv, const float* xa, const float* tv, const float* ta,
+                              float t, float* ov, float* oa, float* device_ms, std::string* err) {
+  if (!opt_.block || !blk_in_) {
+    *err = "block_forward needs an engine created for block runs";
+    return false;
+  }
+  if (!xv || !xa || !tv || !ta || !ov || !oa || !std::isfinite(t) || t < 0.0f) {
+    *err = "block_forward: inputs, outputs and a finite timestep >= 0 are required";
+    return false;
+  }
+  const Geometry& g = g_;
+  const size_t V = g.visual(), H = g.hidden, E = g.action_hidden, T = g.action_chunk;
+  const size_t Nt = g.prompt_tokens;
+  const size_t nxv = V * H, nxa = (1 + T) * E, ntv = Nt * H, nta = Nt * E;
+  CK(cudaMemcpyAsync(blk_in_, xv, nxv * 4, cudaMemcpyHostToDevice, stream_));
+  CK(cudaMemcpyAsync(blk_in_ + nxv, xa, nxa * 4, cudaMemcpyHostToDevice, stream_));
+  CK(cudaMemcpyAsync(blk_in_ + nxv + nxa, tv, ntv * 4, cudaMemcpyHostToDevice, stream_));
+  CK(cudaMemcpyAsync(blk_in_ + nxv + nxa + ntv, ta, nta * 4, cudaMemcpyHostToDevice, stream_));
+  // Row 1 of the timestep frequencies conditions the action tokens (row 0,
+  // t = 0, the state and visual tokens).
+  std::vector<float> f(256);
+  timestep_embedding(t, 256, f.data());
+  CK(cudaMemcpyAsync(freq_f32_ + 256, f.data(), 256 * 4, cudaMemcpyHostToDevice, stream_));
+  launch_f32_to_bf16(freq_f32_ + 256, freq_bf_ + 256, 256, stream_);
+  CK(cudaGetLastError());
+  staged_batch_ = 1;
+  if (!run(1, err)) return false;
+  CK(cudaMemcpyAsync(ov, blk_out_, nxv * 4, cudaMemcpyDeviceToHost, stream_));
+  CK(cudaMemcpyAsync(oa, blk_out_ + nxv, nxa * 4, cudaMemcpyDeviceToHost, stream_));
+  unsigned code = 0;
+  CK(cudaMemcpyAsync(&code, err_word_, 4, cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  if (code != 0) {
+    cudaMemsetAsync(err_word_, 0, 4, stream_);
+    cudaStreamSynchronize(stream_);
+    *err = "device pipeline wait timed out (code " + std::to_string(code) + ")";
+    return false;
+  }
+  if (device_ms) {
+    float a = 0.0f, b = 0.0f, c = 0.0f;
+    last_phase_ms(&a, &b, &c);
+    *device_ms = a + b + c;
+  }
   return true;
 }
 

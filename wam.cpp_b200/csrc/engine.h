@@ -26,6 +26,10 @@ struct Geometry {
   int grid_h = 32, grid_w = 24, vae_z = 48;
   int action_chunk = 48, steps = 10, prompt_tokens = 64, text_dim = 4096;
   float norm_eps = 1e-6f, flow_shift = 5.0f;
+  // Config-1 block variants (BASELINE's literal statement; the reference's
+  // MoT uses 0 / 0): ffn_kind 1 = SiLU-gated FFN (ffn.in holds [gate; up]
+  // rows, 2F x W), norm_kind 1 = RMSNorm inside the AdaLN modulated norms.
+  int ffn_kind = 0, norm_kind = 0;
   int visual() const { return grid_h * grid_w; }
   int prefix() const { return 1 + visual(); }
 };
@@ -40,6 +44,9 @@ struct EngineOptions {
   bool graphs = true;
   bool prompt_cache = true;
   int weight_format = 0;  // 0 BF16, 1 Q8_0 linear weights
+  // Config 1: the engine runs one MoT layer over given hidden states
+  // (block_forward) instead of action chunks; needs layers == 1, max_batch == 1.
+  bool block = false;
 };
 
 struct RequestView {
@@ -122,6 +129,13 @@ class MotEngine {
   // de-normalises them: out [batch][T][real_action_dim].
   bool fetch(const RequestView* reqs, int batch, float* out, std::string* err);
   bool predict(const RequestView* reqs, int batch, float* out, EngineStats* stats, std::string* err);
+  // Config 1 (block engines): one MoT layer, the reference's un-cached layer
+  // (run_mot_step, mot.cpp:1008-1067) over given hidden states: xv [V][H]
+  // visual tokens, xa [1 + T][E] state token then action tokens, tv [Nt][H] /
+  // ta [Nt][E] the experts' text hidden states, t the action tokens' timestep
+  // (state and visual tokens at 0). Outputs ov [V][H], oa [1 + T][E] (F32).
+  bool block_forward(const float* xv, const float* xa, const float* tv, const float* ta, float t,
+                     float* ov, float* oa, float* device_ms, std::string* err);
   void reset();
   int kernels_per_chunk(int batch, bool with_prompt);
   // Runs one chunk eagerly with CUDA events around every op (staged inputs).
@@ -205,6 +219,9 @@ class MotEngine {
   float *in_state_ = nullptr, *in_latent_ = nullptr, *in_prompt_ = nullptr, *in_noise_ = nullptr;
   float *h_state_ = nullptr, *h_latent_ = nullptr, *h_prompt_ = nullptr, *h_noise_ = nullptr;
   float *h_out_ = nullptr, *d_out_ = nullptr;
+  // block engines: F32 inputs [xv | xa | tv | ta] and outputs [ov | oa], the
+  // F32 timestep-frequency rows (row 1 is rewritten per block call)
+  float *blk_in_ = nullptr, *blk_out_ = nullptr, *freq_f32_ = nullptr;
   bf16 *prompt_bf_ = nullptr, *state_bf_ = nullptr, *action_bf_ = nullptr;
   bf16 *text_tmp_ = nullptr, *text_a_ = nullptr, *text_v_ = nullptr, *ckv_ = nullptr;
   bf16 *cols_ = nullptr, *hv_ = nullptr, *hs_ = nullptr, *ha_ = nullptr;

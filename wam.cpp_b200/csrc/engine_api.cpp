@@ -113,6 +113,14 @@ WAM_B200_API int wam_b200_create(const wam_b200_options* o, wam_b200_engine** ou
   eo.weight_format = has_format ? o->weight_format : 0;
   if (eo.weight_format != 0 && eo.weight_format != 1)
     return fail(st, WAM_B200_INVALID_ARGUMENT, "weight_format must be 0 (BF16) or 1 (Q8_0)");
+  if (o->struct_size >= offsetof(wam_b200_options, block_mode) + sizeof(int)) {
+    eo.synthetic.ffn_kind = o->ffn_kind;
+    eo.synthetic.norm_kind = o->norm_kind;
+    eo.block = o->block_mode != 0;
+    if ((o->ffn_kind || o->norm_kind || eo.block) && o->artifact_path)
+      return fail(st, WAM_B200_INVALID_ARGUMENT,
+                  "ffn_kind / norm_kind / block_mode apply to synthetic weights only");
+  }
   std::string err;
   auto e = wamb::MotEngine::create(eo, &err);
   if (!e) {
@@ -242,6 +250,25 @@ WAM_B200_API int wam_b200_profile_graph(wam_b200_engine* e, int batch, int phase
   out->bytes = bytes;
   out->flops = flops;
   out->launches = launches;
+  return ok(st);
+}
+
+WAM_B200_API int wam_b200_block_forward(wam_b200_engine* e, const wam_b200_block_inputs* in,
+                                        float* visual_out, size_t visual_out_n, float* action_out,
+                                        size_t action_out_n, float* device_ms,
+                                        wam_b200_status* st) {
+  if (!e || !in) return fail(st, WAM_B200_INVALID_ARGUMENT, "engine and inputs are required");
+  const wamb::Geometry& g = e->impl->geometry();
+  const size_t nv = static_cast<size_t>(g.visual()) * g.hidden;
+  const size_t na = static_cast<size_t>(1 + g.action_chunk) * g.action_hidden;
+  if (visual_out_n < nv || action_out_n < na)
+    return fail(st, WAM_B200_INVALID_ARGUMENT,
+                "block outputs need [V][H] and [1 + T][E] floats (" + std::to_string(nv) + ", " +
+                    std::to_string(na) + ")");
+  std::string err;
+  if (!e->impl->block_forward(in->visual, in->action, in->text_visual, in->text_action,
+                              in->timestep, visual_out, action_out, device_ms, &err))
+    return fail(st, code_of(err), err);
   return ok(st);
 }
 

@@ -895,6 +895,158 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------ streaming GEMM
+// Token tiles of <= 64 rows (the batch-1 denoise step and the prefix state
+// token): every CTA owns NT = 32, 64 or 128 output features (a divisor of the
+// 256-row weight tile) over the whole K, so no CTA's partial sums ever leave
+// it. Each pipeline stage holds KB consecutive k-blocks of both operands,
+// fetched by one 3-D TMA box each: weights from the re-tiled layout viewed as
+// [N/256][K/64][256][64] (rows n0 % 256 .. + NT of tile n0 / 256, pre-swizzled,
+// copied verbatim) or a row-major [N][K] weight with the 128-byte swizzle;
+// tokens as [K/64][rows][64] with the 128-byte swizzle. UMMA M = 64 (token
+// rows in TMEM lanes 0-15 of each quadrant), N = NT, K = 16. The epilogue
+// applies the fused bias / activation / residual per row straight from TMEM.
+constexpr int kStreamBudget = 200 * 1024;
+
+int stream_stage_bytes(int a_rows, int nt, int kb) { return kb * (a_rows + nt) * kBK * 2; }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_stream_kernel(const __grid_constant__ CUtensorMap tm_w,
+                       const __grid_constant__ CUtensorMap tm_x,
+                       const __grid_constant__ GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int S = args.stages, NT = args.nt, KB = args.kb;
+  const uint32_t a_bytes = static_cast<uint32_t>(KB * args.a_rows * kBK * 2);
+  const uint32_t w_bytes = static_cast<uint32_t>(KB * NT * kBK * 2);
+  const uint32_t stage = a_bytes + w_bytes;
+  uint8_t* tail = smem + S * stage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* empty = full + S;
+  uint64_t* accum = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  float* bias_s = reinterpret_cast<float*>(tail + 256);
+  float* gate_s = bias_s + 128;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * NT;
+  const int rows = args.m < 64 ? args.m : 64;
+  const int nst = args.num_kb / KB;  // stages of work (num_kb % KB == 0)
+  const uint32_t tcols = NT < 32 ? 32 : NT;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tm_w);
+    prefetch_tensormap(&tm_x);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, tcols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  griddep_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_w = WAM_GEMM_WEIGHT_EVICT_FIRST ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_x = policy_evict_last();
+      const bool tiled = args.w_tiled != nullptr;
+      auto load_w = [&](int s, int j) {
+        uint8_t* dst = smem + s * stage + a_bytes;
+        if (tiled)
+          tma_load_4d(dst, &tm_w, &full[s], 0, n0 % kWN, j * KB, n0 / kWN, pol_w);
+        else
+          tma_load_3d(dst, &tm_w, &full[s], 0, n0, j * KB, pol_w);
+      };
+      const int pre = nst < S ? nst : S;
+      const int pre_w = pre < args.pre_w ? pre : args.pre_w;
+      for (int j = 0; j < pre_w; ++j) {
+        mbar_arrive_expect_tx(&full[j], stage);
+        load_w(j, j);
+      }
+      griddep_wait();  // tokens come from the preceding kernel
+      for (int j = 0; j < pre; ++j) {
+        if (j >= pre_w) mbar_arrive_expect_tx(&full[j], stage);
+        tma_load_3d(smem + j * stage, &tm_x, &full[j], 0, 0, j * KB, pol_x);
+        if (j >= pre_w) load_w(j, j);
+      }
+      for (int j = pre; j < nst; ++j) {
+        const int s = j % S;
+        if (!mbar_wait(&empty[s], ((j / S) & 1) ^ 1)) {
+          atomicCAS(args.error, 0u, static_cast<unsigned>(kErrProducerTimeout));
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], stage);
+        load_w(s, j);
+        tma_load_3d(smem + s * stage, &tm_x, &full[s], 0, 0, j * KB, pol_x);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(64, NT);
+      for (int j = 0; j < nst; ++j) {
+        const int s = j % S;
+        if (!mbar_wait(&full[s], (j / S) & 1)) {
+          atomicCAS(args.error, 0u, static_cast<unsigned>(kErrMmaTimeout));
+          break;
+        }
+        tc_fence_after();
+        for (int b = 0; b < KB; ++b) {
+          const uint64_t da = sw128_kmajor_desc(smem_u32(smem + s * stage + b * args.a_rows * 128));
+          const uint64_t db = sw128_kmajor_desc(smem_u32(smem + s * stage + a_bytes + b * NT * 128));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_bf16_ss(tmem_base, da + 2 * k, db + 2 * k, idesc, (j | b | k) != 0 ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accum);
+    }
+  } else if (warp < 6) {
+    griddep_wait();  // residual / gate / outputs are touched only after the preceding kernel
+    const int et = threadIdx.x - 64;
+    for (int jj = et; jj < NT; jj += 128) {
+      const int n = n0 + jj;
+      bias_s[jj] = (args.bias && n < args.n) ? __bfloat162float(args.bias[n]) : 0.0f;
+      gate_s[jj] = (args.gate && n < args.n) ? args.gate[n] : 0.0f;
+    }
+    named_bar_sync(1, 128);
+    const bool ok = mbar_wait(accum, 0);
+    if (!ok) atomicCAS(args.error, 0u, static_cast<unsigned>(kErrEpilogueTimeout));
+    tc_fence_after();
+    const int q = warp & 3;
+    const int row = q * 16 + (lane & 15);  // M = 64: rows 16q.. in lanes 32q..32q+15
+    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    if (q * 16 < rows) {
+#pragma unroll 1
+      for (int c = 0; c < NT; c += 16) {
+        uint32_t r[16];
+        tmem_ld_x16(taddr + c, r);
+        tmem_ld_wait();
+        if (ok && lane < 16 && row < rows)
+          epi_run<16>(args, row, n0 + c, reinterpret_cast<const float*>(r), bias_s + c, gate_s + c);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, tcols);
+  }
+}
+
 // ------------------------------------------------------------ CTA-pair GEMM
 // Tensor-bound GEMMs (>= 256 token rows: the prefix, prompt and batched
 // GEMMs) run on CTA pairs with tcgen05.mma.cta_group::2: one UMMA covers 256
@@ -1241,6 +1393,18 @@ bool g_pair = [] {
   const char* v = std::getenv("WAM_B200_GEMM_PAIR");
   return v && *v == '1';
 }();
+// Streaming GEMM (no split-K) for token tiles of <= 64 rows and N >= 1536
+// (default); WAM_B200_GEMM_STREAM=0 keeps such GEMMs on the split-K kernel,
+// WAM_B200_GEMM_STREAM_NT=32|64|128 fixes the features per CTA.
+bool g_stream = [] {
+  const char* v = std::getenv("WAM_B200_GEMM_STREAM");
+  return !(v && *v == '0');
+}();
+int g_stream_nt = [] {
+  const char* v = std::getenv("WAM_B200_GEMM_STREAM_NT");
+  const int n = v ? std::atoi(v) : 0;
+  return n == 32 || n == 64 || n == 128 ? n : 0;
+}();
 // Stages whose weight copies a GEMM CTA issues before waiting for the
 // preceding kernel (WAM_B200_GEMM_PREW, default 2).
 int g_pre_w = [] {
@@ -1337,6 +1501,106 @@ bool encode_tiled_rows(CUtensorMap* map, const void* base, long long rows) {
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [N/256][K/64][256][64] view of re-tiled weights (pre-swizzled, copied
+// verbatim): box = 64 x nt rows x kb k-blocks of one 256-row tile.
+bool encode_tiled_stream(CUtensorMap* map, const void* base, int n, int k, int nt, int kb) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kBK), static_cast<cuuint64_t>(kWN),
+                              static_cast<cuuint64_t>(k / kBK), static_cast<cuuint64_t>(n / kWN)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(kBK) * 2,
+                                 static_cast<cuuint64_t>(kWN) * kBK * 2,
+                                 static_cast<cuuint64_t>(k / kBK) * kWN * kBK * 2};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(nt),
+                             static_cast<cuuint32_t>(kb), 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Row-major [rows][ld] BF16 viewed as [cols / 64][rows][64] (128-byte swizzle):
+// box = 64 x box_rows x kb k-blocks.
+bool encode_kblocks(CUtensorMap* map, const void* base, int cols, int rows, int ld, int box_rows,
+                    int kb) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kBK), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(cols / kBK)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(kBK) * 2};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows),
+                             static_cast<cuuint32_t>(kb)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Streaming plan: NT = 128 features per CTA when that still gives >= 96 CTAs
+// (enough weight streams to fill HBM) and K <= 4096 (every CTA reads all of the
+// token rows from L2); KB k-blocks per stage so a stage moves >= 24 KB, as many
+// stages as the budget holds (>= 2). Measured on B200 (op cases, µs, streaming
+// vs split-K): 48x14336x3072 19.7 vs 21.7 (NT 128, used); 48x3072x3072 14.2 vs
+// 10.9 (NT 32), 48x9216x3072 18.7 vs 16.9 (NT 64), 48x3072x14336 49.7 vs 20.9
+// (NT 32): narrower tiles lose to split-K, so they are not planned.
+const char* plan_stream(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, int n, int k,
+                        int epilogue, const bf16* bias, const float* gate, const bf16* residual,
+                        int ldr, void* out, int ldo, const GemmScratch& scratch, int num_sms,
+                        bool w_tiled) {
+  (void)num_sms;
+  int nt = 128;
+  if (g_stream_nt > 0) {
+    if (n % g_stream_nt != 0) return "stream: not applicable";
+    nt = g_stream_nt;
+  } else if (n % 128 != 0 || n / 128 < 96 || k > 4096) {
+    return "stream: not applicable";
+  }
+  const int a_rows = a_rows_for(m);
+  const int nkb = k / kBK;
+  int kb = 1;
+  while (kb < 8 && stream_stage_bytes(a_rows, nt, kb) < 24 * 1024 && nkb % (kb * 2) == 0) kb *= 2;
+  int stages = kStreamBudget / stream_stage_bytes(a_rows, nt, kb);
+  if (stages > kMaxStages) stages = kMaxStages;
+  if (stages < 2 || nkb % kb != 0) return "stream: not applicable";
+  if (w_tiled) {
+    if (!encode_tiled_stream(&op->tm_w, w, n, k, nt, kb)) return "gemm: weight tensor map encode failed";
+  } else if (!encode_kblocks(&op->tm_w, w, k, n, k, nt, kb)) {
+    return "gemm: weight tensor map encode failed";
+  }
+  if (!encode_kblocks(&op->tm_x, x, k, m, ldx, a_rows, kb))
+    return "gemm: activation tensor map encode failed";
+  GemmArgs& a = op->args;
+  a.m = m;
+  a.n = n;
+  a.k = k;
+  a.num_kb = nkb;
+  a.splits = 1;
+  a.split_mode = SPLIT_CLUSTER;
+  a.a_rows = a_rows;
+  a.stages = stages;
+  a.pre_w = stages < g_pre_w ? stages : g_pre_w;
+  a.nt = nt;
+  a.kb = kb;
+  a.w_tiled = w_tiled ? w : nullptr;
+  a.w_q8 = nullptr;
+  a.tiles_m = 1;
+  a.tiles_n = n / nt;
+  a.epilogue = epilogue;
+  a.bias = bias;
+  a.gate = gate;
+  a.residual = residual;
+  a.ldr = ldr;
+  a.out = out;
+  a.ldo = ldo;
+  a.workspace = scratch.workspace;
+  a.counters = scratch.counters;
+  a.error = scratch.error;
+  op->stream = true;
+  op->grid = n / nt;
+  op->smem_bytes = stages * stream_stage_bytes(a_rows, nt, kb) + 1024 + kSmemTail;
+  return nullptr;
+}
+
 const char* plan_pair(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, int n, int k,
                       int epilogue, const bf16* bias, const float* gate, const bf16* residual,
                       int ldr, void* out, int ldo, const GemmScratch& scratch, int num_sms,
@@ -1423,6 +1687,11 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
                        scratch, num_sms, c, w_tiled);
     }
   }
+  if (g_stream && m <= 64 && !w_q8 && !pair && force_splits <= 0 && n % 32 == 0 && n >= 1536) {
+    const char* e = plan_stream(op, x, ldx, m, w, n, k, epilogue, bias, gate, residual, ldr, out,
+                                ldo, scratch, num_sms, w_tiled);
+    if (!e || std::strcmp(e, "stream: not applicable") != 0) return e;
+  }
   const int a_rows = a_rows_for(m);
   // The epilogue stages a [token][feature] tile (F32 rows of kPartLd floats at
   // most) in the pipeline stages' shared memory.
@@ -1502,6 +1771,9 @@ cudaError_t gemm_init(int device) {
   e = cudaFuncSetAttribute(gemm_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            pair_smem());
   if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(gemm_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kStreamBudget + 1024 + kSmemTail);
+  if (e != cudaSuccess) return e;
   int sms = 0;
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
     return e;
@@ -1556,6 +1828,7 @@ cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = na;
   if (op.pair) return cudaLaunchKernelEx(&cfg, gemm_tc_pair_kernel, op.tm_w, op.tm_x, op.args);
+  if (op.stream) return cudaLaunchKernelEx(&cfg, gemm_stream_kernel, op.tm_w, op.tm_x, op.args);
   if (op.persistent) return cudaLaunchKernelEx(&cfg, gemm_tc_persistent_kernel, op.tm_w, op.tm_x, op.args);
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, op.tm_w, op.tm_x, op.args);
 }

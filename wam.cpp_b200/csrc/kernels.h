@@ -46,6 +46,8 @@ struct GemmArgs {
   int a_rows;  // token rows loaded per tile (<= 128)
   int stages;  // pipeline stages (one weight + one token k-block each)
   int pre_w;   // stages whose weight copies start before the grid-dependency wait
+  int nt;      // stream kernel: output features per CTA (32, 64 or 128)
+  int kb;      // stream kernel: k-blocks of 64 per pipeline stage
   const bf16* w_tiled;  // weights re-tiled by launch_retile_weights, or null (tensor map)
   const uint8_t* w_q8;  // Q8_0 weight tiles (launch_q8_retile), or null
   int tiles_m, tiles_n;
@@ -76,6 +78,7 @@ struct GemmOp {
   int grid = 0;
   bool persistent = false;  // gemm_tc_persistent_kernel (tiles > SMs, no split-K)
   bool pair = false;        // gemm_tc_pair_kernel (>= 256 tokens, CTA pairs, cta_group::2)
+  bool stream = false;      // gemm_stream_kernel (<= 64 tokens, full K per CTA, no split-K)
   int cluster = 1;          // pair kernel: cluster size (2 x splits)
   int smem_bytes = 0;
 };
@@ -195,12 +198,6 @@ void launch_attention(const AttnArgs& a, cudaStream_t s);
 cudaError_t attention_tc_init();
 bool attention_tc_eligible(const AttnArgs& a);
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s);
-// tcgen05 attention for <= 64 query rows per (sequence, head) with key splits
-// merged inside a thread-block cluster (attention_dec.cu).
-cudaError_t attention_dec_init();
-bool attention_dec_eligible(const AttnArgs& a);
-int attention_dec_splits(const AttnArgs& a, int num_sms);
-cudaError_t launch_attention_dec(const AttnArgs& a, int num_sms, cudaStream_t s);
 
 // Workspace the split-KV merge of `a` needs (0 when it does not split).
 size_t attention_ws_floats(const AttnArgs& a);

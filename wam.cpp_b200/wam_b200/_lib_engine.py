@@ -22,7 +22,14 @@ class Options(C.Structure):
                 ("synthetic_geometry", Geometry), ("synthetic_seed", C.c_uint64),
                 ("synthetic_bias_scale", C.c_float), ("device_index", C.c_int),
                 ("max_batch", C.c_int), ("use_cuda_graphs", C.c_int), ("prompt_cache", C.c_int),
-                ("weight_format", C.c_int)]
+                ("weight_format", C.c_int), ("ffn_kind", C.c_int), ("norm_kind", C.c_int),
+                ("block_mode", C.c_int)]
+
+
+class BlockInputs(C.Structure):
+    _fields_ = [("visual", C.POINTER(C.c_float)), ("action", C.POINTER(C.c_float)),
+                ("text_visual", C.POINTER(C.c_float)), ("text_action", C.POINTER(C.c_float)),
+                ("timestep", C.c_float)]
 
 
 class Request(C.Structure):
@@ -68,3 +75,5 @@ def attach(lib, sig) -> None:
     sig(lib, "wam_b200_phase_ms", i32, [vp, f32p, f32p, f32p])
     sig(lib, "wam_b200_profile", i32, [vp, i32, C.POINTER(OpProfile), i32, st])
     sig(lib, "wam_b200_profile_graph", i32, [vp, i32, i32, i32, i32, C.POINTER(GraphProfile), st])
+    sig(lib, "wam_b200_block_forward", i32,
+        [vp, C.POINTER(BlockInputs), f32p, sz, f32p, sz, f32p, st])

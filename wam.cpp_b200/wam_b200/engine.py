@@ -15,8 +15,8 @@ from dataclasses import dataclass
 import numpy as np
 
 from ._lib import load
-from ._lib_engine import (GEOM_FIELDS, Geometry, GraphProfile, OpProfile, Options, Request, Stats,
-                          Status)
+from ._lib_engine import (GEOM_FIELDS, BlockInputs, Geometry, GraphProfile, OpProfile, Options,
+                          Request, Stats, Status)
 
 KINDS = ("gemm", "attention", "layernorm", "qkv_scatter", "small_linear", "elementwise", "sync")
 PHASES = ("prompt", "prefix", "denoise")
@@ -59,7 +59,11 @@ def _f32(a):
 class Engine:
     def __init__(self, geometry=None, seed: int = 0, artifact: str | None = None,
                  bias_scale: float = 0.0, device: int = 0, max_batch: int = 1,
-                 graphs: bool = True, prompt_cache: bool = True, weights: str = "bf16"):
+                 graphs: bool = True, prompt_cache: bool = True, weights: str = "bf16",
+                 ffn: str = "gelu", norm: str = "layernorm", block: bool = False):
+        """ffn ('gelu' | 'swiglu') and norm ('layernorm' | 'rmsnorm') select the
+        config-1 block variants (synthetic weights); block=True creates an engine
+        for block_forward (one layer over given hidden states)."""
         self.lib = load()
         o = Options()
         o.struct_size = C.sizeof(Options)
@@ -75,6 +79,11 @@ class Engine:
         if weights not in ("bf16", "q8_0"):
             raise ValueError("weights must be 'bf16' or 'q8_0'")
         o.weight_format = 1 if weights == "q8_0" else 0
+        if ffn not in ("gelu", "swiglu") or norm not in ("layernorm", "rmsnorm"):
+            raise ValueError("ffn must be 'gelu' or 'swiglu', norm 'layernorm' or 'rmsnorm'")
+        o.ffn_kind = 1 if ffn == "swiglu" else 0
+        o.norm_kind = 1 if norm == "rmsnorm" else 0
+        o.block_mode = 1 if block else 0
         h = C.c_void_p()
         st = Status()
         _raise(self.lib, self.lib.wam_b200_create(C.byref(o), C.byref(h), C.byref(st)), st,
@@ -188,6 +197,27 @@ class Engine:
                                              reps, C.byref(out), C.byref(st))
         _raise(self.lib, rc, st, "wam_b200_profile_graph")
         return {"ms": out.ms, "bytes": out.bytes, "flops": out.flops, "launches": out.launches}
+
+    def block_forward(self, t: float, xv, xa, tv, ta, with_time: bool = False):
+        """Config 1: one MoT layer over given hidden states (wam_b200_block_forward).
+        xv [V, H], xa [1 + T, E] (state row first), tv [Nt, H], ta [Nt, E] F32.
+        Returns (visual out [V, H], action stream out [1 + T, E]) and, with
+        with_time, the device time in ms."""
+        g = self.geometry
+        V, H, E, T = g["grid_h"] * g["grid_w"], g["hidden"], g["action_hidden"], g["action_chunk"]
+        arrs = [_f32(a) for a in (xv, xa, tv, ta)]
+        fp = C.POINTER(C.c_float)
+        inp = BlockInputs(arrs[0].ctypes.data_as(fp), arrs[1].ctypes.data_as(fp),
+                          arrs[2].ctypes.data_as(fp), arrs[3].ctypes.data_as(fp), t)
+        ov = np.zeros((V, H), np.float32)
+        oa = np.zeros((1 + T, E), np.float32)
+        ms = C.c_float(0.0)
+        st = Status()
+        rc = self.lib.wam_b200_block_forward(self.h, C.byref(inp), ov.ctypes.data_as(fp), ov.size,
+                                             oa.ctypes.data_as(fp), oa.size, C.byref(ms),
+                                             C.byref(st))
+        _raise(self.lib, rc, st, "wam_b200_block_forward")
+        return (ov, oa, ms.value) if with_time else (ov, oa)
 
     def reset(self):
         self.lib.wam_b200_reset(self.h)

@@ -12,7 +12,7 @@ import torch
 from ._lib import check, load
 
 (EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_GATED_RES, EPI_RES, EPI_F32_BIAS, EPI_F32_OUT,
- EPI_BIAS_GELU_R, EPI_BIAS_GELU_ERF) = range(9)
+ EPI_BIAS_GELU_R, EPI_BIAS_GELU_ERF, EPI_MUL) = range(10)
 
 
 def _ptr(t):

@@ -61,6 +61,9 @@ SMALL = Geometry(hidden=512, layers=3, heads=4, ffn=1024, action_hidden=384, act
 # and smoke geometries of the benched configuration (same kernels, split-K
 # plans, persistent GEMMs and attention splits as the full model).
 CONFIG2_L2 = Geometry(layers=2, steps=2)
+# one MoT block at config-2 widths (768 visual tokens, 512
+# text tokens as cross-attention keys, 48 action tokens + the state token).
+CONFIG1 = Geometry(layers=1, steps=1)
 CONFIG2_L1 = Geometry(layers=1, steps=2)
 # 144 visual tokens: the prefix attention (145 / 144 queries) runs as 128-query
 # tensor-core tiles.
@@ -92,6 +95,20 @@ class Request:
     prompt: np.ndarray  # [prompt_tokens, text_dim]
     noise: np.ndarray   # [T, A]
     extra: dict = field(default_factory=dict)
+
+
+def make_block_inputs(g: Geometry, seed: int) -> dict:
+    """Config-1 inputs, N(0, 1) F32: visual [V, H], action stream [1 + T, E]
+    (state token first), the experts' text hidden states [Nt, H] / [Nt, E]
+    (one draw used for both when E == H), and a timestep in [0, 1000)."""
+    r = np.random.Generator(np.random.PCG64(seed))
+    xv = r.standard_normal((g.visual_tokens, g.hidden), dtype=np.float32)
+    xa = r.standard_normal((1 + g.action_chunk, g.action_hidden), dtype=np.float32)
+    tv = r.standard_normal((g.prompt_tokens, g.hidden), dtype=np.float32)
+    ta = tv.copy() if g.action_hidden == g.hidden else r.standard_normal(
+        (g.prompt_tokens, g.action_hidden), dtype=np.float32)
+    t = float(r.uniform(0.0, 1000.0))
+    return {"xv": xv, "xa": xa, "tv": tv, "ta": ta, "t": t}
 
 
 def make_request(g: Geometry, seed: int) -> Request:
