@@ -402,6 +402,41 @@ WAM_B200_API int wam_b200_read_tensor(wam_b200_engine* engine, const char* name,
                                       int layer, float* out, size_t out_n,
                                       wam_b200_status* status);
 
+/* ---------------------------------------------------------------- vision
+ * Stage 1 of the vision front-end: compose three camera views onto the
+ * image_width x image_height canvas (view 0 top half, views 1 / 2 bottom left /
+ * right; each resized to cover its cell with a triangle filter and centre
+ * cropped), patchify 2x2 and map to [-1, 1]. Output [12][h/2][w/2] F32 on the
+ * device, packed channel (c * 2 + dx) * 2 + dy. Bit-identical to the reference's
+ * CPU compose_and_patchify (src/models/gwp05/engine/vae.cpp:1-134); replaces its
+ * CUDA preprocessor (src/models/gwp05/kernels/cuda_preprocess.h:6-14). */
+#define WAM_B200_PIXEL_U8 0         /* RGB, 3 bytes per pixel (PixelFormat::U8) */
+#define WAM_B200_PIXEL_F32_RGB_01 1 /* RGB, 3 floats per pixel in [0, 1] */
+typedef struct wam_b200_image { /* ImageView, engine/engine.h:84-89 */
+  const void* data;
+  int w;
+  int h;
+  int format;
+} wam_b200_image;
+typedef struct wam_b200_preprocessor wam_b200_preprocessor;
+
+/* gwp05_cuda_preprocessor_create / _destroy (cuda_preprocess.cu:139-148): device
+ * buffers for the three views on device_index, grown on demand. */
+WAM_B200_API int wam_b200_preprocessor_create(int device_index, wam_b200_preprocessor** out,
+                                              wam_b200_status* status);
+WAM_B200_API void wam_b200_preprocessor_destroy(wam_b200_preprocessor* preprocessor);
+/* gwp05_cuda_preprocess (cuda_preprocess.cu:150-198): host images (exactly 3,
+ * U8 or F32_RGB_01, w, h > 0), copied to the device on `stream` (NULL: the
+ * legacy default stream), composed into output_device; returns after the stream
+ * has finished. output_width / output_height must be positive and even. */
+WAM_B200_API int wam_b200_preprocess(wam_b200_preprocessor* preprocessor,
+                                     const wam_b200_image* images, int image_count,
+                                     int output_width, int output_height, float* output_device,
+                                     void* stream, wam_b200_status* status);
+/* The same kernel on views already on the device (asynchronous on `stream`). */
+WAM_B200_API int wam_b200_op_preprocess(const wam_b200_image* device_images, int output_width,
+                                        int output_height, float* output_device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -86,6 +86,10 @@ def lib():
                                                  C.c_char_p, C.c_int]
         l.oracle_block.restype = C.c_int
         l.oracle_block.argtypes = [C.c_void_p, C.c_int, C.c_float] + [f32p] * 6
+        i32p = C.POINTER(C.c_int)
+        l.oracle_compose_and_patchify.restype = C.c_int
+        l.oracle_compose_and_patchify.argtypes = [C.POINTER(C.c_void_p), i32p, i32p, i32p,
+                                                  C.c_int, C.c_int, f32p]
         _lib = l
     return _lib
 
@@ -103,6 +107,36 @@ def ref_lib():
     l.wamref_normalize_state.argtypes = [f32p, C.c_int, C.c_int, f32p, f32p, f32p]
     l.wamref_postprocess.argtypes = [f32p, C.c_int, C.c_int, C.c_int, f32p, f32p, f32p, C.c_int, f32p]
     return l
+
+
+REF_VISION_LIB = REF_LIB.parent / "libwamref_vision.so"
+
+
+def _views_args(views):
+    data = (C.c_void_p * 3)(*[v.ctypes.data for v in views])
+    ints = lambda xs: (C.c_int * 3)(*xs)  # noqa: E731
+    return (data, ints([v.shape[1] for v in views]), ints([v.shape[0] for v in views]),
+            ints([0 if v.dtype == np.uint8 else 1 for v in views]))
+
+
+def compose_and_patchify(views, out_w: int, out_h: int, reference: bool = False) -> np.ndarray:
+    """Vision stage 1 on three HWC RGB views (uint8, or float32 in [0, 1]):
+    [12][out_h/2][out_w/2] float32. reference=True runs the reference's own
+    compose_and_patchify (oracle/_ref/libwamref_vision.so, `make ref`)."""
+    views = [np.ascontiguousarray(v) for v in views]
+    out = np.zeros((12, out_h // 2, out_w // 2), np.float32)
+    d, w, h, f = _views_args(views)
+    if reference:
+        if not REF_VISION_LIB.exists():
+            raise FileNotFoundError(REF_VISION_LIB)
+        rl = C.CDLL(str(REF_VISION_LIB))
+        rl.wamref_compose_and_patchify.restype = C.c_int
+        rc = rl.wamref_compose_and_patchify(d, w, h, f, out_w, out_h, _fp(out), C.c_longlong(out.size))
+    else:
+        rc = lib().oracle_compose_and_patchify(d, w, h, f, out_w, out_h, _fp(out))
+    if rc != 0:
+        raise ValueError("compose_and_patchify rejected its inputs")
+    return out
 
 
 def _fp(a):

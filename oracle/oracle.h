@@ -99,6 +99,12 @@ void oracle_visual_positions(int gh, int gw, int32_t* t, int32_t* h, int32_t* w)
 /* Threads the oracle's parallel regions use. */
 int oracle_threads(void);
 
+/* Vision front-end stage 1 (vision.cpp): three views (format 0 U8 RGB, 1 F32
+ * RGB in [0, 1]) composed onto an out_w x out_h canvas, patchified 2x2 into
+ * out [12][out_h / 2][out_w / 2] in [-1, 1]. Returns non-zero on bad input. */
+int oracle_compose_and_patchify(const void* const* data, const int* w, const int* h,
+                                const int* format, int out_w, int out_h, float* out);
+
 #ifdef __cplusplus
 }
 #endif

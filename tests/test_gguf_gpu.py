@@ -8,46 +8,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 gguf = pytest.importorskip("gguf")
-from gguf import quants  # noqa: E402
-
-SEED = 20261201
-
-
-def write_artifact(path, g, q8: bool):
-    from oracle import synth
-
-    w = synth.make_weights(g, SEED, bias_scale=0.02)
-    wr = gguf.GGUFWriter(str(path), "gwp05")
-    wr.add_string("gwp05.architecture", "gwp05")
-    u32 = {"gwp05.hidden": g.hidden, "gwp05.n_layers": g.layers, "gwp05.n_heads": g.heads,
-           "gwp05.head_dim": 128, "gwp05.ffn_dim": g.ffn, "gwp05.action_hidden": g.action_hidden,
-           "gwp05.action_ffn_dim": g.action_ffn, "gwp05.action_dim": g.action_dim,
-           "gwp05.real_state_dim": g.real_state_dim, "gwp05.real_action_dim": g.real_action_dim,
-           "gwp05.num_embodiments": g.num_embodiments, "gwp05.embodiment_id": g.embodiment_id,
-           "gwp05.image_height": g.grid_h * 32, "gwp05.image_width": g.grid_w * 32,
-           "gwp05.action_chunk": g.action_chunk, "gwp05.inference_steps": g.steps,
-           "gwp05.t5_hidden": g.text_dim, "gwp05.vae_z_dim": g.vae_z,
-           "gwp05.prompt_tokens": g.prompt_tokens}
-    for k, v in u32.items():
-        wr.add_uint32(k, v)
-    wr.add_float32("gwp05.norm_eps", g.norm_eps)
-    wr.add_float32("gwp05.flow_shift", g.flow_shift)
-    for name, bits in w.items():
-        inner = synth.linear_inner(name, g)
-        if q8 and inner > 0 and inner % 32 == 0:
-            f = synth.bf16_bits_to_f32(bits.reshape(-1)).reshape(-1, inner)
-            blocks = quants.quantize(f, gguf.GGMLQuantizationType.Q8_0)
-            wr.add_tensor(name, blocks, raw_dtype=gguf.GGMLQuantizationType.Q8_0)
-        else:
-            wr.add_tensor(name, bits.reshape(-1, bits.shape[-1]).view(np.uint16),
-                          raw_shape=bits.reshape(-1, bits.shape[-1]).shape,
-                          raw_dtype=gguf.GGMLQuantizationType.BF16)
-    for name, v in synth.statistics(g).items():
-        wr.add_tensor(name, v.astype(np.float32))
-    wr.write_header_to_file()
-    wr.write_kv_data_to_file()
-    wr.write_tensors_to_file()
-    wr.close()
+from gguf_fixture import SEED, write_artifact  # noqa: E402
 
 
 @pytest.mark.parametrize("q8", [False, True])
@@ -65,3 +26,41 @@ def test_gguf_artifact_matches_synthetic(cuda_device, tmp_path, q8):
     b = Engine(g, seed=SEED, bias_scale=0.02, prompt_cache=False, weights=fmt).predict(req)
     assert np.isfinite(a).all()
     assert np.array_equal(a, b)
+
+
+def test_q8_policy_artifact_matches_device_quantiser(cuda_device, tmp_path):
+    """A mot-q8_0-v1 artifact made by wam_b200.artifact.convert from a BF16
+    artifact gives the same actions, bit for bit, as the engine quantising the
+    synthetic weights on the device; the policy selects the Q8_0 path even when
+    the caller asks for BF16."""
+    from oracle import synth
+    from wam_b200 import artifact
+    from wam_b200.engine import Engine, Req
+
+    g = synth.TINY
+    src, dst = tmp_path / "bf16.gguf", tmp_path / "q8.gguf"
+    write_artifact(src, g, q8=False, policy=artifact.BF16_POLICY_ID)
+    artifact.convert(src, dst)
+    r = synth.make_request(g, 23)
+    req = Req(r.state, r.latent, r.prompt, r.noise)
+    a = Engine(artifact=str(dst), prompt_cache=False, weights="bf16").predict(req)
+    b = Engine(g, seed=SEED, bias_scale=0.02, prompt_cache=False, weights="q8_0").predict(req)
+    c = Engine(artifact=str(src), prompt_cache=False, weights="bf16").predict(req)
+    assert np.isfinite(a).all()
+    assert np.array_equal(a, b)
+    assert not np.array_equal(a, c)
+
+
+@pytest.mark.parametrize("q8,policy,match", [
+    (False, "mot-q8_0-v1", "does not allow"),
+    (True, "mot-vae-bf16-qkv-v1", "does not allow"),
+    (False, "mot-bf16-v1", "unsupported weight policy"),
+])
+def test_engine_rejects_policy_violations(cuda_device, tmp_path, q8, policy, match):
+    from oracle import synth
+    from wam_b200.engine import Engine
+
+    p = tmp_path / "bad.gguf"
+    write_artifact(p, synth.TINY, q8=q8, policy=policy)
+    with pytest.raises(RuntimeError, match=match):
+        Engine(artifact=str(p), prompt_cache=False)

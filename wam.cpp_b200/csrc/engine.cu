@@ -347,6 +347,28 @@ bool MotEngine::load_weights(std::string* err) {
       *err = "artifact lacks gwp05.norm_eps / gwp05.flow_shift";
       return false;
     }
+    // Weight policy (scripts/inspect/inspect_gguf.py:60-75 _policy): an
+    // artifact that names one must be the packed-QKV BF16 policy the engine
+    // reads (mot-vae-bf16-qkv-v1) or its Q8_0 variant (mot-q8_0-v1, written by
+    // wam_b200.artifact), and conversion_policy must agree. Artifacts without
+    // the key (test fixtures) are read as their tensor types say.
+    std::string policy, conversion;
+    if (file.get_str("gwp05.weight_policy", &policy)) {
+      if (file.get_str("gwp05.conversion_policy", &conversion) && conversion != policy) {
+        *err = "artifact gwp05.weight_policy differs from gwp05.conversion_policy";
+        return false;
+      }
+      if (policy == "mot-q8_0-v1") {
+        policy_ = 2;
+        opt_.weight_format = 1;  // what the file does not hold as Q8_0 is quantised at load
+      } else if (policy == "mot-vae-bf16-qkv-v1") {
+        policy_ = 1;
+      } else {
+        *err = "unsupported weight policy " + policy +
+               " (this engine reads mot-vae-bf16-qkv-v1 and mot-q8_0-v1 artifacts)";
+        return false;
+      }
+    }
     loader_ = "gguf";
   }
   const auto specs = tensor_specs(g_);
@@ -428,6 +450,15 @@ bool MotEngine::load_weights(std::string* err) {
     if ((t->type != GGML_BF16 && !q8) || static_cast<int64_t>(t->elements()) != s.second) {
       *err = "artifact tensor " + s.first + " must be BF16 (or Q8_0 for a linear weight) with " +
              std::to_string(s.second) + " elements";
+      ok = false;
+      break;
+    }
+    // mot-q8_0-v1 stores every linear weight whose GGUF rows are whole
+    // 32-value blocks as Q8_0; the BF16 policy stores none.
+    const bool q8_row = inner > 0 && inner % 32 == 0 && !t->ne.empty() && t->ne[0] % 32 == 0;
+    if ((policy_ == 2 && q8_row && !q8) || (policy_ == 1 && q8)) {
+      *err = "artifact tensor " + s.first + " is " + (q8 ? "Q8_0" : "BF16") + ", which policy " +
+             (policy_ == 2 ? "mot-q8_0-v1" : "mot-vae-bf16-qkv-v1") + " does not allow";
       ok = false;
       break;
     }

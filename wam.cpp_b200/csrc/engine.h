@@ -193,6 +193,7 @@ class MotEngine {
   cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
   bool ok_ = false;
   std::string loader_;
+  int policy_ = 0;  // artifact weight policy: 0 none named, 1 mot-vae-bf16-qkv-v1, 2 mot-q8_0-v1
 
   // weights
   void* warena_ = nullptr;

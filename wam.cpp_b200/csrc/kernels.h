@@ -235,4 +235,15 @@ void launch_bf16_to_f32(const bf16* x, float* y, long long n, cudaStream_t s);
 void launch_synth_bf16(bf16* w, long long n, unsigned long long seed, double scale, double center,
                        cudaStream_t s);
 
+// Vision front-end: three camera views composed, resized (cover + centre crop,
+// triangle filter), patchified 2x2 into [12][out_h/2][out_w/2] F32 in [-1, 1]
+// (vision.cu). A view is the reference's ImageView
+// (src/models/gwp05/engine/engine.h:82-89) with its pixels on the device.
+struct PreprocessView {
+  const void* data;
+  int w, h, format;  // format 0: U8 RGB (3 bytes per pixel), 1: F32 RGB in [0, 1]
+};
+bool launch_preprocess(const PreprocessView* views, int out_w, int out_h, float* out,
+                       cudaStream_t stream);
+
 }  // namespace wamb

@@ -119,3 +119,24 @@ def make_request(g: Geometry, seed: int) -> Request:
         prompt=r.standard_normal((g.prompt_tokens, g.text_dim), dtype=np.float32),
         noise=r.standard_normal((g.action_chunk, g.action_dim), dtype=np.float32),
     )
+
+
+# Camera views of the vision front-end: three 640 x 480 RGB frames (the
+# LeRobot camera size) onto config 2's 768 x 1024 canvas (image_width =
+# grid_w * 32, image_height = grid_h * 32).
+VIEWS_CONFIG2 = ((480, 640), (480, 640), (480, 640))
+
+
+def make_views(seed: int, sizes=VIEWS_CONFIG2, formats=("u8", "u8", "u8")) -> list[np.ndarray]:
+    """Seeded synthetic camera views, HWC RGB: uint8 uniform over 0..255
+    ("u8") or float32 uniform in [0, 1) ("f32"), one PCG64 stream per view."""
+    out = []
+    for i, ((h, w), f) in enumerate(zip(sizes, formats)):
+        rng = np.random.Generator(np.random.PCG64([seed, i]))
+        if f == "u8":
+            out.append(rng.integers(0, 256, (h, w, 3), dtype=np.uint8))
+        elif f == "f32":
+            out.append(rng.random((h, w, 3), dtype=np.float32))
+        else:
+            raise ValueError(f)
+    return out
