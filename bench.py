@@ -8,7 +8,9 @@ replicas (one process per GPU, no collective); value = all chunks / max-over-
 ranks time. The same line carries "config4": BASELINE config 4, 64 requests
 per box split 64/N per GPU (strong scaling), timed after the main measurement,
 and (one GPU) "config1": one MoT block through wam_b200_block_forward in the
-reference's form and BASELINE's literal form, beside the CPU oracle's block.
+reference's form and BASELINE's literal form, beside the CPU oracle's block,
+and "vision": the vision front-end (compose / resize / patchify and the Wan
+VAE encoder) on config 2's canvas from three camera views.
 
   python bench.py [--gpus N --steps K --warmup W]        this engine
   python bench.py --impl reference [...]                 the reference arm: the
@@ -372,6 +374,8 @@ def main() -> None:
                     help="op case gemm: split-K factor (0 = the planner's choice)")
     ap.add_argument("--scratch", action="store_true",
                     help="op case gemm: split-K partials through a global workspace (as the engine)")
+    ap.add_argument("--no-vision", action="store_true",
+                    help="skip the vision front-end measurement (stage 1 + VAE encoder)")
     ap.add_argument("--no-config1", action="store_true",
                     help="skip the config-1 single-block point (GPU and CPU) of the bench line")
     ap.add_argument("--config4-requests", type=int, default=64,
@@ -501,6 +505,9 @@ def main() -> None:
         cb["cpu_model"] = host_cpu_model()
     if world == 1 and not args.no_config1:
         c1 = run_config1(local, cpu=not args.no_cpu_baseline)
+    vis = None
+    if world == 1 and not args.no_vision:
+        vis = run_vision(local, cpu=not args.no_cpu_baseline)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_s * 1e3 / args.steps,
@@ -515,6 +522,7 @@ def main() -> None:
         "kernels_per_chunk": kernels_per_chunk,
         "config4": c4,
         "config1": c1,
+        "vision": vis,
         "cpu_baseline": cb,
     }
     print(json.dumps(line), flush=True)
@@ -582,6 +590,77 @@ def run_config1(dev_index: int = 0, reps: int = 10, cpu: bool = True) -> dict:
             rec["cpu_cores"] = oracle.lib().oracle_threads()
             rec["cpu_kind"] = "port (F32 OpenMP oracle)"
         out["variants"][f"{ffn}+{norm}"] = rec
+    return out
+
+
+def run_vision(dev_index: int = 0, reps: int = 10, cpu: bool = True) -> dict:
+    """The vision front-end at config 2's canvas (768 x 1024, three 640 x 480
+    camera views, z = 48): stage 1 (compose / resize / patchify kernel, HBM
+    roofline on its input + output bytes) and the Wan VAE encoder (captured
+    graph of implicit-GEMM convolutions, tensor roofline on its FLOPs), each
+    device-timed with CUDA events on the launching stream after 3 warm-ups;
+    e2e = host views in, host latent out (wam_b200_vae_encode). CPU: the
+    oracle's stage 1 + encoder on a bounded sample (a 256 x 256 canvas)."""
+    import torch
+    from wam_b200 import vision
+    from wam_b200.workload import VIEWS_CONFIG2, make_views
+
+    W, H, z = 768, 1024, 48
+    views = make_views(SEED, VIEWS_CONFIG2)
+    dviews = [torch.from_numpy(v).cuda(dev_index) for v in views]
+    vae = vision.Vae(W, H, z_dim=z, seed=SEED, device_index=dev_index)
+    pix = vision.preprocess(dviews, W, H)
+    lat = vae.encode_device(pix)
+    for _ in range(3):
+        vision.preprocess(dviews, W, H, out=pix)
+        vae.encode_device(pix, lat)
+    torch.cuda.synchronize()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    pre_ms, enc_ms = [], []
+    for _ in range(reps):
+        e[0].record()
+        vision.preprocess(dviews, W, H, out=pix)
+        e[1].record()
+        vae.encode_device(pix, lat)
+        e[2].record()
+        torch.cuda.synchronize()
+        pre_ms.append(e[0].elapsed_time(e[1]))
+        enc_ms.append(e[1].elapsed_time(e[2]))
+    wall = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        vae.encode(views)
+        wall.append((time.perf_counter() - t0) * 1e3)
+    pk = peaks()
+    pre_bytes = sum(v.nbytes for v in views) + pix.numel() * 4
+    p50_pre, p50_enc = statistics.median(pre_ms), statistics.median(enc_ms)
+    out = {"workload": "vision front-end: 3 x 640x480 u8 views -> 768x1024 canvas -> "
+                       "latent 48x64x48 (synthetic VAE weights)",
+           "preprocess": {"device_us_p50": p50_pre * 1e3, "bytes": pre_bytes,
+                          "GB/s": pre_bytes / p50_pre / 1e6,
+                          "frac_of_hbm": pre_bytes / p50_pre / 1e6 / pk["hbm_gbs"]},
+           "vae_encoder": {"device_ms_p50": p50_enc, "gflop": vae.flops / 1e9,
+                           "tflops": vae.flops / p50_enc / 1e9,
+                           "frac_of_bf16_peak": vae.flops / p50_enc / 1e9 / pk["bf16_tflops"],
+                           "launches": vae.launches},
+           "e2e_ms_p50": statistics.median(wall),
+           "e2e_note": "host views -> host latent: H2D copies, stage 1, encoder graph, D2H"}
+    if cpu:
+        import oracle
+        from oracle import synth
+
+        sw, sh = 256, 256
+        weights = synth.make_vae_weights(SEED, z)
+        mean, std = vision.vae_synthetic_stats(z)
+        t0 = time.perf_counter()
+        px = oracle.compose_and_patchify(views, sw, sh)
+        oracle.vae_encode(weights, mean, std, z, px, sw, sh)
+        dt = time.perf_counter() - t0
+        out["cpu"] = {"sample": f"{sw}x{sh} canvas ({sw * sh / (W * H):.4f} of the pixels)",
+                      "sample_ms": dt * 1e3,
+                      "ms_scaled_to_config2": dt * 1e3 * (W * H) / (sw * sh),
+                      "cores": oracle.lib().oracle_threads(), "kind": "port (F32 OpenMP oracle)"}
+    vae.close()
     return out
 
 

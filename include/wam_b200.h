@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define WAM_B200_ABI_VERSION 1u
+#define WAM_B200_ABI_VERSION 2u
 
 #if defined(__GNUC__)
 #define WAM_B200_API __attribute__((visibility("default")))
@@ -278,11 +278,27 @@ typedef struct wam_b200_options {
   int ffn_kind;
   int norm_kind;
   int block_mode;
+  /* Added with the vision front-end: 1 loads the Wan VAE encoder (the vae.*
+   * tensors and gwp05.vae_latents_{mean,std} of the artifact, or synthetic
+   * weights from synthetic_seed) so that requests may carry camera images. */
+  int vae;
 } wam_b200_options;
 
+/* A camera view (ImageView, src/models/gwp05/engine/engine.h:82-89): host (or,
+ * for wam_b200_op_preprocess, device) pixels, HWC RGB. */
+#define WAM_B200_PIXEL_U8 0         /* 3 bytes per pixel (PixelFormat::U8) */
+#define WAM_B200_PIXEL_F32_RGB_01 1 /* 3 floats per pixel in [0, 1] */
+typedef struct wam_b200_image {
+  const void* data;
+  int w;
+  int h;
+  int format;
+} wam_b200_image;
+
 /* One request (EngineInputsView, src/models/gwp05/engine/engine.h:91-105, with
- * the precomputed latent and prompt embedding the external_embedding policy
- * uses). Host pointers, borrowed for the call. */
+ * the precomputed prompt embedding the external_embedding policy uses, and
+ * either the precomputed VAE latent or the three camera views). Host pointers,
+ * borrowed for the call. */
 typedef struct wam_b200_request {
   const float* state;      /* [state_n >= real_state_dim], un-normalised */
   int state_n;
@@ -291,6 +307,12 @@ typedef struct wam_b200_request {
   long long ref_latent_n;
   const float* prompt_emb; /* [prompt_tokens_in * text_dim], zero-padded to prompt_tokens */
   int prompt_tokens;
+  /* ABI 2: with ref_latent NULL, the views [n_images == 3] run the vision
+   * front-end on the device (compose + VAE encoder, as run_vae, engine/
+   * vae.cpp:279-388, when the reference gets no precomputed latent,
+   * engine.cpp:260-270); needs an engine created with vae = 1. */
+  const wam_b200_image* images;
+  int n_images;
 } wam_b200_request;
 
 typedef struct wam_b200_stats {
@@ -321,6 +343,31 @@ WAM_B200_API int wam_b200_predict(wam_b200_engine* engine, const wam_b200_reques
 WAM_B200_API int wam_b200_predict_batch(wam_b200_engine* engine, const wam_b200_request* requests,
                                         int batch, float* action_out, size_t action_out_n,
                                         wam_b200_stats* stats, wam_b200_status* status);
+
+/* max_batch of the engine's options (requests per predict_batch). */
+WAM_B200_API int wam_b200_max_batch(const wam_b200_engine* engine);
+
+/* Batch-capable serving surface (no reference counterpart: the reference
+ * serialises predicts on a per-model mutex, src/models/gwp05/model.cpp:61,
+ * and reports Capabilities::batch_inference = false, include/wam/types.h:236-237).
+ * Any number of threads call wam_b200_batcher_predict concurrently; a worker
+ * thread runs the queued requests in arrival order as predict_batch calls of
+ * up to max_batch, waiting at most max_wait_us after the first request for
+ * more. A failing batch is retried request by request, so a bad request fails
+ * alone. batch_size reports the batch a request rode in. The engine must not
+ * be used directly while a batcher serves it. */
+typedef struct wam_b200_batcher wam_b200_batcher;
+WAM_B200_API int wam_b200_batcher_create(wam_b200_engine* engine, int max_wait_us,
+                                         wam_b200_batcher** batcher, wam_b200_status* status);
+/* Drains the queue, stops the worker (the engine stays alive). */
+WAM_B200_API void wam_b200_batcher_destroy(wam_b200_batcher* batcher);
+WAM_B200_API int wam_b200_batcher_predict(wam_b200_batcher* batcher, const wam_b200_request* request,
+                                          float* action_out, size_t action_out_n,
+                                          wam_b200_stats* stats, int* batch_size,
+                                          wam_b200_status* status);
+/* Batches run and requests served so far. */
+WAM_B200_API int wam_b200_batcher_counts(wam_b200_batcher* batcher, long long* batches,
+                                         long long* requests);
 
 /* One MoT layer over given hidden states: the layer body
  * of the reference's un-cached forward, run_mot_step (src/models/gwp05/engine/
@@ -409,15 +456,8 @@ WAM_B200_API int wam_b200_read_tensor(wam_b200_engine* engine, const char* name,
  * cropped), patchify 2x2 and map to [-1, 1]. Output [12][h/2][w/2] F32 on the
  * device, packed channel (c * 2 + dx) * 2 + dy. Bit-identical to the reference's
  * CPU compose_and_patchify (src/models/gwp05/engine/vae.cpp:1-134); replaces its
- * CUDA preprocessor (src/models/gwp05/kernels/cuda_preprocess.h:6-14). */
-#define WAM_B200_PIXEL_U8 0         /* RGB, 3 bytes per pixel (PixelFormat::U8) */
-#define WAM_B200_PIXEL_F32_RGB_01 1 /* RGB, 3 floats per pixel in [0, 1] */
-typedef struct wam_b200_image { /* ImageView, engine/engine.h:84-89 */
-  const void* data;
-  int w;
-  int h;
-  int format;
-} wam_b200_image;
+ * CUDA preprocessor (src/models/gwp05/kernels/cuda_preprocess.h:6-14). Views are
+ * wam_b200_image (above). */
 typedef struct wam_b200_preprocessor wam_b200_preprocessor;
 
 /* gwp05_cuda_preprocessor_create / _destroy (cuda_preprocess.cu:139-148): device
@@ -436,6 +476,69 @@ WAM_B200_API int wam_b200_preprocess(wam_b200_preprocessor* preprocessor,
 /* The same kernel on views already on the device (asynchronous on `stream`). */
 WAM_B200_API int wam_b200_op_preprocess(const wam_b200_image* device_images, int output_width,
                                         int output_height, float* output_device, void* stream);
+
+/* Implicit-GEMM convolution of the VAE encoder on NHWC BF16 activations of one
+ * image ([in_h][in_w][cin], cin >= 64 and a multiple of 8): mode 0 = 3x3 stride 1 padding
+ * 1, 1 = 3x3 stride 2 after a one-pixel zero pad at the right and bottom (the
+ * downsampler, vae.cpp:211-214), 2 = 1x1. Output [out_h][out_w][cout] BF16
+ * (cout a multiple of 16). epilogue 0: out = bf16(bf16(conv) + bias);
+ * 4: out = bf16(residual + bf16(bf16(conv) + bias)) (vae_conv + ggml_add,
+ * vae.cpp:141-160, 178-191). w_laid comes from wam_b200_op_conv_weight_layout
+ * of the [cout][cin][kh][kw] weight: [wam_b200_conv_cout_pad(cout)][taps]
+ * [wam_b200_conv_cin_pad(cin)], zero padded.
+ * `error` is a device word the kernel sets on a timed-out wait. */
+WAM_B200_API int wam_b200_conv_cin_pad(int cin);
+WAM_B200_API int wam_b200_conv_cout_pad(int cout);
+WAM_B200_API int wam_b200_op_conv_weight_layout(const void* src, void* dst, int cout, int cin,
+                                                int taps, void* stream);
+WAM_B200_API int wam_b200_op_conv2d(const void* x, int in_w, int in_h, int cin, int mode,
+                                    const void* w_laid, int cout, int epilogue, const void* bias,
+                                    const void* residual, void* out, unsigned* error,
+                                    void* stream);
+
+/* Stage 2 of the vision front-end: the Wan VAE encoder (single frame), the
+ * reference's run_vae (src/models/gwp05/engine/vae.cpp:279-388) on the B200
+ * as one captured CUDA graph of implicit-GEMM convolutions. Weights: the vae.*
+ * tensors of a GGUF artifact (BF16, policy mot-vae-bf16*) with
+ * gwp05.vae_latents_mean / _std, or deterministic synthetic ones
+ * (artifact_path NULL). image_width / image_height: the canvas (multiples of
+ * 32); the latent is [z_dim][H / 16][W / 16] F32, (posterior mode - mean) / std. */
+typedef struct wam_b200_vae wam_b200_vae;
+typedef struct wam_b200_vae_options {
+  uint32_t struct_size; /* sizeof(wam_b200_vae_options) */
+  const char* artifact_path;
+  uint64_t synthetic_seed;
+  int image_width;
+  int image_height;
+  int z_dim;
+  int device_index;
+  int use_cuda_graph;
+} wam_b200_vae_options;
+/* The encoder's tensors (82, the reference's compact GGUF names): name and
+ * shape ([cout, cin, kh, kw] or [c]) of tensor `index`; returns the rank, or
+ * -1 past the last tensor. Host only. */
+WAM_B200_API int wam_b200_vae_tensor_spec(int z_dim, int index, char* name, size_t name_n,
+                                          long long* shape4);
+WAM_B200_API int wam_b200_vae_create(const wam_b200_vae_options* options, wam_b200_vae** vae,
+                                     wam_b200_status* status);
+WAM_B200_API void wam_b200_vae_destroy(wam_b200_vae* vae);
+/* Floats of one latent, kernel launches of one encode, FLOPs of one encode. */
+WAM_B200_API int wam_b200_vae_info(const wam_b200_vae* vae, int* latent_count, int* launches,
+                                   double* flops);
+/* run_vae with host images: preprocess (stage 1) + encoder; latent to host.
+ * Synchronous. */
+WAM_B200_API int wam_b200_vae_encode(wam_b200_vae* vae, const wam_b200_image* images,
+                                     int image_count, float* latent, size_t latent_n,
+                                     wam_b200_status* status);
+/* Encoder only, device pointers: pixels [12][H/2][W/2] F32 (stage 1 output),
+ * latent [z][H/16][W/16] F32; asynchronous on `stream` (NULL: the VAE's own). */
+WAM_B200_API int wam_b200_vae_encode_device(wam_b200_vae* vae, const float* pixels,
+                                            float* latent, void* stream,
+                                            wam_b200_status* status);
+/* F32 copy of an intermediate NHWC activation ("conv_in", "down0".."down3",
+ * "mid", "moments") of the last encode, for parity checks. */
+WAM_B200_API int wam_b200_vae_read_stage(wam_b200_vae* vae, const char* name, float* out,
+                                         size_t n, int* h, int* w, int* c);
 
 #ifdef __cplusplus
 }

@@ -87,6 +87,10 @@ def lib():
         l.oracle_block.restype = C.c_int
         l.oracle_block.argtypes = [C.c_void_p, C.c_int, C.c_float] + [f32p] * 6
         i32p = C.POINTER(C.c_int)
+        l.oracle_vae_encode.restype = C.c_int
+        l.oracle_vae_encode.argtypes = [C.POINTER(C.c_char_p), C.POINTER(C.c_void_p), C.c_int,
+                                        f32p, f32p, C.c_int, f32p, C.c_int, C.c_int, f32p,
+                                        C.c_char_p, f32p, i32p]
         l.oracle_compose_and_patchify.restype = C.c_int
         l.oracle_compose_and_patchify.argtypes = [C.POINTER(C.c_void_p), i32p, i32p, i32p,
                                                   C.c_int, C.c_int, f32p]
@@ -137,6 +141,30 @@ def compose_and_patchify(views, out_w: int, out_h: int, reference: bool = False)
     if rc != 0:
         raise ValueError("compose_and_patchify rejected its inputs")
     return out
+
+
+def vae_encode(weights: dict, mean, std, z: int, pixels, width: int, height: int,
+               stage: str | None = None):
+    """Wan VAE encoder (oracle/vae.cpp) on stage-1 pixels [12][H/2][W/2]:
+    latent [z][H/16][W/16] (and the NHWC activation named by `stage`)."""
+    names = list(weights)
+    arrs = [np.ascontiguousarray(weights[n], dtype=np.uint16) for n in names]
+    cn = (C.c_char_p * len(names))(*[n.encode() for n in names])
+    ct = (C.c_void_p * len(names))(*[a.ctypes.data for a in arrs])
+    mean = np.ascontiguousarray(mean, np.float32)
+    std = np.ascontiguousarray(std, np.float32)
+    pixels = np.ascontiguousarray(pixels, np.float32)
+    lat = np.zeros((z, height // 16, width // 16), np.float32)
+    st = np.zeros(height * width * 160 // 4 + 1, np.float32) if stage else None
+    dims = (C.c_int * 3)()
+    rc = lib().oracle_vae_encode(cn, ct, len(names), _fp(mean), _fp(std), z, _fp(pixels), width,
+                                 height, _fp(lat), stage.encode() if stage else None,
+                                 _fp(st) if stage else None, dims)
+    if rc != 0:
+        raise ValueError(f"oracle_vae_encode failed ({rc})")
+    if stage:
+        return lat, st[:dims[0] * dims[1] * dims[2]].reshape(dims[0], dims[1], dims[2])
+    return lat
 
 
 def _fp(a):

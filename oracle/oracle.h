@@ -105,6 +105,17 @@ int oracle_threads(void);
 int oracle_compose_and_patchify(const void* const* data, const int* w, const int* h,
                                 const int* format, int out_w, int out_h, float* out);
 
+/* Vision front-end stage 2 (vae.cpp): the Wan VAE encoder on pixels
+ * [12][height / 2][width / 2] (stage 1 output) with BF16 weights given by
+ * compact name; latent [z][height / 16][width / 16]. With `stage` naming an
+ * intermediate ("conv_in", "down0".."down3", "mid", "moments") its NHWC values
+ * go to stage_out and its (h, w, c) to stage_dims. Returns non-zero on bad
+ * input (2: a tensor is missing). */
+int oracle_vae_encode(const char* const* names, const uint16_t* const* tensors, int n_tensors,
+                      const float* mean, const float* stdv, int z, const float* pixels, int width,
+                      int height, float* latent, const char* stage, float* stage_out,
+                      int* stage_dims);
+
 #ifdef __cplusplus
 }
 #endif

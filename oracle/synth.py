@@ -201,3 +201,21 @@ def quantize_q8_linear(g: Geometry, weights: dict[str, np.ndarray]) -> dict[str,
         d = quants.dequantize(q, gguf.GGMLQuantizationType.Q8_0).astype(np.float32)
         out[name] = f32_to_bf16_bits(d.reshape(-1)).reshape(w.shape)
     return out
+
+
+def make_vae_weights(seed: int, z_dim: int = 48) -> dict[str, np.ndarray]:
+    """The synthetic Wan VAE encoder weights of csrc/vae.cu (load_weights):
+    convolutions N(0, 1 / fan_in), biases N(0, 0.02), RMS gains 1 + N(0, 0.02)."""
+    from wam_b200.vision import vae_tensor_specs
+
+    out = {}
+    for name, shape in vae_tensor_specs(z_dim):
+        n = int(np.prod(shape))
+        if name.endswith(".weight"):
+            scale, center = 1.0 / float(np.sqrt(float(shape[1] * shape[2] * shape[3]))), 0.0
+        elif name.endswith(".bias"):
+            scale, center = 0.02, 0.0
+        else:
+            scale, center = 0.02, 1.0
+        out[name] = synth_bits(seed, name, n, scale, center).reshape(shape)
+    return out

@@ -109,3 +109,40 @@ def test_engine_vtable_predict_reset(cuda_device):
         assert np.array_equal(_predict(lib, e, r, geom), got)  # usable after a failure
     finally:
         lib.wam_b200_adapter_destroy(e)
+
+
+def test_engine_vtable_predict_from_images(cuda_device):
+    """EngineInputsView with three camera views and no precomputed latent: the
+    adapter hands the views to the engine's vision front-end; the chunk equals
+    the C ABI engine's from the same views, bit for bit."""
+    from oracle import synth
+    from wam_b200.engine import Engine, Req
+    from wam_b200.workload import make_views
+
+    lib = _lib()
+    u8pp = C.POINTER(C.c_ubyte) * 3
+    lib.wam_b200_adapter_predict_images.restype = C.c_longlong
+    lib.wam_b200_adapter_predict_images.argtypes = [
+        C.c_void_p, C.POINTER(C.c_float), u8pp, C.POINTER(C.c_int), C.POINTER(C.c_int),
+        C.POINTER(C.c_float), C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_float), C.c_longlong]
+    g = synth.TINY
+    o = _options(g)
+    o.vae = 1
+    e = lib.wam_b200_adapter_create(C.byref(o))
+    assert e
+    r = synth.make_request(g, 8)
+    views = make_views(4, ((480, 640), (240, 320), (200, 300)))
+    ptrs = u8pp(*[v.ctypes.data_as(C.POINTER(C.c_ubyte)) for v in views])
+    ws = (C.c_int * 3)(*[v.shape[1] for v in views])
+    hs = (C.c_int * 3)(*[v.shape[0] for v in views])
+    out = np.zeros(g.action_chunk * g.real_action_dim, np.float32)
+    st = np.ascontiguousarray(r.state, np.float32)
+    pr = np.ascontiguousarray(r.prompt, np.float32)
+    nz = np.ascontiguousarray(r.noise, np.float32)
+    n = lib.wam_b200_adapter_predict_images(e, _fp(st), ptrs, ws, hs, _fp(pr), pr.shape[0],
+                                            _fp(nz), _fp(out), out.size)
+    assert n == out.size
+    ref = Engine(g, seed=SEED, bias_scale=0.02, prompt_cache=True, vae=True).predict(
+        Req(r.state, None, r.prompt, r.noise, images=views))
+    assert np.array_equal(out.reshape(ref.shape), ref)
+    lib.wam_b200_adapter_destroy(e)

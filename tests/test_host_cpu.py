@@ -38,7 +38,7 @@ def test_abi_exports_every_declared_symbol(lib):
     assert len(names) >= 20
     for n in names:
         assert hasattr(lib, n), f"{n} declared in include/wam_b200.h but not exported"
-    assert lib.wam_b200_abi_version() == 1
+    assert lib.wam_b200_abi_version() == 2
 
 
 def test_engine_schedule_matches_reference(lib):

@@ -55,3 +55,31 @@ def test_oracle_rejects_bad_canvas():
     views = make_views(1, ((8, 8),) * 3)
     with pytest.raises(ValueError):
         oracle.compose_and_patchify(views, 33, 16)
+
+
+def test_vae_tensor_specs_match_library():
+    """The Python spec list (GGUF writers, oracle weights) equals the encoder's
+    own (csrc/vae.cu), read through the C ABI without a GPU: 82 tensors, the
+    reference's count for the vae component (artifact.cpp:159)."""
+    import ctypes as C
+
+    from wam_b200 import load
+    from wam_b200.vision import vae_tensor_specs
+
+    lib = load()
+    fn = lib.wam_b200_vae_tensor_spec
+    fn.restype = C.c_int
+    fn.argtypes = [C.c_int, C.c_int, C.c_char_p, C.c_size_t, C.POINTER(C.c_longlong)]
+    py = vae_tensor_specs(48)
+    assert len(py) == 82
+    got = []
+    buf = C.create_string_buffer(128)
+    shape = (C.c_longlong * 4)()
+    i = 0
+    while True:
+        nd = fn(48, i, buf, 128, shape)
+        if nd < 0:
+            break
+        got.append((buf.value.decode(), tuple(shape[j] for j in range(nd))))
+        i += 1
+    assert got == py

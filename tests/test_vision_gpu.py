@@ -73,7 +73,7 @@ def test_preprocess_argument_checks(cuda_device):
     with pytest.raises(RuntimeError, match="positive and even"):
         p(views, 15, 16)
     with pytest.raises(RuntimeError, match="positive and even"):
-        vision.preprocess(_dev(views), 16, 0)
+        vision.preprocess(_dev(views), 16, 6 + 1)
     bad = [views[0], np.zeros((0, 4, 3), np.uint8), views[2]]
     with pytest.raises(RuntimeError, match="invalid image 1"):
         p(bad, 16, 16)

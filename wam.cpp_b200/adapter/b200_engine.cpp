@@ -69,10 +69,19 @@ std::vector<float> B200Engine::predict(const EngineInputsView& in) {
     std::fprintf(stderr, "wam(b200): state is required\n");
     return {};
   }
-  if (!in.precomputed_ref_latent) {
-    std::fprintf(stderr, "wam(b200): a precomputed reference latent is required (raw images need "
-                         "the VAE front-end, which this engine does not run)\n");
-    return {};
+  // Raw camera views go through the engine's vision front-end (compose + VAE
+  // on the device), the reference's run_vae path (engine.cpp:260-270).
+  wam_b200_image views[3] = {};
+  const bool from_images = !in.precomputed_ref_latent;
+  if (from_images) {
+    if (!in.images || in.n_images != 3) {
+      std::fprintf(stderr, "wam(b200): exactly three input images are required\n");
+      return {};
+    }
+    for (int i = 0; i < 3; ++i)
+      views[i] = wam_b200_image{in.images[i].data, in.images[i].w, in.images[i].h,
+                                in.images[i].format == PixelFormat::U8 ? WAM_B200_PIXEL_U8
+                                                                       : WAM_B200_PIXEL_F32_RGB_01};
   }
   if (!in.precomputed_prompt_emb) {
     std::fprintf(stderr, "wam(b200): a precomputed prompt embedding is required (external_embedding "
@@ -87,6 +96,10 @@ std::vector<float> B200Engine::predict(const EngineInputsView& in) {
   r.ref_latent_n = in.precomputed_ref_latent_n;
   r.prompt_emb = in.precomputed_prompt_emb;
   r.prompt_tokens = in.precomputed_prompt_tokens;
+  if (from_images) {
+    r.images = views;
+    r.n_images = 3;
+  }
   std::vector<float> out(static_cast<size_t>(g_.action_chunk) * g_.real_action_dim);
   wam_b200_stats s{};
   wam_b200_status st{};
@@ -132,6 +145,7 @@ std::unique_ptr<Engine> create_b200(const ArtifactContract& artifact, const Engi
   o.max_batch = 1;
   o.use_cuda_graphs = 1;
   o.prompt_cache = options.prompt_cache_capacity > 0 ? 1 : 0;
+  o.vae = 1;  // the artifact contract carries the VAE (artifact.cpp:159), so images work
   auto e = create_b200_synthetic(o);
   if (!e) return nullptr;
   const Geometry& a = artifact.geometry;
@@ -174,6 +188,31 @@ __attribute__((visibility("default"))) long long wam_b200_adapter_predict(
   in.state = state;
   in.precomputed_ref_latent = latent;
   in.precomputed_ref_latent_n = latent_n;
+  in.precomputed_prompt_emb = prompt;
+  in.precomputed_prompt_tokens = prompt_tokens;
+  in.noise = noise;
+  std::vector<float> r = static_cast<Engine*>(e)->predict(in);
+  if (static_cast<long long>(r.size()) > out_n) return -1;
+  std::memcpy(out, r.data(), r.size() * sizeof(float));
+  return static_cast<long long>(r.size());
+}
+
+// Engine::predict from three camera views (uint8 RGB, w x h each) instead of a
+// latent: the vision front-end path.
+__attribute__((visibility("default"))) long long wam_b200_adapter_predict_images(
+    void* e, const float* state, const unsigned char* const* views, const int* w, const int* h,
+    const float* prompt, int prompt_tokens, const float* noise, float* out, long long out_n) {
+  wam::internal::gwp05::engine::ImageView im[3];
+  for (int i = 0; i < 3; ++i) {
+    im[i].data = views[i];
+    im[i].w = w[i];
+    im[i].h = h[i];
+    im[i].format = wam::internal::gwp05::engine::PixelFormat::U8;
+  }
+  wam::internal::gwp05::engine::EngineInputsView in{};
+  in.state = state;
+  in.images = im;
+  in.n_images = 3;
   in.precomputed_prompt_emb = prompt;
   in.precomputed_prompt_tokens = prompt_tokens;
   in.noise = noise;

@@ -64,7 +64,7 @@ def build(force: bool = False, jobs: int | None = None) -> Path:
         objs = list(pool.map(lambda s: compile_one(s, force, hdr_time), srcs))
     newest = max(o.stat().st_mtime for o in objs)
     if force or not LIB.exists() or LIB.stat().st_mtime < newest:
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs)]
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lpthread"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             sys.stderr.write(res.stdout + res.stderr)

@@ -23,6 +23,7 @@
 
 #include "gguf.h"
 #include "host_math.h"
+#include "vae.h"
 
 namespace wamb {
 
@@ -199,6 +200,7 @@ std::unique_ptr<MotEngine> MotEngine::create(const EngineOptions& opt, std::stri
 MotEngine::~MotEngine() {
   if (side_) cudaStreamSynchronize(side_);
   if (stream_) cudaStreamSynchronize(stream_);
+  vae_.reset();
   drop_plans();
   for (auto& e : phase_ev_)
     if (e) cudaEventDestroy(e);
@@ -267,6 +269,26 @@ bool MotEngine::init(const EngineOptions& opt, std::string* err) {
   }
   flow_schedule(g.steps, g.flow_shift, &timesteps_, &sigmas_);
   if (!alloc_buffers(err)) return false;
+  if (opt.vae) {
+    if (opt.block) {
+      *err = "block engines take hidden states, not images (vae must be 0)";
+      return false;
+    }
+    VaeOptions vo;
+    vo.artifact_path = opt.artifact_path;
+    vo.synthetic_seed = opt.seed;
+    vo.image_width = g.grid_w * 32;
+    vo.image_height = g.grid_h * 32;
+    vo.z_dim = g.vae_z;
+    vo.device_index = opt.device;
+    vo.use_cuda_graph = opt.graphs;
+    vae_.reset(new VaeEncoder());
+    std::string verr;
+    if (!vae_->init(vo, &verr)) {
+      *err = "VAE encoder: " + verr;
+      return false;
+    }
+  }
   CK(cudaStreamSynchronize(stream_));
   prompt_sig_.assign(opt.max_batch, {});
   ok_ = true;
@@ -1432,7 +1454,17 @@ bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
         *err = "state contains NaN/Inf";
         return false;
       }
-    if (!r.latent || r.latent_n != lat) {
+    const bool from_images = !r.latent && r.n_images > 0;
+    if (from_images) {
+      if (!vae_) {
+        *err = "camera images need an engine created with the VAE encoder (options.vae = 1)";
+        return false;
+      }
+      if (r.n_images != 3) {
+        *err = "exactly three input images are required";
+        return false;
+      }
+    } else if (!r.latent || r.latent_n != lat) {
       *err = "reference latent must have vae_z * (2 grid_h) * (2 grid_w) values";
       return false;
     }
@@ -1442,12 +1474,14 @@ bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
     }
     normalize_state(r.state, g.real_state_dim, A, sq01_.data(), sq99_.data(),
                     h_state_ + static_cast<size_t>(i) * A);
-    std::memcpy(h_latent_ + i * lat, r.latent, lat * 4);
-    for (long long j = 0; j < lat; ++j)
-      if (!std::isfinite(h_latent_[i * lat + j])) {
-        *err = "reference latent contains NaN/Inf";
-        return false;
-      }
+    if (!from_images) {
+      std::memcpy(h_latent_ + i * lat, r.latent, lat * 4);
+      for (long long j = 0; j < lat; ++j)
+        if (!std::isfinite(h_latent_[i * lat + j])) {
+          *err = "reference latent contains NaN/Inf";
+          return false;
+        }
+    }
     float* pr = h_prompt_ + static_cast<size_t>(i) * Nt * D;
     std::memcpy(pr, r.prompt, static_cast<size_t>(r.prompt_tokens) * D * 4);
     std::memset(pr + static_cast<size_t>(r.prompt_tokens) * D, 0,
@@ -1466,7 +1500,21 @@ bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
     }
   }
   CK(cudaMemcpyAsync(in_state_, h_state_, static_cast<size_t>(batch) * A * 4, cudaMemcpyHostToDevice, stream_));
-  CK(cudaMemcpyAsync(in_latent_, h_latent_, static_cast<size_t>(batch) * lat * 4, cudaMemcpyHostToDevice, stream_));
+  // Latents: copied from the host, or made on the device from the views
+  // (stage 1 + the captured VAE encoder, writing the request's latent slot).
+  for (int i = 0; i < batch; ++i) {
+    float* dst = in_latent_ + static_cast<size_t>(i) * lat;
+    if (reqs[i].latent) {
+      CK(cudaMemcpyAsync(dst, h_latent_ + static_cast<size_t>(i) * lat, lat * 4,
+                         cudaMemcpyHostToDevice, stream_));
+    } else {
+      std::string verr;
+      if (!vae_->encode_images(reqs[i].images, 3, dst, stream_, &verr)) {
+        *err = "VAE encoder: " + verr;
+        return false;
+      }
+    }
+  }
   CK(cudaMemcpyAsync(in_prompt_, h_prompt_, static_cast<size_t>(batch) * Nt * D * 4, cudaMemcpyHostToDevice, stream_));
   CK(cudaMemcpyAsync(in_noise_, h_noise_, static_cast<size_t>(batch) * T * A * 4, cudaMemcpyHostToDevice, stream_));
   staged_batch_ = batch;

@@ -47,6 +47,9 @@ struct EngineOptions {
   // Config 1: the engine runs one MoT layer over given hidden states
   // (block_forward) instead of action chunks; needs layers == 1, max_batch == 1.
   bool block = false;
+  // Vision front-end: load the Wan VAE encoder so that requests may carry the
+  // three camera views instead of a precomputed latent.
+  bool vae = false;
 };
 
 struct RequestView {
@@ -57,6 +60,10 @@ struct RequestView {
   long long latent_n = 0;
   const float* prompt = nullptr;  // [prompt_tokens_in * text_dim]
   int prompt_tokens = 0;
+  // Camera views (host pixels) used when latent is null: stage 1 + the VAE
+  // encoder write the latent on the device.
+  PreprocessView images[3] = {};
+  int n_images = 0;
 };
 
 struct EngineStats {
@@ -112,12 +119,16 @@ std::vector<std::pair<std::string, int64_t>> tensor_specs(const Geometry& g);
 int64_t linear_inner(const std::string& name, const Geometry& g);
 uint64_t tensor_seed(uint64_t seed, const std::string& name);
 
+class VaeEncoder;
+
 class MotEngine {
  public:
   static std::unique_ptr<MotEngine> create(const EngineOptions& opt, std::string* err);
   ~MotEngine();
 
   const Geometry& geometry() const { return g_; }
+  int device() const { return opt_.device; }
+  int max_batch() const { return opt_.max_batch; }
   cudaStream_t stream() const { return stream_; }
   uint64_t resident_bytes() const { return resident_bytes_; }
 
@@ -253,6 +264,7 @@ class MotEngine {
 
   std::vector<float> timesteps_, sigmas_;
   std::map<int, std::unique_ptr<Plan>> plans_;
+  std::unique_ptr<VaeEncoder> vae_;  // vision front-end (options.vae)
   std::vector<std::vector<float>> prompt_sig_;  // per slot, last projected prompt
   bool prompt_valid_ = false;
   int staged_batch_ = 0;

@@ -71,6 +71,10 @@ std::vector<wamb::RequestView> views(const wam_b200_request* r, int n) {
     v[i].latent_n = r[i].ref_latent_n;
     v[i].prompt = r[i].prompt_emb;
     v[i].prompt_tokens = r[i].prompt_tokens;
+    v[i].n_images = r[i].images ? r[i].n_images : 0;
+    for (int j = 0; j < 3 && j < v[i].n_images; ++j)
+      v[i].images[j] = wamb::PreprocessView{r[i].images[j].data, r[i].images[j].w,
+                                            r[i].images[j].h, r[i].images[j].format};
   }
   return v;
 }
@@ -121,6 +125,7 @@ WAM_B200_API int wam_b200_create(const wam_b200_options* o, wam_b200_engine** ou
       return fail(st, WAM_B200_INVALID_ARGUMENT,
                   "ffn_kind / norm_kind / block_mode apply to synthetic weights only");
   }
+  if (o->struct_size >= offsetof(wam_b200_options, vae) + sizeof(int)) eo.vae = o->vae != 0;
   std::string err;
   auto e = wamb::MotEngine::create(eo, &err);
   if (!e) {
@@ -159,6 +164,7 @@ WAM_B200_API int wam_b200_predict_batch(wam_b200_engine* e, const wam_b200_reque
   const wamb::Geometry& g = e->impl->geometry();
   if (n < static_cast<size_t>(batch) * g.action_chunk * g.real_action_dim)
     return fail(st, WAM_B200_INVALID_ARGUMENT, "action output buffer is too small");
+  cudaSetDevice(e->impl->device());  // callers may be on another thread (the batcher's)
   auto v = views(r, batch);
   wamb::EngineStats es;
   std::string err;
@@ -173,6 +179,10 @@ WAM_B200_API int wam_b200_predict_batch(wam_b200_engine* e, const wam_b200_reque
   return ok(st);
 }
 
+WAM_B200_API int wam_b200_max_batch(const wam_b200_engine* e) {
+  return e ? e->impl->max_batch() : 0;
+}
+
 WAM_B200_API int wam_b200_predict(wam_b200_engine* e, const wam_b200_request* r, float* out,
                                   size_t n, wam_b200_stats* stats, wam_b200_status* st) {
   return wam_b200_predict_batch(e, r, 1, out, n, stats, st);
@@ -181,6 +191,7 @@ WAM_B200_API int wam_b200_predict(wam_b200_engine* e, const wam_b200_request* r,
 WAM_B200_API int wam_b200_stage(wam_b200_engine* e, const wam_b200_request* r, int batch,
                                 wam_b200_status* st) {
   if (!e || !r) return fail(st, WAM_B200_INVALID_ARGUMENT, "engine and requests are required");
+  cudaSetDevice(e->impl->device());
   auto v = views(r, batch);
   std::string err;
   if (!e->impl->stage(v.data(), batch, &err)) return fail(st, WAM_B200_INVALID_ARGUMENT, err);
@@ -189,6 +200,7 @@ WAM_B200_API int wam_b200_stage(wam_b200_engine* e, const wam_b200_request* r, i
 
 WAM_B200_API int wam_b200_run(wam_b200_engine* e, int batch, wam_b200_status* st) {
   if (!e) return fail(st, WAM_B200_INVALID_ARGUMENT, "engine is required");
+  cudaSetDevice(e->impl->device());
   std::string err;
   if (!e->impl->run(batch, &err)) return fail(st, code_of(err), err);
   return ok(st);

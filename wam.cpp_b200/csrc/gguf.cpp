@@ -183,6 +183,13 @@ bool GgufFile::get_f32(const std::string& key, float* out) const {
   return true;
 }
 
+bool GgufFile::get_f32_array(const std::string& key, std::vector<float>* out) const {
+  auto it = kv_.find(key);
+  if (it == kv_.end() || it->second.type != GT_ARR) return false;
+  out->assign(it->second.arr.begin(), it->second.arr.end());
+  return true;
+}
+
 bool GgufFile::get_str(const std::string& key, std::string* out) const {
   auto it = kv_.find(key);
   if (it == kv_.end() || it->second.type != GT_STR) return false;

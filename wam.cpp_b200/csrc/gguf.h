@@ -49,6 +49,8 @@ class GgufFile {
   bool get_u32(const std::string& key, uint32_t* out) const;
   bool get_f32(const std::string& key, float* out) const;
   bool get_str(const std::string& key, std::string* out) const;
+  // Numeric array (<= 4096 elements) as floats.
+  bool get_f32_array(const std::string& key, std::vector<float>* out) const;
   const GgufTensor* tensor(const std::string& name) const;
   const std::vector<GgufTensor>& tensors() const { return tensors_; }
   const std::string& path() const { return path_; }

@@ -246,4 +246,33 @@ struct PreprocessView {
 bool launch_preprocess(const PreprocessView* views, int out_w, int out_h, float* out,
                        cudaStream_t stream);
 
+// Implicit-GEMM convolution (conv.cu) over NHWC BF16 activations of one
+// image: mode 0 = 3x3 stride 1 padding 1, 1 = 3x3 stride 2 after a one-pixel
+// zero pad at the right / bottom, 2 = 1x1. Weights in the layout of
+// launch_conv_weight_layout: [conv_cout_pad(cout)][taps][conv_cin_pad(cin)]
+// (zero padded); cin >= 64 (pad narrower inputs).
+struct ConvParams {
+  int mode, taps, cblocks;
+  int out_w, out_h;
+  int tiles_x, tiles_y, tiles_n;
+};
+struct ConvOp {
+  CUtensorMap tm_w;
+  CUtensorMap tm_x;
+  ConvParams params;
+  GemmArgs args;
+  int grid = 0;
+};
+int conv_cin_pad(int cin);
+int conv_cout_pad(int cout);
+// src: the GGUF / torch layout [cout][cin][kh][kw] (taps = kh * kw).
+void launch_conv_weight_layout(const bf16* src, bf16* dst, int cout, int cin, int taps,
+                               cudaStream_t stream);
+// Epilogue EPI_BIAS (out = bf16(bf16(conv) + b)) or EPI_RES (out = bf16(residual
+// + bf16(bf16(conv) + b))). Returns nullptr or a static error message.
+const char* conv_plan(ConvOp* op, const bf16* x, int in_w, int in_h, int cin, int mode,
+                      const bf16* w_laid, int cout, int epilogue, const bf16* bias,
+                      const bf16* residual, bf16* out, int num_sms);
+bool conv_launch(const ConvOp& op, unsigned* error, cudaStream_t stream, bool pdl);
+
 }  // namespace wamb

@@ -23,7 +23,11 @@ class Options(C.Structure):
                 ("synthetic_bias_scale", C.c_float), ("device_index", C.c_int),
                 ("max_batch", C.c_int), ("use_cuda_graphs", C.c_int), ("prompt_cache", C.c_int),
                 ("weight_format", C.c_int), ("ffn_kind", C.c_int), ("norm_kind", C.c_int),
-                ("block_mode", C.c_int)]
+                ("block_mode", C.c_int), ("vae", C.c_int)]
+
+
+class Image(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("w", C.c_int), ("h", C.c_int), ("format", C.c_int)]
 
 
 class BlockInputs(C.Structure):
@@ -36,7 +40,7 @@ class Request(C.Structure):
     _fields_ = [("state", C.POINTER(C.c_float)), ("state_n", C.c_int),
                 ("noise", C.POINTER(C.c_float)), ("ref_latent", C.POINTER(C.c_float)),
                 ("ref_latent_n", C.c_longlong), ("prompt_emb", C.POINTER(C.c_float)),
-                ("prompt_tokens", C.c_int)]
+                ("prompt_tokens", C.c_int), ("images", C.POINTER(Image)), ("n_images", C.c_int)]
 
 
 class Stats(C.Structure):
@@ -63,6 +67,13 @@ def attach(lib, sig) -> None:
     sig(lib, "wam_b200_destroy", None, [vp])
     sig(lib, "wam_b200_reset", i32, [vp])
     sig(lib, "wam_b200_geometry_of", i32, [vp, C.POINTER(Geometry)])
+    sig(lib, "wam_b200_max_batch", i32, [vp])
+    sig(lib, "wam_b200_batcher_create", i32, [vp, i32, C.POINTER(vp), st])
+    sig(lib, "wam_b200_batcher_destroy", None, [vp])
+    sig(lib, "wam_b200_batcher_predict", i32, [vp, C.POINTER(Request), f32p, sz,
+                                               C.POINTER(Stats), C.POINTER(i32), st])
+    sig(lib, "wam_b200_batcher_counts", i32, [vp, C.POINTER(C.c_longlong),
+                                              C.POINTER(C.c_longlong)])
     sig(lib, "wam_b200_predict", i32, [vp, C.POINTER(Request), f32p, sz, C.POINTER(Stats), st])
     sig(lib, "wam_b200_predict_batch", i32,
         [vp, C.POINTER(Request), i32, f32p, sz, C.POINTER(Stats), st])

@@ -15,7 +15,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from ._lib import load
-from ._lib_engine import (GEOM_FIELDS, BlockInputs, Geometry, GraphProfile, OpProfile, Options,
+from ._lib_engine import (Image, GEOM_FIELDS, BlockInputs, Geometry, GraphProfile, OpProfile, Options,
                           Request, Stats, Status)
 
 KINDS = ("gemm", "attention", "layernorm", "qkv_scatter", "small_linear", "elementwise", "sync")
@@ -46,10 +46,14 @@ def geometry_struct(g) -> Geometry:
 
 @dataclass
 class Req:
+    """One request. `latent` is the precomputed VAE latent; with latent None,
+    `images` (three HWC RGB views, uint8 or float32) run the engine's vision
+    front-end (engine created with vae=True)."""
     state: np.ndarray
-    latent: np.ndarray
+    latent: np.ndarray | None
     prompt: np.ndarray
     noise: np.ndarray | None = None
+    images: list | None = None
 
 
 def _f32(a):
@@ -60,7 +64,8 @@ class Engine:
     def __init__(self, geometry=None, seed: int = 0, artifact: str | None = None,
                  bias_scale: float = 0.0, device: int = 0, max_batch: int = 1,
                  graphs: bool = True, prompt_cache: bool = True, weights: str = "bf16",
-                 ffn: str = "gelu", norm: str = "layernorm", block: bool = False):
+                 ffn: str = "gelu", norm: str = "layernorm", block: bool = False,
+                 vae: bool = False):
         """ffn ('gelu' | 'swiglu') and norm ('layernorm' | 'rmsnorm') select the
         config-1 block variants (synthetic weights); block=True creates an engine
         for block_forward (one layer over given hidden states)."""
@@ -84,6 +89,7 @@ class Engine:
         o.ffn_kind = 1 if ffn == "swiglu" else 0
         o.norm_kind = 1 if norm == "rmsnorm" else 0
         o.block_mode = 1 if block else 0
+        o.vae = 1 if vae else 0
         h = C.c_void_p()
         st = Status()
         _raise(self.lib, self.lib.wam_b200_create(C.byref(o), C.byref(h), C.byref(st)), st,
@@ -108,13 +114,25 @@ class Engine:
         arr = (Request * len(reqs))()
         keep = []
         for i, r in enumerate(reqs):
-            s, lat, pr = _f32(r.state), _f32(r.latent), _f32(r.prompt)
-            keep += [s, lat, pr]
+            s, pr = _f32(r.state), _f32(r.prompt)
+            keep += [s, pr]
             fp = C.POINTER(C.c_float)
             arr[i].state = s.ctypes.data_as(fp)
             arr[i].state_n = s.size
-            arr[i].ref_latent = lat.ctypes.data_as(fp)
-            arr[i].ref_latent_n = lat.size
+            if r.latent is not None:
+                lat = _f32(r.latent)
+                keep.append(lat)
+                arr[i].ref_latent = lat.ctypes.data_as(fp)
+                arr[i].ref_latent_n = lat.size
+            if r.images is not None:
+                views = [np.ascontiguousarray(v) for v in r.images]
+                imgs = (Image * len(views))()
+                for j, v in enumerate(views):
+                    imgs[j] = Image(v.ctypes.data, int(v.shape[1]), int(v.shape[0]),
+                                    0 if v.dtype == np.uint8 else 1)
+                keep += views + [imgs]
+                arr[i].images = imgs
+                arr[i].n_images = len(views)
             arr[i].prompt_emb = pr.ctypes.data_as(fp)
             arr[i].prompt_tokens = pr.shape[0] if pr.ndim == 2 else pr.size // self.geometry["text_dim"]
             if r.noise is not None:
@@ -236,3 +254,45 @@ class Engine:
                                            C.byref(st))
         _raise(self.lib, rc, st, "wam_b200_read_tensor")
         return out
+
+
+class Batcher:
+    """The batch-capable serving surface over one engine
+    (wam_b200_batcher_*): predict() may be called from many threads at once;
+    queued requests run together as predict_batch calls of up to the engine's
+    max_batch, waiting at most max_wait_us after the first for more."""
+
+    def __init__(self, engine: Engine, max_wait_us: int = 200):
+        self.engine = engine
+        self.lib = engine.lib
+        self.h = C.c_void_p()
+        st = Status()
+        _raise(self.lib, self.lib.wam_b200_batcher_create(engine.h, max_wait_us, C.byref(self.h),
+                                                          C.byref(st)),
+               st, "wam_b200_batcher_create")
+
+    def predict(self, req: Req):
+        """(action chunk [action_chunk, real_action_dim], batch size it ran in)."""
+        arr, keep = self.engine._requests([req])
+        out = self.engine._out(1)[0]
+        st, s, b = Status(), Stats(), C.c_int()
+        rc = self.lib.wam_b200_batcher_predict(self.h, arr, out.ctypes.data_as(C.POINTER(C.c_float)),
+                                               out.size, C.byref(s), C.byref(b), C.byref(st))
+        _raise(self.lib, rc, st, "wam_b200_batcher_predict")
+        return out, b.value
+
+    def counts(self):
+        nb, nr = C.c_longlong(), C.c_longlong()
+        self.lib.wam_b200_batcher_counts(self.h, C.byref(nb), C.byref(nr))
+        return nb.value, nr.value
+
+    def close(self):
+        if self.h:
+            self.lib.wam_b200_batcher_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -228,3 +228,61 @@ def qkv_scatter(src, heads, rows_per_seq, q_out=None, k_out=None, v_out=None, q_
     rc = load().wam_b200_op_qkv_scatter(C.byref(a), _stream())
     check(rc, "wam_b200_op_qkv_scatter")
     torch.cuda.current_stream().synchronize() if keep else None
+
+
+CONV_3X3, CONV_3X3_S2, CONV_1X1 = 0, 1, 2
+
+
+class ConvWeight:
+    """A [cout, cin, kh, kw] BF16 convolution weight laid out for the implicit-
+    GEMM kernel by wam_b200_op_conv_weight_layout: [cout_pad][taps][cin_pad]."""
+
+    def __init__(self, w):
+        lib = load()
+        _conv_sigs(lib)
+        cout, cin, kh, kw = w.shape
+        taps = kh * kw
+        if (kh, kw) not in ((3, 3), (1, 1)):
+            raise ValueError("conv kernels are 3x3 or 1x1")
+        self.cout, self.cin, self.taps = cout, cin, taps
+        self.data = torch.empty(lib.wam_b200_conv_cout_pad(cout) * taps *
+                                lib.wam_b200_conv_cin_pad(cin), dtype=torch.bfloat16,
+                                device=w.device)
+        rc = lib.wam_b200_op_conv_weight_layout(_ptr(w.contiguous()), _ptr(self.data), cout, cin,
+                                                taps, _stream())
+        check(rc, "wam_b200_op_conv_weight_layout")
+
+
+def _conv_sigs(lib):
+    if getattr(lib, "_conv_sigs", False):
+        return
+    vp, i32 = C.c_void_p, C.c_int
+    lib.wam_b200_conv_cin_pad.restype = i32
+    lib.wam_b200_conv_cin_pad.argtypes = [i32]
+    lib.wam_b200_conv_cout_pad.restype = i32
+    lib.wam_b200_conv_cout_pad.argtypes = [i32]
+    lib.wam_b200_op_conv_weight_layout.restype = i32
+    lib.wam_b200_op_conv_weight_layout.argtypes = [vp, vp, i32, i32, i32, vp]
+    lib.wam_b200_op_conv2d.restype = i32
+    lib.wam_b200_op_conv2d.argtypes = [vp, i32, i32, i32, i32, vp, i32, i32, vp, vp, vp, vp, vp]
+    lib._conv_sigs = True
+
+
+def conv2d(x, w: ConvWeight, mode: int, bias=None, residual=None, out=None, error=None):
+    """NHWC BF16 convolution x [H, W, cin] -> [H', W', cout] (mode CONV_3X3,
+    CONV_3X3_S2 or CONV_1X1); with `residual` the epilogue adds it (EPI_RES)."""
+    lib = load()
+    _conv_sigs(lib)
+    h, wd, cin = x.shape
+    if cin != w.cin or (w.taps == 1) != (mode == CONV_1X1):
+        raise ValueError("conv: weight does not match the input / mode")
+    oh, ow = (h // 2, wd // 2) if mode == CONV_3X3_S2 else (h, wd)
+    if out is None:
+        out = torch.empty((oh, ow, w.cout), dtype=torch.bfloat16, device=x.device)
+    if error is None:
+        error = torch.zeros(1, dtype=torch.int32, device=x.device)
+    rc = lib.wam_b200_op_conv2d(_ptr(x.contiguous()), wd, h, cin, mode, _ptr(w.data), w.cout,
+                                EPI_RES if residual is not None else EPI_BIAS, _ptr(bias),
+                                _ptr(residual), _ptr(out), _ptr(error), _stream())
+    check(rc, "wam_b200_op_conv2d")
+    return out
