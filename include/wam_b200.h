@@ -282,6 +282,12 @@ typedef struct wam_b200_options {
    * tensors and gwp05.vae_latents_{mean,std} of the artifact, or synthetic
    * weights from synthetic_seed) so that requests may carry camera images. */
   int vae;
+  /* 1 loads the UMT5 text encoder (the t5.* tensors and gwp05.t5_* geometry of
+   * the artifact; synthetic: hidden = text_dim, 64-dim heads, max tokens =
+   * prompt_tokens and the three sizes below) so that requests may carry prompt
+   * token ids (the reference's resident language-encoder policy). */
+  int t5;
+  int t5_vocab, t5_ffn, t5_layers;
 } wam_b200_options;
 
 /* A camera view (ImageView, src/models/gwp05/engine/engine.h:82-89): host (or,
@@ -313,6 +319,14 @@ typedef struct wam_b200_request {
    * engine.cpp:260-270); needs an engine created with vae = 1. */
   const wam_b200_image* images;
   int n_images;
+  /* ABI 2: with prompt_emb NULL, the prompt token ids [n_lang] (and optional
+   * attention mask [attention_mask_n], a contiguous valid prefix of ones) run
+   * the UMT5 encoder on the device (run_t5, engine/text_encoder.cpp:112-204);
+   * needs an engine created with t5 = 1. */
+  const int32_t* lang_tokens;
+  int n_lang;
+  const int32_t* attention_mask;
+  int attention_mask_n;
 } wam_b200_request;
 
 typedef struct wam_b200_stats {
@@ -531,7 +545,8 @@ WAM_B200_API int wam_b200_vae_encode(wam_b200_vae* vae, const wam_b200_image* im
                                      int image_count, float* latent, size_t latent_n,
                                      wam_b200_status* status);
 /* Encoder only, device pointers: pixels [12][H/2][W/2] F32 (stage 1 output),
- * latent [z][H/16][W/16] F32; asynchronous on `stream` (NULL: the VAE's own). */
+ * latent [z][H/16][W/16] F32; asynchronous on `stream` (NULL: the legacy
+ * default stream). */
 WAM_B200_API int wam_b200_vae_encode_device(wam_b200_vae* vae, const float* pixels,
                                             float* latent, void* stream,
                                             wam_b200_status* status);
@@ -539,6 +554,46 @@ WAM_B200_API int wam_b200_vae_encode_device(wam_b200_vae* vae, const float* pixe
  * "mid", "moments") of the last encode, for parity checks. */
 WAM_B200_API int wam_b200_vae_read_stage(wam_b200_vae* vae, const char* name, float* out,
                                          size_t n, int* h, int* w, int* c);
+
+/* ---------------------------------------------------------------- UMT5
+ * The UMT5 text encoder (the reference's run_t5, src/models/gwp05/engine/
+ * text_encoder.cpp:112-204): prompt token ids -> prompt embedding
+ * [max_tokens][hidden] F32 (rows past the valid prompt zero), the input of the
+ * prompt projection when the language encoder is resident. Weights: the t5.*
+ * tensors of a GGUF artifact (BF16; geometry from gwp05.t5_*), or synthetic
+ * from synthetic_seed and the geometry below. */
+typedef struct wam_b200_t5 wam_b200_t5;
+typedef struct wam_b200_t5_options {
+  uint32_t struct_size; /* sizeof(wam_b200_t5_options) */
+  const char* artifact_path;
+  uint64_t synthetic_seed;
+  int vocab, hidden, ffn, heads, head_dim, layers; /* synthetic geometry (head_dim 64) */
+  int max_tokens;                                  /* n_lang (semantics: 512 at config 2) */
+  int device_index;
+  int use_cuda_graphs;
+} wam_b200_t5_options;
+WAM_B200_API int wam_b200_t5_create(const wam_b200_t5_options* options, wam_b200_t5** t5,
+                                    wam_b200_status* status);
+WAM_B200_API void wam_b200_t5_destroy(wam_b200_t5* t5);
+/* Geometry actually loaded (from the artifact when one is given). */
+WAM_B200_API int wam_b200_t5_geometry(const wam_b200_t5* t5, int* vocab, int* hidden, int* ffn,
+                                      int* heads, int* layers, int* max_tokens);
+/* run_t5 with the reference's input checks (validate_prompt_mask,
+ * text_encoder.cpp:74-109): tokens [n_lang] with 1 <= n_lang <= max_tokens,
+ * optional mask [mask_n == n_lang] of 0/1 forming a contiguous valid prefix;
+ * the valid prefix is encoded. out: host [max_tokens * hidden]. Synchronous. */
+WAM_B200_API int wam_b200_t5_encode(wam_b200_t5* t5, const int32_t* tokens, int n_lang,
+                                    const int32_t* mask, int mask_n, float* out, size_t out_n,
+                                    wam_b200_status* status);
+/* The same into device memory, asynchronous on `stream` (NULL: the legacy
+ * default stream). */
+WAM_B200_API int wam_b200_t5_encode_device(wam_b200_t5* t5, const int32_t* tokens, int n_lang,
+                                           const int32_t* mask, int mask_n, float* out_device,
+                                           void* stream, wam_b200_status* status);
+/* FLOPs and kernel launches of one encode of n valid tokens. */
+WAM_B200_API int wam_b200_t5_info(wam_b200_t5* t5, int n, double* flops, int* launches);
+/* relative_position_bucket (text_encoder.cpp:14-24), for parity checks. */
+WAM_B200_API int wam_b200_t5_relative_bucket(int relative, int buckets, int max_distance);
 
 #ifdef __cplusplus
 }

@@ -87,6 +87,10 @@ def lib():
         l.oracle_block.restype = C.c_int
         l.oracle_block.argtypes = [C.c_void_p, C.c_int, C.c_float] + [f32p] * 6
         i32p = C.POINTER(C.c_int)
+        l.oracle_t5_encode.restype = C.c_int
+        l.oracle_t5_encode.argtypes = [C.POINTER(C.c_char_p), C.POINTER(C.c_void_p), C.c_int,
+                                       C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                       C.POINTER(C.c_int32), C.c_int, C.c_int, f32p]
         l.oracle_vae_encode.restype = C.c_int
         l.oracle_vae_encode.argtypes = [C.POINTER(C.c_char_p), C.POINTER(C.c_void_p), C.c_int,
                                         f32p, f32p, C.c_int, f32p, C.c_int, C.c_int, f32p,
@@ -140,6 +144,23 @@ def compose_and_patchify(views, out_w: int, out_h: int, reference: bool = False)
         rc = lib().oracle_compose_and_patchify(d, w, h, f, out_w, out_h, _fp(out))
     if rc != 0:
         raise ValueError("compose_and_patchify rejected its inputs")
+    return out
+
+
+def t5_encode(weights: dict, g, tokens, max_tokens: int):
+    """UMT5 encoder (oracle/t5.cpp): tokens [n] -> [max_tokens][hidden] F32.
+    g: wam_b200.text.T5Geometry-like (hidden, heads, head_dim, ffn, layers, vocab)."""
+    names = list(weights)
+    arrs = [np.ascontiguousarray(weights[n], dtype=np.uint16) for n in names]
+    cn = (C.c_char_p * len(names))(*[n.encode() for n in names])
+    ct = (C.c_void_p * len(names))(*[a.ctypes.data for a in arrs])
+    tok = np.ascontiguousarray(tokens, np.int32)
+    out = np.zeros((max_tokens, g.hidden), np.float32)
+    rc = lib().oracle_t5_encode(cn, ct, len(names), g.hidden, g.heads, g.head_dim, g.ffn, g.layers,
+                                g.vocab, tok.ctypes.data_as(C.POINTER(C.c_int32)), tok.size,
+                                max_tokens, _fp(out))
+    if rc != 0:
+        raise ValueError(f"oracle_t5_encode failed ({rc})")
     return out
 
 

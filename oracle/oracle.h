@@ -111,6 +111,12 @@ int oracle_compose_and_patchify(const void* const* data, const int* w, const int
  * intermediate ("conv_in", "down0".."down3", "mid", "moments") its NHWC values
  * go to stage_out and its (h, w, c) to stage_dims. Returns non-zero on bad
  * input (2: a tensor is missing). */
+/* UMT5 encoder (t5.cpp) over n valid tokens with BF16 weights by compact name;
+ * out [max_tokens][hidden] (rows >= n zero). Non-zero on bad input. */
+int oracle_t5_encode(const char* const* names, const uint16_t* const* tensors, int n_tensors,
+                     int hidden, int heads, int head_dim, int ffn, int layers, int vocab,
+                     const int32_t* tokens, int n, int max_tokens, float* out);
+
 int oracle_vae_encode(const char* const* names, const uint16_t* const* tensors, int n_tensors,
                       const float* mean, const float* stdv, int z, const float* pixels, int width,
                       int height, float* latent, const char* stage, float* stage_out,

@@ -219,3 +219,26 @@ def make_vae_weights(seed: int, z_dim: int = 48) -> dict[str, np.ndarray]:
             scale, center = 0.02, 1.0
         out[name] = synth_bits(seed, name, n, scale, center).reshape(shape)
     return out
+
+
+def make_t5_weights(seed: int, g) -> dict[str, np.ndarray]:
+    """The synthetic UMT5 weights of csrc/t5.cu (load_weights): linear maps
+    N(0, 1 / fan_in) (q also / sqrt(head_dim)), embedding N(0, 1), relative
+    position bias N(0, 0.5), RMS gains 1 + N(0, 0.02)."""
+    from wam_b200.text import t5_tensor_specs
+
+    out = {}
+    for name, shape in t5_tensor_specs(g):
+        n = int(np.prod(shape))
+        if name.endswith("norm.weight"):
+            scale, center = 0.02, 1.0
+        elif name == "t5.token_embd.weight":
+            scale, center = 1.0, 0.0
+        elif name.endswith(".rel.weight"):
+            scale, center = 0.5, 0.0
+        else:
+            scale, center = 1.0 / float(np.sqrt(float(shape[1]))), 0.0
+            if name.endswith(".sa.q.weight"):
+                scale /= float(np.sqrt(float(g.head_dim)))
+        out[name] = synth_bits(seed, name, n, scale, center).reshape(shape)
+    return out

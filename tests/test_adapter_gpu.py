@@ -146,3 +146,39 @@ def test_engine_vtable_predict_from_images(cuda_device):
         Req(r.state, None, r.prompt, r.noise, images=views))
     assert np.array_equal(out.reshape(ref.shape), ref)
     lib.wam_b200_adapter_destroy(e)
+
+
+def test_engine_vtable_predict_from_tokens(cuda_device):
+    """EngineInputsView with prompt token ids (and a padded mask) and no
+    precomputed embedding: the adapter reports the resident language-encoder
+    policy and its chunk equals the C ABI engine's from the same tokens."""
+    from oracle import synth
+    from wam_b200.engine import Engine, Req
+
+    lib = _lib()
+    i32p = C.POINTER(C.c_int32)
+    lib.wam_b200_adapter_predict_tokens.restype = C.c_longlong
+    lib.wam_b200_adapter_predict_tokens.argtypes = [
+        C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_float), C.c_int, i32p, C.c_int, i32p,
+        C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_float), C.c_longlong]
+    g = synth.TINY
+    o = _options(g)
+    o.t5, o.t5_vocab, o.t5_ffn, o.t5_layers = 1, 1000, 256, 2
+    e = lib.wam_b200_adapter_create(C.byref(o))
+    assert e
+    r = synth.make_request(g, 8)
+    tok = np.concatenate([np.random.default_rng(1).integers(0, 1000, 9), np.zeros(4)]).astype(np.int32)
+    mask = np.array([1] * 9 + [0] * 4, np.int32)
+    out = np.zeros(g.action_chunk * g.real_action_dim, np.float32)
+    st = np.ascontiguousarray(r.state, np.float32)
+    lat = np.ascontiguousarray(r.latent, np.float32)
+    nz = np.ascontiguousarray(r.noise, np.float32)
+    n = lib.wam_b200_adapter_predict_tokens(e, _fp(st), _fp(lat), lat.size,
+                                            tok.ctypes.data_as(i32p), tok.size,
+                                            mask.ctypes.data_as(i32p), mask.size, _fp(nz),
+                                            _fp(out), out.size)
+    assert n == out.size
+    ref = Engine(g, seed=SEED, bias_scale=0.02, t5=True, t5_vocab=1000, t5_ffn=256,
+                 t5_layers=2).predict(Req(r.state, r.latent, None, r.noise, tokens=tok[:9]))
+    assert np.array_equal(out.reshape(ref.shape), ref)
+    lib.wam_b200_adapter_destroy(e)

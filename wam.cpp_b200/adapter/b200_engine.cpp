@@ -4,6 +4,8 @@
 // virtual call on the reference's Engine type.
 #include "b200_engine.h"
 
+#include <cstddef>
+
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -19,7 +21,7 @@ void log_status(const char* what, wam_b200_status* st) {
 
 }  // namespace
 
-B200Engine::B200Engine(wam_b200_engine* handle) : h_(handle) {
+B200Engine::B200Engine(wam_b200_engine* handle, bool text_encoder) : h_(handle) {
   wam_b200_geometry_of(h_, &g_);
   // Config (engine.h:40-80) as the reference's loader fills it for this geometry.
   cfg.n_img = static_cast<std::int64_t>(g_.grid_h) * g_.grid_w;
@@ -55,8 +57,9 @@ B200Engine::B200Engine(wam_b200_engine* handle) : h_(handle) {
   cfg.num_embodiments = g_.num_embodiments;
   cfg.embodiment_id = g_.embodiment_id;
   cfg.flow_shift = g_.flow_shift;
-  language_encoder_policy = LanguageEncoderPolicy::external_embedding;
-  text_encoder_resident = false;  // resident_device_bytes: reported by every predict
+  language_encoder_policy =
+      text_encoder ? LanguageEncoderPolicy::resident : LanguageEncoderPolicy::external_embedding;
+  text_encoder_resident = text_encoder;  // resident_device_bytes: reported by every predict
 }
 
 B200Engine::~B200Engine() {
@@ -83,9 +86,11 @@ std::vector<float> B200Engine::predict(const EngineInputsView& in) {
                                 in.images[i].format == PixelFormat::U8 ? WAM_B200_PIXEL_U8
                                                                        : WAM_B200_PIXEL_F32_RGB_01};
   }
-  if (!in.precomputed_prompt_emb) {
-    std::fprintf(stderr, "wam(b200): a precomputed prompt embedding is required (external_embedding "
-                         "policy)\n");
+  // Without a precomputed prompt embedding the token ids go to the engine's
+  // resident UMT5 encoder (run_t5, text_encoder.cpp:112-204).
+  if (!in.precomputed_prompt_emb && !in.lang_tokens) {
+    std::fprintf(stderr, "wam(b200): a precomputed prompt embedding or prompt token ids are "
+                         "required\n");
     return {};
   }
   wam_b200_request r{};
@@ -99,6 +104,12 @@ std::vector<float> B200Engine::predict(const EngineInputsView& in) {
   if (from_images) {
     r.images = views;
     r.n_images = 3;
+  }
+  if (!in.precomputed_prompt_emb) {
+    r.lang_tokens = in.lang_tokens;
+    r.n_lang = in.n_lang;
+    r.attention_mask = in.attention_mask;
+    r.attention_mask_n = in.attention_mask_n;
   }
   std::vector<float> out(static_cast<size_t>(g_.action_chunk) * g_.real_action_dim);
   wam_b200_stats s{};
@@ -133,7 +144,8 @@ std::unique_ptr<Engine> create_b200_synthetic(const wam_b200_options& options) {
     return nullptr;
   }
   wam_b200_status_free(&st);
-  return std::make_unique<B200Engine>(h);
+  return std::make_unique<B200Engine>(
+      h, options.struct_size >= offsetof(wam_b200_options, t5) + sizeof(int) && options.t5 != 0);
 }
 
 std::unique_ptr<Engine> create_b200(const ArtifactContract& artifact, const EngineOptions& options,
@@ -146,6 +158,7 @@ std::unique_ptr<Engine> create_b200(const ArtifactContract& artifact, const Engi
   o.use_cuda_graphs = 1;
   o.prompt_cache = options.prompt_cache_capacity > 0 ? 1 : 0;
   o.vae = 1;  // the artifact contract carries the VAE (artifact.cpp:159), so images work
+  o.t5 = 1;   // ... and UMT5 (resident language-encoder policy: token ids work)
   auto e = create_b200_synthetic(o);
   if (!e) return nullptr;
   const Geometry& a = artifact.geometry;
@@ -215,6 +228,26 @@ __attribute__((visibility("default"))) long long wam_b200_adapter_predict_images
   in.n_images = 3;
   in.precomputed_prompt_emb = prompt;
   in.precomputed_prompt_tokens = prompt_tokens;
+  in.noise = noise;
+  std::vector<float> r = static_cast<Engine*>(e)->predict(in);
+  if (static_cast<long long>(r.size()) > out_n) return -1;
+  std::memcpy(out, r.data(), r.size() * sizeof(float));
+  return static_cast<long long>(r.size());
+}
+
+// Engine::predict with prompt token ids (and an optional mask) instead of a
+// prompt embedding: the resident UMT5 path.
+__attribute__((visibility("default"))) long long wam_b200_adapter_predict_tokens(
+    void* e, const float* state, const float* latent, int latent_n, const int32_t* tokens,
+    int n_lang, const int32_t* mask, int mask_n, const float* noise, float* out, long long out_n) {
+  wam::internal::gwp05::engine::EngineInputsView in{};
+  in.state = state;
+  in.precomputed_ref_latent = latent;
+  in.precomputed_ref_latent_n = latent_n;
+  in.lang_tokens = tokens;
+  in.n_lang = n_lang;
+  in.attention_mask = mask;
+  in.attention_mask_n = mask_n;
   in.noise = noise;
   std::vector<float> r = static_cast<Engine*>(e)->predict(in);
   if (static_cast<long long>(r.size()) > out_n) return -1;

@@ -21,8 +21,8 @@ class B200Engine final : public Engine {
  public:
   // Takes ownership of an engine created through the C ABI and fills the
   // public telemetry (cfg, resident_device_bytes, language_encoder_policy)
-  // from its geometry.
-  explicit B200Engine(wam_b200_engine* handle);
+  // from its geometry; text_encoder: the engine was created with UMT5 (t5 = 1).
+  explicit B200Engine(wam_b200_engine* handle, bool text_encoder = false);
   ~B200Engine() override;
   B200Engine(const B200Engine&) = delete;
   B200Engine& operator=(const B200Engine&) = delete;
@@ -30,8 +30,9 @@ class B200Engine final : public Engine {
   // Engine::predict (engine.cpp:230-449): de-normalised [action_chunk *
   // real_action_dim] actions, or {} on failure with the reason on stderr (the
   // model layer turns {} into inference_failed, model.cpp:240-245). Takes the
-  // precomputed reference latent and prompt embedding of the
-  // external_embedding policy; raw images and token ids are not accepted.
+  // precomputed reference latent or the three camera views (vision front-end
+  // on the device), and the precomputed prompt embedding or the prompt token
+  // ids (UMT5 on the device, when the engine was created with it).
   std::vector<float> predict(const EngineInputsView& inputs) override;
   // Engine::reset: drops the projected-prompt cache.
   void reset() override;

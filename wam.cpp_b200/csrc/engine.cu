@@ -23,6 +23,7 @@
 
 #include "gguf.h"
 #include "host_math.h"
+#include "t5.h"
 #include "vae.h"
 
 namespace wamb {
@@ -201,6 +202,7 @@ MotEngine::~MotEngine() {
   if (side_) cudaStreamSynchronize(side_);
   if (stream_) cudaStreamSynchronize(stream_);
   vae_.reset();
+  t5_.reset();
   drop_plans();
   for (auto& e : phase_ev_)
     if (e) cudaEventDestroy(e);
@@ -289,8 +291,37 @@ bool MotEngine::init(const EngineOptions& opt, std::string* err) {
       return false;
     }
   }
+  if (opt.t5) {
+    if (opt.block) {
+      *err = "block engines take hidden states, not prompt tokens (t5 must be 0)";
+      return false;
+    }
+    T5Options to;
+    to.artifact_path = opt.artifact_path;
+    to.synthetic_seed = opt.seed;
+    to.geometry.vocab = opt.t5_vocab;
+    to.geometry.hidden = g.text_dim;
+    to.geometry.ffn = opt.t5_ffn;
+    to.geometry.heads = g.text_dim / 64;
+    to.geometry.head_dim = 64;
+    to.geometry.layers = opt.t5_layers;
+    to.geometry.max_tokens = g.prompt_tokens;
+    to.device_index = opt.device;
+    to.use_cuda_graph = opt.graphs;
+    t5_.reset(new T5Encoder());
+    std::string terr;
+    if (!t5_->init(to, &terr)) {
+      *err = "UMT5 encoder: " + terr;
+      return false;
+    }
+    if (t5_->geometry().hidden != g.text_dim) {
+      *err = "UMT5 encoder: t5_hidden differs from the prompt width (text_dim)";
+      return false;
+    }
+  }
   CK(cudaStreamSynchronize(stream_));
-  prompt_sig_.assign(opt.max_batch, {});
+  prompt_key_.assign(opt.max_batch, {});
+  in_prompt_key_.assign(opt.max_batch, {});
   ok_ = true;
   return true;
 }
@@ -1443,6 +1474,7 @@ bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
   }
   const int A = g.action_dim, T = g.action_chunk, Nt = g.prompt_tokens, D = g.text_dim;
   const long long lat = static_cast<long long>(g.vae_z) * 4 * g.visual();
+  staged_keys_.assign(batch, {});
   for (int i = 0; i < batch; ++i) {
     const RequestView& r = reqs[i];
     if (!r.state || r.state_n < g.real_state_dim) {
@@ -1468,7 +1500,27 @@ bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
       *err = "reference latent must have vae_z * (2 grid_h) * (2 grid_w) values";
       return false;
     }
-    if (!r.prompt || r.prompt_tokens < 1 || r.prompt_tokens > Nt) {
+    std::vector<uint8_t>& key = staged_keys_[i];
+    if (!r.prompt && r.tokens) {
+      if (!t5_) {
+        *err = "prompt token ids need an engine created with the UMT5 encoder (options.t5 = 1)";
+        return false;
+      }
+      std::string why;
+      const int valid = t5_valid_tokens(r.n_tokens, r.mask, r.mask_n, Nt, &why);
+      if (valid < 0) {
+        *err = why;
+        return false;
+      }
+      for (int j = 0; j < valid; ++j)
+        if (r.tokens[j] < 0 || r.tokens[j] >= t5_->geometry().vocab) {
+          *err = "token " + std::to_string(r.tokens[j]) + " is outside T5 vocabulary";
+          return false;
+        }
+      key.assign(1, 'T');
+      const uint8_t* tb = reinterpret_cast<const uint8_t*>(r.tokens);
+      key.insert(key.end(), tb, tb + static_cast<size_t>(valid) * 4);
+    } else if (!r.prompt || r.prompt_tokens < 1 || r.prompt_tokens > Nt) {
       *err = "prompt embedding must have 1..prompt_tokens rows";
       return false;
     }
@@ -1482,10 +1534,15 @@ bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
           return false;
         }
     }
-    float* pr = h_prompt_ + static_cast<size_t>(i) * Nt * D;
-    std::memcpy(pr, r.prompt, static_cast<size_t>(r.prompt_tokens) * D * 4);
-    std::memset(pr + static_cast<size_t>(r.prompt_tokens) * D, 0,
-                static_cast<size_t>(Nt - r.prompt_tokens) * D * 4);
+    if (r.prompt) {
+      float* pr = h_prompt_ + static_cast<size_t>(i) * Nt * D;
+      std::memcpy(pr, r.prompt, static_cast<size_t>(r.prompt_tokens) * D * 4);
+      std::memset(pr + static_cast<size_t>(r.prompt_tokens) * D, 0,
+                  static_cast<size_t>(Nt - r.prompt_tokens) * D * 4);
+      key.assign(1, 'E');
+      const uint8_t* pb = reinterpret_cast<const uint8_t*>(pr);
+      key.insert(key.end(), pb, pb + static_cast<size_t>(Nt) * D * 4);
+    }
     float* nz = h_noise_ + static_cast<size_t>(i) * T * A;
     if (r.noise) {
       std::memcpy(nz, r.noise, static_cast<size_t>(T) * A * 4);
@@ -1515,7 +1572,26 @@ bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
       }
     }
   }
-  CK(cudaMemcpyAsync(in_prompt_, h_prompt_, static_cast<size_t>(batch) * Nt * D * 4, cudaMemcpyHostToDevice, stream_));
+  // Prompt embeddings: copied from the host, or (token ids) made by UMT5 on the
+  // device, skipped when the slot already holds that prompt's embedding.
+  for (int i = 0; i < batch; ++i) {
+    const size_t pn = static_cast<size_t>(Nt) * D;
+    if (reqs[i].prompt) {
+      CK(cudaMemcpyAsync(in_prompt_ + i * pn, h_prompt_ + i * pn, pn * 4, cudaMemcpyHostToDevice,
+                         stream_));
+      in_prompt_key_[i].clear();
+    } else if (in_prompt_key_[i] != staged_keys_[i]) {
+      std::string terr;
+      const int valid = static_cast<int>((staged_keys_[i].size() - 1) / 4);
+      if (!t5_->encode(reinterpret_cast<const int32_t*>(staged_keys_[i].data() + 1), valid,
+                       in_prompt_ + i * pn, stream_, &terr)) {
+        *err = "UMT5 encoder: " + terr;
+        in_prompt_key_[i].clear();
+        return false;
+      }
+      in_prompt_key_[i] = staged_keys_[i];
+    }
+  }
   CK(cudaMemcpyAsync(in_noise_, h_noise_, static_cast<size_t>(batch) * T * A * 4, cudaMemcpyHostToDevice, stream_));
   staged_batch_ = batch;
   return true;
@@ -1536,10 +1612,8 @@ bool MotEngine::run(int batch, std::string* err, EngineStats* stats) {
   // slot's prompt equals the one projected last time.
   bool hit = opt_.prompt_cache && prompt_valid_;
   const size_t pn = static_cast<size_t>(g_.prompt_tokens) * g_.text_dim;
-  for (int i = 0; i < batch && hit; ++i) {
-    const std::vector<float>& sig = prompt_sig_[i];
-    hit = sig.size() == pn && std::memcmp(sig.data(), h_prompt_ + i * pn, pn * 4) == 0;
-  }
+  for (int i = 0; i < batch && hit; ++i) hit = prompt_key_[i] == staged_keys_[i];
+  (void)pn;
   auto exec = [&](int which) -> bool {
     if (plan.graph[which]) {
       CK(cudaGraphLaunch(plan.graph[which], stream_));
@@ -1555,8 +1629,8 @@ bool MotEngine::run(int batch, std::string* err, EngineStats* stats) {
   if (!hit) {
     if (!exec(0)) return false;
     if (opt_.prompt_cache) {
-      for (int i = 0; i < batch; ++i) prompt_sig_[i].assign(h_prompt_ + i * pn, h_prompt_ + (i + 1) * pn);
-      for (int i = batch; i < opt_.max_batch; ++i) prompt_sig_[i].clear();
+      for (int i = 0; i < batch; ++i) prompt_key_[i] = staged_keys_[i];
+      for (int i = batch; i < opt_.max_batch; ++i) prompt_key_[i].clear();
       prompt_valid_ = true;
     }
   }
@@ -1771,7 +1845,7 @@ void MotEngine::reset() {
   // Session reset (Gwp05ModelArch::reset, engine.cpp:89-97): forget the
   // projected prompt so the next request re-projects it.
   prompt_valid_ = false;
-  for (auto& s : prompt_sig_) s.clear();
+  for (auto& s : prompt_key_) s.clear();
 }
 
 bool MotEngine::read_tensor(const std::string& name, int slot, int layer, float* out, size_t n,

@@ -50,6 +50,11 @@ struct EngineOptions {
   // Vision front-end: load the Wan VAE encoder so that requests may carry the
   // three camera views instead of a precomputed latent.
   bool vae = false;
+  // Resident language encoder: load UMT5 so that requests may carry prompt
+  // token ids instead of a precomputed prompt embedding (synthetic geometry:
+  // hidden = text_dim, 64-dim heads, max tokens = prompt_tokens, these sizes).
+  bool t5 = false;
+  int t5_vocab = 256384, t5_ffn = 10240, t5_layers = 24;
 };
 
 struct RequestView {
@@ -64,6 +69,11 @@ struct RequestView {
   // encoder write the latent on the device.
   PreprocessView images[3] = {};
   int n_images = 0;
+  // Prompt token ids used when prompt is null (UMT5 on the device).
+  const int32_t* tokens = nullptr;
+  int n_tokens = 0;
+  const int32_t* mask = nullptr;
+  int mask_n = 0;
 };
 
 struct EngineStats {
@@ -120,6 +130,7 @@ int64_t linear_inner(const std::string& name, const Geometry& g);
 uint64_t tensor_seed(uint64_t seed, const std::string& name);
 
 class VaeEncoder;
+class T5Encoder;
 
 class MotEngine {
  public:
@@ -265,7 +276,11 @@ class MotEngine {
   std::vector<float> timesteps_, sigmas_;
   std::map<int, std::unique_ptr<Plan>> plans_;
   std::unique_ptr<VaeEncoder> vae_;  // vision front-end (options.vae)
-  std::vector<std::vector<float>> prompt_sig_;  // per slot, last projected prompt
+  std::unique_ptr<T5Encoder> t5_;    // resident language encoder (options.t5)
+  // Prompt cache keys per batch slot: 'E' + embedding bytes, or 'T' + the
+  // valid token ids; staged_keys_ are those of the staged batch.
+  std::vector<std::vector<uint8_t>> prompt_key_, staged_keys_;
+  std::vector<std::vector<uint8_t>> in_prompt_key_;  // token prompt held in in_prompt_ per slot
   bool prompt_valid_ = false;
   int staged_batch_ = 0;
   std::mt19937 rng_{0x5eed};

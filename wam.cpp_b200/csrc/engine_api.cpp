@@ -72,6 +72,10 @@ std::vector<wamb::RequestView> views(const wam_b200_request* r, int n) {
     v[i].prompt = r[i].prompt_emb;
     v[i].prompt_tokens = r[i].prompt_tokens;
     v[i].n_images = r[i].images ? r[i].n_images : 0;
+    v[i].tokens = r[i].lang_tokens;
+    v[i].n_tokens = r[i].n_lang;
+    v[i].mask = r[i].attention_mask;
+    v[i].mask_n = r[i].attention_mask_n;
     for (int j = 0; j < 3 && j < v[i].n_images; ++j)
       v[i].images[j] = wamb::PreprocessView{r[i].images[j].data, r[i].images[j].w,
                                             r[i].images[j].h, r[i].images[j].format};
@@ -126,6 +130,12 @@ WAM_B200_API int wam_b200_create(const wam_b200_options* o, wam_b200_engine** ou
                   "ffn_kind / norm_kind / block_mode apply to synthetic weights only");
   }
   if (o->struct_size >= offsetof(wam_b200_options, vae) + sizeof(int)) eo.vae = o->vae != 0;
+  if (o->struct_size >= offsetof(wam_b200_options, t5_layers) + sizeof(int)) {
+    eo.t5 = o->t5 != 0;
+    if (o->t5_vocab > 0) eo.t5_vocab = o->t5_vocab;
+    if (o->t5_ffn > 0) eo.t5_ffn = o->t5_ffn;
+    if (o->t5_layers > 0) eo.t5_layers = o->t5_layers;
+  }
   std::string err;
   auto e = wamb::MotEngine::create(eo, &err);
   if (!e) {

@@ -1707,7 +1707,7 @@ cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream) {
   cudaLaunchAttribute attr[2];
   int na = 0;
   attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[na].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+  attr[na].val.programmaticStreamSerializationAllowed = (g_pdl && !op.weights_from_prev) ? 1 : 0;
   ++na;
   if (op.args.splits > 1 && op.args.split_mode != SPLIT_WORKSPACE) {
     attr[na].id = cudaLaunchAttributeClusterDimension;

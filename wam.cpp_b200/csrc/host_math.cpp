@@ -81,6 +81,47 @@ void postprocess_action(const float* action, int steps, int padded, int real, co
     }
 }
 
+int t5_valid_tokens(int n_lang, const int32_t* mask, int mask_n, int max_tokens, std::string* why) {
+  if (n_lang < 1 || n_lang > max_tokens) {
+    *why = "lang token count " + std::to_string(n_lang) + " outside [1," + std::to_string(max_tokens) + "]";
+    return -1;
+  }
+  if (!mask && mask_n != 0) {
+    *why = "T5 mask length is nonzero without a mask";
+    return -1;
+  }
+  if (mask && mask_n != n_lang) {
+    *why = "T5 mask length " + std::to_string(mask_n) + " does not match token count " +
+           std::to_string(n_lang);
+    return -1;
+  }
+  int valid = n_lang;
+  if (mask) {
+    valid = 0;
+    bool padding = false;
+    for (int i = 0; i < n_lang; ++i) {
+      if (mask[i] != 0 && mask[i] != 1) {
+        *why = "T5 mask values must be zero or one";
+        return -1;
+      }
+      if (mask[i] == 1) {
+        if (padding) {
+          *why = "T5 mask must be a contiguous valid prefix";
+          return -1;
+        }
+        ++valid;
+      } else {
+        padding = true;
+      }
+    }
+  }
+  if (valid == 0) {
+    *why = "T5 mask contains no valid tokens";
+    return -1;
+  }
+  return valid;
+}
+
 }  // namespace wamb
 
 extern "C" {

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cstdint>
+#include <string>
 #include <vector>
 
 namespace wamb {
@@ -21,6 +22,10 @@ void timestep_embedding(float t, int dim, float* out);
 void rope_inv_freq(int mode, float* out64);
 // visual_positions (src/models/gwp05/semantics.cpp:235-257), [gh*gw][3] = (t, h, w).
 void visual_positions(int gh, int gw, int* thw);
+// validate_prompt_mask (src/models/gwp05/engine/text_encoder.cpp:74-109) plus
+// the token-count check of run_t5 (:117-121): the number of valid (leading)
+// tokens of a prompt, or -1 with the reason.
+int t5_valid_tokens(int n_lang, const int32_t* mask, int mask_n, int max_tokens, std::string* why);
 // State normalisation (engine.cpp:249-253, semantics.cpp:154-172): the first
 // n values map to [-1, 1] by the q01/q99 statistics, the rest of the padded
 // vector is zero.

@@ -81,6 +81,11 @@ struct GemmOp {
   bool stream = false;      // gemm_stream_kernel (<= 64 tokens, full K per CTA, no split-K)
   int cluster = 1;          // pair kernel: cluster size (2 x splits)
   int smem_bytes = 0;
+  // The "weights" (B operand) are activations written by earlier kernels of the
+  // stream (attention products as GEMMs): the launch then waits for the
+  // preceding kernel to finish (no programmatic early start), because the GEMM
+  // kernels fetch weight stages before their grid-dependency wait.
+  bool weights_from_prev = false;
 };
 
 // Plans one GEMM: picks the token tile and split-K factor, encodes the TMA

@@ -434,7 +434,7 @@ bool VaeEncoder::load_weights(std::string* err) {
 }
 
 bool VaeEncoder::conv(const Act& x, const std::string& wname, int mode, Act* out,
-                      const Act* residual, std::string* err) {
+                      const Act* residual, std::string* err, const std::string& bias_name) {
   const auto it = wconv_.find(wname + ".weight");
   if (it == wconv_.end()) {
     *err = "VAE: no convolution " + wname;
@@ -445,7 +445,8 @@ bool VaeEncoder::conv(const Act& x, const std::string& wname, int mode, Act* out
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, opt_.device_index);
   const char* e = conv_plan(&op, x.p, x.w, x.h, x.c, mode, it->second, cout,
-                            residual ? EPI_RES : EPI_BIAS, w_[wname + ".bias"],
+                            residual ? EPI_RES : EPI_BIAS,
+                            w_[bias_name.empty() ? wname + ".bias" : bias_name],
                             residual ? residual->p : nullptr, out->p, sms);
   if (e) {
     *err = std::string("VAE ") + wname + ": " + e;
@@ -469,7 +470,8 @@ void VaeEncoder::rms(const Act& x, const std::string& gamma, bool silu_on, Act* 
 }
 
 bool VaeEncoder::gemm(const bf16* x, int ldx, int m, const bf16* w, int n, int k, int epi,
-                      const bf16* bias, const bf16* residual, void* out, std::string* err) {
+                      const bf16* bias, const bf16* residual, void* out, std::string* err,
+                      bool weights_from_prev) {
   GemmScratch sc;
   sc.workspace = gemm_ws_;
   sc.workspace_floats = gemm_ws_floats_;
@@ -485,6 +487,7 @@ bool VaeEncoder::gemm(const bf16* x, int ldx, int m, const bf16* w, int n, int k
     *err = std::string("VAE attention GEMM: ") + e;
     return false;
   }
+  op.weights_from_prev = weights_from_prev;
   flops_ += 2.0 * m * n * static_cast<double>(k);
   program_.push_back([op](cudaStream_t s) { return gemm_launch(op, s) == cudaSuccess; });
   return true;
@@ -570,7 +573,7 @@ bool VaeEncoder::mid_attention(const Act& x, Act* out, std::string* err) {
             v, err))
     return false;
   // scores = q k^T (F32, GGML_PREC_F32), softmax(scores / sqrt(C)) (vae.cpp:262-265).
-  if (!gemm(q, C, T, k, T, C, EPI_F32_OUT, nullptr, nullptr, scores, err)) return false;
+  if (!gemm(q, C, T, k, T, C, EPI_F32_OUT, nullptr, nullptr, scores, err, true)) return false;
   const float scale = 1.0f / std::sqrt(static_cast<float>(C));
   const int cols = T;
   program_.push_back([scores, probs, cols, scale](cudaStream_t s) {
@@ -583,7 +586,7 @@ bool VaeEncoder::mid_attention(const Act& x, Act* out, std::string* err) {
     return cudaGetLastError() == cudaSuccess;
   });
   // attended = probs v (F32 out, cast to BF16 for the projection).
-  if (!gemm(probs, T, T, vt, C, T, EPI_BIAS, nullptr, nullptr, o, err)) return false;
+  if (!gemm(probs, T, T, vt, C, T, EPI_BIAS, nullptr, nullptr, o, err, true)) return false;
   *out = act(x.h, x.w, C, err);
   if (!out->p) return false;
   // proj + residual (vae.cpp:268-276).
@@ -652,12 +655,24 @@ bool VaeEncoder::build(std::string* err) {
       !resnet("vae.enc.mid.res.1", ma, 640, &m1, err))
     return false;
   stages_["mid"] = m1;
+  // conv_out emits 2z channels; below 64 they are padded with zero channels
+  // (zero weight rows, zero bias) so that quant_conv reads a whole channel block.
+  const int zc = 2 * opt_.z_dim, zc_pad = zc < 64 ? 64 : zc;
   Act a = act(m1.h, m1.w, 640, err);
-  Act co = act(m1.h, m1.w, 2 * opt_.z_dim, err);
-  Act mo = act(m1.h, m1.w, 2 * opt_.z_dim, err);
+  Act co = act(m1.h, m1.w, zc_pad, err);
+  Act mo = act(m1.h, m1.w, zc, err);
   if (!a.p || !co.p || !mo.p) return false;
   rms(m1, "vae.enc.out_norm", true, &a);
-  if (!conv(a, "vae.enc.out", 0, &co, nullptr, err) || !conv(co, "vae.quant", 2, &mo, nullptr, err))
+  if (zc_pad != zc) {
+    void* b = nullptr;
+    VK(cudaMalloc(&b, zc_pad * 2));
+    allocs_.push_back(b);
+    VK(cudaMemset(b, 0, zc_pad * 2));
+    VK(cudaMemcpy(b, w_["vae.enc.out.bias"], zc * 2, cudaMemcpyDeviceToDevice));
+    w_["vae.enc.out.bias_padded"] = static_cast<bf16*>(b);
+  }
+  if (!conv(a, "vae.enc.out", 0, &co, nullptr, err, zc_pad != zc ? "vae.enc.out.bias_padded" : "") ||
+      !conv(co, "vae.quant", 2, &mo, nullptr, err))
     return false;
   stages_["moments"] = mo;
   float* lat = latent_slot_;
@@ -674,7 +689,7 @@ bool VaeEncoder::build(std::string* err) {
 bool VaeEncoder::encode(const float* pixels, float* latent, cudaStream_t stream, std::string* err) {
   cudaSetDevice(opt_.device_index);
   const size_t pbytes = sizeof(float) * 12 * (opt_.image_height / 2) * (opt_.image_width / 2);
-  cudaStream_t s = stream ? stream : stream_;
+  cudaStream_t s = stream;  // as given: NULL is the legacy default stream
   if (pixels != pixels_slot_) VK(cudaMemcpyAsync(pixels_slot_, pixels, pbytes, cudaMemcpyDeviceToDevice, s));
   if (graph_) {
     VK(cudaGraphLaunch(graph_, s));
@@ -697,7 +712,7 @@ bool VaeEncoder::encode_images(const PreprocessView* views, int n_views, float* 
     return false;
   }
   cudaSetDevice(opt_.device_index);
-  cudaStream_t s = stream ? stream : stream_;
+  cudaStream_t s = stream;  // as given: NULL is the legacy default stream
   PreprocessView dev[3];
   for (int i = 0; i < 3; ++i) {
     const PreprocessView& v = views[i];

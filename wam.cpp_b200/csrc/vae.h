@@ -67,14 +67,14 @@ class VaeEncoder {
   bool load_weights(std::string* err);
   bool build(std::string* err);
   bool conv(const Act& x, const std::string& wname, int mode, Act* out, const Act* residual,
-            std::string* err);
+            std::string* err, const std::string& bias_name = "");
   void rms(const Act& x, const std::string& gamma, bool silu, Act* out);
   bool resnet(const std::string& prefix, const Act& x, int cout, Act* out, std::string* err);
   bool down_block(int index, const Act& x, bool downsample, bool temporal, int cout, Act* out,
                   std::string* err);
   bool mid_attention(const Act& x, Act* out, std::string* err);
   bool gemm(const bf16* x, int ldx, int m, const bf16* w, int n, int k, int epi, const bf16* bias,
-            const bf16* residual, void* out, std::string* err);
+            const bf16* residual, void* out, std::string* err, bool weights_from_prev = false);
 
   VaeOptions opt_;
   cudaStream_t stream_ = nullptr;

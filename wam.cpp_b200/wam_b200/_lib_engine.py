@@ -23,7 +23,8 @@ class Options(C.Structure):
                 ("synthetic_bias_scale", C.c_float), ("device_index", C.c_int),
                 ("max_batch", C.c_int), ("use_cuda_graphs", C.c_int), ("prompt_cache", C.c_int),
                 ("weight_format", C.c_int), ("ffn_kind", C.c_int), ("norm_kind", C.c_int),
-                ("block_mode", C.c_int), ("vae", C.c_int)]
+                ("block_mode", C.c_int), ("vae", C.c_int), ("t5", C.c_int),
+                ("t5_vocab", C.c_int), ("t5_ffn", C.c_int), ("t5_layers", C.c_int)]
 
 
 class Image(C.Structure):
@@ -40,7 +41,9 @@ class Request(C.Structure):
     _fields_ = [("state", C.POINTER(C.c_float)), ("state_n", C.c_int),
                 ("noise", C.POINTER(C.c_float)), ("ref_latent", C.POINTER(C.c_float)),
                 ("ref_latent_n", C.c_longlong), ("prompt_emb", C.POINTER(C.c_float)),
-                ("prompt_tokens", C.c_int), ("images", C.POINTER(Image)), ("n_images", C.c_int)]
+                ("prompt_tokens", C.c_int), ("images", C.POINTER(Image)), ("n_images", C.c_int),
+                ("lang_tokens", C.POINTER(C.c_int32)), ("n_lang", C.c_int),
+                ("attention_mask", C.POINTER(C.c_int32)), ("attention_mask_n", C.c_int)]
 
 
 class Stats(C.Structure):

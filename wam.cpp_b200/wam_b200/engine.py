@@ -48,12 +48,16 @@ def geometry_struct(g) -> Geometry:
 class Req:
     """One request. `latent` is the precomputed VAE latent; with latent None,
     `images` (three HWC RGB views, uint8 or float32) run the engine's vision
-    front-end (engine created with vae=True)."""
+    front-end (engine created with vae=True). `prompt` is the precomputed
+    prompt embedding; with prompt None, `tokens` (and an optional 0/1 `mask`)
+    run the UMT5 encoder (engine created with t5=True)."""
     state: np.ndarray
     latent: np.ndarray | None
-    prompt: np.ndarray
+    prompt: np.ndarray | None
     noise: np.ndarray | None = None
     images: list | None = None
+    tokens: np.ndarray | None = None  # prompt token ids (engine created with t5=True)
+    mask: np.ndarray | None = None
 
 
 def _f32(a):
@@ -65,7 +69,8 @@ class Engine:
                  bias_scale: float = 0.0, device: int = 0, max_batch: int = 1,
                  graphs: bool = True, prompt_cache: bool = True, weights: str = "bf16",
                  ffn: str = "gelu", norm: str = "layernorm", block: bool = False,
-                 vae: bool = False):
+                 vae: bool = False, t5: bool = False, t5_vocab: int = 0, t5_ffn: int = 0,
+                 t5_layers: int = 0):
         """ffn ('gelu' | 'swiglu') and norm ('layernorm' | 'rmsnorm') select the
         config-1 block variants (synthetic weights); block=True creates an engine
         for block_forward (one layer over given hidden states)."""
@@ -90,6 +95,8 @@ class Engine:
         o.norm_kind = 1 if norm == "rmsnorm" else 0
         o.block_mode = 1 if block else 0
         o.vae = 1 if vae else 0
+        o.t5 = 1 if t5 else 0
+        o.t5_vocab, o.t5_ffn, o.t5_layers = t5_vocab, t5_ffn, t5_layers
         h = C.c_void_p()
         st = Status()
         _raise(self.lib, self.lib.wam_b200_create(C.byref(o), C.byref(h), C.byref(st)), st,
@@ -114,11 +121,27 @@ class Engine:
         arr = (Request * len(reqs))()
         keep = []
         for i, r in enumerate(reqs):
-            s, pr = _f32(r.state), _f32(r.prompt)
-            keep += [s, pr]
+            s = _f32(r.state)
+            keep.append(s)
             fp = C.POINTER(C.c_float)
             arr[i].state = s.ctypes.data_as(fp)
             arr[i].state_n = s.size
+            if r.prompt is not None:
+                pr = _f32(r.prompt)
+                keep.append(pr)
+                arr[i].prompt_emb = pr.ctypes.data_as(fp)
+                arr[i].prompt_tokens = (pr.shape[0] if pr.ndim == 2
+                                        else pr.size // self.geometry["text_dim"])
+            if r.tokens is not None:
+                tk = np.ascontiguousarray(r.tokens, np.int32)
+                keep.append(tk)
+                arr[i].lang_tokens = tk.ctypes.data_as(C.POINTER(C.c_int32))
+                arr[i].n_lang = tk.size
+                if r.mask is not None:
+                    mk = np.ascontiguousarray(r.mask, np.int32)
+                    keep.append(mk)
+                    arr[i].attention_mask = mk.ctypes.data_as(C.POINTER(C.c_int32))
+                    arr[i].attention_mask_n = mk.size
             if r.latent is not None:
                 lat = _f32(r.latent)
                 keep.append(lat)
@@ -133,8 +156,6 @@ class Engine:
                 keep += views + [imgs]
                 arr[i].images = imgs
                 arr[i].n_images = len(views)
-            arr[i].prompt_emb = pr.ctypes.data_as(fp)
-            arr[i].prompt_tokens = pr.shape[0] if pr.ndim == 2 else pr.size // self.geometry["text_dim"]
             if r.noise is not None:
                 nz = _f32(r.noise)
                 keep.append(nz)
