@@ -9,8 +9,9 @@ ranks time. The same line carries "config4": BASELINE config 4, 64 requests
 per box split 64/N per GPU (strong scaling), timed after the main measurement,
 and (one GPU) "config1": one MoT block through wam_b200_block_forward in the
 reference's form and BASELINE's literal form, beside the CPU oracle's block,
-and "vision": the vision front-end (compose / resize / patchify and the Wan
-VAE encoder) on config 2's canvas from three camera views.
+"vision": the vision front-end (compose / resize / patchify and the Wan VAE
+encoder) on config 2's canvas from three camera views, and "text_encoder": the
+UMT5-XXL encoder on a 512-token prompt.
 
   python bench.py [--gpus N --steps K --warmup W]        this engine
   python bench.py --impl reference [...]                 the reference arm: the
@@ -374,6 +375,8 @@ def main() -> None:
                     help="op case gemm: split-K factor (0 = the planner's choice)")
     ap.add_argument("--scratch", action="store_true",
                     help="op case gemm: split-K partials through a global workspace (as the engine)")
+    ap.add_argument("--no-text", action="store_true",
+                    help="skip the UMT5 text encoder measurement")
     ap.add_argument("--no-vision", action="store_true",
                     help="skip the vision front-end measurement (stage 1 + VAE encoder)")
     ap.add_argument("--no-config1", action="store_true",
@@ -508,6 +511,9 @@ def main() -> None:
     vis = None
     if world == 1 and not args.no_vision:
         vis = run_vision(local, cpu=not args.no_cpu_baseline)
+    txt = None
+    if world == 1 and not args.no_text:
+        txt = run_text(local, cpu=not args.no_cpu_baseline)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_s * 1e3 / args.steps,
@@ -523,6 +529,7 @@ def main() -> None:
         "config4": c4,
         "config1": c1,
         "vision": vis,
+        "text_encoder": txt,
         "cpu_baseline": cb,
     }
     print(json.dumps(line), flush=True)
@@ -616,16 +623,27 @@ def run_vision(dev_index: int = 0, reps: int = 10, cpu: bool = True) -> dict:
         vae.encode_device(pix, lat)
     torch.cuda.synchronize()
     e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    # Stage 1 takes microseconds: 20 launches captured in one CUDA graph so that
+    # the events time the kernels, not the host's launch calls.
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        vision.preprocess(dviews, W, H, out=pix)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(20):
+                vision.preprocess(dviews, W, H, out=pix)
+    torch.cuda.synchronize()
     pre_ms, enc_ms = [], []
     for _ in range(reps):
         e[0].record()
-        vision.preprocess(dviews, W, H, out=pix)
+        graph.replay()
         e[1].record()
         vae.encode_device(pix, lat)
         e[2].record()
         torch.cuda.synchronize()
-        pre_ms.append(e[0].elapsed_time(e[1]))
+        pre_ms.append(e[0].elapsed_time(e[1]) / 20)
         enc_ms.append(e[1].elapsed_time(e[2]))
+    del graph
     wall = []
     for _ in range(reps):
         t0 = time.perf_counter()
@@ -662,6 +680,64 @@ def run_vision(dev_index: int = 0, reps: int = 10, cpu: bool = True) -> dict:
                       "cores": oracle.lib().oracle_threads(), "kind": "port (F32 OpenMP oracle)"}
     vae.close()
     return out
+
+
+def run_text(dev_index: int = 0, reps: int = 5, cpu: bool = True) -> dict:
+    """The UMT5-XXL text encoder (24 layers, 4096 wide, 64 heads, FFN 10240,
+    synthetic weights) on a 512-token prompt (config 2's N_t): device ms with
+    CUDA events around the captured graph on the launching stream after 2
+    warm-ups, tensor roofline on its FLOPs; e2e = host tokens in, host
+    embedding out (wam_b200_t5_encode). CPU: the oracle on a bounded sample
+    (one layer of the same widths over 64 tokens), scaled by layers x tokens."""
+    import numpy as np
+    import torch
+    from wam_b200.text import T5_XXL, T5Geometry, TextEncoder
+
+    g = T5_XXL
+    enc = TextEncoder(g, seed=SEED, device_index=dev_index)
+    tok = np.random.default_rng(SEED).integers(0, g.vocab, g.max_tokens).astype(np.int32)
+    out = enc.encode_device(tok)
+    for _ in range(2):
+        enc.encode_device(tok, out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ms = []
+    for _ in range(reps):
+        e0.record()
+        enc.encode_device(tok, out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    wall = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        enc.encode(tok)
+        wall.append((time.perf_counter() - t0) * 1e3)
+    flops, launches = enc.info(g.max_tokens)
+    enc.close()
+    torch.cuda.empty_cache()
+    d = statistics.median(ms)
+    pk = peaks()
+    rec = {"workload": f"UMT5-XXL encoder, {g.max_tokens} tokens (synthetic weights)",
+           "device_ms_p50": d, "gflop": flops / 1e9, "tflops": flops / d / 1e9,
+           "frac_of_bf16_peak": flops / d / 1e9 / pk["bf16_tflops"], "launches": launches,
+           "e2e_ms_p50": statistics.median(wall),
+           "e2e_note": "host token ids -> host [512 x 4096] F32 embedding"}
+    if cpu:
+        import oracle
+        from oracle import synth
+
+        sg = T5Geometry(vocab=1000, hidden=g.hidden, ffn=g.ffn, heads=g.heads, head_dim=64,
+                        layers=1, max_tokens=64)
+        w = synth.make_t5_weights(SEED, sg)
+        t = np.random.default_rng(1).integers(0, sg.vocab, 64).astype(np.int32)
+        t0 = time.perf_counter()
+        oracle.t5_encode(w, sg, t, sg.max_tokens)
+        dt = time.perf_counter() - t0
+        rec["cpu"] = {"sample": "1 layer, 64 tokens, XXL widths", "sample_ms": dt * 1e3,
+                      "ms_scaled": dt * 1e3 * g.layers * g.max_tokens / 64,
+                      "cores": oracle.lib().oracle_threads(), "kind": "port (F32 OpenMP oracle)"}
+    return rec
 
 
 def run_config4(args, g, world, rank, local, barrier, max_over_ranks) -> dict:

@@ -22,7 +22,7 @@
 // up to 64] (zero padded) and read with a 2-D map, box {64, 256}.
 //
 // Pipeline as the persistent linear GEMM: warp 0 TMA producer, warp 1 TMEM
-// allocator + single-thread UMMA issuer (M = 128, N = 256, K = 16), warps 2-5
+// allocator + single-thread UMMA issuer (M = 128, N = 160 or 256, K = 16), warps 2-5
 // epilogue (bias, residual, BF16 rounding as the reference's
 // conv -> BF16, + bias -> BF16, + shortcut -> BF16), two TMEM accumulators so
 // one tile's epilogue overlaps the next tile's mainloop; CTAs loop over tiles.
@@ -37,12 +37,18 @@ namespace wamb {
 namespace {
 
 constexpr int kTileW = 16, kTileH = 8;  // output pixels per tile (M = 128)
-constexpr int kCM = 128, kCN = 256, kCK = 64;
+constexpr int kCM = 128, kCN = 256, kCK = 64;  // kCN: the widest N tile (padding unit)
 constexpr int kCThreads = 192;
 constexpr uint32_t kCA = kCM * kCK * 2;   // 16 KB
-constexpr uint32_t kCB = kCN * kCK * 2;   // 32 KB
-constexpr int kCStages = 4;
-constexpr int kCSmem = kCStages * (kCA + kCB) + 1024 + 256 + 2 * kCN * 4;
+// N tile of the kernel: 256 output channels, or 160 when Cout is a multiple of
+// 160 (the VAE's 160 / 320 / 640): a UMMA's time is linear in N, so a 256-wide
+// tile over 160 channels would spend 37.5 % of the tensor time on padding.
+template <int WN>
+struct ConvTile {
+  static constexpr uint32_t kB = WN * kCK * 2;  // 32 / 20 KB per stage
+  static constexpr int kStages = 196608 / (kCA + kB) > 6 ? 6 : 196608 / (kCA + kB);
+  static constexpr int kSmem = kStages * (kCA + kB) + 1024 + 256 + 2 * kCN * 4;
+};
 
 __device__ __forceinline__ void conv_load_a(const CUtensorMap* tm, uint8_t* dst, uint64_t* bar,
                                             const ConvParams& p, int kb, int x0, int y0,
@@ -68,18 +74,21 @@ __device__ __forceinline__ void conv_load_a(const CUtensorMap* tm, uint8_t* dst,
   }
 }
 
+template <int WN>
 __global__ void __launch_bounds__(kCThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ ConvParams p, const __grid_constant__ GemmArgs args) {
+  constexpr int kS = ConvTile<WN>::kStages;
+  constexpr uint32_t kBw = ConvTile<WN>::kB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* smem_a = smem;
-  uint8_t* smem_w = smem + kCStages * kCA;
-  uint8_t* tail = smem_w + kCStages * kCB;
+  uint8_t* smem_w = smem + kS * kCA;
+  uint8_t* tail = smem_w + kS * kBw;
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
-  uint64_t* empty = full + kCStages;
-  uint64_t* acc_full = empty + kCStages;  // [2]
+  uint64_t* empty = full + kS;
+  uint64_t* acc_full = empty + kS;  // [2]
   uint64_t* acc_empty = acc_full + 2;     // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   float* bias_s = reinterpret_cast<float*>(tail + 256);
@@ -93,7 +102,7 @@ __global__ void __launch_bounds__(kCThreads, 1)
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tm_w);
     prefetch_tensormap(&tm_x);
-    for (int s = 0; s < kCStages; ++s) {
+    for (int s = 0; s < kS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -124,14 +133,14 @@ __global__ void __launch_bounds__(kCThreads, 1)
         const int tm = t % tiles_m, tn = t / tiles_m;
         const int x0 = (tm % p.tiles_x) * kTileW, y0 = (tm / p.tiles_x) * kTileH;
         for (int kb = 0; kb < nkb; ++kb, ++g) {
-          const int s = g % kCStages;
-          if (g >= kCStages && !mbar_wait(&empty[s], ((g / kCStages) & 1) ^ 1)) {
+          const int s = g % kS;
+          if (g >= kS && !mbar_wait(&empty[s], ((g / kS) & 1) ^ 1)) {
             atomicCAS(args.error, 0u, static_cast<unsigned>(kErrProducerTimeout));
             good = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], kCA + kCB);
-          tma_load_2d(smem_w + s * kCB, &tm_w, &full[s], kb * kCK, tn * kCN, pol_w);
+          mbar_arrive_expect_tx(&full[s], kCA + kBw);
+          tma_load_2d(smem_w + s * kBw, &tm_w, &full[s], kb * kCK, tn * WN, pol_w);
           if (!waited) {  // the input comes from the preceding kernel
             griddep_wait();
             waited = true;
@@ -142,7 +151,7 @@ __global__ void __launch_bounds__(kCThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kCM, kCN);
+      constexpr uint32_t idesc = umma_idesc_bf16(kCM, WN);
       int g = 0, j = 0;
       bool good = true;
       for (int t = blockIdx.x; t < tiles && good; t += gridDim.x, ++j) {
@@ -152,17 +161,17 @@ __global__ void __launch_bounds__(kCThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t acc = tmem_base + static_cast<uint32_t>(b * kCN);
+        const uint32_t acc = tmem_base + static_cast<uint32_t>(b * WN);
         for (int kb = 0; kb < nkb; ++kb, ++g) {
-          const int s = g % kCStages;
-          if (!mbar_wait(&full[s], (g / kCStages) & 1)) {
+          const int s = g % kS;
+          if (!mbar_wait(&full[s], (g / kS) & 1)) {
             atomicCAS(args.error, 0u, static_cast<unsigned>(kErrMmaTimeout));
             good = false;
             break;
           }
           tc_fence_after();
           const uint64_t da = sw128_kmajor_desc(smem_u32(smem_a + s * kCA));
-          const uint64_t db = sw128_kmajor_desc(smem_u32(smem_w + s * kCB));
+          const uint64_t db = sw128_kmajor_desc(smem_u32(smem_w + s * kBw));
 #pragma unroll
           for (int k = 0; k < kCK / 16; ++k)
             umma_bf16_ss(acc, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
@@ -182,9 +191,9 @@ __global__ void __launch_bounds__(kCThreads, 1)
       const int tm = t % tiles_m, tn = t / tiles_m;
       const int x = (tm % p.tiles_x) * kTileW + (row % kTileW);
       const int y = (tm / p.tiles_x) * kTileH + (row / kTileW);
-      const int n_base = tn * kCN;
+      const int n_base = tn * WN;
       named_bar_sync(1, 128);  // the previous tile's bias is no longer read
-      for (int jj = et; jj < kCN; jj += 128) {
+      for (int jj = et; jj < WN; jj += 128) {
         const int n = n_base + jj;
         bias_s[jj] = (args.bias && n < args.n) ? __bfloat162float(args.bias[n]) : 0.0f;
         gate_s[jj] = 0.0f;
@@ -194,10 +203,10 @@ __global__ void __launch_bounds__(kCThreads, 1)
       if (!ok) atomicCAS(args.error, 0u, static_cast<unsigned>(kErrEpilogueTimeout));
       tc_fence_after();
       const uint32_t taddr =
-          tmem_base + static_cast<uint32_t>(b * kCN) + (static_cast<uint32_t>(q * 32) << 16);
+          tmem_base + static_cast<uint32_t>(b * WN) + (static_cast<uint32_t>(q * 32) << 16);
       const bool valid = ok && x < p.out_w && y < p.out_h;
 #pragma unroll 1
-      for (int c = 0; c < kCN && n_base + c < args.n; c += 16) {
+      for (int c = 0; c < WN && n_base + c < args.n; c += 16) {
         uint32_t r[16];
         tmem_ld_x16(taddr + c, r);
         tmem_ld_wait();
@@ -301,7 +310,8 @@ const char* conv_plan(ConvOp* op, const bf16* x, int in_w, int in_h, int cin, in
   p.out_h = mode == 1 ? in_h / 2 : in_h;
   p.tiles_x = (p.out_w + kTileW - 1) / kTileW;
   p.tiles_y = (p.out_h + kTileH - 1) / kTileH;
-  p.tiles_n = (cout + kCN - 1) / kCN;
+  op->wn = cout % 160 == 0 ? 160 : kCN;
+  p.tiles_n = (cout + op->wn - 1) / op->wn;
   const cuuint64_t c = static_cast<cuuint64_t>(cin);
   if (mode == 1) {
     const cuuint64_t dims[5] = {c, 2, static_cast<cuuint64_t>(in_w / 2), 2,
@@ -320,7 +330,7 @@ const char* conv_plan(ConvOp* op, const bf16* x, int in_w, int in_h, int cin, in
   const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(kpad),
                                static_cast<cuuint64_t>(conv_cout_pad(cout))};
   const cuuint64_t wstr[1] = {static_cast<cuuint64_t>(kpad) * 2};
-  const cuuint32_t wbox[2] = {kCK, kCN};
+  const cuuint32_t wbox[2] = {kCK, static_cast<cuuint32_t>(op->wn)};
   if (!encode(&op->tm_w, w_laid, 2, wdims, wstr, wbox)) return "conv: weight tensor map";
   GemmArgs& a = op->args;
   a = GemmArgs{};
@@ -339,24 +349,31 @@ const char* conv_plan(ConvOp* op, const bf16* x, int in_w, int in_h, int cin, in
   return nullptr;
 }
 
-bool conv_launch(const ConvOp& op, unsigned* error, cudaStream_t stream, bool pdl) {
+template <int WN>
+bool conv_launch_t(const ConvOp& op, unsigned* error, cudaStream_t stream, bool pdl) {
   static std::once_flag once;
   std::call_once(once, [] {
-    cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCSmem);
+    cudaFuncSetAttribute(conv_tc_kernel<WN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         ConvTile<WN>::kSmem);
   });
   GemmArgs a = op.args;
   a.error = error;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(op.grid);
   cfg.blockDim = dim3(kCThreads);
-  cfg.dynamicSmemBytes = kCSmem;
+  cfg.dynamicSmemBytes = ConvTile<WN>::kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, conv_tc_kernel, op.tm_w, op.tm_x, op.params, a) == cudaSuccess;
+  return cudaLaunchKernelEx(&cfg, conv_tc_kernel<WN>, op.tm_w, op.tm_x, op.params, a) == cudaSuccess;
+}
+
+bool conv_launch(const ConvOp& op, unsigned* error, cudaStream_t stream, bool pdl) {
+  return op.wn == 160 ? conv_launch_t<160>(op, error, stream, pdl)
+                      : conv_launch_t<256>(op, error, stream, pdl);
 }
 
 }  // namespace wamb

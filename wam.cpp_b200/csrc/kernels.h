@@ -267,6 +267,7 @@ struct ConvOp {
   ConvParams params;
   GemmArgs args;
   int grid = 0;
+  int wn = 256;  // N tile: 160 when Cout is a multiple of 160, else 256
 };
 int conv_cin_pad(int cin);
 int conv_cout_pad(int cout);

@@ -46,57 +46,59 @@ __global__ void to_nhwc64_kernel(const float* __restrict__ in, bf16* __restrict_
 }
 
 // Per-pixel RMS over C channels (ggml_rms_norm_bf16_f32: x * rsqrt(mean(x^2) + eps)
-// * gamma in F32), optional SiLU, BF16 out. One warp per pixel, C % 8 == 0, C <= 768.
-__global__ void rms_act_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gamma,
-                               bf16* __restrict__ out, int rows, int C, int silu_on) {
-  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const int chunks = C / 8;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * C);
-  float v[3][8];
+// * gamma in F32), optional SiLU, BF16 out. A 256-thread block covers
+// P = 256 / (C / 8) whole pixels, one 16-byte chunk (8 channels) per thread, so
+// every load of the block is issued at once and coalesced; a pixel's sum of
+// squares is reduced in chunk order through shared memory (deterministic).
+// C % 8 == 0, C <= 2048.
+__global__ void __launch_bounds__(256) rms_act_kernel(const bf16* __restrict__ x,
+                                                      const bf16* __restrict__ gamma,
+                                                      bf16* __restrict__ out, int rows, int C,
+                                                      int silu_on) {
+  __shared__ float part[256];
+  __shared__ float inv_s[256];
+  const int chunks = C / 8, P = 256 / chunks;
+  const int t = threadIdx.x, lp = t / chunks, ch = t - lp * chunks;
+  const long long row = static_cast<long long>(blockIdx.x) * P + lp;
+  const bool active = lp < P && row < rows;
+  float v[8];
   float ss = 0.0f;
+  if (active) {
+    const uint4 u = reinterpret_cast<const uint4*>(x + row * C)[ch];
+    const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int j = 0; j < 3; ++j) {
-    const int ch = lane + 32 * j;
-    if (ch < chunks) {
-      const uint4 u = xr[ch];
-      const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        v[j][2 * q] = __uint_as_float(wv[q] << 16);
-        v[j][2 * q + 1] = __uint_as_float(wv[q] & 0xFFFF0000u);
-      }
-#pragma unroll
-      for (int q = 0; q < 8; ++q) ss += v[j][q] * v[j][q];
+    for (int q = 0; q < 4; ++q) {
+      v[2 * q] = __uint_as_float(wv[q] << 16);
+      v[2 * q + 1] = __uint_as_float(wv[q] & 0xFFFF0000u);
     }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) ss += v[q] * v[q];
   }
+  part[t] = ss;
+  __syncthreads();
+  if (t < P) {
+    float s = 0.0f;
+    for (int k = 0; k < chunks; ++k) s += part[t * chunks + k];
+    inv_s[t] = rsqrtf(s / static_cast<float>(C) + kVaeEps);
+  }
+  __syncthreads();
+  if (!active) return;
+  const float inv = inv_s[lp];
+  const uint4 gu = reinterpret_cast<const uint4*>(gamma)[ch];
+  const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
+  uint32_t ow[4];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float inv = rsqrtf(ss / static_cast<float>(C) + kVaeEps);
-  uint4* orow = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * C);
-  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
-#pragma unroll
-  for (int j = 0; j < 3; ++j) {
-    const int ch = lane + 32 * j;
-    if (ch < chunks) {
-      const uint4 gu = gr[ch];
-      const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
-      uint32_t ow[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float a = v[j][2 * q] * inv * __uint_as_float(gw[q] << 16);
-        float b = v[j][2 * q + 1] * inv * __uint_as_float(gw[q] & 0xFFFF0000u);
-        if (silu_on) {
-          a = silu(a);
-          b = silu(b);
-        }
-        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-        ow[q] = *reinterpret_cast<const uint32_t*>(&h);
-      }
-      orow[ch] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+  for (int q = 0; q < 4; ++q) {
+    float a = v[2 * q] * inv * __uint_as_float(gw[q] << 16);
+    float b = v[2 * q + 1] * inv * __uint_as_float(gw[q] & 0xFFFF0000u);
+    if (silu_on) {
+      a = silu(a);
+      b = silu(b);
     }
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    ow[q] = *reinterpret_cast<const uint32_t*>(&h);
   }
+  reinterpret_cast<uint4*>(out + row * C)[ch] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
 }
 
 // 2x2 average pool of x [H][W][C] (F32 sum of the window in row order, x 1/4),
@@ -464,7 +466,9 @@ void VaeEncoder::rms(const Act& x, const std::string& gamma, bool silu_on, Act* 
   const Act in = x, o = *out;
   program_.push_back([in, o, g, silu_on](cudaStream_t s) {
     const int rows = in.h * in.w;
-    rms_act_kernel<<<(rows + 7) / 8, 256, 0, s>>>(in.p, g, o.p, rows, in.c, silu_on ? 1 : 0);
+    const int per_block = 256 / (in.c / 8);
+    rms_act_kernel<<<(rows + per_block - 1) / per_block, 256, 0, s>>>(in.p, g, o.p, rows, in.c,
+                                                                       silu_on ? 1 : 0);
     return cudaGetLastError() == cudaSuccess;
   });
 }
