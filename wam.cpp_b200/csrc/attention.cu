@@ -43,6 +43,67 @@ __device__ __forceinline__ void load_tile(uint32_t smem, const bf16* g, int rows
   }
 }
 
+// Merge of one row slice of a split query tile: this thread's rows_per =
+// 64 / SPL dims of query row row_l, over the SPL splits' partial O and
+// (max, sum), from the L2 workspace (gx) or the peers' shared memory. Every
+// load (16 float4 of O whatever SPL, plus the maxima and sums) is issued
+// before any is used, and the sum runs in split order (deterministic).
+template <int SPL>
+__device__ __forceinline__ void merge_split_rows(const float* ws_blk, size_t slot_floats,
+                                                 uint32_t o_base, uint32_t m_base,
+                                                 uint32_t l_base, int kOld, int row_l, int dseg,
+                                                 float sl2, bool gx, bf16* dst) {
+  constexpr int kRowsPer = kBQ / SPL;
+  constexpr int kC = kRowsPer / 4;  // float4 per split
+  float mv[SPL], lv[SPL], wv[SPL];
+  float4 vv[kC][SPL];
+#pragma unroll
+  for (int p = 0; p < SPL; ++p) {
+    if (gx) {
+      const float* st = ws_blk + p * slot_floats + row_l * kOld + kD;
+      mv[p] = __ldcg(st);
+      lv[p] = __ldcg(st + 1);
+    } else {
+      mv[p] = ld_shared_cluster_f32(mapa_shared(m_base + row_l * 4u, p));
+      lv[p] = ld_shared_cluster_f32(mapa_shared(l_base + row_l * 4u, p));
+    }
+  }
+#pragma unroll
+  for (int ci = 0; ci < kC; ++ci)
+#pragma unroll
+    for (int p = 0; p < SPL; ++p) {
+      const uint32_t off = (row_l * kOld + dseg + ci * 4) * 4u;
+      vv[ci][p] = gx ? __ldcg(reinterpret_cast<const float4*>(ws_blk + p * slot_floats) + off / 16)
+                     : ld_shared_cluster_f32x4(mapa_shared(o_base + off, p));
+    }
+  float mx = -INFINITY;
+#pragma unroll
+  for (int p = 0; p < SPL; ++p) mx = fmaxf(mx, mv[p]);
+  float den = 0.0f;
+#pragma unroll
+  for (int p = 0; p < SPL; ++p) {
+    wv[p] = mv[p] != -INFINITY ? exp2f((mv[p] - mx) * sl2) : 0.0f;
+    den += wv[p] * lv[p];
+  }
+  const float inv_den = 1.0f / den;
+  if (!dst) return;
+#pragma unroll
+  for (int ci = 0; ci < kC; ++ci) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < SPL; ++p) {
+      acc.x = fmaf(wv[p], vv[ci][p].x, acc.x);
+      acc.y = fmaf(wv[p], vv[ci][p].y, acc.y);
+      acc.z = fmaf(wv[p], vv[ci][p].z, acc.z);
+      acc.w = fmaf(wv[p], vv[ci][p].w, acc.w);
+    }
+    uint2 pk;
+    pk.x = pack_bf16(acc.x * inv_den, acc.y * inv_den);
+    pk.y = pack_bf16(acc.z * inv_den, acc.w * inv_den);
+    *reinterpret_cast<uint2*>(dst + ci * 4) = pk;
+  }
+}
+
 // SPLIT: the key range is divided among the `splits` CTAs of a cluster (CTA
 // x = q_block * splits + split); each CTA stages its unnormalised output and
 // running max / sum in shared memory and the cluster merges rows through
@@ -257,32 +318,6 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
     const int dseg = (tid % tpr) * rows_per;
     const int row = q0 + row_l;
     const uint32_t o_base = smem_u32(o_s), m_base = smem_u32(m_s), l_base = smem_u32(l_s);
-    float mv[8], lv[8], wv[8];
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      mv[p] = -INFINITY;
-      lv[p] = 0.0f;
-      if (p < splits) {
-        if (gx) {
-          const float* st = ws_blk + p * slot_floats + row_l * kOld + kD;
-          mv[p] = __ldcg(st);
-          lv[p] = __ldcg(st + 1);
-        } else {
-          mv[p] = ld_shared_cluster_f32(mapa_shared(m_base + row_l * 4u, p));
-          lv[p] = ld_shared_cluster_f32(mapa_shared(l_base + row_l * 4u, p));
-        }
-      }
-    }
-    float mx = -INFINITY;
-#pragma unroll
-    for (int p = 0; p < 8; ++p) mx = fmaxf(mx, mv[p]);
-    float den = 0.0f;
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      wv[p] = mv[p] != -INFINITY ? exp2f((mv[p] - mx) * sl2) : 0.0f;
-      den += wv[p] * lv[p];
-    }
-    const float inv_den = 1.0f / den;
     bf16* dst = nullptr;
     if (row < a.lq) {
       if (a.split_first) {
@@ -293,31 +328,12 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
       }
       dst += head * kD + dseg;
     }
-#pragma unroll 1
-    for (int c = 0; c < rows_per; c += 4) {
-      float4 v[8];
-      const uint32_t off = (row_l * kOld + dseg + c) * 4u;
-#pragma unroll
-      for (int p = 0; p < 8; ++p)
-        if (p < splits)
-          v[p] = gx ? __ldcg(reinterpret_cast<const float4*>(ws_blk + p * slot_floats) + off / 16)
-                    : ld_shared_cluster_f32x4(mapa_shared(o_base + off, p));
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int p = 0; p < 8; ++p)
-        if (p < splits) {
-          acc.x = fmaf(wv[p], v[p].x, acc.x);
-          acc.y = fmaf(wv[p], v[p].y, acc.y);
-          acc.z = fmaf(wv[p], v[p].z, acc.z);
-          acc.w = fmaf(wv[p], v[p].w, acc.w);
-        }
-      if (dst) {
-        uint2 pk;
-        pk.x = pack_bf16(acc.x * inv_den, acc.y * inv_den);
-        pk.y = pack_bf16(acc.z * inv_den, acc.w * inv_den);
-        *reinterpret_cast<uint2*>(dst + c) = pk;
-      }
-    }
+    if (splits == 8)
+      merge_split_rows<8>(ws_blk, slot_floats, o_base, m_base, l_base, kOld, row_l, dseg, sl2, gx, dst);
+    else if (splits == 4)
+      merge_split_rows<4>(ws_blk, slot_floats, o_base, m_base, l_base, kOld, row_l, dseg, sl2, gx, dst);
+    else
+      merge_split_rows<2>(ws_blk, slot_floats, o_base, m_base, l_base, kOld, row_l, dseg, sl2, gx, dst);
     if (!gx) cluster_sync_all();  // peers may still read this CTA's shared memory
   } else {
     // Normalise and store BF16 rows.
