@@ -484,6 +484,7 @@ def main() -> None:
     # profile after it only gives the breakdown by kind.
     hbm_roof = graph_roofline(eng, B, "denoise", pk, "hbm")
     tc_roof = graph_roofline(eng, B, "prefix", pk, "tensor")
+    breakdown_graph = graph_breakdown(eng, B)
     eng.stage(reqs)
     prof = eng.profile(B)
     breakdown = breakdown_from_profile(prof)
@@ -521,7 +522,8 @@ def main() -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": {**workload(g, B, args.weights), "parallelism": f"dp{world} (replicas, no collective)"},
         "roofline": hbm_roof, "roofline_tensor": tc_roof, "clocks": clocks.summary(),
-        "phase_ms": phases, "kernel_breakdown_eager": breakdown,
+        "phase_ms": phases, "kernel_breakdown_graph": breakdown_graph,
+        "kernel_breakdown_eager": breakdown,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_s * 1e3 / args.steps},
         "gpu_launches": kernels_per_chunk * args.steps,
@@ -812,6 +814,28 @@ def graph_roofline(eng, B, phase, pk, bound) -> dict:
                 "timing": f"the chunk's {r['launches']} {phase}-phase GEMM launches captured alone in "
                           f"a CUDA graph (same plans, buffers and PDL), CUDA events around 5 replays"})
     return out
+
+
+def graph_breakdown(eng, B) -> dict:
+    """Device time of each (phase, kind) of the chunk with its launches
+    replayed alone in a CUDA graph (wam_b200_profile_graph; same plans,
+    buffers and PDL as the timed chunk). The kinds' sum falls short of the
+    phase times by the boundaries between kinds."""
+    from wam_b200.engine import KINDS, PHASES
+    out = {}
+    for ph in PHASES:
+        for kind in KINDS:
+            if kind == "sync":
+                continue
+            try:
+                r = eng.profile_graph(B, ph, kind, reps=3)
+            except RuntimeError:  # no launch of this kind in this phase
+                continue
+            if r["launches"] == 0:
+                continue
+            out[f"{ph}/{kind}"] = {"ms": round(r["ms"], 3), "launches": r["launches"],
+                                   "us_per_launch": round(r["ms"] * 1e3 / r["launches"], 2)}
+    return dict(sorted(out.items(), key=lambda kv: -kv[1]["ms"]))
 
 
 def breakdown_from_profile(prof: list[dict]) -> dict:

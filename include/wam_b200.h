@@ -111,8 +111,11 @@ WAM_B200_API int wam_b200_op_gemm_noalloc_error(unsigned* code);
  * and 128 weight rows per k-block), split over 2 or 4 pairs of one cluster when
  * the output tiles are few and a workspace is given. BF16 weights only (row-major
  * or WAM_B200_GEMM_TILED_WEIGHTS); ignored with force_splits > 0 or Q8_0
- * weights. The engine uses it for every such GEMM when the environment variable
- * WAM_B200_GEMM_PAIR=1 is set at load. */
+ * weights. Without the flag, wam_b200_op_gemm and the engine choose CTA pairs
+ * by themselves for GEMMs of >= 256 rows whose 256 x 256 tiles occupy at least
+ * half of the GPU's resident pairs; the environment variable WAM_B200_GEMM_PAIR
+ * set at load to 1 (every GEMM of >= 256 rows) or 0 (only where the flag asks)
+ * overrides that choice. */
 #define WAM_B200_GEMM_PAIR 0x400
 
 /* Quantises n_elems BF16 weights (n_elems % 32 == 0, row-major [n][k]) to GGML

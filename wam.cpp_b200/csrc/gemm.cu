@@ -1284,13 +1284,18 @@ bool g_pdl = [] {
   return !(v && *v && *v != '0');
 }();
 
-// CTA-pair kernel for every GEMM of >= 256 token rows when
-// WAM_B200_GEMM_PAIR=1 (off by default: measured no faster than the one-CTA
-// kernels on the config-2 prefix shapes); a caller can also ask for it per
-// GEMM (gemm_plan's pair argument).
-bool g_pair = [] {
+// CTA-pair kernel choice (WAM_B200_GEMM_PAIR): unset = automatic, for GEMMs
+// of >= 256 token rows whose 256 x 256 pair tiles occupy at least half of the
+// resident pairs (measured in CUDA-graph replay: 768 x 14336 x 3072 61.4 vs
+// 62.7 us, 768 x 9216 x 3072 43.0 vs 44.1, the 64-request prefix 471 vs 495 ms;
+// fewer tiles leave SMs idle that the one-CTA kernel's split-K fills:
+// 768 x 3072 x 14336 87.9 vs 62.7 us); 1 = every GEMM of >= 256 rows; 0 =
+// never. A caller can also ask for it per GEMM (gemm_plan's pair argument).
+int g_pair_mode = [] {
   const char* v = std::getenv("WAM_B200_GEMM_PAIR");
-  return v && *v == '1';
+  if (v && *v == '1') return 1;
+  if (v && *v == '0') return 0;
+  return 2;
 }();
 // Streaming GEMM (no split-K) for token tiles of <= 64 rows and N >= 1536
 // (default); WAM_B200_GEMM_STREAM=0 keeps such GEMMs on the split-K kernel,
@@ -1326,10 +1331,13 @@ ShapeChoice choose_shape(int m, int n, int k, int num_sms, int force_splits, boo
                          bool workspace, bool want_pair) {
   ShapeChoice c;
   const int nkb = k / kBK;
-  if ((g_pair || want_pair) && !w_q8 && force_splits <= 0 && m >= 2 * kTM) {
+  const int pair_tiles = ((m + 2 * kTM - 1) / (2 * kTM)) * ((n + kWN - 1) / kWN);
+  const int pairs = g_cluster_slots[2] > 0 ? g_cluster_slots[2] / 2 : num_sms / 2;
+  const bool pair_auto = g_pair_mode == 2 && 2 * pair_tiles >= pairs;
+  if ((g_pair_mode == 1 || want_pair || pair_auto) && !w_q8 && force_splits <= 0 &&
+      m >= 2 * kTM) {
     c.pair = true;
-    c.tiles = ((m + 2 * kTM - 1) / (2 * kTM)) * ((n + kWN - 1) / kWN);
-    const int pairs = g_cluster_slots[2] > 0 ? g_cluster_slots[2] / 2 : num_sms / 2;
+    c.tiles = pair_tiles;
     if (workspace && c.tiles * 4 < pairs * 3) {
       for (int s = 2; s <= 4; s *= 2) {
         const int clusters = g_cluster_slots[2 * s] > 0 ? g_cluster_slots[2 * s] / (2 * s)
