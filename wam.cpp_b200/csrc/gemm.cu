@@ -216,6 +216,24 @@ __device__ __forceinline__ void copy_out(const GemmArgs& a, const uint8_t* stg, 
   }
 }
 
+// Output tile t of a persistent GEMM -> (token tile, weight tile). Token
+// tiles go in groups of group_m, and a group runs through all weight tiles
+// before the next group starts: a wave of CTAs then covers a few token tiles x
+// many weight tiles, so both operands of the wave stay in L2. (With the token
+// tile fastest over all tiles, every token tile is read from HBM again for
+// each weight tile once the tokens exceed L2.) group_m >= tiles_m is that
+// plain order.
+__device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int& tile_m, int& tile_n) {
+  const int g = a.group_m > 0 && a.group_m < a.tiles_m ? a.group_m : a.tiles_m;
+  const int span = g * a.tiles_n;
+  const int grp = t / span;
+  const int first = grp * g;
+  const int gsize = a.tiles_m - first < g ? a.tiles_m - first : g;
+  const int local = t - grp * span;
+  tile_m = first + local % gsize;
+  tile_n = local / gsize;
+}
+
 // Persistent variant for GEMMs with more output tiles than SMs (prefix,
 // batched denoise; no split-K, BF16 weights): CTA c takes tiles c, c + grid,
 // ... The copy ring runs on across tiles, and two TMEM accumulators (2 x 256
@@ -278,7 +296,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int g = 0;  // stages issued so far
       bool waited = false, good = true;
       for (int t = blockIdx.x; t < tiles && good; t += gridDim.x) {
-        const int tile_m = t % args.tiles_m, tile_n = t / args.tiles_m;
+        int tile_m, tile_n;
+        tile_coords(args, t, tile_m, tile_n);
         const bf16* w_tiles =
             args.w_tiled ? args.w_tiled + static_cast<size_t>(tile_n) * nkb * (kWN * kBK) : nullptr;
         for (int kb = 0; kb < nkb; ++kb, ++g) {
@@ -341,7 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int j = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
       const int b = j & 1;
-      const int tile_m = t % args.tiles_m, tile_n = t / args.tiles_m;
+      int tile_m, tile_n;
+      tile_coords(args, t, tile_m, tile_n);
       const int m_base = tile_m * kTM, n_base = tile_n * kWN;
       const int rows = args.m - m_base < kTM ? args.m - m_base : kTM;
       named_bar_sync(1, 128);  // the previous tile's bias / gate are no longer read
@@ -1045,7 +1065,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int g = 0;
       bool waited = false, good = true;
       for (int t = cl; t < tiles && good; t += ncl) {
-        const int tile_m = t % args.tiles_m, tile_n = t / args.tiles_m;
+        int tile_m, tile_n;
+        tile_coords(args, t, tile_m, tile_n);
         const int m_row = tile_m * (2 * kPairRows) + half * kPairRows;
         for (int i = 0; i < nkb; ++i, ++g) {
           const int s = g % S;
@@ -1113,7 +1134,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int j = 0;
     for (int t = cl; t < tiles; t += ncl, ++j) {
       const int b = j & 1;
-      const int tile_m = t % args.tiles_m, tile_n = t / args.tiles_m;
+      int tile_m, tile_n;
+      tile_coords(args, t, tile_m, tile_n);
       const int m_base = tile_m * (2 * kPairRows) + half * kPairRows, n_base = tile_n * kWN;
       int rows = args.m - m_base;
       rows = rows < 0 ? 0 : (rows > kPairRows ? kPairRows : rows);
@@ -1184,7 +1206,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     cluster_sync_all();
     const int t = cl;
     if (t < tiles) {
-      const int tile_m = t % args.tiles_m, tile_n = t / args.tiles_m;
+      int tile_m, tile_n;
+      tile_coords(args, t, tile_m, tile_n);
       const int m_base = tile_m * (2 * kPairRows) + half * kPairRows, n_base = tile_n * kWN;
       int rows = args.m - m_base;
       rows = rows < 0 ? 0 : (rows > kPairRows ? kPairRows : rows);
@@ -1351,6 +1374,14 @@ ShapeChoice choose_shape(int m, int n, int k, int num_sms, int force_splits, boo
   c.splits = force_splits > 0 ? force_splits : pick_splits(c.tiles, nkb, num_sms);
   if (c.splits > nkb) c.splits = nkb;
   return c;
+}
+
+// Token tiles per group of the persistent tile order (tile_coords): the
+// group's token rows (tile_rows x K BF16) stay within 32 MB of L2, 1 to 16 tiles.
+int group_m_for(int tile_rows, int k) {
+  const long long tile_bytes = static_cast<long long>(tile_rows) * k * 2;
+  long long g = (32ll << 20) / (tile_bytes > 0 ? tile_bytes : 1);
+  return static_cast<int>(g < 1 ? 1 : (g > 16 ? 16 : g));
 }
 
 // One thread per 16-byte chunk: chunk c of row r of tile (nt, kb) goes to
@@ -1534,6 +1565,7 @@ const char* plan_pair(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   a.w_q8 = nullptr;
   a.tiles_m = (m + 2 * kTM - 1) / (2 * kTM);
   a.tiles_n = (n + kWN - 1) / kWN;
+  a.group_m = group_m_for(2 * kTM, k);
   a.epilogue = epilogue;
   a.bias = bias;
   a.gate = gate;
@@ -1657,6 +1689,7 @@ const char* gemm_plan(GemmOp* op, const bf16* x, int ldx, int m, const bf16* w, 
   // More than a wave of unsplit tiles: persistent CTAs (one per SM).
   op->persistent = splits == 1 && !w_q8 && tiles_m * tiles_n > num_sms;
   if (op->persistent) op->grid = num_sms;
+  a.group_m = group_m_for(kTM, k);
   return nullptr;
 }
 

@@ -51,6 +51,7 @@ struct GemmArgs {
   const bf16* w_tiled;  // weights re-tiled by launch_retile_weights, or null (tensor map)
   const uint8_t* w_q8;  // Q8_0 weight tiles (launch_q8_retile), or null
   int tiles_m, tiles_n;
+  int group_m;  // persistent / pair kernels: token tiles per group of the tile order (tile_coords)
   int epilogue;
   const bf16* bias;      // [n] or null
   const float* gate;     // [n] (EPI_GATED_RES)
