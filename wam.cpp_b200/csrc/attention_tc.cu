@@ -11,11 +11,12 @@
 // warp 1 owns TMEM and issues the MMAs (S of tile j + 1 before P V of tile j,
 // so the tensor core runs while the softmax works), warps 2-9 = two threads
 // per query row, each over half the keys / dims (the row max is exchanged
-// through shared memory): softmax from S in TMEM, P as BF16 into a K-major tile, V
-// transposed to K-major in shared memory (ldmatrix.trans / stmatrix), lazy
-// rescaling of O in TMEM (only when the running max grows by more than 2^8),
-// and the final normalised BF16 rows. All operands use the K-major swizzled
-// layout of the GEMM (csrc/gemm.cu).
+// through shared memory): softmax from S in TMEM (one pass, the row's scores
+// held in registers), P as BF16 into a K-major tile, lazy rescaling of O in
+// TMEM (only when the running max grows by more than 2^8), and the final
+// normalised BF16 rows. Q, K and P use the K-major swizzled layout of the GEMM
+// (csrc/gemm.cu); V tiles (double-buffered) are read by the tensor core as
+// they land, as an MN-major operand (dims contiguous), with no transpose.
 //
 // Arithmetic as attention.cu's kernel: F32 scores, softmax(scale * S) with an
 // online max, probabilities rounded to BF16 for P V, F32 accumulation, BF16
@@ -41,8 +42,7 @@ constexpr int kHalf = 128 * 64 * 2;       // 128 rows x 64 dims (or keys), swizz
 constexpr int kTile = 2 * kHalf;          // 32 KB
 constexpr int kOffQ = 0;                  // Q [2 halves of dims]
 constexpr int kOffK = kTile;              // K ring [2][2 halves]
-constexpr int kOffV = 3 * kTile;          // V staging [2 halves of dims], rows = keys
-constexpr int kOffVt = 4 * kTile;         // V^T [2 halves of keys], rows = dims
+constexpr int kOffV = 3 * kTile;          // V ring [2][2 halves of dims], rows = keys
 constexpr int kOffP = 5 * kTile;          // P [2 halves of keys], rows = queries
 constexpr int kOffBar = 6 * kTile;
 constexpr int kOffXch = kOffBar + 256;    // row max / sum exchange between a row's two threads
@@ -64,20 +64,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sq = smem + kOffQ;
   uint8_t* sk = smem + kOffK;
   uint8_t* sv = smem + kOffV;
-  uint8_t* svt = smem + kOffVt;
   uint8_t* sp = smem + kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 6;
-  uint64_t* s_full = bars + 7;   // [2]
-  uint64_t* s_free = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* pv_done = bars + 12;
-  uint64_t* o_full = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* s_free = bars + 11;  // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* pv_done = bars + 14;
+  uint64_t* o_full = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * kRows, head = blockIdx.y, seq = blockIdx.z;
@@ -87,7 +86,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tm_q);
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
-    for (int i = 0; i < 14; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 16; ++i) mbar_init(&bars[i], 1);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -114,9 +113,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(sk + b * kTile + kHalf, &tm_k, &k_full[b], 64, j * kKeys, head, seq, pol_kv);
       };
       auto load_v = [&](int j) {
-        mbar_arrive_expect_tx(v_full, kTile);
-        tma_load_4d(sv, &tm_v, v_full, 0, j * kKeys, head, seq, pol_kv);
-        tma_load_4d(sv + kHalf, &tm_v, v_full, 64, j * kKeys, head, seq, pol_kv);
+        const int b = j & 1;
+        mbar_arrive_expect_tx(&v_full[b], kTile);
+        tma_load_4d(sv + b * kTile, &tm_v, &v_full[b], 0, j * kKeys, head, seq, pol_kv);
+        tma_load_4d(sv + b * kTile + kHalf, &tm_v, &v_full[b], 64, j * kKeys, head, seq, pol_kv);
       };
       int nk_issued = 0, nv_issued = 0;
       // K / V the preceding kernel does not write start before waiting for it.
@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           nk_issued = j + 1;
         }
         if (j >= nv_issued) {
-          if (j >= 1 && !mbar_wait(v_empty, (j - 1) & 1)) {
+          if (j >= 2 && !mbar_wait(&v_empty[j & 1], ((j >> 1) - 1) & 1)) {
             ok = false;
             break;
           }
@@ -154,12 +154,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(q_full, 0);
       for (int j = nk_issued - 2 > 0 ? nk_issued - 2 : 0; j < nk_issued; ++j)
         mbar_wait(&k_full[j & 1], (j >> 1) & 1);
-      if (nv_issued > 0) mbar_wait(v_full, (nv_issued - 1) & 1);
+      for (int j = nv_issued - 2 > 0 ? nv_issued - 2 : 0; j < nv_issued; ++j)
+        mbar_wait(&v_full[j & 1], (j >> 1) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc = umma_idesc_bf16(kRows, kKeys);
+      constexpr uint32_t idesc_pv = umma_idesc_bf16_bmn(kRows, 128);  // V MN-major
       bool ok = mbar_wait(q_full, 0);
       for (int j = 0; j <= nk && ok; ++j) {
         if (j < nk) {
@@ -183,20 +185,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (j >= 1) {
           const int jj = j - 1;
-          if (!mbar_wait(p_full, jj & 1)) {
+          const int vb = jj & 1;
+          if (!mbar_wait(p_full, jj & 1) || !mbar_wait(&v_full[vb], (jj >> 1) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          // O += P V: P K-major over keys (two 64-key halves); V as landed,
+          // [keys][dims] in two 64-dim halves 16 KB apart (MN atoms), 8-key
+          // groups 1024 bytes apart (K atoms): 16 keys = 2048 bytes per step.
+          const uint32_t v_base = smem_u32(sv + vb * kTile);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const uint64_t da = sw128_kmajor_desc(smem_u32(sp + c * kHalf));
-            const uint64_t db = sw128_kmajor_desc(smem_u32(svt + c * kHalf));
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16_ss(t_o, da + 2 * kk, db + 2 * kk, idesc, (jj > 0 || c != 0 || kk != 0) ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t db =
+                  sw128_mnmajor_desc(v_base + static_cast<uint32_t>((c * 4 + kk) * 2048), kHalf, 1024);
+              umma_bf16_ss(t_o, da + 2 * kk, db, idesc_pv, (jj > 0 || c != 0 || kk != 0) ? 1u : 0u);
+            }
           }
           umma_commit(pv_done);
+          umma_commit(&v_empty[vb]);
         }
       }
       if (!ok) fail(a, kErrMmaTimeout);
@@ -225,17 +235,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait(&s_full[b], (j >> 1) & 1);
       tc_fence_after();
       const int valid = a.lk - j * kKeys < kKeys ? a.lk - j * kKeys : kKeys;
-      // pass 1: row max over this thread's valid keys, combined with its partner
+      // This thread's 64 scores of the row, read from TMEM once; row max over
+      // its valid keys, combined with its partner's.
+      uint32_t sa[32], sb[32];
+      tmem_ld_x32(t_s[b] + lane_off + c0, sa);
+      tmem_ld_x32(t_s[b] + lane_off + c0 + 32, sb);
+      tmem_ld_wait();
+      auto score = [&](int i) { return u2f(i < 32 ? sa[i] : sb[i - 32]); };  // i unrolled
       float mt = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 64; c += 32) {
-        uint32_t r[32];
-        tmem_ld_x32(t_s[b] + lane_off + c0 + c, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c0 + c + i < valid) mt = fmaxf(mt, u2f(r[i]));
-      }
+      for (int i = 0; i < 64; ++i)
+        if (c0 + i < valid) mt = fmaxf(mt, score(i));
       xch[half * 128 + row] = mt;
       if (!named_bar_and(1, 256, ok)) {
         ok = false;
@@ -245,29 +255,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_new = fmaxf(m_used, mt);
       const bool rescale = j == 0 || (m_new - m_used) * sl2 > 8.0f;
       const float mb = (rescale ? m_new : m_used) * sl2;
-      // pass 2: probabilities relative to the max in use, BF16-packed
+      // probabilities relative to the max in use, BF16-packed
       uint32_t pk[32];
       float ls = 0.0f;
 #pragma unroll
-      for (int c = 0; c < 64; c += 32) {
-        uint32_t r[32];
-        tmem_ld_x32(t_s[b] + lane_off + c0 + c, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int k = c0 + c + i;
-          const float p0 = k < valid ? exp2f(u2f(r[i]) * sl2 - mb) : 0.0f;
-          const float p1 = k + 1 < valid ? exp2f(u2f(r[i + 1]) * sl2 - mb) : 0.0f;
-          ls += p0 + p1;
-          pk[(c + i) >> 1] = pack_bf16(p0, p1);
-        }
+      for (int i = 0; i < 64; i += 2) {
+        const int k = c0 + i;
+        const float p0 = k < valid ? ex2_approx(score(i) * sl2 - mb) : 0.0f;
+        const float p1 = k + 1 < valid ? ex2_approx(score(i + 1) * sl2 - mb) : 0.0f;
+        ls += p0 + p1;
+        pk[i >> 1] = pack_bf16(p0, p1);
       }
       tc_fence_before();
       named_bar_sync(1, 256);
       if (wt == 0) mbar_arrive(&s_free[b]);
-      // P, V^T and O are free once the previous tile's P V has completed.
+      // P and O are free once the previous tile's P V has completed.
       if (j >= 1) ok = mbar_wait(pv_done, (j - 1) & 1);
-      if (ok) ok = mbar_wait(v_full, j & 1);
       if (!named_bar_and(1, 256, ok)) {
         ok = false;
         break;
@@ -292,41 +295,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (rescale) m_used = m_new;
       l += ls;
-      // V tile j -> V^T (K-major over keys): each warp transposes 2 key groups
-      // x 16 dim groups of 8 x 8 blocks.
-      {
-        const int m = lane >> 3, i8 = lane & 7;
-#pragma unroll
-        for (int kgi = 0; kgi < 2; ++kgi) {
-          const int kg = (wt >> 5) * 2 + kgi;
-          const int key = 8 * kg + i8;
-#pragma unroll
-          for (int dq = 0; dq < 16; dq += 4) {
-            const int dg = dq + m;
-            const uint32_t src = smem_u32(sv) + (dg >> 3) * kHalf + key * 128 +
-                                 ((((dg & 7) ^ (key & 7))) << 4);
-            uint32_t r0, r1, r2, r3;
-            ldmatrix_x4_trans(src, r0, r1, r2, r3);
-            const int dr = 8 * dg + i8;  // row i8 of destination matrix m
-            const uint32_t dst = smem_u32(svt) + (kg >> 3) * kHalf + dr * 128 +
-                                 ((((kg & 7) ^ (dr & 7))) << 4);
-            stmatrix_x4(dst, r0, r1, r2, r3);
-          }
-        }
-      }
       // this thread's 64 keys of the P row -> K-major tile over keys
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const uint32_t off = half * kHalf + row * 128 + ((i ^ (row & 7)) << 4);
         *reinterpret_cast<uint4*>(sp + off) = make_uint4(pk[i * 4], pk[i * 4 + 1], pk[i * 4 + 2], pk[i * 4 + 3]);
       }
-      fence_proxy_async_smem();  // P and V^T (generic stores) are read by the tensor core
+      fence_proxy_async_smem();  // P (generic stores) is read by the tensor core
       tc_fence_before();
       named_bar_sync(1, 256);
-      if (wt == 0) {
-        mbar_arrive(v_empty);
-        mbar_arrive(p_full);
-      }
+      if (wt == 0) mbar_arrive(p_full);
     }
     if (!ok) fail(a, kErrEpilogueTimeout);
     // row sum = both halves' sums

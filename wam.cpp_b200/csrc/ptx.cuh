@@ -337,11 +337,40 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
   return d;
 }
 
+// 2^x by the PTX ex2.approx.ftz.f32 instruction (the special-function unit
+// alone; results below 2^-126 flush to zero). For softmax probabilities that
+// are rounded to BF16 right after.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Shared-memory descriptor of an MN-major operand in the 128-byte swizzled
+// layout (a TMA box of 64 MN-contiguous BF16 per 128-byte row, one row per K
+// index): 8 K rows form a 1024-byte swizzle atom; atoms follow each other
+// along MN `lbo` bytes apart and along K `sbo` bytes apart. Used with the
+// instruction descriptor's MN-major bit for that operand.
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint32_t lbo,
+                                                       uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with BF16 A/B, F32 accumulator, both
 // operands K-major, shape M x N (x K=16).
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
+}
+// The same with the B operand MN-major (N contiguous in shared memory).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int m, int n) {
+  return umma_idesc_bf16(m, n) | (1u << 16);
 }
 
 // Bulk prefetch of a global range into L2 (16-byte aligned address and size).
