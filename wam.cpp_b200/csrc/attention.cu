@@ -220,14 +220,14 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
     }
     float corr[2], rs[2] = {0.0f, 0.0f};
 #pragma unroll
-    for (int r = 0; r < 2; ++r) corr[r] = exp2f((m_run[r] - mx[r]) * sl2);
+    for (int r = 0; r < 2; ++r) corr[r] = ex2_approx((m_run[r] - mx[r]) * sl2);
     uint32_t pf[4][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float p0 = exp2f((s[j][0] - mx[0]) * sl2);
-      const float p1 = exp2f((s[j][1] - mx[0]) * sl2);
-      const float p2 = exp2f((s[j][2] - mx[1]) * sl2);
-      const float p3 = exp2f((s[j][3] - mx[1]) * sl2);
+      const float p0 = ex2_approx((s[j][0] - mx[0]) * sl2);
+      const float p1 = ex2_approx((s[j][1] - mx[0]) * sl2);
+      const float p2 = ex2_approx((s[j][2] - mx[1]) * sl2);
+      const float p3 = ex2_approx((s[j][3] - mx[1]) * sl2);
       rs[0] += p0 + p1;
       rs[1] += p2 + p3;
       const int kk = j >> 1;
