@@ -6,13 +6,13 @@
 // 128. Both products run on the tensor cores with accumulators in TMEM:
 // S = Q K^T (M = 128 queries, N = 128 keys, K = 128 dims) into one of two S
 // buffers, O += P V^T (M = 128 queries, N = 128 dims, K = 128 keys) into O.
-// Roles (320 threads): warp 0 issues the TMA copies (4-D boxes of 128 rows x
+// Roles (576 threads): warp 0 issues the TMA copies (4-D boxes of 128 rows x
 // 64 dims with the 128-byte swizzle; rows past the end are zero-filled),
 // warp 1 owns TMEM and issues the MMAs (S of tile j + 1 before P V of tile j,
-// so the tensor core runs while the softmax works), warps 2-9 = two threads
-// per query row, each over half the keys / dims (the row max is exchanged
-// through shared memory): softmax from S in TMEM (one pass, the row's scores
-// held in registers), P as BF16 into a K-major tile, lazy rescaling of O in
+// so the tensor core runs while the softmax works), warps 2-17 = four threads
+// per query row, each over a quarter of the keys / dims (the row max and sum
+// are exchanged through shared memory): softmax from S in TMEM (one pass, the
+// thread's scores held in registers), P as BF16 into a K-major tile, lazy rescaling of O in
 // TMEM (only when the running max grows by more than 2^8), and the final
 // normalised BF16 rows. Q, K and P use the K-major swizzled layout of the GEMM
 // (csrc/gemm.cu); V tiles (double-buffered) are read by the tensor core as
@@ -35,7 +35,10 @@ namespace wamb {
 
 namespace {
 
-constexpr int kThreads = 320;             // warp 0 copies, 1 MMA, 2-9 softmax (2 per row)
+constexpr int kParts = 4;                 // softmax threads per query row
+constexpr int kCols = 128 / kParts;       // keys (of S) and dims (of O) per softmax thread
+constexpr int kSoftmax = 128 * kParts;    // softmax threads
+constexpr int kThreads = 64 + kSoftmax;   // warp 0 copies, 1 MMA, 2.. softmax
 constexpr int kRows = 128;                // queries per CTA (UMMA M, TMEM lanes)
 constexpr int kKeys = 128;                // keys per tile
 constexpr int kHalf = 128 * 64 * 2;       // 128 rows x 64 dims (or keys), swizzled: 16 KB
@@ -45,8 +48,8 @@ constexpr int kOffK = kTile;              // K ring [2][2 halves]
 constexpr int kOffV = 3 * kTile;          // V ring [2][2 halves of dims], rows = keys
 constexpr int kOffP = 5 * kTile;          // P [2 halves of keys], rows = queries
 constexpr int kOffBar = 6 * kTile;
-constexpr int kOffXch = kOffBar + 256;    // row max / sum exchange between a row's two threads
-constexpr int kSmem = 6 * kTile + 256 + 1024 + 1024 + 256;
+constexpr int kOffXch = kOffBar + 256;    // row max / sum exchange between a row's kParts threads
+constexpr int kSmem = 6 * kTile + 256 + 4 * 128 * kParts + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;       // S[0], S[1], O (128 columns each)
 
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
@@ -214,64 +217,64 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(o_full, 0);
     }
   } else {
-    // ----------------------------------------- softmax / P / V^T / output
-    // Two threads per query row (warps w and w + 4 share a TMEM lane
-    // quadrant); thread half h owns key columns and output dims 64h..64h+63.
+    // ------------------------------------------------- softmax / P / output
+    // kParts threads per query row (warps w, w + 4, ... share a TMEM lane
+    // quadrant); thread part p owns key columns and output dims
+    // kCols p .. kCols (p + 1) - 1.
     const int wt = threadIdx.x - 64;
     const int qd = warp & 3;  // TMEM lane quadrant
-    const int half = (warp - 2) >> 2;
+    const int part = (warp - 2) >> 2;
     const int row = qd * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
-    const int c0 = half * 64;
-    float* xch = reinterpret_cast<float*>(smem + kOffXch);  // [2][128]
+    const int c0 = part * kCols;
+    float* xch = reinterpret_cast<float*>(smem + kOffXch);  // [kParts][128]
     const float sl2 = a.scale * 1.4426950408889634f;
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
       const int b = j & 1;
-      // Each wait's outcome is AND-ed over the 256 threads at the next named
-      // barrier, so they all leave the loop together (a thread giving up
+      // Each wait's outcome is AND-ed over the softmax threads at the next
+      // named barrier, so they all leave the loop together (a thread giving up
       // alone would strand the others at the barrier).
       ok = mbar_wait(&s_full[b], (j >> 1) & 1);
       tc_fence_after();
       const int valid = a.lk - j * kKeys < kKeys ? a.lk - j * kKeys : kKeys;
-      // This thread's 64 scores of the row, read from TMEM once; row max over
-      // its valid keys, combined with its partner's.
-      uint32_t sa[32], sb[32];
-      tmem_ld_x32(t_s[b] + lane_off + c0, sa);
-      tmem_ld_x32(t_s[b] + lane_off + c0 + 32, sb);
+      // This thread's kCols scores of the row, read from TMEM once; row max
+      // over its valid keys, combined with the row's other parts.
+      uint32_t sc[kCols];
+      tmem_ld_x32(t_s[b] + lane_off + c0, sc);
       tmem_ld_wait();
-      auto score = [&](int i) { return u2f(i < 32 ? sa[i] : sb[i - 32]); };  // i unrolled
       float mt = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 64; ++i)
-        if (c0 + i < valid) mt = fmaxf(mt, score(i));
-      xch[half * 128 + row] = mt;
-      if (!named_bar_and(1, 256, ok)) {
+      for (int i = 0; i < kCols; ++i)
+        if (c0 + i < valid) mt = fmaxf(mt, u2f(sc[i]));
+      xch[part * 128 + row] = mt;
+      if (!named_bar_and(1, kSoftmax, ok)) {
         ok = false;
         break;
       }
-      mt = fmaxf(xch[row], xch[128 + row]);
+#pragma unroll
+      for (int q = 0; q < kParts; ++q) mt = fmaxf(mt, xch[q * 128 + row]);
       const float m_new = fmaxf(m_used, mt);
       const bool rescale = j == 0 || (m_new - m_used) * sl2 > 8.0f;
       const float mb = (rescale ? m_new : m_used) * sl2;
       // probabilities relative to the max in use, BF16-packed
-      uint32_t pk[32];
+      uint32_t pk[kCols / 2];
       float ls = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) {
+      for (int i = 0; i < kCols; i += 2) {
         const int k = c0 + i;
-        const float p0 = k < valid ? ex2_approx(score(i) * sl2 - mb) : 0.0f;
-        const float p1 = k + 1 < valid ? ex2_approx(score(i + 1) * sl2 - mb) : 0.0f;
+        const float p0 = k < valid ? ex2_approx(u2f(sc[i]) * sl2 - mb) : 0.0f;
+        const float p1 = k + 1 < valid ? ex2_approx(u2f(sc[i + 1]) * sl2 - mb) : 0.0f;
         ls += p0 + p1;
         pk[i >> 1] = pack_bf16(p0, p1);
       }
       tc_fence_before();
-      named_bar_sync(1, 256);
+      named_bar_sync(1, kSoftmax);
       if (wt == 0) mbar_arrive(&s_free[b]);
       // P and O are free once the previous tile's P V has completed.
       if (j >= 1) ok = mbar_wait(pv_done, (j - 1) & 1);
-      if (!named_bar_and(1, 256, ok)) {
+      if (!named_bar_and(1, kSoftmax, ok)) {
         ok = false;
         break;
       }
@@ -281,38 +284,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (__any_sync(0xffffffffu, rescale) && j > 0) {
         const float corr = exp2f((m_used - m_new) * sl2);
         const float f = rescale ? corr : 1.0f;
-#pragma unroll 1
-        for (int c = 0; c < 64; c += 32) {
-          uint32_t r[32];
-          tmem_ld_x32(t_o + lane_off + c0 + c, r);
-          tmem_ld_wait();
+        uint32_t r[kCols];
+        tmem_ld_x32(t_o + lane_off + c0, r);
+        tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(u2f(r[i]) * f);
-          tmem_st_x32(t_o + lane_off + c0 + c, r);
-        }
+        for (int i = 0; i < kCols; ++i) r[i] = __float_as_uint(u2f(r[i]) * f);
+        tmem_st_x32(t_o + lane_off + c0, r);
         tmem_st_wait();
         if (rescale) l *= corr;
       }
       if (rescale) m_used = m_new;
       l += ls;
-      // this thread's 64 keys of the P row -> K-major tile over keys
+      // this thread's kCols keys of the P row -> K-major tile over keys (64-key
+      // halves of 8 swizzled 16-byte chunks per row)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t off = half * kHalf + row * 128 + ((i ^ (row & 7)) << 4);
+      for (int i = 0; i < kCols / 8; ++i) {
+        const int key = c0 + 8 * i;
+        const int chunk = (key & 63) >> 3;
+        const uint32_t off = (key >> 6) * kHalf + row * 128 + ((chunk ^ (row & 7)) << 4);
         *reinterpret_cast<uint4*>(sp + off) = make_uint4(pk[i * 4], pk[i * 4 + 1], pk[i * 4 + 2], pk[i * 4 + 3]);
       }
       fence_proxy_async_smem();  // P (generic stores) is read by the tensor core
       tc_fence_before();
-      named_bar_sync(1, 256);
+      named_bar_sync(1, kSoftmax);
       if (wt == 0) mbar_arrive(p_full);
     }
     if (!ok) fail(a, kErrEpilogueTimeout);
-    // row sum = both halves' sums
-    xch[half * 128 + row] = l;
-    named_bar_sync(1, 256);
-    l = xch[row] + xch[128 + row];
+    // row sum = the parts' sums
+    xch[part * 128 + row] = l;
+    named_bar_sync(1, kSoftmax);
+    l = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kParts; ++q) l += xch[q * 128 + row];
     if (ok) ok = mbar_wait(o_full, 0);
-    if (named_bar_and(1, 256, ok)) {
+    if (named_bar_and(1, kSoftmax, ok)) {
       tc_fence_after();
       const int qr = q0 + row;
       bf16* dst = nullptr;
@@ -326,20 +331,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         dst += head * 128 + c0;
       }
       const float inv = 1.0f / l;
-#pragma unroll 1
-      for (int c = 0; c < 64; c += 32) {
-        uint32_t r[32];
-        tmem_ld_x32(t_o + lane_off + c0 + c, r);
-        tmem_ld_wait();
-        if (dst) {
+      uint32_t r[kCols];
+      tmem_ld_x32(t_o + lane_off + c0, r);
+      tmem_ld_wait();
+      if (dst) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(dst + c + q * 8) =
-                make_uint4(pack_bf16(u2f(r[8 * q]) * inv, u2f(r[8 * q + 1]) * inv),
-                           pack_bf16(u2f(r[8 * q + 2]) * inv, u2f(r[8 * q + 3]) * inv),
-                           pack_bf16(u2f(r[8 * q + 4]) * inv, u2f(r[8 * q + 5]) * inv),
-                           pack_bf16(u2f(r[8 * q + 6]) * inv, u2f(r[8 * q + 7]) * inv));
-        }
+        for (int q = 0; q < kCols / 8; ++q)
+          *reinterpret_cast<uint4*>(dst + q * 8) =
+              make_uint4(pack_bf16(u2f(r[8 * q]) * inv, u2f(r[8 * q + 1]) * inv),
+                         pack_bf16(u2f(r[8 * q + 2]) * inv, u2f(r[8 * q + 3]) * inv),
+                         pack_bf16(u2f(r[8 * q + 4]) * inv, u2f(r[8 * q + 5]) * inv),
+                         pack_bf16(u2f(r[8 * q + 6]) * inv, u2f(r[8 * q + 7]) * inv));
       }
     }
   }
