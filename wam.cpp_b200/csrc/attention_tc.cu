@@ -49,7 +49,7 @@ constexpr int kOffV = 3 * kTile;          // V ring [2][2 halves of dims], rows 
 constexpr int kOffP = 5 * kTile;          // P [2 halves of keys], rows = queries
 constexpr int kOffBar = 6 * kTile;
 constexpr int kOffXch = kOffBar + 256;    // row max / sum exchange between a row's kParts threads
-constexpr int kSmem = 6 * kTile + 256 + 4 * 128 * kParts + 1024 + 256;
+constexpr int kSmem = 6 * kTile + 256 + 2 * 4 * 128 * kParts + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;       // S[0], S[1], O (128 columns each)
 
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
@@ -90,6 +90,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
     for (int i = 0; i < 16; ++i) mbar_init(&bars[i], 1);
+    // S buffers and P are released / published by every softmax warp
+    for (int i = 0; i < 2; ++i) mbar_init(&s_free[i], kSoftmax / 32);
+    mbar_init(p_full, kSoftmax / 32);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -227,16 +230,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = qd * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
     const int c0 = part * kCols;
-    float* xch = reinterpret_cast<float*>(smem + kOffXch);  // [kParts][128]
+    float* xch_base = reinterpret_cast<float*>(smem + kOffXch);  // [2][kParts][128]
     const float sl2 = a.scale * 1.4426950408889634f;
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
+    // One CTA-wide barrier per tile (the row max exchange; its buffer
+    // alternates by tile parity, so a thread that passes it cannot overwrite
+    // what a slower one still reads). S buffers and P are released per warp.
+    // Every wait's outcome is AND-ed over the softmax threads at that barrier,
+    // so they all leave the loop together (a thread giving up alone would
+    // strand the others at the barrier).
     for (int j = 0; j < nk; ++j) {
       const int b = j & 1;
-      // Each wait's outcome is AND-ed over the softmax threads at the next
-      // named barrier, so they all leave the loop together (a thread giving up
-      // alone would strand the others at the barrier).
-      ok = mbar_wait(&s_full[b], (j >> 1) & 1);
+      float* xch = xch_base + b * kParts * 128;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1)) ok = false;
       tc_fence_after();
       const int valid = a.lk - j * kKeys < kKeys ? a.lk - j * kKeys : kKeys;
       // This thread's kCols scores of the row, read from TMEM once; row max
@@ -270,14 +277,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[i >> 1] = pack_bf16(p0, p1);
       }
       tc_fence_before();
-      named_bar_sync(1, kSoftmax);
-      if (wt == 0) mbar_arrive(&s_free[b]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[b]);
       // P and O are free once the previous tile's P V has completed.
-      if (j >= 1) ok = mbar_wait(pv_done, (j - 1) & 1);
-      if (!named_bar_and(1, kSoftmax, ok)) {
-        ok = false;
-        break;
-      }
+      if (j >= 1 && !mbar_wait(pv_done, (j - 1) & 1)) ok = false;
       tc_fence_after();
       // The TMEM loads / stores are warp-collective: the warp runs them when
       // any of its rows rescales, and the other rows scale by 1.
@@ -306,16 +309,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();  // P (generic stores) is read by the tensor core
       tc_fence_before();
-      named_bar_sync(1, kSoftmax);
-      if (wt == 0) mbar_arrive(p_full);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
     }
     if (!ok) fail(a, kErrEpilogueTimeout);
     // row sum = the parts' sums
-    xch[part * 128 + row] = l;
-    named_bar_sync(1, kSoftmax);
-    l = 0.0f;
+    {
+      float* xch = xch_base + (nk & 1) * kParts * 128;
+      xch[part * 128 + row] = l;
+      named_bar_sync(1, kSoftmax);
+      l = 0.0f;
 #pragma unroll
-    for (int q = 0; q < kParts; ++q) l += xch[q * 128 + row];
+      for (int q = 0; q < kParts; ++q) l += xch[q * 128 + row];
+    }
     if (ok) ok = mbar_wait(o_full, 0);
     if (named_bar_and(1, kSoftmax, ok)) {
       tc_fence_after();
