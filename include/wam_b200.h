@@ -457,6 +457,13 @@ typedef struct wam_b200_graph_profile {
 WAM_B200_API int wam_b200_profile_graph(wam_b200_engine* engine, int batch, int phase, int kind,
                                         int reps, wam_b200_graph_profile* out,
                                         wam_b200_status* status);
+/* The same restricted to the ops of one lane of the phase (lane 0: the main
+ * stream, e.g. the prefix's 768 visual tokens; lane 1: the side stream, e.g.
+ * the prefix state token's action-expert work; -1: every lane). */
+WAM_B200_API int wam_b200_profile_graph_lane(wam_b200_engine* engine, int batch, int phase,
+                                             int kind, int lane, int reps,
+                                             wam_b200_graph_profile* out,
+                                             wam_b200_status* status);
 
 /* Stage dumps as F32 (the reference's WAM_GWP05_CACHE_DUMP_DIR stages,
  * engine/cache.cpp:441-469): "prefix_k"/"prefix_v" [heads][1+V][128],

@@ -1693,7 +1693,8 @@ bool MotEngine::profile(int batch, std::vector<OpProfile>* out, std::string* err
   return true;
 }
 
-bool MotEngine::profile_graph(int batch, int phase, int kind, int reps, float* ms, double* bytes,
+bool MotEngine::profile_graph(int batch, int phase, int kind, int lane, int reps, float* ms,
+                              double* bytes,
                               double* flops, int* launches, std::string* err) {
   if (batch != staged_batch_) {
     *err = "profile_graph() batch differs from the staged batch";
@@ -1716,7 +1717,7 @@ bool MotEngine::profile_graph(int batch, int phase, int kind, int reps, float* m
   CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
   cudaError_t le = cudaSuccess;
   for (auto& op : p.ops) {
-    if (op.kind != kind) continue;
+    if (op.kind != kind || (lane >= 0 && op.lane != lane)) continue;
     le = op.fn(stream_);  // every lane on the main stream: one chain of launches
     if (le != cudaSuccess) break;
     *bytes += op.bytes;

@@ -166,7 +166,8 @@ class MotEngine {
   // captured alone into a CUDA graph (same launches, same buffers, PDL between
   // them) and replayed `reps` times between events: ms per replay, plus their
   // algorithmic bytes / FLOPs and kernel launches per replay.
-  bool profile_graph(int batch, int phase, int kind, int reps, float* ms, double* bytes,
+  // lane: -1 = every lane, else only the ops of that lane (0 main, 1 side).
+  bool profile_graph(int batch, int phase, int kind, int lane, int reps, float* ms, double* bytes,
                      double* flops, int* launches, std::string* err);
   // Device times of the phases of the last run() (ms): prompt, prefix, denoise.
   bool last_phase_ms(float* prompt, float* prefix, float* denoise);

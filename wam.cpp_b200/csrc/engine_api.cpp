@@ -261,12 +261,20 @@ WAM_B200_API int wam_b200_profile(wam_b200_engine* e, int batch, wam_b200_op_pro
 WAM_B200_API int wam_b200_profile_graph(wam_b200_engine* e, int batch, int phase, int kind,
                                         int reps, wam_b200_graph_profile* out,
                                         wam_b200_status* st) {
+  return wam_b200_profile_graph_lane(e, batch, phase, kind, -1, reps, out, st);
+}
+
+WAM_B200_API int wam_b200_profile_graph_lane(wam_b200_engine* e, int batch, int phase, int kind,
+                                             int lane, int reps, wam_b200_graph_profile* out,
+                                             wam_b200_status* st) {
   if (!e || !out) return fail(st, WAM_B200_INVALID_ARGUMENT, "engine and output are required");
+  if (lane < -1 || lane > 1) return fail(st, WAM_B200_INVALID_ARGUMENT, "lane is -1, 0 or 1");
   std::string err;
   float ms = 0.0f;
   double bytes = 0.0, flops = 0.0;
   int launches = 0;
-  if (!e->impl->profile_graph(batch, phase, kind, reps, &ms, &bytes, &flops, &launches, &err))
+  if (!e->impl->profile_graph(batch, phase, kind, lane, reps, &ms, &bytes, &flops, &launches,
+                              &err))
     return fail(st, code_of(err), err);
   out->ms = ms;
   out->bytes = bytes;

@@ -89,5 +89,7 @@ def attach(lib, sig) -> None:
     sig(lib, "wam_b200_phase_ms", i32, [vp, f32p, f32p, f32p])
     sig(lib, "wam_b200_profile", i32, [vp, i32, C.POINTER(OpProfile), i32, st])
     sig(lib, "wam_b200_profile_graph", i32, [vp, i32, i32, i32, i32, C.POINTER(GraphProfile), st])
+    sig(lib, "wam_b200_profile_graph_lane", i32,
+        [vp, i32, i32, i32, i32, i32, C.POINTER(GraphProfile), st])
     sig(lib, "wam_b200_block_forward", i32,
         [vp, C.POINTER(BlockInputs), f32p, sz, f32p, sz, f32p, st])

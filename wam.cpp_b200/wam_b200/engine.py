@@ -228,13 +228,16 @@ class Engine:
                  "ms": a.ms, "bytes": a.bytes, "flops": a.flops, "shape": list(a.shape)}
                 for a in arr[:rc]]
 
-    def profile_graph(self, batch: int, phase: str, kind: str, reps: int = 5) -> dict:
+    def profile_graph(self, batch: int, phase: str, kind: str, reps: int = 5,
+                      lane: int = -1) -> dict:
         """Device time of the (phase, kind) ops of the staged batch replayed
-        alone in a CUDA graph (wam_b200_profile_graph)."""
+        alone in a CUDA graph (wam_b200_profile_graph_lane; lane -1 = all,
+        0 = main stream, 1 = side stream)."""
         out, st = GraphProfile(), Status()
-        rc = self.lib.wam_b200_profile_graph(self.h, batch, PHASES.index(phase), KINDS.index(kind),
-                                             reps, C.byref(out), C.byref(st))
-        _raise(self.lib, rc, st, "wam_b200_profile_graph")
+        rc = self.lib.wam_b200_profile_graph_lane(self.h, batch, PHASES.index(phase),
+                                                  KINDS.index(kind), lane, reps, C.byref(out),
+                                                  C.byref(st))
+        _raise(self.lib, rc, st, "wam_b200_profile_graph_lane")
         return {"ms": out.ms, "bytes": out.bytes, "flops": out.flops, "launches": out.launches}
 
     def block_forward(self, t: float, xv, xa, tv, ta, with_time: bool = False):
