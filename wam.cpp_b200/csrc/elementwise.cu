@@ -260,10 +260,12 @@ __device__ __forceinline__ float rope_theta(const QkvScatter& a, int dim, int po
 }
 
 // One block per token row, threadIdx.y = part (0 q, 1 k, 2 v), 128 threads per
-// part; each thread holds up to MAXC 8-wide chunks of its part (and the norm
-// weights) in registers. MAXC = 0: generic loop.
+// part; each thread holds up to MAXC 8-wide chunks of its part in registers
+// (the norm weights, 12 KB shared by every row, are read again from L1 / L2
+// when the chunk is written), so that three blocks fit an SM and more of the
+// rows' bytes are in flight. MAXC = 0: generic loop.
 template <int MAXC>
-__global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const __grid_constant__ QkvScatter a) {
+__global__ void __launch_bounds__(3 * kRowThreads, 3) qkv_scatter_kernel(const __grid_constant__ QkvScatter a) {
   griddep_wait();
   griddep_launch_dependents();
   __shared__ float red[3][4];
@@ -296,10 +298,12 @@ __global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const __gr
   }
   const int pos1 = a.pos_base + rin;
   const bool rope = a.rope_mode != 0 && which < 2;
-  auto emit = [&](int c, float (&f)[8], const float (&w)[8], float inv) {
+  auto emit = [&](int c, float (&f)[8], float inv) {
     const int d = c * 8;
     const int hd = d & 127;
     if (nw) {
+      float w[8];
+      load8(nw + c * 8, w);
 #pragma unroll
       for (int i = 0; i < 8; ++i) f[i] = f[i] * inv * w[i];
     }
@@ -316,7 +320,7 @@ __global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const __gr
     store8(dst_base + (d >> 7) * head_stride + hd, f);
   };
   if constexpr (MAXC > 0) {
-    float v[MAXC][8], w[MAXC][8];
+    float v[MAXC][8];
     float ss = 0.0f;
     if (col >= 0) {
 #pragma unroll
@@ -324,7 +328,6 @@ __global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const __gr
         const int c = tid + i * kRowThreads;
         if (c < chunks) {
           load8(src + c * 8, v[i]);
-          if (nw) load8(nw + c * 8, w[i]);
 #pragma unroll
           for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
         }
@@ -340,7 +343,7 @@ __global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const __gr
 #pragma unroll
     for (int i = 0; i < MAXC; ++i) {
       const int c = tid + i * kRowThreads;
-      if (c < chunks) emit(c, v[i], w[i], inv);
+      if (c < chunks) emit(c, v[i], inv);
     }
   } else {
     float ss = 0.0f;
@@ -359,10 +362,9 @@ __global__ void __launch_bounds__(3 * kRowThreads) qkv_scatter_kernel(const __gr
     if (col < 0) return;
     const float inv = nw ? rsqrtf(tot / a.hidden + a.eps) : 1.0f;
     for (int c = tid; c < chunks; c += kRowThreads) {
-      float f[8], w[8];
+      float f[8];
       load8(src + c * 8, f);
-      if (nw) load8(nw + c * 8, w);
-      emit(c, f, w, inv);
+      emit(c, f, inv);
     }
   }
 }
