@@ -505,8 +505,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sel1 = 0x7540u | (2 * (j & 1) + 1);
           const float f0 = __uint_as_float(__byte_perm(word, 0x4B000000u, sel0));
           const float f1 = __uint_as_float(__byte_perm(word, 0x4B000000u, sel1));
-          const __nv_bfloat162 h =
-              __floats2bfloat162_rn((f0 - 8388736.0f) * d, (f1 - 8388736.0f) * d);
+          // (f - (2^23 + 128)) * d for both values with packed F32 pairs (each
+          // lane rounds as the scalar subtract and multiply would)
+          const float2 qd = __fmul2_rn(__fadd2_rn(make_float2(f0, f1), make_float2(-8388736.0f, -8388736.0f)),
+                                       make_float2(d, d));
+          const __nv_bfloat162 h = __floats2bfloat162_rn(qd.x, qd.y);
           o[j] = *reinterpret_cast<const uint32_t*>(&h);
         }
         const int ca = 2 * c2, cb = 2 * c2 + 1;
