@@ -41,7 +41,9 @@ constexpr int kTM = 128;              // token rows per tile (UMMA M, TMEM lanes
 constexpr int kWN = 256;              // weight rows per tile (UMMA N, TMEM columns)
 constexpr int kBK = 64;               // K per stage: one 128-byte swizzle row of BF16
 constexpr int kBBytes = kWN * kBK * 2;  // weight tile per stage (32 KB)
-constexpr int kThreads = 256;  // warp 0 copies, 1 MMA, 2-5 epilogue, 2-7 Q8_0 conversion
+constexpr int kThreads = 256;  // warp 0 copies, 1 MMA, 2-5 epilogue
+// gemm_tc_kernel with Q8_0 weights: warps 2-11 convert the stages to BF16.
+constexpr int kThreadsQ8 = 384;
 #ifndef WAM_GEMM_STAGE_BUDGET_KB
 #define WAM_GEMM_STAGE_BUDGET_KB 200
 #endif
@@ -404,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // CTA x = (tile, split) with the split index fastest (one cluster = the splits
 // of one output tile) and the token tile next, so the CTAs that share a weight
 // tile run side by side and the weight tile is read from HBM once.
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsQ8, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ GemmArgs args) {
@@ -473,12 +475,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   griddep_launch_dependents();
 
   bool ok = true;
-  // Q8_0 -> BF16 of every stage of the mainloop by warps 2-7 (ct = 0..191):
+  // Q8_0 -> BF16 of every stage of the mainloop by warps 2.. (ct = 0 ..
+  // conv_threads - 1; the Q8_0 launch has kThreadsQ8 threads):
   // 16 weights (half a Q8_0 block, one scale) per thread and step, two 16-byte
   // swizzled chunks of the UMMA operand row. value = q * d exactly: the byte
   // becomes the float 2^23 + (q + 128) through a byte permute; subtracting
   // 2^23 + 128 leaves q (exact, integers below 2^24), and q * d is exact in F32
   // (8 + 11 significant bits); then rounded to BF16.
+  const int conv_threads = static_cast<int>(blockDim.x) - 64;
   auto q8_convert_stages = [&](int ct) {
     for (int i = 0; i < nkb; ++i) {
       const int s = i % S;
@@ -490,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t* raw = smem_q8 + s * kQ8TileBytes;
       uint8_t* wst = smem_w + s * kBBytes;
 #pragma unroll 2
-      for (int it = ct; it < kWN * 4; it += 192) {
+      for (int it = ct; it < kWN * 4; it += conv_threads) {
         const int r = it >> 2, c2 = it & 3;
         const uint4 qv = *reinterpret_cast<const uint4*>(raw + r * 64 + c2 * 16);
         const float d = __half2float(
@@ -517,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint4*>(wst + r * 128 + ((cb ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
       }
       fence_proxy_async_smem();  // generic-proxy writes -> the tensor cores' async proxy
-      named_bar_sync(2, 192);
+      named_bar_sync(2, conv_threads);
       if (ct == 0) mbar_arrive(&conv[s]);
     }
   };
@@ -737,7 +741,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // order; consecutive threads read consecutive 64-byte token rows.
     cluster_sync_all();
     {
-      // All 192 threads: one (16-feature chunk, token, half) item each pass.
+      // All threads: one (16-feature chunk, token, half) item each pass.
       const bool ok_all = *ok_flag != 0;
       const int sp_n = args.splits;
       const int items = rows * (kWN / 8);
@@ -745,7 +749,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int i1 = static_cast<int>((static_cast<long long>(split + 1) * items) / sp_n);
       const size_t tile_floats = static_cast<size_t>(args.a_rows) * kWN;
       const float* ws_tile = args.workspace + static_cast<size_t>(tile) * sp_n * tile_floats;
-      for (int it = i0 + static_cast<int>(threadIdx.x); it < i1; it += kThreads) {
+      for (int it = i0 + static_cast<int>(threadIdx.x); it < i1; it += static_cast<int>(blockDim.x)) {
         const int c = it / (2 * rows), rem = it % (2 * rows);
         const int rr = rem >> 1, h = rem & 1;
         const float* src0 = ws_tile + (static_cast<size_t>(c) * args.a_rows + rr) * 16 + h * 8;
@@ -1773,6 +1777,7 @@ cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream) {
   if (op.pair) return cudaLaunchKernelEx(&cfg, gemm_tc_pair_kernel, op.tm_w, op.tm_x, op.args);
   if (op.stream) return cudaLaunchKernelEx(&cfg, gemm_stream_kernel, op.tm_w, op.tm_x, op.args);
   if (op.persistent) return cudaLaunchKernelEx(&cfg, gemm_tc_persistent_kernel, op.tm_w, op.tm_x, op.args);
+  if (op.args.w_q8) cfg.blockDim = dim3(kThreadsQ8, 1, 1);
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, op.tm_w, op.tm_x, op.args);
 }
 
