@@ -206,6 +206,7 @@ MotEngine::~MotEngine() {
   drop_plans();
   for (auto& e : phase_ev_)
     if (e) cudaEventDestroy(e);
+  if (h2d_ev_) cudaEventDestroy(h2d_ev_);
   for (void* p : allocs_) cudaFree(p);
   if (h_state_) cudaFreeHost(h_state_);
   if (h_latent_) cudaFreeHost(h_latent_);
@@ -322,6 +323,9 @@ bool MotEngine::init(const EngineOptions& opt, std::string* err) {
   CK(cudaStreamSynchronize(stream_));
   prompt_key_.assign(opt.max_batch, {});
   in_prompt_key_.assign(opt.max_batch, {});
+  h_prompt_ver_.assign(opt.max_batch, 0);
+  h_prompt_rows_.assign(opt.max_batch, 0);
+  prompt_copy_.assign(opt.max_batch, 0);
   ok_ = true;
   return true;
 }
@@ -1474,6 +1478,8 @@ bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
   }
   const int A = g.action_dim, T = g.action_chunk, Nt = g.prompt_tokens, D = g.text_dim;
   const long long lat = static_cast<long long>(g.vae_z) * 4 * g.visual();
+  // The previous batch's copies out of the pinned buffers have completed.
+  if (h2d_ev_) CK(cudaEventSynchronize(h2d_ev_));
   staged_keys_.assign(batch, {});
   for (int i = 0; i < batch; ++i) {
     const RequestView& r = reqs[i];
@@ -1535,13 +1541,25 @@ bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
         }
     }
     if (r.prompt) {
+      // The slot's pinned buffer keeps the last prompt staged through it. With
+      // the projected-prompt cache, an unchanged prompt (compared byte for
+      // byte) keeps the slot's version, which is its cache key; any other
+      // prompt is copied in under a new version. (The device copy below runs
+      // for every request either way.)
+      // The host copy itself runs below, in pieces overlapped with their
+      // device copies.
       float* pr = h_prompt_ + static_cast<size_t>(i) * Nt * D;
-      std::memcpy(pr, r.prompt, static_cast<size_t>(r.prompt_tokens) * D * 4);
-      std::memset(pr + static_cast<size_t>(r.prompt_tokens) * D, 0,
-                  static_cast<size_t>(Nt - r.prompt_tokens) * D * 4);
+      const size_t nb = static_cast<size_t>(r.prompt_tokens) * D * 4;
+      const bool same = opt_.prompt_cache && h_prompt_ver_[i] != 0 &&
+                        h_prompt_rows_[i] == r.prompt_tokens && std::memcmp(pr, r.prompt, nb) == 0;
+      prompt_copy_[i] = !same;
+      if (!same) {
+        h_prompt_ver_[i] = prompt_ver_next_++;
+        h_prompt_rows_[i] = r.prompt_tokens;
+      }
       key.assign(1, 'E');
-      const uint8_t* pb = reinterpret_cast<const uint8_t*>(pr);
-      key.insert(key.end(), pb, pb + static_cast<size_t>(Nt) * D * 4);
+      const uint8_t* vb = reinterpret_cast<const uint8_t*>(&h_prompt_ver_[i]);
+      key.insert(key.end(), vb, vb + sizeof(uint64_t));
     }
     float* nz = h_noise_ + static_cast<size_t>(i) * T * A;
     if (r.noise) {
@@ -1577,8 +1595,30 @@ bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
   for (int i = 0; i < batch; ++i) {
     const size_t pn = static_cast<size_t>(Nt) * D;
     if (reqs[i].prompt) {
-      CK(cudaMemcpyAsync(in_prompt_ + i * pn, h_prompt_ + i * pn, pn * 4, cudaMemcpyHostToDevice,
-                         stream_));
+      float* pr = h_prompt_ + i * pn;
+      if (prompt_copy_[i]) {
+        // 1 MB pieces: each piece's DMA runs while the next one is copied
+        // into the pinned slot (no earlier copy reads the slot any more:
+        // h2d_ev_ was waited for above).
+        const size_t rows_b = static_cast<size_t>(reqs[i].prompt_tokens) * D * 4;
+        const size_t piece = size_t(1) << 20;
+        for (size_t off = 0; off < pn * 4; off += piece) {
+          const size_t len = pn * 4 - off < piece ? pn * 4 - off : piece;
+          uint8_t* dst = reinterpret_cast<uint8_t*>(pr) + off;
+          if (off + len <= rows_b) {
+            std::memcpy(dst, reinterpret_cast<const uint8_t*>(reqs[i].prompt) + off, len);
+          } else if (off >= rows_b) {
+            std::memset(dst, 0, len);
+          } else {
+            std::memcpy(dst, reinterpret_cast<const uint8_t*>(reqs[i].prompt) + off, rows_b - off);
+            std::memset(dst + (rows_b - off), 0, off + len - rows_b);
+          }
+          CK(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(in_prompt_ + i * pn) + off, dst, len,
+                             cudaMemcpyHostToDevice, stream_));
+        }
+      } else {
+        CK(cudaMemcpyAsync(in_prompt_ + i * pn, pr, pn * 4, cudaMemcpyHostToDevice, stream_));
+      }
       in_prompt_key_[i].clear();
     } else if (in_prompt_key_[i] != staged_keys_[i]) {
       std::string terr;
@@ -1593,6 +1633,8 @@ bool MotEngine::stage(const RequestView* reqs, int batch, std::string* err) {
     }
   }
   CK(cudaMemcpyAsync(in_noise_, h_noise_, static_cast<size_t>(batch) * T * A * 4, cudaMemcpyHostToDevice, stream_));
+  if (!h2d_ev_) CK(cudaEventCreateWithFlags(&h2d_ev_, cudaEventDisableTiming));
+  CK(cudaEventRecord(h2d_ev_, stream_));
   staged_batch_ = batch;
   return true;
 }

@@ -204,6 +204,9 @@ class MotEngine {
     int scratch_gen = 0;  // split-K scratch generation the launches point into
   };
   cudaEvent_t phase_ev_[4] = {nullptr, nullptr, nullptr, nullptr};
+  // Recorded after a batch's host-to-device copies: the next stage() waits
+  // for it before it rewrites the pinned host buffers those copies read.
+  cudaEvent_t h2d_ev_ = nullptr;
   bool phase_prompt_ran_ = false;
   void drop_plans();
   int scratch_gen_ = 0;
@@ -282,6 +285,13 @@ class MotEngine {
   // valid token ids; staged_keys_ are those of the staged batch.
   std::vector<std::vector<uint8_t>> prompt_key_, staged_keys_;
   std::vector<std::vector<uint8_t>> in_prompt_key_;  // token prompt held in in_prompt_ per slot
+  // Version of the embedding prompt in each slot of h_prompt_ (0: none yet) and
+  // its row count: the key of an embedding prompt is its slot's version, which
+  // changes only when a different prompt is staged through the slot.
+  std::vector<uint64_t> h_prompt_ver_;
+  std::vector<int> h_prompt_rows_;
+  std::vector<char> prompt_copy_;  // staged batch: slot's prompt is copied into h_prompt_
+  uint64_t prompt_ver_next_ = 1;
   bool prompt_valid_ = false;
   int staged_batch_ = 0;
   std::mt19937 rng_{0x5eed};
