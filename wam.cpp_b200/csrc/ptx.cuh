@@ -127,6 +127,23 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
 
 // Contiguous bulk copy global -> shared completing on an mbarrier (16-byte
 // aligned addresses, size a multiple of 16).
+// Bulk copy shared -> global (both 16-byte aligned, bytes a multiple of 16),
+// in the executing thread's bulk async-group.
+__device__ __forceinline__ void bulk_store(void* dst, const void* src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(dst)),
+               "r"(smem_u32(src_smem)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every bulk copy this thread committed has completed its writes.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's completed async-proxy global writes before its later
+// generic-proxy operations (e.g. a release that other CTAs acquire).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                           uint64_t cache_policy) {
   asm volatile(
