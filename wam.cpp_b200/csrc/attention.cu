@@ -119,7 +119,9 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int split = SPLIT ? static_cast<int>(blockIdx.x) % splits : 0;
-  const int q0 = (SPLIT ? static_cast<int>(blockIdx.x) / splits : static_cast<int>(blockIdx.x)) * kBQ;
+  const int qblk = SPLIT ? static_cast<int>(blockIdx.x) / splits : static_cast<int>(blockIdx.x);
+  const int q0 = a.q_begin + qblk * kBQ;
+  const int q_end = a.q_end > 0 ? a.q_end : a.lq;
   const int head = blockIdx.y;
   const int seq = blockIdx.z;
 
@@ -294,8 +296,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
     const size_t slot_floats = static_cast<size_t>(kBQ) * kOld;
     float* ws_blk = nullptr;
     if (gx) {
-      const size_t blk = (static_cast<size_t>(seq) * gridDim.y + head) * (gridDim.x / splits) +
-                         (q0 / kBQ);
+      const size_t blk = (static_cast<size_t>(seq) * gridDim.y + head) * (gridDim.x / splits) + qblk;
       ws_blk = a.ws + blk * splits * slot_floats;
       __syncthreads();
       float* mine = ws_blk + split * slot_floats;
@@ -319,7 +320,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
     const int row = q0 + row_l;
     const uint32_t o_base = smem_u32(o_s), m_base = smem_u32(m_s), l_base = smem_u32(l_s);
     bf16* dst = nullptr;
-    if (row < a.lq) {
+    if (row < q_end) {
       if (a.split_first) {
         dst = row == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
                        : a.out + (static_cast<long long>(seq) * (a.lq - 1) + row - 1) * a.ldo;
@@ -341,7 +342,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int row = q0 + warp * 16 + (lane >> 2) + r * 8;
-      if (row >= a.lq) continue;
+      if (row >= q_end) continue;
       bf16* dst;
       if (a.split_first) {
         dst = row == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
@@ -370,8 +371,13 @@ cudaError_t attention_init() {
                               kSmem);
 }
 
+namespace {
+// Query rows this launch computes.
+int launch_rows(const AttnArgs& a) { return (a.q_end > 0 ? a.q_end : a.lq) - a.q_begin; }
+}  // namespace
+
 int attention_splits(const AttnArgs& a, int num_sms) {
-  const int qblocks = (a.lq + kBQ - 1) / kBQ;
+  const int qblocks = (launch_rows(a) + kBQ - 1) / kBQ;
   const int ctas = qblocks * a.heads * a.batch;
   const int kblocks = (a.lk + kBKey - 1) / kBKey;
   const int slots = 2 * num_sms;  // 80 KB of shared memory per CTA
@@ -388,21 +394,41 @@ size_t attention_ws_floats(const AttnArgs& a) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int splits = attention_splits(a, sms);
   if (splits == 1) return 0;
-  const size_t qblocks = (a.lq + kBQ - 1) / kBQ;
+  const size_t qblocks = (launch_rows(a) + kBQ - 1) / kBQ;
   return qblocks * a.heads * a.batch * splits * kBQ * (kD + 4);
 }
 
-void launch_attention(const AttnArgs& a_in, cudaStream_t s) {
-  if (attention_tc_eligible(a_in) && launch_attention_tc(a_in, s) == cudaSuccess) return;
+namespace {
+
+int num_sms_cached() {
   static int sms = 0;
   if (!sms) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
+  return sms;
+}
+
+// Rows of a tcgen05 launch that end in a ragged tile of <= 64 rows which alone
+// would start a second wave of CTAs (e.g. 769 prefix queries x 24 heads: 144
+// CTAs of full tiles + 24 of one row each): the full tiles run on the tcgen05
+// kernel in one wave and the tail on the mma.sync kernel; else 0.
+int tc_split_rows(const AttnArgs& a) {
+  if (a.q_begin != 0 || a.q_end != 0) return 0;
+  const int full = (a.lq / 128) * 128, rem = a.lq - full;
+  const long long per_tile = static_cast<long long>(a.heads) * a.batch;
+  const int sms = num_sms_cached();
+  if (full == 0 || rem == 0 || rem > kBQ) return 0;
+  if ((full / 128) * per_tile > sms || (full / 128 + 1) * per_tile <= sms) return 0;
+  return full;
+}
+
+void launch_attention_decode(const AttnArgs& a_in, cudaStream_t s) {
+  const int sms = num_sms_cached();
   AttnArgs a = a_in;
   const int splits = attention_splits(a, sms);
-  const int qblocks = (a.lq + kBQ - 1) / kBQ;
+  const int qblocks = (launch_rows(a) + kBQ - 1) / kBQ;
   if (a.ws && static_cast<size_t>(qblocks) * a.heads * a.batch * splits * kBQ * (kD + 4) >
                   a.ws_floats)
     a.ws = nullptr;  // too small: merge through distributed shared memory
@@ -425,6 +451,31 @@ void launch_attention(const AttnArgs& a_in, cudaStream_t s) {
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   cudaLaunchKernelEx(&cfg, attention_kernel<true>, a, splits);
+}
+
+}  // namespace
+
+int attention_launch_count(const AttnArgs& a) {
+  return attention_tc_eligible(a) && tc_split_rows(a) > 0 ? 2 : 1;
+}
+
+void launch_attention(const AttnArgs& a, cudaStream_t s) {
+  if (attention_tc_eligible(a)) {
+    const int full = tc_split_rows(a);
+    if (full > 0) {
+      AttnArgs head = a;
+      head.q_end = full;
+      if (launch_attention_tc(head, s) == cudaSuccess) {
+        AttnArgs tail = a;
+        tail.q_begin = full;
+        launch_attention_decode(tail, s);
+        return;
+      }
+    } else if (launch_attention_tc(a, s) == cudaSuccess) {
+      return;
+    }
+  }
+  launch_attention_decode(a, s);
 }
 
 }  // namespace wamb

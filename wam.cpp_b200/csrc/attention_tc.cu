@@ -82,7 +82,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * kRows, head = blockIdx.y, seq = blockIdx.z;
+  const int q0 = a.q_begin + blockIdx.x * kRows, head = blockIdx.y, seq = blockIdx.z;
+  const int q_end = a.q_end > 0 ? a.q_end : a.lq;
   const int nk = (a.lk + kKeys - 1) / kKeys;
 
   if (threadIdx.x == 0) {
@@ -327,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int qr = q0 + row;
       bf16* dst = nullptr;
-      if (qr < a.lq) {
+      if (qr < q_end) {
         if (a.split_first) {
           dst = qr == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
                         : a.out + (static_cast<long long>(seq) * (a.lq - 1) + qr - 1) * a.ldo;
@@ -425,7 +426,8 @@ cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s) {
       !encode_rows(&mv, a.v, a.lk, a.heads, a.batch, a.kv_head_stride, a.kv_seq_stride))
     return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.lq + kRows - 1) / kRows, a.heads, a.batch);
+  const int rows = (a.q_end > 0 ? a.q_end : a.lq) - a.q_begin;
+  cfg.gridDim = dim3((rows + kRows - 1) / kRows, a.heads, a.batch);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmem;
   cfg.stream = s;

@@ -892,7 +892,7 @@ bool MotEngine::build(int b, std::string* err) {
       p.add([a](cudaStream_t s) {
         launch_attention(a, s);
         return cudaGetLastError();
-      }, OP_ATTENTION, 1, 2.0 * bq + bkv, 4.0 * a.batch * a.heads * double(a.lq) * a.lk * 128.0);
+      }, OP_ATTENTION, attention_launch_count(a), 2.0 * bq + bkv, 4.0 * a.batch * a.heads * double(a.lq) * a.lk * 128.0);
     };
     auto ln_mod = [&](Program& p, const bf16* x, int rows, int cols, const float* scale,
                       const float* shift, bf16* y) {

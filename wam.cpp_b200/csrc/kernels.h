@@ -197,10 +197,16 @@ struct AttnArgs {
   float* ws = nullptr;
   size_t ws_floats = 0;
   unsigned* error = nullptr;  // device error word for a wait that gave up (tcgen05 kernel)
+  // Query rows [q_begin, q_end) of each sequence are computed by this launch
+  // (q_end 0: lq); lq stays the sequence's query count (output addressing).
+  int q_begin = 0, q_end = 0;
 };
 // Picks the kernel: 128-query tcgen05 tiles (attention_tc.cu) for >= 128
 // queries, the mma.sync kernel below otherwise.
 void launch_attention(const AttnArgs& a, cudaStream_t s);
+// Kernels launch_attention(a) issues (2 when a ragged tail of < 64 query rows
+// runs on the mma.sync kernel so that the 128-row tiles fit one wave).
+int attention_launch_count(const AttnArgs& a);
 cudaError_t attention_tc_init();
 bool attention_tc_eligible(const AttnArgs& a);
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s);
