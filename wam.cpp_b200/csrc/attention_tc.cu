@@ -12,11 +12,13 @@
 // so the tensor core runs while the softmax works), warps 2-17 = four threads
 // per query row, each over a quarter of the keys / dims (the row max and sum
 // are exchanged through shared memory): softmax from S in TMEM (one pass, the
-// thread's scores held in registers), P as BF16 into a K-major tile, lazy rescaling of O in
-// TMEM (only when the running max grows by more than 2^8), and the final
-// normalised BF16 rows. Q, K and P use the K-major swizzled layout of the GEMM
-// (csrc/gemm.cu); V tiles (double-buffered) are read by the tensor core as
-// they land, as an MN-major operand (dims contiguous), with no transpose.
+// thread's scores held in registers), P as BF16 written back into the first
+// 64 columns of its own S buffer in TMEM (the A operand of P V), lazy
+// rescaling of O in TMEM (only when the running max grows by more than 2^8),
+// and the final normalised BF16 rows. Q and K use the K-major swizzled layout
+// of the GEMM (csrc/gemm.cu); V tiles (double-buffered) are read by the tensor
+// core as they land, as an MN-major operand (dims contiguous), with no
+// transpose.
 //
 // Arithmetic as attention.cu's kernel: F32 scores, softmax(scale * S) with an
 // online max, probabilities rounded to BF16 for P V, F32 accumulation, BF16
@@ -46,10 +48,9 @@ constexpr int kTile = 2 * kHalf;          // 32 KB
 constexpr int kOffQ = 0;                  // Q [2 halves of dims]
 constexpr int kOffK = kTile;              // K ring [2][2 halves]
 constexpr int kOffV = 3 * kTile;          // V ring [2][2 halves of dims], rows = keys
-constexpr int kOffP = 5 * kTile;          // P [2 halves of keys], rows = queries
-constexpr int kOffBar = 6 * kTile;
+constexpr int kOffBar = 5 * kTile;
 constexpr int kOffXch = kOffBar + 256;    // row max / sum exchange between a row's kParts threads
-constexpr int kSmem = 6 * kTile + 256 + 2 * 4 * 128 * kParts + 1024 + 256;
+constexpr int kSmem = 5 * kTile + 256 + 2 * 4 * 128 * kParts + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;       // S[0], S[1], O (128 columns each)
 
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
@@ -67,7 +68,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sq = smem + kOffQ;
   uint8_t* sk = smem + kOffK;
   uint8_t* sv = smem + kOffV;
-  uint8_t* sp = smem + kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
@@ -91,8 +91,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
     for (int i = 0; i < 16; ++i) mbar_init(&bars[i], 1);
-    // S buffers and P are released / published by every softmax warp
-    for (int i = 0; i < 2; ++i) mbar_init(&s_free[i], kSoftmax / 32);
+    // P is published by every softmax warp (an S buffer is freed by the
+    // commit of the P V that read the P written into it)
     mbar_init(p_full, kSoftmax / 32);
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -198,22 +198,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          // O += P V: P K-major over keys (two 64-key halves); V as landed,
+          // O += P V: P in TMEM (the first 64 columns of S buffer jj % 2, two
+          // BF16 keys per column: 8 columns per 16-key step); V as landed,
           // [keys][dims] in two 64-dim halves 16 KB apart (MN atoms), 8-key
           // groups 1024 bytes apart (K atoms): 16 keys = 2048 bytes per step.
           const uint32_t v_base = smem_u32(sv + vb * kTile);
+          const uint32_t p_tmem = t_s[jj & 1];
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const uint64_t da = sw128_kmajor_desc(smem_u32(sp + c * kHalf));
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t db =
-                  sw128_mnmajor_desc(v_base + static_cast<uint32_t>((c * 4 + kk) * 2048), kHalf, 1024);
-              umma_bf16_ss(t_o, da + 2 * kk, db, idesc_pv, (jj > 0 || c != 0 || kk != 0) ? 1u : 0u);
-            }
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t db = sw128_mnmajor_desc(v_base + static_cast<uint32_t>(kk * 2048), kHalf, 1024);
+            umma_bf16_ts(t_o, p_tmem + static_cast<uint32_t>(kk * 8), db, idesc_pv,
+                         (jj > 0 || kk != 0) ? 1u : 0u);
           }
           umma_commit(pv_done);
           umma_commit(&v_empty[vb]);
+          umma_commit(&s_free[jj & 1]);  // its P has been read
         }
       }
       if (!ok) fail(a, kErrMmaTimeout);
@@ -277,9 +276,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         ls += p0 + p1;
         pk[i >> 1] = pack_bf16(p0, p1);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[b]);
       // P and O are free once the previous tile's P V has completed.
       if (j >= 1 && !mbar_wait(pv_done, (j - 1) & 1)) ok = false;
       tc_fence_after();
@@ -299,16 +295,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (rescale) m_used = m_new;
       l += ls;
-      // this thread's kCols keys of the P row -> K-major tile over keys (64-key
-      // halves of 8 swizzled 16-byte chunks per row)
-#pragma unroll
-      for (int i = 0; i < kCols / 8; ++i) {
-        const int key = c0 + 8 * i;
-        const int chunk = (key & 63) >> 3;
-        const uint32_t off = (key >> 6) * kHalf + row * 128 + ((chunk ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(sp + off) = make_uint4(pk[i * 4], pk[i * 4 + 1], pk[i * 4 + 2], pk[i * 4 + 3]);
-      }
-      fence_proxy_async_smem();  // P (generic stores) is read by the tensor core
+      // this thread's kCols keys of the P row -> TMEM columns kCols/2 * part ..
+      // of its S buffer (every thread's scores were read before the row-max
+      // barrier, so no part overwrites scores another part still needs)
+      tmem_st_x16(t_s[b] + lane_off + static_cast<uint32_t>(part * (kCols / 2)), pk);
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
