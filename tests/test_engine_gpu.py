@@ -178,3 +178,27 @@ def test_engine_pair_gemm_matches_oracle(cuda_device):
     res = subprocess.run([sys.executable, "-c", code], env=env, cwd=str(repo),
                          capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+
+
+def test_profile_graph_lanes(cuda_device):
+    """wam_b200_profile_graph_lane: the prefix GEMMs of the main lane (visual
+    tokens) and of the side lane (state token) add up to all of them, in
+    launches, FLOPs and bytes; each replay is timed."""
+    from oracle import synth
+    from wam_b200.engine import Engine
+
+    geom = synth.TINY
+    eng = Engine(geom, seed=SEED, bias_scale=0.02, prompt_cache=False)
+    _, rq = _req(geom, 5)
+    eng.stage([rq])
+    eng.run(1)
+    both = eng.profile_graph(1, "prefix", "gemm", reps=2)
+    main = eng.profile_graph(1, "prefix", "gemm", reps=2, lane=0)
+    side = eng.profile_graph(1, "prefix", "gemm", reps=2, lane=1)
+    assert main["launches"] > 0 and side["launches"] > 0
+    assert main["launches"] + side["launches"] == both["launches"]
+    assert abs(main["flops"] + side["flops"] - both["flops"]) <= 1e-6 * both["flops"]
+    assert abs(main["bytes"] + side["bytes"] - both["bytes"]) <= 1e-6 * both["bytes"]
+    assert main["ms"] > 0 and side["ms"] > 0 and both["ms"] > 0
+    with pytest.raises(RuntimeError):
+        eng.profile_graph(1, "prefix", "gemm", reps=1, lane=2)
