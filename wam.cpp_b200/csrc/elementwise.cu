@@ -270,10 +270,12 @@ __global__ void __launch_bounds__(3 * kRowThreads, 3) qkv_scatter_kernel(const _
   griddep_launch_dependents();
   __shared__ float red[3][4];
   const int row = blockIdx.x;
-  const int which = threadIdx.y;
+  const int layer = blockIdx.y;
+  const int which = threadIdx.y + (3 - static_cast<int>(blockDim.y));  // blocks without q: parts 1, 2
   const int tid = threadIdx.x;
   const int col = which == 0 ? a.q_col : (which == 1 ? a.k_col : a.v_col);
-  const bf16* src = a.src + static_cast<long long>(row) * a.ld_src + (col < 0 ? 0 : col);
+  const bf16* src = a.src + layer * a.src_layer_stride + static_cast<long long>(row) * a.ld_src +
+                    (col < 0 ? 0 : col);
   const int seq = row / a.rows_per_seq;
   const int rin = row - seq * a.rows_per_seq;
   const int chunks = a.hidden >> 3;
@@ -281,15 +283,17 @@ __global__ void __launch_bounds__(3 * kRowThreads, 3) qkv_scatter_kernel(const _
   long long head_stride = 0;
   if (col >= 0) {
     if (which == 0) {
-      dst_base = a.q_out + seq * a.q_seq_stride + static_cast<long long>(a.q_row_offset + rin) * 128;
+      dst_base = a.q_out + layer * a.out_layer_stride + seq * a.q_seq_stride +
+                 static_cast<long long>(a.q_row_offset + rin) * 128;
       head_stride = a.q_head_stride;
     } else {
-      dst_base = (which == 1 ? a.k_out : a.v_out) + seq * a.kv_seq_stride +
-                 static_cast<long long>(a.kv_row_offset + rin) * 128;
+      dst_base = (which == 1 ? a.k_out : a.v_out) + layer * a.out_layer_stride +
+                 seq * a.kv_seq_stride + static_cast<long long>(a.kv_row_offset + rin) * 128;
       head_stride = a.kv_head_stride;
     }
   }
-  const bf16* nw = which == 0 ? a.q_norm : (which == 1 ? a.k_norm : nullptr);
+  const bf16* nw = which == 0 ? a.q_norm
+                              : (which == 1 ? (a.k_norms ? a.k_norms[layer] : a.k_norm) : nullptr);
   int pt = 0, ph = 0, pw = 0;
   if (a.rope_mode == 2 && which < 2 && col >= 0) {
     pt = a.pos_thw[rin * 3 + 0];
@@ -546,7 +550,7 @@ void launch_rms_modulate(const bf16* x, int ldx, int rows, int cols, const float
 
 void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s) {
   const int per = (a.hidden / 8 + kRowThreads - 1) / kRowThreads;
-  const dim3 grid(a.rows), block(kRowThreads, 3);
+  const dim3 grid(a.rows, a.layers), block(kRowThreads, a.q_col < 0 ? 2 : 3);
   if (per <= 1)
     launch_pdl(qkv_scatter_kernel<1>, grid, block, 0, s, a);
   else if (per <= 2)

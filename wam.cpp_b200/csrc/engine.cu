@@ -661,6 +661,7 @@ bool MotEngine::alloc_buffers(std::string* err) {
     const size_t per_layer = B * Nt * 2 * H * sizeof(bf16);
     pkv_layers_ = static_cast<int>(std::min<size_t>(L, std::max<size_t>(1, (4ull << 30) / per_layer)));
     AL(pkv_, bf16, B * Nt * static_cast<size_t>(pkv_layers_) * 2 * H);
+    AL(knorm_tab_, const bf16*, 2 * static_cast<size_t>(L));
   }
   AL(err_word_, unsigned, 1);
   // A split GEMM holds at most one wave of CTAs, each with a partial tile of
@@ -879,7 +880,7 @@ bool MotEngine::build(int b, std::string* err) {
       p.add([q](cudaStream_t s) {
         launch_qkv_scatter(q, s);
         return cudaGetLastError();
-      }, OP_QKV, 1, 4.0 * parts * q.rows * q.hidden);
+      }, OP_QKV, 1, 4.0 * parts * q.rows * q.hidden * q.layers);
     };
     auto attend = [&](Program& p, const AttnArgs& a_in) {
       // Key splits merge through the lane's workspace (dead between GEMMs).
@@ -1037,6 +1038,22 @@ bool MotEngine::build(int b, std::string* err) {
     const bool pkv_ok = pkv_ && !rowmajor_weights_ && H % 256 == 0 && E % 64 == 0 &&
                         pkv_block(".a", E, &pw[0], &pb[0]) && pkv_block(".v", H, &pw[1], &pb[1]);
     if (pkv_ok) {
+      // Every layer's prompt k-norm weight, in a device table for the scatter.
+      std::vector<const bf16*> knorms(2 * static_cast<size_t>(L), nullptr);
+      for (int x = 0; x < 2; ++x)
+        for (int l = 0; l < L; ++l) {
+          const std::string pfx = "gwp.blk." + std::to_string(l) + (x ? ".v" : ".a");
+          knorms[static_cast<size_t>(x) * L + l] = W(pfx + ".ca.kn.weight", H);
+          if (!knorms[static_cast<size_t>(x) * L + l]) {
+            ok = false;
+            e2 = "missing " + pfx + ".ca.kn";
+          }
+        }
+      if (ok && cudaMemcpy(knorm_tab_, knorms.data(), knorms.size() * sizeof(const bf16*),
+                           cudaMemcpyHostToDevice) != cudaSuccess) {
+        ok = false;
+        e2 = "prompt k-norm table upload failed";
+      }
       for (int x = 0; x < 2 && ok; ++x) {
         const bf16* text = x ? text_v_ : text_a_;
         const int tw = x ? H : E;
@@ -1051,10 +1068,10 @@ bool MotEngine::build(int b, std::string* err) {
                               nullptr, nullptr, 0, pkv_, nl * 2 * H, true, false,
                               std::string("prompt projection") + xs, &e2))
             ok = false;
-          for (int l = l0; l < l1 && ok; ++l) {
-            const std::string pfx = "gwp.blk." + std::to_string(l) + xs;
+          if (ok) {
+            // K-norm + head-major scatter of the chunk's layers in one launch.
             QkvScatter q{};
-            q.src = pkv_ + static_cast<size_t>(l - l0) * 2 * H;
+            q.src = pkv_;
             q.ld_src = nl * 2 * H;
             q.rows = b * Nt;
             q.rows_per_seq = Nt;
@@ -1063,16 +1080,16 @@ bool MotEngine::build(int b, std::string* err) {
             q.q_col = -1;
             q.k_col = 0;
             q.v_col = H;
-            q.k_norm = W(pfx + ".ca.kn.weight", H);
+            q.k_norm = knorms[static_cast<size_t>(x) * L + l0];
+            q.k_norms = knorm_tab_ + static_cast<size_t>(x) * L + l0;
             q.eps = eps;
-            q.k_out = (x ? k_vis_ : k_prompt_) + l * prL;
-            q.v_out = (x ? v_vis_ : v_prompt_) + l * prL;
+            q.k_out = (x ? k_vis_ : k_prompt_) + l0 * prL;
+            q.v_out = (x ? v_vis_ : v_prompt_) + l0 * prL;
             q.kv_seq_stride = prB;
             q.kv_head_stride = static_cast<long long>(Nt) * 128;
-            if (!q.k_norm) {
-              ok = false;
-              e2 = "missing " + pfx + ".ca.kn";
-            }
+            q.layers = nl;
+            q.src_layer_stride = 2 * static_cast<long long>(H);
+            q.out_layer_stride = prL;
             scatter(pp, q);
           }
         }

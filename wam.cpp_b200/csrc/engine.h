@@ -274,6 +274,9 @@ class MotEngine {
   int pkv_layers_ = 0;
   // Split-K exchange workspace, one per lane (the lanes' GEMMs may overlap).
   float* gemm_ws_[2] = {nullptr, nullptr};
+  // Device table of the prompt k-norm weights, [expert][layer] (one prompt
+  // K / V scatter launch covers the layers of a projection chunk).
+  const bf16** knorm_tab_ = nullptr;
   size_t gemm_ws_floats_ = 0;
   unsigned* err_word_ = nullptr;
 

@@ -167,7 +167,15 @@ struct QkvScatter {
   bf16* v_out;
   long long kv_seq_stride, kv_head_stride;
   int kv_row_offset;
+  // Several layers in one launch (grid y = layer): layer l reads its rows at
+  // src + l * src_layer_stride, takes its k norm from k_norms[l] (a device
+  // array) when k_norms is set, and writes q_out / k_out / v_out +
+  // l * out_layer_stride.
+  int layers = 1;
+  long long src_layer_stride = 0, out_layer_stride = 0;
+  const bf16* const* k_norms = nullptr;
 };
+// Blocks carry only the parts a launch writes (k and v when q_col < 0).
 void launch_qkv_scatter(const QkvScatter& a, cudaStream_t s);
 
 // Flash attention over head-major Q/K/V with softmax(scale * QK^T) V,
