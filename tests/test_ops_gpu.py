@@ -56,6 +56,55 @@ def test_decode_attention_vs_torch(cuda_device, B, heads, lq, lk, qs):
     _attention_case(B, heads, lq, lk, qs)
 
 
+_FORCED_DEC_TC = r"""
+import sys
+sys.path.insert(0, "wam.cpp_b200")
+import torch
+from wam_b200 import ops
+
+def rel_l2(a, b):
+    a, b = a.double(), b.double()
+    return float((a - b).norm() / (b.norm() + 1e-30))
+
+cases = [(1, 24, 48, 817, 1.0), (1, 24, 48, 512, 1.0), (2, 3, 1, 64, 1.0), (1, 24, 1, 512, 1.0),
+         (3, 5, 33, 250, 8.0), (1, 2, 64, 896, 4.0), (2, 4, 17, 1, 1.0), (1, 3, 40, 129, 1.0),
+         (2, 24, 48, 817, 1.0)]
+worst = 0.0
+for B, H, lq, lk, qs in cases:
+    g = torch.Generator().manual_seed(lq * 31 + lk)
+    q = (torch.randn(B, H, lq, 128, generator=g) * qs).to(torch.bfloat16).cuda()
+    k = torch.randn(B, H, lk, 128, generator=g).to(torch.bfloat16).cuda()
+    v = torch.randn(B, H, lk, 128, generator=g).to(torch.bfloat16).cuda()
+    y = ops.attention(q, k, v)
+    s = torch.einsum("bhqd,bhkd->bhqk", q.float(), k.float()) / 128 ** 0.5
+    o = torch.einsum("bhqk,bhkd->bhqd", torch.softmax(s, dim=-1), v.float())
+    ref = o.permute(0, 2, 1, 3).reshape(B * lq, H * 128)
+    torch.cuda.synchronize()
+    err = rel_l2(y.float(), ref)
+    if not torch.isfinite(y.float()).all() or err >= 1e-2:
+        raise SystemExit(f"case {(B, H, lq, lk, qs)}: rel-L2 {err}")
+    worst = max(worst, err)
+print("worst rel-L2", worst)
+"""
+
+
+def test_decode_attention_tc_forced(cuda_device):
+    """The tcgen05 decode kernel (one CTA per (sequence, head), every key's
+    score in TMEM, exact two-pass softmax) on every eligible shape, batch 1
+    included, where the automatic choice takes the mma.sync kernel:
+    WAM_B200_ATTN_DEC_TC=1 in a child process. 1 and 129 keys (one / two
+    tiles, ragged), 896 keys (seven full tiles), 1-64 queries."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    env = dict(os.environ, WAM_B200_ATTN_DEC_TC="1")
+    r = subprocess.run([sys.executable, "-c", _FORCED_DEC_TC], env=env, capture_output=True, text=True,
+                       cwd=str(Path(__file__).resolve().parent.parent), timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
 def _attention_case(B, heads, lq, lk, qs):
     from wam_b200 import ops
 

@@ -367,6 +367,7 @@ cudaError_t attention_init() {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
   if ((e = attention_tc_init()) != cudaSuccess) return e;
+  if ((e = attention_dec_tc_init()) != cudaSuccess) return e;
   return cudaFuncSetAttribute(attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               kSmem);
 }
@@ -475,6 +476,7 @@ void launch_attention(const AttnArgs& a, cudaStream_t s) {
       return;
     }
   }
+  if (attention_dec_tc_eligible(a) && launch_attention_dec_tc(a, s) == cudaSuccess) return;
   launch_attention_decode(a, s);
 }
 

@@ -370,10 +370,13 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+}  // namespace
+
 // [batch][heads][rows][128] BF16 with the given strides (elements), boxes of
-// 128 rows x 64 dims with the 128-byte swizzle; rows past `rows` read as zero.
-bool encode_rows(CUtensorMap* m, const void* base, int rows, int heads, int batch,
-                 long long head_stride, long long seq_stride) {
+// box_rows rows x 64 dims with the 128-byte swizzle; rows past `rows` read as
+// zero.
+bool attn_encode_rows(CUtensorMap* m, const void* base, int rows, int heads, int batch,
+                      long long head_stride, long long seq_stride, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   if (batch == 1) seq_stride = head_stride * heads;
@@ -381,11 +384,18 @@ bool encode_rows(CUtensorMap* m, const void* base, int rows, int heads, int batc
                               static_cast<cuuint64_t>(batch)};
   const cuuint64_t strides[3] = {256, static_cast<cuuint64_t>(head_stride) * 2,
                                  static_cast<cuuint64_t>(seq_stride) * 2};
-  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(box_rows), 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+namespace {
+
+bool encode_rows(CUtensorMap* m, const void* base, int rows, int heads, int batch,
+                 long long head_stride, long long seq_stride) {
+  return attn_encode_rows(m, base, rows, heads, batch, head_stride, seq_stride, 128);
 }
 
 bool tc_enabled() {

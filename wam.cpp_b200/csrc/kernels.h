@@ -210,7 +210,8 @@ struct AttnArgs {
   int q_begin = 0, q_end = 0;
 };
 // Picks the kernel: 128-query tcgen05 tiles (attention_tc.cu) for >= 128
-// queries, the mma.sync kernel below otherwise.
+// queries; for <= 64 queries over <= 896 keys one tcgen05 CTA per (sequence,
+// head) (attention_dec_tc.cu); the mma.sync kernel (attention.cu) otherwise.
 void launch_attention(const AttnArgs& a, cudaStream_t s);
 // Kernels launch_attention(a) issues (2 when a ragged tail of < 64 query rows
 // runs on the mma.sync kernel so that the 128-row tiles fit one wave).
@@ -218,6 +219,15 @@ int attention_launch_count(const AttnArgs& a);
 cudaError_t attention_tc_init();
 bool attention_tc_eligible(const AttnArgs& a);
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s);
+// tcgen05 attention for <= 64 queries over <= 896 keys per (sequence, head),
+// one CTA each (attention_dec_tc.cu).
+cudaError_t attention_dec_tc_init();
+bool attention_dec_tc_eligible(const AttnArgs& a);
+cudaError_t launch_attention_dec_tc(const AttnArgs& a, cudaStream_t s);
+// TMA map of [batch][heads][rows][128] BF16 (element strides), boxes of
+// box_rows rows x 64 dims, 128-byte swizzle, rows past `rows` zero-filled.
+bool attn_encode_rows(CUtensorMap* m, const void* base, int rows, int heads, int batch,
+                      long long head_stride, long long seq_stride, int box_rows);
 
 // Workspace the split-KV merge of `a` needs (0 when it does not split).
 size_t attention_ws_floats(const AttnArgs& a);

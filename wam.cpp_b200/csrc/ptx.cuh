@@ -316,6 +316,15 @@ __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
+// 8 consecutive accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr));
+}
+
 // 32 consecutive accumulator columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -411,6 +420,10 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
 // The same with the B operand MN-major (N contiguous in shared memory).
 __host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int m, int n) {
   return umma_idesc_bf16(m, n) | (1u << 16);
+}
+// Both operands MN-major (A: M contiguous, B: N contiguous in shared memory).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_mn(int m, int n) {
+  return umma_idesc_bf16(m, n) | (1u << 15) | (1u << 16);
 }
 
 // Bulk prefetch of a global range into L2 (16-byte aligned address and size).
