@@ -48,15 +48,19 @@ def test_attention_vs_torch(cuda_device, B, heads, lq, lk):
     (1, 24, 1, 512, 1.0),     # prefix state token over the prompt keys
     (1, 2, 64, 3000, 4.0),    # 64 query rows, 24 tiles per CTA, wide scores (O rescaled)
     (3, 5, 33, 250, 8.0),     # ragged rows / keys, very wide scores
+    (1, 2, 64, 896, 4.0),     # 64 queries, seven full key tiles (every TMEM column)
+    (2, 4, 17, 1, 1.0),       # a single key
+    (1, 3, 40, 129, 1.0),     # two key tiles, the second with one key; 40 queries (N = 48)
 ])
 def test_decode_attention_vs_torch(cuda_device, B, heads, lq, lk, qs):
-    """The decode attention (<= 64 queries per head, key splits merged in a
-    cluster) against torch F32, including multi-tile online softmax and wide
-    score ranges."""
+    """The decode attention (<= 64 queries per head: the tcgen05 kernel of
+    attention_dec_tc.cu, one CTA or a cluster of 2 / 4 key-split CTAs per
+    (sequence, head); the mma.sync kernel beyond 896 keys) against torch F32,
+    including ragged key tiles and wide score ranges."""
     _attention_case(B, heads, lq, lk, qs)
 
 
-_FORCED_DEC_TC = r"""
+_DECODE_CASES = r"""
 import sys
 sys.path.insert(0, "wam.cpp_b200")
 import torch
@@ -88,19 +92,18 @@ print("worst rel-L2", worst)
 """
 
 
-def test_decode_attention_tc_forced(cuda_device):
-    """The tcgen05 decode kernel (one CTA per (sequence, head), every key's
-    score in TMEM, exact two-pass softmax) on every eligible shape, batch 1
-    included, where the automatic choice takes the mma.sync kernel:
-    WAM_B200_ATTN_DEC_TC=1 in a child process. 1 and 129 keys (one / two
-    tiles, ragged), 896 keys (seven full tiles), 1-64 queries."""
+def test_decode_attention_mma_sync(cuda_device):
+    """The mma.sync decode kernel (attention.cu: 64-query blocks, keys split
+    over up to 8 CTAs merged through L2 or distributed shared memory), which
+    the tcgen05 kernel replaces for <= 896 keys, on the same shapes:
+    WAM_B200_ATTN_DEC_TC=0 in a child process."""
     import os
     import subprocess
     import sys
     from pathlib import Path
 
-    env = dict(os.environ, WAM_B200_ATTN_DEC_TC="1")
-    r = subprocess.run([sys.executable, "-c", _FORCED_DEC_TC], env=env, capture_output=True, text=True,
+    env = dict(os.environ, WAM_B200_ATTN_DEC_TC="0")
+    r = subprocess.run([sys.executable, "-c", _DECODE_CASES], env=env, capture_output=True, text=True,
                        cwd=str(Path(__file__).resolve().parent.parent), timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
 

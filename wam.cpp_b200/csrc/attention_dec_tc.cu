@@ -1,10 +1,12 @@
 // tcgen05 attention for the denoise step: <= 64 queries per (sequence, head)
 // over <= 896 keys (the 48 action queries over the joint keys, prefix + action,
-// 817 at config 2, and over the 512 prompt keys), taken when the (sequence,
-// head) grid fills the SMs (batched requests; see dec_tc_mode below).
+// 817 at config 2, and over the 512 prompt keys).
 //
-// One CTA per (sequence, head) holds every key of the head, so there is no key
-// split and no merge of partial rows. The scores are computed transposed,
+// One CTA per (sequence, head) holds all of its keys, or, while the grid is
+// smaller than the SMs, a cluster of 2 or 4 CTAs splits them by 128-key tiles
+// (each CTA with its own max; the partial O^T, max and sum are published in
+// shared memory and every CTA merges a quarter / half of the query slots from
+// its peers' through distributed shared memory). The scores are computed transposed,
 // S^T = K Q^T (M = 128 keys of a tile, N = 64 query slots, K = 128 dims), each
 // key tile into its own 64 TMEM columns (7 tiles + O^T = 512 columns): a TMEM
 // lane is a key, so the exponentials of a tile are spread over all four lane
@@ -55,9 +57,11 @@ constexpr int kOffQ = 0;
 constexpr int kOffRing = kOffQ + 2 * kQHalf;
 constexpr int kOffP = kOffRing + kRing * kTile;
 constexpr int kOffBar = kOffP + 2 * kPBuf;
-constexpr int kNumBars = 1 + 2 * kRing + kMaxTiles + 2 + 2 + 1;
+constexpr int kNumBars = 1 + 2 * kRing + kMaxTiles + 2 + 2 + 1 + 2;
 constexpr int kOffRed = kOffBar + 8 * 32;  // [2 (max, sum)][4 quadrants][2 halves][32] F32
-constexpr int kSmem = kOffRed + 2 * 4 * 2 * 32 * 4 + 1024;
+constexpr int kOffX = kOffRed + 2 * 4 * 2 * 32 * 4;  // key splits: this CTA's [2][64] scaled max, sum
+constexpr int kSmem = kOffX + 2 * 64 * 4 + 1024;
+constexpr int kMaxSplits = 4;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = kMaxTiles * kSlots;  // O^T columns
 
@@ -91,7 +95,8 @@ __device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32], int lane)
 
 __global__ void __launch_bounds__(kThreads, 1)
     attention_dec_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnArgs a) {
+                            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnArgs a,
+                            int splits) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -106,12 +111,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_full + kMaxTiles;          // [2]
   uint64_t* p_free = p_full + 2;                  // [2]
   uint64_t* o_full = p_free + 2;
+  uint64_t* x_ready = o_full + 1;  // key splits: every peer's partials are published
+  uint64_t* x_done = o_full + 2;   // key splits: every peer has read this CTA's partials
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   float* red = reinterpret_cast<float*>(smem + kOffRed);
+  float* xm = reinterpret_cast<float*>(smem + kOffX);  // [64] scaled max per query slot
+  float* xl = xm + 64;                                  // [64] sum per query slot
+  float* xo = reinterpret_cast<float*>(ring);           // [64 slots][128 dims] F32 partial O (ring slot 0)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.x, seq = blockIdx.y;
-  const int nk = (a.lk + kKeys - 1) / kKeys;  // 1 .. kMaxTiles (checked by the host)
+  // With key splits the CTAs of a (sequence, head) form a cluster along x;
+  // split r takes key tiles [r nk_all / splits, (r + 1) nk_all / splits).
+  const int split = splits > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int head = static_cast<int>(blockIdx.x) / splits, seq = blockIdx.y;
+  const int nk_all = (a.lk + kKeys - 1) / kKeys;  // 1 .. kMaxTiles (checked by the host)
+  const int t_begin = split * nk_all / splits;
+  const int nk = (split + 1) * nk_all / splits - t_begin;  // >= 1: splits <= nk_all
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tm_q);
@@ -120,6 +135,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], 1);
     mbar_init(&p_full[0], kSoftWarps);
     mbar_init(&p_full[1], kSoftWarps);
+    if (splits > 1) {
+      mbar_init(x_ready, splits - 1);
+      mbar_init(x_done, splits - 1);
+    }
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -130,6 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Every peer's mbarriers exist before anyone arrives on them remotely (all
+  // threads converged here, right after the CTA barrier).
+  if (splits > 1) cluster_sync_all();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
@@ -141,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int items = 2 * nk;
       auto load = [&](int i) {
         const int slot = i % kRing;
-        const int t = i < nk ? i : i - nk;
+        const int t = t_begin + (i < nk ? i : i - nk);
         const CUtensorMap* m = i < nk ? &tm_k : &tm_v;
         uint8_t* dst = ring + slot * kTile;
         mbar_arrive_expect_tx(&slot_full[slot], kTile);
@@ -151,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       // K / V rows the preceding kernel does not write start before waiting for it.
       while (issued < items && issued < kRing) {
-        const int t = issued < nk ? issued : issued - nk;
+        const int t = t_begin + (issued < nk ? issued : issued - nk);
         const int end = (t + 1) * kKeys < a.lk ? (t + 1) * kKeys : a.lk;
         if (end > a.static_keys) break;
         load(issued++);
@@ -251,8 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < nk; ++t) {
       if (!mbar_wait(&s_full[t], 0)) ok = false;
       tc_fence_after();
-      const int key = t * kKeys + quad * 32 + lane;
-      if (t * kKeys + quad * 32 >= a.lk) continue;  // warp-uniform: no key of this warp
+      const int key = (t_begin + t) * kKeys + quad * 32 + lane;
+      if ((t_begin + t) * kKeys + quad * 32 >= a.lk) continue;  // warp-uniform: no key of this warp
       uint32_t r[4][8];
 #pragma unroll
       for (int c = 0; c < 4; ++c)
@@ -271,13 +293,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the max over all keys of this thread's 32 query columns, pre-scaled:
     // lane i combines the quadrants of column i, then every lane takes all 32
     float mb[32];
+    float mb_lane;  // column `lane`'s, kept for the merge of key splits
     {
       float v = red_m[half * 32 + lane];
 #pragma unroll
       for (int q = 1; q < 4; ++q) v = fmaxf(v, red_m[(q * 2 + half) * 32 + lane]);
-      v *= sl2;
+      mb_lane = v * sl2;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) mb[i] = __shfl_sync(0xffffffffu, v, i);
+      for (int i = 0; i < 32; ++i) mb[i] = __shfl_sync(0xffffffffu, mb_lane, i);
     }
 
     // Pass 2: probabilities -> P^T buffers, per-query sums.
@@ -287,8 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int prow = quad * 32 + lane;  // key row of the P^T tile
     for (int t = 0; t < nk && ok; ++t) {
       const int b = t & 1;
-      const int key = t * kKeys + prow;
-      const bool warp_keys = t * kKeys + quad * 32 < a.lk;
+      const int key = (t_begin + t) * kKeys + prow;
+      const bool warp_keys = (t_begin + t) * kKeys + quad * 32 < a.lk;
       uint4 pk[4];
       uint32_t r[4][8];
       if (warp_keys) {
@@ -330,7 +353,98 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok) fail(a, kErrEpilogueTimeout);
     red_l[(quad * 2 + half) * 32 + lane] = warp_reduce_scatter32<false>(l, lane);
     if (ok) ok = mbar_wait(o_full, 0);
-    if (named_bar_and(1, kSoft, ok)) {
+    const bool all_ok = named_bar_and(1, kSoft, ok);
+    if (splits > 1) {
+      // ----------------------------------------------- merge of key splits
+      // Publish this CTA's unnormalised O^T ([slot][dim] F32 in ring slot 0,
+      // free once every MMA has completed), scaled max and sum per query slot;
+      // then every CTA combines ceil(lq / splits) query slots over all splits
+      // from the peers' shared memory (split order: deterministic). The
+      // handshake (x_ready, x_done) runs whatever happened before, so that no
+      // CTA leaves while a peer may still read its shared memory or arrive on
+      // its barriers; outputs are written only when every wait succeeded.
+      tc_fence_after();
+      float lsum = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) lsum += red_l[(q * 2 + half) * 32 + lane];
+      if (quad == 0) {
+        const int col = 16 * (lane >> 3) + 8 * half + (lane & 7);
+        xm[col] = mb_lane;
+        xl[col] = lsum;
+      }
+      const int d = quad * 32 + lane;
+      if (all_ok) {
+        uint32_t r[4][8];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (chunk_ok[c]) tmem_ld_x8(tmem + lane_off + kTmemO + static_cast<uint32_t>(16 * c + 8 * half), r[c]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (!chunk_ok[c]) continue;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) xo[(16 * c + 8 * half + i) * 128 + d] = u2f(r[c][i]);
+        }
+      }
+      named_bar_sync(1, kSoft);
+      if (warp == 2 && lane == 0)
+        for (int p = 0; p < splits; ++p)
+          if (p != split) mbar_arrive_cluster(mapa_shared(smem_u32(x_ready), static_cast<uint32_t>(p)));
+      const bool xok = mbar_wait_cluster(x_ready, 0);
+      const int cols = (lq + splits - 1) / splits;
+      const int wt = static_cast<int>(threadIdx.x) - 64;
+      if (xok && all_ok) {
+        for (int it = wt; it < cols * 16; it += kSoft) {
+          const int j = split * cols + it / 16, g = it % 16;
+          if (j >= lq) break;
+          float mp[kMaxSplits], lp[kMaxSplits];
+          float4 o0[kMaxSplits], o1[kMaxSplits];
+#pragma unroll
+          for (int p = 0; p < kMaxSplits; ++p) {
+            if (p >= splits) break;
+            const uint32_t rk = static_cast<uint32_t>(p);
+            mp[p] = ld_shared_cluster_f32(mapa_shared(smem_u32(xm + j), rk));
+            lp[p] = ld_shared_cluster_f32(mapa_shared(smem_u32(xl + j), rk));
+            const uint32_t ob = mapa_shared(smem_u32(xo + j * 128 + g * 8), rk);
+            o0[p] = ld_shared_cluster_f32x4(ob);
+            o1[p] = ld_shared_cluster_f32x4(ob + 16);
+          }
+          float mx = mp[0];
+#pragma unroll
+          for (int p = 1; p < kMaxSplits; ++p)
+            if (p < splits) mx = fmaxf(mx, mp[p]);
+          float den = 0.0f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int p = 0; p < kMaxSplits; ++p) {
+            if (p >= splits) break;
+            const float w = ex2_approx(mp[p] - mx);
+            den += w * lp[p];
+            acc[0] += w * o0[p].x; acc[1] += w * o0[p].y; acc[2] += w * o0[p].z; acc[3] += w * o0[p].w;
+            acc[4] += w * o1[p].x; acc[5] += w * o1[p].y; acc[6] += w * o1[p].z; acc[7] += w * o1[p].w;
+          }
+          const float f = 1.0f / den;
+          bf16* dst;
+          if (a.split_first) {
+            dst = j == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
+                         : a.out + (static_cast<long long>(seq) * (lq - 1) + j - 1) * a.ldo;
+          } else {
+            dst = a.out + (static_cast<long long>(seq) * lq + j) * a.ldo;
+          }
+          *reinterpret_cast<uint4*>(dst + head * 128 + g * 8) =
+              make_uint4(pack_bf16(acc[0] * f, acc[1] * f), pack_bf16(acc[2] * f, acc[3] * f),
+                         pack_bf16(acc[4] * f, acc[5] * f), pack_bf16(acc[6] * f, acc[7] * f));
+        }
+      } else if (!xok) {
+        fail(a, kErrEpilogueTimeout);
+      }
+      // this CTA is done reading its peers; it leaves once they are done with it
+      named_bar_sync(1, kSoft);
+      if (warp == 2 && lane == 0) {
+        for (int p = 0; p < splits; ++p)
+          if (p != split) mbar_arrive_cluster(mapa_shared(smem_u32(x_done), static_cast<uint32_t>(p)));
+        if (!mbar_wait_cluster(x_done, 0)) fail(a, kErrEpilogueTimeout);
+      }
+    } else if (all_ok) {
       tc_fence_after();
       // 1 / (sum over all keys) of column `lane` (quadrants in order), shared
       // over the warp by shuffles
@@ -374,21 +488,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// WAM_B200_ATTN_DEC_TC: 0 = never, 1 = every eligible launch, unset = when
-// the (sequence, head) grid fills the SMs. With fewer CTAs the mma.sync kernel
-// (attention.cu), which splits each head's keys over up to 8 CTAs, is faster:
-// one CTA feeds the tensor core all of its head's K and V from shared memory,
-// and the tensor core's operand reads (~52 bytes per cycle per SM measured)
-// bound it at ~3.4 us for 817 keys (batch 1: 10.9 against 9.3 us per launch;
-// batch 8: 24.4 against 25.0; batch 64: 140.4 against 142.1).
-int dec_tc_mode() {
-  static const int mode = [] {
+// WAM_B200_ATTN_DEC_TC=0 sends these shapes to the mma.sync kernel
+// (attention.cu). Measured in the engine's graph, us per launch, this kernel
+// against that one: batch 1 9.30 / 9.33 (4 key splits), batch 8 24.4 / 25.0,
+// batch 64 140.4 / 142.1.
+bool dec_tc_enabled() {
+  static const bool on = [] {
     const char* v = std::getenv("WAM_B200_ATTN_DEC_TC");
-    if (v && v[0] == '0') return 0;
-    if (v && v[0] == '1') return 1;
-    return 2;
+    return !(v && v[0] == '0');
   }();
-  return mode;
+  return on;
 }
 
 int sm_count() {
@@ -408,13 +517,22 @@ cudaError_t attention_dec_tc_init() {
 }
 
 bool attention_dec_tc_eligible(const AttnArgs& a) {
-  const int mode = dec_tc_mode();
-  if (mode == 0 || (mode == 2 && static_cast<long long>(a.heads) * a.batch < sm_count())) return false;
-  return a.lq >= 1 && a.lq <= kSlots && a.lk >= 1 && a.lk <= kMaxTiles * kKeys &&
+  return dec_tc_enabled() && a.lq >= 1 && a.lq <= kSlots && a.lk >= 1 && a.lk <= kMaxTiles * kKeys &&
          a.q_begin == 0 && a.q_end == 0 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 &&
          (reinterpret_cast<uintptr_t>(a.k) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.v) & 15) == 0 &&
          a.q_head_stride % 8 == 0 && a.q_seq_stride % 8 == 0 && a.kv_head_stride % 8 == 0 &&
          a.kv_seq_stride % 8 == 0 && a.batch <= 65535;
+}
+
+// Key splits (CTAs per (sequence, head), a cluster): the most of 1 / 2 / 4,
+// at most one per key tile, whose CTAs still fit the SMs in one wave.
+int dec_tc_splits(const AttnArgs& a) {
+  const int nk = (a.lk + kKeys - 1) / kKeys;
+  const long long ctas = static_cast<long long>(a.heads) * a.batch;
+  int best = 1;
+  for (int c = 2; c <= kMaxSplits; c *= 2)
+    if (c <= nk && ctas * c <= sm_count()) best = c;
+  return best;
 }
 
 cudaError_t launch_attention_dec_tc(const AttnArgs& a, cudaStream_t s) {
@@ -423,17 +541,22 @@ cudaError_t launch_attention_dec_tc(const AttnArgs& a, cudaStream_t s) {
       !attn_encode_rows(&mk, a.k, a.lk, a.heads, a.batch, a.kv_head_stride, a.kv_seq_stride, kKeys) ||
       !attn_encode_rows(&mv, a.v, a.lk, a.heads, a.batch, a.kv_head_stride, a.kv_seq_stride, kKeys))
     return cudaErrorInvalidValue;
+  const int splits = dec_tc_splits(a);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.heads, a.batch, 1);
+  cfg.gridDim = dim3(a.heads * splits, a.batch, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = splits;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, attention_dec_tc_kernel, mq, mk, mv, a);
+  cfg.numAttrs = splits > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, attention_dec_tc_kernel, mq, mk, mv, a, splits);
 }
 
 }  // namespace wamb

@@ -210,8 +210,9 @@ struct AttnArgs {
   int q_begin = 0, q_end = 0;
 };
 // Picks the kernel: 128-query tcgen05 tiles (attention_tc.cu) for >= 128
-// queries; for <= 64 queries over <= 896 keys one tcgen05 CTA per (sequence,
-// head) (attention_dec_tc.cu); the mma.sync kernel (attention.cu) otherwise.
+// queries; for <= 64 queries over <= 896 keys tcgen05 with every key's score
+// in TMEM, one CTA or a key-split cluster of 2 / 4 per (sequence, head)
+// (attention_dec_tc.cu); the mma.sync kernel (attention.cu) otherwise.
 void launch_attention(const AttnArgs& a, cudaStream_t s);
 // Kernels launch_attention(a) issues (2 when a ragged tail of < 64 query rows
 // runs on the mma.sync kernel so that the 128-row tiles fit one wave).
@@ -219,8 +220,8 @@ int attention_launch_count(const AttnArgs& a);
 cudaError_t attention_tc_init();
 bool attention_tc_eligible(const AttnArgs& a);
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s);
-// tcgen05 attention for <= 64 queries over <= 896 keys per (sequence, head),
-// one CTA each (attention_dec_tc.cu).
+// tcgen05 attention for <= 64 queries over <= 896 keys per (sequence, head)
+// (attention_dec_tc.cu).
 cudaError_t attention_dec_tc_init();
 bool attention_dec_tc_eligible(const AttnArgs& a);
 cudaError_t launch_attention_dec_tc(const AttnArgs& a, cudaStream_t s);
