@@ -93,6 +93,54 @@ __device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32], int lane)
   return v[0];
 }
 
+// Key-split merge: query slots [split cols, (split + 1) cols) of every split's
+// published (scaled max, sum, unnormalised O^T) in its shared memory, read
+// through distributed shared memory. Each (slot, 8-dim group) item issues
+// all of its SPL x 4 loads before using any.
+template <int SPL>
+__device__ __forceinline__ void merge_slots(const AttnArgs& a, const float* xm, const float* xl,
+                                            const float* xo, int split, int cols, int wt, int lq,
+                                            int seq, int head) {
+  for (int it = wt; it < cols * 16; it += kSoft) {
+    const int j = split * cols + it / 16, g = it % 16;
+    if (j >= lq) break;
+    const uint32_t am = smem_u32(xm + j), al = smem_u32(xl + j), ao = smem_u32(xo + j * 128 + g * 8);
+    float mp[SPL], lp[SPL];
+    float4 o0[SPL], o1[SPL];
+#pragma unroll
+    for (int p = 0; p < SPL; ++p) {
+      const uint32_t rk = static_cast<uint32_t>(p);
+      mp[p] = ld_shared_cluster_f32(mapa_shared(am, rk));
+      lp[p] = ld_shared_cluster_f32(mapa_shared(al, rk));
+      const uint32_t ob = mapa_shared(ao, rk);
+      o0[p] = ld_shared_cluster_f32x4(ob);
+      o1[p] = ld_shared_cluster_f32x4(ob + 16);
+    }
+    float mx = mp[0];
+#pragma unroll
+    for (int p = 1; p < SPL; ++p) mx = fmaxf(mx, mp[p]);
+    float den = 0.0f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int p = 0; p < SPL; ++p) {
+      const float w = ex2_approx(mp[p] - mx);
+      den += w * lp[p];
+      acc[0] += w * o0[p].x; acc[1] += w * o0[p].y; acc[2] += w * o0[p].z; acc[3] += w * o0[p].w;
+      acc[4] += w * o1[p].x; acc[5] += w * o1[p].y; acc[6] += w * o1[p].z; acc[7] += w * o1[p].w;
+    }
+    const float f = 1.0f / den;
+    bf16* dst;
+    if (a.split_first) {
+      dst = j == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
+                   : a.out + (static_cast<long long>(seq) * (lq - 1) + j - 1) * a.ldo;
+    } else {
+      dst = a.out + (static_cast<long long>(seq) * lq + j) * a.ldo;
+    }
+    *reinterpret_cast<uint4*>(dst + head * 128 + g * 8) =
+        make_uint4(pack_bf16(acc[0] * f, acc[1] * f), pack_bf16(acc[2] * f, acc[3] * f),
+                   pack_bf16(acc[4] * f, acc[5] * f), pack_bf16(acc[6] * f, acc[7] * f));
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     attention_dec_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                             const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnArgs a,
@@ -394,46 +442,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int cols = (lq + splits - 1) / splits;
       const int wt = static_cast<int>(threadIdx.x) - 64;
       if (xok && all_ok) {
-        for (int it = wt; it < cols * 16; it += kSoft) {
-          const int j = split * cols + it / 16, g = it % 16;
-          if (j >= lq) break;
-          float mp[kMaxSplits], lp[kMaxSplits];
-          float4 o0[kMaxSplits], o1[kMaxSplits];
-#pragma unroll
-          for (int p = 0; p < kMaxSplits; ++p) {
-            if (p >= splits) break;
-            const uint32_t rk = static_cast<uint32_t>(p);
-            mp[p] = ld_shared_cluster_f32(mapa_shared(smem_u32(xm + j), rk));
-            lp[p] = ld_shared_cluster_f32(mapa_shared(smem_u32(xl + j), rk));
-            const uint32_t ob = mapa_shared(smem_u32(xo + j * 128 + g * 8), rk);
-            o0[p] = ld_shared_cluster_f32x4(ob);
-            o1[p] = ld_shared_cluster_f32x4(ob + 16);
-          }
-          float mx = mp[0];
-#pragma unroll
-          for (int p = 1; p < kMaxSplits; ++p)
-            if (p < splits) mx = fmaxf(mx, mp[p]);
-          float den = 0.0f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int p = 0; p < kMaxSplits; ++p) {
-            if (p >= splits) break;
-            const float w = ex2_approx(mp[p] - mx);
-            den += w * lp[p];
-            acc[0] += w * o0[p].x; acc[1] += w * o0[p].y; acc[2] += w * o0[p].z; acc[3] += w * o0[p].w;
-            acc[4] += w * o1[p].x; acc[5] += w * o1[p].y; acc[6] += w * o1[p].z; acc[7] += w * o1[p].w;
-          }
-          const float f = 1.0f / den;
-          bf16* dst;
-          if (a.split_first) {
-            dst = j == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
-                         : a.out + (static_cast<long long>(seq) * (lq - 1) + j - 1) * a.ldo;
-          } else {
-            dst = a.out + (static_cast<long long>(seq) * lq + j) * a.ldo;
-          }
-          *reinterpret_cast<uint4*>(dst + head * 128 + g * 8) =
-              make_uint4(pack_bf16(acc[0] * f, acc[1] * f), pack_bf16(acc[2] * f, acc[3] * f),
-                         pack_bf16(acc[4] * f, acc[5] * f), pack_bf16(acc[6] * f, acc[7] * f));
-        }
+        if (splits == 4)
+          merge_slots<4>(a, xm, xl, xo, split, cols, wt, lq, seq, head);
+        else
+          merge_slots<2>(a, xm, xl, xo, split, cols, wt, lq, seq, head);
       } else if (!xok) {
         fail(a, kErrEpilogueTimeout);
       }
