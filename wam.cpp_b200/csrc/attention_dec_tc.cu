@@ -45,7 +45,7 @@ namespace {
 constexpr int kKeys = 128;                // keys per tile (UMMA M of S^T, TMEM lanes)
 constexpr int kSlots = 64;                // query slots (UMMA N)
 constexpr int kMaxTiles = 7;              // 7 x 64 S^T columns + 64 O^T columns = 512
-constexpr int kRing = 5;                  // K / V tile slots
+constexpr int kRing = 4;                  // K / V tile slots
 constexpr int kSoftWarps = 8;
 constexpr int kSoft = 32 * kSoftWarps;
 constexpr int kThreads = 64 + kSoft;
@@ -59,8 +59,12 @@ constexpr int kOffP = kOffRing + kRing * kTile;
 constexpr int kOffBar = kOffP + 2 * kPBuf;
 constexpr int kNumBars = 1 + 2 * kRing + kMaxTiles + 2 + 2 + 1 + 2;
 constexpr int kOffRed = kOffBar + 8 * 32;  // [2 (max, sum)][4 quadrants][2 halves][32] F32
-constexpr int kOffX = kOffRed + 2 * 4 * 2 * 32 * 4;  // key splits: this CTA's [2][64] scaled max, sum
-constexpr int kSmem = kOffX + 2 * 64 * 4 + 1024;
+// Key splits: receive area of the query slots this CTA merges, written by
+// every split of its cluster: scaled max [64], sum [64] and unnormalised O
+// [64][128] F32, each indexed [split * cols + slot] (splits * cols <= 64).
+constexpr int kOffX = kOffRed + 2 * 4 * 2 * 32 * 4;
+constexpr int kOffXO = kOffX + 2 * 64 * 4;
+constexpr int kSmem = kOffXO + 64 * 128 * 4 + 1024;
 constexpr int kMaxSplits = 4;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = kMaxTiles * kSlots;  // O^T columns
@@ -93,28 +97,25 @@ __device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32], int lane)
   return v[0];
 }
 
-// Key-split merge: query slots [split cols, (split + 1) cols) of every split's
-// published (scaled max, sum, unnormalised O^T) in its shared memory, read
-// through distributed shared memory. Each (slot, 8-dim group) item issues
-// all of its SPL x 4 loads before using any.
+// Key-split merge of this CTA's query slots [split cols, (split + 1) cols)
+// from its receive area (every split's scaled max, sum and unnormalised O),
+// in split order.
 template <int SPL>
 __device__ __forceinline__ void merge_slots(const AttnArgs& a, const float* xm, const float* xl,
                                             const float* xo, int split, int cols, int wt, int lq,
                                             int seq, int head) {
   for (int it = wt; it < cols * 16; it += kSoft) {
-    const int j = split * cols + it / 16, g = it % 16;
+    const int jl = it / 16, g = it % 16, j = split * cols + jl;
     if (j >= lq) break;
-    const uint32_t am = smem_u32(xm + j), al = smem_u32(xl + j), ao = smem_u32(xo + j * 128 + g * 8);
     float mp[SPL], lp[SPL];
     float4 o0[SPL], o1[SPL];
 #pragma unroll
     for (int p = 0; p < SPL; ++p) {
-      const uint32_t rk = static_cast<uint32_t>(p);
-      mp[p] = ld_shared_cluster_f32(mapa_shared(am, rk));
-      lp[p] = ld_shared_cluster_f32(mapa_shared(al, rk));
-      const uint32_t ob = mapa_shared(ao, rk);
-      o0[p] = ld_shared_cluster_f32x4(ob);
-      o1[p] = ld_shared_cluster_f32x4(ob + 16);
+      mp[p] = xm[p * cols + jl];
+      lp[p] = xl[p * cols + jl];
+      const float4* ob = reinterpret_cast<const float4*>(xo + (p * cols + jl) * 128 + g * 8);
+      o0[p] = ob[0];
+      o1[p] = ob[1];
     }
     float mx = mp[0];
 #pragma unroll
@@ -159,13 +160,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_full + kMaxTiles;          // [2]
   uint64_t* p_free = p_full + 2;                  // [2]
   uint64_t* o_full = p_free + 2;
-  uint64_t* x_ready = o_full + 1;  // key splits: every peer's partials are published
-  uint64_t* x_done = o_full + 2;   // key splits: every peer has read this CTA's partials
+  uint64_t* x_ready = o_full + 1;  // key splits: every split's partials have arrived
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   float* red = reinterpret_cast<float*>(smem + kOffRed);
-  float* xm = reinterpret_cast<float*>(smem + kOffX);  // [64] scaled max per query slot
-  float* xl = xm + 64;                                  // [64] sum per query slot
-  float* xo = reinterpret_cast<float*>(ring);           // [64 slots][128 dims] F32 partial O (ring slot 0)
+  float* xm = reinterpret_cast<float*>(smem + kOffX);   // receive area (key splits)
+  float* xl = xm + 64;
+  float* xo = reinterpret_cast<float*>(smem + kOffXO);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // With key splits the CTAs of a (sequence, head) form a cluster along x;
@@ -183,10 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], 1);
     mbar_init(&p_full[0], kSoftWarps);
     mbar_init(&p_full[1], kSoftWarps);
-    if (splits > 1) {
-      mbar_init(x_ready, splits - 1);
-      mbar_init(x_done, splits - 1);
-    }
+    if (splits > 1) mbar_init(x_ready, splits);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -404,24 +401,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool all_ok = named_bar_and(1, kSoft, ok);
     if (splits > 1) {
       // ----------------------------------------------- merge of key splits
-      // Publish this CTA's unnormalised O^T ([slot][dim] F32 in ring slot 0,
-      // free once every MMA has completed), scaled max and sum per query slot;
-      // then every CTA combines ceil(lq / splits) query slots over all splits
-      // from the peers' shared memory (split order: deterministic). The
-      // handshake (x_ready, x_done) runs whatever happened before, so that no
-      // CTA leaves while a peer may still read its shared memory or arrive on
-      // its barriers; outputs are written only when every wait succeeded.
+      // CTA r of the cluster merges query slots [r cols, (r + 1) cols). Every
+      // split posts its scaled max, sum and unnormalised O^T of those slots
+      // into the owner's receive area (remote stores; the area is used by
+      // nothing else), then arrives (release, cluster scope) on every
+      // owner's x_ready; an owner merges from its own shared memory once all
+      // splits have arrived. No CTA reads another's memory, and nothing is
+      // written into a CTA after its x_ready has completed, so a CTA may
+      // leave as soon as it has merged. The arrivals happen whatever went
+      // before (outputs only when every wait succeeded).
       tc_fence_after();
+      const int cols = (lq + splits - 1) / splits;
       float lsum = 0.0f;
 #pragma unroll
       for (int q = 0; q < 4; ++q) lsum += red_l[(q * 2 + half) * 32 + lane];
       if (quad == 0) {
         const int col = 16 * (lane >> 3) + 8 * half + (lane & 7);
-        xm[col] = mb_lane;
-        xl[col] = lsum;
+        if (col < lq) {
+          const int own = col / cols, jl = col - own * cols;
+          st_shared_cluster_f32(mapa_shared(smem_u32(xm + split * cols + jl), static_cast<uint32_t>(own)), mb_lane);
+          st_shared_cluster_f32(mapa_shared(smem_u32(xl + split * cols + jl), static_cast<uint32_t>(own)), lsum);
+        }
       }
-      const int d = quad * 32 + lane;
       if (all_ok) {
+        const int d = quad * 32 + lane;
         uint32_t r[4][8];
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -431,15 +434,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 4; ++c) {
           if (!chunk_ok[c]) continue;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) xo[(16 * c + 8 * half + i) * 128 + d] = u2f(r[c][i]);
+          for (int i = 0; i < 8; ++i) {
+            const int j = 16 * c + 8 * half + i;
+            if (j >= lq) continue;
+            const int own = j / cols, jl = j - own * cols;
+            st_shared_cluster_f32(
+                mapa_shared(smem_u32(xo + (split * cols + jl) * 128 + d), static_cast<uint32_t>(own)),
+                u2f(r[c][i]));
+          }
         }
       }
+      fence_acq_rel_cluster();  // this thread's remote stores before the arrivals below
       named_bar_sync(1, kSoft);
       if (warp == 2 && lane == 0)
-        for (int p = 0; p < splits; ++p)
-          if (p != split) mbar_arrive_cluster(mapa_shared(smem_u32(x_ready), static_cast<uint32_t>(p)));
+        for (int p = 0; p < splits; ++p) mbar_arrive_cluster(mapa_shared(smem_u32(x_ready), static_cast<uint32_t>(p)));
       const bool xok = mbar_wait_cluster(x_ready, 0);
-      const int cols = (lq + splits - 1) / splits;
       const int wt = static_cast<int>(threadIdx.x) - 64;
       if (xok && all_ok) {
         if (splits == 4)
@@ -448,13 +457,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           merge_slots<2>(a, xm, xl, xo, split, cols, wt, lq, seq, head);
       } else if (!xok) {
         fail(a, kErrEpilogueTimeout);
-      }
-      // this CTA is done reading its peers; it leaves once they are done with it
-      named_bar_sync(1, kSoft);
-      if (warp == 2 && lane == 0) {
-        for (int p = 0; p < splits; ++p)
-          if (p != split) mbar_arrive_cluster(mapa_shared(smem_u32(x_done), static_cast<uint32_t>(p)));
-        if (!mbar_wait_cluster(x_done, 0)) fail(a, kErrEpilogueTimeout);
       }
     } else if (all_ok) {
       tc_fence_after();
