@@ -60,7 +60,7 @@ constexpr int kOffBar = kOffP + 2 * kPBuf;
 constexpr int kNumBars = 1 + 2 * kRing + kMaxTiles + 2 + 2 + 1 + 2;
 constexpr int kOffRed = kOffBar + 8 * 32;  // [2 (max, sum)][4 quadrants][2 halves][32] F32
 // Key splits: receive area of the query slots this CTA merges, written by
-// every split of its cluster: scaled max [64], sum [64] and unnormalised O
+// every split of its cluster: (scaled max, sum) [64][2] and unnormalised O
 // [64][128] F32, each indexed [split * cols + slot] (splits * cols <= 64).
 constexpr int kOffX = kOffRed + 2 * 4 * 2 * 32 * 4;
 constexpr int kOffXO = kOffX + 2 * 64 * 4;
@@ -101,9 +101,8 @@ __device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32], int lane)
 // from its receive area (every split's scaled max, sum and unnormalised O),
 // in split order.
 template <int SPL>
-__device__ __forceinline__ void merge_slots(const AttnArgs& a, const float* xm, const float* xl,
-                                            const float* xo, int split, int cols, int wt, int lq,
-                                            int seq, int head) {
+__device__ __forceinline__ void merge_slots(const AttnArgs& a, const float* xml, const float* xo, int split,
+                                            int cols, int wt, int lq, int seq, int head) {
   for (int it = wt; it < cols * 16; it += kSoft) {
     const int jl = it / 16, g = it % 16, j = split * cols + jl;
     if (j >= lq) break;
@@ -111,8 +110,8 @@ __device__ __forceinline__ void merge_slots(const AttnArgs& a, const float* xm, 
     float4 o0[SPL], o1[SPL];
 #pragma unroll
     for (int p = 0; p < SPL; ++p) {
-      mp[p] = xm[p * cols + jl];
-      lp[p] = xl[p * cols + jl];
+      mp[p] = xml[2 * (p * cols + jl)];
+      lp[p] = xml[2 * (p * cols + jl) + 1];
       const float4* ob = reinterpret_cast<const float4*>(xo + (p * cols + jl) * 128 + g * 8);
       o0[p] = ob[0];
       o1[p] = ob[1];
@@ -163,8 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* x_ready = o_full + 1;  // key splits: every split's partials have arrived
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   float* red = reinterpret_cast<float*>(smem + kOffRed);
-  float* xm = reinterpret_cast<float*>(smem + kOffX);   // receive area (key splits)
-  float* xl = xm + 64;
+  float* xml = reinterpret_cast<float*>(smem + kOffX);  // receive area (key splits)
   float* xo = reinterpret_cast<float*>(smem + kOffXO);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -183,8 +181,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], 1);
     mbar_init(&p_full[0], kSoftWarps);
     mbar_init(&p_full[1], kSoftWarps);
-    if (splits > 1) mbar_init(x_ready, splits);
     fence_barrier_init();
+    if (splits > 1) {
+      // every split sends (scaled max, sum) and 128 O values of each of this
+      // CTA's query slots below lq: 520 bytes per slot and split
+      const int cols = (a.lq + splits - 1) / splits;
+      const int mine = a.lq - split * cols < cols ? a.lq - split * cols : cols;
+      mbar_init(x_ready, 1);
+      fence_barrier_init();
+      mbar_arrive_expect_tx(x_ready, static_cast<uint32_t>(splits * (mine > 0 ? mine : 0) * 520));
+    }
     fence_proxy_async_smem();
   }
   if (warp == 1) {
@@ -402,14 +408,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (splits > 1) {
       // ----------------------------------------------- merge of key splits
       // CTA r of the cluster merges query slots [r cols, (r + 1) cols). Every
-      // split posts its scaled max, sum and unnormalised O^T of those slots
-      // into the owner's receive area (remote stores; the area is used by
-      // nothing else), then arrives (release, cluster scope) on every
-      // owner's x_ready; an owner merges from its own shared memory once all
-      // splits have arrived. No CTA reads another's memory, and nothing is
-      // written into a CTA after its x_ready has completed, so a CTA may
-      // leave as soon as it has merged. The arrivals happen whatever went
-      // before (outputs only when every wait succeeded).
+      // split sends its scaled max, sum and unnormalised O^T of those slots
+      // into the owner's receive area with st.async from registers, counted
+      // in bytes on the owner's x_ready (which expects them since kernel
+      // start); an owner merges from its own shared memory once all have
+      // landed. No CTA reads another's memory and nothing is written into a
+      // CTA after its x_ready has completed, so each may leave once merged.
+      // The sends happen whatever went before (outputs only when every wait
+      // succeeded).
       tc_fence_after();
       const int cols = (lq + splits - 1) / splits;
       float lsum = 0.0f;
@@ -418,12 +424,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (quad == 0) {
         const int col = 16 * (lane >> 3) + 8 * half + (lane & 7);
         if (col < lq) {
-          const int own = col / cols, jl = col - own * cols;
-          st_shared_cluster_f32(mapa_shared(smem_u32(xm + split * cols + jl), static_cast<uint32_t>(own)), mb_lane);
-          st_shared_cluster_f32(mapa_shared(smem_u32(xl + split * cols + jl), static_cast<uint32_t>(own)), lsum);
+          const uint32_t own = static_cast<uint32_t>(col / cols);
+          const int jl = col - static_cast<int>(own) * cols;
+          st_async_v2_b32(mapa_shared(smem_u32(xml + 2 * (split * cols + jl)), own), __float_as_uint(mb_lane),
+                          __float_as_uint(lsum), mapa_shared(smem_u32(x_ready), own));
         }
       }
-      if (all_ok) {
+      {
         const int d = quad * 32 + lane;
         uint32_t r[4][8];
 #pragma unroll
@@ -437,24 +444,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 8; ++i) {
             const int j = 16 * c + 8 * half + i;
             if (j >= lq) continue;
-            const int own = j / cols, jl = j - own * cols;
-            st_shared_cluster_f32(
-                mapa_shared(smem_u32(xo + (split * cols + jl) * 128 + d), static_cast<uint32_t>(own)),
-                u2f(r[c][i]));
+            const uint32_t own = static_cast<uint32_t>(j / cols);
+            const int jl = j - static_cast<int>(own) * cols;
+            st_async_b32(mapa_shared(smem_u32(xo + (split * cols + jl) * 128 + d), own), r[c][i],
+                         mapa_shared(smem_u32(x_ready), own));
           }
         }
       }
-      fence_acq_rel_cluster();  // this thread's remote stores before the arrivals below
-      named_bar_sync(1, kSoft);
-      if (warp == 2 && lane == 0)
-        for (int p = 0; p < splits; ++p) mbar_arrive_cluster(mapa_shared(smem_u32(x_ready), static_cast<uint32_t>(p)));
       const bool xok = mbar_wait_cluster(x_ready, 0);
       const int wt = static_cast<int>(threadIdx.x) - 64;
       if (xok && all_ok) {
         if (splits == 4)
-          merge_slots<4>(a, xm, xl, xo, split, cols, wt, lq, seq, head);
+          merge_slots<4>(a, xml, xo, split, cols, wt, lq, seq, head);
         else
-          merge_slots<2>(a, xm, xl, xo, split, cols, wt, lq, seq, head);
+          merge_slots<2>(a, xml, xo, split, cols, wt, lq, seq, head);
       } else if (!xok) {
         fail(a, kErrEpilogueTimeout);
       }

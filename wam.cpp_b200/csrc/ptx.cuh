@@ -502,6 +502,21 @@ __device__ __forceinline__ void st_shared_cluster_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
+// st.async of one / two 32-bit values into shared memory of a CTA of the
+// cluster (shared::cluster address), completion counted in bytes on that
+// CTA's mbarrier (shared::cluster address). The source is registers: nothing
+// of the sender's memory is read later.
+__device__ __forceinline__ void st_async_b32(uint32_t addr, uint32_t v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v),
+               "r"(remote_bar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_v2_b32(uint32_t addr, uint32_t v0, uint32_t v1, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "r"(v0), "r"(v1), "r"(remote_bar)
+               : "memory");
+}
+
 // Orders this thread's earlier memory operations (remote shared-memory stores
 // included) at cluster scope before its later ones.
 __device__ __forceinline__ void fence_acq_rel_cluster() {
