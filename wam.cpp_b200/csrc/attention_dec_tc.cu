@@ -431,23 +431,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       {
-        const int d = quad * 32 + lane;
         uint32_t r[4][8];
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           if (chunk_ok[c]) tmem_ld_x8(tmem + lane_off + kTmemO + static_cast<uint32_t>(16 * c + 8 * half), r[c]);
         tmem_ld_wait();
+        // 4 x 4 transposes within groups of 4 lanes: lane 4m + s then holds
+        // query slot 4k + s of the chunk for dims 4m .. 4m + 3 (one 16-byte
+        // store)
+        const int s0 = lane & 1, s1 = (lane >> 1) & 1;
+        const int dbase = quad * 32 + (lane & ~3);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          if (!chunk_ok[c]) continue;
+          if (!chunk_ok[c]) continue;  // warp-uniform
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int j = 16 * c + 8 * half + i;
+          for (int k = 0; k < 2; ++k) {
+            uint32_t t[4] = {r[c][4 * k], r[c][4 * k + 1], r[c][4 * k + 2], r[c][4 * k + 3]};
+#pragma unroll
+            for (int jj = 0; jj < 4; jj += 2) {
+              const uint32_t recv = __shfl_xor_sync(0xffffffffu, s0 ? t[jj] : t[jj + 1], 1);
+              if (s0) t[jj] = recv; else t[jj + 1] = recv;
+            }
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+              const uint32_t recv = __shfl_xor_sync(0xffffffffu, s1 ? t[jj] : t[jj + 2], 2);
+              if (s1) t[jj] = recv; else t[jj + 2] = recv;
+            }
+            const int j = 16 * c + 8 * half + 4 * k + (lane & 3);
             if (j >= lq) continue;
             const uint32_t own = static_cast<uint32_t>(j / cols);
             const int jl = j - static_cast<int>(own) * cols;
-            st_async_b32(mapa_shared(smem_u32(xo + (split * cols + jl) * 128 + d), own), r[c][i],
-                         mapa_shared(smem_u32(x_ready), own));
+            st_async_v4_b32(mapa_shared(smem_u32(xo + (split * cols + jl) * 128 + dbase), own), t[0], t[1], t[2],
+                            t[3], mapa_shared(smem_u32(x_ready), own));
           }
         }
       }

@@ -517,6 +517,14 @@ __device__ __forceinline__ void st_async_v2_b32(uint32_t addr, uint32_t v0, uint
                : "memory");
 }
 
+__device__ __forceinline__ void st_async_v4_b32(uint32_t addr, uint32_t v0, uint32_t v1, uint32_t v2,
+                                                uint32_t v3, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   addr),
+               "r"(v0), "r"(v1), "r"(v2), "r"(v3), "r"(remote_bar)
+               : "memory");
+}
+
 // Orders this thread's earlier memory operations (remote shared-memory stores
 // included) at cluster scope before its later ones.
 __device__ __forceinline__ void fence_acq_rel_cluster() {
