@@ -72,7 +72,7 @@ def rel_l2(a, b):
 
 cases = [(1, 24, 48, 817, 1.0), (1, 24, 48, 512, 1.0), (2, 3, 1, 64, 1.0), (1, 24, 1, 512, 1.0),
          (3, 5, 33, 250, 8.0), (1, 2, 64, 896, 4.0), (2, 4, 17, 1, 1.0), (1, 3, 40, 129, 1.0),
-         (2, 24, 48, 817, 1.0)]
+         (2, 24, 48, 817, 1.0), (1, 24, 769, 769, 1.0)]
 worst = 0.0
 for B, H, lq, lk, qs in cases:
     g = torch.Generator().manual_seed(lq * 31 + lk)
@@ -95,8 +95,9 @@ print("worst rel-L2", worst)
 def test_decode_attention_mma_sync(cuda_device):
     """The mma.sync decode kernel (attention.cu: 64-query blocks, keys split
     over up to 8 CTAs merged through L2 or distributed shared memory), which
-    the tcgen05 kernel replaces for <= 896 keys, on the same shapes:
-    WAM_B200_ATTN_DEC_TC=0 in a child process."""
+    the tcgen05 kernel replaces for <= 896 keys, on the same shapes and on the
+    one-row ragged tail of a 769-query launch: WAM_B200_ATTN_DEC_TC=0 in a
+    child process."""
     import os
     import subprocess
     import sys

@@ -414,7 +414,8 @@ int num_sms_cached() {
 // Rows of a tcgen05 launch that end in a ragged tile of <= 64 rows which alone
 // would start a second wave of CTAs (e.g. 769 prefix queries x 24 heads: 144
 // CTAs of full tiles + 24 of one row each): the full tiles run on the tcgen05
-// kernel in one wave and the tail on the mma.sync kernel; else 0.
+// kernel in one wave and the tail on the decode kernel (tcgen05 for <= 896
+// keys, else mma.sync); else 0.
 int tc_split_rows(const AttnArgs& a) {
   if (a.q_begin != 0 || a.q_end != 0) return 0;
   const int full = (a.lq / 128) * 128, rem = a.lq - full;
@@ -469,7 +470,8 @@ void launch_attention(const AttnArgs& a, cudaStream_t s) {
       if (launch_attention_tc(head, s) == cudaSuccess) {
         AttnArgs tail = a;
         tail.q_begin = full;
-        launch_attention_decode(tail, s);
+        if (!attention_dec_tc_eligible(tail) || launch_attention_dec_tc(tail, s) != cudaSuccess)
+          launch_attention_decode(tail, s);
         return;
       }
     } else if (launch_attention_tc(a, s) == cudaSuccess) {

@@ -102,10 +102,10 @@ __device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32], int lane)
 // in split order.
 template <int SPL>
 __device__ __forceinline__ void merge_slots(const AttnArgs& a, const float* xml, const float* xo, int split,
-                                            int cols, int wt, int lq, int seq, int head) {
+                                            int cols, int wt, int nq, int q0, int seq, int head) {
   for (int it = wt; it < cols * 16; it += kSoft) {
     const int jl = it / 16, g = it % 16, j = split * cols + jl;
-    if (j >= lq) break;
+    if (j >= nq) break;
     float mp[SPL], lp[SPL];
     float4 o0[SPL], o1[SPL];
 #pragma unroll
@@ -128,12 +128,13 @@ __device__ __forceinline__ void merge_slots(const AttnArgs& a, const float* xml,
       acc[4] += w * o1[p].x; acc[5] += w * o1[p].y; acc[6] += w * o1[p].z; acc[7] += w * o1[p].w;
     }
     const float f = 1.0f / den;
+    const int row = q0 + j;  // query row of the sequence
     bf16* dst;
     if (a.split_first) {
-      dst = j == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
-                   : a.out + (static_cast<long long>(seq) * (lq - 1) + j - 1) * a.ldo;
+      dst = row == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
+                     : a.out + (static_cast<long long>(seq) * (a.lq - 1) + row - 1) * a.ldo;
     } else {
-      dst = a.out + (static_cast<long long>(seq) * lq + j) * a.ldo;
+      dst = a.out + (static_cast<long long>(seq) * a.lq + row) * a.ldo;
     }
     *reinterpret_cast<uint4*>(dst + head * 128 + g * 8) =
         make_uint4(pack_bf16(acc[0] * f, acc[1] * f), pack_bf16(acc[2] * f, acc[3] * f),
@@ -184,9 +185,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     if (splits > 1) {
       // every split sends (scaled max, sum) and 128 O values of each of this
-      // CTA's query slots below lq: 520 bytes per slot and split
-      const int cols = (a.lq + splits - 1) / splits;
-      const int mine = a.lq - split * cols < cols ? a.lq - split * cols : cols;
+      // CTA's query slots below nq: 520 bytes per slot and split
+      const int nq = (a.q_end > 0 ? a.q_end : a.lq) - a.q_begin;
+      const int cols = (nq + splits - 1) / splits;
+      const int mine = nq - split * cols < cols ? nq - split * cols : cols;
       mbar_init(x_ready, 1);
       fence_barrier_init();
       mbar_arrive_expect_tx(x_ready, static_cast<uint32_t>(splits * (mine > 0 ? mine : 0) * 520));
@@ -232,8 +234,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       griddep_wait();
       griddep_launch_dependents();
       mbar_arrive_expect_tx(q_full, 2 * kQHalf);
-      tma_load_4d(sq, &tm_q, q_full, 0, 0, head, seq, pol);
-      tma_load_4d(sq + kQHalf, &tm_q, q_full, 64, 0, head, seq, pol);
+      tma_load_4d(sq, &tm_q, q_full, 0, a.q_begin, head, seq, pol);
+      tma_load_4d(sq + kQHalf, &tm_q, q_full, 64, a.q_begin, head, seq, pol);
       bool ok = true;
       for (; issued < items; ++issued) {
         if (issued >= kRing &&
@@ -257,9 +259,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // contiguous: two 64-dim atoms 16 KB apart, 8-key groups 1024 bytes
       // apart, 16 keys = 2048 bytes per step), B = P^T MN-major (one 64-query
       // atom, 8-key groups 1024 bytes apart).
-      // S^T over the query slots in use (N = lq rounded up to 16; its columns
-      // >= lq see the zero-filled Q rows)
-      const uint32_t idesc_s = umma_idesc_bf16(kKeys, ((a.lq + 15) / 16) * 16);
+      // S^T over the query slots in use (N = the launch's rows rounded up to
+      // 16; the columns past them are discarded)
+      const int nq = (a.q_end > 0 ? a.q_end : a.lq) - a.q_begin;
+      const uint32_t idesc_s = umma_idesc_bf16(kKeys, ((nq + 15) / 16) * 16);
       constexpr uint32_t idesc_o = umma_idesc_bf16_mn(128, kSlots);
       bool ok = mbar_wait(q_full, 0);
       for (int t = 0; t < nk && ok; ++t) {
@@ -308,13 +311,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;              // TMEM lane quadrant: keys / dims 32 quad ..
     const int half = (warp - 2) >> 2;       // query chunks 16 c + 8 half (c = 0..3)
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const int lq = a.lq;
+    // query rows [q0, q0 + nq) of the sequence are this launch's slots 0 .. nq - 1
+    const int q0 = a.q_begin;
+    const int nq = (a.q_end > 0 ? a.q_end : a.lq) - q0;
     const float sl2 = a.scale * 1.4426950408889634f;
     float* red_m = red;                     // [4][2][32]
     float* red_l = red + 4 * 2 * 32;
     bool chunk_ok[4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) chunk_ok[c] = 16 * c + 8 * half < lq;
+    for (int c = 0; c < 4; ++c) chunk_ok[c] = 16 * c + 8 * half < nq;
     bool ok = true;
 
     // Pass 1: per-query max over this thread's keys (one per tile).
@@ -417,13 +422,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The sends happen whatever went before (outputs only when every wait
       // succeeded).
       tc_fence_after();
-      const int cols = (lq + splits - 1) / splits;
+      const int cols = (nq + splits - 1) / splits;
       float lsum = 0.0f;
 #pragma unroll
       for (int q = 0; q < 4; ++q) lsum += red_l[(q * 2 + half) * 32 + lane];
       if (quad == 0) {
         const int col = 16 * (lane >> 3) + 8 * half + (lane & 7);
-        if (col < lq) {
+        if (col < nq) {
           const uint32_t own = static_cast<uint32_t>(col / cols);
           const int jl = col - static_cast<int>(own) * cols;
           st_async_v2_b32(mapa_shared(smem_u32(xml + 2 * (split * cols + jl)), own), __float_as_uint(mb_lane),
@@ -458,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (s1) t[jj] = recv; else t[jj + 2] = recv;
             }
             const int j = 16 * c + 8 * half + 4 * k + (lane & 3);
-            if (j >= lq) continue;
+            if (j >= nq) continue;
             const uint32_t own = static_cast<uint32_t>(j / cols);
             const int jl = j - static_cast<int>(own) * cols;
             st_async_v4_b32(mapa_shared(smem_u32(xo + (split * cols + jl) * 128 + dbase), own), t[0], t[1], t[2],
@@ -470,9 +475,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int wt = static_cast<int>(threadIdx.x) - 64;
       if (xok && all_ok) {
         if (splits == 4)
-          merge_slots<4>(a, xml, xo, split, cols, wt, lq, seq, head);
+          merge_slots<4>(a, xml, xo, split, cols, wt, nq, q0, seq, head);
         else
-          merge_slots<2>(a, xml, xo, split, cols, wt, lq, seq, head);
+          merge_slots<2>(a, xml, xo, split, cols, wt, nq, q0, seq, head);
       } else if (!xok) {
         fail(a, kErrEpilogueTimeout);
       }
@@ -498,13 +503,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 8; ++i) {
           const float f = __shfl_sync(0xffffffffu, inv, 8 * c + i);
           const int qr = 16 * c + 8 * half + i;
-          if (qr >= lq) continue;
+          if (qr >= nq) continue;
+          const int row = q0 + qr;
           bf16* dst;
           if (a.split_first) {
-            dst = qr == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
-                          : a.out + (static_cast<long long>(seq) * (lq - 1) + qr - 1) * a.ldo;
+            dst = row == 0 ? a.out_first + static_cast<long long>(seq) * a.ldo_first
+                           : a.out + (static_cast<long long>(seq) * (a.lq - 1) + row - 1) * a.ldo;
           } else {
-            dst = a.out + (static_cast<long long>(seq) * lq + qr) * a.ldo;
+            dst = a.out + (static_cast<long long>(seq) * a.lq + row) * a.ldo;
           }
           dst[head * 128 + d] = __float2bfloat16_rn(u2f(r[c][i]) * f);
         }
@@ -549,8 +555,9 @@ cudaError_t attention_dec_tc_init() {
 }
 
 bool attention_dec_tc_eligible(const AttnArgs& a) {
-  return dec_tc_enabled() && a.lq >= 1 && a.lq <= kSlots && a.lk >= 1 && a.lk <= kMaxTiles * kKeys &&
-         a.q_begin == 0 && a.q_end == 0 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 &&
+  const int rows = (a.q_end > 0 ? a.q_end : a.lq) - a.q_begin;
+  return dec_tc_enabled() && rows >= 1 && rows <= kSlots && a.q_begin >= 0 && a.lk >= 1 &&
+         a.lk <= kMaxTiles * kKeys && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 &&
          (reinterpret_cast<uintptr_t>(a.k) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.v) & 15) == 0 &&
          a.q_head_stride % 8 == 0 && a.q_seq_stride % 8 == 0 && a.kv_head_stride % 8 == 0 &&
          a.kv_seq_stride % 8 == 0 && a.batch <= 65535;
